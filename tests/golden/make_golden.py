@@ -1,0 +1,212 @@
+"""Generate the golden fixtures in this folder by running IRON's own golden code.
+
+Run where the IRON source tree is available (it is NOT needed afterwards):
+
+    python tests/golden/make_golden.py /path/to/IRON
+
+The reference package ``__init__``s import the NPU toolchain (``aie``), which is
+not installable off-NPU, so the golden modules are loaded by file path with a
+one-symbol stand-in for ``iron.common.test_utils.torch_dtype_map``.  Functions
+that live inside modules importing ``aie`` at top level (the Qwen3 runtime's
+packers and rope table, the fused-MLP test's kernel-faithful golden) are
+extracted with ``ast`` and executed unchanged in a small namespace.
+
+Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
+  gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
+  decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz
+"""
+
+from __future__ import annotations
+
+import ast
+import importlib.util
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().to(torch.bfloat16).view(torch.uint16).numpy().copy()
+
+
+def setup_shim(ref: Path):
+    iron = types.ModuleType("iron")
+    iron.__path__ = []
+    common = types.ModuleType("iron.common")
+    common.__path__ = []
+    tu = types.ModuleType("iron.common.test_utils")
+    tu.torch_dtype_map = {"bf16": torch.bfloat16, "f32": torch.float32, "i8": torch.int8,
+                          "ui8": torch.uint8, "i16": torch.int16, "i32": torch.int32}
+    ops = types.ModuleType("iron.operators")
+    ops.__path__ = []
+    for m in (iron, common, tu, ops):
+        sys.modules[m.__name__] = m
+
+
+def load(ref: Path, rel: str, modname: str):
+    spec = importlib.util.spec_from_file_location(modname, ref / rel)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[modname] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def extract(ref: Path, rel: str, names: list[str], cls: str | None = None, extra_globals=None):
+    """Exec selected top-level (or class-level) function defs of a file unchanged."""
+    src = (ref / rel).read_text()
+    tree = ast.parse(src)
+    body = tree.body
+    if cls is not None:
+        body = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == cls).body
+    fns = [n for n in body if isinstance(n, ast.FunctionDef) and n.name in names]
+    missing = set(names) - {f.name for f in fns}
+    if missing:
+        raise KeyError(f"{rel}: {missing}")
+    mod = ast.Module(body=fns, type_ignores=[])
+    g = {"np": np, "torch": torch, **(extra_globals or {})}
+    exec(compile(mod, str(ref / rel), "exec"), g)
+    return {n: g[n] for n in names}
+
+
+def main(ref: Path):
+    setup_shim(ref)
+    rms = load(ref, "iron/operators/rms_norm/reference.py", "iron.operators.rms_norm.reference")
+    rope = load(ref, "iron/operators/rope/reference.py", "iron.operators.rope.reference")
+    qkv = load(ref, "iron/operators/qkv_head_dp/reference.py", "iron.operators.qkv_head_dp.reference")
+    attn = load(ref, "iron/operators/decode_attn/reference.py", "ref_decode_attn")
+    g8 = load(ref, "iron/operators/gemv_int8/reference.py", "ref_gemv_int8")
+    mlp = load(ref, "iron/operators/swiglu_mlp_dp/reference.py", "ref_swiglu_mlp_dp")
+    gemv = load(ref, "iron/operators/gemv/reference.py", "ref_gemv")
+    silu = load(ref, "iron/operators/silu/reference.py", "ref_silu")
+    add = load(ref, "iron/operators/elementwise_add/reference.py", "ref_add")
+    mul = load(ref, "iron/operators/elementwise_mul/reference.py", "ref_mul")
+
+    # ---- int8 GEMV: the reference's own generator + a group-32 variant ----
+    g = g8.generate_golden_reference(M=256, K=1024)
+    rng = np.random.default_rng(7)
+    s32 = torch.from_numpy((rng.random((256, 1024 // 32)) * 0.05 + 0.01).astype(np.float32)).to(torch.bfloat16)
+    c32 = g8.reference(torch.from_numpy(g["w_int8"]), s32, g["B"]).to(torch.bfloat16)
+    wire_signed = g8.pack_payload(g["w_int8"][:16], g["scales"][:16], 2, 4, "signed")
+    wire_biased = g8.pack_payload(g["w_int8"][:16], g["scales"][:16], 1, 2, "biased")
+    np.savez_compressed(
+        OUT / "gemv_int8.npz", w_int8=g["w_int8"], scales=bits(g["scales"]), x=bits(g["B"]),
+        y=bits(g["C"]), scales_g32=bits(s32), y_g32=bits(c32),
+        wire_signed_c2_t4=wire_signed.view(torch.uint16).numpy(),
+        wire_biased_c1_t2=wire_biased.view(torch.uint16).numpy())
+
+    # ---- RTN quantiser + tile packer + rope table from the Qwen3 runtime ----
+    app = "iron/applications/qwen3_0.6b/qwen3_npu_int8.py"
+    fns = extract(ref, app, ["_set_int8_rtn", "_pack_int8", "_precompute_rope_angles"], cls="Qwen3NPU")
+    captured = {}
+
+    class FakeSelf:
+        def _set(self, name, t):
+            captured[name] = t
+
+        def _pack_int8(self, *a):
+            return fns["_pack_int8"](self, *a)
+
+    w = (torch.randn(64, 256, generator=torch.Generator().manual_seed(3)) * 0.02).to(torch.bfloat16)
+    w[5, :128] = 0  # an all-zero group exercises the s=1 branch
+    fns["_set_int8_rtn"](FakeSelf(), "W", w, 64, 256, 1, 4, signed=True)
+    wire128 = captured["W"].view(torch.uint16).numpy()
+    fns["_set_int8_rtn"](FakeSelf(), "W2", w, 64, 256, 2, 2, signed=False)
+    wire128b = captured["W2"].view(torch.uint16).numpy()
+    ns = types.SimpleNamespace()
+    rope_mod = extract(ref, app, ["_precompute_rope_angles"], cls="Qwen3NPU",
+                       extra_globals={"head_dim": 128, "rope_theta": 1e6, "max_seq_len": 1200})
+    rope_mod["_precompute_rope_angles"](ns)
+    np.savez_compressed(OUT / "rtn_pack.npz", w=bits(w), wire_signed_t4=wire128,
+                        wire_biased_c2_t2=wire128b, angle_table=bits(ns.angle_table))
+
+    # ---- RMSNorm: reference generator (weighted, eps 1e-6) + N(0,1) rows ----
+    gr = rms.generate_golden_reference(rows=4, cols=1024, weighted=True, eps=1e-6)
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(3, 1024, generator=gen).to(torch.bfloat16)
+    wv = (1 + 0.1 * torch.randn(1024, generator=gen)).to(torch.bfloat16)
+    y = rms.reference(x, wv, weighted=True, eps=1e-6)
+    np.savez_compressed(OUT / "rms_norm.npz", x_gen=bits(gr["input"]), w_gen=bits(gr["weight"]),
+                        y_gen=bits(gr["output"]), x=bits(x), w=bits(wv), y=bits(y))
+
+    # ---- RoPE two-halves from an angle row ----
+    xr = torch.randn(16, 1, 128, generator=gen).to(torch.bfloat16)
+    ang = ns.angle_table[777].reshape(1, 128)
+    yr = rope.reference(xr, ang, method_type=0, rows=1, cols=128)
+    np.savez_compressed(OUT / "rope.npz", x=bits(xr.reshape(16, 128)), ang=bits(ang), y=bits(yr))
+
+    # ---- fused QKV head (float weights, Qwen3-0.6B head geometry, D=256) ----
+    D, HD, Hq, Hkv = 256, 128, 4, 2
+    cur = torch.randn(D, generator=gen).to(torch.bfloat16)
+    n_in = (1 + 0.1 * torch.randn(D, generator=gen)).to(torch.bfloat16)
+    wqkv = (0.05 * torch.randn((Hq + 2 * Hkv) * HD, D, generator=gen)).to(torch.bfloat16)
+    n_qn = (1 + 0.1 * torch.randn(HD, generator=gen)).to(torch.bfloat16)
+    n_kn = (1 + 0.1 * torch.randn(HD, generator=gen)).to(torch.bfloat16)
+    angq = ns.angle_table[345]
+    out = qkv.reference(cur, n_in, wqkv, n_qn, n_kn, angq, D, HD, Hq, Hkv, eps=1e-6)
+    np.savez_compressed(OUT / "qkv_head.npz", cur=bits(cur), n_in=bits(n_in), wqkv=bits(wqkv),
+                        n_qn=bits(n_qn), n_kn=bits(n_kn), ang=bits(angq), out=bits(out),
+                        dims=np.array([D, HD, Hq, Hkv]))
+
+    # ---- decode attention: reference generator + several causal boundaries ----
+    ga = attn.generate_golden_reference(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=256)
+    kv = ga["kv_in"].reshape(8, 2 * 256, 128)
+    K, V = kv[:, :256], kv[:, 256:]
+    outs = {}
+    for sp in (0, 1, 31, 32, 33, 100, 255):
+        outs[f"O_{sp}"] = bits(attn.reference(ga["Q"], K, V, sp, 128, 16, 8))
+    np.savez_compressed(OUT / "decode_attn.npz", Q=bits(ga["Q"]), K=bits(K), V=bits(V),
+                        O_gen=bits(ga["O"]), **outs)
+
+    # ---- SwiGLU MLP: f32 goldens (plain and fuse_o) + the kernel-faithful golden ----
+    gm = mlp.generate_golden_reference(D=128, FF=384)
+    gf = mlp.generate_golden_reference_fused_o(D=128, FF=384, QD=256)
+    tf = extract(ref, "iron/operators/swiglu_mlp_dp/test.py",
+                 ["matvec_int8", "silu_bf16_inplace", "reference", "quantize_weights"],
+                 extra_globals={"GROUP": 128})
+    torch.manual_seed(42)
+    Dk, FFk = 256, 768
+    wg_q, wg_s = tf["quantize_weights"](torch.randn(FFk, Dk) * 0.1)
+    wu_q, wu_s = tf["quantize_weights"](torch.randn(FFk, Dk))
+    wd_q, wd_s = tf["quantize_weights"](torch.randn(Dk, FFk))
+    qg = torch.from_numpy(wg_q.astype(np.int16) - 128).float()
+    qu = torch.from_numpy(wu_q.astype(np.int16) - 128).float()
+    qd = torch.from_numpy(wd_q.astype(np.int16) - 128).float()
+    mv = tf["matvec_int8"]
+    kcur = torch.randn(Dk).to(torch.bfloat16) * 0.2
+    ka = torch.randn(Dk).to(torch.bfloat16) * 0.2
+    kn = torch.rand(Dk) + 0.5
+    knxt = tf["reference"](kcur, ka, kn,
+                           lambda v: mv(qg, wg_s, v).to(torch.bfloat16),
+                           lambda v: mv(qu, wu_s, v).to(torch.bfloat16),
+                           lambda v: mv(qd, wd_s, v).to(torch.bfloat16), eps=1e-6)
+    sil_in = (torch.randn(4096, generator=gen) * 4).to(torch.bfloat16)
+    np.savez_compressed(
+        OUT / "swiglu.npz",
+        **{f"f32_{k}": v.view(np.uint16) for k, v in gm.items()},
+        **{f"fo_{k}": v.view(np.uint16) for k, v in gf.items()},
+        k_wg_q=wg_q, k_wg_s=wg_s, k_wu_q=wu_q, k_wu_s=wu_s, k_wd_q=wd_q, k_wd_s=wd_s,
+        k_cur=bits(kcur), k_a=bits(ka), k_npf=kn.numpy(), k_nxt=bits(knxt),
+        silu_in=bits(sil_in), silu_tanh_out=bits(tf["silu_bf16_inplace"](sil_in)))
+
+    # ---- elementwise + SiLU goldens ----
+    ea = (torch.randn(2048, generator=gen) * 3).to(torch.bfloat16)
+    eb = (torch.randn(2048, generator=gen) * 3).to(torch.bfloat16)
+    np.savez_compressed(OUT / "elementwise.npz", a=bits(ea), b=bits(eb),
+                        add=bits(add.reference(ea, eb)), mul=bits(mul.reference(ea, eb)),
+                        silu=bits(silu.reference(ea)))
+
+    # ---- bf16 GEMV golden (reference generator) ----
+    gb = gemv.generate_golden_reference(M=256, K=512)
+    np.savez_compressed(OUT / "gemv_bf16.npz", A=bits(gb["A"]), B=bits(gb["B"]), C=bits(gb["C"]))
+    print("wrote fixtures to", OUT)
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the IRON source tree>")
+    main(Path(sys.argv[1]))

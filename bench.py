@@ -1,0 +1,344 @@
+#!/usr/bin/env python3
+"""Qwen3-0.6B int8 (group 32) batch-1 greedy decode throughput on B200.
+
+Workload: 28 layers, hidden 1024, 16/8 heads, head_dim 128,
+SwiGLU 3072, vocab 151936 with a tied bf16 embedding/lm_head, projection
+weights int8 RTN in groups of 32 (synthetic, seeded), batch 1.  A 1024-token
+random prompt is prefilled token by token (as the reference does), then greedy
+decode steps are timed.  One step = one decoded token.  Every step streams
+~0.78 GB of weights + the KV cache from HBM, far more than the 126 MB L2, so no
+L2 flush is needed between steps.
+
+  value   tokens/s of K back-to-back decode steps, inputs resident in HBM, CUDA
+          events on the decoder's stream, max over ranks (whole-job aggregate).
+  e2e     tokens/s through the public API (Qwen3B200.step_tokens): per step the
+          token id and position go host->device from pinned memory and the next
+          token comes back device->host.
+  --gpus N: N independent replicas (the 0.6B batch-1 path does not shard), one
+          per GPU, launched under torchrun; the value sums the replicas.
+  --impl reference: the reference's CPU golden path (the numpy restatement in
+          oracle/, the reference being NPU-only) on the host cores, one rank.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Qwen3 decode tokens/s"
+UNIT = "tokens/s"
+PROMPT = 1024
+GROUP = 32
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
+    return ap.parse_args()
+
+
+def workload(args):
+    return {"workload": f"qwen3-0.6b int8-g{GROUP} greedy decode, batch 1, bf16 tied lm_head, "
+                        f"{args.prompt}-token random prompt prefilled",
+            "batch": 1, "layers": 28, "vocab": 151936, "group": GROUP, "prompt_tokens": args.prompt,
+            "l2": "no flush: ~0.78 GB of weights streamed per step, larger than the 126 MB L2",
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        self.f.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.f.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle sample (test infrastructure: the checker and the CPU baseline only)
+# ---------------------------------------------------------------------------
+def cpu_sample(weights_np, kv_np, shape, pos, token, n_tokens, threads):
+    """Time the composed CPU oracle (oracle/qwen3.py) for ``n_tokens`` decode steps at
+    ``pos`` on the GPU run's own weights and KV cache.  Returns (tokens/s, info, logits)."""
+    from oracle import ops
+    from oracle.qwen3 import OracleQwen3
+    used = ops.set_threads(threads)
+    orc = OracleQwen3(shape, weights_np, kv_np.shape[2])
+    orc.kv[...] = kv_np
+    t_layer, t_head = [], []
+    logits = None
+    for _ in range(n_tokens):
+        x = orc.embed(token)
+        for i in range(shape.n_layers):
+            t0 = time.perf_counter()
+            x = orc.layer(i, x, pos)
+            t_layer.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        xf = ops.rms_norm_ref(x.reshape(1, -1), weights_np["final_norm"], weighted=True, eps=shape.eps).reshape(-1)
+        logits = ops.gemv_bf16(weights_np["embed"], xf)
+        t_head.append(time.perf_counter() - t0)
+    per_token = statistics.mean(t_layer) * shape.n_layers + statistics.mean(t_head)
+    return 1.0 / per_token, used, logits
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, rank):
+    """Reference arm: the CPU golden path on the host cores (one rank)."""
+    import numpy as np
+    if rank != 0:
+        return
+    from oracle import ops
+    from oracle.bf16 import rnd, round_bits
+    from oracle.qwen3 import OracleQwen3, Qwen3Shape
+    shape = Qwen3Shape(group=GROUP)
+    rng = np.random.default_rng(args.seed)
+    threads = len(os.sched_getaffinity(0))
+    ops.set_threads(threads)
+    # synthetic weights with the GPU arm's distributions (numpy generator on the host)
+    D, FF, QD, QKV = shape.D, shape.FF, shape.Hq * shape.HD, (shape.Hq + 2 * shape.Hkv) * shape.HD
+    layers = []
+    for _ in range(shape.n_layers):
+        L = {}
+        for name, (M, K) in (("wqkv", (QKV, D)), ("wo", (D, QD)), ("wg", (FF, D)), ("wu", (FF, D)),
+                             ("wd", (D, FF))):
+            q = rng.integers(-127, 128, (M, K), dtype=np.int8)
+            s = round_bits(np.full((M, K // GROUP), 0.02 * 3 / 127, np.float32))
+            L[name + "_q"], L[name + "_s"] = q, s
+        for name, n in (("norm1", D), ("norm2", D), ("qn", shape.HD), ("kn", shape.HD)):
+            L[name] = rnd(1 + 0.1 * rng.standard_normal(n).astype(np.float32))
+        layers.append(L)
+    w = {"layers": layers, "final_norm": rnd(1 + 0.1 * rng.standard_normal(D).astype(np.float32)),
+         "embed": rnd(0.02 * rng.standard_normal((shape.V, D)).astype(np.float32))}
+    max_seq = args.prompt + 8
+    kv = rnd(rng.standard_normal((shape.n_layers, shape.Hkv, max_seq, 2, shape.HD)).astype(np.float32))
+    orc = OracleQwen3(shape, w, max_seq)
+    orc.kv[...] = kv
+    pos = args.prompt
+    # one step = one layer of a token, or the final norm + lm_head + argmax (step n_layers)
+    times = {"layer": [], "head": []}
+    x = orc.embed(1)
+
+    def step(i):
+        nonlocal x
+        t0 = time.perf_counter()
+        j = i % (shape.n_layers + 1)
+        if j < shape.n_layers:
+            x = orc.layer(j, x, pos)
+            return "layer", time.perf_counter() - t0
+        xf = ops.rms_norm_ref(x.reshape(1, -1), w["final_norm"], weighted=True, eps=shape.eps).reshape(-1)
+        tok = int(np.argmax(ops.gemv_bf16(w["embed"], xf)))
+        x = orc.embed(tok)
+        return "head", time.perf_counter() - t0
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        kind, dt = step(args.warmup + i)
+        times[kind].append(dt)
+    elapsed = time.perf_counter() - t0
+    lay = statistics.mean(times["layer"]) if times["layer"] else elapsed / max(1, args.steps)
+    head = statistics.mean(times["head"]) if times["head"] else lay * 1.1
+    tps = 1.0 / (lay * shape.n_layers + head)
+    sample = (f"{args.steps} steps of one decoder layer (or the final norm + bf16 lm_head + argmax) at "
+              f"position {pos}; tokens/s = 1/(28*mean layer time + head time); weights synthetic int8 g{GROUP}")
+    line = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * elapsed / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xbf16",
+            "data": "synthetic", "config": workload(args), "impl": "reference",
+            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from iron_b200.qwen3 import Qwen3B200, Qwen3Config, Qwen3Weights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = Qwen3Config.qwen3_0_6b()
+    K, W = args.steps, args.warmup
+    max_seq = (args.prompt + W + 2 * K + 8 + 63) // 64 * 64
+    w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
+    dec = Qwen3B200(w, max_seq=max_seq, device=dev)
+    g = torch.Generator().manual_seed(args.seed + 1000 * rank)
+    prompt = torch.randint(0, cfg.V, (args.prompt,), generator=g).tolist()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                          if "CUDA_VISIBLE_DEVICES" in os.environ and world == 1 else local_rank)
+    clocks.start()
+    # prefill, token by token through the decode step (qwen3_0.6b/check_cosine_int8.py:51-52)
+    t_pre = time.perf_counter()
+    for p, t in enumerate(prompt):
+        nxt = dec.step_tokens([t], p)
+    prefill_s = time.perf_counter() - t_pre
+    pos = args.prompt
+    dec.set_position(pos)
+    with torch.cuda.stream(dec.stream):
+        dec.tok.copy_(nxt.to(dev))
+    for _ in range(W):
+        dec.run_step(from_tokens=True, advance=True)
+    pos += W
+    # ---- timed region: K back-to-back decode steps, device-resident inputs ----
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(dec.stream)
+    for _ in range(K):
+        dec.run_step(from_tokens=True, advance=True)
+    e1.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    pos += K
+    t_ms = e0.elapsed_time(e1)
+    # ---- e2e: public API per step (H2D token+position, D2H token) ----
+    tok = int(dec.tok[0])
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e2.record(dec.stream)
+    last_in, last_pos = tok, pos
+    for _ in range(K):
+        last_in, last_pos = tok, pos
+        tok = int(dec.step_tokens([tok], pos)[0])
+        pos += 1
+    e3.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2.elapsed_time(e3)
+    clocks.stop()
+    clk = clocks.summary()
+    # ---- dominant kernel: the bf16 lm_head GEMV + argmax, timed on the decoder stream ----
+    lm_ms = dec.time_lm_head(reps=20)
+    lm_bytes = cfg.V * cfg.D * 2 + cfg.D * 2  # algorithmic bytes: the bf16 weight stream + x
+    # ---- aggregate over ranks ----
+    tt = torch.tensor([t_ms, e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms = float(tt[0]), float(tt[1])
+    value = world * K / (t_ms / 1000.0)
+    e2e = world * K / (e2e_ms / 1000.0)
+    if rank != 0:
+        return
+    from iron_b200 import _lib  # noqa: F401
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = lm_bytes / (lm_ms / 1000.0) / 1e9
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xbf16", "data": "synthetic", "config": workload(args),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": K * dec.launches_per_step(),
+            "roofline": {"bound": "hbm", "kernel": "gemv_bf16_kernel (lm_head 151936x1024 + argmax)",
+                         "achieved": achieved, "peak": peak,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+            "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+            "prefill_s": prefill_s}
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle.qwen3 import Qwen3Shape
+        wnp = w.to_numpy()
+        kvnp = dec.kv.float().cpu().numpy().reshape(cfg.n_layers, cfg.Hkv, max_seq, 2, cfg.HD)
+        threads = len(os.sched_getaffinity(0))
+        # the oracle reproduces the GPU's last token from the same state (parity spot check)
+        ptok = last_pos
+        tps, used, logits = cpu_sample(wnp, kvnp, Qwen3Shape(group=GROUP), ptok, last_in,
+                                       args.cpu_tokens, threads)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": used, "kind": "port",
+                                "sample": f"{args.cpu_tokens} full decode tokens (28 layers + bf16 lm_head) of "
+                                          f"the numpy oracle at position {ptok} on this run's weights and KV cache"}
+        import numpy as np
+        line["oracle_spot_check"] = {"position": ptok, "input_token": last_in,
+                                     "gpu_token": tok, "oracle_token": int(np.argmax(logits))}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

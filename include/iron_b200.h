@@ -1,0 +1,177 @@
+/*
+ * iron_b200 C ABI -- B200 (sm_100a) kernels for the Qwen3 decode hot path of IRON.
+ *
+ * Conventions (every entry point):
+ *   - Pointers are DEVICE pointers owned by the caller (e.g. torch tensors'
+ *     data_ptr()).  bf16 data is passed as uint16_t bit patterns.
+ *   - `stream` is a cudaStream_t (or NULL for the legacy default stream) passed
+ *     as void*.  Every launch is asynchronous on that stream.
+ *   - Return 0 on success, a negative IRON_ERR_* code on failure; the message is
+ *     available from iron_last_error() (thread-local).  No entry point
+ *     allocates device memory; scratch space ("workspace") is caller-provided,
+ *     sized by the matching *_workspace_bytes() query.
+ *   - Runtime parameters that change between CUDA-graph replays (positions,
+ *     KV lengths) are read from device memory when the *_dev pointer is non-NULL.
+ *
+ * int8 weight wire (IRON's int8 tile wire, gemv_int8/reference.py:59-80 and
+ * qwen3_npu_int8.py:381-436): rows are grouped in tiles of `tile_m` rows, each
+ * tile stored as [tile_m*K int8 payload | tile_m*(K/group) bf16 scales].  Tiles
+ * are grouped into per-core windows of `rows_per_core` rows stored as
+ * `tiles_per_core` tiles (a window may carry trailing pad tiles, the fuse_o Wo
+ * wire of swiglu_mlp_dp/op_ours.py:357-421).  The plain wire has
+ * rows_per_core = M and tiles_per_core = M / tile_m.  The native layout of this
+ * library is tile_m = 1 (row-interleaved [K int8 | K/group bf16]).
+ * domain: 0 = signed two's complement q, 1 = biased q + 128 (mv_int8.cc).
+ * Every row start must be 16-byte aligned.
+ */
+#ifndef IRON_B200_H
+#define IRON_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IRON_OK 0
+#define IRON_ERR_ARG (-1)      /* invalid argument / shape */
+#define IRON_ERR_ALIGN (-2)    /* pointer or stride misaligned */
+#define IRON_ERR_CUDA (-3)     /* CUDA launch / runtime error */
+#define IRON_ERR_UNSUPPORTED (-4)
+#define IRON_ERR_TIMEOUT (-5)  /* a bounded device-side wait gave up */
+
+/* ---- library ---------------------------------------------------------- */
+/* Version string of the library. */
+const char* iron_version(void);
+/* Copy the calling thread's last error message into buf (NUL-terminated); returns its length. */
+int iron_last_error(char* buf, int buflen);
+
+/* ---- int8 group-dequant GEMV (W8A16) -------------------------------------
+ * y[b, m] = bf16( sum_k q[m,k] * s[m, k/group] * x[b, k] )           (epilogue 0)
+ * y[b, m] = bf16( r[b, m] + bf16(sum ...) )                          (epilogue 1, residual)
+ * Replaces GEMVInt8 (iron/operators/gemv_int8/op.py:20-178), kernel
+ * matvec_vectorized_int8_bf16 (aie_kernels/aie2p/mv_int8_signed.cc:103-115,
+ * biased: mv_int8.cc:60-114).  batch: 1..8 activation rows sharing the weight.
+ * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.
+ */
+int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
+                    int rows_per_core, int tiles_per_core, int domain,
+                    const uint16_t* x, int batch, const uint16_t* residual,
+                    uint16_t* y, void* stream);
+
+/* Dequantise a wire to float32 q*s (exact), row-major (M, K).  Test/inspection
+ * entry point for the bit-exact dequant check (GEMVInt8.reference, op.py:173-178). */
+int iron_dequant_w8(const void* wire, int M, int K, int group, int tile_m,
+                    int rows_per_core, int tiles_per_core, int domain,
+                    float* out, void* stream);
+
+/* Symmetric per-(row, group) RTN int8 quantiser + packer into the plain wire.
+ * w: bf16 (M, K) row-major.  Bit-exact with Qwen3NPU._set_int8_rtn
+ * (qwen3_npu_int8.py:457-491): s = bf16(absmax/127) (s = 1 for an all-zero
+ * group), q = clamp(rint(w / s), -127, 127). */
+int iron_quantize_rtn(const uint16_t* w, int M, int K, int group, int tile_m, int domain,
+                      void* wire_out, void* stream);
+
+/* ---- bf16 GEMV ------------------------------------------------------------
+ * y[b, m] = bf16( sum_k A[m, k] * x[b, k] )  (f32 accumulation).
+ * independent != 0: `batch` independent GEMVs, A[b] (M, K) each (the num_batches
+ * mode of iron/operators/gemv/op.py:151-157).  Replaces GEMV (gemv/op.py:20-163,
+ * kernel aie_kernels/generic/mv.cc:47-90). */
+int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
+                   int independent, uint16_t* y, void* stream);
+
+/* lm_head GEMV fused with a greedy argmax over the bf16-rounded logits (ties ->
+ * lowest index, as numpy.argmax in qwen3_npu_int8.py:619-620).  logits may be
+ * NULL (not stored).  token_out: int32[batch].  workspace: iron_argmax_workspace_bytes(). */
+int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
+                             uint16_t* logits, int32_t* token_out, void* workspace,
+                             void* stream);
+int iron_lm_head_w8_argmax(const void* wire, int M, int K, int group, const uint16_t* x,
+                           int batch, uint16_t* logits, int32_t* token_out, void* workspace,
+                           void* stream);
+int64_t iron_argmax_workspace_bytes(int batch);
+/* Greedy argmax over bf16 rows: token_out[b] = argmax_m logits[b, m]. */
+int iron_argmax_bf16(const uint16_t* logits, int M, int batch, int32_t* token_out,
+                     void* workspace, void* stream);
+
+/* ---- RMSNorm / elementwise ---------------------------------------------------
+ * y = bf16(x * rsqrt(mean(x^2) + eps) [* w]) per row of `cols`; f32 math
+ * (aie_kernels/aie2p/rms_norm.cc:9-53; op iron/operators/rms_norm/op.py:20-130). */
+int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
+                 float eps, void* stream);
+/* c = bf16(a + b)   (iron/operators/elementwise_add/op.py, aie_kernels/generic/add.cc) */
+int iron_add(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream);
+/* c = bf16(a * b)   (iron/operators/elementwise_mul/op.py, aie_kernels/generic/mul.cc) */
+int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream);
+/* y = bf16(silu(x)); mode 0: x*sigmoid(x) in f32 (silu/reference.py:8-10),
+ * mode 1: the tanh form with bf16 roundings (aie_kernels/aie2p/silu.cc). */
+int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream);
+/* out[i, :] = table[ids[i], :]  (token embedding gather, bf16 rows of D). */
+int iron_embedding(const uint16_t* table, const int32_t* ids, int n, int D, uint16_t* out,
+                   void* stream);
+
+/* Advance the device-resident decode positions by one token for `batch` streams:
+ * pos += 1; seq_len = pos + 1; kv_off = pos * 2 * HD (the host-side per-token
+ * parameter writes of qwen3_npu_int8.py:600-610, done on the device so a
+ * captured decode step can be replayed back to back). */
+int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int batch, int HD,
+                        void* stream);
+
+/* ---- fused QKV head ------------------------------------------------------------
+ * QKVHeadDataParallelOurs (iron/operators/qkv_head_dp/op_ours.py:31-262; golden
+ * qkv_head_dp/reference.py:13-33): hn = RMSNorm_w(cur, n_in); raw = bf16(Wqkv@hn);
+ * q,k = RoPE(RMSNorm_w(head, n_qn|n_kn), ang); v = raw.  q -> q_out (Hq*HD);
+ * K_t,V_t -> kv_cache.  `batch` independent streams: cur (batch, D), q_out
+ * (batch, Hq*HD), kv_cache (batch, Hkv, 2*max_seq*HD).
+ * kv layout: per KV head a region of 2*max_seq*HD bf16 holding per-token
+ * [K_t | V_t] (the KV_TOKEN_INTERLEAVED layout, decode_attn.cc:92-99).  K_t is
+ * written at element offset kv_off of every head region and V_t at kv_off + HD
+ * (kv_off = seq_pos*2*HD, the k_cache_offset parameter of qwen3_npu_int8.py:600,
+ * 608); kv_off_dev (int32[batch]) overrides kv_off when non-NULL.
+ * ang_is_table = 0: ang holds one interleaved [cos, sin, ...] row of HD per stream;
+ * 1: ang is a (max_seq, HD) table and the row kv_off/(2*HD) is used.
+ * raw_ws: bf16 workspace of batch*(Hq+2*Hkv)*HD elements. */
+int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const void* wqkv_wire, int group,
+                  int tile_m, int domain, const uint16_t* n_qn, const uint16_t* n_kn,
+                  const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv_cache,
+                  int D, int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
+                  const int32_t* kv_off_dev, float eps, uint16_t* raw_ws, void* stream);
+
+/* ---- decode attention ---------------------------------------------------------
+ * GQA single-query attention per stream over positions [0, seq_len), base-2
+ * softmax with scale log2(e)/sqrt(HD) (decode_attn/reference.py:26-38; kernels
+ * aie_kernels/aie2p/decode_attn.cc:117-311; op decode_attn/op.py:20-181).
+ * q (batch, H, HD); kv per stream per KV head (2*max_seq*HD): kv_layout
+ * 0 = per-token [K_t | V_t] (kv_token_interleaved, decode_attn/op.py:49-52),
+ * 1 = [K half | V half] (the combined arg of decode_attn/reference.py:74-93),
+ * 2 = [K_block | V_block] per block_kv tokens (decode_attn.cc:95-97).  seq_lens_dev (int32[batch]) overrides
+ * seq_len when non-NULL (ragged streams).  Split-KV flash decoding: partial
+ * (m, l, o) per split in `workspace`, merged by a second pass. */
+int64_t iron_decode_attn_workspace_bytes(int batch, int H, int HD, int max_seq);
+int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t* out, int batch, int H,
+                     int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
+                     const int32_t* seq_lens_dev, void* workspace, int64_t workspace_bytes,
+                     void* stream);
+
+/* ---- fused SwiGLU MLP block ---------------------------------------------------
+ * SwiGLUMLPDataParallelOurs (iron/operators/swiglu_mlp_dp/op_ours.py:47-582;
+ * golden swiglu_mlp_dp/test.py:79-91, reference.py:8-67):
+ *   a  = bf16(Wo @ cx)            (fuse_o; else a is an input of D)
+ *   x1 = bf16(cur + a)
+ *   hf = bf16(RMSNorm_w(x1, n_pf))
+ *   gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf))
+ *   nxt = bf16(x1 + bf16(Wd@gh))
+ * Wires are described like iron_gemv_w8a16 (tile_m, rows_per_core, tiles_per_core).
+ * x1_ws (batch*D) and gh_ws (batch*FF) are bf16 workspaces (the reference's
+ * a_scratch / gh_scratch round-trip buffers). */
+int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, const uint16_t* n_pf,
+                   const void* wo, int wo_tile_m, int wo_rows_per_core, int wo_tiles_per_core,
+                   const void* wg, const void* wu, int gu_tile_m, const void* wd, int d_tile_m,
+                   int group, int domain, uint16_t* x1_ws, uint16_t* gh_ws, uint16_t* nxt,
+                   int D, int FF, int QD, int batch, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRON_B200_H */

@@ -1,0 +1,91 @@
+"""ctypes binding of ``libiron_b200.so`` (the C ABI declared in ``include/iron_b200.h``).
+
+There is no fallback: if the library is missing or a call fails, an exception
+is raised.  ``lib()`` loads the in-tree library once per process.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libiron_b200.so"
+
+P = C.c_void_p
+I = C.c_int
+I64 = C.c_int64
+F = C.c_float
+
+# name -> (restype, argtypes); mirrors include/iron_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "iron_version": (C.c_char_p, []),
+    "iron_last_error": (I, [C.c_char_p, I]),
+    "iron_gemv_w8a16": (I, [P, I, I, I, I, I, I, I, P, I, P, P, P]),
+    "iron_dequant_w8": (I, [P, I, I, I, I, I, I, I, P, P]),
+    "iron_quantize_rtn": (I, [P, I, I, I, I, I, P, P]),
+    "iron_gemv_bf16": (I, [P, I, I, P, I, I, P, P]),
+    "iron_lm_head_bf16_argmax": (I, [P, I, I, P, I, P, P, P, P]),
+    "iron_lm_head_w8_argmax": (I, [P, I, I, I, P, I, P, P, P, P]),
+    "iron_argmax_workspace_bytes": (I64, [I]),
+    "iron_argmax_bf16": (I, [P, I, I, P, P, P]),
+    "iron_rmsnorm": (I, [P, P, P, I, I, F, P]),
+    "iron_add": (I, [P, P, P, I64, P]),
+    "iron_mul": (I, [P, P, P, I64, P]),
+    "iron_silu": (I, [P, P, I64, I, P]),
+    "iron_embedding": (I, [P, P, I, I, P, P]),
+    "iron_decode_advance": (I, [P, P, P, I, I, P]),
+    "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, P, P]),
+    "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),
+    "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
+    "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),
+}
+
+_LIB = None
+
+
+class IronError(RuntimeError):
+    """A non-zero status from the iron_b200 C ABI."""
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m iron_b200.build` (needs nvcc)")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    lib().iron_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def call(name: str, *args) -> int:
+    """Call an ABI function; raise IronError on a negative status."""
+    rc = getattr(lib(), name)(*args)
+    if rc < 0:
+        raise IronError(f"{name} failed ({rc}): {last_error()}")
+    return rc
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None -> NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("iron_b200 kernels take CUDA tensors (got a CPU tensor)")
+    return t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream

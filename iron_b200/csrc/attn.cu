@@ -1,0 +1,240 @@
+// Decode attention: split-KV flash decoding over a GQA KV cache.
+//
+// Pass 1: grid (split, kv_head, stream).  Each CTA owns one KV head of one
+// stream and a contiguous slice of its positions; its 4 warps take positions
+// round-robin.  A lane holds HD/32 consecutive dims of every query head of the
+// GQA group (so a K or V row is one coalesced 8-byte-per-lane load), q.k is a
+// warp butterfly sum, and each warp keeps a base-2 online softmax state
+// (m, l, o) per head -- the streaming form of decode_attn.cc:208-279.  The
+// warps merge in shared memory and the CTA writes one partial per head.
+// Pass 2: grid (head, stream) merges the splits: M = max m_s,
+// o = sum o_s 2^(m_s-M) / sum l_s 2^(m_s-M)  (decode_attn/reference.py:26-38).
+#include "common.cuh"
+
+namespace iron {
+
+struct AttnParams {
+  const uint16_t* q;     // [batch][H][HD]
+  const uint16_t* kv;    // per stream, per kv head: 2*max_seq*HD
+  float* ws;             // [batch][H][nsplit][HD + 2]
+  int H, KV, max_seq, layout, block_kv, seq_len, nsplit;
+  const int32_t* seq_lens;
+  float scale;           // log2(e)/sqrt(HD)
+};
+
+template <int HD, int GQ>
+__global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
+  constexpr int PER = HD / 32;
+  constexpr int U = 4;  // positions per warp iteration
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int L = p.seq_lens ? p.seq_lens[b] : p.seq_len;
+  L = L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
+  const int chunk = (L + p.nsplit - 1) / p.nsplit;
+  const int start = split * chunk;
+  const int end = min(L, start + chunk);
+
+  float q[GQ][PER];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    const uint16_t* qs = p.q + ((size_t)b * p.H + kvh * GQ + h) * HD + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) q[h][e] = bf2f(qs[e]);
+  }
+  const uint16_t* head = p.kv + ((size_t)b * p.KV + kvh) * 2 * (size_t)p.max_seq * HD;
+  // element offsets of K_j / V_j inside the head region for the three layouts
+  auto koff = [&](int j) -> size_t {
+    if (p.layout == 0) return (size_t)j * 2 * HD;
+    if (p.layout == 1) return (size_t)j * HD;
+    const int bk = j / p.block_kv, jj = j - bk * p.block_kv;
+    return ((size_t)bk * 2 * p.block_kv + jj) * HD;
+  };
+  const size_t voff = p.layout == 0 ? HD : (p.layout == 1 ? (size_t)p.max_seq * HD : (size_t)p.block_kv * HD);
+
+  float m[GQ], l[GQ], o[GQ][PER];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) o[h][e] = 0.f;
+  }
+
+  for (int j0 = start + wid * U; j0 < end; j0 += 4 * U) {
+    float kf[U][PER], vf[U][PER];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = min(j0 + u, end - 1);
+      const uint16_t* kr = head + koff(j) + lane * PER;
+      const uint16_t* vr = kr + voff;
+      if constexpr (PER == 4) {
+        const uint2 kk = ldg_stream8(kr), vv = ldg_stream8(vr);
+        kf[u][0] = bf_lo(kk.x);
+        kf[u][1] = bf_hi(kk.x);
+        kf[u][2] = bf_lo(kk.y);
+        kf[u][3] = bf_hi(kk.y);
+        vf[u][0] = bf_lo(vv.x);
+        vf[u][1] = bf_hi(vv.x);
+        vf[u][2] = bf_lo(vv.y);
+        vf[u][3] = bf_hi(vv.y);
+      } else {
+        static_assert(PER == 2, "head_dim 64 or 128");
+        const uint32_t kk = __ldg((const uint32_t*)kr), vv = __ldg((const uint32_t*)vr);
+        kf[u][0] = bf_lo(kk);
+        kf[u][1] = bf_hi(kk);
+        vf[u][0] = bf_lo(vv);
+        vf[u][1] = bf_hi(vv);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      float s[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) d = fmaf(q[h][e], kf[u][e], d);
+        s[u] = warp_sum(d) * p.scale;
+        if (j0 + u >= end) s[u] = -INFINITY;
+      }
+      float mn = m[h];
+#pragma unroll
+      for (int u = 0; u < U; ++u) mn = fmaxf(mn, s[u]);
+      const float corr = exp2f(m[h] - mn);
+      float ls = l[h] * corr;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) o[h][e] *= corr;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float pu = exp2f(s[u] - mn);
+        ls += pu;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) o[h][e] = fmaf(pu, vf[u][e], o[h][e]);
+      }
+      l[h] = ls;
+      m[h] = mn;
+    }
+  }
+
+  // merge the 4 warps
+  __shared__ float sm_m[4][GQ], sm_l[4][GQ];
+  __shared__ float sm_o[4][GQ][HD];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    if (lane == 0) {
+      sm_m[wid][h] = m[h];
+      sm_l[wid][h] = l[h];
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) sm_o[wid][h][lane * PER + e] = o[h][e];
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < GQ * HD; t += blockDim.x) {
+    const int h = t / HD, d = t - h * HD;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w][h]);
+    float oo = 0.f, ll = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm_m[w][h] - M);
+        oo = fmaf(sm_o[w][h][d], f, oo);
+        ll = fmaf(sm_l[w][h], f, ll);
+      }
+    }
+    float* dst = p.ws + (((size_t)b * p.H + kvh * GQ + h) * p.nsplit + split) * (HD + 2);
+    dst[d] = oo;
+    if (d == 0) {
+      dst[HD] = M;
+      dst[HD + 1] = ll;
+    }
+  }
+}
+
+template <int HD>
+__global__ void attn_combine_kernel(const float* ws, int H, int nsplit, uint16_t* out) {
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const float* src = ws + ((size_t)b * H + h) * nsplit * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, src[s * (HD + 2) + HD]);
+  float oo = 0.f, ll = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < nsplit; ++s) {
+      const float* ps = src + s * (HD + 2);
+      const float f = exp2f(ps[HD] - M);
+      oo = fmaf(ps[d], f, oo);
+      ll = fmaf(ps[HD + 1], f, ll);
+    }
+  }
+  out[((size_t)b * H + h) * HD + d] = f2bf(ll > 0.f ? oo / ll : 0.f);
+}
+
+static int nsplit_cap(int max_seq) {
+  int n = (max_seq + 63) / 64;
+  return n < 1 ? 1 : (n > 256 ? 256 : n);
+}
+
+template <int HD, int GQ>
+static void launch_split(const AttnParams& p, int batch, cudaStream_t st) {
+  dim3 g(p.nsplit, p.KV, batch);
+  attn_split_kernel<HD, GQ><<<g, 128, 0, st>>>(p);
+}
+
+}  // namespace iron
+
+using namespace iron;
+
+extern "C" int64_t iron_decode_attn_workspace_bytes(int batch, int H, int HD, int max_seq) {
+  return (int64_t)batch * H * nsplit_cap(max_seq) * (HD + 2) * 4;
+}
+
+extern "C" int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t* out, int batch, int H,
+                                int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
+                                const int32_t* seq_lens_dev, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
+  IRON_REQUIRE(q && kv && out && workspace, IRON_ERR_ARG, "decode_attn: null pointer");
+  IRON_REQUIRE(batch >= 1 && KV >= 1 && H % KV == 0 && max_seq >= 1, IRON_ERR_ARG,
+               "decode_attn: bad shape batch=%d H=%d KV=%d max_seq=%d", batch, H, KV, max_seq);
+  IRON_REQUIRE(kv_layout >= 0 && kv_layout <= 2, IRON_ERR_ARG, "decode_attn: kv_layout must be 0, 1 or 2");
+  IRON_REQUIRE(kv_layout != 2 || (block_kv > 0 && max_seq % block_kv == 0), IRON_ERR_ARG,
+               "decode_attn: block layout needs block_kv dividing max_seq");
+  IRON_REQUIRE(seq_lens_dev || (seq_len >= 1 && seq_len <= max_seq), IRON_ERR_ARG,
+               "decode_attn: seq_len %d not in [1, %d]", seq_len, max_seq);
+  IRON_REQUIRE(workspace_bytes >= iron_decode_attn_workspace_bytes(batch, H, HD, max_seq), IRON_ERR_ARG,
+               "decode_attn: workspace of %lld bytes is too small", (long long)workspace_bytes);
+  IRON_REQUIRE(iron_aligned(kv, 8) && iron_aligned(q, 4), IRON_ERR_ALIGN, "decode_attn: kv must be 8-byte aligned");
+  AttnParams p;
+  p.q = q;
+  p.kv = kv;
+  p.ws = (float*)workspace;
+  p.H = H;
+  p.KV = KV;
+  p.max_seq = max_seq;
+  p.layout = kv_layout;
+  p.block_kv = block_kv;
+  p.seq_len = seq_len;
+  p.seq_lens = seq_lens_dev;
+  p.scale = 1.4426950408889634f / sqrtf((float)HD);
+  const int target = 4 * iron_num_sms();
+  int ns = (target + batch * KV - 1) / (batch * KV);
+  const int cap = nsplit_cap(seq_lens_dev ? max_seq : seq_len);
+  ns = ns < 1 ? 1 : (ns > cap ? cap : ns);
+  p.nsplit = ns;
+  const int GQ = H / KV;
+  cudaStream_t st = (cudaStream_t)stream;
+#define IRON_ATTN_CASE(hd, gq) \
+  if (HD == hd && GQ == gq) { launch_split<hd, gq>(p, batch, st); goto combine; }
+  IRON_ATTN_CASE(128, 1) IRON_ATTN_CASE(128, 2) IRON_ATTN_CASE(128, 4) IRON_ATTN_CASE(128, 8)
+  IRON_ATTN_CASE(64, 1) IRON_ATTN_CASE(64, 2) IRON_ATTN_CASE(64, 4) IRON_ATTN_CASE(64, 8)
+#undef IRON_ATTN_CASE
+  return iron_set_error(IRON_ERR_UNSUPPORTED, "decode_attn: head_dim %d / GQA group %d unsupported", HD, GQ);
+combine : {
+  int rc = iron_check_launch("attn_split_kernel");
+  if (rc) return rc;
+  dim3 g(H, batch);
+  if (HD == 128)
+    attn_combine_kernel<128><<<g, 128, 0, st>>>(p.ws, H, ns, out);
+  else
+    attn_combine_kernel<64><<<g, 64, 0, st>>>(p.ws, H, ns, out);
+  return iron_check_launch("attn_combine_kernel");
+}
+}

@@ -1,0 +1,185 @@
+// RMSNorm, elementwise ops, embedding gather and the per-head q/k-norm + RoPE +
+// KV-cache epilogue of the fused QKV head.
+#include "common.cuh"
+
+namespace iron {
+
+// one CTA per row; float32 math, one bf16 rounding (aie_kernels/aie2p/rms_norm.cc:9-53)
+__global__ void rmsnorm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* y, int cols, float eps) {
+  __shared__ float red[32];
+  const uint16_t* xr = x + (size_t)blockIdx.x * cols;
+  uint16_t* yr = y + (size_t)blockIdx.x * cols;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = bf2f(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = rms_inv(ss, cols, eps);
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    float v = bf2f(xr[i]) * inv;
+    if (w) v *= bf2f(w[i]);
+    yr[i] = f2bf(v);
+  }
+}
+
+__global__ void eltwise_kernel(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, int op) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = bf2f(a[i]);
+    float r;
+    if (op == 0) {
+      r = x + bf2f(b[i]);
+    } else if (op == 1) {
+      r = x * bf2f(b[i]);
+    } else if (op == 2) {
+      r = x / (1.0f + expf(-x));
+    } else {
+      r = silu_tanh_bf16(x);
+    }
+    c[i] = f2bf(r);
+  }
+}
+
+__global__ void embedding_kernel(const uint16_t* table, const int32_t* ids, int D, uint16_t* out) {
+  const int i = blockIdx.x;
+  const uint16_t* src = table + (size_t)ids[i] * D;
+  for (int k = threadIdx.x; k < D; k += blockDim.x) out[(size_t)i * D + k] = src[k];
+}
+
+// Per-head epilogue of the fused QKV head (qkv_head_dp/reference.py:29-33).
+// grid (Hq + Hkv, batch), one warp per head.  q heads: RMSNorm_w(n_qn) -> RoPE ->
+// q_out.  kv heads: RMSNorm_w(n_kn) -> RoPE -> K_t, and V_t = raw v, both written
+// to the cache at the stream's position.
+template <int HD>
+__global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
+                                       const uint16_t* ang, int ang_is_table, uint16_t* q_out,
+                                       uint16_t* kv, int Hq, int Hkv, int max_seq, int kv_off,
+                                       const int32_t* kv_off_dev, float eps) {
+  constexpr int PER = HD / 32;
+  const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+  const int QKV = (Hq + 2 * Hkv) * HD;
+  const int off = kv_off_dev ? kv_off_dev[b] : kv_off;  // element offset of K_t in a head region
+  const bool isq = head < Hq;
+  const uint16_t* src = raw + (size_t)b * QKV + (size_t)head * HD;
+  const uint16_t* nw = isq ? n_qn : n_kn;
+  const uint16_t* a = ang + (size_t)(ang_is_table ? off / (2 * HD) : b) * HD;
+  // lane owns element pairs (i, i + HD/2) for i = lane + 32*j, j < PER/2
+  float v[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER / 2; ++j) {
+    const int i = lane + 32 * j;
+    v[2 * j] = bf2f(src[i]);
+    v[2 * j + 1] = bf2f(src[i + HD / 2]);
+    ss = fmaf(v[2 * j], v[2 * j], ss);
+    ss = fmaf(v[2 * j + 1], v[2 * j + 1], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = rms_inv(ss, HD, eps);
+  uint16_t o[PER];
+#pragma unroll
+  for (int j = 0; j < PER / 2; ++j) {
+    const int i = lane + 32 * j;
+    const float x1 = rbf(v[2 * j] * inv * bf2f(nw[i]));
+    const float x2 = rbf(v[2 * j + 1] * inv * bf2f(nw[i + HD / 2]));
+    const float c = bf2f(a[2 * i]), s = bf2f(a[2 * i + 1]);
+    // rope/reference.py:150-154: y1 = x1*c - x2*s, y2 = x2*c + x1*s (float32)
+    o[2 * j] = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+    o[2 * j + 1] = f2bf(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+  }
+  if (isq) {
+    uint16_t* dst = q_out + ((size_t)b * Hq + head) * HD;
+#pragma unroll
+    for (int j = 0; j < PER / 2; ++j) {
+      dst[lane + 32 * j] = o[2 * j];
+      dst[lane + 32 * j + HD / 2] = o[2 * j + 1];
+    }
+  } else {
+    const int kh = head - Hq;
+    uint16_t* dst = kv + ((size_t)b * Hkv + kh) * max_seq * 2 * HD + off;
+    const uint16_t* vsrc = raw + (size_t)b * QKV + (size_t)(Hq + Hkv + kh) * HD;
+#pragma unroll
+    for (int j = 0; j < PER / 2; ++j) {
+      dst[lane + 32 * j] = o[2 * j];
+      dst[lane + 32 * j + HD / 2] = o[2 * j + 1];
+    }
+    for (int i = lane; i < HD; i += 32) dst[HD + i] = vsrc[i];
+  }
+}
+
+int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
+                           const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
+                           int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
+                           const int32_t* kv_off_dev, float eps, cudaStream_t st) {
+  dim3 g(Hq + Hkv, batch);
+  if (HD == 128) {
+    qk_norm_rope_kv_kernel<128><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
+                                                   max_seq, kv_off, kv_off_dev, eps);
+  } else if (HD == 64) {
+    qk_norm_rope_kv_kernel<64><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
+                                                  max_seq, kv_off, kv_off_dev, eps);
+  } else {
+    return iron_set_error(IRON_ERR_UNSUPPORTED, "qkv head: head_dim %d (supported: 64, 128)", HD);
+  }
+  return iron_check_launch("qk_norm_rope_kv_kernel");
+}
+
+__global__ void decode_advance_kernel(int32_t* pos, int32_t* len, int32_t* off, int batch, int HD) {
+  const int b = threadIdx.x;
+  if (b < batch) {
+    const int p = pos[b] + 1;
+    pos[b] = p;
+    len[b] = p + 1;
+    off[b] = p * 2 * HD;
+  }
+}
+
+static int elt_grid(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  const int64_t cap = (int64_t)iron_num_sms() * 8;
+  return (int)(g < cap ? (g < 1 ? 1 : g) : cap);
+}
+
+}  // namespace iron
+
+using namespace iron;
+
+extern "C" int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
+                            float eps, void* stream) {
+  IRON_REQUIRE(x && y && rows > 0 && cols > 0, IRON_ERR_ARG, "rmsnorm: bad arguments");
+  rmsnorm_kernel<<<rows, cols >= 1024 ? 512 : 128, 0, (cudaStream_t)stream>>>(x, w, y, cols, eps);
+  return iron_check_launch("rmsnorm_kernel");
+}
+
+static int elt(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, int op, void* stream) {
+  IRON_REQUIRE(a && c && n >= 0 && (b || op >= 2), IRON_ERR_ARG, "eltwise: bad arguments");
+  if (n == 0) return IRON_OK;
+  eltwise_kernel<<<elt_grid(n), 256, 0, (cudaStream_t)stream>>>(a, b, c, n, op);
+  return iron_check_launch("eltwise_kernel");
+}
+
+extern "C" int iron_add(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream) {
+  return elt(a, b, c, n, 0, stream);
+}
+extern "C" int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream) {
+  return elt(a, b, c, n, 1, stream);
+}
+extern "C" int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream) {
+  IRON_REQUIRE(mode == 0 || mode == 1, IRON_ERR_ARG, "silu: mode must be 0 or 1");
+  return elt(x, nullptr, y, n, 2 + mode, stream);
+}
+extern "C" int iron_embedding(const uint16_t* table, const int32_t* ids, int n, int D, uint16_t* out,
+                              void* stream) {
+  IRON_REQUIRE(table && ids && out && n >= 0 && D > 0, IRON_ERR_ARG, "embedding: bad arguments");
+  if (n == 0) return IRON_OK;
+  embedding_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(table, ids, D, out);
+  return iron_check_launch("embedding_kernel");
+}
+
+extern "C" int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int batch, int HD,
+                                   void* stream) {
+  IRON_REQUIRE(pos && seq_len && kv_off && batch >= 1 && batch <= 1024, IRON_ERR_ARG,
+               "decode_advance: bad arguments");
+  decode_advance_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(pos, seq_len, kv_off, batch, HD);
+  return iron_check_launch("decode_advance_kernel");
+}

@@ -1,0 +1,316 @@
+"""Qwen3 decode runtime on the B200 (the counterpart of IRON's ``Qwen3NPU``).
+
+IRON's runtime (iron/applications/qwen3_0.6b/qwen3_npu_int8.py:129-621) packs
+int8 weights into tile wires, builds one OperatorSequence of
+``[QKV head, decode attention, fused MLP] x 28 + RMSNorm + lm_head`` and, per
+token, writes ``x``, the RoPE row, ``k_cache_offset`` and ``S_kv_eff`` then
+dispatches once and argmaxes the logits on the host.  Here the same chain is
+launched through the C ABI and captured in one CUDA graph per step shape; the
+positions live in device memory (advanced on the device after each step), the
+RoPE row is selected on the device from the angle table, and the greedy argmax
+runs in the lm_head epilogue, so a decode step needs no host traffic beyond
+the 4-byte token it returns.
+
+Weights use the native wire (row-interleaved ``[K int8 | K/G bf16]``, signed
+payload) with quant group ``group`` (32 by default, as BASELINE's configs).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import call as abi, ptr
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    D: int = 1024
+    FF: int = 3072
+    Hq: int = 16
+    Hkv: int = 8
+    HD: int = 128
+    V: int = 151936
+    n_layers: int = 28
+    eps: float = 1e-6
+    theta: float = 1e6
+
+    @property
+    def QD(self) -> int:
+        return self.Hq * self.HD
+
+    @property
+    def QKV(self) -> int:
+        return (self.Hq + 2 * self.Hkv) * self.HD
+
+    @classmethod
+    def qwen3_0_6b(cls):
+        return cls()
+
+    @classmethod
+    def qwen3_8b(cls):
+        return cls(D=4096, FF=12288, Hq=32, Hkv=8, HD=128, V=151936, n_layers=36)
+
+
+def wire_nbytes(M: int, K: int, group: int) -> int:
+    return M * (K + 2 * (K // group))
+
+
+def quantize_to_wire(w_bf16: torch.Tensor, group: int, tile_m: int = 1, domain: int = 0) -> torch.Tensor:
+    """RTN int8 quantise a (M, K) bf16 CUDA tensor into a plain wire (uint8 CUDA tensor)."""
+    M, K = w_bf16.shape
+    out = torch.empty(wire_nbytes(M, K, group), dtype=torch.uint8, device=w_bf16.device)
+    abi("iron_quantize_rtn", ptr(w_bf16.contiguous()), M, K, group, tile_m, domain, ptr(out),
+        _lib.stream_ptr())
+    return out
+
+
+def wire_to_numpy(wire: torch.Tensor, M: int, K: int, group: int):
+    """(q int8 (M,K), scale_bits uint16 (M,K/G)) host copies of a tile_m=1 signed wire."""
+    b = wire.cpu().numpy().reshape(M, K + 2 * (K // group))
+    return b[:, :K].view(np.int8).copy(), b[:, K:].copy().view(np.uint16)
+
+
+def rope_angle_table(max_seq: int, head_dim: int, theta: float) -> torch.Tensor:
+    """Interleaved half-dim [cos, sin] rows, bf16 (Qwen3NPU._precompute_rope_angles,
+    qwen3_npu_int8.py:580-591): float32 angles, cos/sin rounded to bf16."""
+    half = head_dim // 2
+    inv_freq = 1.0 / (theta ** (torch.arange(0, half, dtype=torch.float32) / half))
+    t = torch.arange(max_seq, dtype=torch.float32)
+    freqs = torch.outer(t, inv_freq)
+    cos = freqs.cos().to(torch.bfloat16)
+    sin = freqs.sin().to(torch.bfloat16)
+    return torch.stack([cos, sin], dim=-1).reshape(max_seq, head_dim)
+
+
+class Qwen3Weights:
+    """Device-resident Qwen3 weights in the native int8 wire (tile_m = 1, signed)."""
+
+    def __init__(self, cfg: Qwen3Config, group: int, layers: list, final_norm, embed, lm_wire=None):
+        self.cfg, self.group = cfg, group
+        self.layers, self.final_norm, self.embed, self.lm_wire = layers, final_norm, embed, lm_wire
+
+    @classmethod
+    def synthetic(cls, cfg: Qwen3Config, seed: int = 0, group: int = 32, device="cuda",
+                  int8_lm_head: bool = False, n_layers: int | None = None):
+        """Seeded synthetic weights with BASELINE's distributions: projection masters
+        N(0, 0.02) -> int8 RTN per group; RMSNorm weights 1 + N(0, 0.1); tied bf16
+        embedding N(0, 0.02)."""
+        g = torch.Generator(device=device).manual_seed(seed)
+        nl = cfg.n_layers if n_layers is None else n_layers
+
+        def randn(*shape, std=1.0, mean=0.0):
+            return (torch.randn(*shape, generator=g, device=device) * std + mean).to(torch.bfloat16)
+
+        def qw(M, K):
+            return quantize_to_wire(randn(M, K, std=0.02), group)
+
+        layers = []
+        for _ in range(nl):
+            L = {"norm1": randn(cfg.D, std=0.1, mean=1.0)}
+            L["wqkv"] = qw(cfg.QKV, cfg.D)
+            L["qn"] = randn(cfg.HD, std=0.1, mean=1.0)
+            L["kn"] = randn(cfg.HD, std=0.1, mean=1.0)
+            L["wo"] = qw(cfg.D, cfg.QD)
+            L["norm2"] = randn(cfg.D, std=0.1, mean=1.0)
+            L["wg"] = qw(cfg.FF, cfg.D)
+            L["wu"] = qw(cfg.FF, cfg.D)
+            L["wd"] = qw(cfg.D, cfg.FF)
+            layers.append(L)
+        final_norm = randn(cfg.D, std=0.1, mean=1.0)
+        embed = randn(cfg.V, cfg.D, std=0.02)
+        lm = quantize_to_wire(embed, group) if int8_lm_head else None
+        torch.cuda.synchronize()
+        return cls(cfg, group, layers, final_norm, embed, lm)
+
+    def weight_bytes(self) -> int:
+        per = sum(t.numel() * t.element_size() for t in self.layers[0].values())
+        return per * len(self.layers)
+
+    def to_numpy(self, n_layers: int | None = None) -> dict:
+        """Host copies in the layout of ``oracle.qwen3.OracleQwen3`` (test use)."""
+        c, G = self.cfg, self.group
+
+        def f(t):
+            return t.float().cpu().numpy()
+
+        out = {"layers": []}
+        for L in self.layers[:n_layers]:
+            d = {"norm1": f(L["norm1"]), "qn": f(L["qn"]), "kn": f(L["kn"]), "norm2": f(L["norm2"])}
+            for name, (M, K) in (("wqkv", (c.QKV, c.D)), ("wo", (c.D, c.QD)), ("wg", (c.FF, c.D)),
+                                 ("wu", (c.FF, c.D)), ("wd", (c.D, c.FF))):
+                d[name + "_q"], d[name + "_s"] = wire_to_numpy(L[name], M, K, G)
+            out["layers"].append(d)
+        out["final_norm"] = f(self.final_norm)
+        out["embed"] = f(self.embed)
+        if self.lm_wire is not None:
+            out["lm_q"], out["lm_s"] = wire_to_numpy(self.lm_wire, c.V, c.D, G)
+        return out
+
+
+class Qwen3B200:
+    """Greedy Qwen3 decoder over ``batch`` independent streams on one GPU.
+
+    ``__call__(x, seq_pos)`` keeps Qwen3NPU's interface (qwen3_npu_int8.py:594-621):
+    hidden state of the new token in, greedy token id out.  ``step_tokens`` feeds
+    token ids through the embedding; ``generate`` prefills a prompt token by token
+    (as check_cosine_int8.py:51-52 does) and then decodes greedily."""
+
+    def __init__(self, weights: Qwen3Weights, max_seq: int, batch: int = 1, lm_head: str = "bf16",
+                 use_graph: bool = True, keep_logits: bool = False, device="cuda"):
+        cfg = weights.cfg
+        self.cfg, self.w, self.max_seq, self.B = cfg, weights, max_seq, batch
+        if lm_head not in ("bf16", "int8"):
+            raise ValueError("lm_head must be 'bf16' or 'int8'")
+        if lm_head == "int8" and weights.lm_wire is None:
+            raise ValueError("int8 lm_head requested but the weights carry no lm_head wire")
+        if lm_head == "int8" or keep_logits:
+            keep_logits = True
+        self.lm_head, self.use_graph = lm_head, use_graph
+        dev = torch.device(device)
+        B, L = batch, len(weights.layers)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.x = torch.zeros(B, cfg.D, **bf)
+        self.xf = torch.zeros(B, cfg.D, **bf)
+        self.q = torch.zeros(B, cfg.QD, **bf)
+        self.raw = torch.zeros(B, cfg.QKV, **bf)
+        self.attn = torch.zeros(B, cfg.QD, **bf)
+        self.x1 = torch.zeros(B, cfg.D, **bf)
+        self.gh = torch.zeros(B, cfg.FF, **bf)
+        self.kv = torch.zeros(L, B, cfg.Hkv, 2 * max_seq * cfg.HD, **bf)
+        self.angles = rope_angle_table(max_seq, cfg.HD, cfg.theta).to(dev)
+        self.logits = torch.zeros(B, cfg.V, **bf) if keep_logits else None
+        # device params: token ids, positions, valid lengths, KV element offsets
+        self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.len = torch.ones(B, dtype=torch.int32, device=dev)
+        self.off = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.attn_ws = torch.empty(_lib.lib().iron_decode_attn_workspace_bytes(B, cfg.Hq, cfg.HD, max_seq),
+                                   dtype=torch.uint8, device=dev)
+        self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
+        self.host_in = torch.zeros(2 * B, dtype=torch.int32, pin_memory=True)
+        self.host_tok = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        self.stream = torch.cuda.Stream(device=dev)
+        self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
+
+    # ---- the step, as a flat list of ABI launches ----
+    def _launch_step(self, from_tokens: bool, advance: bool, st: int):
+        c, w, B = self.cfg, self.w, self.B
+        G = w.group
+        if from_tokens:
+            abi("iron_embedding", ptr(w.embed), ptr(self.tok), B, c.D, ptr(self.x), st)
+        for i, Lw in enumerate(w.layers):
+            kv = self.kv[i]
+            abi("iron_qkv_head", ptr(self.x), ptr(Lw["norm1"]), ptr(Lw["wqkv"]), G, 1, 0, ptr(Lw["qn"]),
+                ptr(Lw["kn"]), ptr(self.angles), 1, ptr(self.q), ptr(kv), c.D, c.HD, c.Hq, c.Hkv,
+                self.max_seq, B, 0, ptr(self.off), c.eps, ptr(self.raw), st)
+            abi("iron_decode_attn", ptr(self.q), ptr(kv), ptr(self.attn), B, c.Hq, c.Hkv, c.HD,
+                self.max_seq, 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
+            abi("iron_mlp_block", ptr(self.x), ptr(self.attn), 1, ptr(Lw["norm2"]), ptr(Lw["wo"]), 1, 0, 0,
+                ptr(Lw["wg"]), ptr(Lw["wu"]), 1, ptr(Lw["wd"]), 1, G, 0, ptr(self.x1), ptr(self.gh),
+                ptr(self.x), c.D, c.FF, c.QD, B, c.eps, st)
+        abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xf), B, c.D, c.eps, st)
+        if self.lm_head == "bf16":
+            abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xf), B, ptr(self.logits),
+                ptr(self.tok), ptr(self.argmax_ws), st)
+        else:
+            abi("iron_lm_head_w8_argmax", ptr(w.lm_wire), c.V, c.D, G, ptr(self.xf), B, ptr(self.logits),
+                ptr(self.tok), ptr(self.argmax_ws), st)
+        if advance:
+            abi("iron_decode_advance", ptr(self.pos), ptr(self.len), ptr(self.off), B, c.HD, st)
+
+    def launches_per_step(self, from_tokens: bool = True, advance: bool = True) -> int:
+        """Kernels one step launches: embedding, 7 per layer (QKV GEMV + head epilogue,
+        attention split + combine, O / gate-up / down GEMVs), final RMSNorm, lm_head
+        (+ argmax passes) and the position advance."""
+        head = 2 if self.lm_head == "bf16" else 3
+        return int(from_tokens) + 7 * len(self.w.layers) + 1 + head + int(advance)
+
+    def time_lm_head(self, reps: int = 20) -> float:
+        """Mean duration (ms) of the lm_head GEMV + argmax on the decoder stream."""
+        c, st = self.cfg, self.stream
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        args = (ptr(self.w.embed), c.V, c.D, ptr(self.xf), self.B, ptr(self.logits), ptr(self.tok),
+                ptr(self.argmax_ws), st.cuda_stream)
+        for _ in range(3):
+            abi("iron_lm_head_bf16_argmax", *args)
+        ev[0].record(st)
+        for _ in range(reps):
+            abi("iron_lm_head_bf16_argmax", *args)
+        ev[1].record(st)
+        st.synchronize()
+        return ev[0].elapsed_time(ev[1]) / reps
+
+    def run_step(self, from_tokens: bool = True, advance: bool = True):
+        """Enqueue one decode step on ``self.stream`` (graph replay when enabled)."""
+        st = self.stream
+        key = (from_tokens, advance)
+        with torch.cuda.stream(st):
+            if not self.use_graph:
+                self._launch_step(from_tokens, advance, st.cuda_stream)
+                return
+            g = self._graphs.get(key)
+            if g is None:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st):
+                    self._launch_step(from_tokens, advance, st.cuda_stream)
+                self._graphs[key] = g
+            g.replay()
+
+    def set_position(self, pos):
+        """Host write of the per-stream positions (int or sequence of B ints)."""
+        p = torch.as_tensor(pos, dtype=torch.int32).reshape(-1).expand(self.B).clone()
+        with torch.cuda.stream(self.stream):
+            self.pos.copy_(p.to(self.pos.device, non_blocking=False))
+            self.len.copy_(self.pos + 1)
+            self.off.copy_(self.pos * (2 * self.cfg.HD))
+
+    def reset(self):
+        self.kv.zero_()
+        self.set_position(0)
+
+    def __call__(self, x, seq_pos: int) -> int:
+        """Qwen3NPU.__call__: hidden state (D,) bf16 of the new token -> argmax token."""
+        if self.B != 1:
+            raise ValueError("__call__ is the batch-1 interface; use step_tokens for batches")
+        self.set_position(seq_pos)
+        with torch.cuda.stream(self.stream):
+            self.x[0].copy_(torch.as_tensor(x).to(torch.bfloat16).reshape(-1), non_blocking=False)
+        self.run_step(from_tokens=False, advance=False)
+        self.stream.synchronize()
+        return int(self.tok[0].item())
+
+    def step_tokens(self, tokens, pos) -> torch.Tensor:
+        """One step for B streams from token ids at positions ``pos`` -> next tokens (host)."""
+        self.set_position(pos)
+        with torch.cuda.stream(self.stream):
+            self.tok.copy_(torch.as_tensor(tokens, dtype=torch.int32).reshape(self.B).to(self.tok.device))
+        self.run_step(from_tokens=True, advance=False)
+        self.stream.synchronize()
+        return self.tok.cpu()
+
+    def generate(self, prompt, n_new: int) -> list:
+        """Prefill ``prompt`` (ids, batch 1) token by token, then greedy-decode ``n_new`` tokens.
+
+        The decode steps replay the captured step back to back: the device advances
+        the position and feeds each argmax token to the next step's embedding; the
+        tokens are gathered on the device and read back once."""
+        if self.B != 1:
+            raise ValueError("generate() is batch 1")
+        if len(prompt) + n_new > self.max_seq:
+            raise ValueError("prompt + new tokens exceed max_seq")
+        for p, t in enumerate(prompt):
+            self.step_tokens([t], p)
+        hist = torch.empty(n_new, dtype=torch.int32, device=self.tok.device)
+        self.set_position(len(prompt))
+        with torch.cuda.stream(self.stream):
+            hist[0].copy_(self.tok[0])
+        for i in range(1, n_new):
+            self.run_step(from_tokens=True, advance=True)
+            with torch.cuda.stream(self.stream):
+                hist[i].copy_(self.tok[0])
+        self.stream.synchronize()
+        return hist.cpu().tolist()

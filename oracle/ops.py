@@ -15,12 +15,28 @@ the reference file:line it restates.  Conventions:
 from __future__ import annotations
 
 import math
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
 from .bf16 import from_bits, rnd, round_bits
 
 F32 = np.float32
+
+_POOL: ThreadPoolExecutor | None = None
+_THREADS = 1
+
+
+def set_threads(n: int) -> int:
+    """Spread the row blocks of the int8 GEMV over ``n`` host threads (numpy releases
+    the GIL inside its array loops).  Returns the thread count in use."""
+    global _POOL, _THREADS
+    n = max(1, int(n))
+    if _POOL is not None:
+        _POOL.shutdown()
+    _POOL = ThreadPoolExecutor(n) if n > 1 else None
+    _THREADS = n
+    return n
 
 
 # ---------------------------------------------------------------------------
@@ -116,7 +132,7 @@ def dequant_f32(q, scale_bits):
 # GEMV
 # ---------------------------------------------------------------------------
 
-def gemv_int8_premul(q, scale_bits, x, chunk_rows: int = 8192):
+def gemv_int8_premul(q, scale_bits, x, chunk_rows: int = 0):
     """int8 GEMV with the kernel's premultiplied activations, float32 result.
 
     Restates ``gemv_int8/reference.py:25-40`` (the kernel of
@@ -132,12 +148,22 @@ def gemv_int8_premul(q, scale_bits, x, chunk_rows: int = 8192):
     m, k = q.shape
     g = k // s.shape[1]
     out = np.empty((xb.shape[0], m), np.float64)
-    for r0 in range(0, m, chunk_rows):
-        qs = q[r0:r0 + chunk_rows].astype(F32)
+    if chunk_rows <= 0:
+        chunk_rows = max(128, min(8192, -(-m // (4 * _THREADS))))
+
+    def block(r0):
+        qs = q[r0:r0 + chunk_rows].astype(np.float64)
         se = np.repeat(s[r0:r0 + chunk_rows], g, axis=1)
         for b in range(xb.shape[0]):
             xs = rnd(xb[b][None, :] * se)
-            out[b, r0:r0 + chunk_rows] = (qs.astype(np.float64) * xs).sum(axis=1)
+            out[b, r0:r0 + chunk_rows] = (qs * xs).sum(axis=1)
+
+    starts = range(0, m, chunk_rows)
+    if _POOL is not None and len(starts) > 1:
+        list(_POOL.map(block, starts))
+    else:
+        for r0 in starts:
+            block(r0)
     out = out.astype(F32)
     return out[0] if squeeze else out
 
@@ -342,3 +368,29 @@ def swiglu_mlp_kernel_form(cur, a, n_pf, matvec_g, matvec_u, matvec_d, eps=1e-5)
     gh = rnd(silu_tanh_bf16(g) * u)
     d = rnd(matvec_d(gh))
     return rnd(x1 + d)
+
+
+def pack_wo_tiled(q, scale_bits, cols: int, tsi_o: int, n_o_tiles: int, domain: str = "signed"):
+    """The fuse_o Wo wire: per core, ``n_o_tiles`` tiles of ``tsi_o`` rows covering the
+    core's window, rows past the matrix end zero (payload and scale).
+
+    Restates ``Qwen3NPU._set_wo_tiled`` (qwen3_npu_int8.py:407-436)."""
+    q = np.asarray(q, dtype=np.int8)
+    m, k = q.shape
+    ng = np.asarray(scale_bits).shape[1]
+    rows_per_col = m // cols
+    pad = n_o_tiles * tsi_o - rows_per_col
+    if pad < 0:
+        raise ValueError("tiles do not cover the per-core window")
+    wb = (q.astype(np.int16) + 128).astype(np.uint8) if domain == "biased" else q.view(np.uint8)
+    W = np.zeros((m + pad, k), np.uint8)
+    S = np.zeros((m + pad, ng * 2), np.uint8)
+    W[:m] = wb
+    S[:m] = np.ascontiguousarray(np.asarray(scale_bits, np.uint16)).view(np.uint8).reshape(m, ng * 2)
+    chunks = []
+    for g in range(cols):
+        for j in range(n_o_tiles):
+            r0 = g * rows_per_col + j * tsi_o
+            chunks.append(W[r0:r0 + tsi_o].reshape(-1))
+            chunks.append(S[r0:r0 + tsi_o].reshape(-1))
+    return np.concatenate(chunks)

@@ -1,0 +1,218 @@
+"""GPU parity of RMSNorm, elementwise ops, the fused QKV head, decode attention and the
+fused SwiGLU MLP block, each through its IRON-compatible operator class."""
+
+import numpy as np
+import pytest
+import torch
+
+from iron_b200.operators import (DecodeAttention, ElementwiseAdd, ElementwiseMul, QKVHeadDataParallelOurs,
+                                 RMSNorm, SiLU, SwiGLUMLPDataParallel, SwiGLUMLPDataParallelOurs)
+from iron_b200.test_utils import verify_buffer
+from oracle import ops
+from oracle.bf16 import from_bits, rnd
+
+from helpers import assert_close, assert_ulps, dev_bf16, dev_u8, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _out(n):
+    return torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+
+
+def test_rmsnorm_against_reference_golden(golden):
+    g = golden("rms_norm")
+    for xk, wk, yk, rows in (("x_gen", "w_gen", "y_gen", 4), ("x", "w", "y", 3)):
+        op = RMSNorm(size=rows * 1024, num_aie_columns=1, num_channels=1, tile_size=1024, weighted=True,
+                     epsilon=1e-6)
+        y = _out(rows * 1024)
+        op.get_callable()(dev_bf16(g[xk]).reshape(rows, 1024), dev_bf16(g[wk]), y.reshape(rows, 1024))
+        torch.cuda.synchronize()
+        # the reference test's tolerance (rms_norm/test.py: rel 0.04, abs 1e-6) against its golden
+        assert not verify_buffer(host(y), "y", from_bits(g[yk]), rel_tol=0.04, abs_tol=1e-6)
+        # and the kernel-form (float32, one rounding) restatement to 1 ulp
+        want = ops.rms_norm_f32(from_bits(g[xk]).reshape(rows, 1024), from_bits(g[wk]), 1e-6)
+        assert_ulps(host(y), want, max_ulp=1, frac_exact=0.99, what="rmsnorm f32 form")
+
+
+def test_elementwise_against_reference_golden(golden):
+    g = golden("elementwise")
+    a, b = dev_bf16(g["a"]), dev_bf16(g["b"])
+    for cls, key in ((ElementwiseAdd, "add"), (ElementwiseMul, "mul")):
+        c = _out(2048)
+        cls(size=2048, tile_size=256).get_callable()(a, b, c)
+        torch.cuda.synchronize()
+        assert np.array_equal(host(c), from_bits(g[key])), key
+    y = _out(2048)
+    SiLU(size=2048, num_aie_columns=8, tile_size=256).get_callable()(a, y)
+    torch.cuda.synchronize()
+    assert_ulps(host(y), from_bits(g["silu"]), max_ulp=1, frac_exact=0.99, what="silu")
+
+
+def test_silu_tanh_form_against_kernel_golden(golden):
+    g = golden("swiglu")
+    x = dev_bf16(g["silu_in"])
+    y = _out(x.numel())
+    SiLU(size=x.numel(), num_aie_columns=8, tile_size=512, tanh_form=True).get_callable()(x, y)
+    torch.cuda.synchronize()
+    assert_ulps(host(y), from_bits(g["silu_tanh_out"]), max_ulp=1, frac_exact=0.99, what="silu tanh")
+
+
+def _qkv_case(D, Hq, Hkv, HD, group, tile_m, max_seq, pos, seed=0):
+    rng = np.random.default_rng(seed)
+    QKV = (Hq + 2 * Hkv) * HD
+    w = rng.standard_normal((QKV, D)).astype(np.float32) * 0.02
+    q8, s8 = ops.quantize_rtn(rnd(w), group)
+    cur = rnd(rng.standard_normal(D).astype(np.float32))
+    n_in = rnd(1 + 0.1 * rng.standard_normal(D).astype(np.float32))
+    n_qn = rnd(1 + 0.1 * rng.standard_normal(HD).astype(np.float32))
+    n_kn = rnd(1 + 0.1 * rng.standard_normal(HD).astype(np.float32))
+    ang = ops.rope_angle_table(max_seq, HD, 1e6)[pos]
+    return q8, s8, cur, n_in, n_qn, n_kn, ang
+
+
+@pytest.mark.parametrize("group,tile_m,pos", [(128, 4, 0), (32, 1, 77), (128, 4, 511)])
+def test_qkv_head_op(group, tile_m, pos):
+    """QKVHeadDataParallelOurs vs qkv_head_dp/reference.py:13-33 with the premul int8 matvec;
+    K_t, V_t land at k_cache_offset = pos*2*HD of every head region; nothing else changes."""
+    D, Hq, Hkv, HD, S = 1024, 16, 8, 128, 512
+    q8, s8, cur, n_in, n_qn, n_kn, ang = _qkv_case(D, Hq, Hkv, HD, group, tile_m, S, pos)
+    op = QKVHeadDataParallelOurs(D=D, HD=HD, Hq=Hq, Hkv=Hkv, max_seq=S, tile_size_input=tile_m,
+                                 kernel_source="mv_int8_signed.cc", kv_offset_parameter="k_cache_offset",
+                                 group_size=group)
+    call = op.get_callable()
+    call.params.write("k_cache_offset", pos * 2 * HD)
+    call.params.sync()
+    wire = dev_u8(ops.pack_tile_wire(q8, s8, tile_m, 8, "signed")).view(torch.bfloat16)
+    q = _out(Hq * HD)
+    kv = torch.full((Hkv * S * HD * 2,), 7.0, dtype=torch.bfloat16, device="cuda")
+    call(dev_bf16(cur), dev_bf16(n_in), wire, dev_bf16(n_qn), dev_bf16(n_kn), dev_bf16(ang), q, kv)
+    torch.cuda.synchronize()
+    want = ops.qkv_head(cur, n_in, lambda hn: ops.gemv_int8_premul(q8, s8, hn), n_qn, n_kn, ang,
+                        D, HD, Hq, Hkv, 1e-6)
+    QD, KVD = Hq * HD, Hkv * HD
+    assert_close(host(q), want[:QD], what="q")
+    kvh = host(kv).reshape(Hkv, S, 2, HD)
+    assert_close(kvh[:, pos, 0], want[QD:QD + KVD].reshape(Hkv, HD), what="K_t")
+    assert_close(kvh[:, pos, 1], want[QD + KVD:].reshape(Hkv, HD), what="V_t")
+    untouched = np.ones((Hkv, S), bool)
+    untouched[:, pos] = False
+    assert np.all(kvh[untouched] == 7.0)
+
+
+@pytest.mark.parametrize("sp", [0, 1, 31, 32, 33, 100, 255])
+def test_decode_attention_against_reference_golden(golden, sp):
+    """decode_attn/reference.py golden vectors (H=16, KV=8, D=128), [K half | V half] buffer."""
+    g = golden("decode_attn")
+    S = 256
+    op = DecodeAttention(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=S,
+                         use_runtime_seq_len=True, kv_halves=True)
+    call = op.get_callable()
+    call.params.write("S_kv_eff", sp + 1)
+    call.params.sync()
+    kv = np.concatenate([from_bits(g["K"]), from_bits(g["V"])], axis=1)  # (KV, 2S, D)
+    o = _out(16 * 128)
+    call(dev_bf16(g["Q"]), dev_bf16(kv).reshape(8, 2 * S * 128), o.reshape(16, 128))
+    torch.cuda.synchronize()
+    want = from_bits(g[f"O_{sp}"])
+    assert_close(host(o), want, what=f"seq_pos {sp}")
+    assert_ulps(host(o), want, max_ulp=2, frac_exact=0.9, what=f"seq_pos {sp}")
+
+
+@pytest.mark.parametrize("layout", ["token", "block"])
+@pytest.mark.parametrize("L", [1, 33, 64, 65, 130, 511, 512])
+def test_decode_attention_layouts_and_unaligned_lengths(layout, L):
+    """seq_pos values of decode_attn/test_seqpos_unaligned.py:80 over both cache layouts."""
+    rng = np.random.default_rng(L)
+    H, KV, D, S, B = 16, 8, 128, 512, 64
+    Q = rnd(rng.standard_normal((H, D)).astype(np.float32))
+    K = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    V = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    if layout == "token":
+        kv = np.stack([K, V], axis=2).reshape(KV, 2 * S * D)
+        op = DecodeAttention(num_heads=H, num_kv_heads=KV, head_dim=D, seq_len_kv=S, use_runtime_seq_len=True)
+    else:
+        kv = np.concatenate([K.reshape(KV, S // B, B, D), V.reshape(KV, S // B, B, D)], axis=2).reshape(KV, -1)
+        op = DecodeAttention(num_heads=H, num_kv_heads=KV, head_dim=D, seq_len_kv=S, block_kv=B,
+                             use_runtime_seq_len=True, kv_token_interleaved=False)
+    call = op.get_callable()
+    call.params.write("S_kv_eff", L)
+    call.params.sync()
+    o = _out(H * D)
+    call(dev_bf16(Q), dev_bf16(kv), o.reshape(H, D))
+    torch.cuda.synchronize()
+    want = ops.decode_attention(Q, K, V, L - 1, D, H, KV)
+    assert_close(host(o).reshape(H, D), want, what=f"L={L}")
+    assert not np.isnan(host(o)).any()
+
+
+def test_mlp_kernel_golden_biased_wire(golden):
+    """The kernel-faithful golden of swiglu_mlp_dp/test.py (biased q+128 wire, tiles 12/4)."""
+    g = golden("swiglu")
+    D, FF = 256, 768
+    op = SwiGLUMLPDataParallelOurs(D=D, FF=FF, num_aie_columns=2, epsilon=1e-6)
+    wire = {}
+    for name, K, tm in (("wg", D, 12), ("wu", D, 12), ("wd", FF, 4)):
+        q = (g[f"k_{name}_q"].astype(np.int16) - 128).astype(np.int8)
+        wire[name] = dev_u8(ops.pack_tile_wire(q, g[f"k_{name}_s"], tm, 2, "biased")).view(torch.bfloat16)
+        assert wire[name].numel() == op.get_arg_spec()[{"wg": 3, "wu": 4, "wd": 5}[name]].shape[0]
+    nxt = _out(D)
+    gh = _out(FF)
+    op.get_callable()(dev_bf16(g["k_cur"]), dev_bf16(g["k_a"]), dev_bf16(rnd(g["k_npf"])), wire["wg"],
+                      wire["wu"], wire["wd"], gh, nxt)
+    torch.cuda.synchronize()
+    # the reference test's tolerance (swiglu_mlp_dp/test.py:190-191)
+    assert not verify_buffer(host(nxt), "nxt", from_bits(g["k_nxt"]), rel_tol=0.05, abs_tol=0.05)
+    assert_close(host(nxt), from_bits(g["k_nxt"]), what="nxt")
+
+
+@pytest.mark.parametrize("group", [128, 32])
+def test_mlp_fuse_o_tile_major_wo(group):
+    """fuse_o arm at the Qwen3-0.6B shape: Wo in the per-core tile-major wire with pad rows
+    (qwen3_npu_int8.py:407-436), gate/up 12-row tiles, down 4-row tiles, signed payload."""
+    D, FF, QD = 1024, 3072, 2048
+    rng = np.random.default_rng(group)
+    W = {}
+    for name, (M, K) in (("wg", (FF, D)), ("wu", (FF, D)), ("wd", (D, FF)), ("wo", (D, QD))):
+        W[name] = ops.quantize_rtn(rnd(rng.standard_normal((M, K)).astype(np.float32) * 0.02), group)
+    cur = rnd(rng.standard_normal(D).astype(np.float32))
+    cx = rnd(rng.standard_normal(QD).astype(np.float32))
+    npf = rnd(1 + 0.1 * rng.standard_normal(D).astype(np.float32))
+    op = SwiGLUMLPDataParallelOurs(D=D, FF=FF, num_aie_columns=8, epsilon=1e-6, QD=QD, fuse_o=True,
+                                   kernel_source="mv_int8_signed.cc", group_size=group)
+    n, n_o, tsi_o, _ = op._wo_tiling()
+    spec = op.get_arg_spec()
+    wo = ops.pack_wo_tiled(*W["wo"], cols=n, tsi_o=tsi_o, n_o_tiles=n_o)
+    assert wo.size // 2 == spec[3].shape[0]
+    bufs = [dev_bf16(cur), dev_bf16(cx), dev_bf16(npf), dev_u8(wo).view(torch.bfloat16)]
+    for name, tm in (("wg", 12), ("wu", 12), ("wd", 4)):
+        bufs.append(dev_u8(ops.pack_tile_wire(*W[name], tm, n, "signed")).view(torch.bfloat16))
+    nxt = _out(D)
+    bufs += [_out(FF), _out(D), nxt]
+    op.get_callable()(*bufs)
+    torch.cuda.synchronize()
+    mv = {k: (lambda v, k=k: ops.gemv_int8_premul(*W[k], v)) for k in W}
+    a = rnd(mv["wo"](cx))
+    want = ops.swiglu_mlp_kernel_form(cur, a, npf, mv["wg"], mv["wu"], mv["wd"], 1e-6)
+    assert_close(host(nxt), want, what="nxt")
+    # the float32 golden of swiglu_mlp_dp/reference.py:54-67 within the reference's tolerance
+    deq = {k: ops.dequant_f32(*W[k]) for k in W}
+    f32 = ops.swiglu_mlp_fused_o(cur, cx, npf, deq["wo"], deq["wg"], deq["wu"], deq["wd"], D, FF, QD, 1e-6)
+    assert not verify_buffer(host(nxt), "nxt", f32, rel_tol=0.05, abs_tol=0.05)
+
+
+def test_mlp_bf16_arm():
+    D, FF = 512, 1536
+    rng = np.random.default_rng(4)
+    Wg, Wu, Wd = (rnd(rng.standard_normal(s).astype(np.float32) * 0.05) for s in ((FF, D), (FF, D), (D, FF)))
+    cur, a = (rnd(rng.standard_normal(D).astype(np.float32)) for _ in range(2))
+    npf = rnd(rng.random(D).astype(np.float32) + 0.5)
+    nxt = _out(D)
+    SwiGLUMLPDataParallel(D=D, FF=FF, num_aie_columns=2, epsilon=1e-6).get_callable()(
+        dev_bf16(cur), dev_bf16(a), dev_bf16(npf), dev_bf16(Wg).reshape(-1), dev_bf16(Wu).reshape(-1),
+        dev_bf16(Wd).reshape(-1), _out(FF), nxt)
+    torch.cuda.synchronize()
+    want = ops.swiglu_mlp_kernel_form(cur, a, npf, lambda v: Wg.astype(np.float64) @ v,
+                                      lambda v: Wu.astype(np.float64) @ v, lambda v: Wd.astype(np.float64) @ v,
+                                      1e-6)
+    assert_close(host(nxt), want, what="bf16 arm")

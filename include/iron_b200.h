@@ -106,9 +106,10 @@ int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void*
 /* y = bf16(silu(x)); mode 0: x*sigmoid(x) in f32 (silu/reference.py:8-10),
  * mode 1: the tanh form with bf16 roundings (aie_kernels/aie2p/silu.cc). */
 int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream);
-/* out[i, :] = table[ids[i], :]  (token embedding gather, bf16 rows of D). */
-int iron_embedding(const uint16_t* table, const int32_t* ids, int n, int D, uint16_t* out,
-                   void* stream);
+/* out[i, :] = table[ids[i], :]  (token embedding gather, bf16 rows of D; an id
+ * outside [0, vocab) yields a zero row). */
+int iron_embedding(const uint16_t* table, int vocab, const int32_t* ids, int n, int D,
+                   uint16_t* out, void* stream);
 
 /* Advance the device-resident decode positions by one token for `batch` streams:
  * pos += 1; seq_len = pos + 1; kv_off = pos * 2 * HD (the host-side per-token
@@ -128,6 +129,7 @@ int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int bat
  * written at element offset kv_off of every head region and V_t at kv_off + HD
  * (kv_off = seq_pos*2*HD, the k_cache_offset parameter of qwen3_npu_int8.py:600,
  * 608); kv_off_dev (int32[batch]) overrides kv_off when non-NULL.
+ * An offset that is not a token slot of the cache writes nothing.
  * ang_is_table = 0: ang holds one interleaved [cos, sin, ...] row of HD per stream;
  * 1: ang is a (max_seq, HD) table and the row kv_off/(2*HD) is used.
  * raw_ws: bf16 workspace of batch*(Hq+2*Hkv)*HD elements. */

@@ -32,7 +32,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_add": (I, [P, P, P, I64, P]),
     "iron_mul": (I, [P, P, P, I64, P]),
     "iron_silu": (I, [P, P, I64, I, P]),
-    "iron_embedding": (I, [P, P, I, I, P, P]),
+    "iron_embedding": (I, [P, I, P, I, I, P, P]),
     "iron_decode_advance": (I, [P, P, P, I, I, P]),
     "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, P, P]),
     "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),

@@ -40,10 +40,13 @@ __global__ void eltwise_kernel(const uint16_t* a, const uint16_t* b, uint16_t* c
   }
 }
 
-__global__ void embedding_kernel(const uint16_t* table, const int32_t* ids, int D, uint16_t* out) {
+// ids outside [0, vocab) produce a zero row instead of an out-of-range read
+__global__ void embedding_kernel(const uint16_t* table, const int32_t* ids, int vocab, int D, uint16_t* out) {
   const int i = blockIdx.x;
-  const uint16_t* src = table + (size_t)ids[i] * D;
-  for (int k = threadIdx.x; k < D; k += blockDim.x) out[(size_t)i * D + k] = src[k];
+  const int id = ids[i];
+  const bool ok = id >= 0 && id < vocab;
+  const uint16_t* src = table + (size_t)(ok ? id : 0) * D;
+  for (int k = threadIdx.x; k < D; k += blockDim.x) out[(size_t)i * D + k] = ok ? src[k] : (uint16_t)0;
 }
 
 // Per-head epilogue of the fused QKV head (qkv_head_dp/reference.py:29-33).
@@ -59,6 +62,8 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
   const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
   const int QKV = (Hq + 2 * Hkv) * HD;
   const int off = kv_off_dev ? kv_off_dev[b] : kv_off;  // element offset of K_t in a head region
+  // an offset outside the cache (e.g. a stale runtime parameter) writes nothing
+  if (off < 0 || off % (2 * HD) != 0 || off / (2 * HD) >= max_seq) return;
   const bool isq = head < Hq;
   const uint16_t* src = raw + (size_t)b * QKV + (size_t)head * HD;
   const uint16_t* nw = isq ? n_qn : n_kn;
@@ -168,11 +173,11 @@ extern "C" int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, vo
   IRON_REQUIRE(mode == 0 || mode == 1, IRON_ERR_ARG, "silu: mode must be 0 or 1");
   return elt(x, nullptr, y, n, 2 + mode, stream);
 }
-extern "C" int iron_embedding(const uint16_t* table, const int32_t* ids, int n, int D, uint16_t* out,
-                              void* stream) {
-  IRON_REQUIRE(table && ids && out && n >= 0 && D > 0, IRON_ERR_ARG, "embedding: bad arguments");
+extern "C" int iron_embedding(const uint16_t* table, int vocab, const int32_t* ids, int n, int D,
+                              uint16_t* out, void* stream) {
+  IRON_REQUIRE(table && ids && out && n >= 0 && D > 0 && vocab > 0, IRON_ERR_ARG, "embedding: bad arguments");
   if (n == 0) return IRON_OK;
-  embedding_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(table, ids, D, out);
+  embedding_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(table, ids, vocab, D, out);
   return iron_check_launch("embedding_kernel");
 }
 

@@ -201,7 +201,7 @@ class Qwen3B200:
         c, w, B = self.cfg, self.w, self.B
         G = w.group
         if from_tokens:
-            abi("iron_embedding", ptr(w.embed), ptr(self.tok), B, c.D, ptr(self.x), st)
+            abi("iron_embedding", ptr(w.embed), c.V, ptr(self.tok), B, c.D, ptr(self.x), st)
         for i, Lw in enumerate(w.layers):
             kv = self.kv[i]
             abi("iron_qkv_head", ptr(self.x), ptr(Lw["norm1"]), ptr(Lw["wqkv"]), G, 1, 0, ptr(Lw["qn"]),

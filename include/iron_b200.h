@@ -95,10 +95,13 @@ int iron_argmax_bf16(const uint16_t* logits, int M, int batch, int32_t* token_ou
                      void* workspace, void* stream);
 
 /* ---- RMSNorm / elementwise ---------------------------------------------------
- * y = bf16(x * rsqrt(mean(x^2) + eps) [* w]) per row of `cols`; f32 math
- * (aie_kernels/aie2p/rms_norm.cc:9-53; op iron/operators/rms_norm/op.py:20-130). */
+ * Weighted RMSNorm per row of `cols` (op iron/operators/rms_norm/op.py:20-130).
+ * mode 0: y = bf16(x * rsqrt(mean(x^2) + eps) * w) in f32, the device kernel's
+ * arithmetic (aie_kernels/aie2p/rms_norm.cc:9-53).  mode 1: the golden's
+ * arithmetic on bf16 tensors (rms_norm/reference.py:8-17), each of x^2, mean,
+ * +eps, sqrt, x/rms, *w rounded to bf16.  w may be NULL (unweighted). */
 int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
-                 float eps, void* stream);
+                 float eps, int mode, void* stream);
 /* c = bf16(a + b)   (iron/operators/elementwise_add/op.py, aie_kernels/generic/add.cc) */
 int iron_add(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream);
 /* c = bf16(a * b)   (iron/operators/elementwise_mul/op.py, aie_kernels/generic/mul.cc) */
@@ -132,12 +135,15 @@ int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int bat
  * An offset that is not a token slot of the cache writes nothing.
  * ang_is_table = 0: ang holds one interleaved [cos, sin, ...] row of HD per stream;
  * 1: ang is a (max_seq, HD) table and the row kv_off/(2*HD) is used.
+ * norm_mode selects the RMSNorm arithmetic of the input and q/k norms (see
+ * iron_rmsnorm; the QKV golden uses mode 1).
  * raw_ws: bf16 workspace of batch*(Hq+2*Hkv)*HD elements. */
 int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const void* wqkv_wire, int group,
                   int tile_m, int domain, const uint16_t* n_qn, const uint16_t* n_kn,
                   const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv_cache,
                   int D, int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                  const int32_t* kv_off_dev, float eps, uint16_t* raw_ws, void* stream);
+                  const int32_t* kv_off_dev, float eps, int norm_mode, uint16_t* raw_ws,
+                  void* stream);
 
 /* ---- decode attention ---------------------------------------------------------
  * GQA single-query attention per stream over positions [0, seq_len), base-2

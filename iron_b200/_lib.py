@@ -28,13 +28,13 @@ SIGNATURES: dict[str, tuple] = {
     "iron_lm_head_w8_argmax": (I, [P, I, I, I, P, I, P, P, P, P]),
     "iron_argmax_workspace_bytes": (I64, [I]),
     "iron_argmax_bf16": (I, [P, I, I, P, P, P]),
-    "iron_rmsnorm": (I, [P, P, P, I, I, F, P]),
+    "iron_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
     "iron_add": (I, [P, P, P, I64, P]),
     "iron_mul": (I, [P, P, P, I64, P]),
     "iron_silu": (I, [P, P, I64, I, P]),
     "iron_embedding": (I, [P, I, P, I, I, P, P]),
     "iron_decode_advance": (I, [P, P, P, I, I, P]),
-    "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, P, P]),
+    "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, I, P, P]),
     "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
     "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),

@@ -7,7 +7,7 @@ namespace iron {
 int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                            const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
                            int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                           const int32_t* kv_off_dev, float eps, cudaStream_t st);
+                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st);
 }
 using namespace iron;
 
@@ -15,7 +15,8 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
                              int tile_m, int domain, const uint16_t* n_qn, const uint16_t* n_kn,
                              const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv_cache,
                              int D, int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                             const int32_t* kv_off_dev, float eps, uint16_t* raw_ws, void* stream) {
+                             const int32_t* kv_off_dev, float eps, int norm_mode, uint16_t* raw_ws,
+                             void* stream) {
   IRON_REQUIRE(cur && n_in && n_qn && n_kn && ang && q_out && kv_cache && raw_ws, IRON_ERR_ARG,
                "qkv_head: null pointer");
   IRON_REQUIRE(kv_off_dev || (kv_off >= 0 && kv_off % (2 * HD) == 0 && kv_off / (2 * HD) < max_seq),
@@ -31,6 +32,7 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
   p.ld_x = D;
   p.rms_w = n_in;
   p.eps = eps;
+  p.rms_mode = norm_mode;
   p.y = raw_ws;
   p.ld_y = M;
   p.nb = batch;
@@ -39,7 +41,7 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
   rc = gemv_w8_launch(p, false, st);
   if (rc) return rc;
   return qk_norm_rope_kv_launch(raw_ws, n_qn, n_kn, ang, ang_is_table, q_out, kv_cache, HD, Hq, Hkv,
-                                max_seq, batch, kv_off, kv_off_dev, eps, st);
+                                max_seq, batch, kv_off, kv_off_dev, eps, norm_mode, st);
 }
 
 extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, const uint16_t* n_pf,

@@ -104,10 +104,36 @@ __device__ __forceinline__ void bfp_scale(float m, float& sc, float& inv) {
   inv = __uint_as_float((uint32_t)ie << 23);
 }
 
-// Weighted RMSNorm constant: 1/sqrt(mean(x^2) + eps) in float32
-// (aie_kernels/aie2p/rms_norm.cc:36-38 computes the same quantity).
-__device__ __forceinline__ float rms_inv(float sum_sq, int n, float eps) {
-  return rsqrtf(sum_sq / (float)n + eps);
+// Weighted RMSNorm in two numerical forms.
+//  mode 0 (kernel form, aie_kernels/aie2p/rms_norm.cc:9-53): float32 sum of
+//    squares, inv = 1/sqrt(sum/n + eps), y = bf16(x * inv * w), one rounding.
+//  mode 1 (golden form, rms_norm/reference.py:8-17 on bf16 tensors): every
+//    torch op rounds to bf16 -- x^2, mean, + eps, sqrt, x / rms, * w.
+struct RmsCoef {
+  float inv, rms;
+  int mode;
+};
+__device__ __forceinline__ float rms_sq(float v, int mode) {
+  const float s = v * v;
+  return mode ? rbf(s) : s;
+}
+__device__ __forceinline__ RmsCoef rms_coef(float sum_sq, int n, float eps, int mode) {
+  RmsCoef c;
+  c.mode = mode;
+  if (mode == 0) {
+    c.inv = rsqrtf(sum_sq / (float)n + eps);
+    c.rms = 0.f;
+  } else {
+    const float mean = rbf(sum_sq / (float)n);
+    const float ms = rbf(mean + eps);
+    c.rms = rbf(sqrtf(ms));
+    c.inv = 0.f;
+  }
+  return c;
+}
+// normalised, weighted value before the final bf16 rounding
+__device__ __forceinline__ float rms_apply(float v, float w, const RmsCoef& c) {
+  return c.mode == 0 ? v * c.inv * w : rbf(v / c.rms) * w;
 }
 
 // sigmoid via tanh with bf16 rounding after every vector op, the arithmetic of

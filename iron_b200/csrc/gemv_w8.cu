@@ -41,14 +41,11 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
     }
     if (p.rms_w) {
       float ss = 0.f;
-      for (int i = tid; i < K; i += blockDim.x) {
-        float v = bf2f(xr[i]);
-        ss = fmaf(v, v, ss);
-      }
+      for (int i = tid; i < K; i += blockDim.x) ss += rms_sq(bf2f(xr[i]), p.rms_mode);
       ss = block_sum(ss, misc);
-      const float inv = rms_inv(ss, K, p.eps);
+      const RmsCoef rc = rms_coef(ss, K, p.eps, p.rms_mode);
       for (int i = tid; i < K; i += blockDim.x)
-        xq[b * K + i] = f2bf(bf2f(xr[i]) * inv * bf2f(p.rms_w[i]));
+        xq[b * K + i] = f2bf(rms_apply(bf2f(xr[i]), bf2f(p.rms_w[i]), rc));
     } else {
       for (int i = tid; i < K; i += blockDim.x) xq[b * K + i] = xr[i];
     }

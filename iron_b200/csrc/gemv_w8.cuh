@@ -40,6 +40,7 @@ struct GemvW8Params {
   int ld_x;
   const uint16_t* rms_w;  // non-null: RMS-normalise x with this weight first
   float eps;
+  int rms_mode;           // 0 kernel form, 1 golden form (see RmsCoef)
   const uint16_t* res;  // residual [nb][ld_y]
   uint16_t* y;          // [nb][ld_y]
   int ld_y;

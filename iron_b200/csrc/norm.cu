@@ -5,21 +5,17 @@
 namespace iron {
 
 // one CTA per row; float32 math, one bf16 rounding (aie_kernels/aie2p/rms_norm.cc:9-53)
-__global__ void rmsnorm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* y, int cols, float eps) {
+__global__ void rmsnorm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* y, int cols, float eps,
+                               int mode) {
   __shared__ float red[32];
   const uint16_t* xr = x + (size_t)blockIdx.x * cols;
   uint16_t* yr = y + (size_t)blockIdx.x * cols;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
-    const float v = bf2f(xr[i]);
-    ss = fmaf(v, v, ss);
-  }
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) ss += rms_sq(bf2f(xr[i]), mode);
   ss = block_sum(ss, red);
-  const float inv = rms_inv(ss, cols, eps);
+  const RmsCoef rc = rms_coef(ss, cols, eps, mode);
   for (int i = threadIdx.x; i < cols; i += blockDim.x) {
-    float v = bf2f(xr[i]) * inv;
-    if (w) v *= bf2f(w[i]);
-    yr[i] = f2bf(v);
+    yr[i] = f2bf(rms_apply(bf2f(xr[i]), w ? bf2f(w[i]) : 1.0f, rc));
   }
 }
 
@@ -57,7 +53,7 @@ template <int HD>
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                                        const uint16_t* ang, int ang_is_table, uint16_t* q_out,
                                        uint16_t* kv, int Hq, int Hkv, int max_seq, int kv_off,
-                                       const int32_t* kv_off_dev, float eps) {
+                                       const int32_t* kv_off_dev, float eps, int norm_mode) {
   constexpr int PER = HD / 32;
   const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
   const int QKV = (Hq + 2 * Hkv) * HD;
@@ -76,17 +72,17 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
     const int i = lane + 32 * j;
     v[2 * j] = bf2f(src[i]);
     v[2 * j + 1] = bf2f(src[i + HD / 2]);
-    ss = fmaf(v[2 * j], v[2 * j], ss);
-    ss = fmaf(v[2 * j + 1], v[2 * j + 1], ss);
+    ss += rms_sq(v[2 * j], norm_mode);
+    ss += rms_sq(v[2 * j + 1], norm_mode);
   }
   ss = warp_sum(ss);
-  const float inv = rms_inv(ss, HD, eps);
+  const RmsCoef rc = rms_coef(ss, HD, eps, norm_mode);
   uint16_t o[PER];
 #pragma unroll
   for (int j = 0; j < PER / 2; ++j) {
     const int i = lane + 32 * j;
-    const float x1 = rbf(v[2 * j] * inv * bf2f(nw[i]));
-    const float x2 = rbf(v[2 * j + 1] * inv * bf2f(nw[i + HD / 2]));
+    const float x1 = rbf(rms_apply(v[2 * j], bf2f(nw[i]), rc));
+    const float x2 = rbf(rms_apply(v[2 * j + 1], bf2f(nw[i + HD / 2]), rc));
     const float c = bf2f(a[2 * i]), s = bf2f(a[2 * i + 1]);
     // rope/reference.py:150-154: y1 = x1*c - x2*s, y2 = x2*c + x1*s (float32)
     o[2 * j] = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
@@ -115,14 +111,14 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
 int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                            const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
                            int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                           const int32_t* kv_off_dev, float eps, cudaStream_t st) {
+                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st) {
   dim3 g(Hq + Hkv, batch);
   if (HD == 128) {
     qk_norm_rope_kv_kernel<128><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                   max_seq, kv_off, kv_off_dev, eps);
+                                                   max_seq, kv_off, kv_off_dev, eps, norm_mode);
   } else if (HD == 64) {
     qk_norm_rope_kv_kernel<64><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                  max_seq, kv_off, kv_off_dev, eps);
+                                                  max_seq, kv_off, kv_off_dev, eps, norm_mode);
   } else {
     return iron_set_error(IRON_ERR_UNSUPPORTED, "qkv head: head_dim %d (supported: 64, 128)", HD);
   }
@@ -150,9 +146,10 @@ static int elt_grid(int64_t n) {
 using namespace iron;
 
 extern "C" int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
-                            float eps, void* stream) {
-  IRON_REQUIRE(x && y && rows > 0 && cols > 0, IRON_ERR_ARG, "rmsnorm: bad arguments");
-  rmsnorm_kernel<<<rows, cols >= 1024 ? 512 : 128, 0, (cudaStream_t)stream>>>(x, w, y, cols, eps);
+                            float eps, int mode, void* stream) {
+  IRON_REQUIRE(x && y && rows > 0 && cols > 0 && (mode == 0 || mode == 1), IRON_ERR_ARG,
+               "rmsnorm: bad arguments");
+  rmsnorm_kernel<<<rows, cols >= 1024 ? 512 : 128, 0, (cudaStream_t)stream>>>(x, w, y, cols, eps, mode);
   return iron_check_launch("rmsnorm_kernel");
 }
 

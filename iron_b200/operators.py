@@ -159,7 +159,11 @@ class GEMV(Operator):
 
 @dataclass
 class RMSNorm(Operator):
-    """(Weighted) RMSNorm over rows of ``tile_size`` (iron/operators/rms_norm/op.py:20-130)."""
+    """(Weighted) RMSNorm over rows of ``tile_size`` (iron/operators/rms_norm/op.py:20-130).
+
+    ``golden_rounding`` (B200 extension, default on) rounds every intermediate to bf16
+    as the op's golden does on bf16 tensors (rms_norm/reference.py:8-17); off gives the
+    float32 single-rounding arithmetic of aie_kernels/aie2p/rms_norm.cc."""
 
     size: int
     num_aie_columns: int
@@ -168,6 +172,7 @@ class RMSNorm(Operator):
     weighted: bool = False
     epsilon: float = 1e-5
     context: object = field(default=None, repr=False)
+    golden_rounding: bool = field(default=True, repr=False)
 
     _name_aliases: ClassVar[dict[str, str]] = {**Operator._name_aliases, "weighted": "w", "epsilon": "eps"}
 
@@ -187,7 +192,7 @@ class RMSNorm(Operator):
     def launch(self, bufs, params, stream):
         x, w, y = (bufs[0], bufs[1], bufs[2]) if self.weighted else (bufs[0], None, bufs[1])
         abi("iron_rmsnorm", ptr(x), ptr(w), ptr(y), self.size // self.tile_size, self.tile_size,
-            float(self.epsilon), stream)
+            float(self.epsilon), 1 if self.golden_rounding else 0, stream)
 
 
 @dataclass
@@ -418,7 +423,7 @@ class QKVHeadDataParallel(Operator):
         abi("iron_qkv_head", ptr(cur), ptr(n_in), ptr(wire), self.group_size, self.tile_size_input,
             _domain(self.kernel_source), ptr(n_qn), ptr(n_kn), ptr(ang), 0, ptr(q), ptr(kv),
             self.D, self.HD, self.Hq, self.Hkv, self.max_seq, 1, self.kv_offset, ptr(off_dev),
-            float(self.epsilon), ptr(self._raw), stream)
+            float(self.epsilon), 1, ptr(self._raw), stream)
 
 
 @dataclass
@@ -482,7 +487,7 @@ class SwiGLUMLPDataParallel(Operator):
         x1, hf, d = self._tmp[:D], self._tmp[D:2 * D], self._tmp[2 * D:3 * D]
         g, u = self._tmp[3 * D:3 * D + FF], self._tmp[3 * D + FF:]
         abi("iron_add", ptr(cur), ptr(a), ptr(x1), D, stream)
-        abi("iron_rmsnorm", ptr(x1), ptr(n_pf), ptr(hf), 1, D, float(self.epsilon), stream)
+        abi("iron_rmsnorm", ptr(x1), ptr(n_pf), ptr(hf), 1, D, float(self.epsilon), 0, stream)
         abi("iron_gemv_bf16", ptr(wg), FF, D, ptr(hf), 1, 0, ptr(g), stream)
         abi("iron_gemv_bf16", ptr(wu), FF, D, ptr(hf), 1, 0, ptr(u), stream)
         abi("iron_silu", ptr(g), ptr(g), FF, 1, stream)

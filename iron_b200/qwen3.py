@@ -206,13 +206,13 @@ class Qwen3B200:
             kv = self.kv[i]
             abi("iron_qkv_head", ptr(self.x), ptr(Lw["norm1"]), ptr(Lw["wqkv"]), G, 1, 0, ptr(Lw["qn"]),
                 ptr(Lw["kn"]), ptr(self.angles), 1, ptr(self.q), ptr(kv), c.D, c.HD, c.Hq, c.Hkv,
-                self.max_seq, B, 0, ptr(self.off), c.eps, ptr(self.raw), st)
+                self.max_seq, B, 0, ptr(self.off), c.eps, 1, ptr(self.raw), st)
             abi("iron_decode_attn", ptr(self.q), ptr(kv), ptr(self.attn), B, c.Hq, c.Hkv, c.HD,
                 self.max_seq, 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
             abi("iron_mlp_block", ptr(self.x), ptr(self.attn), 1, ptr(Lw["norm2"]), ptr(Lw["wo"]), 1, 0, 0,
                 ptr(Lw["wg"]), ptr(Lw["wu"]), 1, ptr(Lw["wd"]), 1, G, 0, ptr(self.x1), ptr(self.gh),
                 ptr(self.x), c.D, c.FF, c.QD, B, c.eps, st)
-        abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xf), B, c.D, c.eps, st)
+        abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xf), B, c.D, c.eps, 1, st)
         if self.lm_head == "bf16":
             abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xf), B, ptr(self.logits),
                 ptr(self.tok), ptr(self.argmax_ws), st)

@@ -23,14 +23,21 @@ def _out(n):
 def test_rmsnorm_against_reference_golden(golden):
     g = golden("rms_norm")
     for xk, wk, yk, rows in (("x_gen", "w_gen", "y_gen", 4), ("x", "w", "y", 3)):
+        x2d = dev_bf16(g[xk]).reshape(rows, 1024)
+        # golden arithmetic (every torch op rounds to bf16): the golden's bits
         op = RMSNorm(size=rows * 1024, num_aie_columns=1, num_channels=1, tile_size=1024, weighted=True,
                      epsilon=1e-6)
         y = _out(rows * 1024)
-        op.get_callable()(dev_bf16(g[xk]).reshape(rows, 1024), dev_bf16(g[wk]), y.reshape(rows, 1024))
+        op.get_callable()(x2d, dev_bf16(g[wk]), y.reshape(rows, 1024))
         torch.cuda.synchronize()
-        # the reference test's tolerance (rms_norm/test.py: rel 0.04, abs 1e-6) against its golden
+        assert_ulps(host(y), from_bits(g[yk]), max_ulp=1, frac_exact=0.99, what="rmsnorm golden form")
+        # kernel arithmetic (float32, one rounding, rms_norm.cc): within the reference
+        # test's tolerance of the golden (rms_norm/test.py: rel 0.04, abs 1e-6)
+        op = RMSNorm(size=rows * 1024, num_aie_columns=1, num_channels=1, tile_size=1024, weighted=True,
+                     epsilon=1e-6, golden_rounding=False)
+        op.get_callable()(x2d, dev_bf16(g[wk]), y.reshape(rows, 1024))
+        torch.cuda.synchronize()
         assert not verify_buffer(host(y), "y", from_bits(g[yk]), rel_tol=0.04, abs_tol=1e-6)
-        # and the kernel-form (float32, one rounding) restatement to 1 ulp
         want = ops.rms_norm_f32(from_bits(g[xk]).reshape(rows, 1024), from_bits(g[wk]), 1e-6)
         assert_ulps(host(y), want, max_ulp=1, frac_exact=0.99, what="rmsnorm f32 form")
 

@@ -247,10 +247,10 @@ static int launch_bf16(GemvBf16Params p, cudaStream_t st, int gridy) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (smem > 48 * 1024 && dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(gemv_bf16_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(gemv_bf16_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr[dev] = true;
   }
-  if (smem > 200 * 1024)
+  if (smem > 227 * 1024)
     return iron_set_error(IRON_ERR_UNSUPPORTED, "gemv_bf16: K=%d x batch=%d exceeds shared memory", p.K, p.nb);
   const int njobs = (p.M + 3) / 4;
   int ks = 1;

@@ -169,10 +169,10 @@ static int launch_t(const GemvW8Params& p, cudaStream_t st) {
   cudaGetDevice(&dev);
   if (smem > 48 * 1024 && dev < 64 && !attr_set[dev]) {
     cudaFuncSetAttribute(gemv_w8_kernel<G, NB, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         200 * 1024);
+                         227 * 1024);
     attr_set[dev] = true;
   }
-  if (smem > 200 * 1024)
+  if (smem > 227 * 1024)
     return iron_set_error(IRON_ERR_UNSUPPORTED, "gemv_w8: K=%d x batch=%d needs %zu B of shared memory",
                           p.K, p.nb, smem);
   const int njobs = (p.M + 3) / 4;

@@ -7,8 +7,13 @@ layer, then the final RMSNorm and the lm_head GEMV, then a host argmax.  This
 module composes the per-operator golden restatements of ``oracle.ops`` in
 exactly that order:
 
-* QKV head: ``qkv_head_dp/reference.py:13-33`` with the premul int8 matvec
-  (``gemv_int8/reference.py:25-40``) as its projection;
+* every int8 projection is the operator's ``reference()`` arithmetic, the exact
+  dequantised matvec ``(q*s) @ x`` in float (``GEMVInt8.reference``,
+  gemv_int8/op.py:173-178; ``SwiGLUMLPDataParallelOurs.reference``,
+  swiglu_mlp_dp/op_ours.py:543-570); ``matvec="premul"`` selects instead the
+  kernel-faithful golden ``gemv_int8/reference.py:25-40`` that rounds
+  ``bf16(x*s)`` before the multiply-accumulate;
+* QKV head: ``qkv_head_dp/reference.py:13-33`` with that matvec as its projection;
 * K_t, V_t appended to the per-layer cache at position ``seq_pos``
   (qwen3_npu_int8.py:596-600, 608);
 * attention: ``decode_attn/reference.py:26-38`` with ``seq_pos`` inclusive
@@ -54,11 +59,15 @@ class OracleQwen3:
     values and optionally ``lm_q``/``lm_s`` (int8 lm_head).
     """
 
-    def __init__(self, shape: Qwen3Shape, weights: dict, max_seq: int, int8_lm_head=False):
+    def __init__(self, shape: Qwen3Shape, weights: dict, max_seq: int, int8_lm_head=False,
+                 matvec: str = "exact"):
         self.s = shape
         self.w = weights
         self.max_seq = max_seq
         self.int8_lm_head = int8_lm_head
+        if matvec not in ("exact", "premul"):
+            raise ValueError("matvec must be 'exact' or 'premul'")
+        self.mv = ops.gemv_int8_exact if matvec == "exact" else ops.gemv_int8_premul
         s = shape
         self.kv = np.zeros((s.n_layers, s.Hkv, max_seq, 2, s.HD), np.float32)
         self.angles = ops.rope_angle_table(max_seq, s.HD, s.theta)
@@ -67,17 +76,17 @@ class OracleQwen3:
         s, L = self.s, self.w["layers"][i]
         QD, KVD = s.Hq * s.HD, s.Hkv * s.HD
         qkv = ops.qkv_head(
-            x, L["norm1"], lambda hn: ops.gemv_int8_premul(L["wqkv_q"], L["wqkv_s"], hn),
+            x, L["norm1"], lambda hn: self.mv(L["wqkv_q"], L["wqkv_s"], hn),
             L["qn"], L["kn"], self.angles[pos], s.D, s.HD, s.Hq, s.Hkv, s.eps)
         q = qkv[:QD].reshape(s.Hq, s.HD)
         self.kv[i, :, pos, 0] = qkv[QD:QD + KVD].reshape(s.Hkv, s.HD)
         self.kv[i, :, pos, 1] = qkv[QD + KVD:].reshape(s.Hkv, s.HD)
         ctx = ops.decode_attention(q, self.kv[i, :, :pos + 1, 0], self.kv[i, :, :pos + 1, 1],
                                    pos, s.HD, s.Hq, s.Hkv)
-        a = rnd(ops.gemv_int8_premul(L["wo_q"], L["wo_s"], ctx.reshape(-1)))
+        a = rnd(self.mv(L["wo_q"], L["wo_s"], ctx.reshape(-1)))
 
         def mv(name):
-            return lambda v: ops.gemv_int8_premul(L[name + "_q"], L[name + "_s"], v)
+            return lambda v: self.mv(L[name + "_q"], L[name + "_s"], v)
 
         return ops.swiglu_mlp_kernel_form(x, a, L["norm2"], mv("wg"), mv("wu"), mv("wd"), s.eps)
 
@@ -91,7 +100,7 @@ class OracleQwen3:
         xf = ops.rms_norm_ref(x.reshape(1, -1), self.w["final_norm"], weighted=True,
                               eps=self.s.eps).reshape(-1)
         if self.int8_lm_head:
-            logits = rnd(ops.gemv_int8_premul(self.w["lm_q"], self.w["lm_s"], xf))
+            logits = rnd(self.mv(self.w["lm_q"], self.w["lm_s"], xf))
         else:
             logits = ops.gemv_bf16(self.w["embed"], xf)
         return logits, int(np.argmax(logits))

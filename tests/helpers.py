@@ -36,8 +36,8 @@ def assert_close(got, want, rtol=RTOL, atol=ATOL, what=""):
 
 def assert_ulps(got, want, max_ulp=1, frac_exact=0.0, what=""):
     """bf16 values within ``max_ulp`` units in the last place."""
-    g = round_bits(np.asarray(got, np.float32)).astype(np.int32)
-    w = round_bits(np.asarray(want, np.float32)).astype(np.int32)
+    g = round_bits(np.asarray(got, np.float32).reshape(-1)).astype(np.int32)
+    w = round_bits(np.asarray(want, np.float32).reshape(-1)).astype(np.int32)
     sg = np.where(g >= 0x8000, 0x8000 - g, g)  # sign-magnitude -> ordered integers
     sw = np.where(w >= 0x8000, 0x8000 - w, w)
     d = np.abs(sg - sw)
@@ -45,4 +45,33 @@ def assert_ulps(got, want, max_ulp=1, frac_exact=0.0, what=""):
     assert np.mean(d == 0) >= frac_exact, f"{what}: only {np.mean(d == 0):.4f} bit-exact"
 
 
-__all__ = ["dev_bf16", "dev_u8", "host", "bits", "assert_close", "assert_ulps", "from_bits", "RTOL", "ATOL"]
+def w8_error_bound(q, s_bits, x):
+    """Bound on |kernel - exact| for the int8 GEMV before its bf16 output rounding.
+
+    The kernel rounds each activation to int16 block floating point per quant group
+    (error <= max|x_g| 2^-15 per element) and accumulates the per-chunk integer sums
+    in float32; returns (bfp bound + float32 bound) per output row, (B, M) or (M,)."""
+    q = np.asarray(q, np.float64)
+    s = from_bits(s_bits).astype(np.float64)
+    x = np.atleast_2d(np.asarray(x, np.float64))
+    M, K = q.shape
+    G = K // s.shape[1]
+    qa = np.abs(q).reshape(M, K // G, G).sum(2) * s                        # (M, KG)
+    xmax = np.abs(x).reshape(x.shape[0], K // G, G).max(2)                   # (B, KG)
+    bfp = (xmax * 2.0 ** -15) @ qa.T                                         # (B, M)
+    terms = np.abs(x) @ (np.abs(q) * np.repeat(s, G, axis=1)).T             # (B, M)
+    out = bfp + 1e-6 * terms
+    return out[0] if np.asarray(x).shape[0] == 1 and out.shape[0] == 1 else out
+
+
+def assert_w8_exact(got, q, s_bits, x, what=""):
+    """|kernel - exact dequantised sum| <= one bf16 rounding + 2 * w8_error_bound."""
+    from oracle import ops
+    exact = ops.gemv_int8_exact(q, s_bits, x)
+    got = np.asarray(got, np.float64).reshape(np.shape(exact))
+    lim = 2.0 ** -8 * np.abs(exact) + 2 * w8_error_bound(q, s_bits, x).reshape(np.shape(exact))
+    bad = np.abs(got - exact) > lim
+    assert not bad.any(), f"{what}: {bad.sum()} rows off the exact sum, worst {np.max(np.abs(got - exact) / lim):.3g}"
+
+
+__all__ = ["w8_error_bound", "assert_w8_exact", "dev_bf16", "dev_u8", "host", "bits", "assert_close", "assert_ulps", "from_bits", "RTOL", "ATOL"]

@@ -165,12 +165,30 @@ def test_mlp_kernel_golden_biased_wire(golden):
         assert wire[name].numel() == op.get_arg_spec()[{"wg": 3, "wu": 4, "wd": 5}[name]].shape[0]
     nxt = _out(D)
     gh = _out(FF)
-    op.get_callable()(dev_bf16(g["k_cur"]), dev_bf16(g["k_a"]), dev_bf16(rnd(g["k_npf"])), wire["wg"],
+    npf = rnd(g["k_npf"])
+    op.get_callable()(dev_bf16(g["k_cur"]), dev_bf16(g["k_a"]), dev_bf16(npf), wire["wg"],
                       wire["wu"], wire["wd"], gh, nxt)
     torch.cuda.synchronize()
-    # the reference test's tolerance (swiglu_mlp_dp/test.py:190-191)
-    assert not verify_buffer(host(nxt), "nxt", from_bits(g["k_nxt"]), rel_tol=0.05, abs_tol=0.05)
-    assert_close(host(nxt), from_bits(g["k_nxt"]), what="nxt")
+    W = {n: ((g[f"k_{n}_q"].astype(np.int16) - 128).astype(np.int8), g[f"k_{n}_s"]) for n in ("wg", "wu", "wd")}
+    cur, a = from_bits(g["k_cur"]), from_bits(g["k_a"])
+    exact = ops.swiglu_mlp_kernel_form(cur, a, npf, *(lambda v, n=n: ops.gemv_int8_exact(*W[n], v)
+                                                      for n in ("wg", "wu", "wd")), eps=1e-6)
+    premul = ops.swiglu_mlp_kernel_form(cur, a, npf, *(lambda v, n=n: ops.gemv_int8_premul(*W[n], v)
+                                                       for n in ("wg", "wu", "wd")), eps=1e-6)
+    _check_mlp(host(nxt), exact, premul, from_bits(g["k_nxt"]))
+
+
+def _check_mlp(got, exact_chain, premul_chain, golden, rel=0.05, abs_=0.05):
+    """The kernels compute every int8 matvec as the exact dequantised sum (the
+    operators' reference(), swiglu_mlp_dp/op_ours.py:543-570), so they are held to the
+    kernel-faithful chain with exact matvecs at the BASELINE tolerance.  Against the
+    premul golden (swiglu_mlp_dp/test.py:53-91) the reference test's tolerance
+    (test.py:190-191) applies, widened by how far that golden itself moves when only its
+    matvec rounding changes (|premul chain - exact chain|)."""
+    assert_close(got, exact_chain, what="vs exact-matvec chain")
+    drift = np.abs(np.asarray(premul_chain, np.float64) - np.asarray(exact_chain, np.float64))
+    tol = np.maximum(abs_, rel * (np.abs(got) + np.abs(golden))) + 2 * drift
+    assert np.all(np.abs(got - golden) <= tol), np.max(np.abs(got - golden) / tol)
 
 
 @pytest.mark.parametrize("group", [128, 32])
@@ -198,14 +216,16 @@ def test_mlp_fuse_o_tile_major_wo(group):
     bufs += [_out(FF), _out(D), nxt]
     op.get_callable()(*bufs)
     torch.cuda.synchronize()
-    mv = {k: (lambda v, k=k: ops.gemv_int8_premul(*W[k], v)) for k in W}
-    a = rnd(mv["wo"](cx))
-    want = ops.swiglu_mlp_kernel_form(cur, a, npf, mv["wg"], mv["wu"], mv["wd"], 1e-6)
-    assert_close(host(nxt), want, what="nxt")
+    out = host(nxt)
+    chains = {}
+    for mode, f in (("exact", ops.gemv_int8_exact), ("premul", ops.gemv_int8_premul)):
+        mv = {k: (lambda v, k=k, f=f: f(*W[k], v)) for k in W}
+        chains[mode] = ops.swiglu_mlp_kernel_form(cur, rnd(mv["wo"](cx)), npf, mv["wg"], mv["wu"], mv["wd"], 1e-6)
+    _check_mlp(out, chains["exact"], chains["premul"], chains["premul"])
     # the float32 golden of swiglu_mlp_dp/reference.py:54-67 within the reference's tolerance
     deq = {k: ops.dequant_f32(*W[k]) for k in W}
     f32 = ops.swiglu_mlp_fused_o(cur, cx, npf, deq["wo"], deq["wg"], deq["wu"], deq["wd"], D, FF, QD, 1e-6)
-    assert not verify_buffer(host(nxt), "nxt", f32, rel_tol=0.05, abs_tol=0.05)
+    assert not verify_buffer(out, "nxt", f32, rel_tol=0.05, abs_tol=0.05)
 
 
 def test_mlp_bf16_arm():

@@ -2,12 +2,16 @@
 //
 // Numerics.  The weight stays int8 in registers.  The activations are staged
 // once per CTA in shared memory as int16 block floating point per quant group
-// (exact for bf16 inputs, see bfp_scale), so the inner product of one 16-byte
-// weight chunk is 8 dp2a instructions with exact int32 accumulation; the group
-// scale s[m,g] * 2^(e_g - 15) is applied once per chunk in float32.  The result
-// is the exact dequantised product sum_k q*s*x up to float32 accumulation,
-// which the reference golden (gemv_int8/reference.py:25-40) approximates with
-// its premultiplied bf16(x*s) activations.
+// (see bfp_scale), so the inner product of one 16-byte weight chunk is 8 dp2a
+// instructions with exact int32 accumulation; the group scale
+// s[m,g] * 2^(e_g - 15) is applied once per chunk in float32.  With LO (used at
+// batch 1) each activation also carries a second int16 word holding the next 15
+// bits, X = X_hi + X_lo 2^-15, which makes the staging exact for every bf16
+// value within 22 binades of its group maximum; a second dp2a pass adds it.
+// The result is the exact dequantised product sum_k q*s*x (GEMVInt8.reference,
+// gemv_int8/op.py:173-178) up to float32 accumulation; the kernel-faithful
+// golden (gemv_int8/reference.py:25-40) approximates the same sum with its
+// premultiplied bf16(x*s) activations.
 //
 // Work split.  A CTA is 8 warps.  `ks` warps share one group of NR rows along K
 // (split-K inside the CTA, reduced through shared memory) so small-M GEMVs
@@ -18,15 +22,17 @@
 
 namespace iron {
 
-template <int G, int NB, bool PAIR>
+template <int G, int NB, bool PAIR, bool LO>
 __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
   constexpr int NR = 4;                      // output rows per job
   constexpr int NRW = PAIR ? 2 * NR : NR;    // weight rows per job
+  constexpr int NW = LO ? 2 : 1;             // int16 words per activation
   extern __shared__ __align__(16) uint8_t smem[];
   const int K = p.K;
   const int KG = K / G;
-  uint16_t* xq = (uint16_t*)smem;                                   // [NB][K]
-  float* xs = (float*)(smem + (size_t)NB * K * 2);                  // [NB][KG]
+  uint16_t* xq = (uint16_t*)smem;                                   // [NB][K] (hi words)
+  uint16_t* xl = xq + (size_t)NB * K;                               // [NB][K] (lo words, LO only)
+  float* xs = (float*)(smem + (size_t)NW * NB * K * 2);             // [NB][KG]
   float* red = xs + NB * KG;                                        // [8][NRW][NB]
   float* misc = red + 8 * NRW * NB;                                 // [32]
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -67,7 +73,12 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
       float sc, inv;
       bfp_scale(m, sc, inv);
 #pragma unroll
-      for (int e = 0; e < PER; ++e) base[e] = (uint16_t)(int16_t)__float2int_rn(v[e] * sc);
+      for (int e = 0; e < PER; ++e) {
+        const float t = v[e] * sc;  // exact: v is bf16, sc a power of two
+        const int hi = __float2int_rn(t);
+        base[e] = (uint16_t)(int16_t)hi;
+        if (LO) xl[(base - xq) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+      }
       if (lane == 0) xs[b * KG + g] = inv;
     }
   }
@@ -109,6 +120,11 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
           const uint4 xa = *(const uint4*)(xq + b * K + c * 16);
           const uint4 xb = *(const uint4*)(xq + b * K + c * 16 + 8);
           const float xsc = xs[b * KG + g];
+          uint4 la = make_uint4(0, 0, 0, 0), lb = la;
+          if (LO) {
+            la = *(const uint4*)(xl + b * K + c * 16);
+            lb = *(const uint4*)(xl + b * K + c * 16 + 8);
+          }
 #pragma unroll
           for (int r = 0; r < NRW; ++r) {
             const uint32_t w0 = wv[r].x ^ xm, w1 = wv[r].y ^ xm, w2 = wv[r].z ^ xm, w3 = wv[r].w ^ xm;
@@ -120,7 +136,19 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
             a = __dp2a_hi((int)xb.y, (int)w2, a);
             a = __dp2a_lo((int)xb.z, (int)w3, a);
             a = __dp2a_hi((int)xb.w, (int)w3, a);
-            acc[r][b] = fmaf((float)a, sv[r] * xsc, acc[r][b]);
+            float af = (float)a;
+            if (LO) {
+              int l = __dp2a_lo((int)la.x, (int)w0, 0);
+              l = __dp2a_hi((int)la.y, (int)w0, l);
+              l = __dp2a_lo((int)la.z, (int)w1, l);
+              l = __dp2a_hi((int)la.w, (int)w1, l);
+              l = __dp2a_lo((int)lb.x, (int)w2, l);
+              l = __dp2a_hi((int)lb.y, (int)w2, l);
+              l = __dp2a_lo((int)lb.z, (int)w3, l);
+              l = __dp2a_hi((int)lb.w, (int)w3, l);
+              af = fmaf((float)l, 1.0f / 32768.0f, af);
+            }
+            acc[r][b] = fmaf(af, sv[r] * xsc, acc[r][b]);
           }
         }
       }
@@ -160,15 +188,15 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
   }
 }
 
-template <int G, int NB, bool PAIR>
+template <int G, int NB, bool PAIR, bool LO = (NB == 1)>
 static int launch_t(const GemvW8Params& p, cudaStream_t st) {
   constexpr int NRW = PAIR ? 8 : 4;
-  const size_t smem = (size_t)NB * p.K * 2 + (size_t)NB * (p.K / G) * 4 + 8 * NRW * NB * 4 + 32 * 4;
+  const size_t smem = (size_t)(LO ? 2 : 1) * NB * p.K * 2 + (size_t)NB * (p.K / G) * 4 + 8 * NRW * NB * 4 + 32 * 4;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (smem > 48 * 1024 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemv_w8_kernel<G, NB, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemv_w8_kernel<G, NB, PAIR, LO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          227 * 1024);
     attr_set[dev] = true;
   }
@@ -181,7 +209,7 @@ static int launch_t(const GemvW8Params& p, cudaStream_t st) {
   const int per_sm = smem > 100 * 1024 ? 1 : (smem > 64 * 1024 ? 2 : 4);
   const int maxgrid = iron_num_sms() * per_sm;
   if (grid > maxgrid) grid = maxgrid;
-  gemv_w8_kernel<G, NB, PAIR><<<grid, 256, smem, st>>>(p);
+  gemv_w8_kernel<G, NB, PAIR, LO><<<grid, 256, smem, st>>>(p);
   return iron_check_launch("gemv_w8_kernel");
 }
 

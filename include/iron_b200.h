@@ -161,6 +161,22 @@ int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t* out, int b
                      const int32_t* seq_lens_dev, void* workspace, int64_t workspace_bytes,
                      void* stream);
 
+/* Decode attention that allocates nothing and takes no workspace: for callers
+ * that cannot allocate device memory themselves (a host plugin without an
+ * allocator, a runtime that forbids allocation while decoding).  No counterpart
+ * in the reference.  The split-KV partials live in a fixed 8 MiB array that every
+ * GPU loading the library holds until exit; iron_decode_attn_static_capacity_bytes()
+ * returns that size, and a shape needing more (iron_decode_attn_workspace_bytes)
+ * is rejected with IRON_ERR_UNSUPPORTED.  The first call on a device looks the
+ * array's device address up (cudaGetSymbolAddress) and caches it; make that first
+ * call before any stream capture on that device.  All calls on a device share the
+ * array and keep the last call's contents (each call rewrites all it reads), so
+ * calls that overlap on the GPU race.  Arguments as iron_decode_attn. */
+int64_t iron_decode_attn_static_capacity_bytes(void);
+int iron_decode_attn_static(const uint16_t* q, const uint16_t* kv, uint16_t* out, int batch, int H,
+                            int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
+                            const int32_t* seq_lens_dev, void* stream);
+
 /* ---- fused SwiGLU MLP block ---------------------------------------------------
  * SwiGLUMLPDataParallelOurs (iron/operators/swiglu_mlp_dp/op_ours.py:47-582;
  * golden swiglu_mlp_dp/test.py:79-91, reference.py:8-67):

@@ -37,6 +37,8 @@ SIGNATURES: dict[str, tuple] = {
     "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, I, P, P]),
     "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
+    "iron_decode_attn_static_capacity_bytes": (I64, []),
+    "iron_decode_attn_static": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P]),
     "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),
 }
 

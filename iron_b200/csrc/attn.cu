@@ -238,3 +238,66 @@ combine : {
   return iron_check_launch("attn_combine_kernel");
 }
 }
+
+// ---------------------------------------------------------------------------
+// Decode attention without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory at the point where they call in:
+// a plugin host that owns no allocator and may not call cudaMalloc, an
+// embedding runtime that forbids allocation on its decode path, or code
+// running under a memory pool that rejects ad-hoc requests.  For them the
+// split-KV partials live in one fixed-size array that every GPU loading this
+// library reserves until the process exits.  Each call writes every partial
+// slot it later reads, so nothing has to start at zero and the array keeps
+// whatever the last call left.  All calls on a device share the one array:
+// two calls that run at the same time on the GPU (different streams, or
+// different host threads) overwrite each other's partials.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#define IRON_ATTN_STATIC_SCRATCH_BYTES (8ll << 20)  // 8 MiB per device
+
+static __device__ __align__(256) float g_attn_static_scratch[IRON_ATTN_STATIC_SCRATCH_BYTES / 4];
+
+// Device address of the array for the current device.  The host-side name of
+// a __device__ array is not a device address, so it is looked up once per
+// device with that device current, then cached.
+static int attn_static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "decode_attn_static: cudaGetDevice: %s",
+                                              cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return iron_set_error(IRON_ERR_UNSUPPORTED, "decode_attn_static: device %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return iron_set_error(IRON_ERR_CUDA, "decode_attn_static: cudaGetSymbolAddress: %s",
+                            cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return IRON_OK;
+}
+
+extern "C" int64_t iron_decode_attn_static_capacity_bytes(void) { return IRON_ATTN_STATIC_SCRATCH_BYTES; }
+
+extern "C" int iron_decode_attn_static(const uint16_t* q, const uint16_t* kv, uint16_t* out, int batch, int H,
+                                       int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
+                                       const int32_t* seq_lens_dev, void* stream) {
+  IRON_REQUIRE(batch >= 1 && H >= 1 && HD >= 1 && max_seq >= 1, IRON_ERR_ARG,
+               "decode_attn_static: bad shape batch=%d H=%d HD=%d max_seq=%d", batch, H, HD, max_seq);
+  const int64_t need = iron_decode_attn_workspace_bytes(batch, H, HD, max_seq);
+  IRON_REQUIRE(need <= IRON_ATTN_STATIC_SCRATCH_BYTES, IRON_ERR_UNSUPPORTED,
+               "decode_attn_static: batch=%d H=%d HD=%d max_seq=%d needs %lld bytes of scratch, more than "
+               "the built-in %lld bytes; use iron_decode_attn with a caller workspace",
+               batch, H, HD, max_seq, (long long)need, (long long)IRON_ATTN_STATIC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  int rc = attn_static_scratch(&ws);
+  if (rc) return rc;
+  return iron_decode_attn(q, kv, out, batch, H, KV, HD, max_seq, kv_layout, block_kv, seq_len, seq_lens_dev,
+                          ws, IRON_ATTN_STATIC_SCRATCH_BYTES, stream);
+}

@@ -32,6 +32,9 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 }
 // round a float to the nearest bf16 value (returned as float)
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+// round a double to the nearest bf16 value through float32 (the f64 -> f32 -> bf16
+// path of a float64 result stored by a float32 program)
+__device__ __forceinline__ float rbf_d(double d) { return rbf((float)d); }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
@@ -69,6 +72,23 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// block-wide double sum for blockDim.x <= 1024; `red` holds >= 32 doubles
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  double t = lane < nw ? red[lane] : 0.0;
+  return warp_sum_d(t);
+}
+
 // block-wide sum for blockDim.x <= 1024; `red` holds >= 32 floats
 __device__ __forceinline__ float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
@@ -104,42 +124,44 @@ __device__ __forceinline__ void bfp_scale(float m, float& sc, float& inv) {
   inv = __uint_as_float((uint32_t)ie << 23);
 }
 
-// Weighted RMSNorm in two numerical forms.
-//  mode 0 (kernel form, aie_kernels/aie2p/rms_norm.cc:9-53): float32 sum of
-//    squares, inv = 1/sqrt(sum/n + eps), y = bf16(x * inv * w), one rounding.
+// Weighted RMSNorm in two numerical forms.  The sum of squares is kept in
+// float64 in both, so it does not depend on the reduction order.
+//  mode 0 (kernel form, aie_kernels/aie2p/rms_norm.cc:9-53): x * w / sqrt(mean(x^2)
+//    + eps) evaluated in float64 and rounded once (through float32) to bf16.
 //  mode 1 (golden form, rms_norm/reference.py:8-17 on bf16 tensors): every
 //    torch op rounds to bf16 -- x^2, mean, + eps, sqrt, x / rms, * w.
 struct RmsCoef {
-  float inv, rms;
+  double inv;
+  float rms;
   int mode;
 };
-__device__ __forceinline__ float rms_sq(float v, int mode) {
-  const float s = v * v;
-  return mode ? rbf(s) : s;
+__device__ __forceinline__ double rms_sq(float v, int mode) {
+  const float s = v * v;  // exact in float64; rounded to float32 by mode 1 only
+  return mode ? (double)rbf(s) : (double)v * (double)v;
 }
-__device__ __forceinline__ RmsCoef rms_coef(float sum_sq, int n, float eps, int mode) {
+__device__ __forceinline__ RmsCoef rms_coef(double sum_sq, int n, float eps, int mode) {
   RmsCoef c;
   c.mode = mode;
   if (mode == 0) {
-    c.inv = rsqrtf(sum_sq / (float)n + eps);
+    c.inv = 1.0 / sqrt(sum_sq / (double)n + (double)eps);
     c.rms = 0.f;
   } else {
-    const float mean = rbf(sum_sq / (float)n);
+    const float mean = rbf((float)(sum_sq / (double)n));
     const float ms = rbf(mean + eps);
     c.rms = rbf(sqrtf(ms));
-    c.inv = 0.f;
+    c.inv = 0.0;
   }
   return c;
 }
 // normalised, weighted value before the final bf16 rounding
 __device__ __forceinline__ float rms_apply(float v, float w, const RmsCoef& c) {
-  return c.mode == 0 ? v * c.inv * w : rbf(v / c.rms) * w;
+  return c.mode == 0 ? (float)((double)v * c.inv * (double)w) : rbf(v / c.rms) * w;
 }
 
 // sigmoid via tanh with bf16 rounding after every vector op, the arithmetic of
 // aie_kernels/aie2p/silu.cc (golden: swiglu_mlp_dp/test.py:70-76)
 __device__ __forceinline__ float silu_tanh_bf16(float g /* bf16 value */) {
-  float th = rbf(tanhf(g * 0.5f));
+  float th = rbf((float)tanh((double)(g * 0.5f)));
   float op = rbf(th + 1.0f);
   float sg = rbf(op * 0.5f);
   return rbf(g * sg);

@@ -32,9 +32,9 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
   const int KG = K / G;
   uint16_t* xq = (uint16_t*)smem;                                   // [NB][K] (hi words)
   uint16_t* xl = xq + (size_t)NB * K;                               // [NB][K] (lo words, LO only)
-  float* xs = (float*)(smem + (size_t)NW * NB * K * 2);             // [NB][KG]
-  float* red = xs + NB * KG;                                        // [8][NRW][NB]
-  float* misc = red + 8 * NRW * NB;                                 // [32]
+  double* red = (double*)(smem + (size_t)NW * NB * K * 2);          // [8][NRW][NB]
+  double* misc = red + 8 * NRW * NB;                                // [32]
+  float* xs = (float*)(misc + 32);                                  // [NB][KG]
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int nb = p.nb;
 
@@ -46,9 +46,9 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
       continue;
     }
     if (p.rms_w) {
-      float ss = 0.f;
+      double ss = 0.0;
       for (int i = tid; i < K; i += blockDim.x) ss += rms_sq(bf2f(xr[i]), p.rms_mode);
-      ss = block_sum(ss, misc);
+      ss = block_sum_d(ss, misc);
       const RmsCoef rc = rms_coef(ss, K, p.eps, p.rms_mode);
       for (int i = tid; i < K; i += blockDim.x)
         xq[b * K + i] = f2bf(rms_apply(bf2f(xr[i]), bf2f(p.rms_w[i]), rc));
@@ -92,11 +92,11 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
   const uint32_t xm = p.xor_mask;
   for (int job0 = blockIdx.x * RG; job0 < njobs; job0 += gridDim.x * RG) {
     const int job = job0 + rg;
-    float acc[NRW][NB];
+    double acc[NRW][NB];  // float64: the integer chunk sums are exact, so is their sum
 #pragma unroll
     for (int r = 0; r < NRW; ++r)
 #pragma unroll
-      for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
+      for (int b = 0; b < NB; ++b) acc[r][b] = 0.0;
     if (job < njobs) {
       const uint8_t* pw[NRW];
       const uint16_t* ps[NRW];
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
             a = __dp2a_hi((int)xb.y, (int)w2, a);
             a = __dp2a_lo((int)xb.z, (int)w3, a);
             a = __dp2a_hi((int)xb.w, (int)w3, a);
-            float af = (float)a;
+            long long t = a;
             if (LO) {
               int l = __dp2a_lo((int)la.x, (int)w0, 0);
               l = __dp2a_hi((int)la.y, (int)w0, l);
@@ -146,9 +146,11 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
               l = __dp2a_hi((int)lb.y, (int)w2, l);
               l = __dp2a_lo((int)lb.z, (int)w3, l);
               l = __dp2a_hi((int)lb.w, (int)w3, l);
-              af = fmaf((float)l, 1.0f / 32768.0f, af);
+              t = t * 32768 + l;  // X_hi 2^15 + X_lo, exact in int64
             }
-            acc[r][b] = fmaf(af, sv[r] * xsc, acc[r][b]);
+            // sv * xsc is exact (bf16 times a power of two); so is the float64 product
+            const double sc = LO ? (double)(sv[r] * xsc) * (1.0 / 32768.0) : (double)(sv[r] * xsc);
+            acc[r][b] = fma((double)t, sc, acc[r][b]);
           }
         }
       }
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
     for (int r = 0; r < NRW; ++r)
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
-        float v = warp_sum(acc[r][b]);
+        const double v = warp_sum_d(acc[r][b]);
         if (lane == 0) red[(wid * NRW + r) * NB + b] = v;
       }
     __syncthreads();
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
       const int r = lane / NB, b = lane - (lane / NB) * NB;
       const int row = job * NR + r;
       if (row < p.M && b < nb) {
-        float s0 = 0.f, s1 = 0.f;
+        double s0 = 0.0, s1 = 0.0;
         for (int s = 0; s < KS; ++s) {
           s0 += red[((rg * KS + s) * NRW + r) * NB + b];
           if (PAIR) s1 += red[((rg * KS + s) * NRW + NR + r) * NB + b];
@@ -174,13 +176,13 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
         uint16_t* yo = p.y + (size_t)b * p.ld_y + row;
         if (PAIR) {
           // gh = bf16(silu_tanh(bf16(g)) * bf16(u))  (swiglu_mlp_dp/test.py:87-89)
-          *yo = f2bf(silu_tanh_bf16(rbf(s0)) * rbf(s1));
+          *yo = f2bf(silu_tanh_bf16(rbf_d(s0)) * rbf_d(s1));
         } else if (p.epi == EPI_RESID) {
-          *yo = f2bf(bf2f(p.res[(size_t)b * p.ld_y + row]) + rbf(s0));
+          *yo = f2bf(bf2f(p.res[(size_t)b * p.ld_y + row]) + rbf_d(s0));
         } else if (p.epi == EPI_F32) {
-          ((float*)p.y)[(size_t)b * p.ld_y + row] = s0;
+          ((float*)p.y)[(size_t)b * p.ld_y + row] = (float)s0;
         } else {
-          *yo = f2bf(s0);
+          *yo = f2bf((float)s0);
         }
       }
     }
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(GemvW8Params p) {
 template <int G, int NB, bool PAIR, bool LO = (NB == 1)>
 static int launch_t(const GemvW8Params& p, cudaStream_t st) {
   constexpr int NRW = PAIR ? 8 : 4;
-  const size_t smem = (size_t)(LO ? 2 : 1) * NB * p.K * 2 + (size_t)NB * (p.K / G) * 4 + 8 * NRW * NB * 4 + 32 * 4;
+  const size_t smem = (size_t)(LO ? 2 : 1) * NB * p.K * 2 + 8 * NRW * NB * 8 + 32 * 8 + (size_t)NB * (p.K / G) * 4;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

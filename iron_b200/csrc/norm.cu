@@ -7,12 +7,12 @@ namespace iron {
 // one CTA per row; float32 math, one bf16 rounding (aie_kernels/aie2p/rms_norm.cc:9-53)
 __global__ void rmsnorm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* y, int cols, float eps,
                                int mode) {
-  __shared__ float red[32];
+  __shared__ double red[32];
   const uint16_t* xr = x + (size_t)blockIdx.x * cols;
   uint16_t* yr = y + (size_t)blockIdx.x * cols;
-  float ss = 0.f;
+  double ss = 0.0;
   for (int i = threadIdx.x; i < cols; i += blockDim.x) ss += rms_sq(bf2f(xr[i]), mode);
-  ss = block_sum(ss, red);
+  ss = block_sum_d(ss, red);
   const RmsCoef rc = rms_coef(ss, cols, eps, mode);
   for (int i = threadIdx.x; i < cols; i += blockDim.x) {
     yr[i] = f2bf(rms_apply(bf2f(xr[i]), w ? bf2f(w[i]) : 1.0f, rc));
@@ -66,7 +66,7 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
   const uint16_t* a = ang + (size_t)(ang_is_table ? off / (2 * HD) : b) * HD;
   // lane owns element pairs (i, i + HD/2) for i = lane + 32*j, j < PER/2
   float v[PER];
-  float ss = 0.f;
+  double ss = 0.0;
 #pragma unroll
   for (int j = 0; j < PER / 2; ++j) {
     const int i = lane + 32 * j;
@@ -75,7 +75,7 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
     ss += rms_sq(v[2 * j], norm_mode);
     ss += rms_sq(v[2 * j + 1], norm_mode);
   }
-  ss = warp_sum(ss);
+  ss = warp_sum_d(ss);
   const RmsCoef rc = rms_coef(ss, HD, eps, norm_mode);
   uint16_t o[PER];
 #pragma unroll

@@ -194,6 +194,67 @@ int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, con
                    int group, int domain, uint16_t* x1_ws, uint16_t* gh_ws, uint16_t* nxt,
                    int D, int FF, int QD, int batch, float eps, void* stream);
 
+/* ---- whole decode step ----------------------------------------------------------
+ * One greedy Qwen3 decode token (batch 1) in ONE persistent cooperative kernel:
+ * the Qwen3NPU.__call__ chain (qwen3_npu_int8.py:594-621; runlist :249-281) of
+ * n_layers x [QKV head, decode attention, fused O-proj + SwiGLU MLP], the final
+ * RMSNorm and the lm_head with greedy argmax.  The arithmetic of every stage is
+ * the one of the per-operator entry points above (iron_qkv_head with the golden
+ * RMSNorm form, iron_decode_attn, iron_mlp_block, iron_rmsnorm mode 1,
+ * iron_lm_head_*_argmax).  Weights are in the native wire (tile_m = 1, signed).
+ * Every pointer in the descriptor is a device pointer; `layers` points to a
+ * DEVICE array of n_layers iron_qwen3_layer.  The kernel reads the token from
+ * tok[0] (embed_input != 0) or the hidden state from x, the position from pos[0],
+ * writes the argmax to tok[0] and, when advance != 0, moves pos/seq_len/kv_off one
+ * token on.  Grid barriers and counters live in `sync` (iron_qwen3_sync_words()
+ * int32 words, zero before the first step); every wait is bounded: on timeout
+ * sync[1] holds a nonzero code, the step returns early, and
+ * iron_qwen3_sync_reset() must clear the words before the next step. */
+typedef struct iron_qwen3_layer {
+  const uint16_t* norm1;  /* (D) bf16 */
+  const void* wqkv;       /* ((Hq+2Hkv)*HD, D) wire */
+  const uint16_t* qn;     /* (HD) */
+  const uint16_t* kn;     /* (HD) */
+  const void* wo;         /* (D, Hq*HD) wire */
+  const uint16_t* norm2;  /* (D) */
+  const void* wg;         /* (FF, D) wire */
+  const void* wu;         /* (FF, D) wire */
+  const void* wd;         /* (D, FF) wire */
+} iron_qwen3_layer;
+
+typedef struct iron_qwen3_model {
+  int D, FF, Hq, Hkv, HD, V, n_layers, group, max_seq;
+  float eps;
+  const iron_qwen3_layer* layers;  /* device array */
+  const uint16_t* final_norm;      /* (D) */
+  const uint16_t* embed;           /* (V, D) bf16: embedding, and lm_head when lm_w8 == NULL */
+  const void* lm_w8;               /* (V, D) int8 wire lm_head, or NULL */
+  const uint16_t* angles;          /* (max_seq, HD) interleaved [cos, sin] */
+  uint16_t* kv;                    /* (n_layers, Hkv, 2*max_seq*HD) per-token [K_t|V_t] */
+  uint16_t* x;                     /* (D) residual stream */
+  uint16_t* raw;                   /* ((Hq+2Hkv)*HD) */
+  uint16_t* attn;                  /* (Hq*HD) */
+  uint16_t* x1;                    /* (D) */
+  uint16_t* gh;                    /* (FF) */
+  float* attn_ws;                  /* iron_qwen3_attn_ws_bytes() */
+  void* cand;                      /* iron_qwen3_cand_bytes() */
+  int32_t* tok;
+  int32_t* pos;
+  int32_t* seq_len;
+  int32_t* kv_off;
+  uint16_t* logits;                /* (V) or NULL */
+  int32_t* sync;                   /* iron_qwen3_sync_words() int32, zeroed once */
+} iron_qwen3_model;
+
+int iron_qwen3_sync_words(const iron_qwen3_model* m);
+int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m);
+int64_t iron_qwen3_cand_bytes(void);
+/* Grid size the step kernel will use on the current device (one CTA per SM). */
+int iron_qwen3_grid(const iron_qwen3_model* m);
+int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream);
+/* Zero the sync words (after a timed-out step, or before first use). */
+int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,12 @@ SIGNATURES: dict[str, tuple] = {
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
     "iron_decode_attn_static_capacity_bytes": (I64, []),
     "iron_decode_attn_static": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P]),
+    "iron_qwen3_sync_words": (I, [P]),
+    "iron_qwen3_attn_ws_bytes": (I64, [P]),
+    "iron_qwen3_cand_bytes": (I64, []),
+    "iron_qwen3_grid": (I, [P]),
+    "iron_qwen3_decode_step": (I, [P, I, I, P]),
+    "iron_qwen3_sync_reset": (I, [P, P]),
     "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),
 }
 

@@ -17,6 +17,7 @@ payload) with quant group ``group`` (32 by default, as BASELINE's configs).
 
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 import numpy as np
@@ -151,6 +152,20 @@ class Qwen3Weights:
         return out
 
 
+class _StepLayer(C.Structure):
+    """iron_qwen3_layer (include/iron_b200.h)."""
+    _fields_ = [(n, C.c_void_p) for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd")]
+
+
+class _StepModel(C.Structure):
+    """iron_qwen3_model (include/iron_b200.h)."""
+    _fields_ = ([(n, C.c_int) for n in ("D", "FF", "Hq", "Hkv", "HD", "V", "n_layers", "group", "max_seq")]
+                + [("eps", C.c_float)]
+                + [(n, C.c_void_p) for n in ("layers", "final_norm", "embed", "lm_w8", "angles", "kv", "x", "raw",
+                                             "attn", "x1", "gh", "attn_ws", "cand", "tok", "pos", "seq_len",
+                                             "kv_off", "logits", "sync")])
+
+
 class Qwen3B200:
     """Greedy Qwen3 decoder over ``batch`` independent streams on one GPU.
 
@@ -160,7 +175,7 @@ class Qwen3B200:
     (as check_cosine_int8.py:51-52 does) and then decodes greedily."""
 
     def __init__(self, weights: Qwen3Weights, max_seq: int, batch: int = 1, lm_head: str = "bf16",
-                 use_graph: bool = True, keep_logits: bool = False, device="cuda"):
+                 use_graph: bool = True, keep_logits: bool = False, device="cuda", impl: str | None = None):
         cfg = weights.cfg
         self.cfg, self.w, self.max_seq, self.B = cfg, weights, max_seq, batch
         if lm_head not in ("bf16", "int8"):
@@ -183,18 +198,60 @@ class Qwen3B200:
         self.kv = torch.zeros(L, B, cfg.Hkv, 2 * max_seq * cfg.HD, **bf)
         self.angles = rope_angle_table(max_seq, cfg.HD, cfg.theta).to(dev)
         self.logits = torch.zeros(B, cfg.V, **bf) if keep_logits else None
-        # device params: token ids, positions, valid lengths, KV element offsets
-        self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.len = torch.ones(B, dtype=torch.int32, device=dev)
-        self.off = torch.zeros(B, dtype=torch.int32, device=dev)
+        # device params: token ids, positions, valid lengths, KV element offsets (one
+        # tensor so that a step's (token, position) input is a single 8-byte copy)
+        self.params = torch.zeros(4, B, dtype=torch.int32, device=dev)
+        self.params[2] = 1
+        self.tok, self.pos, self.len, self.off = self.params[0], self.params[1], self.params[2], self.params[3]
+        self.host_params = torch.zeros(2, B, dtype=torch.int32, pin_memory=True)
         self.attn_ws = torch.empty(_lib.lib().iron_decode_attn_workspace_bytes(B, cfg.Hq, cfg.HD, max_seq),
                                    dtype=torch.uint8, device=dev)
         self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
-        self.host_in = torch.zeros(2 * B, dtype=torch.int32, pin_memory=True)
-        self.host_tok = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
+        # "step": the whole token in one persistent kernel (batch 1);
+        # "ops": the chained per-operator kernels, replayed as a CUDA graph
+        self.impl = impl or ("step" if batch == 1 else "ops")
+        if self.impl not in ("step", "ops"):
+            raise ValueError("impl must be 'step' or 'ops'")
+        if self.impl == "step":
+            if batch != 1:
+                raise ValueError("the persistent step kernel decodes one stream (batch 1)")
+            self._init_step(dev)
+
+    def _init_step(self, dev):
+        c, w = self.cfg, self.w
+        layers = (_StepLayer * len(w.layers))()
+        for i, Lw in enumerate(w.layers):
+            for n in _StepLayer._fields_:
+                setattr(layers[i], n[0], ptr(Lw[n[0]]))
+        self._layer_table = torch.frombuffer(bytearray(bytes(layers)), dtype=torch.uint8).to(dev)
+        m = _StepModel()
+        m.D, m.FF, m.Hq, m.Hkv, m.HD, m.V = c.D, c.FF, c.Hq, c.Hkv, c.HD, c.V
+        m.n_layers, m.group, m.max_seq, m.eps = len(w.layers), w.group, self.max_seq, c.eps
+        m.layers = ptr(self._layer_table)
+        m.final_norm, m.embed = ptr(w.final_norm), ptr(w.embed)
+        m.lm_w8 = ptr(w.lm_wire) if self.lm_head == "int8" else None
+        m.angles, m.kv = ptr(self.angles), ptr(self.kv)
+        m.x, m.raw, m.attn, m.x1, m.gh = ptr(self.x), ptr(self.raw), ptr(self.attn), ptr(self.x1), ptr(self.gh)
+        L = _lib.lib()
+        mp = C.byref(m)
+        self.step_ws = torch.empty(L.iron_qwen3_attn_ws_bytes(mp), dtype=torch.uint8, device=dev)
+        self.cand = torch.empty(L.iron_qwen3_cand_bytes(), dtype=torch.uint8, device=dev)
+        self.sync = torch.zeros(L.iron_qwen3_sync_words(mp), dtype=torch.int32, device=dev)
+        m.attn_ws, m.cand = ptr(self.step_ws), ptr(self.cand)
+        m.tok, m.pos, m.seq_len, m.kv_off = ptr(self.tok), ptr(self.pos), ptr(self.len), ptr(self.off)
+        m.logits = ptr(self.logits) if self.logits is not None else None
+        m.sync = ptr(self.sync)
+        self._model = m
+
+    def check(self):
+        """Raise if a persistent step timed out on one of its bounded waits."""
+        if self.impl == "step":
+            err = int(self.sync[1].item())
+            if err:
+                abi("iron_qwen3_sync_reset", C.byref(self._model), self.stream.cuda_stream)
+                raise RuntimeError(f"decode step aborted on a bounded device wait (code {err})")
 
     # ---- the step, as a flat list of ABI launches ----
     def _launch_step(self, from_tokens: bool, advance: bool, st: int):
@@ -226,6 +283,8 @@ class Qwen3B200:
         """Kernels one step launches: embedding, 7 per layer (QKV GEMV + head epilogue,
         attention split + combine, O / gate-up / down GEMVs), final RMSNorm, lm_head
         (+ argmax passes) and the position advance."""
+        if self.impl == "step":
+            return 1
         head = 2 if self.lm_head == "bf16" else 3
         return int(from_tokens) + 7 * len(self.w.layers) + 1 + head + int(advance)
 
@@ -248,6 +307,9 @@ class Qwen3B200:
         """Enqueue one decode step on ``self.stream`` (graph replay when enabled)."""
         st = self.stream
         key = (from_tokens, advance)
+        if self.impl == "step":
+            abi("iron_qwen3_decode_step", C.byref(self._model), int(from_tokens), int(advance), st.cuda_stream)
+            return
         with torch.cuda.stream(st):
             if not self.use_graph:
                 self._launch_step(from_tokens, advance, st.cuda_stream)
@@ -272,25 +334,42 @@ class Qwen3B200:
         self.kv.zero_()
         self.set_position(0)
 
+    def _read_tokens(self) -> torch.Tensor:
+        """Next tokens to the host; the persistent step's error word rides along."""
+        if self.impl == "step":
+            with torch.cuda.stream(self.stream):
+                both = torch.cat([self.tok, self.sync[1:2]]).cpu()
+            if int(both[-1]):
+                self.check()
+            return both[:-1]
+        out = self.tok.cpu()
+        return out
+
+    def _put_inputs(self, tokens, pos):
+        """(token, position) per stream -> device in one copy from pinned memory."""
+        self.host_params[0] = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).expand(self.B)
+        self.host_params[1] = torch.as_tensor(pos, dtype=torch.int32).reshape(-1).expand(self.B)
+        with torch.cuda.stream(self.stream):
+            self.params[0:2].copy_(self.host_params, non_blocking=True)
+            if self.impl == "ops":  # the chained kernels read the derived length / offset too
+                self.len.copy_(self.pos + 1)
+                self.off.copy_(self.pos * (2 * self.cfg.HD))
+
     def __call__(self, x, seq_pos: int) -> int:
         """Qwen3NPU.__call__: hidden state (D,) bf16 of the new token -> argmax token."""
         if self.B != 1:
             raise ValueError("__call__ is the batch-1 interface; use step_tokens for batches")
-        self.set_position(seq_pos)
+        self._put_inputs(0, seq_pos)
         with torch.cuda.stream(self.stream):
             self.x[0].copy_(torch.as_tensor(x).to(torch.bfloat16).reshape(-1), non_blocking=False)
         self.run_step(from_tokens=False, advance=False)
-        self.stream.synchronize()
-        return int(self.tok[0].item())
+        return int(self._read_tokens()[0])
 
     def step_tokens(self, tokens, pos) -> torch.Tensor:
         """One step for B streams from token ids at positions ``pos`` -> next tokens (host)."""
-        self.set_position(pos)
-        with torch.cuda.stream(self.stream):
-            self.tok.copy_(torch.as_tensor(tokens, dtype=torch.int32).reshape(self.B).to(self.tok.device))
+        self._put_inputs(tokens, pos)
         self.run_step(from_tokens=True, advance=False)
-        self.stream.synchronize()
-        return self.tok.cpu()
+        return self._read_tokens()
 
     def generate(self, prompt, n_new: int) -> list:
         """Prefill ``prompt`` (ids, batch 1) token by token, then greedy-decode ``n_new`` tokens.
@@ -313,4 +392,5 @@ class Qwen3B200:
             with torch.cuda.stream(self.stream):
                 hist[i].copy_(self.tok[0])
         self.stream.synchronize()
+        self.check()
         return hist.cpu().tolist()

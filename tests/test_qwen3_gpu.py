@@ -25,11 +25,12 @@ def small():
     return cfg, w
 
 
+@pytest.mark.parametrize("impl", ["step", "ops"])
 @pytest.mark.parametrize("lm_head", ["bf16", "int8"])
-def test_two_layer_decode_matches_oracle(small, lm_head):
+def test_two_layer_decode_matches_oracle(small, lm_head, impl):
     cfg, w = small
     S = 64
-    dec = Qwen3B200(w, max_seq=S, lm_head=lm_head, keep_logits=True)
+    dec = Qwen3B200(w, max_seq=S, lm_head=lm_head, keep_logits=True, impl=impl)
     shape = Qwen3Shape(n_layers=2, group=32)
     orc = OracleQwen3(shape, w.to_numpy(), S, int8_lm_head=(lm_head == "int8"))
     rng = np.random.default_rng(0)
@@ -56,14 +57,69 @@ def test_call_interface_matches_step_tokens(small):
         assert a(x, pos) == int(b.step_tokens([t], pos)[0])
 
 
-def test_graph_replay_equals_eager_full_model():
+@pytest.fixture(scope="module")
+def full():
     cfg = Qwen3Config.qwen3_0_6b()
-    w = Qwen3Weights.synthetic(cfg, seed=2, group=32)
+    return cfg, Qwen3Weights.synthetic(cfg, seed=2, group=32)
+
+
+def test_graph_replay_equals_eager_full_model(full):
+    cfg, w = full
     prompt = list(range(100, 140))
-    g = Qwen3B200(w, max_seq=128, use_graph=True).generate(prompt, 24)
-    e = Qwen3B200(w, max_seq=128, use_graph=False).generate(prompt, 24)
+    g = Qwen3B200(w, max_seq=128, use_graph=True, impl="ops").generate(prompt, 24)
+    e = Qwen3B200(w, max_seq=128, use_graph=False, impl="ops").generate(prompt, 24)
     assert g == e
-    assert Qwen3B200(w, max_seq=128).generate(prompt, 24) == g
+    assert Qwen3B200(w, max_seq=128, impl="ops").generate(prompt, 24) == g
+
+
+def test_step_kernel_equals_chained_kernels_full_model(full):
+    """The persistent one-launch step (28 layers + lm_head + argmax) against the chained
+    per-operator kernels on the same weights: same greedy tokens, close logits."""
+    cfg, w = full
+    prompt = [int(t) for t in np.random.default_rng(3).integers(0, cfg.V, 70)]
+    a = Qwen3B200(w, max_seq=256, impl="step", keep_logits=True)
+    b = Qwen3B200(w, max_seq=256, impl="ops", keep_logits=True)
+    for p, t in enumerate(prompt):
+        ta, tb = int(a.step_tokens([t], p)[0]), int(b.step_tokens([t], p)[0])
+        assert ta == tb, f"position {p}"
+        if p % 23 == 0:
+            assert_close(host(a.logits[0]), host(b.logits[0]), what=f"logits pos {p}")
+    assert a.generate(prompt, 40) == b.generate(prompt, 40)
+
+
+def test_step_kernel_long_context_matches_oracle():
+    """A 1-layer model decoding past several attention splits (ragged last split): at
+    the checked positions the oracle gets the GPU's KV cache and must reproduce the
+    logits and the token."""
+    cfg = Qwen3Config.qwen3_0_6b()
+    w = Qwen3Weights.synthetic(cfg, seed=5, group=32, n_layers=1)
+    S = 1600
+    dec = Qwen3B200(w, max_seq=S, keep_logits=True, impl="step")
+    orc = OracleQwen3(Qwen3Shape(n_layers=1), w.to_numpy(), S)
+    toks = [int(t) for t in np.random.default_rng(9).integers(0, cfg.V, S)]
+    checks = {0, 17, 143, 144, 145, 1000, 1599}
+    for pos in range(S):
+        got = int(dec.step_tokens([toks[pos]], pos)[0])
+        if pos in checks:
+            kv = host(dec.kv[0, 0]).reshape(cfg.Hkv, S, 2, cfg.HD)
+            orc.kv[0, :, :pos] = kv[:, :pos]
+            logits, want = orc.step(orc.embed(toks[pos]), pos)
+            assert_close(host(dec.logits[0]), logits, what=f"pos {pos}")
+            assert got == want, f"pos {pos}"
+            assert_close(kv[:, pos], orc.kv[0, :, pos], what=f"K/V written at {pos}")
+
+
+def test_step_error_word_aborts_and_resets(small):
+    """A nonzero error word makes every CTA leave at its first wait; the host sees it,
+    clears the sync words, and the next step runs normally."""
+    cfg, w = small
+    dec = Qwen3B200(w, max_seq=32, impl="step")
+    want = int(dec.step_tokens([5], 0)[0])
+    dec.sync[1] = 7
+    with pytest.raises(RuntimeError, match="bounded device wait"):
+        dec.step_tokens([5], 0)
+    assert int(dec.sync.abs().sum()) == 0
+    assert int(dec.step_tokens([5], 0)[0]) == want
 
 
 def test_batched_streams_match_single_stream(small):

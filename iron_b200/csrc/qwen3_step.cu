@@ -35,7 +35,7 @@ constexpr int HDIM = 128;       // head_dim of the step kernel
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
 
 enum { SYNC_BAR = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_HEAD0 = 3 };
-enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_COUNTER = 3 };
+enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_INPUT = 3 };
 
 struct Kp {
   iron_qwen3_model m;
@@ -618,6 +618,12 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
   const int QD = m.Hq * HDIM, QKV = (m.Hq + 2 * m.Hkv) * HDIM;
   const int pos = m.pos[0];
   const int unit = blockIdx.x < m.Hkv * p.nsplit ? (int)blockIdx.x : -1;
+  // a position outside the cache or a token outside the vocabulary: record and leave
+  // before touching memory (every CTA takes the same decision)
+  if (pos < 0 || pos >= m.max_seq || (p.embed_input && (m.tok[0] < 0 || m.tok[0] >= m.V))) {
+    if (tid == 0) atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_INPUT);
+    return;
+  }
 
   if (tid == 0) {
     mbar_init(&S.mbar[0]);

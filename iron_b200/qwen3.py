@@ -342,8 +342,8 @@ class Qwen3B200:
             if int(both[-1]):
                 self.check()
             return both[:-1]
-        out = self.tok.cpu()
-        return out
+        with torch.cuda.stream(self.stream):
+            return self.tok.cpu()
 
     def _put_inputs(self, tokens, pos):
         """(token, position) per stream -> device in one copy from pinned memory."""

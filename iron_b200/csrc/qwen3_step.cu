@@ -37,9 +37,11 @@ constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
 enum { SYNC_BAR = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_HEAD0 = 3 };
 enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_INPUT = 3 };
 
+constexpr int SMAX = 16;  // most attention splits per KV head
+
 struct Kp {
   iron_qwen3_model m;
-  int embed_input, advance, nsplit, kmax;
+  int embed_input, advance, smax, kmax;
 };
 
 // ---------------------------------------------------------------------------
@@ -93,6 +95,7 @@ struct Smem {
   float* xs;      // [kmax / 32]
   float* xf;      // [D] lm_head activations (bf16 path)
   float* att;     // attention scratch
+  float* mrg;     // split-merge scratch: [Hq][SMAX] weights, [Hq] sums
   double* red;    // [32]
   uint64_t* mbar; // [2]
   int* flag;      // [4]
@@ -120,12 +123,15 @@ __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
   s.xf = (float*)(base + o);
   o += (size_t)p.m.D * 4;
   s.att = (float*)(base + o);
+  o += (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
+  s.mrg = (float*)(base + o);
   return s;
 }
 
-__host__ __device__ inline size_t smem_bytes(int kmax, int D, int GQ) {
+__host__ __device__ inline size_t smem_bytes(int kmax, int D, int GQ, int Hq) {
   const size_t att = (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
-  return 2 * (size_t)BUF + (size_t)kmax * 4 + 32 * 8 + 16 + 16 + (size_t)(kmax / 32) * 4 + (size_t)D * 4 + att;
+  const size_t mrg = (size_t)(Hq * SMAX + Hq) * 4;
+  return 2 * (size_t)BUF + (size_t)kmax * 4 + 32 * 8 + 16 + 16 + (size_t)(kmax / 32) * 4 + (size_t)D * 4 + att + mrg;
 }
 
 // ---------------------------------------------------------------------------
@@ -292,130 +298,208 @@ __device__ bool wait_buf(const Smem& S, int32_t* sync, int b, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------
-// activation staging (identical arithmetic to gemv_w8_kernel's prologue)
+// activation staging (the arithmetic of gemv_w8_kernel's prologue)
 // ---------------------------------------------------------------------------
-// in-place: xhi holds bf16 bits of K values -> int16 hi words, xlo lo words, xs factors
+// K bf16 values (K % 8 == 0) from global memory to shared memory with 16-byte
+// loads issued back to back; `copy_to` (global) receives the same bits.
+__device__ __forceinline__ void load_bits(uint16_t* dst, const uint16_t* src, int K, bool readonly,
+                                          uint16_t* copy_to = nullptr) {
+  const int n16 = K >> 3;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n16; i += NT) {
+    const uint4 v = readonly ? __ldg(((const uint4*)src) + i) : __ldcg(((const uint4*)src) + i);
+    ((uint4*)dst)[i] = v;
+    if (copy_to) ((uint4*)copy_to)[i] = v;
+  }
+}
+
+// In place: xhi holds the bf16 bits of K values -> int16 hi words; xlo lo words;
+// xs the group factors.  Eight lanes per quant group.
 __device__ void bfp_stage(const Smem& S, int K, int G) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int per = G / 32;
-  for (int gi = wid; gi < K / G; gi += NWARP) {
-    uint16_t* base = S.xhi + gi * G + lane * per;
-    float v[4];
+  const int sub = lane >> 3, sl = lane & 7, per = G / 8;
+  const int ng = K / G;
+  for (int g0 = wid * 4; g0 < ng; g0 += NWARP * 4) {
+    const int gi = g0 + sub;
+    const bool valid = gi < ng;
+    uint16_t* base = S.xhi + (size_t)(valid ? gi : 0) * G + sl * per;
+    float v[16];
     float mx = 0.f;
-    for (int e = 0; e < per; ++e) {
-      v[e] = bf2f(base[e]);
-      mx = fmaxf(mx, fabsf(v[e]));
-    }
-    mx = warp_max(mx);
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (e < per) {
+        v[e] = valid ? bf2f(base[e]) : 0.f;
+        mx = fmaxf(mx, fabsf(v[e]));
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     float sc, inv;
     bfp_scale(mx, sc, inv);
-    for (int e = 0; e < per; ++e) {
-      const float t = v[e] * sc;
-      const int hi = __float2int_rn(t);
-      base[e] = (uint16_t)(int16_t)hi;
-      S.xlo[(base - S.xhi) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+    if (valid) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (e < per) {
+          const float t = v[e] * sc;
+          const int hi = __float2int_rn(t);
+          base[e] = (uint16_t)(int16_t)hi;
+          S.xlo[(base - S.xhi) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+        }
+      if (sl == 0) S.xs[gi] = inv;
     }
-    if (lane == 0) S.xs[gi] = inv;
   }
 }
 
-// RMSNorm(src) * w -> bf16 bits in xhi (mode 0 kernel form, 1 golden form); also
-// returns the normalised values as floats in `outf` when non-null
+// RMSNorm(src) * w -> bf16 bits in xhi (mode 0 kernel form, 1 golden form);
+// `outf` (shared) receives the values as floats when non-null.  Uses xlo as scratch.
 __device__ void stage_rmsnorm(const Smem& S, const uint16_t* src, bool src_readonly, const uint16_t* w, int K,
                               float eps, int mode, float* outf, uint16_t* copy_to) {
-  constexpr int MAXV = 16;  // K <= NT * MAXV
-  float v[MAXV];
+  load_bits(S.xhi, src, K, src_readonly, copy_to);
+  load_bits(S.xlo, w, K, true);
+  __syncthreads();
   double ss = 0.0;
-  int n = 0;
-  for (int i = threadIdx.x; i < K; i += NT, ++n) {
-    v[n] = bf2f(src_readonly ? __ldg(src + i) : ldcg_u16(src + i));
-    ss += rms_sq(v[n], mode);
-  }
+  for (int i = threadIdx.x; i < K; i += NT) ss += rms_sq(bf2f(S.xhi[i]), mode);
   ss = block_sum_d(ss, S.red);
   const RmsCoef rc = rms_coef(ss, K, eps, mode);
-  n = 0;
-  for (int i = threadIdx.x; i < K; i += NT, ++n) {
-    const uint16_t o = f2bf(rms_apply(v[n], bf2f(__ldg(w + i)), rc));
+  for (int i = threadIdx.x; i < K; i += NT) {
+    const uint16_t o = f2bf(rms_apply(bf2f(S.xhi[i]), bf2f(S.xlo[i]), rc));
     S.xhi[i] = o;
     if (outf) outf[i] = bf2f(o);
-    if (copy_to) copy_to[i] = f2bf(v[n]);
   }
 }
 
-__device__ void stage_copy(const Smem& S, const uint16_t* src, int K) {
-  for (int i = threadIdx.x; i < K; i += NT) S.xhi[i] = (uint16_t)ldcg_u16(src + i);
-}
-
 // ---------------------------------------------------------------------------
-// int8 row dot product from shared memory: sum_k q*s*x as in gemv_w8_kernel (LO)
+// int8 rows from shared memory, R (or 2R for gate/up pairs) rows per warp at once:
+// sum_k q*s*x exactly as gemv_w8_kernel with LO staging and float64 accumulation
 // ---------------------------------------------------------------------------
-template <int G>
-__device__ __forceinline__ double row_dot(const uint8_t* row, int K, const Smem& S) {
+template <int G, int NR>
+__device__ __forceinline__ void rows_dot(const uint8_t* const (&rp)[NR], int K, const Smem& S, double (&out)[NR]) {
   const int lane = threadIdx.x & 31;
-  const uint16_t* sc = (const uint16_t*)(row + K);
-  double acc = 0.0;
+  double acc[NR];
+#pragma unroll
+  for (int i = 0; i < NR; ++i) acc[i] = 0.0;
   for (int c = lane; c < (K >> 4); c += 32) {
-    const uint4 w = *(const uint4*)(row + c * 16);
     const int g = (c * 16) / G;
-    const float sv = bf2f(sc[g]);
     const uint4 xa = *(const uint4*)(S.xhi + c * 16), xb = *(const uint4*)(S.xhi + c * 16 + 8);
     const uint4 la = *(const uint4*)(S.xlo + c * 16), lb = *(const uint4*)(S.xlo + c * 16 + 8);
-    int a = __dp2a_lo((int)xa.x, (int)w.x, 0);
-    a = __dp2a_hi((int)xa.y, (int)w.x, a);
-    a = __dp2a_lo((int)xa.z, (int)w.y, a);
-    a = __dp2a_hi((int)xa.w, (int)w.y, a);
-    a = __dp2a_lo((int)xb.x, (int)w.z, a);
-    a = __dp2a_hi((int)xb.y, (int)w.z, a);
-    a = __dp2a_lo((int)xb.z, (int)w.w, a);
-    a = __dp2a_hi((int)xb.w, (int)w.w, a);
-    int l = __dp2a_lo((int)la.x, (int)w.x, 0);
-    l = __dp2a_hi((int)la.y, (int)w.x, l);
-    l = __dp2a_lo((int)la.z, (int)w.y, l);
-    l = __dp2a_hi((int)la.w, (int)w.y, l);
-    l = __dp2a_lo((int)lb.x, (int)w.z, l);
-    l = __dp2a_hi((int)lb.y, (int)w.z, l);
-    l = __dp2a_lo((int)lb.z, (int)w.w, l);
-    l = __dp2a_hi((int)lb.w, (int)w.w, l);
-    const long long t = (long long)a * 32768 + l;
-    acc = fma((double)t, (double)(sv * S.xs[g]) * (1.0 / 32768.0), acc);
+    const float xsc = S.xs[g];
+    uint4 w[NR];
+    float sv[NR];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      w[i] = *(const uint4*)(rp[i] + c * 16);
+      sv[i] = bf2f(((const uint16_t*)(rp[i] + K))[g]);
+    }
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      int a = __dp2a_lo((int)xa.x, (int)w[i].x, 0);
+      a = __dp2a_hi((int)xa.y, (int)w[i].x, a);
+      a = __dp2a_lo((int)xa.z, (int)w[i].y, a);
+      a = __dp2a_hi((int)xa.w, (int)w[i].y, a);
+      a = __dp2a_lo((int)xb.x, (int)w[i].z, a);
+      a = __dp2a_hi((int)xb.y, (int)w[i].z, a);
+      a = __dp2a_lo((int)xb.z, (int)w[i].w, a);
+      a = __dp2a_hi((int)xb.w, (int)w[i].w, a);
+      int l = __dp2a_lo((int)la.x, (int)w[i].x, 0);
+      l = __dp2a_hi((int)la.y, (int)w[i].x, l);
+      l = __dp2a_lo((int)la.z, (int)w[i].y, l);
+      l = __dp2a_hi((int)la.w, (int)w[i].y, l);
+      l = __dp2a_lo((int)lb.x, (int)w[i].z, l);
+      l = __dp2a_hi((int)lb.y, (int)w[i].z, l);
+      l = __dp2a_lo((int)lb.z, (int)w[i].w, l);
+      l = __dp2a_hi((int)lb.w, (int)w[i].w, l);
+      const long long t = (long long)a * 32768 + l;
+      acc[i] = fma((double)t, (double)(sv[i] * xsc) * (1.0 / 32768.0), acc[i]);
+    }
   }
-  return warp_sum_d(acc);
+#pragma unroll
+  for (int i = 0; i < NR; ++i) out[i] = warp_sum_d(acc[i]);
 }
 
-// bf16 row dot with float32 activations (the lm_head of gemv_bf16_kernel)
-__device__ __forceinline__ float row_dot_bf16(const uint8_t* row, int K, const float* xf) {
-  const int lane = threadIdx.x & 31;
-  float a = 0.f;
-  for (int c = lane; c < (K >> 3); c += 32) {
-    const uint4 w = *(const uint4*)(row + c * 16);
-    const float4 x0 = *(const float4*)(xf + c * 8), x1 = *(const float4*)(xf + c * 8 + 4);
-    a = fmaf(bf_lo(w.x), x0.x, a);
-    a = fmaf(bf_hi(w.x), x0.y, a);
-    a = fmaf(bf_lo(w.y), x0.z, a);
-    a = fmaf(bf_hi(w.y), x0.w, a);
-    a = fmaf(bf_lo(w.z), x1.x, a);
-    a = fmaf(bf_hi(w.z), x1.y, a);
-    a = fmaf(bf_lo(w.w), x1.z, a);
-    a = fmaf(bf_hi(w.w), x1.w, a);
+// the rows of one chunk: n rows (pairs when PAIR: gate rows then up rows) of rb bytes
+template <int G, int R, bool PAIR, class Epi>
+__device__ void chunk_rows(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
+  constexpr int NR = PAIR ? 2 * R : R;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int r0 = wid * R; r0 < n; r0 += NWARP * R) {
+    const uint8_t* rp[NR];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int r = min(r0 + i, n - 1);
+      rp[i] = wb + (size_t)r * rb;
+      if (PAIR) rp[R + i] = wb + (size_t)(n + r) * rb;
+    }
+    double out[NR];
+    rows_dot<G, NR>(rp, K, S, out);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        if (r0 + i < n) epi(r0 + i, out[i], PAIR ? out[R + i] : 0.0);
+    }
   }
-  return warp_sum(a);
+}
+
+template <int G, bool PAIR, class Epi>
+__device__ void chunk_gemv(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
+  const int R = (n + NWARP - 1) / NWARP;
+  if (R <= 1)
+    chunk_rows<G, 1, PAIR>(wb, n, rb, K, S, epi);
+  else if (R == 2)
+    chunk_rows<G, 2, PAIR>(wb, n, rb, K, S, epi);
+  else if (R == 3)
+    chunk_rows<G, 3, PAIR>(wb, n, rb, K, S, epi);
+  else
+    chunk_rows<G, 4, PAIR>(wb, n, rb, K, S, epi);
+}
+
+// bf16 rows with float32 activations: the lm_head arithmetic of gemv_bf16_kernel
+template <int R>
+__device__ __forceinline__ void rows_dot_bf16(const uint8_t* const (&rp)[R], int K, const float* xf, float (&out)[R]) {
+  const int lane = threadIdx.x & 31;
+  float a[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) a[i] = 0.f;
+  for (int c = lane; c < (K >> 3); c += 32) {
+    const float4 x0 = *(const float4*)(xf + c * 8), x1 = *(const float4*)(xf + c * 8 + 4);
+    uint4 w[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) w[i] = *(const uint4*)(rp[i] + c * 16);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      a[i] = fmaf(bf_lo(w[i].x), x0.x, a[i]);
+      a[i] = fmaf(bf_hi(w[i].x), x0.y, a[i]);
+      a[i] = fmaf(bf_lo(w[i].y), x0.z, a[i]);
+      a[i] = fmaf(bf_hi(w[i].y), x0.w, a[i]);
+      a[i] = fmaf(bf_lo(w[i].z), x1.x, a[i]);
+      a[i] = fmaf(bf_hi(w[i].z), x1.y, a[i]);
+      a[i] = fmaf(bf_lo(w[i].w), x1.z, a[i]);
+      a[i] = fmaf(bf_hi(w[i].w), x1.w, a[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
 }
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
+// splits per KV head for a context of L positions (about 128 positions each)
+__device__ __forceinline__ int att_splits(int L, int smax) {
+  const int s = (L + 127) / 128;
+  return s < 1 ? 1 : (s > smax ? smax : s);
+}
+
 // ---------------------------------------------------------------------------
-// attention unit: one KV head, one split of the positions
+// attention unit: one KV head, one split of the positions; writes the split's
+// partial (o, m, l) per query head.  The merge happens in the O-proj prologue.
 // ---------------------------------------------------------------------------
 template <int GQ>
-__device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, int P, int32_t* sync) {
+__device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P) {
   const iron_qwen3_model& m = p.m;
   constexpr int PER = HDIM / 32;
   constexpr int U = 4;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int ns = p.nsplit;
-  const int h = unit / ns, s = unit - h * ns;
   const int L = P + 1;
   const int chunk = (L + ns - 1) / ns;
   const int start = s * chunk, end = min(L, start + chunk);
@@ -425,54 +509,58 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, 
   float* part = vt + HDIM;             // [NWARP][GQ][HD+2]
   uint16_t* head = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
   const uint16_t* ang = m.angles + (size_t)P * HDIM;
-  const int QKV = (m.Hq + 2 * m.Hkv) * HDIM;
-  (void)QKV;
-  // per-head q/k RMSNorm (golden form) + RoPE, v copy: the arithmetic of qk_norm_rope_kv_kernel
+  const bool owner = P >= start && P < end;
+  // per-head q/k RMSNorm (golden form) + RoPE and the v copy: qk_norm_rope_kv_kernel's arithmetic
   for (int t = wid; t < GQ + 2; t += NWARP) {
     if (t == GQ + 1) {
       const uint16_t* vs = m.raw + (size_t)(m.Hq + m.Hkv + h) * HDIM;
-      for (int i = lane; i < HDIM; i += 32) {
-        const uint16_t v = (uint16_t)ldcg_u16(vs + i);
-        vt[i] = bf2f(v);
-        if (P >= start && P < end) head[(size_t)P * 2 * HDIM + HDIM + i] = v;
-      }
+      const uint2 v = __ldcg(((const uint2*)vs) + lane);
+      vt[lane * 4 + 0] = bf_lo(v.x);
+      vt[lane * 4 + 1] = bf_hi(v.x);
+      vt[lane * 4 + 2] = bf_lo(v.y);
+      vt[lane * 4 + 3] = bf_hi(v.y);
+      if (owner) ((uint2*)(head + (size_t)P * 2 * HDIM + HDIM))[lane] = v;
       continue;
     }
     const bool isq = t < GQ;
     const int hh = isq ? h * GQ + t : m.Hq + h;
     const uint16_t* src = m.raw + (size_t)hh * HDIM;
     const uint16_t* nw = isq ? m.layers[layer].qn : m.layers[layer].kn;
-    float v[PER];
-    double ss = 0.0;
+    float v[PER], wv[PER], cs[PER], sn[PER];
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
       const int i = lane + 32 * j;
       v[2 * j] = bf2f(ldcg_u16(src + i));
       v[2 * j + 1] = bf2f(ldcg_u16(src + i + HDIM / 2));
-      ss += rms_sq(v[2 * j], 1);
-      ss += rms_sq(v[2 * j + 1], 1);
+      wv[2 * j] = bf2f(__ldg(nw + i));
+      wv[2 * j + 1] = bf2f(__ldg(nw + i + HDIM / 2));
+      cs[j] = bf2f(__ldg(ang + 2 * i));
+      sn[j] = bf2f(__ldg(ang + 2 * i + 1));
     }
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) ss += rms_sq(v[e], 1);
     ss = warp_sum_d(ss);
     const RmsCoef rc = rms_coef(ss, HDIM, m.eps, 1);
     float* dst = isq ? qf + t * HDIM : kt;
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
       const int i = lane + 32 * j;
-      const float x1 = rbf(rms_apply(v[2 * j], bf2f(__ldg(nw + i)), rc));
-      const float x2 = rbf(rms_apply(v[2 * j + 1], bf2f(__ldg(nw + i + HDIM / 2)), rc));
-      const float c = bf2f(__ldg(ang + 2 * i)), sn = bf2f(__ldg(ang + 2 * i + 1));
-      const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
-      const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn)));
+      const float x1 = rbf(rms_apply(v[2 * j], wv[2 * j], rc));
+      const float x2 = rbf(rms_apply(v[2 * j + 1], wv[2 * j + 1], rc));
+      const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, cs[j]), __fmul_rn(x2, sn[j])));
+      const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, cs[j]), __fmul_rn(x1, sn[j])));
       dst[i] = bf2f(o1);
       dst[i + HDIM / 2] = bf2f(o2);
-      if (!isq && P >= start && P < end) {
+      if (!isq && owner) {
         head[(size_t)P * 2 * HDIM + i] = o1;
         head[(size_t)P * 2 * HDIM + i + HDIM / 2] = o2;
       }
     }
   }
   __syncthreads();
-  // flash decoding over [start, end): the online softmax of attn_split_kernel
+  // flash decoding over [start, end): the online softmax of attn_split_kernel, with the
+  // next group of positions loaded while the current one is reduced
   const float scale = 1.4426950408889634f / sqrtf((float)HDIM);
   float q[GQ][PER];
 #pragma unroll
@@ -487,7 +575,23 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, 
 #pragma unroll
     for (int e = 0; e < PER; ++e) o[g][e] = 0.f;
   }
-  for (int j0 = start + wid * U; j0 < end; j0 += NWARP * U) {
+  auto load = [&](int j0, uint2 (&kk)[U], uint2 (&vv)[U]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = min(j0 + u, end - 1);
+      if (j != P) {
+        const uint16_t* kr = head + (size_t)j * 2 * HDIM + lane * PER;
+        kk[u] = ldg_stream8(kr);
+        vv[u] = ldg_stream8(kr + HDIM);
+      }
+    }
+  };
+  uint2 kc[U], vc[U], kn[U], vn[U];
+  int j0 = start + wid * U;
+  if (j0 < end) load(j0, kc, vc);
+  for (; j0 < end; j0 += NWARP * U) {
+    const int jn = j0 + NWARP * U;
+    if (jn < end) load(jn, kn, vn);
     float kf[U][PER], vf[U][PER];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -499,16 +603,14 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, 
           vf[u][e] = vt[lane * PER + e];
         }
       } else {
-        const uint16_t* kr = head + (size_t)j * 2 * HDIM + lane * PER;
-        const uint2 kk = ldg_stream8(kr), vv = ldg_stream8(kr + HDIM);
-        kf[u][0] = bf_lo(kk.x);
-        kf[u][1] = bf_hi(kk.x);
-        kf[u][2] = bf_lo(kk.y);
-        kf[u][3] = bf_hi(kk.y);
-        vf[u][0] = bf_lo(vv.x);
-        vf[u][1] = bf_hi(vv.x);
-        vf[u][2] = bf_lo(vv.y);
-        vf[u][3] = bf_hi(vv.y);
+        kf[u][0] = bf_lo(kc[u].x);
+        kf[u][1] = bf_hi(kc[u].x);
+        kf[u][2] = bf_lo(kc[u].y);
+        kf[u][3] = bf_hi(kc[u].y);
+        vf[u][0] = bf_lo(vc[u].x);
+        vf[u][1] = bf_hi(vc[u].x);
+        vf[u][2] = bf_lo(vc[u].y);
+        vf[u][3] = bf_hi(vc[u].y);
       }
     }
 #pragma unroll
@@ -539,8 +641,13 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, 
       ll[g] = ls;
       mm[g] = mn;
     }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      kc[u] = kn[u];
+      vc[u] = vn[u];
+    }
   }
-  // merge the warps, write this split's partial (o, m, l) per head
+  // merge the warps; write this split's partial per head
 #pragma unroll
   for (int g = 0; g < GQ; ++g) {
     float* pw = part + (wid * GQ + g) * (HDIM + 2);
@@ -572,34 +679,53 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int unit, 
       ws[g * (HDIM + 2) + HDIM + 1] = lsum;
     }
   }
-  // the last split of this KV head merges all splits (attn_combine_kernel's arithmetic)
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd((int*)&sync[SYNC_HEAD0 + h], 1);
-    S.flag[1] = (old == ns - 1);
+}
+
+// Merge the split partials of every head (attn_combine_kernel's arithmetic) into
+// bf16 bits in xhi; CTA 0 also stores them to m.attn.
+template <int GQ>
+__device__ void stage_attention(const Kp& p, const Smem& S, int ns) {
+  const iron_qwen3_model& m = p.m;
+  const int Hq = m.Hq;
+  float* wgt = S.mrg;            // [Hq][SMAX]: m, then 2^(m - M)
+  float* lsum = S.mrg + Hq * SMAX;  // [Hq]
+  float* lv = (float*)S.xlo;     // [Hq][SMAX] l values (xlo is free until the BFP pass)
+  for (int t = threadIdx.x; t < Hq * ns; t += NT) {
+    const int hh = t / ns, sp = t - hh * ns;
+    const int h = hh / GQ, g = hh - h * GQ;
+    const float* ps = m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2);
+    wgt[hh * SMAX + sp] = __ldcg(ps + HDIM);
+    lv[hh * SMAX + sp] = __ldcg(ps + HDIM + 1);
   }
   __syncthreads();
-  if (S.flag[1]) {
-    __threadfence();
-    for (int t = threadIdx.x; t < GQ * HDIM; t += NT) {
-      const int g = t / HDIM, d = t - g * HDIM;
-      const float* base = m.attn_ws + ((size_t)h * ns * GQ + g) * (HDIM + 2);
-      const size_t stride = (size_t)GQ * (HDIM + 2);
-      float M = -INFINITY;
-      for (int q2 = 0; q2 < ns; ++q2) M = fmaxf(M, __ldcg(base + q2 * stride + HDIM));
-      float oo = 0.f, lsum = 0.f;
-      if (M != -INFINITY) {
-        for (int q2 = 0; q2 < ns; ++q2) {
-          const float* ps = base + q2 * stride;
-          const float f = exp2f(__ldcg(ps + HDIM) - M);
-          oo = fmaf(__ldcg(ps + d), f, oo);
-          lsum = fmaf(__ldcg(ps + HDIM + 1), f, lsum);
-        }
-      }
-      m.attn[(size_t)(h * GQ + g) * HDIM + d] = f2bf(lsum > 0.f ? oo / lsum : 0.f);
+  for (int hh = threadIdx.x; hh < Hq; hh += NT) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, wgt[hh * SMAX + sp]);
+    float l = 0.f;
+    for (int sp = 0; sp < ns; ++sp) {
+      const float f = M != -INFINITY ? exp2f(wgt[hh * SMAX + sp] - M) : 0.f;
+      wgt[hh * SMAX + sp] = f;
+      l = fmaf(lv[hh * SMAX + sp], f, l);
     }
-    if (threadIdx.x == 0) atomicExch((int*)&sync[SYNC_HEAD0 + h], 0);
+    lsum[hh] = l;
+  }
+  __syncthreads();
+  const int QD = Hq * HDIM;
+  for (int i = threadIdx.x; i < QD; i += NT) {
+    const int hh = i / HDIM, d = i - hh * HDIM;
+    const int h = hh / GQ, g = hh - h * GQ;
+    float ov[SMAX];
+#pragma unroll
+    for (int sp = 0; sp < SMAX; ++sp)
+      if (sp < ns) ov[sp] = __ldcg(m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2) + d);
+    float oo = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < SMAX; ++sp)
+      if (sp < ns) oo = fmaf(ov[sp], wgt[hh * SMAX + sp], oo);
+    const float l = lsum[hh];
+    const uint16_t b = f2bf(l > 0.f ? oo / l : 0.f);
+    S.xhi[i] = b;
+    if (blockIdx.x == 0) m.attn[i] = b;
   }
 }
 
@@ -612,18 +738,19 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
   const iron_qwen3_model& m = p.m;
   const Smem S = carve(smem_raw, p, GQ);
   int32_t* sync = m.sync;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int N = gridDim.x;
   const Plan P = make_plan(p);
-  const int QD = m.Hq * HDIM, QKV = (m.Hq + 2 * m.Hkv) * HDIM;
+  const int QD = m.Hq * HDIM;
   const int pos = m.pos[0];
-  const int unit = blockIdx.x < m.Hkv * p.nsplit ? (int)blockIdx.x : -1;
   // a position outside the cache or a token outside the vocabulary: record and leave
   // before touching memory (every CTA takes the same decision)
   if (pos < 0 || pos >= m.max_seq || (p.embed_input && (m.tok[0] < 0 || m.tok[0] >= m.V))) {
     if (tid == 0) atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_INPUT);
     return;
   }
+  const int ns = att_splits(pos + 1, p.smax);
+  const int unit = blockIdx.x < m.Hkv * ns ? (int)blockIdx.x : -1;
 
   if (tid == 0) {
     mbar_init(&S.mbar[0]);
@@ -634,6 +761,7 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
   if (tid == 0) {
     issue(p, P, S, 0, 0);
     issue(p, P, S, 1, 1);
+    prefetch_layer_l2(p, P, 0);
     prefetch_layer_l2(p, P, 1);
   }
   int ci = 0;            // next chunk to consume
@@ -675,8 +803,8 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
       if (tid == 0) {
         prefetch_layer_l2(p, P, layer + 2);
         if (unit >= 0) {  // this CTA's KV range of this layer, one phase ahead
-          const int L = pos + 1, ns = p.nsplit, h = unit / ns, s = unit - (unit / ns) * ns;
-          const int chunk = (L + ns - 1) / ns, st = s * chunk, en = min(min(L, st + chunk), pos);
+          const int L = pos + 1, h = unit / ns, sp = unit - (unit / ns) * ns;
+          const int chunk = (L + ns - 1) / ns, st = sp * chunk, en = min(min(L, st + chunk), pos);
           if (en > st) {
             const uint16_t* hb = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
             prefetch_l2(hb + (size_t)st * 2 * HDIM, (uint32_t)(en - st) * 4 * HDIM);
@@ -686,31 +814,27 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
       __syncthreads();
       const int rbq = rowb(m.D, G);
       ok = consume(PH_QKV, [&](const Chunk& ch, const uint8_t* wb) {
-        for (int r = wid; r < ch.r1 - ch.r0; r += NWARP) {
-          const double a = row_dot<G>(wb + (size_t)r * rbq, m.D, S);
-          if (lane == 0) m.raw[ch.r0 + r] = f2bf((float)a);
-        }
+        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbq, m.D, S, [&](int r, double a, double) {
+          m.raw[ch.r0 + r] = f2bf((float)a);
+        });
       });
       if (!ok || !barrier()) break;
     }
-    // ---- attention (per KV head and split) + merge by the last split ----
-    if (unit >= 0) attention_unit<GQ>(p, S, layer, unit, pos, sync);
+    // ---- attention: one KV head and one split of the positions per CTA ----
+    if (unit >= 0) attention_unit<GQ>(p, S, layer, unit / ns, unit - (unit / ns) * ns, ns, pos);
     if (!barrier()) break;
-    // ---- O-proj + residual: x1 = bf16(x + bf16(Wo @ attn)) ----
+    // ---- O-proj + residual: x1 = bf16(x + bf16(Wo @ attn)); the split merge first ----
     {
-      stage_copy(S, m.attn, QD);
+      stage_attention<GQ>(p, S, ns);
       __syncthreads();
       bfp_stage(S, QD, G);
       __syncthreads();
       const int rbo = rowb(QD, G);
       ok = consume(PH_O, [&](const Chunk& ch, const uint8_t* wb) {
-        for (int r = wid; r < ch.r1 - ch.r0; r += NWARP) {
-          const double a = row_dot<G>(wb + (size_t)r * rbo, QD, S);
-          if (lane == 0) {
-            const int row = ch.r0 + r;
-            m.x1[row] = f2bf(bf2f(ldcg_u16(m.x + row)) + rbf_d(a));
-          }
-        }
+        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbo, QD, S, [&](int r, double a, double) {
+          const int row = ch.r0 + r;
+          m.x1[row] = f2bf(bf2f(ldcg_u16(m.x + row)) + rbf_d(a));
+        });
       });
       if (!ok || !barrier()) break;
     }
@@ -722,30 +846,24 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
       __syncthreads();
       const int rbg = rowb(m.D, G);
       ok = consume(PH_GU, [&](const Chunk& ch, const uint8_t* wb) {
-        const int n = ch.r1 - ch.r0;
-        for (int r = wid; r < n; r += NWARP) {
-          const double g = row_dot<G>(wb + (size_t)r * rbg, m.D, S);
-          const double u = row_dot<G>(wb + (size_t)(n + r) * rbg, m.D, S);
-          if (lane == 0) m.gh[ch.r0 + r] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
-        }
+        chunk_gemv<G, true>(wb, ch.r1 - ch.r0, rbg, m.D, S, [&](int r, double g, double u) {
+          m.gh[ch.r0 + r] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
+        });
       });
       if (!ok || !barrier()) break;
     }
     // ---- down + residual: x = bf16(x1 + bf16(Wd @ gh)) ----
     {
-      stage_copy(S, m.gh, m.FF);
+      load_bits(S.xhi, m.gh, m.FF, false);
       __syncthreads();
       bfp_stage(S, m.FF, G);
       __syncthreads();
       const int rbd = rowb(m.FF, G);
       ok = consume(PH_D, [&](const Chunk& ch, const uint8_t* wb) {
-        for (int r = wid; r < ch.r1 - ch.r0; r += NWARP) {
-          const double a = row_dot<G>(wb + (size_t)r * rbd, m.FF, S);
-          if (lane == 0) {
-            const int row = ch.r0 + r;
-            m.x[row] = f2bf(bf2f(ldcg_u16(m.x1 + row)) + rbf_d(a));
-          }
-        }
+        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbd, m.FF, S, [&](int r, double a, double) {
+          const int row = ch.r0 + r;
+          m.x[row] = f2bf(bf2f(ldcg_u16(m.x1 + row)) + rbf_d(a));
+        });
       });
       if (!ok || !barrier()) break;
     }
@@ -760,20 +878,37 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     const int rbh = m.lm_w8 ? rowb(m.D, G) : m.D * 2;
+    auto track = [&](int idx, uint16_t o) {
+      if (m.logits) m.logits[idx] = o;
+      if (better(bf2f(o), idx, bv, bi)) {
+        bv = bf2f(o);
+        bi = idx;
+      }
+    };
     ok = consume(5, [&](const Chunk& ch, const uint8_t* wb) {
-      for (int r = wid; r < ch.r1 - ch.r0; r += NWARP) {
-        const uint8_t* row = wb + (size_t)r * rbh;
-        const uint16_t o = m.lm_w8 ? f2bf((float)row_dot<G>(row, m.D, S)) : f2bf(row_dot_bf16(row, m.D, S.xf));
-        const int idx = ch.r0 + r;
-        if (m.logits && lane == 0) m.logits[idx] = o;
-        if (better(bf2f(o), idx, bv, bi)) {
-          bv = bf2f(o);
-          bi = idx;
+      const int n = ch.r1 - ch.r0;
+      if (m.lm_w8) {
+        chunk_gemv<G, false>(wb, n, rbh, m.D, S, [&](int r, double a, double) { track(ch.r0 + r, f2bf((float)a)); });
+      } else {
+        constexpr int R = 3;
+        const int wid = tid >> 5;
+        for (int r0 = wid * R; r0 < n; r0 += NWARP * R) {
+          const uint8_t* rp[R];
+#pragma unroll
+          for (int i = 0; i < R; ++i) rp[i] = wb + (size_t)min(r0 + i, n - 1) * rbh;
+          float out[R];
+          rows_dot_bf16<R>(rp, m.D, S.xf, out);
+          if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < R; ++i)
+              if (r0 + i < n) track(ch.r0 + r0 + i, f2bf(out[i]));
+          }
         }
       }
     });
     if (ok) {
-      // CTA-best (all lanes of a warp agree), then publish and let the last CTA reduce
+      // CTA-best over the warps' lane 0, then publish and let the last CTA reduce
+      const int wid = tid >> 5;
       if (lane == 0) {
         S.att[wid] = bv;
         ((int*)S.att)[NWARP + wid] = bi;
@@ -886,11 +1021,14 @@ using namespace iron::qstep;
 extern "C" int iron_qwen3_sync_words(const iron_qwen3_model* m) { return SYNC_HEAD0 + (m ? m->Hkv : 64); }
 extern "C" int64_t iron_qwen3_cand_bytes(void) { return 1024 * 8; }
 extern "C" int iron_qwen3_grid(const iron_qwen3_model* m) { return grid_for(m, 0); }
+static int smax_for(const iron_qwen3_model* m, int grid) {
+  int s = grid / m->Hkv;
+  return s < 1 ? 1 : (s > SMAX ? SMAX : s);
+}
+
 extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
   if (!m || m->Hkv < 1) return 0;
-  const int grid = grid_for(m, 0);
-  const int ns = grid / m->Hkv < 1 ? 1 : grid / m->Hkv;
-  return (int64_t)m->Hkv * ns * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
+  return (int64_t)m->Hkv * smax_for(m, grid_for(m, 0)) * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
 }
 
 extern "C" int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream) {
@@ -909,11 +1047,11 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   p.advance = advance;
   p.kmax = kmax_of(m);
   const int GQ = m->Hq / m->Hkv;
-  const size_t smem = smem_bytes(p.kmax, m->D, GQ);
+  const size_t smem = smem_bytes(p.kmax, m->D, GQ, m->Hq);
   IRON_REQUIRE(smem <= 227 * 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: %zu bytes of shared memory", smem);
   const int grid = grid_for(m, smem);
   IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
-  p.nsplit = grid / m->Hkv < 1 ? 1 : grid / m->Hkv;
+  p.smax = smax_for(m, grid);
   cudaStream_t st = (cudaStream_t)stream;
 #define IRON_STEP_CASE(g, gq) \
   if (m->group == g && GQ == gq) return launch<g, gq>(p, grid, smem, st);

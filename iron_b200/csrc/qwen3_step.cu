@@ -96,6 +96,7 @@ struct Smem {
   float* xf;      // [D] lm_head activations (bf16 path)
   float* att;     // attention scratch
   float* mrg;     // split-merge scratch: [Hq][SMAX] weights, [Hq] sums
+  iron_qwen3_layer* lay;  // [n_layers] copy of the layer pointer table
   double* red;    // [32]
   uint64_t* mbar; // [2]
   int* flag;      // [4]
@@ -125,13 +126,17 @@ __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
   s.att = (float*)(base + o);
   o += (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
   s.mrg = (float*)(base + o);
+  o += (size_t)(p.m.Hq * SMAX + p.m.Hq) * 4;
+  o = (o + 15) & ~(size_t)15;
+  s.lay = (iron_qwen3_layer*)(base + o);
   return s;
 }
 
-__host__ __device__ inline size_t smem_bytes(int kmax, int D, int GQ, int Hq) {
+__host__ __device__ inline size_t smem_bytes(int kmax, int D, int GQ, int Hq, int n_layers) {
   const size_t att = (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
   const size_t mrg = (size_t)(Hq * SMAX + Hq) * 4;
-  return 2 * (size_t)BUF + (size_t)kmax * 4 + 32 * 8 + 16 + 16 + (size_t)(kmax / 32) * 4 + (size_t)D * 4 + att + mrg;
+  return 2 * (size_t)BUF + (size_t)kmax * 4 + 32 * 8 + 16 + 16 + (size_t)(kmax / 32) * 4 + (size_t)D * 4 + att + mrg +
+         16 + (size_t)n_layers * sizeof(iron_qwen3_layer);
 }
 
 // ---------------------------------------------------------------------------
@@ -219,7 +224,7 @@ __device__ void issue(const Kp& p, const Plan& P, const Smem& S, int i, int b) {
     rb = m.lm_w8 ? rowb(m.D, G) : m.D * 2;
     src[0] = m.lm_w8 ? (const uint8_t*)m.lm_w8 + (size_t)ch.r0 * rb : (const uint8_t*)(m.embed + (size_t)ch.r0 * m.D);
   } else {
-    const iron_qwen3_layer& L = m.layers[ch.layer];
+    const iron_qwen3_layer& L = S.lay[ch.layer];
     const int QD = m.Hq * m.HD;
     if (ch.kind == PH_QKV) {
       rb = rowb(m.D, G);
@@ -250,10 +255,10 @@ __device__ void issue(const Kp& p, const Plan& P, const Smem& S, int i, int b) {
 }
 
 // L2 prefetch of every weight chunk of `layer` that this CTA will copy
-__device__ void prefetch_layer_l2(const Kp& p, const Plan& P, int layer) {
+__device__ void prefetch_layer_l2(const Kp& p, const Plan& P, const Smem& S, int layer) {
   if (layer >= p.m.n_layers) return;
   const iron_qwen3_model& m = p.m;
-  const iron_qwen3_layer& L = m.layers[layer];
+  const iron_qwen3_layer& L = S.lay[layer];
   const int G = m.group, QD = m.Hq * m.HD;
   struct R {
     const void* base;
@@ -525,7 +530,7 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int
     const bool isq = t < GQ;
     const int hh = isq ? h * GQ + t : m.Hq + h;
     const uint16_t* src = m.raw + (size_t)hh * HDIM;
-    const uint16_t* nw = isq ? m.layers[layer].qn : m.layers[layer].kn;
+    const uint16_t* nw = isq ? S.lay[layer].qn : S.lay[layer].kn;
     float v[PER], wv[PER], cs[PER], sn[PER];
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
@@ -711,21 +716,32 @@ __device__ void stage_attention(const Kp& p, const Smem& S, int ns) {
   }
   __syncthreads();
   const int QD = Hq * HDIM;
-  for (int i = threadIdx.x; i < QD; i += NT) {
-    const int hh = i / HDIM, d = i - hh * HDIM;
-    const int h = hh / GQ, g = hh - h * GQ;
-    float ov[SMAX];
+  constexpr int B4 = 4;  // outputs per thread per pass, their partial loads in flight together
+  for (int i0 = threadIdx.x; i0 < QD; i0 += NT * B4) {
+    float ov[B4][SMAX];
 #pragma unroll
-    for (int sp = 0; sp < SMAX; ++sp)
-      if (sp < ns) ov[sp] = __ldcg(m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2) + d);
-    float oo = 0.f;
+    for (int k = 0; k < B4; ++k) {
+      const int i = i0 + k * NT;
+      const int hh = i / HDIM, d = i - hh * HDIM;
+      const int h = hh / GQ, g = hh - h * GQ;
 #pragma unroll
-    for (int sp = 0; sp < SMAX; ++sp)
-      if (sp < ns) oo = fmaf(ov[sp], wgt[hh * SMAX + sp], oo);
-    const float l = lsum[hh];
-    const uint16_t b = f2bf(l > 0.f ? oo / l : 0.f);
-    S.xhi[i] = b;
-    if (blockIdx.x == 0) m.attn[i] = b;
+      for (int sp = 0; sp < SMAX; ++sp)
+        if (i < QD && sp < ns) ov[k][sp] = __ldcg(m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2) + d);
+    }
+#pragma unroll
+    for (int k = 0; k < B4; ++k) {
+      const int i = i0 + k * NT;
+      if (i >= QD) break;
+      const int hh = i / HDIM;
+      float oo = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < SMAX; ++sp)
+        if (sp < ns) oo = fmaf(ov[k][sp], wgt[hh * SMAX + sp], oo);
+      const float l = lsum[hh];
+      const uint16_t b = f2bf(l > 0.f ? oo / l : 0.f);
+      S.xhi[i] = b;
+      if (blockIdx.x == 0) m.attn[i] = b;
+    }
   }
 }
 
@@ -757,12 +773,16 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
     mbar_init(&S.mbar[1]);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  {  // the layer pointer table, read once
+    const int nw = m.n_layers * (int)(sizeof(iron_qwen3_layer) / 8);
+    for (int i = tid; i < nw; i += NT) ((unsigned long long*)S.lay)[i] = __ldg(((const unsigned long long*)m.layers) + i);
+  }
   __syncthreads();
   if (tid == 0) {
     issue(p, P, S, 0, 0);
     issue(p, P, S, 1, 1);
-    prefetch_layer_l2(p, P, 0);
-    prefetch_layer_l2(p, P, 1);
+    prefetch_layer_l2(p, P, S, 0);
+    prefetch_layer_l2(p, P, S, 1);
   }
   int ci = 0;            // next chunk to consume
   unsigned epoch = 0;    // grid barriers passed
@@ -792,7 +812,7 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
   };
 
   for (int layer = 0; layer < m.n_layers && ok; ++layer) {
-    const iron_qwen3_layer& Lw = m.layers[layer];
+    const iron_qwen3_layer& Lw = S.lay[layer];
     // ---- QKV: hn = RMSNorm_golden(x, norm1); raw = bf16(Wqkv @ hn) ----
     {
       const bool emb = layer == 0 && p.embed_input;
@@ -800,9 +820,16 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
       stage_rmsnorm(S, xs, emb, Lw.norm1, m.D, m.eps, 1, nullptr, (emb && blockIdx.x == 0) ? m.x : nullptr);
       __syncthreads();
       bfp_stage(S, m.D, G);
-      if (tid == 0) {
-        prefetch_layer_l2(p, P, layer + 2);
-        if (unit >= 0) {  // this CTA's KV range of this layer, one phase ahead
+      __syncthreads();
+      const int rbq = rowb(m.D, G);
+      ok = consume(PH_QKV, [&](const Chunk& ch, const uint8_t* wb) {
+        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbq, m.D, S, [&](int r, double a, double) {
+          m.raw[ch.r0 + r] = f2bf((float)a);
+        });
+      });
+      if (tid == 0 && ok) {
+        prefetch_layer_l2(p, P, S, layer + 2);
+        if (unit >= 0) {  // this CTA's KV range of this layer, ahead of the attention phase
           const int L = pos + 1, h = unit / ns, sp = unit - (unit / ns) * ns;
           const int chunk = (L + ns - 1) / ns, st = sp * chunk, en = min(min(L, st + chunk), pos);
           if (en > st) {
@@ -811,13 +838,6 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
           }
         }
       }
-      __syncthreads();
-      const int rbq = rowb(m.D, G);
-      ok = consume(PH_QKV, [&](const Chunk& ch, const uint8_t* wb) {
-        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbq, m.D, S, [&](int r, double a, double) {
-          m.raw[ch.r0 + r] = f2bf((float)a);
-        });
-      });
       if (!ok || !barrier()) break;
     }
     // ---- attention: one KV head and one split of the positions per CTA ----
@@ -1047,7 +1067,7 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   p.advance = advance;
   p.kmax = kmax_of(m);
   const int GQ = m->Hq / m->Hkv;
-  const size_t smem = smem_bytes(p.kmax, m->D, GQ, m->Hq);
+  const size_t smem = smem_bytes(p.kmax, m->D, GQ, m->Hq, m->n_layers);
   IRON_REQUIRE(smem <= 227 * 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: %zu bytes of shared memory", smem);
   const int grid = grid_for(m, smem);
   IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);

@@ -60,7 +60,7 @@ class OracleQwen3:
     """
 
     def __init__(self, shape: Qwen3Shape, weights: dict, max_seq: int, int8_lm_head=False,
-                 matvec: str = "exact"):
+                 matvec: str = "exact", angles=None):
         self.s = shape
         self.w = weights
         self.max_seq = max_seq
@@ -70,7 +70,10 @@ class OracleQwen3:
         self.mv = ops.gemv_int8_exact if matvec == "exact" else ops.gemv_int8_premul
         s = shape
         self.kv = np.zeros((s.n_layers, s.Hkv, max_seq, 2, s.HD), np.float32)
-        self.angles = ops.rope_angle_table(max_seq, s.HD, s.theta)
+        # the RoPE row table is an input of the decode step (qwen3_npu_int8.py:603-604),
+        # computed on the host; a caller may pass the exact table the device uses
+        self.angles = (ops.rope_angle_table(max_seq, s.HD, s.theta) if angles is None
+                       else np.asarray(angles, np.float32))
 
     def layer(self, i: int, x, pos: int):
         s, L = self.s, self.w["layers"][i]

@@ -201,15 +201,20 @@ int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, con
  * RMSNorm and the lm_head with greedy argmax.  The arithmetic of every stage is
  * the one of the per-operator entry points above (iron_qkv_head with the golden
  * RMSNorm form, iron_decode_attn, iron_mlp_block, iron_rmsnorm mode 1,
- * iron_lm_head_*_argmax).  Weights are in the native wire (tile_m = 1, signed).
- * Every pointer in the descriptor is a device pointer; `layers` points to a
- * DEVICE array of n_layers iron_qwen3_layer.  The kernel reads the token from
- * tok[0] (embed_input != 0) or the hidden state from x, the position from pos[0],
- * writes the argmax to tok[0] and, when advance != 0, moves pos/seq_len/kv_off one
- * token on.  Grid barriers and counters live in `sync` (iron_qwen3_sync_words()
- * int32 words, zero before the first step); every wait is bounded: on timeout
- * sync[1] holds a nonzero code, the step returns early, and
- * iron_qwen3_sync_reset() must clear the words before the next step. */
+ * iron_lm_head_*_argmax); the O and down projections are summed along K in
+ * float64 pieces before their single bf16 rounding.  QKV and gate/up weights are
+ * in the native wire (tile_m = 1, signed); O and down also in the column-blocked
+ * forms made by iron_qwen3_pack_wo_heads / iron_qwen3_pack_wd_cols.  Every pointer
+ * in the descriptor is a device pointer, weight and table pointers 16-byte aligned
+ * (weight rows are bulk-copied); `layers` points to a DEVICE array of n_layers
+ * iron_qwen3_layer.  The kernel reads the token from tok[0] (embed_input != 0) or
+ * the hidden state from x, the position from pos[0], writes the argmax to tok[0],
+ * the final hidden state to x and, when advance != 0, moves pos/seq_len/kv_off one
+ * token on.  Barrier counters live in `sync` (iron_qwen3_sync_words() int32 words)
+ * and float64 accumulators in `attn_ws` (iron_qwen3_attn_ws_bytes()); both must be
+ * zero before the first step.  Every wait is bounded: on timeout sync[1] holds a
+ * nonzero code, the step returns early, and iron_qwen3_sync_reset() must clear
+ * both before the next step. */
 typedef struct iron_qwen3_layer {
   const uint16_t* norm1;  /* (D) bf16 */
   const void* wqkv;       /* ((Hq+2Hkv)*HD, D) wire */
@@ -220,6 +225,9 @@ typedef struct iron_qwen3_layer {
   const void* wg;         /* (FF, D) wire */
   const void* wu;         /* (FF, D) wire */
   const void* wd;         /* (D, FF) wire */
+  const void* wo_heads;   /* iron_qwen3_pack_wo_heads(wo) */
+  const void* wd_cols;    /* iron_qwen3_pack_wd_cols(wd): int8 (FF/4, D, 4) */
+  const uint16_t* wd_col_scales; /* ... and its scales (FF/group, D) bf16 */
 } iron_qwen3_layer;
 
 typedef struct iron_qwen3_model {
@@ -231,19 +239,21 @@ typedef struct iron_qwen3_model {
   const void* lm_w8;               /* (V, D) int8 wire lm_head, or NULL */
   const uint16_t* angles;          /* (max_seq, HD) interleaved [cos, sin] */
   uint16_t* kv;                    /* (n_layers, Hkv, 2*max_seq*HD) per-token [K_t|V_t] */
-  uint16_t* x;                     /* (D) residual stream */
+  uint16_t* x;                     /* (D) hidden state in (embed_input == 0) / final hidden state out */
   uint16_t* raw;                   /* ((Hq+2Hkv)*HD) */
-  uint16_t* attn;                  /* (Hq*HD) */
-  uint16_t* x1;                    /* (D) */
-  uint16_t* gh;                    /* (FF) */
-  float* attn_ws;                  /* iron_qwen3_attn_ws_bytes() */
+  uint16_t* attn;                  /* (Hq*HD), unused by the step kernel */
+  uint16_t* x1;                    /* (D), unused by the step kernel */
+  uint16_t* gh;                    /* (FF), unused by the step kernel */
+  float* attn_ws;                  /* iron_qwen3_attn_ws_bytes(): split partials + accumulators */
   void* cand;                      /* iron_qwen3_cand_bytes() */
   int32_t* tok;
   int32_t* pos;
   int32_t* seq_len;
   int32_t* kv_off;
   uint16_t* logits;                /* (V) or NULL */
-  int32_t* sync;                   /* iron_qwen3_sync_words() int32, zeroed once */
+  int32_t* sync;                   /* iron_qwen3_sync_words() int32 */
+  uint16_t* trace;                 /* (n_layers + 1, D) or NULL: the hidden state entering each layer,
+                                      then the final one (parity checks layer by layer) */
 } iron_qwen3_model;
 
 int iron_qwen3_sync_words(const iron_qwen3_model* m);
@@ -252,7 +262,19 @@ int64_t iron_qwen3_cand_bytes(void);
 /* Grid size the step kernel will use on the current device (one CTA per SM). */
 int iron_qwen3_grid(const iron_qwen3_model* m);
 int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream);
-/* Zero the sync words (after a timed-out step, or before first use). */
+/* Weight forms for the step kernel's K-split projections, made once at load time from
+ * native wires (no reference counterpart: they re-order the wires that
+ * qwen3_npu_int8.py:381-436 packs for the NPU).
+ * wo_heads: for each KV head h, the D rows of Wo restricted to h's (Hq/Hkv)*HD
+ *   columns as [int8 columns | their bf16 group scales | zero pad to 16 bytes];
+ *   iron_qwen3_pack_wo_heads_bytes() bytes.
+ * wd_cols: int8 (FF/4, D, 4) = Wd[r, 4j..4j+3] at [j][r], and bf16 scales
+ *   (FF/group, D) = the scale of row r, group g at [g][r]. */
+int64_t iron_qwen3_pack_wo_heads_bytes(int D, int QD, int Hkv, int group);
+int iron_qwen3_pack_wo_heads(const void* wo_wire, int D, int QD, int Hkv, int group, void* out, void* stream);
+int iron_qwen3_pack_wd_cols(const void* wd_wire, int D, int FF, int group, void* out_q, uint16_t* out_scales,
+                            void* stream);
+/* Zero the sync words and the accumulators (after a timed-out step, or before first use). */
 int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream);
 
 #ifdef __cplusplus

@@ -1,48 +1,84 @@
 // One greedy Qwen3 decode token (batch 1) as ONE persistent cooperative kernel.
 //
-// Layout of the work.  The grid is one CTA per SM.  A token is a sequence of
-// phases separated by grid barriers: for every layer QKV -> attention -> O-proj
-// -> gate/up -> down, then the lm_head.  In each GEMV phase a CTA owns a
-// contiguous range of output rows.  Its weight rows (native wire, tile_m = 1)
-// arrive in shared memory by cp.async.bulk (no multicast) into two buffers.
-// Copies are issued in a fixed per-CTA chunk order one chunk ahead, so the next
-// phase's weights stream in while this phase computes and while the grid waits
-// at the barrier; the weights do not depend on the activations.  The attention
-// phase's KV range is prefetched to L2 one phase early.
+// Why one kernel.  At batch 1 a decode token streams ~0.9 GB (weights, KV) but
+// each projection is only a few microseconds of HBM time, so the token is bound
+// by the latency of the dependency chain between projections, not by bandwidth.
+// The kernel keeps that chain short:
 //
-// Arithmetic.  Every stage uses the device code of the per-operator entry
-// points:
-//   - activations staged as exact int16 block floating point (hi + lo words);
-//   - dp2a chunk sums with float64 accumulation;
-//   - the golden RMSNorm form for the QKV input, q/k and the final norm, and
-//     the kernel form for the MLP norm;
-//   - the same bf16 stores between stages.
-// So the token equals the chained kernels' token up to float64 / float32
-// summation order.
+//   - One CTA per SM.  The CTAs form Hkv KV-head groups of about N / Hkv CTAs.
+//     Group h computes the q/k/v rows of KV head h (QKV rows are taken in head
+//     order), runs head h's attention with one split of the positions per CTA,
+//     merges the splits and multiplies the merged heads by head h's column block
+//     of Wo.  Inside the attention block only the group's own CTAs wait for one
+//     another.
+//   - The O and down projections are split along K: O by KV head, down by the
+//     slice of gate/up rows a CTA computed itself, so the SwiGLU output never
+//     leaves the CTA.  Partial sums are float64 and meet through float64 atomics
+//     in per-layer accumulators.
+//   - Per layer that leaves two grid barriers (after O, after down) and two
+//     group barriers (after QKV, after the attention splits).
+//   - Weights do not depend on activations, so each CTA's weight share streams
+//     through a shared-memory ring by cp.async.bulk (no multicast).  A producer
+//     warp issues the copies as far ahead as the ring allows (about a layer), so
+//     issuing never sits on the compute path.  The attention KV range is
+//     prefetched to L2 one phase early.
 //
-// Synchronisation.  Grid barriers and the per-KV-head split counters are
-// int32 words in global memory.  Every wait is bounded by %globaltimer.  On
-// timeout the CTA records an error code and returns; the other CTAs see it and
-// return too.  In-flight bulk copies are drained (bounded) before exit.
+// Weight layouts.  QKV and gate/up rows use the native wire (tile_m = 1, row
+// [K int8 | K/G bf16 scales]).  O uses wo_heads: for each KV head h the rows of Wo
+// restricted to h's GQ*HD columns, [GQ*HD int8 | GQ*HD/G bf16 | pad to 16 bytes].
+// Down uses wd_cols: int8 [FF/4][D][4] (four consecutive K columns of one row in a
+// 32-bit word) and scales [FF/G][D] bf16, so a CTA's K slice is contiguous.
+// iron_qwen3_pack_wo_heads / iron_qwen3_pack_wd_cols build both from the wires.
+//
+// Arithmetic.  The stages use the device arithmetic of the per-operator entry
+// points: activations staged as exact int16 block floating point (hi + lo words),
+// dp2a sums per 16 (or 4) columns, float64 accumulation, the golden RMSNorm form
+// for the QKV input, q/k and the final norm, the kernel form for the MLP norm, and
+// the same bf16 roundings between stages.  The K-split partial sums meet in
+// float64, so a projection output equals the unsplit float64 sum up to float64
+// summation order before its single bf16 rounding.
+//
+// Synchronisation.  Barriers are int32 counters in global memory whose targets
+// grow with the layer; the last CTA of the token resets them.  Every wait is
+// bounded by %globaltimer: on timeout the CTA records an error code and returns;
+// the other CTAs see the code in their own waits and return too.  In-flight bulk
+// copies are drained (bounded) before a CTA exits.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace iron {
 namespace qstep {
 
+// 8 compute warps and one producer warp (168 registers a thread, no spills; more warps
+// cap registers at 128 and spill in the inner loops)
 constexpr int NT = 256, NWARP = NT / 32;
-constexpr int BUF = 48 * 1024;  // bytes per weight buffer (two buffers)
-constexpr int HDIM = 128;       // head_dim of the step kernel
+constexpr int HDIM = 128;        // head_dim of the step kernel
+constexpr int NMB = 16;          // ring slots (chunks in flight at most)
+constexpr int GMAX = 24;         // most CTAs in one KV-head group (attention splits)
+constexpr int XREP = 8;          // down-projection accumulator replicas: KV-head group h adds into
+                                 // replica h % XREP (atomics to one address serialise in L2)
+constexpr int SLICE_MAX = 64;    // widest down-projection K slice of one CTA
+constexpr int PIECE = 32768;     // bytes per cp.async.bulk instruction
+constexpr int SMEM_MAX = 227 * 1024;
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
 
-enum { SYNC_BAR = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_HEAD0 = 3 };
+// sync words (the G2 counters follow the Hkv G1 counters)
+enum { SYNC_B1 = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_B2 = 3, SYNC_PARITY = 4, SYNC_G1 = 8 };
 enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_INPUT = 3 };
-
-constexpr int SMAX = 16;  // most attention splits per KV head
+// chunk kinds of a layer, in stream order; the lm_head chunks follow the last layer
+enum { CK_QKV = 0, CK_O = 1, CK_GU = 2, CK_D = 3 };
 
 struct Kp {
   iron_qwen3_model m;
-  int embed_input, advance, smax, kmax;
+  int embed_input, advance;
+  int ring;     // ring bytes
+  int lm_rows;  // lm_head rows per chunk
+  int kst;      // staging length max(D, GQ*HD)
 };
+
+__host__ __device__ inline int rowb(int K, int G) { return K + 2 * (K / G); }
+__host__ __device__ inline int rowb_heads(int GQ, int G) { return (rowb(GQ * HDIM, G) + 15) & ~15; }
 
 // ---------------------------------------------------------------------------
 // PTX helpers: mbarrier, bulk copies, acquire loads, timer
@@ -83,206 +119,318 @@ __device__ __forceinline__ unsigned ld_acquire(const int32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint32_t ldcg_u16(const uint16_t* p) { return (uint32_t)__ldcg(p); }
 
-// ---------------------------------------------------------------------------
-// shared memory
-// ---------------------------------------------------------------------------
-struct Smem {
-  uint8_t* buf[2];
-  uint16_t* xhi;  // [kmax] bf16 bits, then int16 hi words
-  uint16_t* xlo;  // [kmax]
-  float* xs;      // [kmax / 32]
-  float* xf;      // [D] lm_head activations (bf16 path)
-  float* att;     // attention scratch
-  float* mrg;     // split-merge scratch: [Hq][SMAX] weights, [Hq] sums
-  iron_qwen3_layer* lay;  // [n_layers] copy of the layer pointer table
-  double* red;    // [32]
-  uint64_t* mbar; // [2]
-  int* flag;      // [4]
-};
+// Phase timestamps for profiling builds (-DIRON_STEP_PROFILE): thread 0 of each CTA
+// stores %globaltimer at the marked points into a buffer registered with
+// iron_qwen3_step_profile_buffer ([CTA][64 layer rows][32 marks] u64).  Compiled
+// out otherwise.
+#ifdef IRON_STEP_PROFILE
+__device__ unsigned long long* g_step_prof;
+#define STEP_MARK(row, k)                                                                                      \
+  do {                                                                                                         \
+    if (threadIdx.x == 0 && g_step_prof) g_step_prof[((size_t)blockIdx.x * 64 + (row)) * 32 + (k)] = gtimer(); \
+  } while (0)
+#define STEP_CLK(row, k)                                                                                          \
+  do {                                                                                                            \
+    if (threadIdx.x == 0 && g_step_prof) g_step_prof[((size_t)blockIdx.x * 64 + (row)) * 32 + (k)] = clock64(); \
+  } while (0)
+#else
+#define STEP_MARK(row, k) \
+  do {                    \
+  } while (0)
+#define STEP_CLK(row, k) \
+  do {                   \
+  } while (0)
+#endif
 
-__device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
-  Smem s;
-  size_t o = 0;
-  s.buf[0] = base + o;
-  o += BUF;
-  s.buf[1] = base + o;
-  o += BUF;
-  s.xhi = (uint16_t*)(base + o);
-  o += (size_t)p.kmax * 2;
-  s.xlo = (uint16_t*)(base + o);
-  o += (size_t)p.kmax * 2;
-  s.red = (double*)(base + o);
-  o += 32 * 8;
-  s.mbar = (uint64_t*)(base + o);
-  o += 2 * 8;
-  s.flag = (int*)(base + o);
-  o += 16;
-  s.xs = (float*)(base + o);
-  o += (size_t)(p.kmax / 32) * 4;
-  s.xf = (float*)(base + o);
-  o += (size_t)p.m.D * 4;
-  s.att = (float*)(base + o);
-  o += (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
-  s.mrg = (float*)(base + o);
-  o += (size_t)(p.m.Hq * SMAX + p.m.Hq) * 4;
-  o = (o + 15) & ~(size_t)15;
-  s.lay = (iron_qwen3_layer*)(base + o);
-  return s;
-}
+// barrier of the NT compute threads only (the producer warp runs on its own)
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
-__host__ __device__ inline size_t smem_bytes(int kmax, int D, int GQ, int Hq, int n_layers) {
-  const size_t att = (size_t)(GQ * HDIM + 2 * HDIM + NWARP * GQ * (HDIM + 2)) * 4;
-  const size_t mrg = (size_t)(Hq * SMAX + Hq) * 4;
-  return 2 * (size_t)BUF + (size_t)kmax * 4 + 32 * 8 + 16 + 16 + (size_t)(kmax / 32) * 4 + (size_t)D * 4 + att + mrg +
-         16 + (size_t)n_layers * sizeof(iron_qwen3_layer);
+__device__ __forceinline__ double csum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  csync();
+  if (lane == 0) red[wid] = v;
+  csync();
+  double t = lane < NWARP ? red[lane] : 0.0;
+  return warp_sum_d(t);
 }
 
 // ---------------------------------------------------------------------------
-// work partition and the per-CTA chunk sequence
+// work partition of one CTA (identical in all its threads)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void part(int M, int c, int N, int& lo, int& hi) {
+__host__ __device__ inline void part(int M, int c, int N, int& lo, int& hi) {
   lo = (int)((long long)M * c / N);
   hi = (int)((long long)M * (c + 1) / N);
 }
-__device__ __forceinline__ int rowb(int K, int G) { return K + 2 * (K / G); }
 
-enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4 };
+// KV-head group of CTA c: CTAs [h*N/Hkv, (h+1)*N/Hkv)
+__host__ __device__ inline void head_group(int c, int N, int Hkv, int& h, int& c0, int& c1) {
+  h = 0;
+  while (h + 1 < Hkv && (int)((long long)(h + 1) * N / Hkv) <= c) ++h;
+  c0 = (int)((long long)h * N / Hkv);
+  c1 = (int)((long long)(h + 1) * N / Hkv);
+}
 
-struct Plan {  // identical in every thread of a CTA
-  int lo[5], hi[5], rpc[5], nch[5];  // per GEMV phase kind: my rows, rows per chunk, chunks
-  int per_layer;                     // chunks per layer
-  int hlo, hhi, hrpc, hnch;          // lm_head
-  int total;
+struct Plan {
+  int h, gi, gsz;       // KV-head group, index in the group, group size
+  int q0, q1;           // group-local QKV rows: q rows of the group's GQ heads, then k, then v
+  int o0, o1;           // O rows (against head h's column block)
+  int u0, u1;           // gate/up rows / 4 = down-projection K slice / 4
+  int ga, nsg;          // first scale group of the slice, scale groups it touches
+  int hlo, hhi, hnch;   // lm_head rows, chunks
+  int total;            // chunks of the token
+  uint32_t bytes[4];    // chunk bytes per layer kind
 };
 
 __device__ Plan make_plan(const Kp& p) {
   const iron_qwen3_model& m = p.m;
   Plan P;
-  const int G = m.group, N = gridDim.x, c = blockIdx.x;
-  const int QKV = (m.Hq + 2 * m.Hkv) * m.HD, QD = m.Hq * m.HD;
-  const int Ms[5] = {QKV, 0, m.D, m.FF, m.D};
-  const int Ks[5] = {m.D, 0, QD, m.D, m.FF};
-  P.per_layer = 0;
-  for (int k = 0; k < 5; ++k) {
-    if (k == PH_ATT) {
-      P.lo[k] = P.hi[k] = P.rpc[k] = P.nch[k] = 0;
-      continue;
-    }
-    part(Ms[k], c, N, P.lo[k], P.hi[k]);
-    const int unit = rowb(Ks[k], G) * (k == PH_GU ? 2 : 1);
-    P.rpc[k] = BUF / unit;
-    P.nch[k] = (P.hi[k] - P.lo[k] + P.rpc[k] - 1) / P.rpc[k];
-    P.per_layer += P.nch[k];
-  }
+  const int N = gridDim.x, c = blockIdx.x, G = m.group, GQ = m.Hq / m.Hkv, D = m.D;
+  int c0, c1;
+  head_group(c, N, m.Hkv, P.h, c0, c1);
+  P.gi = c - c0;
+  P.gsz = c1 - c0;
+  part((GQ + 2) * HDIM, P.gi, P.gsz, P.q0, P.q1);
+  part(D, P.gi, P.gsz, P.o0, P.o1);
+  part(m.FF / 4, c, N, P.u0, P.u1);
+  const int k0 = 4 * P.u0, k1 = 4 * P.u1;
+  P.ga = k0 / G;
+  P.nsg = k1 > k0 ? (k1 - 1) / G - P.ga + 1 : 0;
+  P.bytes[CK_QKV] = (uint32_t)(P.q1 - P.q0) * rowb(D, G);
+  P.bytes[CK_O] = (uint32_t)(P.o1 - P.o0) * rowb_heads(GQ, G);
+  P.bytes[CK_GU] = 2u * (uint32_t)(k1 - k0) * rowb(D, G);
+  P.bytes[CK_D] = (uint32_t)(P.u1 - P.u0) * D * 4 + (uint32_t)P.nsg * D * 2;
   part(m.V, c, N, P.hlo, P.hhi);
-  P.hrpc = BUF / (m.lm_w8 ? rowb(m.D, G) : m.D * 2);
-  P.hnch = (P.hhi - P.hlo + P.hrpc - 1) / P.hrpc;
-  P.total = P.per_layer * m.n_layers + P.hnch;
+  P.hnch = (P.hhi - P.hlo + p.lm_rows - 1) / p.lm_rows;
+  P.total = 4 * m.n_layers + P.hnch;
   return P;
 }
 
-struct Chunk {
-  int layer, kind, r0, r1;  // kind 5 = lm_head
+// source row of group-local QKV row r of KV head h (q rows of heads h*GQ.., k, v)
+__device__ __forceinline__ int qkv_src_row(int r, int h, int GQ, int Hq, int Hkv) {
+  if (r < GQ * HDIM) return h * GQ * HDIM + r;
+  if (r < (GQ + 1) * HDIM) return Hq * HDIM + h * HDIM + (r - GQ * HDIM);
+  return (Hq + Hkv) * HDIM + h * HDIM + (r - (GQ + 1) * HDIM);
+}
+
+// ---------------------------------------------------------------------------
+// shared memory
+// ---------------------------------------------------------------------------
+struct RingState {                // shared by the producer lane and compute thread 0
+  unsigned long long tail;        // bytes released by the compute threads (monotonic)
+  int issued, consumed, abort;    // chunks issued / released; compute threads left early
+  uint32_t slot[NMB];             // ring offset of the chunk in each slot
+  unsigned long long end[NMB];    // allocation offset after the chunk
 };
 
-__device__ Chunk chunk_at(const Plan& P, int i, int n_layers) {
-  Chunk ch;
-  if (i < P.per_layer * n_layers) {
-    ch.layer = i / P.per_layer;
-    int j = i - ch.layer * P.per_layer;
-    int k = 0;
-    for (;; ++k) {
-      if (k == PH_ATT) continue;
-      if (j < P.nch[k]) break;
-      j -= P.nch[k];
-    }
-    ch.kind = k;
-    ch.r0 = P.lo[k] + j * P.rpc[k];
-    ch.r1 = min(P.hi[k], ch.r0 + P.rpc[k]);
-  } else {
-    const int j = i - P.per_layer * n_layers;
-    ch.layer = n_layers;
-    ch.kind = 5;
-    ch.r0 = P.hlo + j * P.hrpc;
-    ch.r1 = min(P.hhi, ch.r0 + P.hrpc);
-  }
-  return ch;
+struct Smem {
+  uint8_t* ring;
+  uint16_t* xhi;   // [kst] bf16 bits, then int16 hi words
+  uint16_t* xlo;   // [kst] norm weights before the BFP pass, then lo words
+  float* xs;       // [kst / 16] block factors
+  uint16_t* sx;    // [D] residual x (bf16 bits)
+  uint16_t* sx1;   // [D] residual x1
+  float* xf;       // [D] final normed x (bf16 lm_head path)
+  float* ghv;      // [SLICE_MAX] this CTA's SwiGLU outputs
+  uint16_t* dh;    // [SLICE_MAX] their int16 hi words
+  uint16_t* dl;    // [SLICE_MAX] lo words
+  float* att;      // attention scratch
+  float* mst;      // [GMAX][GQ][HD + 2] the split partials of this CTA's KV head
+  iron_qwen3_layer* lay;  // [n_layers] copy of the layer pointer table
+  double* red;     // [32]
+  uint64_t* mbar;  // [NMB + 1]
+  RingState* rs;
+  int* flag;       // [8]; flag[4] holds the down slice's block factor (float bits)
+};
+
+__host__ __device__ inline size_t att_floats(int GQ) {
+  return (size_t)GQ * HDIM + 2 * HDIM + (size_t)NWARP * GQ * (HDIM + 2);
 }
 
-// thread 0: bulk-copy chunk i into buffer b
-__device__ void issue(const Kp& p, const Plan& P, const Smem& S, int i, int b) {
-  if (i >= P.total) return;
-  const iron_qwen3_model& m = p.m;
-  const Chunk ch = chunk_at(P, i, m.n_layers);
-  const int G = m.group, n = ch.r1 - ch.r0;
-  const uint8_t* src[2] = {nullptr, nullptr};
-  uint32_t rb = 0;
-  int nsrc = 1;
-  if (ch.kind == 5) {
-    rb = m.lm_w8 ? rowb(m.D, G) : m.D * 2;
-    src[0] = m.lm_w8 ? (const uint8_t*)m.lm_w8 + (size_t)ch.r0 * rb : (const uint8_t*)(m.embed + (size_t)ch.r0 * m.D);
-  } else {
-    const iron_qwen3_layer& L = S.lay[ch.layer];
-    const int QD = m.Hq * m.HD;
-    if (ch.kind == PH_QKV) {
-      rb = rowb(m.D, G);
-      src[0] = (const uint8_t*)L.wqkv + (size_t)ch.r0 * rb;
-    } else if (ch.kind == PH_O) {
-      rb = rowb(QD, G);
-      src[0] = (const uint8_t*)L.wo + (size_t)ch.r0 * rb;
-    } else if (ch.kind == PH_GU) {
-      rb = rowb(m.D, G);
-      src[0] = (const uint8_t*)L.wg + (size_t)ch.r0 * rb;
-      src[1] = (const uint8_t*)L.wu + (size_t)ch.r0 * rb;
-      nsrc = 2;
-    } else {
-      rb = rowb(m.FF, G);
-      src[0] = (const uint8_t*)L.wd + (size_t)ch.r0 * rb;
-    }
-  }
-  const uint32_t bytes = (uint32_t)n * rb;
-  fence_proxy_async();  // generic-proxy use of this buffer happens before the async writes
-  mbar_expect(&S.mbar[b], bytes * nsrc);
-  for (int s = 0; s < nsrc; ++s) {
-    uint8_t* dst = S.buf[b] + (size_t)s * bytes;
-    for (uint32_t o = 0; o < bytes; o += 16384u) {
-      const uint32_t len = min(16384u, bytes - o);
-      bulk_g2s(dst + o, src[s] + o, len, &S.mbar[b]);
-    }
-  }
+// bytes of everything but the ring (carve's layout: 17 arrays, each rounded up to 16 bytes)
+__host__ __device__ inline size_t fixed_smem(int kst, int D, int GQ, int n_layers) {
+  size_t o = 32 * 8 + (NMB + 1) * 8 + sizeof(RingState) + 8 * 4;
+  o += (size_t)kst * 4 + (size_t)(kst / 16) * 4;
+  o += (size_t)D * 2 * 2 + (size_t)D * 4;
+  o += SLICE_MAX * 4 + SLICE_MAX * 2 * 2;
+  o += att_floats(GQ) * 4 + (size_t)GMAX * GQ * (HDIM + 2) * 4;
+  o += (size_t)n_layers * sizeof(iron_qwen3_layer);
+  return o + 17 * 16 + 64;
 }
 
-// L2 prefetch of every weight chunk of `layer` that this CTA will copy
-__device__ void prefetch_layer_l2(const Kp& p, const Plan& P, const Smem& S, int layer) {
-  if (layer >= p.m.n_layers) return;
-  const iron_qwen3_model& m = p.m;
-  const iron_qwen3_layer& L = S.lay[layer];
-  const int G = m.group, QD = m.Hq * m.HD;
-  struct R {
-    const void* base;
-    int k, K;
-  } rs[5] = {{L.wqkv, PH_QKV, m.D}, {L.wo, PH_O, QD}, {L.wg, PH_GU, m.D}, {L.wu, PH_GU, m.D}, {L.wd, PH_D, m.FF}};
-  for (int t = 0; t < 5; ++t) {
-    const int rb = rowb(rs[t].K, G);
-    const int n = P.hi[rs[t].k] - P.lo[rs[t].k];
-    if (n <= 0) continue;
-    const uint8_t* s = (const uint8_t*)rs[t].base + (size_t)P.lo[rs[t].k] * rb;
-    const uint32_t bytes = (uint32_t)n * rb;
-    for (uint32_t o = 0; o < bytes; o += 65536u) prefetch_l2(s + o, min(65536u, bytes - o));
-  }
+__device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
+  Smem s;
+  size_t o = (size_t)p.ring;
+  s.ring = base;
+  auto take = [&](size_t bytes) {  // every array starts on a 16-byte boundary (vector loads, bulk copies)
+    uint8_t* r = base + o;
+    o += (bytes + 15) & ~(size_t)15;
+    return r;
+  };
+  s.red = (double*)take(32 * 8);
+  s.mbar = (uint64_t*)take((NMB + 1) * 8);  // ring slots, then the split-merge copy
+  s.rs = (RingState*)take((sizeof(RingState) + 15) & ~(size_t)15);
+  s.flag = (int*)take(8 * 4);
+  s.xhi = (uint16_t*)take((size_t)p.kst * 2);
+  s.xlo = (uint16_t*)take((size_t)p.kst * 2);
+  s.xs = (float*)take((size_t)(p.kst / 16) * 4);
+  s.sx = (uint16_t*)take((size_t)p.m.D * 2);
+  s.sx1 = (uint16_t*)take((size_t)p.m.D * 2);
+  s.xf = (float*)take((size_t)p.m.D * 4);
+  s.ghv = (float*)take(SLICE_MAX * 4);
+  s.dh = (uint16_t*)take(SLICE_MAX * 2);
+  s.dl = (uint16_t*)take(SLICE_MAX * 2);
+  s.att = (float*)take(att_floats(GQ) * 4);
+  s.mst = (float*)take((size_t)GMAX * GQ * (HDIM + 2) * 4);
+  s.lay = (iron_qwen3_layer*)take((size_t)p.m.n_layers * sizeof(iron_qwen3_layer));
+  return s;
 }
 
 // ---------------------------------------------------------------------------
-// bounded waits (thread 0) and CTA-wide abort
+// the chunk stream: per layer QKV, O, gate/up, down; then the lm_head
 // ---------------------------------------------------------------------------
-__device__ bool grid_barrier(int32_t* sync, unsigned target) {
-  __threadfence();
-  atomicAdd((unsigned*)&sync[SYNC_BAR], 1u);
+struct Seg {
+  const uint8_t* src;
+  uint32_t bytes;
+};
+
+// segments of chunk i, copied back to back into one ring slot; returns their count
+__device__ int chunk_segs(const Kp& p, const Plan& P, const Smem& S, int i, Seg (&sg)[3]) {
+  const iron_qwen3_model& m = p.m;
+  const int G = m.group, D = m.D, GQ = m.Hq / m.Hkv;
+  const int lay = i >> 2;
+  if (lay >= m.n_layers) {
+    const int j = i - 4 * m.n_layers;
+    const int r0 = P.hlo + j * p.lm_rows, r1 = min(P.hhi, r0 + p.lm_rows);
+    const uint32_t rb = m.lm_w8 ? rowb(D, G) : D * 2;
+    const uint8_t* base = m.lm_w8 ? (const uint8_t*)m.lm_w8 : (const uint8_t*)m.embed;
+    sg[0] = {base + (size_t)r0 * rb, (uint32_t)(r1 - r0) * rb};
+    return 1;
+  }
+  const iron_qwen3_layer& L = S.lay[lay];
+  switch (i & 3) {
+    case CK_QKV: {
+      const uint32_t rb = rowb(D, G);
+      int n = 0, r = P.q0;
+      while (r < P.q1) {  // split at the q / k / v boundaries of the group-local order
+        const int lim = r < GQ * HDIM ? GQ * HDIM : (r < (GQ + 1) * HDIM ? (GQ + 1) * HDIM : (GQ + 2) * HDIM);
+        const int e = min(P.q1, lim);
+        sg[n++] = {(const uint8_t*)L.wqkv + (size_t)qkv_src_row(r, P.h, GQ, m.Hq, m.Hkv) * rb,
+                   (uint32_t)(e - r) * rb};
+        r = e;
+      }
+      return n;
+    }
+    case CK_O: {
+      const uint32_t rb = rowb_heads(GQ, G);
+      sg[0] = {(const uint8_t*)L.wo_heads + ((size_t)P.h * D + P.o0) * rb, (uint32_t)(P.o1 - P.o0) * rb};
+      return 1;
+    }
+    case CK_GU: {
+      const uint32_t rb = rowb(D, G);
+      const size_t off = (size_t)(4 * P.u0) * rb;
+      const uint32_t bytes = (uint32_t)(4 * (P.u1 - P.u0)) * rb;
+      sg[0] = {(const uint8_t*)L.wg + off, bytes};
+      sg[1] = {(const uint8_t*)L.wu + off, bytes};
+      return 2;
+    }
+    default: {
+      sg[0] = {(const uint8_t*)L.wd_cols + (size_t)P.u0 * D * 4, (uint32_t)(P.u1 - P.u0) * D * 4};
+      sg[1] = {(const uint8_t*)L.wd_col_scales + (size_t)P.ga * D * 2, (uint32_t)P.nsg * D * 2};
+      return 2;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t chunk_bytes(const Kp& p, const Plan& P, int i) {
+  if ((i >> 2) < p.m.n_layers) {  // a switch, not an indexed array: P stays in registers
+    switch (i & 3) {
+      case CK_QKV: return P.bytes[CK_QKV];
+      case CK_O: return P.bytes[CK_O];
+      case CK_GU: return P.bytes[CK_GU];
+      default: return P.bytes[CK_D];
+    }
+  }
+  const int j = i - 4 * p.m.n_layers;
+  const int r0 = P.hlo + j * p.lm_rows, r1 = min(P.hhi, r0 + p.lm_rows);
+  return (uint32_t)(r1 - r0) * (p.m.lm_w8 ? rowb(p.m.D, p.m.group) : p.m.D * 2);
+}
+
+// wait (bounded) until the copies of chunks [from, to) have landed
+__device__ void drain(const Smem& S, int from, int to) {
+  for (int k = from; k < to; ++k) {
+    const unsigned long long t0 = gtimer();
+    while (!mbar_test(&S.mbar[k % NMB], (uint32_t)((k / NMB) & 1)) && gtimer() - t0 < 20ull * 1000 * 1000) {
+    }
+  }
+}
+
+// The producer lane: issue every chunk of the token in stream order, each as soon
+// as its ring space and slot are released.  Every wait is bounded; it stops when
+// the compute threads leave early or the grid's error word is set, and then waits
+// for its copies in flight.
+// (inlined: a call that takes P or S by address would move the compute threads' copies
+// to local memory, which the small L1 left beside 227 KB of shared memory does not keep)
+__device__ __forceinline__ void producer(const Kp& p, const Plan& P, const Smem& S, int32_t* sync) {
+  volatile RingState& rs = *S.rs;
+  const uint32_t R = (uint32_t)p.ring;
+  unsigned long long head = 0;
+  bool stop = false;
+  for (int i = 0; i < P.total && !stop; ++i) {
+    const uint32_t bytes = chunk_bytes(p, P, i);
+    unsigned long long start = head;
+    const uint32_t off = (uint32_t)(start % R);
+    if (off + bytes > R) start += R - off;  // does not fit before the end: wrap
+    const unsigned long long t0 = gtimer();
+    for (unsigned it = 0;; ++it) {
+      if (start + bytes - rs.tail <= R && i - rs.consumed < NMB) break;
+      if (rs.abort) {
+        stop = true;
+        break;
+      }
+      if ((it & 15) == 15) {
+        if (ld_acquire(&sync[SYNC_ERR]) != 0) {
+          stop = true;
+          break;
+        }
+        if (gtimer() - t0 > TIMEOUT_NS) {
+          atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_COPY);
+          stop = true;
+          break;
+        }
+      }
+      __nanosleep(32);
+    }
+    if (stop) break;
+    const int sl = i % NMB;
+    rs.slot[sl] = (uint32_t)(start % R);
+    rs.end[sl] = start + bytes;
+    head = start + bytes;
+    Seg sg[3];
+    const int ns = chunk_segs(p, P, S, i, sg);
+    uint8_t* dst = S.ring + (uint32_t)(start % R);
+    fence_proxy_async();  // the compute threads' reads of this space happen before the async writes
+    mbar_expect(&S.mbar[sl], bytes);
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      if (s >= ns) break;
+      for (uint32_t o = 0; o < sg[s].bytes; o += PIECE)
+        bulk_g2s(dst + o, sg[s].src + o, min((uint32_t)PIECE, sg[s].bytes - o), &S.mbar[sl]);
+      dst += sg[s].bytes;
+    }
+    rs.issued = i + 1;
+  }
+  if (stop) drain(S, rs.consumed, rs.issued);
+}
+
+// ---------------------------------------------------------------------------
+// bounded waits (thread 0)
+// ---------------------------------------------------------------------------
+__device__ bool wait_count(int32_t* sync, int word, unsigned target) {
   const unsigned long long t0 = gtimer();
   for (unsigned it = 0;; ++it) {
-    if (ld_acquire(&sync[SYNC_BAR]) >= target) return true;
+    if (ld_acquire(&sync[word]) >= target) return true;
     if (ld_acquire(&sync[SYNC_ERR]) != 0) return false;
     if ((it & 63) == 63 && gtimer() - t0 > TIMEOUT_NS) {
       atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_BARRIER);
@@ -291,13 +439,16 @@ __device__ bool grid_barrier(int32_t* sync, unsigned target) {
   }
 }
 
-__device__ bool wait_buf(const Smem& S, int32_t* sync, int b, uint32_t parity) {
+__device__ bool wait_slot(uint64_t* mb, int32_t* sync, uint32_t parity) {
   const unsigned long long t0 = gtimer();
   for (unsigned it = 0;; ++it) {
-    if (mbar_test(&S.mbar[b], parity)) return true;
-    if ((it & 63) == 63 && gtimer() - t0 > TIMEOUT_NS) {
-      atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_COPY);
-      return false;
+    if (mbar_test(mb, parity)) return true;
+    if ((it & 63) == 63) {
+      if (ld_acquire(&sync[SYNC_ERR]) != 0) return false;
+      if (gtimer() - t0 > TIMEOUT_NS) {
+        atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_COPY);
+        return false;
+      }
     }
   }
 }
@@ -305,19 +456,6 @@ __device__ bool wait_buf(const Smem& S, int32_t* sync, int b, uint32_t parity) {
 // ---------------------------------------------------------------------------
 // activation staging (the arithmetic of gemv_w8_kernel's prologue)
 // ---------------------------------------------------------------------------
-// K bf16 values (K % 8 == 0) from global memory to shared memory with 16-byte
-// loads issued back to back; `copy_to` (global) receives the same bits.
-__device__ __forceinline__ void load_bits(uint16_t* dst, const uint16_t* src, int K, bool readonly,
-                                          uint16_t* copy_to = nullptr) {
-  const int n16 = K >> 3;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n16; i += NT) {
-    const uint4 v = readonly ? __ldg(((const uint4*)src) + i) : __ldcg(((const uint4*)src) + i);
-    ((uint4*)dst)[i] = v;
-    if (copy_to) ((uint4*)copy_to)[i] = v;
-  }
-}
-
 // In place: xhi holds the bf16 bits of K values -> int16 hi words; xlo lo words;
 // xs the group factors.  Eight lanes per quant group.
 __device__ void bfp_stage(const Smem& S, int K, int G) {
@@ -355,35 +493,63 @@ __device__ void bfp_stage(const Smem& S, int K, int G) {
   }
 }
 
-// RMSNorm(src) * w -> bf16 bits in xhi (mode 0 kernel form, 1 golden form);
-// `outf` (shared) receives the values as floats when non-null.  Uses xlo as scratch.
-__device__ void stage_rmsnorm(const Smem& S, const uint16_t* src, bool src_readonly, const uint16_t* w, int K,
-                              float eps, int mode, float* outf, uint16_t* copy_to) {
-  load_bits(S.xhi, src, K, src_readonly, copy_to);
-  load_bits(S.xlo, w, K, true);
-  __syncthreads();
+// RMSNorm of the bf16 bits in `src` (shared) with the weight bits already in xlo
+// -> bf16 bits in xhi (mode 0 kernel form, 1 golden form); `outf` (shared)
+// receives the values as floats when non-null.
+__device__ void stage_norm(const Smem& S, const uint16_t* src, int K, float eps, int mode, float* outf) {
   double ss = 0.0;
-  for (int i = threadIdx.x; i < K; i += NT) ss += rms_sq(bf2f(S.xhi[i]), mode);
-  ss = block_sum_d(ss, S.red);
+  for (int i = threadIdx.x; i < K; i += NT) ss += rms_sq(bf2f(src[i]), mode);
+  ss = csum_d(ss, S.red);
   const RmsCoef rc = rms_coef(ss, K, eps, mode);
   for (int i = threadIdx.x; i < K; i += NT) {
-    const uint16_t o = f2bf(rms_apply(bf2f(S.xhi[i]), bf2f(S.xlo[i]), rc));
+    const uint16_t o = f2bf(rms_apply(bf2f(src[i]), bf2f(S.xlo[i]), rc));
     S.xhi[i] = o;
     if (outf) outf[i] = bf2f(o);
   }
 }
 
+// dst[i] = bf16(src[i] + bf16(sum over the nrep replicas acc[r*D + i])) over the D
+// residual rows, replicas summed in a fixed order; every accumulator load of a thread
+// is issued before the first store (D <= 4 * NT)
+template <int NREP>
+__device__ __forceinline__ void resid_add(uint16_t* dst, const uint16_t* src, const double* acc, int D) {
+  constexpr int MAXV = 4;
+  double v[MAXV][NREP];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = threadIdx.x + k * NT;
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) v[k][r] = i < D ? __ldcg(acc + (size_t)r * D + i) : 0.0;
+  }
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = threadIdx.x + k * NT;
+    double a = v[k][0];
+#pragma unroll
+    for (int r = 1; r < NREP; ++r) a += v[k][r];
+    if (i < D) dst[i] = f2bf(bf2f(src[i]) + rbf_d(a));
+  }
+}
+
+// K bf16 values (K % 8 == 0, read-only data) into shared memory with 16-byte loads
+__device__ __forceinline__ void load_ro(uint16_t* dst, const uint16_t* src, int K) {
+  for (int i = threadIdx.x; i < (K >> 3); i += NT) ((uint4*)dst)[i] = __ldg(((const uint4*)src) + i);
+}
+
 // ---------------------------------------------------------------------------
-// int8 rows from shared memory, R (or 2R for gate/up pairs) rows per warp at once:
-// sum_k q*s*x exactly as gemv_w8_kernel with LO staging and float64 accumulation
+// int8 rows from shared memory: LPR lanes per row, 16 columns a lane per step, NR rows
+// (2NR for gate/up pairs) per lane group at once: sum_k q*s*x exactly as
+// gemv_w8_kernel with LO staging and float64 accumulation.  The 16-column dp2a sums
+// run as two chains of four so that their latencies overlap.
 // ---------------------------------------------------------------------------
-template <int G, int NR>
+template <int G, int NR, int LPR>
 __device__ __forceinline__ void rows_dot(const uint8_t* const (&rp)[NR], int K, const Smem& S, double (&out)[NR]) {
-  const int lane = threadIdx.x & 31;
+  const int sub = threadIdx.x & (LPR - 1);
   double acc[NR];
 #pragma unroll
   for (int i = 0; i < NR; ++i) acc[i] = 0.0;
-  for (int c = lane; c < (K >> 4); c += 32) {
+#pragma unroll 2
+  for (int c = sub; c < (K >> 4); c += LPR) {
     const int g = (c * 16) / G;
     const uint4 xa = *(const uint4*)(S.xhi + c * 16), xb = *(const uint4*)(S.xhi + c * 16 + 8);
     const uint4 la = *(const uint4*)(S.xlo + c * 16), lb = *(const uint4*)(S.xlo + c * 16 + 8);
@@ -397,64 +563,71 @@ __device__ __forceinline__ void rows_dot(const uint8_t* const (&rp)[NR], int K, 
     }
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
-      int a = __dp2a_lo((int)xa.x, (int)w[i].x, 0);
-      a = __dp2a_hi((int)xa.y, (int)w[i].x, a);
-      a = __dp2a_lo((int)xa.z, (int)w[i].y, a);
-      a = __dp2a_hi((int)xa.w, (int)w[i].y, a);
-      a = __dp2a_lo((int)xb.x, (int)w[i].z, a);
-      a = __dp2a_hi((int)xb.y, (int)w[i].z, a);
-      a = __dp2a_lo((int)xb.z, (int)w[i].w, a);
-      a = __dp2a_hi((int)xb.w, (int)w[i].w, a);
-      int l = __dp2a_lo((int)la.x, (int)w[i].x, 0);
-      l = __dp2a_hi((int)la.y, (int)w[i].x, l);
-      l = __dp2a_lo((int)la.z, (int)w[i].y, l);
-      l = __dp2a_hi((int)la.w, (int)w[i].y, l);
-      l = __dp2a_lo((int)lb.x, (int)w[i].z, l);
-      l = __dp2a_hi((int)lb.y, (int)w[i].z, l);
-      l = __dp2a_lo((int)lb.z, (int)w[i].w, l);
-      l = __dp2a_hi((int)lb.w, (int)w[i].w, l);
-      const long long t = (long long)a * 32768 + l;
+      int a0 = __dp2a_lo((int)xa.x, (int)w[i].x, 0), a1 = __dp2a_hi((int)xa.y, (int)w[i].x, 0);
+      a0 = __dp2a_lo((int)xa.z, (int)w[i].y, a0);
+      a1 = __dp2a_hi((int)xa.w, (int)w[i].y, a1);
+      a0 = __dp2a_lo((int)xb.x, (int)w[i].z, a0);
+      a1 = __dp2a_hi((int)xb.y, (int)w[i].z, a1);
+      a0 = __dp2a_lo((int)xb.z, (int)w[i].w, a0);
+      a1 = __dp2a_hi((int)xb.w, (int)w[i].w, a1);
+      int l0 = __dp2a_lo((int)la.x, (int)w[i].x, 0), l1 = __dp2a_hi((int)la.y, (int)w[i].x, 0);
+      l0 = __dp2a_lo((int)la.z, (int)w[i].y, l0);
+      l1 = __dp2a_hi((int)la.w, (int)w[i].y, l1);
+      l0 = __dp2a_lo((int)lb.x, (int)w[i].z, l0);
+      l1 = __dp2a_hi((int)lb.y, (int)w[i].z, l1);
+      l0 = __dp2a_lo((int)lb.z, (int)w[i].w, l0);
+      l1 = __dp2a_hi((int)lb.w, (int)w[i].w, l1);
+      const long long t = (long long)(a0 + a1) * 32768 + (l0 + l1);
       acc[i] = fma((double)t, (double)(sv[i] * xsc) * (1.0 / 32768.0), acc[i]);
     }
   }
 #pragma unroll
-  for (int i = 0; i < NR; ++i) out[i] = warp_sum_d(acc[i]);
+  for (int i = 0; i < NR; ++i) {
+    double v = acc[i];
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    out[i] = v;
+  }
 }
 
-// the rows of one chunk: n rows (pairs when PAIR: gate rows then up rows) of rb bytes
-template <int G, int R, bool PAIR, class Epi>
+// The n rows of one chunk (rb bytes each; with PAIR the n gate rows, then the n up
+// rows).  The NG = NT/LPR lane groups take rows b + rg + i*NG of each block of
+// NG*R rows; every lane of a warp runs the same trip count (the shuffles need it).
+template <int G, int R, int LPR, bool PAIR, class Epi>
 __device__ void chunk_rows(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
   constexpr int NR = PAIR ? 2 * R : R;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int r0 = wid * R; r0 < n; r0 += NWARP * R) {
+  constexpr int NG = NT / LPR;
+  const int rg = threadIdx.x / LPR, sub = threadIdx.x & (LPR - 1);
+  for (int b = 0; b < n; b += NG * R) {
     const uint8_t* rp[NR];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-      const int r = min(r0 + i, n - 1);
+      const int r = min(b + rg + i * NG, n - 1);
       rp[i] = wb + (size_t)r * rb;
       if (PAIR) rp[R + i] = wb + (size_t)(n + r) * rb;
     }
     double out[NR];
-    rows_dot<G, NR>(rp, K, S, out);
-    if (lane == 0) {
+    rows_dot<G, NR, LPR>(rp, K, S, out);
+    if (sub == 0) {
 #pragma unroll
       for (int i = 0; i < R; ++i)
-        if (r0 + i < n) epi(r0 + i, out[i], PAIR ? out[R + i] : 0.0);
+        if (b + rg + i * NG < n) epi(b + rg + i * NG, out[i], PAIR ? out[R + i] : 0.0);
     }
   }
 }
 
-template <int G, bool PAIR, class Epi>
+template <int G, int LPR, bool PAIR, class Epi>
 __device__ void chunk_gemv(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
-  const int R = (n + NWARP - 1) / NWARP;
+  constexpr int NG = NT / LPR;
+  const int R = (n + NG - 1) / NG;
   if (R <= 1)
-    chunk_rows<G, 1, PAIR>(wb, n, rb, K, S, epi);
+    chunk_rows<G, 1, LPR, PAIR>(wb, n, rb, K, S, epi);
   else if (R == 2)
-    chunk_rows<G, 2, PAIR>(wb, n, rb, K, S, epi);
+    chunk_rows<G, 2, LPR, PAIR>(wb, n, rb, K, S, epi);
   else if (R == 3)
-    chunk_rows<G, 3, PAIR>(wb, n, rb, K, S, epi);
+    chunk_rows<G, 3, LPR, PAIR>(wb, n, rb, K, S, epi);
   else
-    chunk_rows<G, 4, PAIR>(wb, n, rb, K, S, epi);
+    chunk_rows<G, 4, LPR, PAIR>(wb, n, rb, K, S, epi);
 }
 
 // bf16 rows with float32 activations: the lm_head arithmetic of gemv_bf16_kernel
@@ -485,29 +658,52 @@ __device__ __forceinline__ void rows_dot_bf16(const uint8_t* const (&rp)[R], int
   for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
 }
 
+// the same with this lane's activations held in registers: xr[k] = xf[(lane + 32k)*8 ..]
+template <int R, int KC>
+__device__ __forceinline__ void rows_dot_bf16_reg(const uint8_t* const (&rp)[R], const float (&xr)[KC][8],
+                                                  float (&out)[R]) {
+  const int lane = threadIdx.x & 31;
+  float a[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) a[i] = 0.f;
+#pragma unroll
+  for (int k = 0; k < KC; ++k) {
+    uint4 w[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) w[i] = *(const uint4*)(rp[i] + (lane + 32 * k) * 16);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      a[i] = fmaf(bf_lo(w[i].x), xr[k][0], a[i]);
+      a[i] = fmaf(bf_hi(w[i].x), xr[k][1], a[i]);
+      a[i] = fmaf(bf_lo(w[i].y), xr[k][2], a[i]);
+      a[i] = fmaf(bf_hi(w[i].y), xr[k][3], a[i]);
+      a[i] = fmaf(bf_lo(w[i].z), xr[k][4], a[i]);
+      a[i] = fmaf(bf_hi(w[i].z), xr[k][5], a[i]);
+      a[i] = fmaf(bf_lo(w[i].w), xr[k][6], a[i]);
+      a[i] = fmaf(bf_hi(w[i].w), xr[k][7], a[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-// splits per KV head for a context of L positions (about 128 positions each)
-__device__ __forceinline__ int att_splits(int L, int smax) {
-  const int s = (L + 127) / 128;
-  return s < 1 ? 1 : (s > smax ? smax : s);
-}
-
 // ---------------------------------------------------------------------------
-// attention unit: one KV head, one split of the positions; writes the split's
-// partial (o, m, l) per query head.  The merge happens in the O-proj prologue.
+// attention: KV head h, split s of ns over the positions; writes the split's
+// partial (o, m, l) per query head to the workspace slot [h][s]
 // ---------------------------------------------------------------------------
 template <int GQ>
-__device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P) {
+__device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P) {
   const iron_qwen3_model& m = p.m;
   constexpr int PER = HDIM / 32;
   constexpr int U = 4;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int L = P + 1;
   const int chunk = (L + ns - 1) / ns;
-  const int start = s * chunk, end = min(L, start + chunk);
+  const int start = min(L, s * chunk), end = min(L, start + chunk);
   float* qf = S.att;                   // [GQ][HD]
   float* kt = qf + GQ * HDIM;          // [HD]
   float* vt = kt + HDIM;               // [HD]
@@ -535,8 +731,8 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
       const int i = lane + 32 * j;
-      v[2 * j] = bf2f(ldcg_u16(src + i));
-      v[2 * j + 1] = bf2f(ldcg_u16(src + i + HDIM / 2));
+      v[2 * j] = bf2f(__ldcg(src + i));
+      v[2 * j + 1] = bf2f(__ldcg(src + i + HDIM / 2));
       wv[2 * j] = bf2f(__ldg(nw + i));
       wv[2 * j + 1] = bf2f(__ldg(nw + i + HDIM / 2));
       cs[j] = bf2f(__ldg(ang + 2 * i));
@@ -563,7 +759,8 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int
       }
     }
   }
-  __syncthreads();
+  csync();
+  STEP_MARK(layer, 14);
   // flash decoding over [start, end): the online softmax of attn_split_kernel, with the
   // next group of positions loaded while the current one is reduced
   const float scale = 1.4426950408889634f / sqrtf((float)HDIM);
@@ -663,8 +860,8 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int
       pw[HDIM + 1] = ll[g];
     }
   }
-  __syncthreads();
-  float* ws = m.attn_ws + ((size_t)(h * ns + s) * GQ) * (HDIM + 2);
+  csync();
+  float* ws = m.attn_ws + ((size_t)(h * GMAX + s) * GQ) * (HDIM + 2);
   for (int t = threadIdx.x; t < GQ * HDIM; t += NT) {
     const int g = t / HDIM, d = t - g * HDIM;
     float M = -INFINITY;
@@ -686,78 +883,59 @@ __device__ void attention_unit(const Kp& p, const Smem& S, int layer, int h, int
   }
 }
 
-// Merge the split partials of every head (attn_combine_kernel's arithmetic) into
-// bf16 bits in xhi; CTA 0 also stores them to m.attn.
+// Merge the ns split partials of KV head h (attn_combine_kernel's arithmetic) into
+// bf16 bits in xhi[0, GQ*HD).  The partials are contiguous in the workspace and
+// come in with one bulk copy; `use` counts the calls (mbarrier phase).
 template <int GQ>
-__device__ void stage_attention(const Kp& p, const Smem& S, int ns) {
-  const iron_qwen3_model& m = p.m;
-  const int Hq = m.Hq;
-  float* wgt = S.mrg;            // [Hq][SMAX]: m, then 2^(m - M)
-  float* lsum = S.mrg + Hq * SMAX;  // [Hq]
-  float* lv = (float*)S.xlo;     // [Hq][SMAX] l values (xlo is free until the BFP pass)
-  for (int t = threadIdx.x; t < Hq * ns; t += NT) {
-    const int hh = t / ns, sp = t - hh * ns;
-    const int h = hh / GQ, g = hh - h * GQ;
-    const float* ps = m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2);
-    wgt[hh * SMAX + sp] = __ldcg(ps + HDIM);
-    lv[hh * SMAX + sp] = __ldcg(ps + HDIM + 1);
+__device__ bool merge_splits(const Kp& p, const Smem& S, int h, int ns, int use) {
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    const float* base = p.m.attn_ws + (size_t)h * GMAX * GQ * (HDIM + 2);
+    const uint32_t bytes = (uint32_t)ns * GQ * (HDIM + 2) * 4;
+    // the partials were written through the generic proxy by the group's CTAs
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    mbar_expect(&S.mbar[NMB], bytes);
+    bulk_g2s(S.mst, base, bytes, &S.mbar[NMB]);
+    S.flag[3] = wait_slot(&S.mbar[NMB], p.m.sync, (uint32_t)(use & 1)) ? 1 : 0;
+    if (!S.flag[3]) {  // leaving early: let the copy land first (bounded)
+      const unsigned long long t0 = gtimer();
+      while (!mbar_test(&S.mbar[NMB], (uint32_t)(use & 1)) && gtimer() - t0 < 20ull * 1000 * 1000) {
+      }
+    }
   }
-  __syncthreads();
-  for (int hh = threadIdx.x; hh < Hq; hh += NT) {
+  csync();
+  if (!S.flag[3]) return false;
+  for (int t = tid; t < GQ * HDIM; t += NT) {
+    const int g = t / HDIM, d = t - g * HDIM;
+    const float* ps = S.mst + g * (HDIM + 2);
     float M = -INFINITY;
-    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, wgt[hh * SMAX + sp]);
-    float l = 0.f;
-    for (int sp = 0; sp < ns; ++sp) {
-      const float f = M != -INFINITY ? exp2f(wgt[hh * SMAX + sp] - M) : 0.f;
-      wgt[hh * SMAX + sp] = f;
-      l = fmaf(lv[hh * SMAX + sp], f, l);
+    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, ps[sp * GQ * (HDIM + 2) + HDIM]);
+    float oo = 0.f, lsum = 0.f;
+    if (M != -INFINITY) {
+      for (int sp = 0; sp < ns; ++sp) {
+        const float* q = ps + sp * GQ * (HDIM + 2);
+        const float f = exp2f(q[HDIM] - M);
+        oo = fmaf(q[d], f, oo);
+        lsum = fmaf(q[HDIM + 1], f, lsum);
+      }
     }
-    lsum[hh] = l;
+    S.xhi[t] = f2bf(lsum > 0.f ? oo / lsum : 0.f);
   }
-  __syncthreads();
-  const int QD = Hq * HDIM;
-  constexpr int B4 = 4;  // outputs per thread per pass, their partial loads in flight together
-  for (int i0 = threadIdx.x; i0 < QD; i0 += NT * B4) {
-    float ov[B4][SMAX];
-#pragma unroll
-    for (int k = 0; k < B4; ++k) {
-      const int i = i0 + k * NT;
-      const int hh = i / HDIM, d = i - hh * HDIM;
-      const int h = hh / GQ, g = hh - h * GQ;
-#pragma unroll
-      for (int sp = 0; sp < SMAX; ++sp)
-        if (i < QD && sp < ns) ov[k][sp] = __ldcg(m.attn_ws + ((size_t)(h * ns + sp) * GQ + g) * (HDIM + 2) + d);
-    }
-#pragma unroll
-    for (int k = 0; k < B4; ++k) {
-      const int i = i0 + k * NT;
-      if (i >= QD) break;
-      const int hh = i / HDIM;
-      float oo = 0.f;
-#pragma unroll
-      for (int sp = 0; sp < SMAX; ++sp)
-        if (sp < ns) oo = fmaf(ov[k][sp], wgt[hh * SMAX + sp], oo);
-      const float l = lsum[hh];
-      const uint16_t b = f2bf(l > 0.f ? oo / l : 0.f);
-      S.xhi[i] = b;
-      if (blockIdx.x == 0) m.attn[i] = b;
-    }
-  }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int G, int GQ>
-__global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant__ Kp p) {
+__global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_constant__ Kp p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const iron_qwen3_model& m = p.m;
   const Smem S = carve(smem_raw, p, GQ);
   int32_t* sync = m.sync;
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int N = gridDim.x;
+  const int tid = threadIdx.x;
+  const int N = gridDim.x, D = m.D, NL = m.n_layers;
   const Plan P = make_plan(p);
-  const int QD = m.Hq * HDIM;
   const int pos = m.pos[0];
   // a position outside the cache or a token outside the vocabulary: record and leave
   // before touching memory (every CTA takes the same decision)
@@ -765,139 +943,247 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
     if (tid == 0) atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_INPUT);
     return;
   }
-  const int ns = att_splits(pos + 1, p.smax);
-  const int unit = blockIdx.x < m.Hkv * ns ? (int)blockIdx.x : -1;
-
-  if (tid == 0) {
-    mbar_init(&S.mbar[0]);
-    mbar_init(&S.mbar[1]);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  {  // the layer pointer table, read once
-    const int nw = m.n_layers * (int)(sizeof(iron_qwen3_layer) / 8);
+  // projection accumulators: two sets of [NL][O, down][D] float64 that alternate by
+  // token; this token zeroes the other set for the next one
+  const int parity = __ldcg((const int*)&sync[SYNC_PARITY]) & 1;
+  double* acc_base = (double*)((uint8_t*)m.attn_ws + (size_t)m.Hkv * GMAX * GQ * (HDIM + 2) * 4);
+  const size_t lstride = (size_t)(1 + XREP) * D;  // accumulator doubles per layer
+  double* acc = acc_base + (size_t)parity * NL * lstride;
+  if (tid < NT) {
+    double* other = acc_base + (size_t)(parity ^ 1) * NL * lstride;
+    for (size_t i = (size_t)blockIdx.x * NT + tid; i < NL * lstride; i += (size_t)N * NT) other[i] = 0.0;
+    // the layer pointer table, read once
+    const int nw = NL * (int)(sizeof(iron_qwen3_layer) / 8);
     for (int i = tid; i < nw; i += NT) ((unsigned long long*)S.lay)[i] = __ldg(((const unsigned long long*)m.layers) + i);
   }
-  __syncthreads();
   if (tid == 0) {
-    issue(p, P, S, 0, 0);
-    issue(p, P, S, 1, 1);
-    prefetch_layer_l2(p, P, S, 0);
-    prefetch_layer_l2(p, P, S, 1);
+    for (int i = 0; i <= NMB; ++i) mbar_init(&S.mbar[i]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    S.rs->tail = 0;
+    S.rs->issued = S.rs->consumed = S.rs->abort = 0;
   }
-  int ci = 0;            // next chunk to consume
-  unsigned epoch = 0;    // grid barriers passed
-  bool ok = true;
+  __syncthreads();  // the last barrier of all NT + 32 threads
+  if (tid >= NT) {
+    if (tid == NT) producer(p, P, S, sync);
+    return;
+  }
+  // layer-0 input: the token's embedding row, or the hidden state given in x
+  load_ro(S.sx, p.embed_input ? m.embed + (size_t)m.tok[0] * D : m.x, D);
+  load_ro(S.xlo, S.lay[0].norm1, D);
 
-  auto barrier = [&]() -> bool {
-    __syncthreads();
-    if (tid == 0) S.flag[0] = grid_barrier(sync, (++epoch) * (unsigned)N) ? 1 : 0;
-    else ++epoch;
-    __syncthreads();
-    return S.flag[0] != 0;
-  };
-  // consume my chunks of one phase kind; fn(chunk, buffer) does the math
-  auto consume = [&](int kind, auto&& fn) -> bool {
-    const int nch = kind == 5 ? P.hnch : P.nch[kind];
-    for (int k = 0; k < nch; ++k, ++ci) {
-      const int b = ci & 1;
-      if (tid == 0) S.flag[2] = wait_buf(S, sync, b, (ci >> 1) & 1) ? 1 : 0;
-      __syncthreads();
-      if (!S.flag[2]) return false;
-      const Chunk ch = chunk_at(P, ci, m.n_layers);
-      fn(ch, S.buf[b]);
-      __syncthreads();
-      if (tid == 0) issue(p, P, S, ci + 2, b);
+  bool ok = true;
+  // consume chunk i: fn(buffer) once its copy landed, then release its space
+  volatile RingState& vrs = *S.rs;
+  auto consume = [&](int i, auto&& fn) -> bool {
+    const int sl = i % NMB;
+    if (tid == 0) S.flag[2] = wait_slot(&S.mbar[sl], sync, (uint32_t)((i / NMB) & 1)) ? 1 : 0;
+    csync();
+    if (!S.flag[2]) return false;
+    if ((i >> 2) < NL) STEP_MARK(i >> 2, 16 + (i & 3));
+    fn(S.ring + vrs.slot[sl]);
+    csync();
+    if ((i >> 2) < NL) STEP_MARK(i >> 2, 20 + (i & 3));
+    if (tid == 0) {
+      fence_proxy_async();
+      vrs.tail = vrs.end[sl];
+      vrs.consumed = i + 1;
     }
     return true;
   };
+  auto arrive = [&](int word) {
+    csync();
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd((unsigned*)&sync[word], 1u);
+    }
+  };
+  auto wait = [&](int word, unsigned target) -> bool {
+    if (tid == 0) S.flag[0] = wait_count(sync, word, target) ? 1 : 0;
+    csync();
+    return S.flag[0] != 0;
+  };
 
-  for (int layer = 0; layer < m.n_layers && ok; ++layer) {
+  const int h = P.h, gsz = P.gsz;
+  const int k0 = 4 * P.u0, w = 4 * (P.u1 - P.u0);
+  for (int layer = 0; layer < NL && ok; ++layer) {
     const iron_qwen3_layer& Lw = S.lay[layer];
-    // ---- QKV: hn = RMSNorm_golden(x, norm1); raw = bf16(Wqkv @ hn) ----
-    {
-      const bool emb = layer == 0 && p.embed_input;
-      const uint16_t* xs = emb ? m.embed + (size_t)m.tok[0] * m.D : m.x;
-      stage_rmsnorm(S, xs, emb, Lw.norm1, m.D, m.eps, 1, nullptr, (emb && blockIdx.x == 0) ? m.x : nullptr);
-      __syncthreads();
-      bfp_stage(S, m.D, G);
-      __syncthreads();
-      const int rbq = rowb(m.D, G);
-      ok = consume(PH_QKV, [&](const Chunk& ch, const uint8_t* wb) {
-        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbq, m.D, S, [&](int r, double a, double) {
-          m.raw[ch.r0 + r] = f2bf((float)a);
-        });
+    double* oacc = acc + (size_t)layer * lstride;
+    double* xacc = oacc + (size_t)D * (1 + h % XREP);  // this KV-head group's replica
+    const int c0 = 4 * layer;
+    STEP_MARK(layer, 0);
+    STEP_CLK(layer, 28);
+    // ---- QKV: x = bf16(x1 + bf16(down)), hn = RMSNorm_golden(x, norm1), raw = bf16(Wqkv @ hn) ----
+    if (layer > 0) {
+      if (!(ok = wait(SYNC_B1, (unsigned)layer * N))) break;
+      STEP_MARK(layer, 1);
+      resid_add<XREP>(S.sx, S.sx1, acc + (size_t)(layer - 1) * lstride + D, D);
+    }
+    csync();
+    STEP_MARK(layer, 24);
+    if (m.trace && blockIdx.x == 0)
+      for (int i = tid; i < D; i += NT) m.trace[(size_t)layer * D + i] = S.sx[i];
+    stage_norm(S, S.sx, D, m.eps, 1, nullptr);
+    csync();
+    STEP_MARK(layer, 25);
+    bfp_stage(S, D, G);
+    csync();
+    STEP_MARK(layer, 2);
+    ok = consume(c0 + CK_QKV, [&](const uint8_t* wb) {
+      chunk_gemv<G, 32, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
+        m.raw[qkv_src_row(P.q0 + r, h, GQ, m.Hq, m.Hkv)] = f2bf((float)a);
       });
-      if (tid == 0 && ok) {
-        prefetch_layer_l2(p, P, S, layer + 2);
-        if (unit >= 0) {  // this CTA's KV range of this layer, ahead of the attention phase
-          const int L = pos + 1, h = unit / ns, sp = unit - (unit / ns) * ns;
-          const int chunk = (L + ns - 1) / ns, st = sp * chunk, en = min(min(L, st + chunk), pos);
-          if (en > st) {
-            const uint16_t* hb = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
-            prefetch_l2(hb + (size_t)st * 2 * HDIM, (uint32_t)(en - st) * 4 * HDIM);
+    });
+    if (!ok) break;
+    STEP_MARK(layer, 3);
+    if (tid == 0) {  // this CTA's KV range of this layer, ahead of the attention
+      const int L = pos + 1, chunk = (L + gsz - 1) / gsz;
+      const int st = min(L, P.gi * chunk), en = min(min(L, st + chunk), pos);
+      if (en > st) {
+        const uint16_t* hb = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
+        prefetch_l2(hb + (size_t)st * 2 * HDIM, (uint32_t)(en - st) * 4 * HDIM);
+      }
+    }
+    arrive(SYNC_G1 + h);
+    if (!(ok = wait(SYNC_G1 + h, (unsigned)(layer + 1) * gsz))) break;
+    STEP_MARK(layer, 4);
+    // ---- attention: KV head h, split gi of gsz ----
+    attention_split<GQ>(p, S, layer, h, P.gi, gsz, pos);
+    STEP_MARK(layer, 5);
+    arrive(SYNC_G1 + m.Hkv + h);
+    if (!(ok = wait(SYNC_G1 + m.Hkv + h, (unsigned)(layer + 1) * gsz))) break;
+    STEP_MARK(layer, 6);
+    // ---- O (head h's column block): oacc += Wo[:, head h] @ attn[head h] ----
+    if (!(ok = merge_splits<GQ>(p, S, h, gsz, layer))) break;
+    csync();
+    STEP_MARK(layer, 15);
+    bfp_stage(S, GQ * HDIM, G);
+    csync();
+    STEP_MARK(layer, 7);
+    ok = consume(c0 + CK_O, [&](const uint8_t* wb) {
+      chunk_gemv<G, GQ * HDIM / 16 < 32 ? GQ * HDIM / 16 : 32, false>(wb, P.o1 - P.o0, rowb_heads(GQ, G), GQ * HDIM, S,
+                               [&](int r, double a, double) { atomicAdd(oacc + P.o0 + r, a); });
+    });
+    if (!ok) break;
+    STEP_MARK(layer, 8);
+    load_ro(S.xlo, Lw.norm2, D);
+    arrive(SYNC_B2);
+    if (!(ok = wait(SYNC_B2, (unsigned)(layer + 1) * N))) break;
+    STEP_MARK(layer, 9);
+    // ---- gate/up: x1 = bf16(x + bf16(O)), hf = RMSNorm_kernel(x1, norm2),
+    //      gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for this CTA's slice ----
+    resid_add<1>(S.sx1, S.sx, oacc, D);
+    csync();
+    STEP_MARK(layer, 26);
+    stage_norm(S, S.sx1, D, m.eps, 0, nullptr);
+    csync();
+    bfp_stage(S, D, G);
+    csync();
+    STEP_MARK(layer, 10);
+    ok = consume(c0 + CK_GU, [&](const uint8_t* wb) {
+      chunk_gemv<G, 32, true>(wb, w, rowb(D, G), D, S, [&](int r, double g, double u) {
+        S.ghv[r] = rbf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
+      });
+    });
+    if (!ok) break;
+    STEP_MARK(layer, 11);
+    // the slice as one exact int16 block (hi + lo words)
+    if (tid < 32) {
+      float mx = 0.f;
+      for (int j = tid; j < w; j += 32) mx = fmaxf(mx, fabsf(S.ghv[j]));
+      mx = warp_max(mx);
+      float sc, inv;
+      bfp_scale(mx, sc, inv);
+      for (int j = tid; j < w; j += 32) {
+        const float t = S.ghv[j] * sc;
+        const int hi = __float2int_rn(t);
+        S.dh[j] = (uint16_t)(int16_t)hi;
+        S.dl[j] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+      }
+      if (tid == 0) S.flag[4] = __float_as_int(inv);
+    }
+    csync();
+    STEP_MARK(layer, 12);
+    // ---- down (this CTA's K slice): xacc += Wd[:, k0:k0+w] @ gh[k0:k0+w] ----
+    ok = consume(c0 + CK_D, [&](const uint8_t* wb) {
+      const uint32_t* wq = (const uint32_t*)wb;
+      const uint16_t* wsc = (const uint16_t*)(wb + (size_t)w * D);
+      const uint32_t* xh = (const uint32_t*)S.dh;
+      const uint32_t* xl = (const uint32_t*)S.dl;
+      const float inv = __int_as_float(S.flag[4]);
+      // words j < jb1 belong to the slice's first scale group, j < jb2 to its second,
+      // the rest to its third (a 64-column slice touches at most three groups of 32)
+      const int nw4 = w >> 2;
+      const int jb1 = (min(w, (P.ga + 1) * G - k0)) >> 2, jb2 = (min(w, (P.ga + 2) * G - k0)) >> 2;
+      constexpr int RPT = 4;  // rows per thread and pass, their loads overlapped
+      for (int r0 = tid; r0 < D; r0 += NT * RPT) {
+        int ah[RPT][3], al[RPT][3];
+#pragma unroll
+        for (int q = 0; q < RPT; ++q)
+#pragma unroll
+          for (int e = 0; e < 3; ++e) ah[q][e] = al[q][e] = 0;
+#pragma unroll
+        for (int j = 0; j < SLICE_MAX / 4; ++j) {
+          if (j < nw4) {
+            const int h0 = (int)xh[2 * j], h1 = (int)xh[2 * j + 1], l0 = (int)xl[2 * j], l1 = (int)xl[2 * j + 1];
+            const int e = j < jb1 ? 0 : (j < jb2 ? 1 : 2);
+#pragma unroll
+            for (int q = 0; q < RPT; ++q) {
+              const int r = r0 + q * NT;
+              const int wv = r < D ? (int)wq[(size_t)j * D + r] : 0;
+              const int dh = __dp2a_hi(h1, wv, __dp2a_lo(h0, wv, 0));
+              const int dl = __dp2a_hi(l1, wv, __dp2a_lo(l0, wv, 0));
+              ah[q][0] += e == 0 ? dh : 0;
+              ah[q][1] += e == 1 ? dh : 0;
+              ah[q][2] += e == 2 ? dh : 0;
+              al[q][0] += e == 0 ? dl : 0;
+              al[q][1] += e == 1 ? dl : 0;
+              al[q][2] += e == 2 ? dl : 0;
+            }
           }
         }
+#pragma unroll
+        for (int q = 0; q < RPT; ++q) {
+          const int r = r0 + q * NT;
+          if (r >= D) continue;
+          double a = 0.0;
+#pragma unroll
+          for (int e = 0; e < 3; ++e)
+            if (e < P.nsg) {
+              const long long t = (long long)ah[q][e] * 32768 + al[q][e];
+              a = fma((double)t, (double)(bf2f(wsc[(size_t)e * D + r]) * inv) * (1.0 / 32768.0), a);
+            }
+          atomicAdd(xacc + r, a);
+        }
       }
-      if (!ok || !barrier()) break;
-    }
-    // ---- attention: one KV head and one split of the positions per CTA ----
-    if (unit >= 0) attention_unit<GQ>(p, S, layer, unit / ns, unit - (unit / ns) * ns, ns, pos);
-    if (!barrier()) break;
-    // ---- O-proj + residual: x1 = bf16(x + bf16(Wo @ attn)); the split merge first ----
-    {
-      stage_attention<GQ>(p, S, ns);
-      __syncthreads();
-      bfp_stage(S, QD, G);
-      __syncthreads();
-      const int rbo = rowb(QD, G);
-      ok = consume(PH_O, [&](const Chunk& ch, const uint8_t* wb) {
-        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbo, QD, S, [&](int r, double a, double) {
-          const int row = ch.r0 + r;
-          m.x1[row] = f2bf(bf2f(ldcg_u16(m.x + row)) + rbf_d(a));
-        });
-      });
-      if (!ok || !barrier()) break;
-    }
-    // ---- gate/up: gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)), hf = RMSNorm_kernel(x1) ----
-    {
-      stage_rmsnorm(S, m.x1, false, Lw.norm2, m.D, m.eps, 0, nullptr, nullptr);
-      __syncthreads();
-      bfp_stage(S, m.D, G);
-      __syncthreads();
-      const int rbg = rowb(m.D, G);
-      ok = consume(PH_GU, [&](const Chunk& ch, const uint8_t* wb) {
-        chunk_gemv<G, true>(wb, ch.r1 - ch.r0, rbg, m.D, S, [&](int r, double g, double u) {
-          m.gh[ch.r0 + r] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
-        });
-      });
-      if (!ok || !barrier()) break;
-    }
-    // ---- down + residual: x = bf16(x1 + bf16(Wd @ gh)) ----
-    {
-      load_bits(S.xhi, m.gh, m.FF, false);
-      __syncthreads();
-      bfp_stage(S, m.FF, G);
-      __syncthreads();
-      const int rbd = rowb(m.FF, G);
-      ok = consume(PH_D, [&](const Chunk& ch, const uint8_t* wb) {
-        chunk_gemv<G, false>(wb, ch.r1 - ch.r0, rbd, m.FF, S, [&](int r, double a, double) {
-          const int row = ch.r0 + r;
-          m.x[row] = f2bf(bf2f(ldcg_u16(m.x1 + row)) + rbf_d(a));
-        });
-      });
-      if (!ok || !barrier()) break;
-    }
+    });
+    if (!ok) break;
+    STEP_MARK(layer, 13);
+    load_ro(S.xlo, layer + 1 < NL ? S.lay[layer + 1].norm1 : m.final_norm, D);
+    arrive(SYNC_B1);
   }
 
-  if (ok && S.flag[0]) {
-    // ---- final RMSNorm (golden form) + lm_head + greedy argmax ----
-    stage_rmsnorm(S, m.x, false, m.final_norm, m.D, m.eps, 1, S.xf, nullptr);
-    __syncthreads();
-    if (m.lm_w8) bfp_stage(S, m.D, G);
-    __syncthreads();
+  STEP_MARK(NL, 0);
+  if (ok) ok = wait(SYNC_B1, (unsigned)NL * N);
+  STEP_MARK(NL, 1);
+  STEP_CLK(NL, 29);
+  if (ok) {
+    // ---- final: x = bf16(x1 + bf16(down)), RMSNorm (golden) + lm_head + greedy argmax ----
+    resid_add<XREP>(S.sx, S.sx1, acc + (size_t)(NL - 1) * lstride + D, D);
+    for (int i = tid; i < D; i += NT) {
+      if (blockIdx.x == 0) {
+        m.x[i] = S.sx[i];
+        if (m.trace) m.trace[(size_t)NL * D + i] = S.sx[i];
+      }
+    }
+    csync();
+    stage_norm(S, S.sx, D, m.eps, 1, S.xf);
+    csync();
+    if (m.lm_w8) bfp_stage(S, D, G);
+    csync();
+    const int lane = tid & 31, wid = tid >> 5;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    const int rbh = m.lm_w8 ? rowb(m.D, G) : m.D * 2;
+    const int rbh = m.lm_w8 ? rowb(D, G) : D * 2;
     auto track = [&](int idx, uint16_t o) {
       if (m.logits) m.logits[idx] = o;
       if (better(bf2f(o), idx, bv, bi)) {
@@ -905,42 +1191,53 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
         bi = idx;
       }
     };
-    ok = consume(5, [&](const Chunk& ch, const uint8_t* wb) {
-      const int n = ch.r1 - ch.r0;
-      if (m.lm_w8) {
-        chunk_gemv<G, false>(wb, n, rbh, m.D, S, [&](int r, double a, double) { track(ch.r0 + r, f2bf((float)a)); });
-      } else {
-        constexpr int R = 3;
-        const int wid = tid >> 5;
-        for (int r0 = wid * R; r0 < n; r0 += NWARP * R) {
-          const uint8_t* rp[R];
+    float xr[4][8];  // this lane's activations for the D == 1024 bf16 rows
+    if (D == 1024) {
 #pragma unroll
-          for (int i = 0; i < R; ++i) rp[i] = wb + (size_t)min(r0 + i, n - 1) * rbh;
-          float out[R];
-          rows_dot_bf16<R>(rp, m.D, S.xf, out);
-          if (lane == 0) {
+      for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int i = 0; i < R; ++i)
-              if (r0 + i < n) track(ch.r0 + r0 + i, f2bf(out[i]));
+        for (int e = 0; e < 8; ++e) xr[k][e] = S.xf[(lane + 32 * k) * 8 + e];
+    }
+    for (int j = 0; j < P.hnch && ok; ++j) {
+      const int r0 = P.hlo + j * p.lm_rows, n = min(P.hhi, r0 + p.lm_rows) - r0;
+      ok = consume(4 * NL + j, [&](const uint8_t* wb) {
+        if (m.lm_w8) {
+          chunk_gemv<G, 32, false>(wb, n, rbh, D, S, [&](int r, double a, double) { track(r0 + r, f2bf((float)a)); });
+        } else {
+          constexpr int R = 2;
+          for (int rr = wid * R; rr < n; rr += NWARP * R) {
+            const uint8_t* rp[R];
+#pragma unroll
+            for (int i = 0; i < R; ++i) rp[i] = wb + (size_t)min(rr + i, n - 1) * rbh;
+            float out[R];
+            if (D == 1024)
+              rows_dot_bf16_reg<R, 4>(rp, xr, out);
+            else
+              rows_dot_bf16<R>(rp, D, S.xf, out);
+            if (lane == 0) {
+#pragma unroll
+              for (int i = 0; i < R; ++i)
+                if (rr + i < n) track(r0 + rr + i, f2bf(out[i]));
+            }
           }
         }
-      }
-    });
+      });
+    }
+    STEP_MARK(NL, 2);
     if (ok) {
-      // CTA-best over the warps' lane 0, then publish and let the last CTA reduce
-      const int wid = tid >> 5;
-      if (lane == 0) {
-        S.att[wid] = bv;
-        ((int*)S.att)[NWARP + wid] = bi;
-      }
-      __syncthreads();
+      // CTA-best over the threads that tracked rows, then publish and let the last CTA reduce
+      float* cv_s = S.att;
+      int* ci_s = (int*)(S.att + NT);
+      cv_s[tid] = bv;
+      ci_s[tid] = bi;
+      csync();
       if (tid == 0) {
         float v = -INFINITY;
         int i = 0x7fffffff;
-        for (int w = 0; w < NWARP; ++w)
-          if (better(S.att[w], ((int*)S.att)[NWARP + w], v, i)) {
-            v = S.att[w];
-            i = ((int*)S.att)[NWARP + w];
+        for (int t = 0; t < NT; ++t)
+          if (better(cv_s[t], ci_s[t], v, i)) {
+            v = cv_s[t];
+            i = ci_s[t];
           }
         float* cv = (float*)m.cand;
         int* cix = (int*)m.cand + 1024;
@@ -967,19 +1264,62 @@ __global__ void __launch_bounds__(NT, 1) qwen3_step_kernel(const __grid_constant
             m.seq_len[0] = np + 1;
             m.kv_off[0] = np * 2 * HDIM;
           }
+          // every CTA has passed every wait of this token: reset the counters and
+          // hand the other accumulator set to the next token
+          sync[SYNC_B1] = 0;
+          sync[SYNC_B2] = 0;
+          for (int k = 0; k < 2 * m.Hkv; ++k) sync[SYNC_G1 + k] = 0;
           sync[SYNC_ARGMAX] = 0;
-          sync[SYNC_BAR] = 0;
+          sync[SYNC_PARITY] = parity ^ 1;
           __threadfence();
         }
       }
     }
   }
-  // drain bulk copies still in flight (only after an early exit) before leaving
-  if (tid == 0 && ci < P.total) {
-    for (int k = ci; k < min(ci + 2, P.total); ++k) {
-      const unsigned long long t0 = gtimer();
-      while (!mbar_test(&S.mbar[k & 1], (k >> 1) & 1) && gtimer() - t0 < 20ull * 1000 * 1000) {
-      }
+  // after an early exit: stop the producer and wait for the copies in flight
+  if (tid == 0 && vrs.consumed < P.total) {
+    vrs.abort = 1;
+    drain(S, vrs.consumed, vrs.issued);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// weight packing for the step kernel
+// ---------------------------------------------------------------------------
+// wo_heads[h][r] = [wo[r, h*GQ*HD : (h+1)*GQ*HD] int8 | its GQ*HD/G bf16 scales | 0 pad]
+__global__ void pack_wo_heads_kernel(const uint8_t* wire, int D, int QD, int Hkv, int G, uint8_t* out) {
+  const int GQH = QD / Hkv, rb_in = rowb(QD, G), rb_out = rowb_heads(GQH / HDIM, G);
+  const long long total = (long long)Hkv * D * rb_out;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i % rb_out);
+    const long long hr = i / rb_out;
+    const int r = (int)(hr % D), h = (int)(hr / D);
+    const uint8_t* row = wire + (size_t)r * rb_in;
+    uint8_t v = 0;
+    if (b < GQH)
+      v = row[h * GQH + b];
+    else if (b < GQH + 2 * (GQH / G))
+      v = row[QD + 2 * (h * (GQH / G)) + (b - GQH)];
+    out[i] = v;
+  }
+}
+
+// wd_cols[k/4][r][k%4] = wd[r, k]; wd_col_scales[g][r] = the scale of wd row r, group g
+__global__ void pack_wd_cols_kernel(const uint8_t* wire, int D, int FF, int G, uint8_t* q, uint16_t* s) {
+  const int rb = rowb(FF, G);
+  const long long nq = (long long)FF * D, ns = (long long)(FF / G) * D;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nq + ns;
+       i += (long long)gridDim.x * blockDim.x) {
+    if (i < nq) {
+      const int e = (int)(i & 3);
+      const long long jr = i >> 2;
+      const int r = (int)(jr % D), j = (int)(jr / D);
+      q[i] = wire[(size_t)r * rb + 4 * j + e];
+    } else {
+      const long long k = i - nq;
+      const int r = (int)(k % D), g = (int)(k / D);
+      s[k] = ((const uint16_t*)(wire + (size_t)r * rb + FF))[g];
     }
   }
 }
@@ -991,23 +1331,41 @@ static int launch(const Kp& p, int grid, size_t smem, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
     attr[dev] = true;
   }
   void* args[] = {(void*)&p};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)fn, dim3(grid), dim3(NT), args, smem, st);
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)fn, dim3(grid), dim3(NT + 32), args, smem, st);
   if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 step launch: %s", cudaGetErrorString(e));
   return IRON_OK;
 }
 
-static int kmax_of(const iron_qwen3_model* m) {
-  int k = m->D;
-  if (m->Hq * m->HD > k) k = m->Hq * m->HD;
-  if (m->FF > k) k = m->FF;
-  return k;
+static int grid_for(const iron_qwen3_model* m) {
+  (void)m;
+  return iron_num_sms();
 }
 
-static int validate(const iron_qwen3_model* m) {
+// host mirror of the per-CTA chunk sizes: the largest chunk of any CTA
+static size_t max_chunk(const iron_qwen3_model* m, int N, int lm_rows) {
+  const int G = m->group, GQ = m->Hq / m->Hkv, D = m->D;
+  size_t mx = (size_t)lm_rows * (m->lm_w8 ? rowb(D, G) : D * 2);
+  for (int c = 0; c < N; ++c) {
+    int h, c0, c1, lo, hi;
+    head_group(c, N, m->Hkv, h, c0, c1);
+    part((GQ + 2) * HDIM, c - c0, c1 - c0, lo, hi);
+    mx = std::max(mx, (size_t)(hi - lo) * rowb(D, G));
+    part(D, c - c0, c1 - c0, lo, hi);
+    mx = std::max(mx, (size_t)(hi - lo) * rowb_heads(GQ, G));
+    part(m->FF / 4, c, N, lo, hi);
+    const int k0 = 4 * lo, k1 = 4 * hi;
+    const int nsg = k1 > k0 ? (k1 - 1) / G - k0 / G + 1 : 0;
+    mx = std::max(mx, (size_t)2 * (k1 - k0) * rowb(D, G));
+    mx = std::max(mx, (size_t)(hi - lo) * D * 4 + (size_t)nsg * D * 2);
+  }
+  return mx;
+}
+
+static int validate(const iron_qwen3_model* m, int grid) {
   IRON_REQUIRE(m != nullptr, IRON_ERR_ARG, "qwen3 step: null model");
   IRON_REQUIRE(m->HD == HDIM, IRON_ERR_UNSUPPORTED, "qwen3 step: head_dim %d (supported: 128)", m->HD);
   IRON_REQUIRE(m->Hkv >= 1 && m->Hq % m->Hkv == 0, IRON_ERR_ARG, "qwen3 step: Hq=%d, Hkv=%d", m->Hq, m->Hkv);
@@ -1015,22 +1373,19 @@ static int validate(const iron_qwen3_model* m) {
   IRON_REQUIRE(GQ == 1 || GQ == 2 || GQ == 4 || GQ == 8, IRON_ERR_UNSUPPORTED, "qwen3 step: GQA group %d", GQ);
   IRON_REQUIRE(m->group == 32 || m->group == 64 || m->group == 128, IRON_ERR_ARG, "qwen3 step: group %d",
                m->group);
-  IRON_REQUIRE(m->D % m->group == 0 && m->FF % m->group == 0 && m->D % 256 == 0 && m->D <= 4096, IRON_ERR_ARG,
-               "qwen3 step: D=%d FF=%d must be multiples of the group and D a multiple of 256 (<= 4096)", m->D,
-               m->FF);
-  IRON_REQUIRE(kmax_of(m) <= 16 * NT * 4, IRON_ERR_UNSUPPORTED, "qwen3 step: reduction length too large");
-  IRON_REQUIRE(2 * (m->D + 2 * (m->D / m->group)) <= BUF && m->FF + 2 * (m->FF / m->group) <= BUF, IRON_ERR_UNSUPPORTED,
-               "qwen3 step: rows larger than the %d-byte weight buffers", BUF);
-  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->raw && m->attn && m->x1 &&
-                   m->gh && m->attn_ws && m->cand && m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
+  IRON_REQUIRE(m->D % m->group == 0 && m->FF % m->group == 0 && m->D % 256 == 0 && m->D <= 4096 && m->FF % 4 == 0,
+               IRON_ERR_ARG, "qwen3 step: D=%d FF=%d must be multiples of the group and D a multiple of 256 (<= 4096)",
+               m->D, m->FF);
+  IRON_REQUIRE(grid >= m->Hkv && (grid + m->Hkv - 1) / m->Hkv <= GMAX, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: %d CTAs cannot form %d KV-head groups of at most %d", grid, m->Hkv, GMAX);
+  IRON_REQUIRE(4 * ((m->FF / 4 + grid - 1) / grid) <= SLICE_MAX, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: down-projection slice wider than %d columns", SLICE_MAX);
+  IRON_REQUIRE(m->D <= 4 * NT, IRON_ERR_UNSUPPORTED, "qwen3 step: hidden size %d above %d", m->D, 4 * NT);
+  IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
+  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->raw && m->attn_ws &&
+                   m->cand && m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
                IRON_ERR_ARG, "qwen3 step: null buffer in the model descriptor");
   return IRON_OK;
-}
-
-static int grid_for(const iron_qwen3_model* m, size_t smem) {
-  (void)m;
-  (void)smem;
-  return iron_num_sms();
 }
 
 }  // namespace qstep
@@ -1038,44 +1393,88 @@ static int grid_for(const iron_qwen3_model* m, size_t smem) {
 
 using namespace iron::qstep;
 
-extern "C" int iron_qwen3_sync_words(const iron_qwen3_model* m) { return SYNC_HEAD0 + (m ? m->Hkv : 64); }
-extern "C" int64_t iron_qwen3_cand_bytes(void) { return 1024 * 8; }
-extern "C" int iron_qwen3_grid(const iron_qwen3_model* m) { return grid_for(m, 0); }
-static int smax_for(const iron_qwen3_model* m, int grid) {
-  int s = grid / m->Hkv;
-  return s < 1 ? 1 : (s > SMAX ? SMAX : s);
+#ifdef IRON_STEP_PROFILE
+extern "C" int iron_qwen3_step_profile_buffer(void* buf) {
+  return cudaMemcpyToSymbol(g_step_prof, &buf, sizeof(buf)) == cudaSuccess ? IRON_OK : IRON_ERR_CUDA;
 }
+#endif
+
+extern "C" int iron_qwen3_sync_words(const iron_qwen3_model* m) { return SYNC_G1 + 2 * (m ? m->Hkv : 64); }
+extern "C" int64_t iron_qwen3_cand_bytes(void) { return 1024 * 8; }
+extern "C" int iron_qwen3_grid(const iron_qwen3_model* m) { return grid_for(m); }
+
+static int64_t partial_bytes(const iron_qwen3_model* m) {
+  return (int64_t)m->Hkv * GMAX * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
+}
+static int64_t acc_bytes(const iron_qwen3_model* m) { return (int64_t)2 * m->n_layers * (1 + XREP) * m->D * 8; }
 
 extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
-  if (!m || m->Hkv < 1) return 0;
-  return (int64_t)m->Hkv * smax_for(m, grid_for(m, 0)) * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
+  if (!m || m->Hkv < 1 || m->Hq % m->Hkv != 0) return 0;
+  return partial_bytes(m) + acc_bytes(m);
 }
 
 extern "C" int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream) {
-  IRON_REQUIRE(m && m->sync, IRON_ERR_ARG, "qwen3 sync reset: null");
+  IRON_REQUIRE(m && m->sync && m->attn_ws, IRON_ERR_ARG, "qwen3 sync reset: null");
   cudaError_t e = cudaMemsetAsync(m->sync, 0, (size_t)iron_qwen3_sync_words(m) * 4, (cudaStream_t)stream);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync((uint8_t*)m->attn_ws + partial_bytes(m), 0, (size_t)acc_bytes(m), (cudaStream_t)stream);
   if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 sync reset: %s", cudaGetErrorString(e));
   return IRON_OK;
 }
 
+extern "C" int64_t iron_qwen3_pack_wo_heads_bytes(int D, int QD, int Hkv, int group) {
+  if (D < 1 || Hkv < 1 || group < 1 || QD % (Hkv * HDIM) != 0) return -1;
+  return (int64_t)Hkv * D * rowb_heads(QD / Hkv / HDIM, group);
+}
+
+extern "C" int iron_qwen3_pack_wo_heads(const void* wo_wire, int D, int QD, int Hkv, int group, void* out,
+                                        void* stream) {
+  IRON_REQUIRE(wo_wire && out, IRON_ERR_ARG, "pack_wo_heads: null pointer");
+  IRON_REQUIRE(D >= 1 && Hkv >= 1 && group >= 16 && QD % (Hkv * HDIM) == 0 && (QD / Hkv) % group == 0,
+               IRON_ERR_ARG, "pack_wo_heads: D=%d QD=%d Hkv=%d group=%d", D, QD, Hkv, group);
+  const long long total = iron_qwen3_pack_wo_heads_bytes(D, QD, Hkv, group);
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+  pack_wo_heads_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)wo_wire, D, QD, Hkv, group,
+                                                                  (uint8_t*)out);
+  return iron_check_launch("pack_wo_heads_kernel");
+}
+
+extern "C" int iron_qwen3_pack_wd_cols(const void* wd_wire, int D, int FF, int group, void* out_q,
+                                       uint16_t* out_scales, void* stream) {
+  IRON_REQUIRE(wd_wire && out_q && out_scales, IRON_ERR_ARG, "pack_wd_cols: null pointer");
+  IRON_REQUIRE(D >= 1 && group >= 4 && FF % 4 == 0 && FF % group == 0, IRON_ERR_ARG,
+               "pack_wd_cols: D=%d FF=%d group=%d", D, FF, group);
+  const long long total = (long long)FF * D + (long long)(FF / group) * D;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+  pack_wd_cols_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)wd_wire, D, FF, group,
+                                                                 (uint8_t*)out_q, out_scales);
+  return iron_check_launch("pack_wd_cols_kernel");
+}
+
 extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream) {
-  int rc = validate(m);
+  const int grid = grid_for(m);
+  int rc = validate(m, grid);
   if (rc) return rc;
+  const int GQ = m->Hq / m->Hkv;
   Kp p;
   p.m = *m;
   p.embed_input = embed_input;
   p.advance = advance;
-  p.kmax = kmax_of(m);
-  const int GQ = m->Hq / m->Hkv;
-  const size_t smem = smem_bytes(p.kmax, m->D, GQ, m->Hq, m->n_layers);
-  IRON_REQUIRE(smem <= 227 * 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: %zu bytes of shared memory", smem);
-  const int grid = grid_for(m, smem);
-  IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
-  p.smax = smax_for(m, grid);
+  p.kst = std::max(m->D, GQ * HDIM);
+  const size_t fixed = fixed_smem(p.kst, m->D, GQ, m->n_layers);
+  IRON_REQUIRE(fixed + 64 * 1024 <= (size_t)SMEM_MAX, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: %zu bytes of fixed shared memory leave no room for the weight ring", fixed);
+  p.ring = (int)(((size_t)SMEM_MAX - fixed) & ~(size_t)1023);
+  p.lm_rows = (m->lm_w8 ? 4 : 2) * NWARP;  // one pass of the lm_head row loop per chunk
+  const size_t mc = max_chunk(m, grid, p.lm_rows);
+  IRON_REQUIRE(mc <= (size_t)p.ring, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: a %zu-byte weight share exceeds the %d-byte ring (model too large for one launch)", mc,
+               p.ring);
+  const size_t smem = (size_t)p.ring + fixed;
   cudaStream_t st = (cudaStream_t)stream;
 #define IRON_STEP_CASE(g, gq) \
   if (m->group == g && GQ == gq) return launch<g, gq>(p, grid, smem, st);
-  IRON_STEP_CASE(32, 2) IRON_STEP_CASE(32, 4) IRON_STEP_CASE(32, 1) IRON_STEP_CASE(32, 8)
+  IRON_STEP_CASE(32, 2) IRON_STEP_CASE(32, 1) IRON_STEP_CASE(32, 4) IRON_STEP_CASE(32, 8)
   IRON_STEP_CASE(64, 2) IRON_STEP_CASE(64, 4) IRON_STEP_CASE(128, 2) IRON_STEP_CASE(128, 4)
 #undef IRON_STEP_CASE
   return iron_set_error(IRON_ERR_UNSUPPORTED, "qwen3 step: group %d with GQA group %d", m->group, GQ);

@@ -154,7 +154,8 @@ class Qwen3Weights:
 
 class _StepLayer(C.Structure):
     """iron_qwen3_layer (include/iron_b200.h)."""
-    _fields_ = [(n, C.c_void_p) for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd")]
+    _fields_ = [(n, C.c_void_p) for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd",
+                                          "wo_heads", "wd_cols", "wd_col_scales")]
 
 
 class _StepModel(C.Structure):
@@ -163,7 +164,7 @@ class _StepModel(C.Structure):
                 + [("eps", C.c_float)]
                 + [(n, C.c_void_p) for n in ("layers", "final_norm", "embed", "lm_w8", "angles", "kv", "x", "raw",
                                              "attn", "x1", "gh", "attn_ws", "cand", "tok", "pos", "seq_len",
-                                             "kv_off", "logits", "sync")])
+                                             "kv_off", "logits", "sync", "trace")])
 
 
 class Qwen3B200:
@@ -221,10 +222,28 @@ class Qwen3B200:
 
     def _init_step(self, dev):
         c, w = self.cfg, self.w
+        L = _lib.lib()
+        st = torch.cuda.current_stream(dev).cuda_stream
+        # the column-blocked O / down forms of the K-split projections (made once)
+        self._step_packed = []
         layers = (_StepLayer * len(w.layers))()
         for i, Lw in enumerate(w.layers):
-            for n in _StepLayer._fields_:
-                setattr(layers[i], n[0], ptr(Lw[n[0]]))
+            wo_h = torch.empty(L.iron_qwen3_pack_wo_heads_bytes(c.D, c.QD, c.Hkv, w.group), dtype=torch.uint8,
+                               device=dev)
+            abi("iron_qwen3_pack_wo_heads", ptr(Lw["wo"]), c.D, c.QD, c.Hkv, w.group, ptr(wo_h), st)
+            wd_q = torch.empty(c.FF * c.D, dtype=torch.uint8, device=dev)
+            wd_s = torch.empty((c.FF // w.group) * c.D, dtype=torch.int16, device=dev)
+            abi("iron_qwen3_pack_wd_cols", ptr(Lw["wd"]), c.D, c.FF, w.group, ptr(wd_q), ptr(wd_s), st)
+            self._step_packed.append((wo_h, wd_q, wd_s))
+            for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd"):
+                if ptr(Lw[n]) % 16:  # the kernel bulk-copies weight rows: 16-byte aligned bases
+                    raise ValueError(f"layer {i} {n}: device pointer not 16-byte aligned")
+                setattr(layers[i], n, ptr(Lw[n]))
+            layers[i].wo_heads, layers[i].wd_cols, layers[i].wd_col_scales = ptr(wo_h), ptr(wd_q), ptr(wd_s)
+        torch.cuda.current_stream(dev).synchronize()
+        for n, t in (("embed", w.embed), ("lm_head wire", w.lm_wire)):
+            if t is not None and ptr(t) % 16:
+                raise ValueError(f"{n}: device pointer not 16-byte aligned")
         self._layer_table = torch.frombuffer(bytearray(bytes(layers)), dtype=torch.uint8).to(dev)
         m = _StepModel()
         m.D, m.FF, m.Hq, m.Hkv, m.HD, m.V = c.D, c.FF, c.Hq, c.Hkv, c.HD, c.V
@@ -234,16 +253,25 @@ class Qwen3B200:
         m.lm_w8 = ptr(w.lm_wire) if self.lm_head == "int8" else None
         m.angles, m.kv = ptr(self.angles), ptr(self.kv)
         m.x, m.raw, m.attn, m.x1, m.gh = ptr(self.x), ptr(self.raw), ptr(self.attn), ptr(self.x1), ptr(self.gh)
-        L = _lib.lib()
         mp = C.byref(m)
-        self.step_ws = torch.empty(L.iron_qwen3_attn_ws_bytes(mp), dtype=torch.uint8, device=dev)
+        self.step_ws = torch.zeros(L.iron_qwen3_attn_ws_bytes(mp), dtype=torch.uint8, device=dev)
         self.cand = torch.empty(L.iron_qwen3_cand_bytes(), dtype=torch.uint8, device=dev)
         self.sync = torch.zeros(L.iron_qwen3_sync_words(mp), dtype=torch.int32, device=dev)
         m.attn_ws, m.cand = ptr(self.step_ws), ptr(self.cand)
         m.tok, m.pos, m.seq_len, m.kv_off = ptr(self.tok), ptr(self.pos), ptr(self.len), ptr(self.off)
         m.logits = ptr(self.logits) if self.logits is not None else None
         m.sync = ptr(self.sync)
+        m.trace = None
         self._model = m
+
+    def enable_trace(self) -> torch.Tensor:
+        """Step kernel only: record the hidden state entering every layer and the final
+        one, (n_layers + 1, D) bf16, on every following step (parity checks)."""
+        if self.impl != "step":
+            raise ValueError("the layer trace is recorded by the persistent step kernel")
+        self.trace = torch.zeros(len(self.w.layers) + 1, self.cfg.D, dtype=torch.bfloat16, device=self.x.device)
+        self._model.trace = ptr(self.trace)
+        return self.trace
 
     def check(self):
         """Raise if a persistent step timed out on one of its bounded waits."""

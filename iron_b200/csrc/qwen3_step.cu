@@ -607,12 +607,10 @@ __device__ void chunk_rows(const uint8_t* wb, int n, int rb, int K, const Smem& 
       if (PAIR) rp[R + i] = wb + (size_t)(n + r) * rb;
     }
     double out[NR];
-    rows_dot<G, NR, LPR>(rp, K, S, out);
-    if (sub == 0) {
+    rows_dot<G, NR, LPR>(rp, K, S, out);  // every lane of the group holds all the sums
 #pragma unroll
-      for (int i = 0; i < R; ++i)
-        if (b + rg + i * NG < n) epi(b + rg + i * NG, out[i], PAIR ? out[R + i] : 0.0);
-    }
+    for (int i = 0; i < R; ++i)  // lane i of the group finishes row i, the epilogues side by side
+      if (sub == i && b + rg + i * NG < n) epi(b + rg + i * NG, out[i], PAIR ? out[R + i] : 0.0);
   }
 }
 
@@ -1204,7 +1202,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
         if (m.lm_w8) {
           chunk_gemv<G, 32, false>(wb, n, rbh, D, S, [&](int r, double a, double) { track(r0 + r, f2bf((float)a)); });
         } else {
-          constexpr int R = 2;
+          constexpr int R = 4;
           for (int rr = wid * R; rr < n; rr += NWARP * R) {
             const uint8_t* rp[R];
 #pragma unroll
@@ -1465,7 +1463,7 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   IRON_REQUIRE(fixed + 64 * 1024 <= (size_t)SMEM_MAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: %zu bytes of fixed shared memory leave no room for the weight ring", fixed);
   p.ring = (int)(((size_t)SMEM_MAX - fixed) & ~(size_t)1023);
-  p.lm_rows = (m->lm_w8 ? 4 : 2) * NWARP;  // one pass of the lm_head row loop per chunk
+  p.lm_rows = 4 * NWARP;  // one pass of the lm_head row loop per chunk (64 KB of bf16 rows)
   const size_t mc = max_chunk(m, grid, p.lm_rows);
   IRON_REQUIRE(mc <= (size_t)p.ring, IRON_ERR_UNSUPPORTED,
                "qwen3 step: a %zu-byte weight share exceeds the %d-byte ring (model too large for one launch)", mc,

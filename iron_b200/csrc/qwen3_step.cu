@@ -58,7 +58,7 @@ constexpr int NMB = 16;          // ring slots (chunks in flight at most)
 constexpr int GMAX = 24;         // most CTAs in one KV-head group (attention splits)
 constexpr int XREP = 8;          // down-projection accumulator replicas: KV-head group h adds into
                                  // replica h % XREP (atomics to one address serialise in L2)
-constexpr int SLICE_MAX = 64;    // widest down-projection K slice of one CTA
+constexpr int SLICE_MAX = 32;    // widest down-projection K slice of one CTA
 constexpr int PIECE = 32768;     // bytes per cp.async.bulk instruction
 constexpr int SMEM_MAX = 227 * 1024;
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
@@ -113,6 +113,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+// float64 add to global memory with no value returned (the accumulators only need the sum)
+__device__ __forceinline__ void red_add(double* p, double v) {
+  asm volatile("red.global.add.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire(const int32_t* p) {
   unsigned v;
@@ -458,14 +462,14 @@ __device__ bool wait_slot(uint64_t* mb, int32_t* sync, uint32_t parity) {
 // ---------------------------------------------------------------------------
 // In place: xhi holds the bf16 bits of K values -> int16 hi words; xlo lo words;
 // xs the group factors.  Eight lanes per quant group.
-__device__ void bfp_stage(const Smem& S, int K, int G) {
+__device__ __forceinline__ void bfp_stage_p(uint16_t* xhi, uint16_t* xlo, float* xs, int K, int G) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int sub = lane >> 3, sl = lane & 7, per = G / 8;
   const int ng = K / G;
   for (int g0 = wid * 4; g0 < ng; g0 += NWARP * 4) {
     const int gi = g0 + sub;
     const bool valid = gi < ng;
-    uint16_t* base = S.xhi + (size_t)(valid ? gi : 0) * G + sl * per;
+    uint16_t* base = xhi + (size_t)(valid ? gi : 0) * G + sl * per;
     float v[16];
     float mx = 0.f;
 #pragma unroll
@@ -486,26 +490,33 @@ __device__ void bfp_stage(const Smem& S, int K, int G) {
           const float t = v[e] * sc;
           const int hi = __float2int_rn(t);
           base[e] = (uint16_t)(int16_t)hi;
-          S.xlo[(base - S.xhi) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+          xlo[(base - xhi) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
         }
-      if (sl == 0) S.xs[gi] = inv;
+      if (sl == 0) xs[gi] = inv;
     }
   }
 }
 
+__device__ __forceinline__ void bfp_stage(const Smem& S, int K, int G) { bfp_stage_p(S.xhi, S.xlo, S.xs, K, G); }
+
 // RMSNorm of the bf16 bits in `src` (shared) with the weight bits already in xlo
 // -> bf16 bits in xhi (mode 0 kernel form, 1 golden form); `outf` (shared)
 // receives the values as floats when non-null.
-__device__ void stage_norm(const Smem& S, const uint16_t* src, int K, float eps, int mode, float* outf) {
+__device__ __forceinline__ void stage_norm_p(uint16_t* xhi, const uint16_t* xlo, double* red, const uint16_t* src, int K,
+                                         float eps, int mode, float* outf) {
   double ss = 0.0;
   for (int i = threadIdx.x; i < K; i += NT) ss += rms_sq(bf2f(src[i]), mode);
-  ss = csum_d(ss, S.red);
+  ss = csum_d(ss, red);
   const RmsCoef rc = rms_coef(ss, K, eps, mode);
   for (int i = threadIdx.x; i < K; i += NT) {
-    const uint16_t o = f2bf(rms_apply(bf2f(src[i]), bf2f(S.xlo[i]), rc));
-    S.xhi[i] = o;
+    const uint16_t o = f2bf(rms_apply(bf2f(src[i]), bf2f(xlo[i]), rc));
+    xhi[i] = o;
     if (outf) outf[i] = bf2f(o);
   }
+}
+
+__device__ __forceinline__ void stage_norm(const Smem& S, const uint16_t* src, int K, float eps, int mode, float* outf) {
+  stage_norm_p(S.xhi, S.xlo, S.red, src, K, eps, mode, outf);
 }
 
 // dst[i] = bf16(src[i] + bf16(sum over the nrep replicas acc[r*D + i])) over the D
@@ -614,18 +625,10 @@ __device__ void chunk_rows(const uint8_t* wb, int n, int rb, int K, const Smem& 
   }
 }
 
-template <int G, int LPR, bool PAIR, class Epi>
-__device__ void chunk_gemv(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
-  constexpr int NG = NT / LPR;
-  const int R = (n + NG - 1) / NG;
-  if (R <= 1)
-    chunk_rows<G, 1, LPR, PAIR>(wb, n, rb, K, S, epi);
-  else if (R == 2)
-    chunk_rows<G, 2, LPR, PAIR>(wb, n, rb, K, S, epi);
-  else if (R == 3)
-    chunk_rows<G, 3, LPR, PAIR>(wb, n, rb, K, S, epi);
-  else
-    chunk_rows<G, 4, LPR, PAIR>(wb, n, rb, K, S, epi);
+// one row-block width R per call site keeps a single copy of the row loop in the kernel
+template <int G, int LPR, int R, bool PAIR, class Epi>
+__device__ __forceinline__ void chunk_gemv(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
+  chunk_rows<G, R, LPR, PAIR>(wb, n, rb, K, S, epi);
 }
 
 // bf16 rows with float32 activations: the lm_head arithmetic of gemv_bf16_kernel
@@ -1027,7 +1030,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     csync();
     STEP_MARK(layer, 2);
     ok = consume(c0 + CK_QKV, [&](const uint8_t* wb) {
-      chunk_gemv<G, 32, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
+      chunk_gemv<G, 32, 4, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
         m.raw[qkv_src_row(P.q0 + r, h, GQ, m.Hq, m.Hkv)] = f2bf((float)a);
       });
     });
@@ -1058,8 +1061,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     csync();
     STEP_MARK(layer, 7);
     ok = consume(c0 + CK_O, [&](const uint8_t* wb) {
-      chunk_gemv<G, GQ * HDIM / 16 < 32 ? GQ * HDIM / 16 : 32, false>(wb, P.o1 - P.o0, rowb_heads(GQ, G), GQ * HDIM, S,
-                               [&](int r, double a, double) { atomicAdd(oacc + P.o0 + r, a); });
+      chunk_gemv<G, GQ * HDIM / 16 < 32 ? GQ * HDIM / 16 : 32, 4, false>(wb, P.o1 - P.o0, rowb_heads(GQ, G), GQ * HDIM, S,
+                               [&](int r, double a, double) { red_add(oacc + P.o0 + r, a); });
     });
     if (!ok) break;
     STEP_MARK(layer, 8);
@@ -1078,7 +1081,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     csync();
     STEP_MARK(layer, 10);
     ok = consume(c0 + CK_GU, [&](const uint8_t* wb) {
-      chunk_gemv<G, 32, true>(wb, w, rowb(D, G), D, S, [&](int r, double g, double u) {
+      chunk_gemv<G, 32, 3, true>(wb, w, rowb(D, G), D, S, [&](int r, double g, double u) {
         S.ghv[r] = rbf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
       });
     });
@@ -1109,7 +1112,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
       const uint32_t* xl = (const uint32_t*)S.dl;
       const float inv = __int_as_float(S.flag[4]);
       // words j < jb1 belong to the slice's first scale group, j < jb2 to its second,
-      // the rest to its third (a 64-column slice touches at most three groups of 32)
+      // the rest to its third (a 32-column slice touches at most two groups of 32)
       const int nw4 = w >> 2;
       const int jb1 = (min(w, (P.ga + 1) * G - k0)) >> 2, jb2 = (min(w, (P.ga + 2) * G - k0)) >> 2;
       constexpr int RPT = 4;  // rows per thread and pass, their loads overlapped
@@ -1150,7 +1153,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
               const long long t = (long long)ah[q][e] * 32768 + al[q][e];
               a = fma((double)t, (double)(bf2f(wsc[(size_t)e * D + r]) * inv) * (1.0 / 32768.0), a);
             }
-          atomicAdd(xacc + r, a);
+          red_add(xacc + r, a);
         }
       }
     });
@@ -1200,7 +1203,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
       const int r0 = P.hlo + j * p.lm_rows, n = min(P.hhi, r0 + p.lm_rows) - r0;
       ok = consume(4 * NL + j, [&](const uint8_t* wb) {
         if (m.lm_w8) {
-          chunk_gemv<G, 32, false>(wb, n, rbh, D, S, [&](int r, double a, double) { track(r0 + r, f2bf((float)a)); });
+          chunk_gemv<G, 32, 4, false>(wb, n, rbh, D, S, [&](int r, double a, double) { track(r0 + r, f2bf((float)a)); });
         } else {
           constexpr int R = 4;
           for (int rr = wid * R; rr < n; rr += NWARP * R) {

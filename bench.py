@@ -111,6 +111,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def aggregate_replicas(t_ms, e2e_ms, steps, world, device):
+    """Whole-job numbers of ``world`` independent replicas that each decoded ``steps``
+    tokens: the slowest rank's device time (MAX all-reduce over the process group when
+    world > 1) and the tokens of all ranks over it.  Returns (t_ms, e2e_ms, tokens/s,
+    e2e tokens/s)."""
+    import torch
+    tt = torch.tensor([t_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms = float(tt[0]), float(tt[1])
+    return t_ms, e2e_ms, world * steps / (t_ms / 1000.0), world * steps / (e2e_ms / 1000.0)
+
+
 def token_bytes(cfg, group, ctx):
     """Algorithmic HBM bytes of one batch-1 decode token attending over ``ctx`` positions:
     every int8 projection wire (payload + one bf16 scale per group) once, the norm weights,
@@ -294,12 +308,7 @@ def run_ours(args, rank, world, local_rank):
     ctx0 = args.prompt + W + 1
     step_bytes = sum(token_bytes(cfg, GROUP, ctx0 + i) for i in range(K)) / K
     # ---- aggregate over ranks ----
-    tt = torch.tensor([t_ms, e2e_ms], device=dev)
-    if world > 1:
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms = float(tt[0]), float(tt[1])
-    value = world * K / (t_ms / 1000.0)
-    e2e = world * K / (e2e_ms / 1000.0)
+    t_ms, e2e_ms, value, e2e = aggregate_replicas(t_ms, e2e_ms, K, world, dev)
     if rank != 0:
         return
     from iron_b200 import _lib  # noqa: F401

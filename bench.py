@@ -36,6 +36,12 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "Qwen3 decode tokens/s"
+# DRAM traffic of one step launch beyond its algorithmic bytes, from an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum = 798.5 MB at context 71, where the
+# algorithmic bytes are 788.4 MB): accumulator zeroing, K/V and logit writes.  The
+# weights and the K/V reads scale with the algorithmic bytes, so a launch's traffic is
+# its algorithmic bytes plus this.
+STEP_TRAFFIC_EXTRA = 10.1e6
 UNIT = "tokens/s"
 PROMPT = 1024
 GROUP = 32
@@ -324,7 +330,9 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "kernel": "qwen3_step_kernel (one persistent launch per token)",
                          "bytes_per_launch": step_bytes, "achieved": achieved, "peak": peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
-                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+                         "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": step_bytes + STEP_TRAFFIC_EXTRA if dec.impl == "step" else None,
+                         "traffic_source": "ncu dram bytes of one launch at context 71, scaled by the K/V bytes"},
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "prefill_s": prefill_s}
     if world == 1 and not args.no_cpu_baseline:

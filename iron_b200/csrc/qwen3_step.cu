@@ -56,7 +56,7 @@ constexpr int NT = 256, NWARP = NT / 32;
 constexpr int HDIM = 128;        // head_dim of the step kernel
 constexpr int NMB = 16;          // ring slots (chunks in flight at most)
 constexpr int GMAX = 24;         // most CTAs in one KV-head group (attention splits)
-constexpr int XREP = 8;          // down-projection accumulator replicas: KV-head group h adds into
+constexpr int XREP = 4;          // down-projection accumulator replicas: KV-head group h adds into
                                  // replica h % XREP (atomics to one address serialise in L2)
 constexpr int SLICE_MAX = 32;    // widest down-projection K slice of one CTA
 constexpr int PIECE = 32768;     // bytes per cp.async.bulk instruction
@@ -542,6 +542,82 @@ __device__ __forceinline__ void resid_add(uint16_t* dst, const uint16_t* src, co
   }
 }
 
+// A layer-phase prologue in one pass.  With acc: x = bf16(src + bf16(sum of the NREP
+// accumulator replicas)) into dst (every load of a thread issued first); without: x is
+// dst as it stands.  Then RMSNorm(x) * w (w's bf16 bits already in xlo; mode 0 kernel
+// form, 1 golden form) goes straight into exact int16 block floating point (xhi, xlo,
+// xs), eight lanes per quant group: the arithmetic of stage_norm + bfp_stage with one
+// shared-memory pass.  outf (shared) gets the normalised values, trace (global) gets x.
+template <int G, int NREP>
+__device__ __forceinline__ void prologue(const Smem& S, uint16_t* dst, const uint16_t* src, const double* acc, int D,
+                                         float eps, int mode, float* outf, uint16_t* trace) {
+  constexpr int MAXV = 4;  // D <= 4 * NT
+  double ss = 0.0;
+  if (acc) {
+    double v[MAXV][NREP];
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      const int i = threadIdx.x + k * NT;
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) v[k][r] = i < D ? __ldcg(acc + (size_t)r * D + i) : 0.0;
+    }
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      const int i = threadIdx.x + k * NT;
+      double a = v[k][0];
+#pragma unroll
+      for (int r = 1; r < NREP; ++r) a += v[k][r];
+      if (i < D) {
+        const uint16_t x = f2bf(bf2f(src[i]) + rbf_d(a));
+        dst[i] = x;
+        ss += rms_sq(bf2f(x), mode);
+        if (trace) trace[i] = x;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += NT) {
+      ss += rms_sq(bf2f(dst[i]), mode);
+      if (trace) trace[i] = dst[i];
+    }
+  }
+  ss = csum_d(ss, S.red);  // its barriers also publish dst
+  const RmsCoef rc = rms_coef(ss, D, eps, mode);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int sub = lane >> 3, sl = lane & 7, per = G / 8;
+  const int ng = D / G;
+  for (int g0 = wid * 4; g0 < ng; g0 += NWARP * 4) {
+    const int gi = g0 + sub;
+    const bool valid = gi < ng;
+    const int base = (valid ? gi : 0) * G + sl * per;
+    float v[16];
+    float mx = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (e < per) {
+        v[e] = valid ? bf2f(f2bf(rms_apply(bf2f(dst[base + e]), bf2f(S.xlo[base + e]), rc))) : 0.f;
+        mx = fmaxf(mx, fabsf(v[e]));
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    float sc, inv;
+    bfp_scale(mx, sc, inv);
+    if (valid) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (e < per) {
+          if (outf) outf[base + e] = v[e];
+          const float t = v[e] * sc;
+          const int hi = __float2int_rn(t);
+          S.xhi[base + e] = (uint16_t)(int16_t)hi;
+          S.xlo[base + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
+        }
+      if (sl == 0) S.xs[gi] = inv;
+    }
+  }
+  csync();
+}
+
 // K bf16 values (K % 8 == 0, read-only data) into shared memory with 16-byte loads
 __device__ __forceinline__ void load_ro(uint16_t* dst, const uint16_t* src, int K) {
   for (int i = threadIdx.x; i < (K >> 3); i += NT) ((uint4*)dst)[i] = __ldg(((const uint4*)src) + i);
@@ -971,6 +1047,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   // layer-0 input: the token's embedding row, or the hidden state given in x
   load_ro(S.sx, p.embed_input ? m.embed + (size_t)m.tok[0] * D : m.x, D);
   load_ro(S.xlo, S.lay[0].norm1, D);
+  csync();  // the prologue reads these rows across threads
 
   bool ok = true;
   // consume chunk i: fn(buffer) once its copy landed, then release its space
@@ -1017,17 +1094,11 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     if (layer > 0) {
       if (!(ok = wait(SYNC_B1, (unsigned)layer * N))) break;
       STEP_MARK(layer, 1);
-      resid_add<XREP>(S.sx, S.sx1, acc + (size_t)(layer - 1) * lstride + D, D);
     }
-    csync();
+    prologue<G, XREP>(S, S.sx, S.sx1, layer > 0 ? acc + (size_t)(layer - 1) * lstride + D : nullptr, D, m.eps, 1,
+                      nullptr, (m.trace && blockIdx.x == 0) ? m.trace + (size_t)layer * D : nullptr);
     STEP_MARK(layer, 24);
-    if (m.trace && blockIdx.x == 0)
-      for (int i = tid; i < D; i += NT) m.trace[(size_t)layer * D + i] = S.sx[i];
-    stage_norm(S, S.sx, D, m.eps, 1, nullptr);
-    csync();
     STEP_MARK(layer, 25);
-    bfp_stage(S, D, G);
-    csync();
     STEP_MARK(layer, 2);
     ok = consume(c0 + CK_QKV, [&](const uint8_t* wb) {
       chunk_gemv<G, 32, 4, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
@@ -1072,13 +1143,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 9);
     // ---- gate/up: x1 = bf16(x + bf16(O)), hf = RMSNorm_kernel(x1, norm2),
     //      gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for this CTA's slice ----
-    resid_add<1>(S.sx1, S.sx, oacc, D);
-    csync();
+    prologue<G, 1>(S, S.sx1, S.sx, oacc, D, m.eps, 0, nullptr, nullptr);
     STEP_MARK(layer, 26);
-    stage_norm(S, S.sx1, D, m.eps, 0, nullptr);
-    csync();
-    bfp_stage(S, D, G);
-    csync();
     STEP_MARK(layer, 10);
     ok = consume(c0 + CK_GU, [&](const uint8_t* wb) {
       chunk_gemv<G, 32, 3, true>(wb, w, rowb(D, G), D, S, [&](int r, double g, double u) {
@@ -1169,18 +1235,10 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   STEP_CLK(NL, 29);
   if (ok) {
     // ---- final: x = bf16(x1 + bf16(down)), RMSNorm (golden) + lm_head + greedy argmax ----
-    resid_add<XREP>(S.sx, S.sx1, acc + (size_t)(NL - 1) * lstride + D, D);
-    for (int i = tid; i < D; i += NT) {
-      if (blockIdx.x == 0) {
-        m.x[i] = S.sx[i];
-        if (m.trace) m.trace[(size_t)NL * D + i] = S.sx[i];
-      }
-    }
-    csync();
-    stage_norm(S, S.sx, D, m.eps, 1, S.xf);
-    csync();
-    if (m.lm_w8) bfp_stage(S, D, G);
-    csync();
+    prologue<G, XREP>(S, S.sx, S.sx1, acc + (size_t)(NL - 1) * lstride + D, D, m.eps, 1, S.xf,
+                      blockIdx.x == 0 ? m.x : nullptr);
+    if (m.trace && blockIdx.x == 0)
+      for (int i = tid; i < D; i += NT) m.trace[(size_t)NL * D + i] = S.sx[i];
     const int lane = tid & 31, wid = tid >> 5;
     float bv = -INFINITY;
     int bi = 0x7fffffff;

@@ -29,13 +29,13 @@ ROWS = 64    # layer rows per CTA
 
 # (label, first mark, second mark, from layer): the phase is the time between them
 SPANS = [
-    ("wait for the down sums (B1)", 0, 1, 1), ("residual + accumulator loads", 1, 24, 1),
-    ("QKV RMSNorm", 24, 25, 1), ("QKV BFP staging", 25, 2, 1), ("QKV weights wait", 2, 16, 0),
+    ("wait for the down sums (B1)", 0, 1, 1), ("residual + RMSNorm + BFP staging", 1, 2, 1),
+    ("QKV weights wait", 2, 16, 0),
     ("QKV GEMV", 16, 20, 0), ("QKV slot release", 20, 3, 0), ("group barrier after QKV", 3, 4, 0),
     ("q/k norm + RoPE + v", 4, 14, 0), ("attention split", 14, 5, 0), ("group barrier after splits", 5, 6, 0),
     ("split merge (bulk copy)", 6, 15, 0), ("merged-head BFP staging", 15, 7, 0), ("O weights wait", 7, 17, 0),
     ("O GEMV (K split by head)", 17, 21, 0), ("O slot release", 21, 8, 0), ("grid barrier after O (B2)", 8, 9, 0),
-    ("x1 = x + O sums", 9, 26, 0), ("MLP RMSNorm + BFP", 26, 10, 0), ("gate/up weights wait", 10, 18, 0),
+    ("x1 = x + O sums, RMSNorm, BFP", 9, 10, 0), ("gate/up weights wait", 10, 18, 0),
     ("gate/up GEMV + SiLU*mul", 18, 22, 0), ("gate/up slot release", 22, 11, 0), ("down slice BFP", 11, 12, 0),
     ("down weights wait", 12, 19, 0), ("down GEMV (K slice) + reductions", 19, 23, 0),
     ("down slot release", 23, 13, 0),

@@ -64,7 +64,7 @@ constexpr int SMEM_MAX = 227 * 1024;
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
 
 // sync words (the G2 counters follow the Hkv G1 counters)
-enum { SYNC_B1 = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_B2 = 3, SYNC_PARITY = 4, SYNC_G1 = 8 };
+enum { SYNC_B1 = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_B2 = 3, SYNC_PARITY = 4, SYNC_EPOCH = 5, SYNC_G1 = 8 };
 enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_INPUT = 3 };
 // chunk kinds of a layer, in stream order; the lm_head chunks follow the last layer
 enum { CK_QKV = 0, CK_O = 1, CK_GU = 2, CK_D = 3 };
@@ -118,6 +118,46 @@ __device__ __forceinline__ unsigned long long gtimer() {
 __device__ __forceinline__ void red_add(double* p, double v) {
   asm volatile("red.global.add.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
 }
+__device__ __forceinline__ unsigned ld_relaxed(const int32_t* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Flagged words: (epoch << 32 | data) written by one 64-bit store, so a reader that
+// finds the epoch it waits for also has the data; no fence, counter or poll of a
+// separate word sits between producer and consumer.  Every word is rewritten each
+// token with a larger epoch; the buffers are zeroed with the sync words.
+__device__ __forceinline__ void ll_put(unsigned long long* p, uint32_t data, uint32_t epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | data;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_ld(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// the data of word p once it carries `epoch` (bounded: on timeout or a set error word
+// *bad is set and 0 returned)
+__device__ __forceinline__ uint32_t ll_get(const unsigned long long* p, uint32_t epoch, int32_t* sync, int& bad) {
+  unsigned long long w = ll_ld(p);
+  if ((uint32_t)(w >> 32) == epoch) return (uint32_t)w;
+  const unsigned long long t0 = gtimer();
+  for (unsigned it = 0;; ++it) {
+    w = ll_ld(p);
+    if ((uint32_t)(w >> 32) == epoch) return (uint32_t)w;
+    if ((it & 15) == 15) {
+      if (ld_relaxed(&sync[SYNC_ERR]) != 0) break;
+      if (gtimer() - t0 > TIMEOUT_NS) {
+        atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_BARRIER);
+        break;
+      }
+    }
+  }
+  bad = 1;
+  return 0;
+}
+
 __device__ __forceinline__ unsigned ld_acquire(const int32_t* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -772,8 +812,11 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 // attention: KV head h, split s of ns over the positions; writes the split's
 // partial (o, m, l) per query head to the workspace slot [h][s]
 // ---------------------------------------------------------------------------
+// raw: the flagged q/k/v words of this layer (epoch `ep`); returns false when a wait
+// for them gave up
 template <int GQ>
-__device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P) {
+__device__ bool attention_split(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P,
+                                const unsigned long long* raw, uint32_t ep) {
   const iron_qwen3_model& m = p.m;
   constexpr int PER = HDIM / 32;
   constexpr int U = 4;
@@ -788,11 +831,32 @@ __device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, in
   uint16_t* head = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
   const uint16_t* ang = m.angles + (size_t)P * HDIM;
   const bool owner = P >= start && P < end;
+  // the first K/V positions do not depend on q/k: their loads go out before the norms
+  auto load = [&](int j0, uint2 (&kk)[U], uint2 (&vv)[U]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = min(j0 + u, end - 1);
+      if (j != P) {
+        const uint16_t* kr = head + (size_t)j * 2 * HDIM + lane * PER;
+        kk[u] = ldg_stream8(kr);
+        vv[u] = ldg_stream8(kr + HDIM);
+      }
+    }
+  };
+  uint2 kc[U], vc[U], kn[U], vn[U];
+  int j0 = start + wid * U;
+  if (j0 < end) load(j0, kc, vc);
   // per-head q/k RMSNorm (golden form) + RoPE and the v copy: qk_norm_rope_kv_kernel's arithmetic
+  int bad = 0;
+  if (threadIdx.x == 0) S.flag[6] = 0;
+  csync();
   for (int t = wid; t < GQ + 2; t += NWARP) {
     if (t == GQ + 1) {
-      const uint16_t* vs = m.raw + (size_t)(m.Hq + m.Hkv + h) * HDIM;
-      const uint2 v = __ldcg(((const uint2*)vs) + lane);
+      const unsigned long long* vs = raw + (size_t)(m.Hq + m.Hkv + h) * HDIM + lane * 4;
+      uint32_t b[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) b[e] = ll_get(vs + e, ep, m.sync, bad);
+      const uint2 v = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
       vt[lane * 4 + 0] = bf_lo(v.x);
       vt[lane * 4 + 1] = bf_hi(v.x);
       vt[lane * 4 + 2] = bf_lo(v.y);
@@ -802,14 +866,14 @@ __device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, in
     }
     const bool isq = t < GQ;
     const int hh = isq ? h * GQ + t : m.Hq + h;
-    const uint16_t* src = m.raw + (size_t)hh * HDIM;
+    const unsigned long long* src = raw + (size_t)hh * HDIM;
     const uint16_t* nw = isq ? S.lay[layer].qn : S.lay[layer].kn;
     float v[PER], wv[PER], cs[PER], sn[PER];
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
       const int i = lane + 32 * j;
-      v[2 * j] = bf2f(__ldcg(src + i));
-      v[2 * j + 1] = bf2f(__ldcg(src + i + HDIM / 2));
+      v[2 * j] = bf2f(ll_get(src + i, ep, m.sync, bad));
+      v[2 * j + 1] = bf2f(ll_get(src + i + HDIM / 2, ep, m.sync, bad));
       wv[2 * j] = bf2f(__ldg(nw + i));
       wv[2 * j + 1] = bf2f(__ldg(nw + i + HDIM / 2));
       cs[j] = bf2f(__ldg(ang + 2 * i));
@@ -836,7 +900,9 @@ __device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, in
       }
     }
   }
+  if (bad) S.flag[6] = 1;
   csync();
+  if (S.flag[6]) return false;
   STEP_MARK(layer, 14);
   // flash decoding over [start, end): the online softmax of attn_split_kernel, with the
   // next group of positions loaded while the current one is reduced
@@ -854,20 +920,6 @@ __device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, in
 #pragma unroll
     for (int e = 0; e < PER; ++e) o[g][e] = 0.f;
   }
-  auto load = [&](int j0, uint2 (&kk)[U], uint2 (&vv)[U]) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = min(j0 + u, end - 1);
-      if (j != P) {
-        const uint16_t* kr = head + (size_t)j * 2 * HDIM + lane * PER;
-        kk[u] = ldg_stream8(kr);
-        vv[u] = ldg_stream8(kr + HDIM);
-      }
-    }
-  };
-  uint2 kc[U], vc[U], kn[U], vn[U];
-  int j0 = start + wid * U;
-  if (j0 < end) load(j0, kc, vc);
   for (; j0 < end; j0 += NWARP * U) {
     const int jn = j0 + NWARP * U;
     if (jn < end) load(jn, kn, vn);
@@ -958,6 +1010,7 @@ __device__ void attention_split(const Kp& p, const Smem& S, int layer, int h, in
       ws[g * (HDIM + 2) + HDIM + 1] = lsum;
     }
   }
+  return true;
 }
 
 // Merge the ns split partials of KV head h (attn_combine_kernel's arithmetic) into
@@ -1023,9 +1076,12 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   // projection accumulators: two sets of [NL][O, down][D] float64 that alternate by
   // token; this token zeroes the other set for the next one
   const int parity = __ldcg((const int*)&sync[SYNC_PARITY]) & 1;
+  const uint32_t tok_epoch = (uint32_t)__ldcg((const int*)&sync[SYNC_EPOCH]);
   double* acc_base = (double*)((uint8_t*)m.attn_ws + (size_t)m.Hkv * GMAX * GQ * (HDIM + 2) * 4);
   const size_t lstride = (size_t)(1 + XREP) * D;  // accumulator doubles per layer
   double* acc = acc_base + (size_t)parity * NL * lstride;
+  // flagged q/k/v words of the current layer, after the accumulators
+  unsigned long long* raw_ll = (unsigned long long*)(acc_base + (size_t)2 * NL * lstride);
   if (tid < NT) {
     double* other = acc_base + (size_t)(parity ^ 1) * NL * lstride;
     for (size_t i = (size_t)blockIdx.x * NT + tid; i < NL * lstride; i += (size_t)N * NT) other[i] = 0.0;
@@ -1088,6 +1144,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     double* oacc = acc + (size_t)layer * lstride;
     double* xacc = oacc + (size_t)D * (1 + h % XREP);  // this KV-head group's replica
     const int c0 = 4 * layer;
+    const uint32_t ep = tok_epoch * (uint32_t)NL + (uint32_t)layer + 1u;  // this layer's flag value
     STEP_MARK(layer, 0);
     STEP_CLK(layer, 28);
     // ---- QKV: x = bf16(x1 + bf16(down)), hn = RMSNorm_golden(x, norm1), raw = bf16(Wqkv @ hn) ----
@@ -1102,7 +1159,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 2);
     ok = consume(c0 + CK_QKV, [&](const uint8_t* wb) {
       chunk_gemv<G, 32, 4, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
-        m.raw[qkv_src_row(P.q0 + r, h, GQ, m.Hq, m.Hkv)] = f2bf((float)a);
+        ll_put(raw_ll + qkv_src_row(P.q0 + r, h, GQ, m.Hq, m.Hkv), f2bf((float)a), ep);
       });
     });
     if (!ok) break;
@@ -1115,11 +1172,9 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
         prefetch_l2(hb + (size_t)st * 2 * HDIM, (uint32_t)(en - st) * 4 * HDIM);
       }
     }
-    arrive(SYNC_G1 + h);
-    if (!(ok = wait(SYNC_G1 + h, (unsigned)(layer + 1) * gsz))) break;
     STEP_MARK(layer, 4);
-    // ---- attention: KV head h, split gi of gsz ----
-    attention_split<GQ>(p, S, layer, h, P.gi, gsz, pos);
+    // ---- attention: KV head h, split gi of gsz (its q/k/v rows arrive as flagged words) ----
+    if (!(ok = attention_split<GQ>(p, S, layer, h, P.gi, gsz, pos, raw_ll, ep))) break;
     STEP_MARK(layer, 5);
     arrive(SYNC_G1 + m.Hkv + h);
     if (!(ok = wait(SYNC_G1 + m.Hkv + h, (unsigned)(layer + 1) * gsz))) break;
@@ -1330,6 +1385,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
           for (int k = 0; k < 2 * m.Hkv; ++k) sync[SYNC_G1 + k] = 0;
           sync[SYNC_ARGMAX] = 0;
           sync[SYNC_PARITY] = parity ^ 1;
+          sync[SYNC_EPOCH] = (int)(tok_epoch + 1u);
           __threadfence();
         }
       }
@@ -1441,7 +1497,7 @@ static int validate(const iron_qwen3_model* m, int grid) {
                "qwen3 step: down-projection slice wider than %d columns", SLICE_MAX);
   IRON_REQUIRE(m->D <= 4 * NT, IRON_ERR_UNSUPPORTED, "qwen3 step: hidden size %d above %d", m->D, 4 * NT);
   IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
-  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->raw && m->attn_ws &&
+  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->attn_ws &&
                    m->cand && m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
                IRON_ERR_ARG, "qwen3 step: null buffer in the model descriptor");
   return IRON_OK;
@@ -1466,17 +1522,19 @@ static int64_t partial_bytes(const iron_qwen3_model* m) {
   return (int64_t)m->Hkv * GMAX * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
 }
 static int64_t acc_bytes(const iron_qwen3_model* m) { return (int64_t)2 * m->n_layers * (1 + XREP) * m->D * 8; }
+static int64_t raw_ll_bytes(const iron_qwen3_model* m) { return (int64_t)(m->Hq + 2 * m->Hkv) * HDIM * 8; }
 
 extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
   if (!m || m->Hkv < 1 || m->Hq % m->Hkv != 0) return 0;
-  return partial_bytes(m) + acc_bytes(m);
+  return partial_bytes(m) + acc_bytes(m) + raw_ll_bytes(m);
 }
 
 extern "C" int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream) {
   IRON_REQUIRE(m && m->sync && m->attn_ws, IRON_ERR_ARG, "qwen3 sync reset: null");
   cudaError_t e = cudaMemsetAsync(m->sync, 0, (size_t)iron_qwen3_sync_words(m) * 4, (cudaStream_t)stream);
   if (e == cudaSuccess)
-    e = cudaMemsetAsync((uint8_t*)m->attn_ws + partial_bytes(m), 0, (size_t)acc_bytes(m), (cudaStream_t)stream);
+    e = cudaMemsetAsync((uint8_t*)m->attn_ws + partial_bytes(m), 0, (size_t)(acc_bytes(m) + raw_ll_bytes(m)),
+                        (cudaStream_t)stream);
   if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 sync reset: %s", cudaGetErrorString(e));
   return IRON_OK;
 }

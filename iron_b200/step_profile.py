@@ -7,7 +7,9 @@ product library is untouched), decodes a synthetic Qwen3-0.6B int8-g32 model to
 thread 0 of every CTA stores ``%globaltimer`` at fixed points of each layer
 (``STEP_MARK`` in ``csrc/qwen3_step.cu``); this module turns the stamps into
 microseconds per token for each phase, summed over the layers: the mean over CTAs,
-the slowest CTA, and the mean over layers of the slowest CTA.
+the slowest CTA, and per layer (mean over layers) the slowest and the fastest CTA.
+For a barrier wait the fastest CTA is the last to arrive: its wait is the barrier's
+own latency, the rest is skew.
 
 The stamps cost a global store per mark on one thread; the step time with and
 without them is printed for comparison.
@@ -108,20 +110,22 @@ def main():
         lay = t[:, :NL]
         for name, a, b, first in SPANS:
             v = (lay[:, first:, b] - lay[:, first:, a]) / 1000.0
-            acc.setdefault(name, []).append((v.sum(1).mean(), v.sum(1).max(), v.max(0).mean()))
+            acc.setdefault(name, []).append((v.sum(1).mean(), v.sum(1).max(), v.max(0).mean(), v.min(0).mean()))
         tail = (lay[:, 1:, 0] - lay[:, :-1, 13]) / 1000.0
-        acc.setdefault("layer tail (arrive B1)", []).append((tail.sum(1).mean(), tail.sum(1).max(), tail.max(0).mean()))
+        acc.setdefault("layer tail (arrive B1)", []).append((tail.sum(1).mean(), tail.sum(1).max(), tail.max(0).mean(),
+                                                            tail.min(0).mean()))
         fin = t[:, NL]
         lm = (fin[:, 2] - fin[:, 1]) / 1000.0
-        acc.setdefault("final norm + lm_head + argmax", []).append((lm.mean(), lm.max(), lm.max()))
+        acc.setdefault("final norm + lm_head + argmax", []).append((lm.mean(), lm.max(), lm.max(), lm.min()))
         totals.append((fin[:, 2].max() - t[:, 0, 0].min()) / 1000.0)
     lib.iron_qwen3_step_profile_buffer(C.c_void_p(0))
     print(f"step time without stamps: {plain_ms * 1000:.1f} us; with stamps (first to last stamp): "
           f"{np.mean(totals):.1f} us; context {args.prompt} positions; {n_cta} CTAs")
-    print(f"{'phase':34s} {'mean/CTA':>9s} {'max/CTA':>9s} {'per layer':>10s}   (us per token, summed over layers)")
+    print(f"{'phase':34s} {'mean/CTA':>9s} {'max/CTA':>9s} {'per layer':>10s} {'fastest':>8s}"
+          "   (us per token summed over layers; per layer: slowest and fastest CTA)")
     for name, vals in acc.items():
         m = np.mean(np.array(vals), axis=0)
-        print(f"{name:34s} {m[0]:9.1f} {m[1]:9.1f} {m[2]:10.2f}")
+        print(f"{name:34s} {m[0]:9.1f} {m[1]:9.1f} {m[2]:10.2f} {m[3]:8.2f}")
 
 
 def _build_grid(lib, mp) -> int:

@@ -55,15 +55,18 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--batch", type=int, default=1,
+                    help="independent decode streams per GPU (1: the one-launch step; more: the chained "
+                         "kernels as a CUDA graph)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
     return ap.parse_args()
 
 
 def workload(args):
-    return {"workload": f"qwen3-0.6b int8-g{GROUP} greedy decode, batch 1, bf16 tied lm_head, "
-                        f"{args.prompt}-token random prompt prefilled",
-            "batch": 1, "layers": 28, "vocab": 151936, "group": GROUP, "prompt_tokens": args.prompt,
+    return {"workload": f"qwen3-0.6b int8-g{GROUP} greedy decode, batch {args.batch}, bf16 tied lm_head, "
+                        f"{args.prompt}-token random prompt{'s' if args.batch > 1 else ''} prefilled",
+            "batch": args.batch, "layers": 28, "vocab": 151936, "group": GROUP, "prompt_tokens": args.prompt,
             "l2": "no flush: ~0.78 GB of weights streamed per step, larger than the 126 MB L2",
             "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
 
@@ -131,21 +134,22 @@ def aggregate_replicas(t_ms, e2e_ms, steps, world, device):
     return t_ms, e2e_ms, world * steps / (t_ms / 1000.0), world * steps / (e2e_ms / 1000.0)
 
 
-def token_bytes(cfg, group, ctx):
-    """Algorithmic HBM bytes of one batch-1 decode token attending over ``ctx`` positions:
-    every int8 projection wire (payload + one bf16 scale per group) once, the norm weights,
-    the bf16 tied lm_head once, the embedding row, K/V of all ``ctx`` positions read and the
-    new position's K/V written, plus the activations in and out of each GEMV."""
+def token_bytes(cfg, group, ctx, batch=1):
+    """Algorithmic HBM bytes of one decode step of ``batch`` streams attending over ``ctx``
+    positions each: every int8 projection wire (payload + one bf16 scale per group) and the
+    norm weights once, the bf16 tied lm_head once; per stream the embedding row, K/V of all
+    ``ctx`` positions read and the new position's K/V written, plus the activations in and
+    out of each GEMV."""
     D, FF, HD = cfg.D, cfg.FF, cfg.HD
     QD, QKV = cfg.Hq * HD, (cfg.Hq + 2 * cfg.Hkv) * HD
     wire = lambda M, K: M * K + M * (K // group) * 2
     per_layer = (wire(QKV, D) + wire(D, QD) + 2 * wire(FF, D) + wire(D, FF)
-                 + (2 * D + 2 * HD) * 2                         # norm weights
-                 + 2 * cfg.Hkv * HD * 2 * ctx                   # K/V read
-                 + 2 * cfg.Hkv * HD * 2                         # K/V write
-                 + (D + QKV + QD + D + D + 2 * FF + FF + D) * 2)  # GEMV activations in/out
-    head = cfg.V * D * 2 + D * 2 + D * 2 + 4                   # lm_head, final norm, x, token
-    return cfg.n_layers * per_layer + head + D * 2
+                 + (2 * D + 2 * HD) * 2                                   # norm weights
+                 + batch * (2 * cfg.Hkv * HD * 2 * ctx                    # K/V read
+                            + 2 * cfg.Hkv * HD * 2                        # K/V write
+                            + (D + QKV + QD + D + D + 2 * FF + FF + D) * 2))  # GEMV activations
+    head = cfg.V * D * 2 + D * 2 + batch * (D * 2 + 4)                   # lm_head, final norm, x, token
+    return cfg.n_layers * per_layer + head + batch * D * 2
 
 
 # ---------------------------------------------------------------------------
@@ -257,9 +261,10 @@ def run_ours(args, rank, world, local_rank):
     K, W = args.steps, args.warmup
     max_seq = (args.prompt + W + 2 * K + 8 + 63) // 64 * 64
     w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
-    dec = Qwen3B200(w, max_seq=max_seq, device=dev)
+    B = args.batch
+    dec = Qwen3B200(w, max_seq=max_seq, batch=B, device=dev)
     g = torch.Generator().manual_seed(args.seed + 1000 * rank)
-    prompt = torch.randint(0, cfg.V, (args.prompt,), generator=g).tolist()
+    prompts = torch.randint(0, cfg.V, (B, args.prompt), generator=g).tolist()
 
     def barrier():
         if world > 1:
@@ -270,8 +275,8 @@ def run_ours(args, rank, world, local_rank):
     clocks.start()
     # prefill, token by token through the decode step (qwen3_0.6b/check_cosine_int8.py:51-52)
     t_pre = time.perf_counter()
-    for p, t in enumerate(prompt):
-        nxt = dec.step_tokens([t], p)
+    for p in range(args.prompt):
+        nxt = dec.step_tokens([prompts[b][p] for b in range(B)], p)
     prefill_s = time.perf_counter() - t_pre
     pos = args.prompt
     dec.set_position(pos)
@@ -293,16 +298,17 @@ def run_ours(args, rank, world, local_rank):
     pos += K
     t_ms = e0.elapsed_time(e1)
     # ---- e2e: public API per step (H2D token+position, D2H token) ----
-    tok = int(dec.tok[0])
+    toks = [int(t) for t in dec.tok.cpu()]
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e2.record(dec.stream)
-    last_in, last_pos = tok, pos
+    last_in, last_pos = toks[0], pos
     for _ in range(K):
-        last_in, last_pos = tok, pos
-        tok = int(dec.step_tokens([tok], pos)[0])
+        last_in, last_pos = toks[0], pos
+        toks = [int(t) for t in dec.step_tokens(toks, pos)]
         pos += 1
+    tok = toks[0]
     e3.record(dec.stream)
     torch.cuda.synchronize()
     barrier()
@@ -312,9 +318,9 @@ def run_ours(args, rank, world, local_rank):
     # ---- dominant kernel: the persistent step kernel (the only launch of a step) ----
     # algorithmic bytes of the timed steps, averaged over their attention lengths
     ctx0 = args.prompt + W + 1
-    step_bytes = sum(token_bytes(cfg, GROUP, ctx0 + i) for i in range(K)) / K
+    step_bytes = sum(token_bytes(cfg, GROUP, ctx0 + i, B) for i in range(K)) / K
     # ---- aggregate over ranks ----
-    t_ms, e2e_ms, value, e2e = aggregate_replicas(t_ms, e2e_ms, K, world, dev)
+    t_ms, e2e_ms, value, e2e = aggregate_replicas(t_ms, e2e_ms, K * B, world, dev)
     if rank != 0:
         return
     from iron_b200 import _lib  # noqa: F401
@@ -324,10 +330,12 @@ def run_ours(args, rank, world, local_rank):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xbf16", "data": "synthetic", "config": workload(args),
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 8 if dec.impl == "step" else 4},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": (8 if dec.impl == "step" else 4) * B},
             "gpu_launches": K * dec.launches_per_step(),
-            "roofline": {"bound": "hbm", "kernel": "qwen3_step_kernel (one persistent launch per token)",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("qwen3_step_kernel (one persistent launch per token)" if dec.impl == "step"
+                                    else f"the chained kernels of one step ({dec.launches_per_step()} launches)"),
                          "bytes_per_launch": step_bytes, "achieved": achieved, "peak": peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
                          "unit": "GB/s", "frac": achieved / peak,
@@ -338,7 +346,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.no_cpu_baseline:
         from oracle.qwen3 import Qwen3Shape
         wnp = w.to_numpy()
-        kvnp = dec.kv.float().cpu().numpy().reshape(cfg.n_layers, cfg.Hkv, max_seq, 2, cfg.HD)
+        kvnp = dec.kv[:, 0].float().cpu().numpy().reshape(cfg.n_layers, cfg.Hkv, max_seq, 2, cfg.HD)
         threads = len(os.sched_getaffinity(0))
         # the oracle reproduces the GPU's last token from the same state (parity spot check)
         ptok = last_pos
@@ -346,7 +354,8 @@ def run_ours(args, rank, world, local_rank):
                                        args.cpu_tokens, threads, angles=dec.angles.float().cpu().numpy())
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": used, "kind": "port",
                                 "sample": f"{args.cpu_tokens} full decode tokens (28 layers + bf16 lm_head) of "
-                                          f"the numpy oracle at position {ptok} on this run's weights and KV cache"}
+                                          f"the numpy oracle at position {ptok} on this run's weights and KV cache"
+                                          + (" (stream 0 of the batch)" if B > 1 else "")}
         import numpy as np
         line["oracle_spot_check"] = {"position": ptok, "input_token": last_in,
                                      "gpu_token": tok, "oracle_token": int(np.argmax(logits))}

@@ -51,7 +51,8 @@ int iron_last_error(char* buf, int buflen);
  * y[b, m] = bf16( r[b, m] + bf16(sum ...) )                          (epilogue 1, residual)
  * Replaces GEMVInt8 (iron/operators/gemv_int8/op.py:20-178), kernel
  * matvec_vectorized_int8_bf16 (aie_kernels/aie2p/mv_int8_signed.cc:103-115,
- * biased: mv_int8.cc:60-114).  batch: 1..8 activation rows sharing the weight.
+ * biased: mv_int8.cc:60-114).  batch: activation rows sharing the weight (above 8 they run in
+ * launches of 8 rows, each streaming the weight).
  * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.
  */
 int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,

@@ -300,38 +300,51 @@ extern "C" int64_t iron_argmax_workspace_bytes(int batch) {
 
 extern "C" int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
                               int independent, uint16_t* y, void* stream) {
-  GemvBf16Params p = {};
-  p.A = A;
-  p.M = M;
-  p.K = K;
-  p.x = x;
-  p.nb = batch;
-  p.independent = independent;
-  p.y = y;
   IRON_REQUIRE(y != nullptr, IRON_ERR_ARG, "gemv_bf16: null output");
-  int g = gemv_bf16_dispatch(p, (cudaStream_t)stream);
-  return g < 0 ? g : IRON_OK;
+  IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "gemv_bf16: batch %d below 1", batch);
+  // a shared weight with more than 8 activation rows: launches over 8 rows each
+  const int step = independent ? batch : 8;
+  for (int b0 = 0; b0 < batch; b0 += step) {
+    GemvBf16Params p = {};
+    p.A = A;
+    p.M = M;
+    p.K = K;
+    p.x = x + (size_t)b0 * K;
+    p.nb = batch - b0 < step ? batch - b0 : step;
+    p.independent = independent;
+    p.y = y + (size_t)b0 * M;
+    int g = gemv_bf16_dispatch(p, (cudaStream_t)stream);
+    if (g < 0) return g;
+  }
+  return IRON_OK;
 }
 
 extern "C" int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const uint16_t* x,
                                         int batch, uint16_t* logits, int32_t* token_out,
                                         void* workspace, void* stream) {
   IRON_REQUIRE(workspace && token_out, IRON_ERR_ARG, "lm_head_argmax: null workspace/token_out");
-  IRON_REQUIRE(batch >= 1 && batch <= 8, IRON_ERR_UNSUPPORTED, "lm_head_argmax: batch %d not in 1..8", batch);
-  GemvBf16Params p = {};
-  p.A = A;
-  p.M = M;
-  p.K = K;
-  p.x = x;
-  p.nb = batch;
-  p.y = logits;
-  p.cand_val = (float*)workspace;
-  p.cand_idx = (int*)((char*)workspace + (size_t)batch * kMaxCand * 4);
+  IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "lm_head_argmax: batch %d below 1", batch);
   cudaStream_t st = (cudaStream_t)stream;
-  int grid = gemv_bf16_dispatch(p, st);
-  if (grid < 0) return grid;
-  argmax_reduce_kernel<<<batch, 256, 0, st>>>(p.cand_val, p.cand_idx, grid, token_out);
-  return iron_check_launch("argmax_reduce_kernel");
+  // up to 8 activation rows per launch; rows b0.. use the workspace's candidate slots
+  // from b0 * kMaxCand on
+  for (int b0 = 0; b0 < batch; b0 += 8) {
+    const int nb = batch - b0 < 8 ? batch - b0 : 8;
+    GemvBf16Params p = {};
+    p.A = A;
+    p.M = M;
+    p.K = K;
+    p.x = x + (size_t)b0 * K;
+    p.nb = nb;
+    p.y = logits ? logits + (size_t)b0 * M : nullptr;
+    p.cand_val = (float*)workspace + (size_t)b0 * kMaxCand;
+    p.cand_idx = (int*)((char*)workspace + (size_t)batch * kMaxCand * 4) + (size_t)b0 * kMaxCand;
+    int grid = gemv_bf16_dispatch(p, st);
+    if (grid < 0) return grid;
+    argmax_reduce_kernel<<<nb, 256, 0, st>>>(p.cand_val, p.cand_idx, grid, token_out + b0);
+    int rc = iron_check_launch("argmax_reduce_kernel");
+    if (rc) return rc;
+  }
+  return IRON_OK;
 }
 
 extern "C" int iron_argmax_bf16(const uint16_t* logits, int M, int batch, int32_t* token_out,

@@ -259,7 +259,27 @@ int make_wire(Wire& w, const void* base, int M, int K, int group, int tile_m, in
   return IRON_OK;
 }
 
+static int gemv_w8_launch_rows(GemvW8Params p, bool pair, cudaStream_t st);
+int gemv_stream_launch(const GemvW8Params& p, bool pair, cudaStream_t st);
+
+// Batches above 8 run as successive launches over 8 activation rows each (the weight
+// streams once per launch): the batch-8 kernel's arithmetic for every row.
 int gemv_w8_launch(GemvW8Params p, bool pair, cudaStream_t st) {
+  IRON_REQUIRE(p.nb >= 1, IRON_ERR_UNSUPPORTED, "gemv_w8: batch %d below 1", p.nb);
+  if (p.nb <= 8) return gemv_w8_launch_rows(p, pair, st);
+  for (int b0 = 0; b0 < p.nb; b0 += 8) {
+    GemvW8Params q = p;
+    q.nb = p.nb - b0 < 8 ? p.nb - b0 : 8;
+    q.x = p.x + (size_t)b0 * p.ld_x;
+    q.res = p.res ? p.res + (size_t)b0 * p.ld_y : nullptr;
+    q.y = p.epi == EPI_F32 ? (uint16_t*)((float*)p.y + (size_t)b0 * p.ld_y) : p.y + (size_t)b0 * p.ld_y;
+    const int rc = gemv_w8_launch_rows(q, pair, st);
+    if (rc) return rc;
+  }
+  return IRON_OK;
+}
+
+static int gemv_w8_launch_rows(GemvW8Params p, bool pair, cudaStream_t st) {
   IRON_REQUIRE(p.nb >= 1 && p.nb <= 8, IRON_ERR_UNSUPPORTED, "gemv_w8: batch %d not in 1..8", p.nb);
   IRON_REQUIRE(p.M > 0 && p.K > 0, IRON_ERR_ARG, "gemv_w8: empty shape M=%d K=%d", p.M, p.K);
   IRON_REQUIRE(p.x && p.y, IRON_ERR_ARG, "gemv_w8: null x / y");
@@ -273,6 +293,9 @@ int gemv_w8_launch(GemvW8Params p, bool pair, cudaStream_t st) {
   while (ks < 8 && ((njobs + (8 / ks) - 1) / (8 / ks)) < 2 * iron_num_sms() && (p.K / 16) >= 64 * ks)
     ks *= 2;
   p.ksplit = ks;
+  // plain wires with K <= 4096 stream their rows through shared memory (gemv_stream.cu)
+  const int srd = gemv_stream_launch(p, pair, st);
+  if (srd <= 0) return srd;
   switch (p.wa.G) {
     case 32: return launch_g<32>(p, pair, st);
     case 64: return launch_g<64>(p, pair, st);

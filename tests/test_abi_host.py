@@ -33,8 +33,8 @@ def test_error_reporting_without_gpu():
     """Argument validation runs on the host and reports through iron_last_error."""
     with pytest.raises(_lib.IronError, match="group must be"):
         _lib.call("iron_gemv_w8a16", 16, 64, 1024, 48, 1, 0, 0, 0, 16, 1, None, 16, None)
-    with pytest.raises(_lib.IronError, match="batch"):
-        _lib.call("iron_lm_head_bf16_argmax", 16, 8, 8, 16, 9, None, 16, 16, None)
+    with pytest.raises(_lib.IronError, match="batch 0 below 1"):
+        _lib.call("iron_lm_head_bf16_argmax", 16, 8, 8, 16, 0, None, 16, 16, None)
 
 
 def test_gemvint8_arg_spec_matches_reference_formula():

@@ -82,7 +82,7 @@ SHAPES = [(6144, 1024), (3072, 1024), (1024, 3072), (12288, 4096), (4096, 12288)
 
 
 @pytest.mark.parametrize("N,K", SHAPES)
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 32])
 def test_gemv_w8_baseline_shapes(N, K, batch):
     """BASELINE operator sweep shapes, group 32, masters N(0,0.02), x ~ N(0,1)."""
     torch.manual_seed(N + K + batch)
@@ -162,7 +162,7 @@ def test_bf16_gemv_independent_batches():
         assert_ulps(host(y[b]), ops.gemv_bf16(host(A[b]), host(x[b])), max_ulp=1, what=f"batch {b}")
 
 
-@pytest.mark.parametrize("batch", [1, 3])
+@pytest.mark.parametrize("batch", [1, 3, 11])
 def test_lm_head_bf16_argmax(batch):
     """Fused lm_head + argmax over the Qwen3 vocabulary; ties resolve to the lowest index."""
     torch.manual_seed(11)

@@ -183,6 +183,21 @@ def test_step_error_word_aborts_and_resets(small):
     assert int(dec.step_tokens([5], 0)[0]) == want
 
 
+def test_batch_above_eight_matches_single_streams(small):
+    """Ten streams (the projections run in launches of 8 activation rows) against ten
+    single-stream decoders."""
+    cfg, w = small
+    B = 10
+    multi = Qwen3B200(w, max_seq=32, batch=B)
+    single = [Qwen3B200(w, max_seq=32) for _ in range(B)]
+    rng = np.random.default_rng(12)
+    for pos in range(3):
+        toks = [int(t) for t in rng.integers(0, cfg.V, B)]
+        got = multi.step_tokens(toks, pos)
+        for b in range(B):
+            assert int(single[b].step_tokens([toks[b]], pos)[0]) == int(got[b]), f"stream {b} pos {pos}"
+
+
 def test_batched_streams_match_single_stream(small):
     cfg, w = small
     single = [Qwen3B200(w, max_seq=32) for _ in range(3)]

@@ -260,7 +260,7 @@ int make_wire(Wire& w, const void* base, int M, int K, int group, int tile_m, in
 }
 
 static int gemv_w8_launch_rows(GemvW8Params p, bool pair, cudaStream_t st);
-int gemv_stream_launch(const GemvW8Params& p, bool pair, cudaStream_t st);
+int gemv_mma_launch(const GemvW8Params& p, bool pair, cudaStream_t st);
 
 // Batches above 8 run as successive launches over 8 activation rows each (the weight
 // streams once per launch): the batch-8 kernel's arithmetic for every row.
@@ -268,12 +268,7 @@ int gemv_w8_launch(GemvW8Params p, bool pair, cudaStream_t st) {
   IRON_REQUIRE(p.nb >= 1, IRON_ERR_UNSUPPORTED, "gemv_w8: batch %d below 1", p.nb);
   if (p.nb <= 8) return gemv_w8_launch_rows(p, pair, st);
   for (int b0 = 0; b0 < p.nb; b0 += 8) {
-    GemvW8Params q = p;
-    q.nb = p.nb - b0 < 8 ? p.nb - b0 : 8;
-    q.x = p.x + (size_t)b0 * p.ld_x;
-    q.res = p.res ? p.res + (size_t)b0 * p.ld_y : nullptr;
-    q.y = p.epi == EPI_F32 ? (uint16_t*)((float*)p.y + (size_t)b0 * p.ld_y) : p.y + (size_t)b0 * p.ld_y;
-    const int rc = gemv_w8_launch_rows(q, pair, st);
+    const int rc = gemv_w8_launch_rows(gemv_rows(p, b0, p.nb - b0 < 8 ? p.nb - b0 : 8), pair, st);
     if (rc) return rc;
   }
   return IRON_OK;
@@ -287,15 +282,15 @@ static int gemv_w8_launch_rows(GemvW8Params p, bool pair, cudaStream_t st) {
   if (pair && p.wa.xor_mask != p.wb.xor_mask)
     return iron_set_error(IRON_ERR_ARG, "gemv_w8: paired wires must share a payload domain");
   p.xor_mask = p.wa.xor_mask;
+  // plain wires: exact integer tensor-core dot products over a bulk-copy ring (gemv_mma.cu)
+  const int mrc = gemv_mma_launch(p, pair, st);
+  if (mrc <= 0) return mrc;
   // split K inside the CTA until the grid covers the GPU (at least one chunk per lane)
   const int njobs = (p.M + 3) / 4;
   int ks = 1;
   while (ks < 8 && ((njobs + (8 / ks) - 1) / (8 / ks)) < 2 * iron_num_sms() && (p.K / 16) >= 64 * ks)
     ks *= 2;
   p.ksplit = ks;
-  // plain wires with K <= 4096 stream their rows through shared memory (gemv_stream.cu)
-  const int srd = gemv_stream_launch(p, pair, st);
-  if (srd <= 0) return srd;
   switch (p.wa.G) {
     case 32: return launch_g<32>(p, pair, st);
     case 64: return launch_g<64>(p, pair, st);

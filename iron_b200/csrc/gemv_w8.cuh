@@ -50,6 +50,15 @@ struct GemvW8Params {
   uint32_t xor_mask;
 };
 
+// The same call restricted to batch rows [b0, b0 + n).
+inline GemvW8Params gemv_rows(GemvW8Params p, int b0, int n) {
+  p.nb = n;
+  p.x += (size_t)b0 * p.ld_x;
+  if (p.res) p.res += (size_t)b0 * p.ld_y;
+  p.y = p.epi == EPI_F32 ? (uint16_t*)((float*)p.y + (size_t)b0 * p.ld_y) : p.y + (size_t)b0 * p.ld_y;
+  return p;
+}
+
 int make_wire(Wire& w, const void* base, int M, int K, int group, int tile_m, int rows_per_core,
               int tiles_per_core, int domain);
 // pair: rows of wa (gate) and wb (up) combined as bf16(silu_tanh(g) * u)

@@ -101,6 +101,26 @@ def test_gemv_w8_baseline_shapes(N, K, batch):
     assert np.all(err <= lim), np.max(err / lim)
 
 
+@pytest.mark.parametrize("N,K,group,domain", [(6144, 1024, 32, 0), (1024, 3072, 32, 0), (12288, 4096, 32, 0),
+                                               (4096, 12288, 32, 0), (40, 256, 32, 0), (1000, 3072, 64, 1),
+                                               (300, 2048, 128, 0), (148 * 16 + 5, 768, 32, 1)])
+def test_gemv_w8_batch_rows_match_single_rows(N, K, group, domain):
+    """Every batch row of a batch-5 and a batch-8 call is bit-identical to the batch-1 call on
+    that row: the activations are held at the same precision at every batch size and each
+    output is accumulated in the same order.  Covers K split into segments, ragged row
+    blocks, groups 64/128 and the biased payload domain."""
+    torch.manual_seed(N * 7 + K)
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    wire = quantize_to_wire(w, group, domain=domain)
+    q, s = wire_to_numpy(quantize_to_wire(w, group, domain=0), N, K, group)  # the signed decode
+    x = torch.randn(8, K, device="cuda").to(torch.bfloat16)
+    singles = np.stack([_run_w8(wire, N, K, group, 1, domain, x[b:b + 1].contiguous(), 1)[0] for b in range(8)])
+    assert_w8_exact(singles, q, s, host(x), "batch 1")
+    for batch in (5, 8):
+        out = _run_w8(wire, N, K, group, 1, domain, x[:batch].contiguous(), batch)
+        assert np.array_equal(out, singles[:batch]), f"batch {batch} differs from single rows"
+
+
 def test_gemv_w8_residual_and_biased():
     torch.manual_seed(3)
     M, K = 512, 2048

@@ -1,12 +1,14 @@
 // Decode attention: split-KV flash decoding over a GQA KV cache.
 //
 // Pass 1: grid (split, kv_head, stream).  Each CTA owns one KV head of one
-// stream and a contiguous slice of its positions; its 4 warps take positions
-// round-robin.  A lane holds HD/32 consecutive dims of every query head of the
-// GQA group (so a K or V row is one coalesced 8-byte-per-lane load), q.k is a
-// warp butterfly sum, and each warp keeps a base-2 online softmax state
-// (m, l, o) per head -- the streaming form of decode_attn.cc:208-279.  The
-// warps merge in shared memory and the CTA writes one partial per head.
+// stream and a contiguous slice of its positions; its 4 warps take blocks of
+// positions round-robin.  HD/8 lanes share a K or V row, 16 bytes (8 dims) each,
+// so one warp-wide load covers 32*8/HD positions and a warp keeps U such loads of
+// K and of V in flight.  A lane holds its 8 dims of every query head of the GQA
+// group; q.k is a butterfly over the row's lanes, and each row group keeps a
+// base-2 online softmax state (m, l, o) per head -- the streaming form of
+// decode_attn.cc:208-279.  Row groups merge by shuffles, warps in shared memory,
+// and the CTA writes one partial per head.
 // Pass 2: grid (head, stream) merges the splits: M = max m_s,
 // o = sum o_s 2^(m_s-M) / sum l_s 2^(m_s-M)  (decode_attn/reference.py:26-38).
 #include "common.cuh"
@@ -24,22 +26,25 @@ struct AttnParams {
 
 template <int HD, int GQ>
 __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
-  constexpr int PER = HD / 32;
-  constexpr int U = 4;  // positions per warp iteration
+  constexpr int RL = HD / 8;          // lanes per K / V row, 16 bytes each
+  constexpr int RPW = 32 / RL;        // rows per warp-wide load
+  constexpr int U = GQ >= 8 ? 2 : 4;  // loads per iteration
+  constexpr int PW = U * RPW;         // positions per warp iteration
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int sub = lane % RL, rg = lane / RL;  // dims [8 sub, 8 sub + 8) of row group rg
   int L = p.seq_lens ? p.seq_lens[b] : p.seq_len;
   L = L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
   const int chunk = (L + p.nsplit - 1) / p.nsplit;
   const int start = split * chunk;
   const int end = min(L, start + chunk);
 
-  float q[GQ][PER];
+  float q[GQ][8];
 #pragma unroll
   for (int h = 0; h < GQ; ++h) {
-    const uint16_t* qs = p.q + ((size_t)b * p.H + kvh * GQ + h) * HD + lane * PER;
+    const uint16_t* qs = p.q + ((size_t)b * p.H + kvh * GQ + h) * HD + sub * 8;
 #pragma unroll
-    for (int e = 0; e < PER; ++e) q[h][e] = bf2f(qs[e]);
+    for (int e = 0; e < 8; ++e) q[h][e] = bf2f(qs[e]);
   }
   const uint16_t* head = p.kv + ((size_t)b * p.KV + kvh) * 2 * (size_t)p.max_seq * HD;
   // element offsets of K_j / V_j inside the head region for the three layouts
@@ -51,68 +56,75 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   };
   const size_t voff = p.layout == 0 ? HD : (p.layout == 1 ? (size_t)p.max_seq * HD : (size_t)p.block_kv * HD);
 
-  float m[GQ], l[GQ], o[GQ][PER];
+  // online softmax state of this lane's row group
+  float m[GQ], l[GQ], o[GQ][8];
 #pragma unroll
   for (int h = 0; h < GQ; ++h) {
     m[h] = -INFINITY;
     l[h] = 0.f;
 #pragma unroll
-    for (int e = 0; e < PER; ++e) o[h][e] = 0.f;
+    for (int e = 0; e < 8; ++e) o[h][e] = 0.f;
   }
 
-  for (int j0 = start + wid * U; j0 < end; j0 += 4 * U) {
-    float kf[U][PER], vf[U][PER];
+  for (int j0 = start + wid * PW; j0 < end; j0 += 4 * PW) {
+    uint4 kr[U], vr[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = min(j0 + u, end - 1);
-      const uint16_t* kr = head + koff(j) + lane * PER;
-      const uint16_t* vr = kr + voff;
-      if constexpr (PER == 4) {
-        const uint2 kk = ldg_stream8(kr), vv = ldg_stream8(vr);
-        kf[u][0] = bf_lo(kk.x);
-        kf[u][1] = bf_hi(kk.x);
-        kf[u][2] = bf_lo(kk.y);
-        kf[u][3] = bf_hi(kk.y);
-        vf[u][0] = bf_lo(vv.x);
-        vf[u][1] = bf_hi(vv.x);
-        vf[u][2] = bf_lo(vv.y);
-        vf[u][3] = bf_hi(vv.y);
-      } else {
-        static_assert(PER == 2, "head_dim 64 or 128");
-        const uint32_t kk = __ldg((const uint32_t*)kr), vv = __ldg((const uint32_t*)vr);
-        kf[u][0] = bf_lo(kk);
-        kf[u][1] = bf_hi(kk);
-        vf[u][0] = bf_lo(vv);
-        vf[u][1] = bf_hi(vv);
-      }
+      const int j = min(j0 + u * RPW + rg, end - 1);
+      const uint16_t* kp = head + koff(j) + sub * 8;
+      kr[u] = ldg_stream(kp);
+      vr[u] = ldg_stream(kp + voff);
     }
 #pragma unroll
     for (int h = 0; h < GQ; ++h) {
       float s[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) d = fmaf(q[h][e], kf[u][e], d);
-        s[u] = warp_sum(d) * p.scale;
-        if (j0 + u >= end) s[u] = -INFINITY;
-      }
       float mn = m[h];
 #pragma unroll
-      for (int u = 0; u < U; ++u) mn = fmaxf(mn, s[u]);
+      for (int u = 0; u < U; ++u) {
+        const uint32_t kw[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          d = fmaf(q[h][2 * e], bf_lo(kw[e]), d);
+          d = fmaf(q[h][2 * e + 1], bf_hi(kw[e]), d);
+        }
+#pragma unroll
+        for (int x = 1; x < RL; x <<= 1) d += __shfl_xor_sync(~0u, d, x);
+        s[u] = j0 + u * RPW + rg < end ? d * p.scale : -INFINITY;
+        mn = fmaxf(mn, s[u]);
+      }
+      if (mn == -INFINITY) continue;  // this row group has seen only masked positions
       const float corr = exp2f(m[h] - mn);
       float ls = l[h] * corr;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) o[h][e] *= corr;
+      for (int e = 0; e < 8; ++e) o[h][e] *= corr;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const float pu = exp2f(s[u] - mn);
+        const uint32_t vw[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
         ls += pu;
 #pragma unroll
-        for (int e = 0; e < PER; ++e) o[h][e] = fmaf(pu, vf[u][e], o[h][e]);
+        for (int e = 0; e < 4; ++e) {
+          o[h][2 * e] = fmaf(pu, bf_lo(vw[e]), o[h][2 * e]);
+          o[h][2 * e + 1] = fmaf(pu, bf_hi(vw[e]), o[h][2 * e + 1]);
+        }
       }
       l[h] = ls;
       m[h] = mn;
+    }
+  }
+  // merge the row groups of the warp (lanes RL apart hold the same dims)
+#pragma unroll
+  for (int x = RL; x < 32; x <<= 1) {
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      const float m2 = __shfl_xor_sync(~0u, m[h], x), l2 = __shfl_xor_sync(~0u, l[h], x);
+      const float M = fmaxf(m[h], m2);
+      const float f1 = M == -INFINITY ? 0.f : exp2f(m[h] - M), f2 = M == -INFINITY ? 0.f : exp2f(m2 - M);
+      l[h] = l[h] * f1 + l2 * f2;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[h][e] = o[h][e] * f1 + __shfl_xor_sync(~0u, o[h][e], x) * f2;
+      m[h] = M;
     }
   }
 
@@ -125,8 +137,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
       sm_m[wid][h] = m[h];
       sm_l[wid][h] = l[h];
     }
+    if (rg == 0) {
 #pragma unroll
-    for (int e = 0; e < PER; ++e) sm_o[wid][h][lane * PER + e] = o[h][e];
+      for (int e = 0; e < 8; ++e) sm_o[wid][h][sub * 8 + e] = o[h][e];
+    }
   }
   __syncthreads();
   for (int t = threadIdx.x; t < GQ * HD; t += blockDim.x) {
@@ -173,10 +187,34 @@ static int nsplit_cap(int max_seq) {
   return n < 1 ? 1 : (n > 256 ? 256 : n);
 }
 
+// Resident split CTAs per SM (registers bound them), cached per device.
 template <int HD, int GQ>
-static void launch_split(const AttnParams& p, int batch, cudaStream_t st) {
-  dim3 g(p.nsplit, p.KV, batch);
+static int split_ctas_per_sm() {
+  static int occ[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && occ[dev]) return occ[dev];
+  int n = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_split_kernel<HD, GQ>, 128, 0);
+  if (n < 1) n = 1;
+  if (dev < 64) occ[dev] = n;
+  return n;
+}
+
+// Split count: with few (stream, KV head) pairs, one resident wave of CTAs (the
+// longest chunk per CTA that still fills the GPU); once the pairs alone come near a
+// wave, three waves, so that the SMs stay full while the last CTAs finish.
+// Returns the split count.
+template <int HD, int GQ>
+static int launch_split(AttnParams p, int batch, int cap, cudaStream_t st) {
+  const int wave = split_ctas_per_sm<HD, GQ>() * iron_num_sms(), pairs = batch * p.KV;
+  const int target = 4 * pairs >= wave ? 3 * wave : wave;
+  int ns = (target + pairs - 1) / pairs;
+  ns = ns < 1 ? 1 : (ns > cap ? cap : ns);
+  p.nsplit = ns;
+  dim3 g(ns, p.KV, batch);
   attn_split_kernel<HD, GQ><<<g, 128, 0, st>>>(p);
+  return ns;
 }
 
 }  // namespace iron
@@ -201,7 +239,7 @@ extern "C" int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t*
                "decode_attn: seq_len %d not in [1, %d]", seq_len, max_seq);
   IRON_REQUIRE(workspace_bytes >= iron_decode_attn_workspace_bytes(batch, H, HD, max_seq), IRON_ERR_ARG,
                "decode_attn: workspace of %lld bytes is too small", (long long)workspace_bytes);
-  IRON_REQUIRE(iron_aligned(kv, 8) && iron_aligned(q, 4), IRON_ERR_ALIGN, "decode_attn: kv must be 8-byte aligned");
+  IRON_REQUIRE(iron_aligned(kv, 16) && iron_aligned(q, 4), IRON_ERR_ALIGN, "decode_attn: kv must be 16-byte aligned");
   AttnParams p;
   p.q = q;
   p.kv = kv;
@@ -214,15 +252,12 @@ extern "C" int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t*
   p.seq_len = seq_len;
   p.seq_lens = seq_lens_dev;
   p.scale = 1.4426950408889634f / sqrtf((float)HD);
-  const int target = 4 * iron_num_sms();
-  int ns = (target + batch * KV - 1) / (batch * KV);
   const int cap = nsplit_cap(seq_lens_dev ? max_seq : seq_len);
-  ns = ns < 1 ? 1 : (ns > cap ? cap : ns);
-  p.nsplit = ns;
+  int ns = 0;
   const int GQ = H / KV;
   cudaStream_t st = (cudaStream_t)stream;
 #define IRON_ATTN_CASE(hd, gq) \
-  if (HD == hd && GQ == gq) { launch_split<hd, gq>(p, batch, st); goto combine; }
+  if (HD == hd && GQ == gq) { ns = launch_split<hd, gq>(p, batch, cap, st); goto combine; }
   IRON_ATTN_CASE(128, 1) IRON_ATTN_CASE(128, 2) IRON_ATTN_CASE(128, 4) IRON_ATTN_CASE(128, 8)
   IRON_ATTN_CASE(64, 1) IRON_ATTN_CASE(64, 2) IRON_ATTN_CASE(64, 4) IRON_ATTN_CASE(64, 8)
 #undef IRON_ATTN_CASE

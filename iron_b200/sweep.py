@@ -10,7 +10,8 @@
 Launches run back to back over enough copies of the weight (or KV cache) that the
 copies together exceed twice the 126 MB L2, each launch reading a copy the previous
 ones evicted, so the operands come from HBM as in a decode step; CUDA events time
-the whole sequence, queued behind a short device sleep so host launch cost is hidden.  Achieved GB/s = algorithmic bytes / time per launch:
+the whole sequence, queued behind a short device sleep so host launch cost is hidden.
+A first row times an 8-element add the same way: the per-launch floor of this method.  Achieved GB/s = algorithmic bytes / time per launch:
 GEMV ``N*K + N*(K/G)*2 + B*K*2 + B*N*2``, attention ``B*2*Hkv*HD*L*2 + B*Hq*HD*4``; the
 fraction is against ``MEASURED_PEAKS.json`` ``hbm_gbs``.
 """
@@ -46,9 +47,9 @@ def _timed(fns, reps: int) -> float:
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = max(reps, len(fns))
-    # Hold the stream for ~2 ms so every launch below is queued before the first event
+    # Hold the stream for ~10 ms so every launch below is queued before the first event
     # fires: the host's per-launch cost stays outside the measured interval.
-    torch.cuda._sleep(4_000_000)
+    torch.cuda._sleep(20_000_000)
     e0.record(st)
     for i in range(n):
         fns[i % len(fns)]()
@@ -69,6 +70,12 @@ def main():
     st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
     rows = []
     g = torch.Generator(device=dev).manual_seed(0)
+    # launch floor: an 8-element add through the same C ABI, timed the same way
+    a = torch.zeros(8, dtype=torch.bfloat16, device=dev)
+    s_ = st()
+    ms = _timed([lambda: _lib.call("iron_add", a.data_ptr(), a.data_ptr(), a.data_ptr(), 8, s_)], args.reps)
+    rows.append({"kernel": "launch_floor", "us": ms * 1e3})
+    print(json.dumps(rows[-1]), flush=True)
     for N, K in GEMV_SHAPES:
         wbytes = N * K + N * (K // G) * 2
         w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)

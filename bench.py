@@ -58,9 +58,15 @@ def parse():
     ap.add_argument("--batch", type=int, default=1,
                     help="independent decode streams per GPU (1: the one-launch step; more: the chained "
                          "kernels as a CUDA graph)")
+    ap.add_argument("--model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b",
+                    help="qwen3-8b: BASELINE config 4, tensor parallel over the torchrun world "
+                         "(NCCL), a synthetic --prompt-position KV context (default 4096)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.model == "qwen3-8b" and args.prompt == PROMPT:
+        args.prompt = 4096
+    return args
 
 
 def workload(args):
@@ -362,6 +368,126 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_tp(args, rank, world, local_rank):
+    """Qwen3-8B int8-g32 greedy decode, tensor parallel over the
+    torchrun world (iron_b200/tp.py; NCCL all-reduce of the O / down partials, all-gather
+    of the vocabulary-parallel argmax).  The context is ``--prompt`` positions of N(0, 1)
+    K/V per stream (synthetic: prefilling 4096 tokens through 36 layers would only
+    repeat the decode step); then W warm-up and K timed greedy steps."""
+    import numpy as np
+    import torch
+    from iron_b200.qwen3 import Qwen3Config, Qwen3Weights
+    from iron_b200.tp import Qwen3TP
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = Qwen3Config.qwen3_8b()
+    K, W, B, P = args.steps, args.warmup, args.batch, args.prompt
+    max_seq = (P + W + 2 * K + 8 + 63) // 64 * 64
+    w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
+    cpu_layer = w.to_numpy(n_layers=1) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    dec = Qwen3TP(w, rank, world, max_seq=max_seq, batch=B, device=dev)
+    del w
+    torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(args.seed + 17 + rank)
+    dec.kv[..., :P * 2 * cfg.HD].normal_(generator=g)  # per-token [K_t | V_t]: positions [0, P)
+    dec.set_position(P)
+    first = torch.randint(0, cfg.V, (B,), generator=torch.Generator().manual_seed(args.seed + 1))
+    with torch.cuda.stream(dec.stream):
+        dec.tok.copy_(first.to(dev, torch.int32))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                          if "CUDA_VISIBLE_DEVICES" in os.environ and world == 1 else local_rank)
+    clocks.start()
+    for _ in range(W):
+        dec.run_step(from_tokens=True, advance=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(dec.stream)
+    for _ in range(K):
+        dec.run_step(from_tokens=True, advance=True)
+    e1.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    pos = P + W + K
+    toks = [int(t) for t in dec.tok.cpu()]
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e2.record(dec.stream)
+    for _ in range(K):
+        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        pos += 1
+    e3.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2.elapsed_time(e3)
+    clocks.stop()
+    clk = clocks.summary()
+    tt = torch.tensor([t_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms = float(tt[0]), float(tt[1])
+    dec.close()
+    if rank != 0:
+        return
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    # every weight, the lm_head and the K/V heads are split over the ranks: bytes per GPU
+    step_bytes = sum(token_bytes(cfg, GROUP, P + W + 1 + i, B) for i in range(K)) / K / world
+    achieved = step_bytes / (t_ms / K / 1000.0) / 1e9
+    line = {"metric": METRIC, "value": K * B / (t_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8xbf16", "data": "synthetic",
+            "config": {"workload": f"qwen3-8b int8-g{GROUP} greedy decode, batch {B}, bf16 tied lm_head, "
+                                   f"{P}-position synthetic N(0,1) KV context",
+                       "batch": B, "layers": 36, "hidden": 4096, "vocab": 151936, "group": GROUP,
+                       "context": P, "parallelism": f"tp{world}",
+                       "collectives": "NCCL all_reduce of batch x 4096 float32 twice per layer, "
+                                      "all_gather of 8 bytes per stream per step",
+                       "l2": "no flush: ~9 GB / world of weights streamed per step, larger than the L2"},
+            "e2e": {"value": K * B / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": K * dec.launches_per_step(),
+            "roofline": {"bound": "hbm", "kernel": f"the chained kernels of one step ({dec.launches_per_step()} "
+                                                   f"launches) per GPU",
+                         "bytes_per_launch": step_bytes, "achieved": achieved, "peak": peak,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+            "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    if cpu_layer is not None:
+        from oracle import ops
+        from oracle.bf16 import rnd
+        from oracle.qwen3 import OracleQwen3, Qwen3Shape
+        threads = ops.set_threads(len(os.sched_getaffinity(0)))
+        shape = Qwen3Shape(D=cfg.D, FF=cfg.FF, Hq=cfg.Hq, Hkv=cfg.Hkv, HD=cfg.HD, V=cfg.V, n_layers=1, group=GROUP)
+        orc = OracleQwen3(shape, cpu_layer, P + 1)
+        rng = np.random.default_rng(args.seed)
+        orc.kv[...] = rnd(rng.standard_normal(orc.kv.shape).astype(np.float32))
+        x = cpu_layer["embed"][int(first[0])]
+        t0 = time.perf_counter()
+        orc.layer(0, x, P)
+        t_layer = time.perf_counter() - t0
+        rows = cfg.V // 16  # the lm_head on 1/16 of its rows, scaled
+        t0 = time.perf_counter()
+        ops.gemv_bf16(cpu_layer["embed"][:rows], x)
+        t_head = (time.perf_counter() - t0) * 16
+        tps = 1.0 / (cfg.n_layers * t_layer + t_head)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"one Qwen3-8B decoder layer of the numpy oracle at position {P} "
+                                          f"(x 36) + the bf16 lm_head on 1/16 of its rows (x 16), this run's "
+                                          f"weights"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -378,7 +504,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.model == "qwen3-8b":
+            run_tp(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

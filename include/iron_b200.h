@@ -279,6 +279,29 @@ int iron_qwen3_pack_wd_cols(const void* wd_wire, int D, int FF, int group, void*
 /* Zero the sync words and the accumulators (after a timed-out step, or before first use). */
 int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream);
 
+/* ---- tensor-parallel building blocks ---------------------------------------------
+ * No reference counterpart: IRON decodes on one NPU.  Tensor-parallel Qwen3
+ * (iron_b200/tp.py) splits QKV by heads, O and down along K (row-parallel), gate/up
+ * by rows and the lm_head by vocabulary; these entry points cut the fused blocks at
+ * the cross-rank sums and the cross-rank argmax.
+ *
+ * iron_gemv_w8a16_ex: iron_gemv_w8a16 on plain wires (tile_m = 1) with the
+ * epilogues exposed.  wire_b != NULL: gate/up pair, y = bf16(silu_tanh(bf16(Wa@h)) *
+ * bf16(Wb@h)) (epi 0 only).  rms_w != NULL: h = bf16(RMSNorm_w(x)) first (rms_mode as
+ * iron_rmsnorm).  epi 0: y bf16 = bf16(sum); 1: y bf16 = bf16(residual + bf16(sum));
+ * 2: y float32 = float(sum) (a rank's partial sum).  x rows ld_x apart, y rows ld_y. */
+int iron_gemv_w8a16_ex(const void* wire_a, const void* wire_b, int M, int K, int group, int domain,
+                       const uint16_t* x, int ld_x, int batch, const uint16_t* rms_w, float eps,
+                       int rms_mode, const uint16_t* residual, int epi, void* y, int ld_y, void* stream);
+/* y = bf16(res + bf16(sum)) elementwise (sum: float32, the all-reduced partials). */
+int iron_resid_add_f32(const uint16_t* res, const float* sum, uint16_t* y, int64_t n, void* stream);
+/* pairs[b] = (float bits of logits[b, tok[b]], tok[b] + offset): a rank's greedy
+ * candidate over its vocabulary rows [offset, offset + M). */
+int iron_argmax_pair(const uint16_t* logits, int M, int batch, const int32_t* tok, int offset,
+                     int32_t* pairs, void* stream);
+/* tok_out[b] = index of the largest value over pairs[r][b], r < n (ties -> lowest index). */
+int iron_argmax_merge(const int32_t* pairs, int n, int batch, int32_t* tok_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

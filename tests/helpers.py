@@ -3,7 +3,7 @@
 import numpy as np
 import torch
 
-from iron_b200.test_utils import allclose_report
+from iron_b200.test_utils import allclose_report, cosine
 from oracle.bf16 import from_bits, round_bits
 
 RTOL, ATOL = 2e-2, 1e-2  # the BASELINE bf16 gate
@@ -74,4 +74,15 @@ def assert_w8_exact(got, q, s_bits, x, what=""):
     assert not bad.any(), f"{what}: {bad.sum()} rows off the exact sum, worst {np.max(np.abs(got - exact) / lim):.3g}"
 
 
-__all__ = ["w8_error_bound", "assert_w8_exact", "dev_bf16", "dev_u8", "host", "bits", "assert_close", "assert_ulps", "from_bits", "RTOL", "ATOL"]
+def logit_gate(got, want, what, max_outside):
+    """Full-model logit agreement: at most ``max_outside`` of the logits outside the bf16
+    tolerance, none more than 0.1 away (a few bf16 ulps of the largest logits), and the
+    two vectors aligned."""
+    err = np.abs(got - want)
+    outside = np.mean(err > ATOL + RTOL * np.abs(want))
+    assert outside <= max_outside, f"{what}: {outside:.2%} of logits outside rtol {RTOL} / atol {ATOL}"
+    assert err.max() <= 0.1, f"{what}: max |err| {err.max():.3g}"
+    assert cosine(got, want) >= 0.9995, f"{what}: cosine {cosine(got, want):.6f}"
+
+
+__all__ = ["logit_gate", "w8_error_bound", "assert_w8_exact", "dev_bf16", "dev_u8", "host", "bits", "assert_close", "assert_ulps", "from_bits", "RTOL", "ATOL"]

@@ -11,10 +11,9 @@ import pytest
 import torch
 
 from iron_b200.qwen3 import Qwen3B200, Qwen3Config, Qwen3Weights
-from iron_b200.test_utils import cosine
 from oracle.qwen3 import OracleQwen3, Qwen3Shape
 
-from helpers import ATOL, RTOL, assert_close, host
+from helpers import ATOL, RTOL, assert_close, host, logit_gate
 
 pytestmark = pytest.mark.gpu
 
@@ -73,17 +72,6 @@ def test_graph_replay_equals_eager_full_model(full):
     assert Qwen3B200(w, max_seq=128, impl="ops").generate(prompt, 24) == g
 
 
-def _logit_gate(got, want, what, max_outside):
-    """Full-model logit agreement: at most ``max_outside`` of the logits outside the bf16
-    tolerance, none more than 0.1 away (a few bf16 ulps of the largest logits), and the
-    two vectors aligned."""
-    err = np.abs(got - want)
-    outside = np.mean(err > ATOL + RTOL * np.abs(want))
-    assert outside <= max_outside, f"{what}: {outside:.2%} of logits outside rtol {RTOL} / atol {ATOL}"
-    assert err.max() <= 0.1, f"{what}: max |err| {err.max():.3g}"
-    assert cosine(got, want) >= 0.9995, f"{what}: cosine {cosine(got, want):.6f}"
-
-
 def test_full_model_layer_by_layer_matches_oracle(full):
     """All 28 layers + lm_head of the one-launch step, checked layer by layer: the step
     records the hidden state entering every layer (``enable_trace``); the oracle runs
@@ -139,7 +127,7 @@ def test_step_kernel_equals_chained_kernels_full_model(full):
         a.kv.copy_(b.kv)
         ta, tb = int(a.step_tokens([t], p)[0]), int(b.step_tokens([t], p)[0])
         la, lb = host(a.logits[0]), host(b.logits[0])
-        _logit_gate(la, lb, f"pos {p}", max_outside=0.1)
+        logit_gate(la, lb, f"pos {p}", max_outside=0.1)
         if ta == tb:
             agree += 1
         else:

@@ -4,9 +4,9 @@
 // Data movement.  A decode GEMV is one pass over the weight.  One CTA per SM owns a
 // contiguous block of output rows, cut into tiles of 16 rows.  A producer warp
 // copies each tile's rows (all of K, or 4096-column pieces when K is larger) into a
-// ring of shared-memory slots with one cp.async.bulk per row and piece (no
-// multicast); the row stride is padded to 16 mod 128 bytes so that ldmatrix and the
-// scale loads are free of bank conflicts.  Eight consumer warps take work items of
+// ring of shared-memory slots with one CTA-local cp.async.bulk per row and piece;
+// the row stride is padded to 16 mod 128 bytes so that ldmatrix and the scale loads
+// are free of bank conflicts.  Eight consumer warps take work items of
 // 128..1024 columns of a slot in turn, so a small row block still gives every warp
 // work; a slot is released when all its items are done.
 //

@@ -18,7 +18,7 @@
 //   - Per layer that leaves two grid barriers (after O, after down) and two
 //     group barriers (after QKV, after the attention splits).
 //   - Weights do not depend on activations, so each CTA's weight share streams
-//     through a shared-memory ring by cp.async.bulk (no multicast).  A producer
+//     through a shared-memory ring by cp.async.bulk (CTA-local copies).  A producer
 //     warp issues the copies as far ahead as the ring allows (about a layer), so
 //     issuing never sits on the compute path.  The attention KV range is
 //     prefetched to L2 one phase early.

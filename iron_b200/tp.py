@@ -23,8 +23,9 @@ rounding that the fused residual epilogue applies.
 
 ``Qwen3TP._stages`` is a generator of launches that yields at every cross-rank
 step; ``NcclCollective`` performs them with ``torch.distributed`` on the decode
-stream, and tests drive several ranks on one GPU in lock step
-(``step_lockstep``) to check the split arithmetic with the real kernels.
+stream (captured, with the kernels, in the step's CUDA graph after one eager
+step), and tests drive several ranks on one GPU in lock step (``step_lockstep``)
+to check the split arithmetic with the real kernels.
 """
 
 from __future__ import annotations
@@ -138,7 +139,7 @@ class Qwen3TP(Qwen3B200):
                  batch: int = 1, use_graph: bool | None = None, device="cuda", collective=None):
         local = shard_weights(weights, rank, world)
         if use_graph is None:
-            use_graph = world == 1
+            use_graph = True
         super().__init__(local, max_seq, batch=batch, keep_logits=True, use_graph=use_graph, device=device,
                          impl="ops")
         self.rank, self.world = rank, world
@@ -152,6 +153,19 @@ class Qwen3TP(Qwen3B200):
         if collective is None:
             collective = LocalCollective() if world == 1 else NcclCollective()
         self.collective = collective
+        self._eager_done: set = set()
+
+    def run_step(self, from_tokens: bool = True, advance: bool = True):
+        """As Qwen3B200.run_step; with world > 1 the first step of each kind runs eagerly
+        (it sets up the NCCL communicators), later ones replay a captured graph that
+        holds the collectives too."""
+        key = (from_tokens, advance)
+        if self.use_graph and self.world > 1 and key not in self._eager_done:
+            self._eager_done.add(key)
+            with torch.cuda.stream(self.stream):
+                self._launch_step(from_tokens, advance, self.stream.cuda_stream)
+            return
+        super().run_step(from_tokens, advance)
 
     def launches_per_step(self, from_tokens: bool = True, advance: bool = True) -> int:
         """Our kernels per step (batch <= 8): embedding; per layer QKV GEMV + head

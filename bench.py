@@ -37,11 +37,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "Qwen3 decode tokens/s"
 # DRAM traffic of one step launch beyond its algorithmic bytes, from an ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum = 798.5 MB at context 71, where the
+# (dram__bytes_read.sum + dram__bytes_write.sum = 795.5 MB at context 71, where the
 # algorithmic bytes are 788.4 MB): accumulator zeroing, K/V and logit writes.  The
 # weights and the K/V reads scale with the algorithmic bytes, so a launch's traffic is
 # its algorithmic bytes plus this.
-STEP_TRAFFIC_EXTRA = 10.1e6
+STEP_TRAFFIC_EXTRA = 7.1e6
 UNIT = "tokens/s"
 PROMPT = 1024
 GROUP = 32

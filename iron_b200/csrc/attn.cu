@@ -209,7 +209,7 @@ template <int HD, int GQ>
 static int launch_split(AttnParams p, int batch, int cap, cudaStream_t st) {
   const int wave = split_ctas_per_sm<HD, GQ>() * iron_num_sms(), pairs = batch * p.KV;
   const int target = 4 * pairs >= wave ? 3 * wave : wave;
-  int ns = (target + pairs - 1) / pairs;
+  int ns = target / pairs;  // rounded down: a few CTAs past the last wave would run alone
   ns = ns < 1 ? 1 : (ns > cap ? cap : ns);
   p.nsplit = ns;
   dim3 g(ns, p.KV, batch);

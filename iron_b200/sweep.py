@@ -1,6 +1,7 @@
 """Operator sweep: achieved HBM bandwidth of the decode kernels.
 
-``python -m iron_b200.sweep [--reps N] [--json FILE]`` times, on synthetic data:
+``python -m iron_b200.sweep [--reps N] [--json FILE]`` times, on synthetic data
+(``--capture`` instead runs the small case of an ncu capture of the GEMV):
 
 - the int8 group-32 GEMV ``iron_gemv_w8a16`` at (N, K) in {(6144,1024), (3072,1024),
   (1024,3072), (12288,4096), (4096,12288)} and batch in {1, 8, 32};
@@ -58,11 +59,47 @@ def _timed(fns, reps: int) -> float:
     return e0.elapsed_time(e1) / n
 
 
+CAPTURE_CASES = [(6144, 1024, 8), (1024, 3072, 8), (6144, 1024, 1)]
+
+
+def capture_case():
+    """The small case of an ncu capture of the GEMV kernel: for each of CAPTURE_CASES
+    ~300 MB of weight copies, each run once (the launches ``ncu --launch-skip`` passes
+    over), then one launch per case on a copy that has left the L2."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    st = torch.cuda.current_stream().cuda_stream
+    cases, warm = [], 0
+    for N, K, B in CAPTURE_CASES:
+        w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)
+        ws = [w0] + [w0.clone() for _ in range(max(1, 300 * 2**20 // (N * K)) - 1)]
+        x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty(B, N, dtype=torch.bfloat16, device=dev)
+        cases.append((N, K, B, ws, x, y))
+
+    def run(N, K, B, w, x, y):
+        _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B, None, y.data_ptr(), st)
+
+    for N, K, B, ws, x, y in cases:
+        for w in ws[1:]:
+            run(N, K, B, w, x, y)
+            warm += 1
+    torch.cuda.synchronize()
+    for N, K, B, ws, x, y in cases:
+        run(N, K, B, ws[0], x, y)
+    torch.cuda.synchronize()
+    print(f"warm-up launches: {warm}; then one launch each of {CAPTURE_CASES}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=50)
     ap.add_argument("--json", type=str, default=None)
+    ap.add_argument("--capture", action="store_true", help="run only the small ncu capture case of the GEMV")
     args = ap.parse_args()
+    if args.capture:
+        capture_case()
+        return
     root = Path(__file__).resolve().parents[1]
     peaks = root / "MEASURED_PEAKS.json"
     peak = json.loads(peaks.read_text())["hbm_gbs"] if peaks.exists() else 6650.0

@@ -51,14 +51,22 @@ int iron_last_error(char* buf, int buflen);
  * y[b, m] = bf16( r[b, m] + bf16(sum ...) )                          (epilogue 1, residual)
  * Replaces GEMVInt8 (iron/operators/gemv_int8/op.py:20-178), kernel
  * matvec_vectorized_int8_bf16 (aie_kernels/aie2p/mv_int8_signed.cc:103-115,
- * biased: mv_int8.cc:60-114).  batch: activation rows sharing the weight (above 8 they run in
- * launches of 8 rows, each streaming the weight).
+ * biased: mv_int8.cc:60-114).  batch: activation rows sharing the weight.  Batch 1..8
+ * (and 9..15) computes the exact dequantised sum (one bf16 rounding; launches of 8
+ * rows); batch 16..256 on plain wires runs one tcgen05 tensor-core contraction with
+ * the weight dequantised to bf16 (bf16(q*s), float32 accumulation), within the
+ * bf16 tolerance of the exact sum (see iron_tc_status).
  * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.
  */
 int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
                     int rows_per_core, int tiles_per_core, int domain,
                     const uint16_t* x, int batch, const uint16_t* residual,
                     uint16_t* y, void* stream);
+
+/* Error word of the tensor-core path (batch >= 16) on the current device: 0, or
+ * the code of the first bounded device wait that timed out.  clear != 0 also resets
+ * it (and the kernel's split-K counters).  No reference counterpart. */
+int iron_tc_status(int clear);
 
 /* Dequantise a wire to float32 q*s (exact), row-major (M, K).  Test/inspection
  * entry point for the bit-exact dequant check (GEMVInt8.reference, op.py:173-178). */

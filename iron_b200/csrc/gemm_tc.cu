@@ -1,0 +1,565 @@
+// Batched int8 group-quantised projections on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), for decode batches of 16..256 streams.
+//
+// At batch >= 16 a decode projection Y[b, m] = sum_k q[m,k] s[m,k/G] x[b,k] is a real
+// (skinny) contraction.  The weight streams once per launch (the 8-row launches of
+// the exact GEMV would stream it batch/8 times):
+//   - warp 0 (one lane) issues TMA copies per 64-column k-block: the int8 rows of a
+//     128-row tile (box 64 x 128, no swizzle) and the activations (box 64 x N bf16,
+//     128-byte swizzle, rows past the batch zero-filled), plus the tile's group
+//     scales for its whole K range once;
+//   - warps 1-4 dequantise the tile into bf16 w = bf16(q * s) straight into the
+//     128-byte-swizzled K-major layout the tensor core reads, and after the last
+//     k-block run the epilogue (each warp owns one 32-lane quarter of TMEM);
+//   - warp 5 allocates TMEM (N float32 columns per output tile, 2N for a gate/up
+//     pair), one lane issues tcgen05.mma (M = 128, N = batch padded to 16, K = 16 per
+//     instruction, bf16 x bf16 -> f32) and commits each k-block's MMAs to the stage's
+//     mbarrier, which frees the stage for the next copies.
+// K is split over CTAs so that the grid fills the GPU; each split writes its float32
+// partial tile to a fixed scratch array and the tile's last split (per-tile arrival
+// counter) adds the partials in split order and applies the epilogue, so results do
+// not depend on timing.
+//
+// Numerics: weights rounded to bf16 once (relative error <= 2^-9 per weight),
+// products and sums in float32 on the tensor core, the same bf16 epilogues as the
+// exact GEMV.  Within the BASELINE tolerance; the batch <= 8 kernels keep the exact
+// form.
+//
+// Every wait is bounded by %globaltimer; on a timeout the CTA records an error code
+// in a device word (iron_tc_status), lets its copies and MMAs finish (bounded), frees
+// its TMEM and returns.  The split-K scratch is one array per GPU: launches on
+// different streams of one GPU must not overlap.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemv_w8.cuh"
+
+namespace iron {
+namespace tc {
+
+constexpr int BM = 128;         // weight rows per tile (the MMA's M)
+constexpr int BK = 64;          // k per stage: one 128-byte swizzled bf16 row
+constexpr int NTH = 192;        // warp 0 TMA, warps 1-4 dequant + epilogue, warp 5 MMA
+constexpr int SMEM_MAX = 227 * 1024;
+constexpr size_t WS_FLOATS = 4u << 20;  // 16 MB of split-K partials
+constexpr int MAX_TILES = 4096;
+constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;
+
+__device__ float g_ws[WS_FLOATS];
+__device__ int g_counters[MAX_TILES];
+__device__ int g_status;
+
+struct TcParams {
+  int M, K, N, nb;              // N: MMA n (batch padded to 16); nb: batch rows
+  int splits, kbps;             // k-block splits and k-blocks per split
+  int sbox;                     // bytes of scales loaded per row and split
+  int stages, ncols;            // pipeline stages, TMEM columns
+  int epi;
+  const uint16_t* res;
+  void* y;
+  int ld_y;
+  uint32_t xor_mask;
+  int off_a, off_x, off_raw, off_scale, off_bar;
+};
+
+__device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(sa(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the phase of parity `par`; on a timeout (or another role's abort)
+// sets the abort flag and returns false.
+__device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t par, volatile int* abort_, int code) {
+  if (mbar_test(b, par)) return true;
+  const unsigned long long t0 = gtimer();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_test(b, par)) return true;
+    if ((it & 15) == 0) {
+      if (*abort_) return false;
+      if (gtimer() - t0 > TIMEOUT_NS) {
+        *abort_ = 1;
+        atomicExch(&g_status, code);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(sa(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(sa(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte-swizzled UMMA shared-memory descriptor: 8-row groups 1024 B apart
+// (stride byte offset), leading byte offset unused (1), version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
+}
+
+template <int G, bool PAIR>
+__global__ void __launch_bounds__(NTH, 1)
+    gemm_tc_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap tm_raw0,
+                   const __grid_constant__ CUtensorMap tm_sc0, const __grid_constant__ CUtensorMap tm_raw1,
+                   const __grid_constant__ CUtensorMap tm_sc1, const __grid_constant__ CUtensorMap tm_x) {
+  constexpr int NW = PAIR ? 2 : 1;
+  extern __shared__ uint8_t sm_dyn[];
+  // 1024-byte alignment for the swizzled tiles (the launch adds 1 KB of slack)
+  uint8_t* sm = sm_dyn + ((1024 - (sa(sm_dyn) & 1023)) & 1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x / p.splits, split = blockIdx.x - tile * p.splits;
+  const int row0 = tile * BM;
+  const int kb0 = split * p.kbps;
+  const int nkb = min(p.kbps, p.K / BK - kb0);
+  const int k0 = kb0 * BK;
+  const int N = p.N, S = p.stages;
+  uint8_t* atile = sm + p.off_a;      // [S][NW][128 rows][128 B] bf16, swizzled
+  uint8_t* xtile = sm + p.off_x;      // [S][N rows][128 B] bf16, swizzled
+  uint8_t* raw = sm + p.off_raw;      // [S][NW][128 rows][64 B] int8
+  uint8_t* scales = sm + p.off_scale; // [NW][128 rows][sbox B] bf16 group scales
+  uint64_t* bars = (uint64_t*)(sm + p.off_bar);
+  uint64_t* raw_full = bars;          // TMA bytes of a stage landed
+  uint64_t* a_full = bars + S;        // the stage's A tiles dequantised (4 warps)
+  uint64_t* freeb = bars + 2 * S;     // the stage's MMAs done (tcgen05.commit)
+  uint64_t* sc_full = bars + 3 * S;
+  uint64_t* acc_full = sc_full + 1;
+  uint32_t* tmem_slot = (uint32_t*)(acc_full + 1);
+  volatile int* abort_ = (volatile int*)(tmem_slot + 1);
+  volatile int* lastf = abort_ + 1;
+  volatile int* gof = abort_ + 2;
+  // the split's first group gfirst sits sdelta bytes into its 16-byte-aligned scale box
+  const int gfirst = k0 / G;
+  const int sdelta = (2 * gfirst) & 15;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&a_full[i], 4);
+      mbar_init(&freeb[i], 1);
+    }
+    mbar_init(sc_full, 1);
+    mbar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *abort_ = 0;
+    *lastf = 0;
+    *gof = 0;
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
+                 "r"(p.ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {  // ---- TMA producer ----
+    int issued = 0;
+    if (lane == 0 && nkb > 0) {
+      const int xs = p.K + 2 * gfirst - sdelta;
+      mbar_expect(sc_full, (uint32_t)(NW * BM * p.sbox));
+      tma_2d(scales, &tm_sc0, xs, row0, sc_full);
+      if (PAIR) tma_2d(scales + BM * p.sbox, &tm_sc1, xs, row0, sc_full);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        if (i >= S && !wait_phase(&freeb[s], (uint32_t)((i / S - 1) & 1), abort_, 1)) break;
+        mbar_expect(&raw_full[s], (uint32_t)(NW * BM * BK + N * 128));
+        const int kx = k0 + i * BK;
+        tma_2d(raw + (size_t)(s * NW) * BM * BK, &tm_raw0, kx, row0, &raw_full[s]);
+        if (PAIR) tma_2d(raw + (size_t)(s * NW + 1) * BM * BK, &tm_raw1, kx, row0, &raw_full[s]);
+        tma_2d(xtile + (size_t)s * N * 128, &tm_x, kx, 0, &raw_full[s]);
+        issued = i + 1;
+      }
+      // no copy may still be in flight when the CTA exits
+      for (int i = max(0, issued - S); i < issued; ++i) {
+        const unsigned long long t0 = gtimer();
+        while (!mbar_test(&raw_full[i % S], (uint32_t)((i / S) & 1)) && gtimer() - t0 < 20ull * 1000 * 1000) {
+        }
+      }
+      const unsigned long long t0 = gtimer();
+      while (!mbar_test(sc_full, 0) && gtimer() - t0 < 20ull * 1000 * 1000) {
+      }
+    }
+  } else if (warp == 5) {  // ---- MMA issuer ----
+    if (lane == 0 && nkb > 0) {
+      // kind::f16: D float32, A and B bf16, both K-major, N = p.N, M = 128
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+                             ((uint32_t)(BM >> 4) << 24);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        const uint32_t par = (uint32_t)((i / S) & 1);
+        if (!wait_phase(&raw_full[s], par, abort_, 2) || !wait_phase(&a_full[s], par, abort_, 3)) break;
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(sa(xtile + (size_t)s * N * 128));
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const uint64_t adesc = sw128_desc(sa(atile + (size_t)(s * NW + w) * BM * 128));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes per 16 columns inside the swizzle atom
+            mma_bf16(tmem + (uint32_t)(w * N), adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&freeb[s]);
+      }
+      mma_commit(acc_full);  // arrives once every MMA issued above has completed
+    }
+  } else {  // ---- warps 1-4: dequantise, then the epilogue ----
+    const int t = tid - 32;  // 0..127
+    // lane 0 waits and the warp follows its answer: warp-uniform control flow
+    auto wait_warp = [&](uint64_t* b, uint32_t par, int code) -> bool {
+      int r = 1;
+      if (lane == 0) r = wait_phase(b, par, abort_, code);
+      r = __shfl_sync(~0u, r, 0);
+      if (r) mbar_test(b, par);  // every lane observes the completed phase
+      return r != 0;
+    };
+    bool ok = nkb > 0 && wait_warp(sc_full, 0, 4);
+    for (int i = 0; ok && i < nkb; ++i) {
+      const int s = i % S;
+      if (!wait_warp(&raw_full[s], (uint32_t)((i / S) & 1), 5)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const uint8_t* rt = raw + (size_t)(s * NW + w) * BM * BK;
+        uint8_t* at = atile + (size_t)(s * NW + w) * BM * 128;
+        const uint16_t* sc = (const uint16_t*)(scales + (size_t)w * BM * p.sbox);
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int r = (t >> 2) + 32 * it, c = t & 3;  // row, 16-column chunk
+          uint4 q = *(const uint4*)(rt + r * BK + c * 16);
+          q.x ^= p.xor_mask;
+          q.y ^= p.xor_mask;
+          q.z ^= p.xor_mask;
+          q.w ^= p.xor_mask;
+          const int g = (k0 + i * BK + c * 16) / G;
+          const float sf = bf2f(sc[(size_t)r * (p.sbox >> 1) + (sdelta >> 1) + (g - gfirst)]);
+          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int8_t b0 = (int8_t)(qw[e] & 0xff), b1 = (int8_t)((qw[e] >> 8) & 0xff);
+            const int8_t b2 = (int8_t)((qw[e] >> 16) & 0xff), b3 = (int8_t)(qw[e] >> 24);
+            o[2 * e] = pack_bf16x2((float)b0 * sf, (float)b1 * sf);
+            o[2 * e + 1] = pack_bf16x2((float)b2 * sf, (float)b3 * sf);
+          }
+          // 16-byte chunk j of row r sits at chunk j ^ (r & 7) (128-byte swizzle)
+          *(uint4*)(at + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *(uint4*)(at + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+      fence_proxy_async();  // the tensor core reads these stores through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+    // ---- epilogue: warp quarter (warp % 4) owns TMEM lanes / tile rows 32q..32q+31 ----
+    ok = ok && wait_warp(acc_full, 0, 6);
+    if (!ok && lane == 0) *abort_ = 1;
+    bar_epi();  // the four warps take one decision
+    if (t == 0) *gof = *abort_ ? 0 : 1;
+    bar_epi();
+    ok = *gof != 0;
+    tc_fence_after();
+    const int q = warp & 3, row = 32 * q + lane, m = row0 + row;
+    const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+    auto finish = [&](int b, float a0, float a1) {
+      if (b >= p.nb || m >= p.M) return;
+      uint16_t* yo = (uint16_t*)p.y + (size_t)b * p.ld_y + m;
+      if (PAIR) {
+        *yo = f2bf(silu_tanh_bf16(rbf(a0)) * rbf(a1));
+      } else if (p.epi == EPI_RESID) {
+        *yo = f2bf(bf2f(p.res[(size_t)b * p.ld_y + m]) + rbf(a0));
+      } else if (p.epi == EPI_F32) {
+        ((float*)p.y)[(size_t)b * p.ld_y + m] = a0;
+      } else {
+        *yo = f2bf(a0);
+      }
+    };
+    if (ok) {
+      float* part = g_ws + ((size_t)(tile * p.splits + split) * NW * N) * BM;
+      for (int c0 = 0; c0 < N; c0 += 16) {
+        float v[16], u[16];
+        tmem_ld16(taddr + (uint32_t)c0, v);
+        if (PAIR) tmem_ld16(taddr + (uint32_t)(N + c0), u);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (p.splits == 1) {
+            finish(c0 + j, v[j], PAIR ? u[j] : 0.f);
+          } else {
+            part[(size_t)(c0 + j) * BM + row] = v[j];
+            if (PAIR) part[(size_t)(N + c0 + j) * BM + row] = u[j];
+          }
+        }
+      }
+      if (p.splits > 1) {
+        __threadfence();
+        bar_epi();
+        if (t == 0) *lastf = atomicAdd(&g_counters[tile], 1) == p.splits - 1;
+        bar_epi();
+        if (*lastf) {
+          __threadfence();
+          for (int b = 0; b < N; ++b) {
+            float a0 = 0.f, a1 = 0.f;
+            for (int s2 = 0; s2 < p.splits; ++s2) {
+              const float* pp = g_ws + ((size_t)(tile * p.splits + s2) * NW * N) * BM;
+              a0 += __ldcg(pp + (size_t)b * BM + row);
+              if (PAIR) a1 += __ldcg(pp + (size_t)(N + b) * BM + row);
+            }
+            finish(b, a0, a1);
+          }
+          if (t == 0) g_counters[tile] = 0;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    // MMAs may still run after an abort: wait (bounded) for the final commit first
+    const unsigned long long t0 = gtimer();
+    while (nkb > 0 && !mbar_test(acc_full, 0) && gtimer() - t0 < 20ull * 1000 * 1000) {
+    }
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.ncols) : "memory");
+  }
+}
+
+// rms-normalised activations for a batched launch: y[b] = bf16(RMSNorm_w(x[b])), the
+// prologue arithmetic of the GEMV kernels
+__global__ void rms_rows_kernel(const uint16_t* x, int ld_x, const uint16_t* w, int K, float eps, int mode,
+                                uint16_t* y) {
+  const int b = blockIdx.x;
+  const uint16_t* xr = x + (size_t)b * ld_x;
+  __shared__ double red[32];
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) ss += rms_sq(bf2f(xr[i]), mode);
+  ss = warp_sum_d(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const RmsCoef rc = rms_coef(red[0], K, eps, mode);
+  for (int i = threadIdx.x; i < K; i += blockDim.x)
+    y[(size_t)b * K + i] = f2bf(rms_apply(bf2f(xr[i]), bf2f(w[i]), rc));
+}
+
+__device__ uint16_t g_xnorm[256 * 16384];  // normalised activations of one launch
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)f;
+  }
+  return fn;
+}
+
+static bool map2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                  uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int G, bool PAIR>
+static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStream_t st) {
+  using namespace tc;
+  constexpr int NW = PAIR ? 2 : 1;
+  const int M = p.M, K = p.K, nb = p.nb;
+  const int N = (nb + 15) / 16 * 16;
+  const int tiles = (M + BM - 1) / BM;
+  const int kblocks = K / BK;
+  if (tiles > MAX_TILES) return 1;
+  // split K so that about one CTA per SM runs, at least 2 k-blocks per split
+  int splits = (iron_num_sms() + tiles - 1) / tiles;
+  if (splits > kblocks / 2) splits = kblocks / 2;
+  if (splits < 1) splits = 1;
+  int kbps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kbps - 1) / kbps;
+  while (splits > 1 && (size_t)tiles * splits * NW * N * BM > WS_FLOATS) {
+    kbps *= 2;
+    splits = (kblocks + kbps - 1) / kbps;
+  }
+  TcParams tp = {};
+  tp.M = M;
+  tp.K = K;
+  tp.N = N;
+  tp.nb = nb;
+  tp.splits = splits;
+  tp.kbps = kbps;
+  // scales of a split: from the 16-byte boundary at or below its first one
+  tp.sbox = ((17 + 2 * kbps * BK / G) + 15) / 16 * 16;
+  if (tp.sbox > 256) return 1;
+  int nc = 32;
+  while (nc < NW * N) nc *= 2;
+  if (nc > 512) return 1;
+  tp.ncols = nc;
+  tp.epi = p.epi;
+  tp.res = p.res;
+  tp.y = p.y;
+  tp.ld_y = p.ld_y;
+  tp.xor_mask = p.wa.xor_mask;
+  const int per_stage = NW * BM * 128 + N * 128 + NW * BM * BK;
+  const int fixed = NW * BM * tp.sbox + 1024 /* alignment slack */ + 256 /* barriers, flags */;
+  int S = (SMEM_MAX - fixed) / per_stage;
+  if (S > 6) S = 6;
+  if (S < 2) return 1;
+  tp.stages = S;
+  tp.off_a = 0;
+  tp.off_x = tp.off_a + S * NW * BM * 128;
+  tp.off_raw = tp.off_x + S * N * 128;
+  tp.off_scale = tp.off_raw + S * NW * BM * BK;
+  tp.off_bar = (tp.off_scale + NW * BM * tp.sbox + 15) / 16 * 16;
+  const size_t smem = (size_t)tp.off_bar + (3 * S + 2) * 8 + 16 + 1024;  // + tmem slot, flags; + alignment
+  const uint64_t RB = (uint64_t)K + 2 * (K / G);
+  CUtensorMap mr0, ms0, mr1, ms1, mx;
+  if (!map2d(&mr0, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wa.base, RB, M, RB, BK, BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !map2d(&ms0, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wa.base, RB, M, RB, tp.sbox, BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !map2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, nb, (uint64_t)ld_x * 2, BK, N,
+             CU_TENSOR_MAP_SWIZZLE_128B))
+    return 1;
+  mr1 = mr0;
+  ms1 = ms0;
+  if (PAIR && (!map2d(&mr1, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wb.base, RB, M, RB, BK, BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+               !map2d(&ms1, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wb.base, RB, M, RB, tp.sbox, BM,
+                      CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return 1;
+  auto fn = gemm_tc_kernel<G, PAIR>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+    attr[dev] = true;
+  }
+  fn<<<tiles * splits, NTH, smem, st>>>(tp, mr0, ms0, mr1, ms1, mx);
+  return iron_check_launch("gemm_tc_kernel");
+}
+
+// 0: launched (or a launch error < 0); 1: not handled (the caller runs the exact GEMV
+// in 8-row launches).  Plain wires, 16 <= batch <= 256, K a multiple of 64 and of
+// 8 * group, 16-byte aligned activations with rows a multiple of 8 elements apart.
+int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
+  using namespace tc;
+  if (p.nb < 16 || p.nb > 256 || !p.wa.plain1 || (pair && !p.wb.plain1)) return 1;
+  if (p.K % 64 || p.K % (8 * p.wa.G) || p.K > 16384) return 1;
+  if (!iron_aligned(p.wa.base, 16) || (pair && !iron_aligned(p.wb.base, 16))) return 1;
+  const uint16_t* x = p.x;
+  int ld_x = p.ld_x;
+  if (p.rms_w) {  // normalise first: the tensor-core kernel reads x through TMA
+    uint16_t* xn = nullptr;
+    if (cudaGetSymbolAddress((void**)&xn, g_xnorm) != cudaSuccess) return 1;
+    rms_rows_kernel<<<p.nb, 256, 0, st>>>(p.x, p.ld_x, p.rms_w, p.K, p.eps, p.rms_mode, xn);
+    int rc = iron_check_launch("rms_rows_kernel");
+    if (rc) return rc;
+    x = xn;
+    ld_x = p.K;
+  }
+  if (!iron_aligned(x, 16) || ld_x % 8) return 1;
+  switch (p.wa.G) {
+    case 32: return pair ? tc_launch<32, true>(p, x, ld_x, st) : tc_launch<32, false>(p, x, ld_x, st);
+    case 64: return pair ? tc_launch<64, true>(p, x, ld_x, st) : tc_launch<64, false>(p, x, ld_x, st);
+    case 128: return pair ? tc_launch<128, true>(p, x, ld_x, st) : tc_launch<128, false>(p, x, ld_x, st);
+  }
+  return 1;
+}
+
+}  // namespace iron
+
+using namespace iron;
+
+// Error word of the tensor-core projections on the current device: 0, or the code of
+// the first bounded wait that timed out.  clear != 0 resets it together with the
+// split-K arrival counters (an aborted launch can leave them mid-count).
+extern "C" int iron_tc_status(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int));
+    void* c = nullptr;
+    if (cudaGetSymbolAddress(&c, tc::g_counters) == cudaSuccess) cudaMemset(c, 0, sizeof(tc::g_counters));
+    cudaDeviceSynchronize();
+  }
+  return v;
+}

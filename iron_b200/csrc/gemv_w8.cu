@@ -262,11 +262,19 @@ int make_wire(Wire& w, const void* base, int M, int K, int group, int tile_m, in
 static int gemv_w8_launch_rows(GemvW8Params p, bool pair, cudaStream_t st);
 int gemv_mma_launch(const GemvW8Params& p, bool pair, cudaStream_t st);
 
-// Batches above 8 run as successive launches over 8 activation rows each (the weight
-// streams once per launch): the batch-8 kernel's arithmetic for every row.
+// Batches of 9..15 (and larger ones the tensor-core kernel does not take) run as
+// successive launches over 8 activation rows each (the weight streams once per
+// launch): the batch-8 kernel's arithmetic for every row.
+int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st);
+
 int gemv_w8_launch(GemvW8Params p, bool pair, cudaStream_t st) {
   IRON_REQUIRE(p.nb >= 1, IRON_ERR_UNSUPPORTED, "gemv_w8: batch %d below 1", p.nb);
   if (p.nb <= 8) return gemv_w8_launch_rows(p, pair, st);
+  // 16 streams and more: one tensor-core contraction that streams the weight once (gemm_tc.cu)
+  if (p.nb >= 16 && (!pair || p.wa.xor_mask == p.wb.xor_mask)) {
+    const int rc = gemm_tc_launch(p, pair, st);
+    if (rc <= 0) return rc;
+  }
   for (int b0 = 0; b0 < p.nb; b0 += 8) {
     const int rc = gemv_w8_launch_rows(gemv_rows(p, b0, p.nb - b0 < 8 ? p.nb - b0 : 8), pair, st);
     if (rc) return rc;

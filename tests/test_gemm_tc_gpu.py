@@ -1,0 +1,109 @@
+"""Batch >= 16 int8 projections on the tcgen05 tensor cores (csrc/gemm_tc.cu).
+
+The kernel dequantises each weight to bf16(q*s) and accumulates in float32 on the
+tensor core, so it is checked (a) tightly against the same bf16-dequantised weights
+in float64 (only the float32 summation order and the output rounding differ) and
+(b) against the exact dequantised sum (oracle.ops.gemv_int8_exact) within one bf16
+rounding of every weight -- the BASELINE bf16 tolerance.  Shapes cover split K,
+ragged row tiles, groups 64/128 (a split may start inside a group), the biased
+payload domain, the residual / float32 / gate-up + RMSNorm epilogues, and batches
+16..256."""
+
+import numpy as np
+import pytest
+import torch
+
+from iron_b200 import _lib
+from iron_b200.qwen3 import quantize_to_wire, wire_to_numpy
+from oracle import ops
+from oracle.bf16 import from_bits, rnd
+
+from helpers import host
+
+pytestmark = pytest.mark.gpu
+
+
+def _deq_bf16(q, s_bits, G):
+    return rnd(q.astype(np.float32) * np.repeat(from_bits(s_bits), G, axis=1)).astype(np.float64)
+
+
+def _check(out, q, s_bits, x, G, what):
+    x = np.asarray(x, np.float64)
+    w = _deq_bf16(q, s_bits, G)
+    want = x @ w.T
+    mag = np.abs(x) @ np.abs(w).T
+    lim = 2.0 ** -8 * np.abs(want) + 1e-5 * mag + 1e-30
+    err = np.abs(np.asarray(out, np.float64) - want)
+    assert np.all(err <= lim), f"{what}: vs bf16 weights, worst {np.max(err / lim):.3g}"
+    exact = ops.gemv_int8_exact(q, s_bits, x)
+    lim2 = 2.0 ** -8 * np.abs(exact) + 2.0 ** -8 * mag + 1e-30
+    err2 = np.abs(np.asarray(out, np.float64) - exact)
+    assert np.all(err2 <= lim2), f"{what}: vs exact, worst {np.max(err2 / lim2):.3g}"
+
+
+def _gemv(wire, M, K, G, domain, x, residual=None):
+    B = x.shape[0]
+    y = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_gemv_w8a16", wire.data_ptr(), M, K, G, 1, 0, 0, domain, x.data_ptr(), B,
+              None if residual is None else residual.data_ptr(), y.data_ptr(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    return y
+
+
+@pytest.mark.parametrize("M,K,G,B,domain", [(6144, 1024, 32, 32, 0), (12288, 4096, 32, 32, 0),
+                                            (4096, 12288, 32, 16, 0), (1000, 3072, 64, 20, 1),
+                                            (300, 2048, 128, 64, 0), (3072, 1024, 32, 256, 0),
+                                            (1024, 3072, 32, 33, 0)])
+def test_tc_projection_matches_dequantised_reference(M, K, G, B, domain):
+    assert _lib.lib().iron_tc_status(1) == 0
+    torch.manual_seed(M + K + B)
+    w = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    wire = quantize_to_wire(w, G, domain=domain)
+    q, s = wire_to_numpy(quantize_to_wire(w, G, domain=0), M, K, G)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    y1 = _gemv(wire, M, K, G, domain, x)
+    y2 = _gemv(wire, M, K, G, domain, x)
+    assert _lib.lib().iron_tc_status(0) == 0
+    assert torch.equal(y1, y2), "not deterministic"
+    _check(host(y1), q, s, host(x), G, f"{M}x{K} g{G} b{B}")
+
+
+def test_tc_residual_f32_and_gate_up_rms_epilogues():
+    torch.manual_seed(5)
+    M, K, G, B = 3072, 1024, 32, 24
+    wg = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    wu = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    qg, sg = wire_to_numpy(quantize_to_wire(wg, G), M, K, G)
+    qu, su = wire_to_numpy(quantize_to_wire(wu, G), M, K, G)
+    gw, uw = quantize_to_wire(wg, G), quantize_to_wire(wu, G)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    r = torch.randn(B, M, device="cuda").to(torch.bfloat16)
+    st = _lib.stream_ptr()
+    # residual: y = bf16(r + bf16(sum))
+    y = _gemv(gw, M, K, G, 0, x, r)
+    base = host(_gemv(gw, M, K, G, 0, x))
+    want = rnd(host(r) + base)
+    assert np.array_equal(host(y), want)
+    # float32 partial sums (epilogue 2) round to the bf16 result
+    y32 = torch.empty(B, M, dtype=torch.float32, device="cuda")
+    _lib.call("iron_gemv_w8a16_ex", gw.data_ptr(), None, M, K, G, 0, x.data_ptr(), K, B, None, 0.0, 0, None, 2,
+              y32.data_ptr(), M, st)
+    torch.cuda.synchronize()
+    assert np.array_equal(rnd(host(y32)), base)
+    _check(host(y32), qg, sg, host(x), G, "f32 epilogue")
+    # gate/up pair with the RMSNorm prologue: bf16(silu_tanh(bf16(Wg h)) * bf16(Wu h))
+    nw = (1 + 0.1 * torch.randn(K, device="cuda")).to(torch.bfloat16)
+    gh = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_gemv_w8a16_ex", gw.data_ptr(), uw.data_ptr(), M, K, G, 0, x.data_ptr(), K, B, nw.data_ptr(),
+              1e-6, 0, None, 0, gh.data_ptr(), M, st)
+    torch.cuda.synchronize()
+    assert _lib.lib().iron_tc_status(0) == 0
+    h = ops.rms_norm_f32(host(x), host(nw), 1e-6)
+    g = rnd(h.astype(np.float64) @ _deq_bf16(qg, sg, G).T)
+    u = rnd(h.astype(np.float64) @ _deq_bf16(qu, su, G).T)
+    want = rnd(ops.silu_tanh_bf16(g) * u)
+    got = host(gh)
+    # one bf16 step of g or u (float32 summation order) moves an output by ~2 ulps
+    err = np.abs(got - want)
+    lim = 2.0 ** -6 * np.abs(want) + 1e-4
+    assert np.mean(err <= lim) >= 0.999 and np.max(err) <= 0.05, f"pair: {np.mean(err <= lim):.4f}, max {err.max()}"

@@ -8,10 +8,11 @@
 //     128-row tile (box 64 x 128, no swizzle) and the activations (box 64 x N bf16,
 //     128-byte swizzle, rows past the batch zero-filled), plus the tile's group
 //     scales for its whole K range once;
-//   - warps 1-4 dequantise the tile into bf16 w = bf16(q * s) straight into the
+//   - warps 1-8 dequantise the tile into bf16 w = bf16(q * s) straight into the
 //     128-byte-swizzled K-major layout the tensor core reads, and after the last
-//     k-block run the epilogue (each warp owns one 32-lane quarter of TMEM);
-//   - warp 5 allocates TMEM (N float32 columns per output tile, 2N for a gate/up
+//     k-block run the epilogue (warp w reads TMEM lane quarter w % 4, half of the
+//     columns each);
+//   - warp 9 allocates TMEM (N float32 columns per output tile, 2N for a gate/up
 //     pair), one lane issues tcgen05.mma (M = 128, N = batch padded to 16, K = 16 per
 //     instruction, bf16 x bf16 -> f32) and commits each k-block's MMAs to the stage's
 //     mbarrier, which frees the stage for the next copies.
@@ -39,8 +40,11 @@ namespace tc {
 
 constexpr int BM = 128;         // weight rows per tile (the MMA's M)
 constexpr int BK = 64;          // k per stage: one 128-byte swizzled bf16 row
-constexpr int NTH = 192;        // warp 0 TMA, warps 1-4 dequant + epilogue, warp 5 MMA
+constexpr int NDQ = 8;          // dequantising / epilogue warps (1..8)
+constexpr int NTH = 32 * (NDQ + 2);  // warp 0 TMA, warps 1..NDQ dequant + epilogue, warp NDQ+1 MMA
+constexpr int MMA_WARP = NDQ + 1;
 constexpr int SMEM_MAX = 227 * 1024;
+constexpr int SMEM_CTA = 113 * 1024;  // two CTAs per SM
 constexpr size_t WS_FLOATS = 4u << 20;  // 16 MB of split-K partials
 constexpr int MAX_TILES = 4096;
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;
@@ -144,17 +148,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void bar_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * NDQ) : "memory"); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
 }
 
-template <int G, bool PAIR>
-__global__ void __launch_bounds__(NTH, 1)
+// W16: the weight is bf16 already (the tied lm_head, bf16 GEMVs): TMA writes its
+// tiles in the swizzled layout directly and warps 1-4 only run the epilogue.
+template <int G, bool PAIR, bool W16>
+__global__ void __launch_bounds__(NTH, 2)
     gemm_tc_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap tm_raw0,
                    const __grid_constant__ CUtensorMap tm_sc0, const __grid_constant__ CUtensorMap tm_raw1,
                    const __grid_constant__ CUtensorMap tm_sc1, const __grid_constant__ CUtensorMap tm_x) {
+  static_assert(!(W16 && PAIR), "bf16 weights: single projections only");
   constexpr int NW = PAIR ? 2 : 1;
   extern __shared__ uint8_t sm_dyn[];
   // 1024-byte alignment for the swizzled tiles (the launch adds 1 KB of slack)
@@ -187,7 +194,7 @@ __global__ void __launch_bounds__(NTH, 1)
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&a_full[i], 4);
+      mbar_init(&a_full[i], NDQ);
       mbar_init(&freeb[i], 1);
     }
     mbar_init(sc_full, 1);
@@ -197,7 +204,7 @@ __global__ void __launch_bounds__(NTH, 1)
     *lastf = 0;
     *gof = 0;
   }
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
                  "r"(p.ncols)
                  : "memory");
@@ -211,17 +218,24 @@ __global__ void __launch_bounds__(NTH, 1)
   if (warp == 0) {  // ---- TMA producer ----
     int issued = 0;
     if (lane == 0 && nkb > 0) {
-      const int xs = p.K + 2 * gfirst - sdelta;
-      mbar_expect(sc_full, (uint32_t)(NW * BM * p.sbox));
-      tma_2d(scales, &tm_sc0, xs, row0, sc_full);
-      if (PAIR) tma_2d(scales + BM * p.sbox, &tm_sc1, xs, row0, sc_full);
+      if (!W16) {
+        const int xs = p.K + 2 * gfirst - sdelta;
+        mbar_expect(sc_full, (uint32_t)(NW * BM * p.sbox));
+        tma_2d(scales, &tm_sc0, xs, row0, sc_full);
+        if (PAIR) tma_2d(scales + BM * p.sbox, &tm_sc1, xs, row0, sc_full);
+      }
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         if (i >= S && !wait_phase(&freeb[s], (uint32_t)((i / S - 1) & 1), abort_, 1)) break;
-        mbar_expect(&raw_full[s], (uint32_t)(NW * BM * BK + N * 128));
         const int kx = k0 + i * BK;
-        tma_2d(raw + (size_t)(s * NW) * BM * BK, &tm_raw0, kx, row0, &raw_full[s]);
-        if (PAIR) tma_2d(raw + (size_t)(s * NW + 1) * BM * BK, &tm_raw1, kx, row0, &raw_full[s]);
+        if (W16) {
+          mbar_expect(&raw_full[s], (uint32_t)(BM * 128 + N * 128));
+          tma_2d(atile + (size_t)s * BM * 128, &tm_raw0, kx, row0, &raw_full[s]);
+        } else {
+          mbar_expect(&raw_full[s], (uint32_t)(NW * BM * BK + N * 128));
+          tma_2d(raw + (size_t)(s * NW) * BM * BK, &tm_raw0, kx, row0, &raw_full[s]);
+          if (PAIR) tma_2d(raw + (size_t)(s * NW + 1) * BM * BK, &tm_raw1, kx, row0, &raw_full[s]);
+        }
         tma_2d(xtile + (size_t)s * N * 128, &tm_x, kx, 0, &raw_full[s]);
         issued = i + 1;
       }
@@ -232,10 +246,10 @@ __global__ void __launch_bounds__(NTH, 1)
         }
       }
       const unsigned long long t0 = gtimer();
-      while (!mbar_test(sc_full, 0) && gtimer() - t0 < 20ull * 1000 * 1000) {
+      while (!W16 && !mbar_test(sc_full, 0) && gtimer() - t0 < 20ull * 1000 * 1000) {
       }
     }
-  } else if (warp == 5) {  // ---- MMA issuer ----
+  } else if (warp == MMA_WARP) {  // ---- MMA issuer ----
     if (lane == 0 && nkb > 0) {
       // kind::f16: D float32, A and B bf16, both K-major, N = p.N, M = 128
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(NTH, 1)
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t par = (uint32_t)((i / S) & 1);
-        if (!wait_phase(&raw_full[s], par, abort_, 2) || !wait_phase(&a_full[s], par, abort_, 3)) break;
+        if (!wait_phase(&raw_full[s], par, abort_, 2) || (!W16 && !wait_phase(&a_full[s], par, abort_, 3))) break;
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(sa(xtile + (size_t)s * N * 128));
 #pragma unroll
@@ -258,8 +272,8 @@ __global__ void __launch_bounds__(NTH, 1)
       }
       mma_commit(acc_full);  // arrives once every MMA issued above has completed
     }
-  } else {  // ---- warps 1-4: dequantise, then the epilogue ----
-    const int t = tid - 32;  // 0..127
+  } else {  // ---- warps 1..NDQ: dequantise, then the epilogue ----
+    const int t = tid - 32;  // 0 .. 32 * NDQ - 1
     // lane 0 waits and the warp follows its answer: warp-uniform control flow
     auto wait_warp = [&](uint64_t* b, uint32_t par, int code) -> bool {
       int r = 1;
@@ -268,8 +282,8 @@ __global__ void __launch_bounds__(NTH, 1)
       if (r) mbar_test(b, par);  // every lane observes the completed phase
       return r != 0;
     };
-    bool ok = nkb > 0 && wait_warp(sc_full, 0, 4);
-    for (int i = 0; ok && i < nkb; ++i) {
+    bool ok = nkb > 0 && (W16 || wait_warp(sc_full, 0, 4));
+    for (int i = 0; !W16 && ok && i < nkb; ++i) {
       const int s = i % S;
       if (!wait_warp(&raw_full[s], (uint32_t)((i / S) & 1), 5)) {
         ok = false;
@@ -281,8 +295,8 @@ __global__ void __launch_bounds__(NTH, 1)
         uint8_t* at = atile + (size_t)(s * NW + w) * BM * 128;
         const uint16_t* sc = (const uint16_t*)(scales + (size_t)w * BM * p.sbox);
 #pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int r = (t >> 2) + 32 * it, c = t & 3;  // row, 16-column chunk
+        for (int it = 0; it < 4 * 4 / NDQ; ++it) {
+          const int r = (t >> 2) + 8 * NDQ * it, c = t & 3;  // row, 16-column chunk
           uint4 q = *(const uint4*)(rt + r * BK + c * 16);
           q.x ^= p.xor_mask;
           q.y ^= p.xor_mask;
@@ -308,15 +322,17 @@ __global__ void __launch_bounds__(NTH, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[s]);
     }
-    // ---- epilogue: warp quarter (warp % 4) owns TMEM lanes / tile rows 32q..32q+31 ----
+    // ---- epilogue: warp w owns TMEM lane quarter w % 4 (tile rows 32q..32q+31) and
+    // the column half (w - 1) / 4 ----
     ok = ok && wait_warp(acc_full, 0, 6);
     if (!ok && lane == 0) *abort_ = 1;
-    bar_epi();  // the four warps take one decision
+    bar_epi();  // the epilogue warps take one decision
     if (t == 0) *gof = *abort_ ? 0 : 1;
     bar_epi();
     ok = *gof != 0;
     tc_fence_after();
     const int q = warp & 3, row = 32 * q + lane, m = row0 + row;
+    const int half = (warp - 1) / 4;  // columns [half * N/2, (half + 1) * N/2) in 16-column steps
     const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
     auto finish = [&](int b, float a0, float a1) {
       if (b >= p.nb || m >= p.M) return;
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(NTH, 1)
     };
     if (ok) {
       float* part = g_ws + ((size_t)(tile * p.splits + split) * NW * N) * BM;
-      for (int c0 = 0; c0 < N; c0 += 16) {
+      for (int c0 = 16 * half; c0 < N; c0 += 32) {
         float v[16], u[16];
         tmem_ld16(taddr + (uint32_t)c0, v);
         if (PAIR) tmem_ld16(taddr + (uint32_t)(N + c0), u);
@@ -354,7 +370,7 @@ __global__ void __launch_bounds__(NTH, 1)
         bar_epi();
         if (*lastf) {
           __threadfence();
-          for (int b = 0; b < N; ++b) {
+          for (int b = half; b < N; b += 2) {
             float a0 = 0.f, a1 = 0.f;
             for (int s2 = 0; s2 < p.splits; ++s2) {
               const float* pp = g_ws + ((size_t)(tile * p.splits + s2) * NW * N) * BM;
@@ -370,7 +386,7 @@ __global__ void __launch_bounds__(NTH, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     // MMAs may still run after an abort: wait (bounded) for the final commit first
     const unsigned long long t0 = gtimer();
     while (nkb > 0 && !mbar_test(acc_full, 0) && gtimer() - t0 < 20ull * 1000 * 1000) {
@@ -450,8 +466,8 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   const int tiles = (M + BM - 1) / BM;
   const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
-  // split K so that about one CTA per SM runs, at least 2 k-blocks per split
-  int splits = (iron_num_sms() + tiles - 1) / tiles;
+  // split K so that the CTAs make about one wave (two per SM), at least 2 k-blocks per split
+  int splits = 2 * iron_num_sms() / tiles;
   if (splits > kblocks / 2) splits = kblocks / 2;
   if (splits < 1) splits = 1;
   int kbps = (kblocks + splits - 1) / splits;
@@ -481,7 +497,8 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   tp.xor_mask = p.wa.xor_mask;
   const int per_stage = NW * BM * 128 + N * 128 + NW * BM * BK;
   const int fixed = NW * BM * tp.sbox + 1024 /* alignment slack */ + 256 /* barriers, flags */;
-  int S = (SMEM_MAX - fixed) / per_stage;
+  int S = (SMEM_CTA - fixed) / per_stage;
+  if (S < 2) S = (SMEM_MAX - fixed) / per_stage;  // large batches: one CTA per SM
   if (S > 6) S = 6;
   if (S < 2) return 1;
   tp.stages = S;
@@ -504,7 +521,7 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
                !map2d(&ms1, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wb.base, RB, M, RB, tp.sbox, BM,
                       CU_TENSOR_MAP_SWIZZLE_NONE)))
     return 1;
-  auto fn = gemm_tc_kernel<G, PAIR>;
+  auto fn = gemm_tc_kernel<G, PAIR, false>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -513,6 +530,66 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
     attr[dev] = true;
   }
   fn<<<tiles * splits, NTH, smem, st>>>(tp, mr0, ms0, mr1, ms1, mx);
+  return iron_check_launch("gemm_tc_kernel");
+}
+
+// bf16 weights: y[b, m] = bf16(sum_k A[m, k] x[b, k]), float32 accumulation.
+int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int ld_x, int nb, uint16_t* y,
+                        int ld_y, cudaStream_t st) {
+  using namespace tc;
+  if (nb < 16 || nb > 256 || K % 64 || !iron_aligned(A, 16) || !iron_aligned(x, 16) || ld_x % 8) return 1;
+  const int N = (nb + 15) / 16 * 16;
+  const int tiles = (M + BM - 1) / BM;
+  const int kblocks = K / BK;
+  if (tiles > MAX_TILES) return 1;
+  int splits = 2 * iron_num_sms() / tiles;
+  if (splits > kblocks / 2) splits = kblocks / 2;
+  if (splits < 1) splits = 1;
+  int kbps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kbps - 1) / kbps;
+  while (splits > 1 && (size_t)tiles * splits * N * BM > WS_FLOATS) {
+    kbps *= 2;
+    splits = (kblocks + kbps - 1) / kbps;
+  }
+  TcParams tp = {};
+  tp.M = M;
+  tp.K = K;
+  tp.N = N;
+  tp.nb = nb;
+  tp.splits = splits;
+  tp.kbps = kbps;
+  tp.sbox = 0;
+  int nc = 32;
+  while (nc < N) nc *= 2;
+  tp.ncols = nc;
+  tp.epi = EPI_STORE;
+  tp.y = y;
+  tp.ld_y = ld_y;
+  const int per_stage = BM * 128 + N * 128;
+  int S = (SMEM_CTA - 1024 - 256) / per_stage;
+  if (S < 2) S = (SMEM_MAX - 1024 - 256) / per_stage;
+  if (S > 6) S = 6;
+  if (S < 2) return 1;
+  tp.stages = S;
+  tp.off_a = 0;
+  tp.off_x = S * BM * 128;
+  tp.off_raw = tp.off_x + S * N * 128;
+  tp.off_scale = tp.off_raw;
+  tp.off_bar = tp.off_scale;
+  const size_t smem = (size_t)tp.off_bar + (3 * S + 2) * 8 + 16 + 1024;
+  CUtensorMap ma, mx;
+  if (!map2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, K, M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !map2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, nb, (uint64_t)ld_x * 2, BK, N, CU_TENSOR_MAP_SWIZZLE_128B))
+    return 1;
+  auto fn = gemm_tc_kernel<32, false, true>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+    attr[dev] = true;
+  }
+  fn<<<tiles * splits, NTH, smem, st>>>(tp, ma, ma, ma, ma, mx);
   return iron_check_launch("gemm_tc_kernel");
 }
 

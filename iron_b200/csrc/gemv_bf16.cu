@@ -290,6 +290,12 @@ static int gemv_bf16_dispatch(GemvBf16Params p, cudaStream_t st) {
   return rc ? rc : grid;
 }
 
+int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int ld_x, int nb, uint16_t* y,
+                        int ld_y, cudaStream_t st);
+
+// logits of a batched lm_head whose caller keeps none (batch x vocab <= 8 M values)
+__device__ uint16_t g_lm_logits[8u << 20];
+
 }  // namespace iron
 
 using namespace iron;
@@ -302,6 +308,11 @@ extern "C" int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x
                               int independent, uint16_t* y, void* stream) {
   IRON_REQUIRE(y != nullptr, IRON_ERR_ARG, "gemv_bf16: null output");
   IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "gemv_bf16: batch %d below 1", batch);
+  // 16+ rows of a shared weight: one tensor-core contraction (gemm_tc.cu)
+  if (!independent && batch >= 16) {
+    const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, y, M, (cudaStream_t)stream);
+    if (rc <= 0) return rc;
+  }
   // a shared weight with more than 8 activation rows: launches over 8 rows each
   const int step = independent ? batch : 8;
   for (int b0 = 0; b0 < batch; b0 += step) {
@@ -325,6 +336,18 @@ extern "C" int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const u
   IRON_REQUIRE(workspace && token_out, IRON_ERR_ARG, "lm_head_argmax: null workspace/token_out");
   IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "lm_head_argmax: batch %d below 1", batch);
   cudaStream_t st = (cudaStream_t)stream;
+  // 16+ rows: the logits from one tensor-core contraction, then the argmax passes
+  if (batch >= 16) {
+    uint16_t* L = logits;
+    if (!L && (size_t)batch * M <= (8u << 20) &&
+        cudaGetSymbolAddress((void**)&L, g_lm_logits) != cudaSuccess)
+      L = nullptr;
+    if (L) {
+      const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, L, M, st);
+      if (rc < 0) return rc;
+      if (rc == 0) return iron_argmax_bf16(L, M, batch, token_out, workspace, stream);
+    }
+  }
   // up to 8 activation rows per launch; rows b0.. use the workspace's candidate slots
   // from b0 * kMaxCand on
   for (int b0 = 0; b0 < batch; b0 += 8) {

@@ -62,15 +62,16 @@ def _timed(fns, reps: int) -> float:
 CAPTURE_CASES = [(6144, 1024, 8), (1024, 3072, 8), (6144, 1024, 1)]
 
 
-def capture_case():
-    """The small case of an ncu capture of the GEMV kernel: for each of CAPTURE_CASES
+def capture_case(shapes=None):
+    """The small case of an ncu capture of the GEMV kernel: for each case (N, K, batch)
     ~300 MB of weight copies, each run once (the launches ``ncu --launch-skip`` passes
     over), then one launch per case on a copy that has left the L2."""
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     st = torch.cuda.current_stream().cuda_stream
     cases, warm = [], 0
-    for N, K, B in CAPTURE_CASES:
+    shapes = shapes or CAPTURE_CASES
+    for N, K, B in shapes:
         w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)
         ws = [w0] + [w0.clone() for _ in range(max(1, 300 * 2**20 // (N * K)) - 1)]
         x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
@@ -88,17 +89,19 @@ def capture_case():
     for N, K, B, ws, x, y in cases:
         run(N, K, B, ws[0], x, y)
     torch.cuda.synchronize()
-    print(f"warm-up launches: {warm}; then one launch each of {CAPTURE_CASES}")
+    print(f"warm-up launches: {warm}; then one launch each of {shapes}")
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=50)
     ap.add_argument("--json", type=str, default=None)
-    ap.add_argument("--capture", action="store_true", help="run only the small ncu capture case of the GEMV")
+    ap.add_argument("--capture", nargs="?", const="", default=None,
+                    help="run only the small ncu capture case of the GEMV (optional NxKxB,NxKxB,... shapes)")
     args = ap.parse_args()
-    if args.capture:
-        capture_case()
+    if args.capture is not None:
+        shapes = [tuple(int(v) for v in c.split("x")) for c in args.capture.split(",") if c]
+        capture_case(shapes or None)
         return
     root = Path(__file__).resolve().parents[1]
     peaks = root / "MEASURED_PEAKS.json"

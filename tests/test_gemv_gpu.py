@@ -187,7 +187,7 @@ def test_bf16_gemv_independent_batches():
         assert_ulps(host(y[b]), ops.gemv_bf16(host(A[b]), host(x[b])), max_ulp=1, what=f"batch {b}")
 
 
-@pytest.mark.parametrize("batch", [1, 3, 11])
+@pytest.mark.parametrize("batch", [1, 3, 11, 16, 40])
 def test_lm_head_bf16_argmax(batch):
     """Fused lm_head + argmax over the Qwen3 vocabulary; ties resolve to the lowest index."""
     torch.manual_seed(11)
@@ -208,3 +208,22 @@ def test_lm_head_bf16_argmax(batch):
     assert int(tok[0]) == 777
     want = ops.gemv_bf16(host(E)[:4096], host(x)[0])
     assert_ulps(lg[0][:4096], want, max_ulp=1, frac_exact=0.95, what="logits")
+    if batch >= 16:  # the tensor-core path with no logits buffer gives the same tokens
+        tok2 = torch.empty(batch, dtype=torch.int32, device="cuda")
+        _lib.call("iron_lm_head_bf16_argmax", E.data_ptr(), V, D, x.data_ptr(), batch, None, tok2.data_ptr(),
+                  ws.data_ptr(), _lib.stream_ptr())
+        torch.cuda.synchronize()
+        assert torch.equal(tok, tok2)
+        assert _lib.lib().iron_tc_status(0) == 0
+
+
+def test_bf16_gemv_shared_weight_batch32_tensor_cores():
+    torch.manual_seed(12)
+    M, K, B = 4096, 1024, 32
+    A = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    y = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_gemv_bf16", A.data_ptr(), M, K, x.data_ptr(), B, 0, y.data_ptr(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    for b in (0, 13, 31):
+        assert_ulps(host(y[b]), ops.gemv_bf16(host(A), host(x[b])), max_ulp=1, frac_exact=0.95, what=f"row {b}")

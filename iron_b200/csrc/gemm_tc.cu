@@ -298,20 +298,21 @@ __global__ void __launch_bounds__(NTH, 2)
         for (int it = 0; it < 4 * 4 / NDQ; ++it) {
           const int r = (t >> 2) + 8 * NDQ * it, c = t & 3;  // row, 16-column chunk
           uint4 q = *(const uint4*)(rt + r * BK + c * 16);
-          q.x ^= p.xor_mask;
-          q.y ^= p.xor_mask;
-          q.z ^= p.xor_mask;
-          q.w ^= p.xor_mask;
+          // signed payload byte b -> b + 128 (the biased domain is already b + 128)
+          const uint32_t flip = p.xor_mask ^ 0x80808080u;
+          const uint32_t qw[4] = {q.x ^ flip, q.y ^ flip, q.z ^ flip, q.w ^ flip};
           const int g = (k0 + i * BK + c * 16) / G;
           const float sf = bf2f(sc[(size_t)r * (p.sbox >> 1) + (sdelta >> 1) + (g - gfirst)]);
-          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
           uint32_t o[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int8_t b0 = (int8_t)(qw[e] & 0xff), b1 = (int8_t)((qw[e] >> 8) & 0xff);
-            const int8_t b2 = (int8_t)((qw[e] >> 16) & 0xff), b3 = (int8_t)(qw[e] >> 24);
-            o[2 * e] = pack_bf16x2((float)b0 * sf, (float)b1 * sf);
-            o[2 * e + 1] = pack_bf16x2((float)b2 * sf, (float)b3 * sf);
+            // the float 2^23 + (b + 128) from one byte permute, minus 2^23 + 128: exactly b
+            float f[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              f[j] = __uint_as_float(__byte_perm(qw[e], 0x4B000000u, 0x7440u | (uint32_t)j)) - 8388736.0f;
+            o[2 * e] = pack_bf16x2(f[0] * sf, f[1] * sf);
+            o[2 * e + 1] = pack_bf16x2(f[2] * sf, f[3] * sf);
           }
           // 16-byte chunk j of row r sits at chunk j ^ (r & 7) (128-byte swizzle)
           *(uint4*)(at + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -466,9 +467,11 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   const int tiles = (M + BM - 1) / BM;
   const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
-  // split K so that the CTAs make about one wave (two per SM), at least 2 k-blocks per split
+  // split K so that the CTAs make about one wave (two per SM), at least 4 k-blocks per
+  // split (a shorter split is mostly start-up, and every split adds a partial tile to
+  // the last CTA's reduction)
   int splits = 2 * iron_num_sms() / tiles;
-  if (splits > kblocks / 2) splits = kblocks / 2;
+  if (splits > kblocks / 4) splits = kblocks / 4;
   if (splits < 1) splits = 1;
   int kbps = (kblocks + splits - 1) / splits;
   splits = (kblocks + kbps - 1) / kbps;
@@ -543,7 +546,7 @@ int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int 
   const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
   int splits = 2 * iron_num_sms() / tiles;
-  if (splits > kblocks / 2) splits = kblocks / 2;
+  if (splits > kblocks / 4) splits = kblocks / 4;
   if (splits < 1) splits = 1;
   int kbps = (kblocks + splits - 1) / splits;
   splits = (kblocks + kbps - 1) / kbps;

@@ -58,14 +58,18 @@ def parse():
     ap.add_argument("--batch", type=int, default=1,
                     help="independent decode streams per GPU (1: the one-launch step; more: the chained "
                          "kernels as a CUDA graph)")
-    ap.add_argument("--model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b",
+    ap.add_argument("--model", choices=["qwen3-0.6b", "qwen3-8b", "llama-1b"], default="qwen3-0.6b",
                     help="qwen3-8b: BASELINE config 4, tensor parallel over the torchrun world "
-                         "(NCCL), a synthetic --prompt-position KV context (default 4096)")
+                         "(NCCL), a synthetic --prompt-position KV context (default 4096); llama-1b: "
+                         "config 5, --batch streams per GPU (default 64) with ragged synthetic KV "
+                         "lengths U[256, 8192], replicas across GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
     args = ap.parse_args()
     if args.model == "qwen3-8b" and args.prompt == PROMPT:
         args.prompt = 4096
+    if args.model == "llama-1b" and args.batch == 1:
+        args.batch = 64
     return args
 
 
@@ -488,6 +492,123 @@ def run_tp(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def llama_step_bytes(cfg, lens):
+    """Algorithmic HBM bytes of one batched Llama decode step: every bf16 weight and the
+    tied lm_head once, each stream's K/V of its positions read and the new one
+    written, the activations in and out of each projection."""
+    D, FF, HD = cfg.D, cfg.FF, cfg.HD
+    weights = (cfg.QKV * D + D * cfg.QD + 3 * FF * D) * 2 + 2 * D * 2
+    kv = sum(2 * cfg.Hkv * HD * 2 * (n + 1) for n in lens)
+    acts = len(lens) * (D + cfg.QKV + 2 * cfg.QD + 3 * D + 4 * FF) * 2
+    return cfg.n_layers * weights + cfg.n_layers * (kv + acts) + cfg.V * D * 2 + D * 2
+
+
+def run_llama(args, rank, world, local_rank):
+    """Llama-3.2-1B-shaped bf16 decode, --batch independent streams per
+    GPU (64 by default) whose K/V lengths are drawn uniform in [256, 8192] (seeded per
+    rank) over a synthetic N(0, 1) cache; replicas across the torchrun world."""
+    import numpy as np
+    import torch
+    from iron_b200.llama import LlamaB200, LlamaConfig, LlamaWeights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = LlamaConfig.llama_3_2_1b()
+    K, W, B = args.steps, args.warmup, args.batch
+    rng = np.random.default_rng(args.seed + 31 * rank)
+    lens = [int(v) for v in rng.integers(256, 8193, B)]
+    max_seq = (max(lens) + W + 2 * K + 8 + 63) // 64 * 64
+    w = LlamaWeights.synthetic(cfg, seed=args.seed, device=dev)
+    dec = LlamaB200(w, max_seq=max_seq, batch=B, device=dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 17 + rank)
+    dec.kv.normal_(generator=g)
+    dec.set_positions(lens)
+    first = torch.randint(0, cfg.V, (B,), generator=torch.Generator().manual_seed(args.seed + 1))
+    with torch.cuda.stream(dec.stream):
+        dec.tok.copy_(first.to(dev, torch.int32))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                          if "CUDA_VISIBLE_DEVICES" in os.environ and world == 1 else local_rank)
+    clocks.start()
+    for _ in range(W):
+        dec.run_step(advance=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(dec.stream)
+    for _ in range(K):
+        dec.run_step(advance=True)
+    e1.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    pos = [n + W + K for n in lens]
+    toks = [int(t) for t in dec.tok.cpu()]
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e2.record(dec.stream)
+    for _ in range(K):
+        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        pos = [p + 1 for p in pos]
+    e3.record(dec.stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2.elapsed_time(e3)
+    clocks.stop()
+    clk = clocks.summary()
+    t_ms, e2e_ms, value, e2e = aggregate_replicas(t_ms, e2e_ms, K * B, world, dev)
+    if rank != 0:
+        return
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    step_bytes = sum(llama_step_bytes(cfg, [n + W + i for n in lens]) for i in range(K)) / K
+    achieved = step_bytes / (t_ms / K / 1000.0) / 1e9
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"llama-3.2-1b-shaped bf16 greedy decode, {B} streams per GPU, ragged "
+                                   f"synthetic N(0,1) KV lengths U[256, 8192] (mean {sum(lens) / B:.0f})",
+                       "batch_per_gpu": B, "layers": 16, "hidden": 2048, "vocab": 128256,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "no flush: ~11 GB streamed per step per GPU, larger than the L2"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": K * dec.launches_per_step(),
+            "roofline": {"bound": "hbm", "kernel": f"the chained kernels of one step ({dec.launches_per_step()} "
+                                                   f"launches)",
+                         "bytes_per_launch": step_bytes, "achieved": achieved, "peak": peak,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+            "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import ops
+        from oracle.llama import LlamaShape, OracleLlama, linear
+        threads = ops.set_threads(len(os.sched_getaffinity(0)))
+        wn = w.to_numpy(n_layers=1)
+        n = lens[0]
+        orc = OracleLlama(LlamaShape(n_layers=1), wn, n + 1, angles=dec.angles[:n + 1].float().cpu().numpy())
+        orc.kv[0] = dec.kv[0, 0].float().cpu().numpy().reshape(cfg.Hkv, max_seq, 2, cfg.HD)[:, :n + 1]
+        x = wn["embed"][int(first[0])]
+        t0 = time.perf_counter()
+        orc.layer(0, x, n)
+        t_layer = time.perf_counter() - t0
+        rows = cfg.V // 16
+        t0 = time.perf_counter()
+        linear(wn["embed"][:rows], x)
+        t_head = (time.perf_counter() - t0) * 16
+        tps = 1.0 / (cfg.n_layers * t_layer + t_head)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"one stream: one decoder layer of the numpy oracle (llama_cpu.py "
+                                          f"restated) at position {n} (x 16) + the lm_head on 1/16 of its rows "
+                                          f"(x 16), this run's weights and K/V"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -506,6 +627,8 @@ def main():
     try:
         if args.model == "qwen3-8b":
             run_tp(args, rank, world, local_rank)
+        elif args.model == "llama-1b":
+            run_llama(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

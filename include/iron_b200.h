@@ -115,6 +115,12 @@ int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, in
 int iron_add(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream);
 /* c = bf16(a * b)   (iron/operators/elementwise_mul/op.py, aie_kernels/generic/mul.cc) */
 int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream);
+/* RoPE (two halves, interleaved [cos, sin] rows of ang_table, row = position) of the
+ * q and k heads of raw (batch, (Hq + 2 Hkv) HD) and the K/V cache write at each
+ * stream's element offset kv_off_dev[b] (per-token [K_t | V_t] layout), without the
+ * per-head norms of iron_qkv_head: the Llama path (llama_cpu.py:14-38, 94-115). */
+int iron_rope_kv(const uint16_t* raw, const uint16_t* ang_table, uint16_t* q_out, uint16_t* kv_cache, int HD,
+                 int Hq, int Hkv, int max_seq, int batch, const int32_t* kv_off_dev, void* stream);
 /* y = bf16(silu(x)); mode 0: x*sigmoid(x) in f32 (silu/reference.py:8-10),
  * mode 1: the tanh form with bf16 roundings (aie_kernels/aie2p/silu.cc). */
 int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream);

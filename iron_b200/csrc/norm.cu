@@ -81,8 +81,9 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
 #pragma unroll
   for (int j = 0; j < PER / 2; ++j) {
     const int i = lane + 32 * j;
-    const float x1 = rbf(rms_apply(v[2 * j], bf2f(nw[i]), rc));
-    const float x2 = rbf(rms_apply(v[2 * j + 1], bf2f(nw[i + HD / 2]), rc));
+    // no norm weights: RoPE alone (Llama: llama_cpu.py:14-38)
+    const float x1 = nw ? rbf(rms_apply(v[2 * j], bf2f(nw[i]), rc)) : v[2 * j];
+    const float x2 = nw ? rbf(rms_apply(v[2 * j + 1], bf2f(nw[i + HD / 2]), rc)) : v[2 * j + 1];
     const float c = bf2f(a[2 * i]), s = bf2f(a[2 * i + 1]);
     // rope/reference.py:150-154: y1 = x1*c - x2*s, y2 = x2*c + x1*s (float32)
     o[2 * j] = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
@@ -166,6 +167,17 @@ extern "C" int iron_add(const uint16_t* a, const uint16_t* b, uint16_t* c, int64
 extern "C" int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void* stream) {
   return elt(a, b, c, n, 1, stream);
 }
+// RoPE of q and k heads of a raw (batch, (Hq + 2 Hkv) HD) projection and the K/V cache
+// write at each stream's offset, without per-head norms.
+extern "C" int iron_rope_kv(const uint16_t* raw, const uint16_t* ang_table, uint16_t* q_out, uint16_t* kv_cache,
+                            int HD, int Hq, int Hkv, int max_seq, int batch, const int32_t* kv_off_dev,
+                            void* stream) {
+  IRON_REQUIRE(raw && ang_table && q_out && kv_cache && kv_off_dev && batch >= 1 && Hq >= 1 && Hkv >= 1,
+               IRON_ERR_ARG, "rope_kv: bad arguments");
+  return qk_norm_rope_kv_launch(raw, nullptr, nullptr, ang_table, 1, q_out, kv_cache, HD, Hq, Hkv, max_seq, batch,
+                                0, kv_off_dev, 0.f, 0, (cudaStream_t)stream);
+}
+
 extern "C" int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream) {
   IRON_REQUIRE(mode == 0 || mode == 1, IRON_ERR_ARG, "silu: mode must be 0 or 1");
   return elt(x, nullptr, y, n, 2 + mode, stream);

@@ -13,7 +13,7 @@ extracted with ``ast`` and executed unchanged in a small namespace.
 
 Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
   gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
-  decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz
+  decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz
 """
 
 from __future__ import annotations
@@ -203,6 +203,32 @@ def main(ref: Path):
     # ---- bf16 GEMV golden (reference generator) ----
     gb = gemv.generate_golden_reference(M=256, K=512)
     np.savez_compressed(OUT / "gemv_bf16.npz", A=bits(gb["A"]), B=bits(gb["B"]), C=bits(gb["C"]))
+    # ---- Llama decode block (llama_cpu.py, the C5 CPU path) ----
+    import math
+    lf = extract(ref, "iron/applications/llama_3.2_1b/llama_cpu.py",
+                 ["rope_forward", "rms_norm_forward", "grouped_query_attention_forward", "swiglu_ffn_forward",
+                  "transformer_block_forward"], extra_globals={"math": math})
+    hf = extract(ref, "iron/applications/llama_3.2_1b/llama_inference_harness.py", ["compute_rope_angles"])
+    lg = torch.Generator().manual_seed(51)
+    D, H, KVH, HD, FF, T = 256, 4, 2, 64, 512, 5  # T cached positions, one new token
+    bf = torch.bfloat16
+
+    def lw(*shape, std=0.02, mean=0.0):
+        return (torch.randn(*shape, generator=lg) * std + mean).to(bf)
+
+    x = lw(1, 1, D, std=1.0)
+    wts = {"norm1": lw(D, std=0.1, mean=1.0), "wq": lw(H * HD, D), "wk": lw(KVH * HD, D), "wv": lw(KVH * HD, D),
+           "wo": lw(D, H * HD), "norm2": lw(D, std=0.1, mean=1.0), "wg": lw(FF, D), "wu": lw(FF, D),
+           "wd": lw(D, FF)}
+    kc, vc = lw(1, KVH, T, HD, std=1.0), lw(1, KVH, T, HD, std=1.0)
+    angles = hf["compute_rope_angles"](HD, 64, 500000.0)
+    out, k2, v2 = lf["transformer_block_forward"](x, kc, vc, H, KVH, wts["norm1"], wts["wq"], wts["wk"], wts["wv"],
+                                                  wts["wo"], wts["norm2"], wts["wg"], wts["wu"], wts["wd"],
+                                                  angles, None)
+    np.savez_compressed(OUT / "llama_block.npz", x=bits(x.reshape(D)), kc=bits(kc[0]), vc=bits(vc[0]),
+                        angles=angles.numpy(), out=bits(out.reshape(D)), k_new=bits(k2[0, :, T]),
+                        v_new=bits(v2[0, :, T]), dims=np.array([D, H, KVH, HD, FF, T]),
+                        **{k: bits(v) for k, v in wts.items()})
     print("wrote fixtures to", OUT)
 
 

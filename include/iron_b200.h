@@ -108,7 +108,9 @@ int iron_argmax_bf16(const uint16_t* logits, int M, int batch, int32_t* token_ou
  * mode 0: y = bf16(x * rsqrt(mean(x^2) + eps) * w) in f32, the device kernel's
  * arithmetic (aie_kernels/aie2p/rms_norm.cc:9-53).  mode 1: the golden's
  * arithmetic on bf16 tensors (rms_norm/reference.py:8-17), each of x^2, mean,
- * +eps, sqrt, x/rms, *w rounded to bf16.  w may be NULL (unweighted). */
+ * +eps, sqrt, x/rms, *w rounded to bf16.  mode 2: the Llama form (llama_cpu.py:41-46)
+ * on bf16 tensors, x^2, mean, +eps, rsqrt, x*r, w* rounded to bf16.  w may be NULL
+ * (unweighted). */
 int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
                  float eps, int mode, void* stream);
 /* c = bf16(a + b)   (iron/operators/elementwise_add/op.py, aie_kernels/generic/add.cc) */

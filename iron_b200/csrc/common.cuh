@@ -130,6 +130,8 @@ __device__ __forceinline__ void bfp_scale(float m, float& sc, float& inv) {
 //    + eps) evaluated in float64 and rounded once (through float32) to bf16.
 //  mode 1 (golden form, rms_norm/reference.py:8-17 on bf16 tensors): every
 //    torch op rounds to bf16 -- x^2, mean, + eps, sqrt, x / rms, * w.
+//  mode 2 (Llama form, llama_cpu.py:41-46 on bf16 tensors): x^2, mean, + eps,
+//    rsqrt (correctly rounded), x * r, w * . each rounded to bf16.
 struct RmsCoef {
   double inv;
   float rms;
@@ -145,17 +147,23 @@ __device__ __forceinline__ RmsCoef rms_coef(double sum_sq, int n, float eps, int
   if (mode == 0) {
     c.inv = 1.0 / sqrt(sum_sq / (double)n + (double)eps);
     c.rms = 0.f;
-  } else {
+  } else if (mode == 1) {
     const float mean = rbf((float)(sum_sq / (double)n));
     const float ms = rbf(mean + eps);
     c.rms = rbf(sqrtf(ms));
+    c.inv = 0.0;
+  } else {  // mode 2: c.rms holds r = bf16(rsqrt(bf16(mean + eps)))
+    const float mean = rbf((float)(sum_sq / (double)n));
+    const float ms = rbf(mean + eps);
+    c.rms = rbf((float)(1.0 / sqrt((double)ms)));
     c.inv = 0.0;
   }
   return c;
 }
 // normalised, weighted value before the final bf16 rounding
 __device__ __forceinline__ float rms_apply(float v, float w, const RmsCoef& c) {
-  return c.mode == 0 ? (float)((double)v * c.inv * (double)w) : rbf(v / c.rms) * w;
+  if (c.mode == 0) return (float)((double)v * c.inv * (double)w);
+  return c.mode == 1 ? rbf(v / c.rms) * w : w * rbf(v * c.rms);
 }
 
 // sigmoid via tanh with bf16 rounding after every vector op, the arithmetic of

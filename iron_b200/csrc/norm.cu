@@ -148,7 +148,7 @@ using namespace iron;
 
 extern "C" int iron_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int cols,
                             float eps, int mode, void* stream) {
-  IRON_REQUIRE(x && y && rows > 0 && cols > 0 && (mode == 0 || mode == 1), IRON_ERR_ARG,
+  IRON_REQUIRE(x && y && rows > 0 && cols > 0 && mode >= 0 && mode <= 2, IRON_ERR_ARG,
                "rmsnorm: bad arguments");
   rmsnorm_kernel<<<rows, cols >= 1024 ? 512 : 128, 0, (cudaStream_t)stream>>>(x, w, y, cols, eps, mode);
   return iron_check_launch("rmsnorm_kernel");

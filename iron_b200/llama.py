@@ -5,8 +5,9 @@ llama_3.2_1b/llama_npu.py) and on the CPU through llama_cpu.py.  Here one GPU
 decodes ``batch`` independent streams, each at its own position (ragged K/V
 lengths), with the chained operator kernels replayed as one CUDA graph per step:
 
-  embedding -> per layer: RMSNorm, QKV projection (bf16 weights), RoPE + K/V
-  cache write, GQA decode attention over each stream's own length, O projection,
+  embedding -> per layer: RMSNorm (the Llama form, iron_rmsnorm mode 2), QKV
+  projection (bf16 weights), RoPE + K/V cache write, GQA decode attention over each
+  stream's own length, O projection,
   residual add, RMSNorm, gate and up projections, SiLU, multiply, down projection,
   residual add -> final RMSNorm -> tied lm_head + greedy argmax -> positions += 1.
 
@@ -130,7 +131,7 @@ class LlamaB200:
         abi("iron_embedding", ptr(w.embed), c.V, ptr(self.tok), B, c.D, ptr(self.x), st)
         for i, Lw in enumerate(w.layers):
             kv = self.kv[i]
-            abi("iron_rmsnorm", ptr(self.x), ptr(Lw["norm1"]), ptr(self.xn), B, c.D, c.eps, 1, st)
+            abi("iron_rmsnorm", ptr(self.x), ptr(Lw["norm1"]), ptr(self.xn), B, c.D, c.eps, 2, st)
             abi("iron_gemv_bf16", ptr(Lw["wqkv"]), c.QKV, c.D, ptr(self.xn), B, 0, ptr(self.raw), st)
             abi("iron_rope_kv", ptr(self.raw), ptr(self.angles), ptr(self.q), ptr(kv), c.HD, c.Hq, c.Hkv,
                 self.max_seq, B, ptr(self.off), st)
@@ -138,14 +139,14 @@ class LlamaB200:
                 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
             abi("iron_gemv_bf16", ptr(Lw["wo"]), c.D, c.QD, ptr(self.attn), B, 0, ptr(self.o), st)
             abi("iron_add", ptr(self.x), ptr(self.o), ptr(self.x1), B * c.D, st)
-            abi("iron_rmsnorm", ptr(self.x1), ptr(Lw["norm2"]), ptr(self.xn), B, c.D, c.eps, 1, st)
+            abi("iron_rmsnorm", ptr(self.x1), ptr(Lw["norm2"]), ptr(self.xn), B, c.D, c.eps, 2, st)
             abi("iron_gemv_bf16", ptr(Lw["wg"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.g), st)
             abi("iron_gemv_bf16", ptr(Lw["wu"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.u), st)
             abi("iron_silu", ptr(self.g), ptr(self.g), B * c.FF, 0, st)
             abi("iron_mul", ptr(self.g), ptr(self.u), ptr(self.g), B * c.FF, st)
             abi("iron_gemv_bf16", ptr(Lw["wd"]), c.D, c.FF, ptr(self.g), B, 0, ptr(self.o), st)
             abi("iron_add", ptr(self.x1), ptr(self.o), ptr(self.x), B * c.D, st)
-        abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xn), B, c.D, c.eps, 1, st)
+        abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xn), B, c.D, c.eps, 2, st)
         abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xn), B,
             None if self.logits is None else ptr(self.logits), ptr(self.tok), ptr(self.argmax_ws), st)
         if advance:

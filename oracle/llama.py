@@ -76,8 +76,13 @@ class OracleLlama:
     ``(FF, D)``, ``wd (D, FF)``; ``final_norm (D)``, ``embed (V, D)`` (tied lm_head).
     All bf16 values as float32."""
 
-    def __init__(self, shape: LlamaShape, weights: dict, max_seq: int, angles=None):
-        self.s, self.w = shape, weights
+    def __init__(self, shape: LlamaShape, weights: dict, max_seq: int, angles=None,
+                 exact_attention: bool = False):
+        """``exact_attention``: softmax and context in float64, rounded once -- the
+        quantity the reference's bf16 op chain approximates (its scores and
+        probabilities are rounded to bf16); the float32 flash attention of the GPU
+        path is checked against this form."""
+        self.s, self.w, self.exact_attention = shape, weights, exact_attention
         self.kv = np.zeros((shape.n_layers, shape.Hkv, max_seq, 2, shape.HD), F32)
         self.angles = (ops.rope_angle_table(max_seq, shape.HD, shape.theta) if angles is None
                        else np.asarray(angles, F32))
@@ -98,6 +103,11 @@ class OracleLlama:
             kvh = hh * s.Hkv // s.Hq  # repeat_interleave: query head hh reads KV head hh // group
             K = self.kv[i, kvh, :pos + 1, 0].astype(np.float64)
             V = self.kv[i, kvh, :pos + 1, 1].astype(np.float64)
+            if self.exact_attention:
+                sc = (K @ q[hh].astype(np.float64)) / math.sqrt(s.HD)
+                e = np.exp(sc - sc.max())
+                ctx[hh] = rnd(((e @ V) / e.sum()).astype(F32))
+                continue
             sc = rnd((K @ q[hh].astype(np.float64)).astype(F32))
             sc = rnd((sc / F32(math.sqrt(s.HD))).astype(F32))
             e = np.exp(sc.astype(np.float64) - float(sc.max()))

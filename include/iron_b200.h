@@ -55,7 +55,9 @@ int iron_last_error(char* buf, int buflen);
  * (and 9..15) computes the exact dequantised sum (one bf16 rounding; launches of 8
  * rows); batch 16..256 on plain wires runs one tcgen05 tensor-core contraction with
  * the weight dequantised to bf16 (bf16(q*s), float32 accumulation), within the
- * bf16 tolerance of the exact sum (see iron_tc_status).
+ * bf16 tolerance of the exact sum (see iron_tc_status).  That contraction keeps its
+ * split-K partial sums in one scratch array per GPU (and normalises RMS inputs into
+ * another): such calls on different streams of one GPU must not overlap.
  * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.
  */
 int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
@@ -85,13 +87,18 @@ int iron_quantize_rtn(const uint16_t* w, int M, int K, int group, int tile_m, in
  * y[b, m] = bf16( sum_k A[m, k] * x[b, k] )  (f32 accumulation).
  * independent != 0: `batch` independent GEMVs, A[b] (M, K) each (the num_batches
  * mode of iron/operators/gemv/op.py:151-157).  Replaces GEMV (gemv/op.py:20-163,
- * kernel aie_kernels/generic/mv.cc:47-90). */
+ * kernel aie_kernels/generic/mv.cc:47-90).  A shared weight with 16..256 rows runs
+ * the tcgen05 contraction of iron_gemv_w8a16 (same per-GPU scratch: such calls on
+ * different streams of one GPU must not overlap). */
 int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
                    int independent, uint16_t* y, void* stream);
 
 /* lm_head GEMV fused with a greedy argmax over the bf16-rounded logits (ties ->
  * lowest index, as numpy.argmax in qwen3_npu_int8.py:619-620).  logits may be
- * NULL (not stored).  token_out: int32[batch].  workspace: iron_argmax_workspace_bytes(). */
+ * NULL (not stored).  token_out: int32[batch].  workspace: iron_argmax_workspace_bytes().
+ * Batch 16..256: one tcgen05 contraction; with logits NULL the logits go to a per-GPU
+ * scratch array (batch * M <= 8 Mi values), so such calls on different streams of one
+ * GPU must not overlap. */
 int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
                              uint16_t* logits, int32_t* token_out, void* workspace,
                              void* stream);

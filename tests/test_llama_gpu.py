@@ -88,6 +88,9 @@ def test_llama_graph_replay_advances_positions(model):
     a.set_positions([p + 1 for p in pos])
     for _ in range(3):
         a.run_step(advance=True)
+    # 16+ streams use the tensor-core kernels' per-GPU scratch: calls on different
+    # streams must not overlap, so the second decoder starts after the first is done
+    a.stream.synchronize()
     cur = [int(t) for t in tb]
     for k in range(3):
         cur = [int(t) for t in b.step_tokens(cur, [p + 1 + k for p in pos])]

@@ -39,13 +39,12 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   const int start = split * chunk;
   const int end = min(L, start + chunk);
 
-  float q[GQ][8];
-#pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    const uint16_t* qs = p.q + ((size_t)b * p.H + kvh * GQ + h) * HD + sub * 8;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[h][e] = bf2f(qs[e]);
-  }
+  // the group's queries in shared memory (float32), not registers: the freed
+  // registers let more CTAs (more K/V bytes in flight) share an SM
+  __shared__ __align__(16) float sq[GQ][HD];
+  for (int i = threadIdx.x; i < GQ * HD; i += blockDim.x)
+    sq[i / HD][i % HD] = bf2f(p.q[((size_t)b * p.H + kvh * GQ) * HD + i]);
+  __syncthreads();
   const uint16_t* head = p.kv + ((size_t)b * p.KV + kvh) * 2 * (size_t)p.max_seq * HD;
   // element offsets of K_j / V_j inside the head region for the three layouts
   auto koff = [&](int j) -> size_t {
@@ -82,11 +81,13 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const uint32_t kw[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+        const float4 qa = *(const float4*)&sq[h][sub * 8], qb = *(const float4*)&sq[h][sub * 8 + 4];
+        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
         float d = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          d = fmaf(q[h][2 * e], bf_lo(kw[e]), d);
-          d = fmaf(q[h][2 * e + 1], bf_hi(kw[e]), d);
+          d = fmaf(qv[2 * e], bf_lo(kw[e]), d);
+          d = fmaf(qv[2 * e + 1], bf_hi(kw[e]), d);
         }
 #pragma unroll
         for (int x = 1; x < RL; x <<= 1) d += __shfl_xor_sync(~0u, d, x);

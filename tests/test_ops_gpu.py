@@ -42,6 +42,20 @@ def test_rmsnorm_against_reference_golden(golden):
         assert_ulps(host(y), want, max_ulp=1, frac_exact=0.99, what="rmsnorm f32 form")
 
 
+def test_rmsnorm_llama_form_matches_oracle():
+    """iron_rmsnorm mode 2 (llama_cpu.py:41-46 on bf16 tensors) against oracle.llama.rms_norm."""
+    from iron_b200 import _lib
+    from oracle.llama import rms_norm as llama_norm
+    torch.manual_seed(21)
+    rows, cols = 7, 2048
+    x = (torch.randn(rows, cols, device="cuda") * 3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(cols, device="cuda")).to(torch.bfloat16)
+    y = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_rmsnorm", x.data_ptr(), w.data_ptr(), y.data_ptr(), rows, cols, 1e-5, 2, _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert_ulps(host(y), llama_norm(host(x), host(w), 1e-5), max_ulp=1, frac_exact=0.99, what="llama norm")
+
+
 def test_elementwise_against_reference_golden(golden):
     g = golden("elementwise")
     a, b = dev_bf16(g["a"]), dev_bf16(g["b"])

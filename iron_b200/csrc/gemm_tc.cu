@@ -150,8 +150,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 __device__ __forceinline__ void bar_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * NDQ) : "memory"); }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
+// bf16(lo) in the low half, bf16(hi) in the high half: one round-to-nearest-even
+// conversion instruction for the pair
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 
 // W16: the weight is bf16 already (the tied lm_head, bf16 GEMVs): TMA writes its
@@ -303,16 +307,21 @@ __global__ void __launch_bounds__(NTH, 2)
           const uint32_t qw[4] = {q.x ^ flip, q.y ^ flip, q.z ^ flip, q.w ^ flip};
           const int g = (k0 + i * BK + c * 16) / G;
           const float sf = bf2f(sc[(size_t)r * (p.sbox >> 1) + (sdelta >> 1) + (g - gfirst)]);
+          // -(2^23 + 2^7) * s is exact: the 8-bit significand of s shifted by 7 and by 23
+          // spans 24 bits
+          const float soff = -8388736.0f * sf;
           uint32_t o[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            // the float 2^23 + (b + 128) from one byte permute, minus 2^23 + 128: exactly b
+            // one byte permute gives the float 2^23 + (b + 128); one fma with s and soff
+            // gives b * s, exact in float32 (8-bit b times 8-bit s), rounded to bf16 once
+            // by the pack -- the same bits as bf16(float(b) * s)
             float f[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              f[j] = __uint_as_float(__byte_perm(qw[e], 0x4B000000u, 0x7440u | (uint32_t)j)) - 8388736.0f;
-            o[2 * e] = pack_bf16x2(f[0] * sf, f[1] * sf);
-            o[2 * e + 1] = pack_bf16x2(f[2] * sf, f[3] * sf);
+              f[j] = fmaf(__uint_as_float(__byte_perm(qw[e], 0x4B000000u, 0x7440u | (uint32_t)j)), sf, soff);
+            o[2 * e] = pack_bf16x2(f[0], f[1]);
+            o[2 * e + 1] = pack_bf16x2(f[2], f[3]);
           }
           // 16-byte chunk j of row r sits at chunk j ^ (r & 7) (128-byte swizzle)
           *(uint4*)(at + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -371,14 +380,40 @@ __global__ void __launch_bounds__(NTH, 2)
         bar_epi();
         if (*lastf) {
           __threadfence();
-          for (int b = half; b < N; b += 2) {
-            float a0 = 0.f, a1 = 0.f;
-            for (int s2 = 0; s2 < p.splits; ++s2) {
-              const float* pp = g_ws + ((size_t)(tile * p.splits + s2) * NW * N) * BM;
-              a0 += __ldcg(pp + (size_t)b * BM + row);
-              if (PAIR) a1 += __ldcg(pp + (size_t)(N + b) * BM + row);
+          // CB columns at a time, the partials of U splits loaded before any is added:
+          // U * CB * NW loads in flight per thread; sums in split order as always
+          constexpr int CB = 4, U = 4;
+          const float* base = g_ws + (size_t)tile * p.splits * NW * N * BM + row;
+          for (int b0 = half; b0 < N; b0 += 2 * CB) {
+            float a0[CB], a1[CB];
+#pragma unroll
+            for (int c = 0; c < CB; ++c) a0[c] = a1[c] = 0.f;
+            for (int s0 = 0; s0 < p.splits; s0 += U) {
+              float v0[U][CB], v1[U][CB];
+#pragma unroll
+              for (int u = 0; u < U; ++u) {
+                const float* pp = base + (size_t)(s0 + u) * NW * N * BM;
+#pragma unroll
+                for (int c = 0; c < CB; ++c) {
+                  const int b = b0 + 2 * c;
+                  const bool in = s0 + u < p.splits && b < N;
+                  v0[u][c] = in ? __ldcg(pp + (size_t)b * BM) : 0.f;
+                  v1[u][c] = (PAIR && in) ? __ldcg(pp + (size_t)(N + b) * BM) : 0.f;
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < U; ++u)
+                if (s0 + u < p.splits) {
+#pragma unroll
+                  for (int c = 0; c < CB; ++c) {
+                    a0[c] += v0[u][c];
+                    if (PAIR) a1[c] += v1[u][c];
+                  }
+                }
             }
-            finish(b, a0, a1);
+#pragma unroll
+            for (int c = 0; c < CB; ++c)
+              if (b0 + 2 * c < N) finish(b0 + 2 * c, a0[c], a1[c]);
           }
           if (t == 0) g_counters[tile] = 0;
         }

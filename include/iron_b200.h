@@ -45,6 +45,11 @@ extern "C" {
 const char* iron_version(void);
 /* Copy the calling thread's last error message into buf (NUL-terminated); returns its length. */
 int iron_last_error(char* buf, int buflen);
+/* Kernels this library has launched in this process (every successful launch, from any
+ * thread; replays of a captured CUDA graph are not launches of the library).  A
+ * diagnostic with no counterpart in the reference: the difference across one eager or
+ * captured decode step is the number of kernels that step runs. */
+int64_t iron_launch_count(void);
 
 /* ---- int8 group-dequant GEMV (W8A16) -------------------------------------
  * y[b, m] = bf16( sum_k q[m,k] * s[m, k/group] * x[b, k] )           (epilogue 0)

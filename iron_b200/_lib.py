@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
     "iron_add": (I, [P, P, P, I64, P]),
     "iron_tc_status": (I, [I]),
+    "iron_launch_count": (I64, []),
     "iron_rope_kv": (I, [P, P, P, P, I, I, I, I, I, P, P]),
     "iron_gemv_w8a16_ex": (I, [P, P, I, I, I, I, P, I, I, P, C.c_float, I, P, I, P, I, P]),
     "iron_resid_add_f32": (I, [P, P, P, I64, P]),
@@ -77,6 +78,11 @@ def lib():
             fn.argtypes = args
         _LIB = L
     return _LIB
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process (``iron_launch_count``)."""
+    return int(lib().iron_launch_count())
 
 
 def last_error() -> str:

@@ -3,6 +3,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 static thread_local char g_err[512] = {0};
@@ -15,12 +17,20 @@ int iron_set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+static std::atomic<long long> g_launches{0};
+
+void iron_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// every kernel launch site of the library calls this right after its launch
 int iron_check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return iron_set_error(IRON_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  iron_count_launch();
   return IRON_OK;
 }
+
+extern "C" int64_t iron_launch_count(void) { return (int64_t)g_launches.load(std::memory_order_relaxed); }
 
 int iron_num_sms() {
   static int cache[64] = {0};

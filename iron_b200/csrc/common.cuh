@@ -11,7 +11,10 @@
 // host-side error reporting (thread-local message, negative status codes)
 // ---------------------------------------------------------------------------
 int iron_set_error(int code, const char* fmt, ...);
+// cudaGetLastError after a launch: a negative code on failure, else counts the launch
 int iron_check_launch(const char* what);
+// counts a launch whose status was checked another way (iron_launch_count)
+void iron_count_launch();
 
 #define IRON_REQUIRE(cond, code, ...)                                  \
   do {                                                                 \

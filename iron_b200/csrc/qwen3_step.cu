@@ -1452,6 +1452,7 @@ static int launch(const Kp& p, int grid, size_t smem, cudaStream_t st) {
   void* args[] = {(void*)&p};
   cudaError_t e = cudaLaunchCooperativeKernel((const void*)fn, dim3(grid), dim3(NT + 32), args, smem, st);
   if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 step launch: %s", cudaGetErrorString(e));
+  iron_count_launch();
   return IRON_OK;
 }
 

@@ -119,12 +119,23 @@ class LlamaB200:
         self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict = {}
+        self._step_launches: dict = {}  # advance -> kernels one step launched
 
     def launches_per_step(self, advance: bool = True) -> int:
-        """Our kernels per step at 16+ streams: embedding; per layer 2 RMSNorms, 5
+        """Our kernels per step, as the library counted them over the last eager or captured
+        step; before any, the count at 16+ streams: embedding; per layer 2 RMSNorms, 5
         projections, RoPE, attention split + combine, 2 adds, SiLU, multiply; final
         RMSNorm, lm_head + 2 argmax passes; the position advance."""
+        counted = self._step_launches.get(advance)
+        if counted is not None:  # counted by the library over an eager or captured step
+            return counted
         return 1 + 15 * len(self.w.layers) + 1 + 3 + int(advance)
+
+    def _launch_counted(self, advance: bool, st: int):
+        """_launch_step with the library's launch count taken around it."""
+        c0 = _lib.launch_count()
+        self._launch_step(advance, st)
+        self._step_launches[advance] = _lib.launch_count() - c0
 
     def _launch_step(self, advance: bool, st: int):
         c, w, B = self.cfg, self.w, self.B
@@ -157,13 +168,13 @@ class LlamaB200:
         st = self.stream
         with torch.cuda.stream(st):
             if not self.use_graph:
-                self._launch_step(advance, st.cuda_stream)
+                self._launch_counted(advance, st.cuda_stream)
                 return
             g = self._graphs.get(advance)
             if g is None:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=st):
-                    self._launch_step(advance, st.cuda_stream)
+                    self._launch_counted(advance, st.cuda_stream)
                 self._graphs[advance] = g
             g.replay()
 

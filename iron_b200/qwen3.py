@@ -210,6 +210,7 @@ class Qwen3B200:
         self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
+        self._step_launches: dict = {}  # (from_tokens, advance) -> kernels one step launched
         # "step": the whole token in one persistent kernel (batch 1);
         # "ops": the chained per-operator kernels, replayed as a CUDA graph
         self.impl = impl or ("step" if batch == 1 else "ops")
@@ -308,11 +309,15 @@ class Qwen3B200:
             abi("iron_decode_advance", ptr(self.pos), ptr(self.len), ptr(self.off), B, c.HD, st)
 
     def launches_per_step(self, from_tokens: bool = True, advance: bool = True) -> int:
-        """Kernels one step launches: embedding, 7 per layer (QKV GEMV + head epilogue,
-        attention split + combine, O / gate-up / down GEMVs), final RMSNorm, lm_head
-        (+ argmax passes) and the position advance."""
+        """Kernels one step launches, as the library counted them over the last eager or
+        captured step of this kind; before any, the batch <= 8 count: embedding, 7 per
+        layer (QKV GEMV + head epilogue, attention split + combine, O / gate-up / down
+        GEMVs), final RMSNorm, lm_head (+ argmax passes) and the position advance."""
         if self.impl == "step":
             return 1
+        counted = self._step_launches.get((from_tokens, advance))
+        if counted is not None:  # counted by the library over an eager or captured step
+            return counted
         head = 2 if self.lm_head == "bf16" else 3
         return int(from_tokens) + 7 * len(self.w.layers) + 1 + head + int(advance)
 
@@ -340,15 +345,21 @@ class Qwen3B200:
             return
         with torch.cuda.stream(st):
             if not self.use_graph:
-                self._launch_step(from_tokens, advance, st.cuda_stream)
+                self._launch_counted(key, st.cuda_stream)
                 return
             g = self._graphs.get(key)
             if g is None:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=st):
-                    self._launch_step(from_tokens, advance, st.cuda_stream)
+                    self._launch_counted(key, st.cuda_stream)
                 self._graphs[key] = g
             g.replay()
+
+    def _launch_counted(self, key, st: int):
+        """_launch_step with the library's launch count taken around it."""
+        c0 = _lib.launch_count()
+        self._launch_step(key[0], key[1], st)
+        self._step_launches[key] = _lib.launch_count() - c0
 
     def set_position(self, pos):
         """Host write of the per-stream positions (int or sequence of B ints)."""

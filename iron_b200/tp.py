@@ -163,15 +163,19 @@ class Qwen3TP(Qwen3B200):
         if self.use_graph and self.world > 1 and key not in self._eager_done:
             self._eager_done.add(key)
             with torch.cuda.stream(self.stream):
-                self._launch_step(from_tokens, advance, self.stream.cuda_stream)
+                self._launch_counted(key, self.stream.cuda_stream)
             return
         super().run_step(from_tokens, advance)
 
     def launches_per_step(self, from_tokens: bool = True, advance: bool = True) -> int:
-        """Our kernels per step (batch <= 8): embedding; per layer QKV GEMV + head
+        """Our kernels per step, as the library counted them over the last eager or captured
+        step of this kind; before any, the batch <= 8 count: embedding; per layer QKV GEMV + head
         epilogue, attention split + combine, O GEMV, residual add, gate/up GEMV, down
         GEMV, residual add; final RMSNorm; lm_head GEMV + argmax pass; argmax pair and
         merge; the position advance."""
+        counted = self._step_launches.get((from_tokens, advance))
+        if counted is not None:  # counted by the library over an eager or captured step
+            return counted
         return int(from_tokens) + 9 * len(self.w.layers) + 1 + 2 + 2 + int(advance)
 
     def _stages(self, from_tokens: bool, advance: bool, st: int):

@@ -30,11 +30,14 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_error_reporting_without_gpu():
-    """Argument validation runs on the host and reports through iron_last_error."""
+    """Argument validation runs on the host and reports through iron_last_error; a
+    rejected call launches nothing (iron_launch_count stays put)."""
+    c0 = _lib.launch_count()
     with pytest.raises(_lib.IronError, match="group must be"):
         _lib.call("iron_gemv_w8a16", 16, 64, 1024, 48, 1, 0, 0, 0, 16, 1, None, 16, None)
     with pytest.raises(_lib.IronError, match="batch 0 below 1"):
         _lib.call("iron_lm_head_bf16_argmax", 16, 8, 8, 16, 0, None, 16, 16, None)
+    assert _lib.launch_count() == c0 >= 0
 
 
 def test_gemvint8_arg_spec_matches_reference_formula():

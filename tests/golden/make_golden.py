@@ -2,7 +2,9 @@
 
 Run where the IRON source tree is available (it is NOT needed afterwards):
 
-    python tests/golden/make_golden.py /path/to/IRON
+    python tests/golden/make_golden.py /path/to/IRON [--only NAME ...]
+
+(``--only gptq_pack`` writes just that fixture and leaves the others as committed.)
 
 The reference package ``__init__``s import the NPU toolchain (``aie``), which is
 not installable off-NPU, so the golden modules are loaded by file path with a
@@ -13,7 +15,8 @@ extracted with ``ast`` and executed unchanged in a small namespace.
 
 Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
   gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
-  decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz
+  decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz,
+  gptq_pack.npz
 """
 
 from __future__ import annotations
@@ -73,8 +76,52 @@ def extract(ref: Path, rel: str, names: list[str], cls: str | None = None, extra
     return {n: g[n] for n in names}
 
 
-def main(ref: Path):
+def gptq_pack(ref: Path):
+    """The Qwen3 runtime's GPTQ import (``_set_int8`` -> ``_gptq_rows`` -> ``_pack_int8``)
+    on seeded random checkpoint tensors: two projections stacked along M (as q/k/v),
+    K = 256 in groups of 128 (the packer's fixed group), every byte value 0..255 in the
+    words, fp16 scales including an fp16 subnormal; both payload domains, one row per
+    tile and one column (the plain wire)."""
+    app = "iron/applications/qwen3_0.6b/qwen3_npu_int8.py"
+    fns = extract(ref, app, ["_set_int8", "_gptq_rows", "_pack_int8"], cls="Qwen3NPU")
+    captured = {}
+
+    class FakeSelf:
+        def _set(self, name, t):
+            captured[name] = t
+
+        def _gptq_rows(self, *a, **k):
+            return fns["_gptq_rows"](self, *a, **k)
+
+        def _pack_int8(self, *a):
+            return fns["_pack_int8"](self, *a)
+
+    rng = np.random.default_rng(23)
+    K, Ms = 256, (24, 8)
+    qws, scs = [], []
+    for M in Ms:
+        words = rng.integers(0, 2 ** 32, size=(K // 4, M), dtype=np.uint64).astype(np.uint32)
+        words[0, 0], words[1, 0] = 0x00000000, 0xFFFFFFFF  # q = -128 and q = 127 everywhere in a word
+        qws.append(torch.from_numpy(words.view(np.int32).copy()))
+        sc = (rng.random((K // 128, M)) * 0.05 + 1e-4).astype(np.float16)
+        sc[0, 1] = np.float16(6e-8)  # an fp16 subnormal
+        scs.append(torch.from_numpy(sc))
+    out = {}
+    for signed, tag in ((True, "signed"), (False, "biased")):
+        fns["_set_int8"](FakeSelf(), tag, qws, scs, sum(Ms), K, 1, 1, signed=signed)
+        out[f"wire_{tag}"] = captured[tag].view(torch.uint8).numpy()
+    np.savez_compressed(OUT / "gptq_pack.npz", qweight_a=qws[0].numpy(), qweight_b=qws[1].numpy(),
+                        scales_a=scs[0].numpy().view(np.uint16), scales_b=scs[1].numpy().view(np.uint16),
+                        **out)
+
+
+def main(ref: Path, only: list[str] | None = None):
     setup_shim(ref)
+    if only:
+        for name in only:
+            {"gptq_pack": gptq_pack}[name](ref)
+        print("wrote", ", ".join(only), "to", OUT)
+        return
     rms = load(ref, "iron/operators/rms_norm/reference.py", "iron.operators.rms_norm.reference")
     rope = load(ref, "iron/operators/rope/reference.py", "iron.operators.rope.reference")
     qkv = load(ref, "iron/operators/qkv_head_dp/reference.py", "iron.operators.qkv_head_dp.reference")
@@ -229,10 +276,11 @@ def main(ref: Path):
                         angles=angles.numpy(), out=bits(out.reshape(D)), k_new=bits(k2[0, :, T]),
                         v_new=bits(v2[0, :, T]), dims=np.array([D, H, KVH, HD, FF, T]),
                         **{k: bits(v) for k, v in wts.items()})
+    gptq_pack(ref)
     print("wrote fixtures to", OUT)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <path to the IRON source tree>")
-    main(Path(sys.argv[1]))
+    if len(sys.argv) < 2 or (len(sys.argv) > 2 and sys.argv[2] != "--only"):
+        sys.exit("usage: make_golden.py <path to the IRON source tree> [--only NAME ...]")
+    main(Path(sys.argv[1]), sys.argv[3:] if len(sys.argv) > 2 else None)

@@ -3,7 +3,7 @@
 The reference's Qwen3 int8 application decodes from a GPTQ checkpoint: symmetric
 int8 with zero-point 128 and one fp16 scale per (group of K, output row); the tied
 lm_head stays bf16 (iron/applications/qwen3_0.6b/qwen3_npu_int8.py:144-181 names the
-tensors).  It repacks every projection on the host: ``_gptq_rows`` (:350-381) unpacks
+tensors).  It repacks every projection on the host: ``_gptq_rows`` (:350-379) unpacks
 ``qweight`` -- (K/4, M) 32-bit words, the byte j of word (r, m) (least significant
 first) holding u = q + 128 for column k = 4r + j of row m -- into row-major payload
 bytes, either as u itself (the biased domain) or as q in two's complement (the signed
@@ -63,15 +63,30 @@ def gptq_to_wire(qweight: torch.Tensor, scales: torch.Tensor, domain: int = 0) -
     return torch.cat([payload, sc.view(torch.uint8).reshape(M, -1)], dim=1).reshape(-1)
 
 
-def gptq_stack_to_wire(parts, domain: int = 0) -> torch.Tensor:
-    """Projections sharing K stacked along M (q, k, v; as ``_set_int8``) into one wire:
-    plain-wire rows are independent, so the wire of the stack is the wires in order."""
+def gptq_stack_to_wire(parts, domain: int = 0, tile_m: int = 1, cols: int = 1) -> torch.Tensor:
+    """Projections sharing K stacked along M (q, k, v; as ``_set_int8``) into one wire.
+
+    tile_m = 1: the plain wire (rows are independent, so the wire of the stack is the
+    wires in order).  tile_m > 1: the per-core tile wire the fused operators take
+    (``_pack_int8``, qwen3_npu_int8.py:381-405): each column's rows in tiles of tile_m
+    rows, a tile being its rows' payload bytes then their scales.  The columns cover
+    consecutive row ranges, so the tiles run in row order; M must split into cols
+    equal ranges of whole tiles."""
     parts = list(parts)
     Ks = {4 * qw.shape[0] for qw, _ in parts}
     Gs = {gptq_group(qw, sc) for qw, sc in parts}
     if len(Ks) != 1 or len(Gs) != 1:
         raise ValueError(f"gptq: stacked projections need one K and one group, got K {Ks}, group {Gs}")
-    return torch.cat([gptq_to_wire(qw, sc, domain) for qw, sc in parts])
+    if tile_m == 1:
+        return torch.cat([gptq_to_wire(qw, sc, domain) for qw, sc in parts])
+    rows = [gptq_rows(qw, sc, domain) for qw, sc in parts]
+    payload = torch.cat([p for p, _ in rows])
+    sc = torch.cat([s for _, s in rows])
+    M = payload.shape[0]
+    if tile_m < 1 or cols < 1 or M % cols or (M // cols) % tile_m:
+        raise ValueError(f"gptq: {M} rows do not split into {cols} columns of {tile_m}-row tiles")
+    n = M // tile_m
+    return torch.cat([payload.reshape(n, -1), sc.view(torch.uint8).reshape(n, -1)], dim=1).reshape(-1)
 
 
 def _getter(tensors):

@@ -80,8 +80,9 @@ def gptq_pack(ref: Path):
     """The Qwen3 runtime's GPTQ import (``_set_int8`` -> ``_gptq_rows`` -> ``_pack_int8``)
     on seeded random checkpoint tensors: two projections stacked along M (as q/k/v),
     K = 256 in groups of 128 (the packer's fixed group), every byte value 0..255 in the
-    words, fp16 scales including an fp16 subnormal; both payload domains, one row per
-    tile and one column (the plain wire)."""
+    words, fp16 scales including an fp16 subnormal; both payload domains with one row
+    per tile and one column (the plain wire), and the signed wire in tiles of 4 rows
+    over 2 columns."""
     app = "iron/applications/qwen3_0.6b/qwen3_npu_int8.py"
     fns = extract(ref, app, ["_set_int8", "_gptq_rows", "_pack_int8"], cls="Qwen3NPU")
     captured = {}
@@ -110,6 +111,9 @@ def gptq_pack(ref: Path):
     for signed, tag in ((True, "signed"), (False, "biased")):
         fns["_set_int8"](FakeSelf(), tag, qws, scs, sum(Ms), K, 1, 1, signed=signed)
         out[f"wire_{tag}"] = captured[tag].view(torch.uint8).numpy()
+    # per-core tiles as the fused ops take them: 2 columns, 4 rows per tile
+    fns["_set_int8"](FakeSelf(), "tiles", qws, scs, sum(Ms), K, 2, 4, signed=True)
+    out["wire_signed_c2_t4"] = captured["tiles"].view(torch.uint8).numpy()
     np.savez_compressed(OUT / "gptq_pack.npz", qweight_a=qws[0].numpy(), qweight_b=qws[1].numpy(),
                         scales_a=scs[0].numpy().view(np.uint16), scales_b=scs[1].numpy().view(np.uint16),
                         **out)

@@ -37,6 +37,17 @@ def test_gptq_wire_matches_reference_import(golden, domain, tag):
     assert np.array_equal(wire.numpy(), golden[f"wire_{tag}"])
 
 
+def test_gptq_tile_wire_matches_reference_import(golden):
+    """The per-core tile wire (4-row tiles over 2 columns) of the same import, and the
+    oracle's tile packer on the unpacked rows."""
+    wire = gptq_stack_to_wire(_parts(golden), 0, tile_m=4, cols=2)
+    assert np.array_equal(wire.numpy(), golden["wire_signed_c2_t4"])
+    q, s_bits = wire_to_numpy(gptq_stack_to_wire(_parts(golden), 0), 32, 256, 128)
+    assert np.array_equal(wire.numpy(), ops.pack_tile_wire(q, s_bits, 4, 2, "signed"))
+    with pytest.raises(ValueError, match="do not split"):
+        gptq_stack_to_wire(_parts(golden), 0, tile_m=3, cols=2)
+
+
 def test_gptq_wire_dequantises_to_checkpoint_weights(golden):
     """Independently of the reference code: the GPTQ weight is (u - 128) * scale with u
     the byte k % 4 of word (k / 4, m); the signed wire must hold q = u - 128 and the

@@ -14,7 +14,10 @@ Here the same unpacking runs with torch ops on the tensors' device (one-time
 conversion) and writes the plain wire the kernels stream (tile_m = 1: per row
 ``[K payload bytes | K/G bf16 scales]``, ``quantize_to_wire``'s format), so a loaded
 checkpoint runs every decode path unchanged: the weight integers are the
-checkpoint's, no re-quantisation.
+checkpoint's, no re-quantisation.  The reference's other two wires come out too, for
+callers of the IRON-shaped operators that pass them: the per-core tile wire
+(``gptq_stack_to_wire`` with tile_m > 1) and fuse_o's tile-major Wo
+(``gptq_wo_tile_major``).
 """
 
 from __future__ import annotations
@@ -87,6 +90,33 @@ def gptq_stack_to_wire(parts, domain: int = 0, tile_m: int = 1, cols: int = 1) -
         raise ValueError(f"gptq: {M} rows do not split into {cols} columns of {tile_m}-row tiles")
     n = M // tile_m
     return torch.cat([payload.reshape(n, -1), sc.view(torch.uint8).reshape(n, -1)], dim=1).reshape(-1)
+
+
+def gptq_wo_tile_major(qweight: torch.Tensor, scales: torch.Tensor, cols: int, tile_rows: int,
+                       tiles_per_core: int, domain: int = 0) -> torch.Tensor:
+    """fuse_o's Wo in the per-core tile-major wire (``_set_wo_tiled``,
+    qwen3_npu_int8.py:407-436): core c streams ``tiles_per_core`` tiles of
+    ``tile_rows`` rows from row c * M/cols on, each tile its payload bytes then its
+    scales.  A window that runs past the core's rows repeats the next core's rows, and
+    past the matrix end reads pad rows with payload and scale bytes 0 (weight 0 in
+    either payload domain)."""
+    payload, sc = gptq_rows(qweight, scales, domain)
+    M, K = payload.shape
+    if cols < 1 or tile_rows < 1 or M % cols:
+        raise ValueError(f"gptq: {M} rows do not split into {cols} cores")
+    rpc = M // cols
+    pad = tiles_per_core * tile_rows - rpc
+    if pad < 0:
+        raise ValueError(f"gptq: {tiles_per_core} tiles of {tile_rows} rows do not cover a core's {rpc} rows")
+    sb = sc.view(torch.uint8).reshape(M, -1)
+    W = torch.cat([payload, payload.new_zeros(pad, K)])
+    S = torch.cat([sb, sb.new_zeros(pad, sb.shape[1])])
+    dev = payload.device
+    starts = (torch.arange(cols, device=dev)[:, None] * rpc
+              + torch.arange(tiles_per_core, device=dev)[None, :] * tile_rows).reshape(-1)
+    rows = starts[:, None] + torch.arange(tile_rows, device=dev)[None, :]  # (tiles, tile_rows)
+    n = rows.shape[0]
+    return torch.cat([W[rows].reshape(n, -1), S[rows].reshape(n, -1)], dim=1).reshape(-1)
 
 
 def _getter(tensors):

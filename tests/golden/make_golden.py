@@ -81,10 +81,11 @@ def gptq_pack(ref: Path):
     on seeded random checkpoint tensors: two projections stacked along M (as q/k/v),
     K = 256 in groups of 128 (the packer's fixed group), every byte value 0..255 in the
     words, fp16 scales including an fp16 subnormal; both payload domains with one row
-    per tile and one column (the plain wire), and the signed wire in tiles of 4 rows
-    over 2 columns."""
+    per tile and one column (the plain wire), the signed wire in tiles of 4 rows over
+    2 columns, and fuse_o's tile-major Wo wire (``_set_wo_tiled``) with overlapping
+    per-core windows and pad rows."""
     app = "iron/applications/qwen3_0.6b/qwen3_npu_int8.py"
-    fns = extract(ref, app, ["_set_int8", "_gptq_rows", "_pack_int8"], cls="Qwen3NPU")
+    fns = extract(ref, app, ["_set_int8", "_gptq_rows", "_pack_int8", "_set_wo_tiled"], cls="Qwen3NPU")
     captured = {}
 
     class FakeSelf:
@@ -114,6 +115,14 @@ def gptq_pack(ref: Path):
     # per-core tiles as the fused ops take them: 2 columns, 4 rows per tile
     fns["_set_int8"](FakeSelf(), "tiles", qws, scs, sum(Ms), K, 2, 4, signed=True)
     out["wire_signed_c2_t4"] = captured["tiles"].view(torch.uint8).numpy()
+    # fuse_o's Wo: 2 cores of 16 rows, windows of 3 tiles x 6 rows (rows 16-17 twice, 2 pad rows)
+    words = rng.integers(0, 2 ** 32, size=(K // 4, 32), dtype=np.uint64).astype(np.uint32)
+    qwo = torch.from_numpy(words.view(np.int32).copy())
+    sco = torch.from_numpy((rng.random((K // 128, 32)) * 0.05 + 1e-4).astype(np.float16))
+    w_q, s_mg = fns["_gptq_rows"](FakeSelf(), qwo, sco, signed=True)
+    fns["_set_wo_tiled"](FakeSelf(), "wo", w_q, s_mg, 32, K, 2, 6, 3)
+    out.update(qweight_o=qwo.numpy(), scales_o=sco.numpy().view(np.uint16),
+               wire_wo_c2_t6_n3=captured["wo"].view(torch.uint8).numpy())
     np.savez_compressed(OUT / "gptq_pack.npz", qweight_a=qws[0].numpy(), qweight_b=qws[1].numpy(),
                         scales_a=scs[0].numpy().view(np.uint16), scales_b=scs[1].numpy().view(np.uint16),
                         **out)

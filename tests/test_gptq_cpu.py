@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 import torch
 
-from iron_b200.gptq import gptq_rows, gptq_stack_to_wire, gptq_to_wire, load_qwen3_gptq
+from iron_b200.gptq import gptq_rows, gptq_stack_to_wire, gptq_to_wire, gptq_wo_tile_major, load_qwen3_gptq
 from iron_b200.qwen3 import Qwen3Config, wire_nbytes, wire_to_numpy
 from oracle import ops
 from oracle.bf16 import from_bits
@@ -46,6 +46,18 @@ def test_gptq_tile_wire_matches_reference_import(golden):
     assert np.array_equal(wire.numpy(), ops.pack_tile_wire(q, s_bits, 4, 2, "signed"))
     with pytest.raises(ValueError, match="do not split"):
         gptq_stack_to_wire(_parts(golden), 0, tile_m=3, cols=2)
+
+
+def test_gptq_wo_tile_major_matches_reference_import(golden):
+    """fuse_o's Wo wire: 2 cores of 16 rows, windows of 3 tiles x 6 rows, so rows 16-17
+    appear in both cores' windows and the last window reads 2 zero pad rows."""
+    qw, sc = torch.from_numpy(golden["qweight_o"]), torch.from_numpy(golden["scales_o"].view(np.float16))
+    wire = gptq_wo_tile_major(qw, sc, cols=2, tile_rows=6, tiles_per_core=3)
+    assert np.array_equal(wire.numpy(), golden["wire_wo_c2_t6_n3"])
+    with pytest.raises(ValueError, match="do not cover"):
+        gptq_wo_tile_major(qw, sc, cols=2, tile_rows=5, tiles_per_core=3)
+    with pytest.raises(ValueError, match="cores"):
+        gptq_wo_tile_major(qw, sc, cols=3, tile_rows=6, tiles_per_core=3)
 
 
 def test_gptq_wire_dequantises_to_checkpoint_weights(golden):

@@ -327,6 +327,22 @@ def decode_attention(Q, K, V, seq_pos: int, head_dim: int, num_heads: int, num_k
     return rnd(out.astype(F32))
 
 
+def decode_attention_batch(Q, K, V, s_kv_base: int, causal: bool, head_dim: int, num_heads: int,
+                           num_kv_heads: int):
+    """Multi-query (verify-mode) decode attention over one KV stream.
+
+    Restates ``cpu_reference_batch`` (decode_attn/test_batch.py:31-46), the golden of
+    DecodeAttention's ``batch_queries`` / ``num_new_tokens`` mode: the N new tokens sit
+    at positions ``s_kv_base .. s_kv_base + N - 1``; with ``causal`` query m attends
+    positions ``[0, s_kv_base + m]``, otherwise every position of K/V.  Each query is
+    ``decode_attention`` at its own boundary.  Q: (N, H, D); K, V: (KV, S, D); bf16 out
+    (N, H, D)."""
+    Q = np.asarray(Q)
+    S = np.asarray(K).shape[1]
+    return np.stack([decode_attention(Q[m], K, V, (s_kv_base + m) if causal else S - 1, head_dim, num_heads,
+                                      num_kv_heads, causal=True) for m in range(Q.shape[0])])
+
+
 def swiglu_mlp(cur, a, n_pf, Wg, Wu, Wd, D, FF, epsilon=1e-5):
     """Float32 SwiGLU MLP block golden (swiglu_mlp_dp/reference.py:8-38).
 

@@ -16,7 +16,7 @@ extracted with ``ast`` and executed unchanged in a small namespace.
 Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
   gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
   decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz,
-  gptq_pack.npz
+  gptq_pack.npz, decode_attn_batch.npz
 """
 
 from __future__ import annotations
@@ -128,11 +128,29 @@ def gptq_pack(ref: Path):
                         **out)
 
 
+def decode_attn_batch(ref: Path):
+    """DecodeAttention's multi-query verify mode: the batch test's CPU golden
+    (``cpu_reference_batch``, float32 out) on N(0, 1) data, 16 new tokens after 192
+    cached positions of a 256-position cache, causal and non-causal (16 query heads,
+    8 KV heads, head_dim 128)."""
+    fns = extract(ref, "iron/operators/decode_attn/test_batch.py", ["cpu_reference_batch"],
+                  extra_globals={"math": __import__("math")})
+    g = torch.Generator().manual_seed(29)
+    N, H, KV, D, S, base = 16, 16, 8, 128, 256, 192
+    Q = torch.randn(N, H, D, generator=g).to(torch.bfloat16)
+    K = torch.randn(KV, S, D, generator=g).to(torch.bfloat16)
+    V = torch.randn(KV, S, D, generator=g).to(torch.bfloat16)
+    out = {f"O_{tag}": fns["cpu_reference_batch"](Q, K, V, base, N, S, causal, head_dim=D, GQA=H // KV).numpy()
+           for causal, tag in ((True, "causal"), (False, "noncausal"))}
+    np.savez_compressed(OUT / "decode_attn_batch.npz", Q=bits(Q), K=bits(K), V=bits(V),
+                        dims=np.array([N, H, KV, D, S, base]), **out)
+
+
 def main(ref: Path, only: list[str] | None = None):
     setup_shim(ref)
     if only:
         for name in only:
-            {"gptq_pack": gptq_pack}[name](ref)
+            {"gptq_pack": gptq_pack, "decode_attn_batch": decode_attn_batch}[name](ref)
         print("wrote", ", ".join(only), "to", OUT)
         return
     rms = load(ref, "iron/operators/rms_norm/reference.py", "iron.operators.rms_norm.reference")
@@ -290,6 +308,7 @@ def main(ref: Path, only: list[str] | None = None):
                         v_new=bits(v2[0, :, T]), dims=np.array([D, H, KVH, HD, FF, T]),
                         **{k: bits(v) for k, v in wts.items()})
     gptq_pack(ref)
+    decode_attn_batch(ref)
     print("wrote fixtures to", OUT)
 
 

@@ -109,6 +109,29 @@ def test_decode_attention(golden, sp):
         assert np.abs(o - want).max() < 2e-2
 
 
+@pytest.mark.parametrize("tag", ["causal", "noncausal"])
+def test_decode_attention_batch_verify_mode(golden, tag):
+    """DecodeAttention's multi-query verify mode (decode_attn/test_batch.py:31-46): 16
+    new tokens after 192 cached positions.  The golden is float32: the oracle's bf16
+    output must be its rounding -- bit-exact at >= 99.9 %, one ulp where a float32 sum
+    rounds the other way, and more only for outputs so near zero that float32's
+    absolute summation error (256 terms) spans several of their ulps.  A causal query
+    m must equal the single-query oracle at position 192 + m."""
+    g = golden("decode_attn_batch")
+    N, H, KV, D, S, base = (int(v) for v in g["dims"])
+    Q, K, V = (from_bits(g[k]) for k in ("Q", "K", "V"))
+    o = ops.decode_attention_batch(Q, K, V, base, tag == "causal", D, H, KV)
+    assert o.shape == (N, H, D)
+    want = g[f"O_{tag}"]
+    ulp = np.abs(round_bits(o).astype(np.int32) - round_bits(want).astype(np.int32))
+    assert np.mean(ulp == 0) >= 0.999
+    far = ulp > 1
+    assert np.all(np.abs(o.astype(np.float64) - want)[far] <= 2e-5), np.abs(o - want)[far].max()
+    if tag == "causal":
+        for m in (0, 7, N - 1):
+            assert np.array_equal(o[m], ops.decode_attention(Q[m], K, V, base + m, D, H, KV))
+
+
 def test_swiglu_f32_goldens(golden):
     g = golden("swiglu")
     f = {k[4:]: from_bits(v) for k, v in g.items() if k.startswith("f32_")}

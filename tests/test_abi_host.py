@@ -85,3 +85,13 @@ def test_sequence_layout_slices_and_conflicts():
     r2 = RMSNorm(size=2048, num_aie_columns=1, num_channels=1, tile_size=1024)
     with pytest.raises(ValueError, match="conflicting"):
         OperatorSequence("t", [(r1, "x", "w", "y"), (r2, "y", "x")], ["x"], ["x"]).calculate_buffer_layout()
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    """The product has no CPU path: without the built library every call raises."""
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libiron_b200.so")
+    monkeypatch.setattr(_lib, "_LIB", None)
+    with pytest.raises(ImportError, match="not built"):
+        _lib.call("iron_gemv_w8a16", 16, 64, 1024, 32, 1, 0, 0, 0, 16, 1, None, 16, None)
+    with pytest.raises(ImportError, match="not built"):
+        _lib.launch_count()

@@ -343,6 +343,18 @@ def decode_attention_batch(Q, K, V, s_kv_base: int, causal: bool, head_dim: int,
                                       num_kv_heads, causal=True) for m in range(Q.shape[0])])
 
 
+def mha_prefill(Q, K, V, head_dim: int, num_heads: int, num_kv_heads: int):
+    """Causal GQA self-attention over a prompt (the prefill MHA golden).
+
+    Restates ``mha/reference.py:26-93``: ``scaled_dot_product_attention`` with
+    ``is_causal=True`` and scale ``1/sqrt(d)`` after ``repeat_interleave`` of the KV heads,
+    so query head h reads KV head ``h // (H/KV)`` and position i attends ``[0, i]`` --
+    ``decode_attention_batch`` with the new tokens starting at position 0.
+    Q: (H, S, D); K, V: (KV, S, D); bf16 out (H, S, D)."""
+    Qt = np.asarray(Q).transpose(1, 0, 2)
+    return decode_attention_batch(Qt, K, V, 0, True, head_dim, num_heads, num_kv_heads).transpose(1, 0, 2)
+
+
 def swiglu_mlp(cur, a, n_pf, Wg, Wu, Wd, D, FF, epsilon=1e-5):
     """Float32 SwiGLU MLP block golden (swiglu_mlp_dp/reference.py:8-38).
 

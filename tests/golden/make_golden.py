@@ -16,7 +16,7 @@ extracted with ``ast`` and executed unchanged in a small namespace.
 Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
   gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
   decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz,
-  gptq_pack.npz, decode_attn_batch.npz
+  gptq_pack.npz, decode_attn_batch.npz, mha_prefill.npz
 """
 
 from __future__ import annotations
@@ -146,11 +146,23 @@ def decode_attn_batch(ref: Path):
                         dims=np.array([N, H, KV, D, S, base]), **out)
 
 
+def mha_prefill(ref: Path):
+    """The prefill MHA golden (torch's causal SDPA in bf16, GQA by repeat_interleave)
+    from its own generator: 4 query heads over 2 KV heads, head_dim 64, a 128-token
+    prompt and a 96-token one (padded by the generator to 128 with zeros)."""
+    m = load(ref, "iron/operators/mha/reference.py", "ref_mha")
+    out = {}
+    for S in (128, 96):
+        g = m.generate_golden_reference(heads=4, S_q=S, S_kv=S, d=64, num_kv_heads=2)
+        out.update({f"{k}_{S}": bits(g[k]) for k in ("Q", "K", "V", "O")})
+    np.savez_compressed(OUT / "mha_prefill.npz", **out)
+
+
 def main(ref: Path, only: list[str] | None = None):
     setup_shim(ref)
     if only:
         for name in only:
-            {"gptq_pack": gptq_pack, "decode_attn_batch": decode_attn_batch}[name](ref)
+            {"gptq_pack": gptq_pack, "decode_attn_batch": decode_attn_batch, "mha_prefill": mha_prefill}[name](ref)
         print("wrote", ", ".join(only), "to", OUT)
         return
     rms = load(ref, "iron/operators/rms_norm/reference.py", "iron.operators.rms_norm.reference")
@@ -309,6 +321,7 @@ def main(ref: Path, only: list[str] | None = None):
                         **{k: bits(v) for k, v in wts.items()})
     gptq_pack(ref)
     decode_attn_batch(ref)
+    mha_prefill(ref)
     print("wrote fixtures to", OUT)
 
 

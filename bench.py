@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Qwen3-0.6B int8 (group 32) batch-1 greedy decode throughput on B200.
 
-Workload: 28 layers, hidden 1024, 16/8 heads, head_dim 128,
+Workload (Qwen3-0.6B, the headline configuration): 28 layers, hidden 1024, 16/8 heads, head_dim 128,
 SwiGLU 3072, vocab 151936 with a tied bf16 embedding/lm_head, projection
 weights int8 RTN in groups of 32 (synthetic, seeded), batch 1.  A 1024-token
 random prompt is prefilled token by token (as the reference does), then greedy
@@ -59,7 +59,7 @@ def parse():
                     help="independent decode streams per GPU (1: the one-launch step; more: the chained "
                          "kernels as a CUDA graph)")
     ap.add_argument("--model", choices=["qwen3-0.6b", "qwen3-8b", "llama-1b"], default="qwen3-0.6b",
-                    help="qwen3-8b: BASELINE config 4, tensor parallel over the torchrun world "
+                    help="qwen3-8b: Qwen3-8B int8, tensor parallel over the torchrun world "
                          "(NCCL), a synthetic --prompt-position KV context (default 4096); llama-1b: "
                          "config 5, --batch streams per GPU (default 64) with ragged synthetic KV "
                          "lengths U[256, 8192], replicas across GPUs")
@@ -373,7 +373,7 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_tp(args, rank, world, local_rank):
-    """BASELINE config 4: Qwen3-8B int8-g32 greedy decode, tensor parallel over the
+    """Qwen3-8B int8-g32 greedy decode, tensor parallel over the
     torchrun world (iron_b200/tp.py; NCCL all-reduce of the O / down partials, all-gather
     of the vocabulary-parallel argmax).  The context is ``--prompt`` positions of N(0, 1)
     K/V per stream (synthetic: prefilling 4096 tokens through 36 layers would only
@@ -504,7 +504,7 @@ def llama_step_bytes(cfg, lens):
 
 
 def run_llama(args, rank, world, local_rank):
-    """BASELINE config 5: Llama-3.2-1B-shaped bf16 decode, --batch independent streams per
+    """Llama-3.2-1B-shaped bf16 decode, --batch independent streams per
     GPU (64 by default) whose K/V lengths are drawn uniform in [256, 8192] (seeded per
     rank) over a synthetic N(0, 1) cache; replicas across the torchrun world."""
     import numpy as np

@@ -1,4 +1,4 @@
-"""Batched bf16 Llama decode on the B200 (Llama-3.2-1B shape).
+"""Batched bf16 Llama decode on the B200 (Llama-3.2-1B shape, many ragged streams per GPU).
 
 IRON runs Llama-3.2-1B on the NPU through bf16 operators (iron/applications/
 llama_3.2_1b/llama_npu.py) and on the CPU through llama_cpu.py.  Here one GPU

@@ -12,7 +12,7 @@ runs in the lm_head epilogue, so a decode step needs no host traffic beyond
 the 4-byte token it returns.
 
 Weights use the native wire (row-interleaved ``[K int8 | K/G bf16]``, signed
-payload) with quant group ``group`` (32 by default, as BASELINE's configs).
+payload) with quant group ``group`` (32 by default; the reference's checkpoint uses 128).
 """
 
 from __future__ import annotations
@@ -97,7 +97,7 @@ class Qwen3Weights:
     @classmethod
     def synthetic(cls, cfg: Qwen3Config, seed: int = 0, group: int = 32, device="cuda",
                   int8_lm_head: bool = False, n_layers: int | None = None):
-        """Seeded synthetic weights with BASELINE's distributions: projection masters
+        """Seeded synthetic weights (no checkpoint needed): projection masters
         N(0, 0.02) -> int8 RTN per group; RMSNorm weights 1 + N(0, 0.1); tied bf16
         embedding N(0, 0.02)."""
         g = torch.Generator(device=device).manual_seed(seed)

@@ -1,4 +1,5 @@
-"""Operator sweep: achieved HBM bandwidth of the decode kernels.
+"""Operator sweep: achieved HBM bandwidth of the decode kernels (int8 GEMV shapes x batch 1/8/32,
+decode attention batch x context).
 
 ``python -m iron_b200.sweep [--reps N] [--json FILE]`` times, on synthetic data
 (``--capture`` instead runs the small case of an ncu capture of the GEMV):

@@ -4,7 +4,7 @@
 fails when ``|out - ref| > max(abs_tol, rel_tol * (|out| + |ref|))``, and an
 optional ``max_error_rate`` lets a fraction of elements fail.  ``allclose``
 is the torch-style rule ``|out - ref| <= atol + rtol * |ref|`` used for the
-BASELINE gate (rtol 2e-2, atol 1e-2).
+decode path's bf16 gate (rtol 2e-2, atol 1e-2).
 """
 
 from __future__ import annotations

@@ -6,7 +6,7 @@ import torch
 from iron_b200.test_utils import allclose_report, cosine
 from oracle.bf16 import from_bits, round_bits
 
-RTOL, ATOL = 2e-2, 1e-2  # the BASELINE bf16 gate
+RTOL, ATOL = 2e-2, 1e-2  # the decode path's bf16 gate
 
 
 def dev_bf16(x) -> torch.Tensor:

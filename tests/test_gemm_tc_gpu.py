@@ -4,7 +4,7 @@ The kernel dequantises each weight to bf16(q*s) and accumulates in float32 on th
 tensor core, so it is checked (a) tightly against the same bf16-dequantised weights
 in float64 (only the float32 summation order and the output rounding differ) and
 (b) against the exact dequantised sum (oracle.ops.gemv_int8_exact) within one bf16
-rounding of every weight -- the BASELINE bf16 tolerance.  Shapes cover split K,
+rounding of every weight -- the bf16 gate.  Shapes cover split K,
 ragged row tiles, groups 64/128 (a split may start inside a group), the biased
 payload domain, the residual / float32 / gate-up + RMSNorm epilogues, and batches
 16..256."""

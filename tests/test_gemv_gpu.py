@@ -84,7 +84,7 @@ SHAPES = [(6144, 1024), (3072, 1024), (1024, 3072), (12288, 4096), (4096, 12288)
 @pytest.mark.parametrize("N,K", SHAPES)
 @pytest.mark.parametrize("batch", [1, 8, 32])
 def test_gemv_w8_baseline_shapes(N, K, batch):
-    """BASELINE operator sweep shapes, group 32, masters N(0,0.02), x ~ N(0,1)."""
+    """The operator sweep's shapes, group 32, masters N(0,0.02), x ~ N(0,1)."""
     torch.manual_seed(N + K + batch)
     w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
     wire = quantize_to_wire(w, 32)
@@ -98,7 +98,7 @@ def test_gemv_w8_baseline_shapes(N, K, batch):
         assert np.all(np.abs(out - exact) <= 2.0 ** -8 * (np.abs(exact) + mag) + 1e-30)
     else:
         assert_w8_exact(out, q, s, xh, "vs exact")
-    # vs the premul golden: the BASELINE tolerance widened by that golden's own rounding bound
+    # vs the premul golden: the bf16 gate widened by that golden's own rounding bound
     premul = rnd(ops.gemv_int8_premul(q, s, xh))
     bound = _premul_bound(q, s, xh)
     err = np.abs(out - premul)

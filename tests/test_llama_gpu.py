@@ -2,7 +2,7 @@
 the reference's llama_cpu.py (oracle/llama.py).
 
 Streams start at different positions over a shared random K/V prefix (ragged
-lengths, as BASELINE config 5); at 20 streams every projection and the lm_head run
+lengths, as the Llama benchmark); at 20 streams every projection and the lm_head run
 on the tcgen05 tensor cores, at 3 streams on the GEMV kernels.  The oracle's
 attention is its exact form (float64 softmax and context, one rounding), which the
 reference's bf16 op chain approximates; the oracle's bf16 chain itself is pinned to

@@ -196,7 +196,7 @@ def _check_mlp(got, exact_chain, premul_chain, golden, rel=0.05, abs_=0.05):
     """The kernels compute every int8 matvec as the exact dequantised sum (the
     operators' reference(), swiglu_mlp_dp/op_ours.py:543-570) with float64
     accumulation, so they are held to the kernel-faithful chain with exact matvecs on
-    the device's own inputs: BASELINE tolerance and >= 99% bit-exact.  Against the
+    the device's own inputs: the bf16 gate and >= 99% bit-exact.  Against the
     reference golden (swiglu_mlp_dp/test.py:53-91) the reference test's tolerance
     (test.py:190-191) applies, widened by how far that golden moves when only its
     matvec rounding changes (|premul chain - exact chain|) and by the golden's own

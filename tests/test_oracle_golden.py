@@ -203,7 +203,7 @@ def test_llama_block_matches_reference_cpu_path(golden):
     of inputs (measured: rsqrt(bf16 1.0546875) = 0.9765625, the correctly rounded value
     is 0.97265625), and the post-attention RMSNorm of this fixture meets such an input:
     its scale lands one bf16 ulp apart, which moves every later value by ~0.4 %.  The
-    block output is therefore checked within the BASELINE gate (rtol 2e-2, atol 1e-2)."""
+    block output is therefore checked within the bf16 gate (rtol 2e-2, atol 1e-2)."""
     from oracle.llama import LlamaShape, OracleLlama
     g = golden("llama_block")
     D, H, KVH, HD, FF, T = (int(v) for v in g["dims"])

@@ -231,17 +231,25 @@ int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, con
  * RMSNorm and the lm_head with greedy argmax.  The arithmetic of every stage is
  * the one of the per-operator entry points above (iron_qkv_head with the golden
  * RMSNorm form, iron_decode_attn, iron_mlp_block, iron_rmsnorm mode 1,
- * iron_lm_head_*_argmax); the O and down projections are summed along K in
- * float64 pieces before their single bf16 rounding.  QKV and gate/up weights are
- * in the native wire (tile_m = 1, signed); O and down also in the column-blocked
- * forms made by iron_qwen3_pack_wo_heads / iron_qwen3_pack_wd_cols.  Every pointer
- * in the descriptor is a device pointer, weight and table pointers 16-byte aligned
- * (weight rows are bulk-copied); `layers` points to a DEVICE array of n_layers
+ * iron_lm_head_*_argmax): exact int8 x block-floating-point dot products summed in
+ * float64, one bf16 rounding per projection output; the O projection is summed over
+ * the KV-head groups in group order.  Results do not depend on timing: two steps from
+ * the same state give the same bits.
+ * The projections read their weights in 16-row tiles made once by
+ * iron_qwen3_pack_tiles (the *_t fields); the plain wires stay in the descriptor for
+ * the caller's other paths.  wqkv_t holds the QKV rows in KV-head-group order: for
+ * each KV head h the q rows of query heads h*Hq/Hkv .. (h+1)*Hq/Hkv - 1, then the k
+ * rows of head h, then its v rows.  wo_t holds, for each KV head h, the tiles of the
+ * D rows of Wo restricted to h's (Hq/Hkv)*HD columns.  lm_w8, when set, is the int8
+ * lm_head in tiles (iron_qwen3_pack_tiles of the V x D wire).
+ * Every pointer in the descriptor is a device pointer, weight and table pointers
+ * 16-byte aligned (they are bulk-copied); `layers` points to a DEVICE array of n_layers
  * iron_qwen3_layer.  The kernel reads the token from tok[0] (embed_input != 0) or
  * the hidden state from x, the position from pos[0], writes the argmax to tok[0],
  * the final hidden state to x and, when advance != 0, moves pos/seq_len/kv_off one
- * token on.  Barrier counters live in `sync` (iron_qwen3_sync_words() int32 words)
- * and float64 accumulators in `attn_ws` (iron_qwen3_attn_ws_bytes()); both must be
+ * token on.  Activations pass between the CTAs as epoch-tagged words in `attn_ws`
+ * (iron_qwen3_attn_ws_bytes()); `sync` holds iron_qwen3_sync_words() int32 words (the
+ * error word at index 1, the token epoch, the argmax arrival count); both must be
  * zero before the first step.  Every wait is bounded: on timeout sync[1] holds a
  * nonzero code, the step returns early, and iron_qwen3_sync_reset() must clear
  * both before the next step. */
@@ -255,9 +263,11 @@ typedef struct iron_qwen3_layer {
   const void* wg;         /* (FF, D) wire */
   const void* wu;         /* (FF, D) wire */
   const void* wd;         /* (D, FF) wire */
-  const void* wo_heads;   /* iron_qwen3_pack_wo_heads(wo) */
-  const void* wd_cols;    /* iron_qwen3_pack_wd_cols(wd): int8 (FF/4, D, 4) */
-  const uint16_t* wd_col_scales; /* ... and its scales (FF/group, D) bf16 */
+  const void* wqkv_t;     /* tiles of wqkv, rows in KV-head-group order */
+  const void* wo_t;       /* tiles of wo, per KV head h its column block */
+  const void* wg_t;       /* tiles of wg */
+  const void* wu_t;       /* tiles of wu */
+  const void* wd_t;       /* tiles of wd */
 } iron_qwen3_layer;
 
 typedef struct iron_qwen3_model {
@@ -266,15 +276,15 @@ typedef struct iron_qwen3_model {
   const iron_qwen3_layer* layers;  /* device array */
   const uint16_t* final_norm;      /* (D) */
   const uint16_t* embed;           /* (V, D) bf16: embedding, and lm_head when lm_w8 == NULL */
-  const void* lm_w8;               /* (V, D) int8 wire lm_head, or NULL */
+  const void* lm_w8;               /* int8 lm_head tiles (iron_qwen3_pack_tiles of the (V, D) wire), or NULL */
   const uint16_t* angles;          /* (max_seq, HD) interleaved [cos, sin] */
   uint16_t* kv;                    /* (n_layers, Hkv, 2*max_seq*HD) per-token [K_t|V_t] */
   uint16_t* x;                     /* (D) hidden state in (embed_input == 0) / final hidden state out */
-  uint16_t* raw;                   /* ((Hq+2Hkv)*HD) */
+  uint16_t* raw;                   /* ((Hq+2Hkv)*HD), unused by the step kernel */
   uint16_t* attn;                  /* (Hq*HD), unused by the step kernel */
   uint16_t* x1;                    /* (D), unused by the step kernel */
   uint16_t* gh;                    /* (FF), unused by the step kernel */
-  float* attn_ws;                  /* iron_qwen3_attn_ws_bytes(): split partials + accumulators */
+  float* attn_ws;                  /* iron_qwen3_attn_ws_bytes(): the hand-off words */
   void* cand;                      /* iron_qwen3_cand_bytes() */
   int32_t* tok;
   int32_t* pos;
@@ -292,19 +302,18 @@ int64_t iron_qwen3_cand_bytes(void);
 /* Grid size the step kernel will use on the current device (one CTA per SM). */
 int iron_qwen3_grid(const iron_qwen3_model* m);
 int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream);
-/* Weight forms for the step kernel's K-split projections, made once at load time from
- * native wires (no reference counterpart: they re-order the wires that
- * qwen3_npu_int8.py:381-436 packs for the NPU).
- * wo_heads: for each KV head h, the D rows of Wo restricted to h's (Hq/Hkv)*HD
- *   columns as [int8 columns | their bf16 group scales | zero pad to 16 bytes];
- *   iron_qwen3_pack_wo_heads_bytes() bytes.
- * wd_cols: int8 (FF/4, D, 4) = Wd[r, 4j..4j+3] at [j][r], and bf16 scales
- *   (FF/group, D) = the scale of row r, group g at [g][r]. */
-int64_t iron_qwen3_pack_wo_heads_bytes(int D, int QD, int Hkv, int group);
-int iron_qwen3_pack_wo_heads(const void* wo_wire, int D, int QD, int Hkv, int group, void* out, void* stream);
-int iron_qwen3_pack_wd_cols(const void* wd_wire, int D, int FF, int group, void* out_q, uint16_t* out_scales,
-                            void* stream);
-/* Zero the sync words and the accumulators (after a timed-out step, or before first use). */
+/* Weight tiles for the step kernel, made once at load time from plain wires (no
+ * reference counterpart: they re-order the wires that qwen3_npu_int8.py:381-436 packs
+ * for the NPU).  Rows [0, M) of a wire whose rows are `row_stride` bytes apart
+ * ([K_full int8 | K_full/group bf16]), columns [col0, col0 + K), become ceil(M/16)
+ * tiles of iron_qwen3_tiles_bytes(M, K, group) bytes in all: per 32-column block,
+ * 32 lanes x 16 bytes in the A-fragment order of mma.sync m16n8k32 (lane l: rows
+ * l/4 and l/4 + 8, columns 4(l%4).. and 16 + 4(l%4)..), then per quantisation group
+ * the scales of rows g and g + 8 side by side (g < 8).  Rows past M are zero. */
+int64_t iron_qwen3_tiles_bytes(int M, int K, int group);
+int iron_qwen3_pack_tiles(const void* wire, int64_t row_stride, int M, int K_full, int col0, int K, int group,
+                          void* out, void* stream);
+/* Zero the sync words and the hand-off words (after a timed-out step, or before first use). */
 int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream);
 
 /* ---- tensor-parallel building blocks ---------------------------------------------

@@ -52,9 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "iron_qwen3_grid": (I, [P]),
     "iron_qwen3_decode_step": (I, [P, I, I, P]),
     "iron_qwen3_sync_reset": (I, [P, P]),
-    "iron_qwen3_pack_wo_heads_bytes": (I64, [I, I, I, I]),
-    "iron_qwen3_pack_wo_heads": (I, [P, I, I, I, I, P, P]),
-    "iron_qwen3_pack_wd_cols": (I, [P, I, I, I, P, P, P]),
+    "iron_qwen3_tiles_bytes": (I64, [I, I, I]),
+    "iron_qwen3_pack_tiles": (I, [P, I64, I, I, I, I, I, P, P]),
     "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),
 }
 

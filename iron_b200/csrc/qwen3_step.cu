@@ -1,48 +1,42 @@
 // One greedy Qwen3 decode token (batch 1) as ONE persistent cooperative kernel.
 //
-// Why one kernel.  At batch 1 a decode token streams ~0.9 GB (weights, KV) but
-// each projection is only a few microseconds of HBM time, so the token is bound
-// by the latency of the dependency chain between projections, not by bandwidth.
-// The kernel keeps that chain short:
+// Why one kernel.  At batch 1 a Qwen3-0.6B token streams ~0.9 GB (weights, K/V),
+// but a single projection is only a few microseconds of HBM time: the token is
+// bound by the latency of the dependency chain between projections.  Weights and
+// cached K/V do not depend on activations, so a producer warp per CTA streams them
+// into a shared-memory ring (CTA-local cp.async.bulk) about a layer ahead, and the
+// compute warps only ever wait for activations.
 //
-//   - One CTA per SM.  The CTAs form Hkv KV-head groups of about N / Hkv CTAs.
-//     Group h computes the q/k/v rows of KV head h (QKV rows are taken in head
-//     order), runs head h's attention with one split of the positions per CTA,
-//     merges the splits and multiplies the merged heads by head h's column block
-//     of Wo.  Inside the attention block only the group's own CTAs wait for one
-//     another.
-//   - The O and down projections are split along K: O by KV head, down by the
-//     slice of gate/up rows a CTA computed itself, so the SwiGLU output never
-//     leaves the CTA.  Partial sums are float64 and meet through float64 atomics
-//     in per-layer accumulators.
-//   - Per layer that leaves two grid barriers (after O, after down) and two
-//     group barriers (after QKV, after the attention splits).
-//   - Weights do not depend on activations, so each CTA's weight share streams
-//     through a shared-memory ring by cp.async.bulk (CTA-local copies).  A producer
-//     warp issues the copies as far ahead as the ring allows (about a layer), so
-//     issuing never sits on the compute path.  The attention KV range is
-//     prefetched to L2 one phase early.
+// Hand-offs.  Activations move between CTAs as flagged 64-bit words: the payload
+// and the (token, layer) epoch in one store, so a reader that sees the epoch it
+// waits for also has the data.  There is no grid barrier, no fence on the hand-off
+// path and no floating-point atomic: every sum is formed in a fixed order, and two
+// runs from the same state give the same bits.  Per layer (CTAs form Hkv KV-head
+// groups of N / Hkv CTAs):
 //
-// Weight layouts.  QKV and gate/up rows use the native wire (tile_m = 1, row
-// [K int8 | K/G bf16 scales]).  O uses wo_heads: for each KV head h the rows of Wo
-// restricted to h's GQ*HD columns, [GQ*HD int8 | GQ*HD/G bf16 | pad to 16 bytes].
-// Down uses wd_cols: int8 [FF/4][D][4] (four consecutive K columns of one row in a
-// 32-bit word) and scales [FF/G][D] bf16, so a CTA's K slice is contiguous.
-// iron_qwen3_pack_wo_heads / iron_qwen3_pack_wd_cols build both from the wires.
+//   x  --(all CTAs)-->  RMSNorm + QKV rows of KV head h (group h's CTAs, 16-row tiles)
+//   q/k/v words  -->   every CTA of group h: q/k RMSNorm + RoPE, one split of head h's
+//                      positions (flash decoding); the split's (m, l, o) as words
+//   split words  -->   every CTA of group h merges the splits and multiplies the merged
+//                      heads by head h's column block of Wo for its O row tiles: a
+//                      K-split partial per (h, row) as words
+//   O partials   -->   every CTA: x1 = x + sum over h (fixed order), RMSNorm, its
+//                      gate/up row tiles, SiLU * up: h values as words
+//   h words      -->   the CTAs holding down row tiles: x_next = x1 + Wd h as words
 //
-// Arithmetic.  The stages use the device arithmetic of the per-operator entry
-// points: activations staged as exact int16 block floating point (hi + lo words),
-// dp2a sums per 16 (or 4) columns, float64 accumulation, the golden RMSNorm form
-// for the QKV input, q/k and the final norm, the kernel form for the MLP norm, and
-// the same bf16 roundings between stages.  The K-split partial sums meet in
-// float64, so a projection output equals the unsplit float64 sum up to float64
-// summation order before its single bf16 rounding.
+// Projections.  Weight tiles of 16 rows are pre-packed in the A-fragment order of
+// mma.sync m16n8k32 (s8): a lane loads its fragment of a 32-column block with one
+// conflict-free 16-byte shared load.  Activations are staged as exact 31-bit block
+// floating point, four balanced signed bytes per value (the B fragment: digit d of
+// value k in column d), so one MMA gives exact integer sums of 16 rows x 32 columns;
+// the sums are scaled by weight scale x activation scale in float64 (exact) and
+// accumulated in float64.  The warps split a tile's k-blocks into slices whose sums
+// are added in slice order.  One bf16 rounding per output, as the per-operator
+// kernels (iron_gemv_w8a16) do.
 //
-// Synchronisation.  Barriers are int32 counters in global memory whose targets
-// grow with the layer; the last CTA of the token resets them.  Every wait is
-// bounded by %globaltimer: on timeout the CTA records an error code and returns;
-// the other CTAs see the code in their own waits and return too.  In-flight bulk
-// copies are drained (bounded) before a CTA exits.
+// Every wait is bounded by %globaltimer: on timeout a CTA records an error code in
+// the sync words and leaves; the other CTAs see it in their own waits and leave too.
+// In-flight bulk copies are drained (bounded) before a CTA exits.
 #include <algorithm>
 
 #include "common.cuh"
@@ -50,38 +44,39 @@
 namespace iron {
 namespace qstep {
 
-// 8 compute warps and one producer warp (168 registers a thread, no spills; more warps
-// cap registers at 128 and spill in the inner loops)
+// 8 compute warps and one producer warp
 constexpr int NT = 256, NWARP = NT / 32;
-constexpr int HDIM = 128;        // head_dim of the step kernel
-constexpr int NMB = 16;          // ring slots (chunks in flight at most)
-constexpr int GMAX = 24;         // most CTAs in one KV-head group (attention splits)
-constexpr int XREP = 4;          // down-projection accumulator replicas: KV-head group h adds into
-                                 // replica h % XREP (atomics to one address serialise in L2)
-constexpr int SLICE_MAX = 32;    // widest down-projection K slice of one CTA
-constexpr int PIECE = 32768;     // bytes per cp.async.bulk instruction
+constexpr int HDIM = 128;         // head_dim of the step kernel
+constexpr int TR = 16;            // rows per weight tile (the MMA's M)
+constexpr int NMB = 16;           // ring slots (chunks in flight at most)
+constexpr int GMAX = 24;          // most CTAs in one KV-head group (attention splits)
+constexpr int KVP = 64;           // cached positions per K/V chunk (32 KB)
+constexpr int NTMAX = 16;         // most tiles of one projection in one CTA
+constexpr int HKVMAX = 8;         // most KV heads (O partial sums summed per row)
+constexpr int LMT = 4;            // int8 lm_head tiles per chunk
+constexpr int XBS = 288;          // bytes of one 32-column block of B fragments (padded)
+constexpr int PIECE = 32768;      // bytes per cp.async.bulk instruction
 constexpr int SMEM_MAX = 227 * 1024;
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;  // per wait
 
-// sync words (the G2 counters follow the Hkv G1 counters)
-enum { SYNC_B1 = 0, SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_B2 = 3, SYNC_PARITY = 4, SYNC_EPOCH = 5, SYNC_G1 = 8 };
-enum { ERR_BARRIER = 1, ERR_COPY = 2, ERR_INPUT = 3 };
-// chunk kinds of a layer, in stream order; the lm_head chunks follow the last layer
-enum { CK_QKV = 0, CK_O = 1, CK_GU = 2, CK_D = 3 };
+enum { SYNC_ERR = 1, SYNC_ARGMAX = 2, SYNC_EPOCH = 3, SYNC_WORDS = 8 };
+enum { ERR_WAIT = 1, ERR_COPY = 2, ERR_INPUT = 3 };
 
 struct Kp {
   iron_qwen3_model m;
   int embed_input, advance;
   int ring;     // ring bytes
-  int lm_rows;  // lm_head rows per chunk
-  int kst;      // staging length max(D, GQ*HD)
+  int lm_rows;  // bf16 lm_head rows per chunk
+  int kmax;     // longest staged activation (max of D, GQ*HD, FF)
+  int hbn;      // bf16 values of the polled-vector buffer
 };
 
 __host__ __device__ inline int rowb(int K, int G) { return K + 2 * (K / G); }
-__host__ __device__ inline int rowb_heads(int GQ, int G) { return (rowb(GQ * HDIM, G) + 15) & ~15; }
+// bytes of one packed tile of 16 rows x K
+__host__ __device__ inline size_t tileb(int K, int G) { return (size_t)TR * rowb(K, G); }
 
 // ---------------------------------------------------------------------------
-// PTX helpers: mbarrier, bulk copies, acquire loads, timer
+// PTX helpers: mbarrier, bulk copies, flagged words, timer
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t* b) {
@@ -105,63 +100,106 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(src), "r"(bytes), "r"(sa(b))
                : "memory");
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// float64 add to global memory with no value returned (the accumulators only need the sum)
-__device__ __forceinline__ void red_add(double* p, double v) {
-  asm volatile("red.global.add.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
+__device__ __forceinline__ unsigned ld_acquire(const int32_t* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ unsigned ld_relaxed(const int32_t* p) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// D = A (16x32 s8, row) * B (32x8 s8, col), exact int32
+__device__ __forceinline__ void mma_s8(int (&c)[4], const uint4& a, uint2 b) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(0));
+}
 
-// Flagged words: (epoch << 32 | data) written by one 64-bit store, so a reader that
-// finds the epoch it waits for also has the data; no fence, counter or poll of a
-// separate word sits between producer and consumer.  Every word is rewritten each
-// token with a larger epoch; the buffers are zeroed with the sync words.
+// Flagged words.  Two forms: (epoch << 32 | 32-bit payload) for bf16 pairs and
+// float32 values, and (16-bit tag << 48 | the top 48 bits of a float64) for the O
+// partial sums (sign, exponent and 36 significand bits: 2^-37 relative, far below
+// the bf16 rounding that follows).  Each word is written once per (token, layer)
+// with a value that differs from its previous one; zero is never a valid tag.
 __device__ __forceinline__ void ll_put(unsigned long long* p, uint32_t data, uint32_t epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | data;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ll_put_d(unsigned long long* p, double v, uint32_t tag16) {
+  const unsigned long long w =
+      ((unsigned long long)tag16 << 48) | ((unsigned long long)__double_as_longlong(v) >> 16);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ double ll_val_d(unsigned long long w) {
+  return __longlong_as_double((long long)(w << 16));
 }
 __device__ __forceinline__ unsigned long long ll_ld(const unsigned long long* p) {
   unsigned long long w;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
-// the data of word p once it carries `epoch` (bounded: on timeout or a set error word
-// *bad is set and 0 returned)
-__device__ __forceinline__ uint32_t ll_get(const unsigned long long* p, uint32_t epoch, int32_t* sync, int& bad) {
-  unsigned long long w = ll_ld(p);
-  if ((uint32_t)(w >> 32) == epoch) return (uint32_t)w;
-  const unsigned long long t0 = gtimer();
+__device__ __forceinline__ uint32_t tag16_of(uint32_t epoch) { return epoch % 65535u + 1u; }
+
+// Wait (bounded) until the U words addr(0..U-1) whose bit is set in `want` carry the
+// tag (their bits from `tshift` up equal `tag`).  v[u] holds word u's last load (the
+// caller issues the first loads together); each round reloads every word still
+// pending at once, so a round costs one memory round trip however many words lag.
+// False when the wait gave up (timeout, or the grid's error word is set).
+template <int U, class Addr>
+__device__ __forceinline__ bool poll_rounds(Addr addr, unsigned long long (&v)[U], uint32_t want, uint32_t tag,
+                                            int tshift, int32_t* sync) {
+  unsigned long long t0 = 0;
   for (unsigned it = 0;; ++it) {
-    w = ll_ld(p);
-    if ((uint32_t)(w >> 32) == epoch) return (uint32_t)w;
-    if ((it & 15) == 15) {
-      if (ld_relaxed(&sync[SYNC_ERR]) != 0) break;
+    uint32_t pending = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (((want >> u) & 1u) && (uint32_t)(v[u] >> tshift) != tag) pending |= 1u << u;
+    if (!pending) return true;
+    if (it == 0) {
+      t0 = gtimer();
+    } else if ((it & 7) == 0) {
+      if (ld_relaxed(&sync[SYNC_ERR]) != 0) return false;
       if (gtimer() - t0 > TIMEOUT_NS) {
-        atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_BARRIER);
-        break;
+        atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_WAIT);
+        return false;
       }
     }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if ((pending >> u) & 1u) v[u] = ll_ld(addr(u));
   }
-  bad = 1;
-  return 0;
 }
 
-__device__ __forceinline__ unsigned ld_acquire(const int32_t* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// Wait (bounded) until every word w[i], i = threadIdx.x + j * NT < n, carries the tag;
+// then f(i, word) for each, in increasing i.  The U words of a thread are loaded and
+// reloaded together (U <= 32).
+template <int U, class F>
+__device__ __forceinline__ bool poll(const unsigned long long* w, int n, uint32_t tag, int tshift, int32_t* sync,
+                                     F f) {
+  for (int base = 0; base < n; base += U * NT) {
+    unsigned long long v[U];
+    uint32_t want = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * NT + threadIdx.x;
+      v[u] = i < n ? ll_ld(w + i) : 0ull;
+      if (i < n) want |= 1u << u;
+    }
+    const unsigned long long* wb = w + base + threadIdx.x;
+    if (!poll_rounds<U>([&](int u) { return wb + u * NT; }, v, want, tag, tshift, sync)) return false;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if ((want >> u) & 1u) f(base + u * NT + threadIdx.x, v[u]);
+  }
+  return true;
 }
 
 // Phase timestamps for profiling builds (-DIRON_STEP_PROFILE): thread 0 of each CTA
@@ -174,21 +212,25 @@ __device__ unsigned long long* g_step_prof;
   do {                                                                                                         \
     if (threadIdx.x == 0 && g_step_prof) g_step_prof[((size_t)blockIdx.x * 64 + (row)) * 32 + (k)] = gtimer(); \
   } while (0)
-#define STEP_CLK(row, k)                                                                                          \
-  do {                                                                                                            \
-    if (threadIdx.x == 0 && g_step_prof) g_step_prof[((size_t)blockIdx.x * 64 + (row)) * 32 + (k)] = clock64(); \
-  } while (0)
 #else
 #define STEP_MARK(row, k) \
   do {                    \
-  } while (0)
-#define STEP_CLK(row, k) \
-  do {                   \
   } while (0)
 #endif
 
 // barrier of the NT compute threads only (the producer warp runs on its own)
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+
+// barrier of the compute threads that also returns whether any of them passed true
+__device__ __forceinline__ bool cvote_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(NT)
+      : "memory");
+  return r != 0;
+}
 
 __device__ __forceinline__ double csum_d(double v, double* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -218,44 +260,68 @@ __host__ __device__ inline void head_group(int c, int N, int Hkv, int& h, int& c
 
 struct Plan {
   int h, gi, gsz;       // KV-head group, index in the group, group size
-  int q0, q1;           // group-local QKV rows: q rows of the group's GQ heads, then k, then v
-  int o0, o1;           // O rows (against head h's column block)
-  int u0, u1;           // gate/up rows / 4 = down-projection K slice / 4
-  int ga, nsg;          // first scale group of the slice, scale groups it touches
-  int hlo, hhi, hnch;   // lm_head rows, chunks
+  int qt0, qnt;         // QKV tiles of group h (q rows of its heads, then k, then v)
+  int ot0, ont;         // O tiles of head h's column block (D / TR per head)
+  int gt0, gnt;         // gate/up pair tiles
+  int dt0, dnt;         // down tiles
+  int kst, ken, own;    // cached K/V positions [kst, ken) of this split; it holds pos
+  int nkv, cpl;         // K/V chunks per layer; chunks per layer (4 + nkv)
+  int hlo, hhi, hnch;   // lm_head rows (bf16) or tiles (int8), chunks
   int total;            // chunks of the token
-  uint32_t bytes[4];    // chunk bytes per layer kind
 };
 
-__device__ Plan make_plan(const Kp& p) {
-  const iron_qwen3_model& m = p.m;
-  Plan P;
-  const int N = gridDim.x, c = blockIdx.x, G = m.group, GQ = m.Hq / m.Hkv, D = m.D;
+// Tiles per CTA are balanced two ways: QKV and O within the KV-head group, gate/up
+// over all CTAs; the down tiles go to the CTAs holding the smaller gate/up share.
+__host__ __device__ inline void plan_tiles(const iron_qwen3_model& m, int c, int N, Plan& P) {
+  const int GQ = m.Hq / m.Hkv;
   int c0, c1;
   head_group(c, N, m.Hkv, P.h, c0, c1);
   P.gi = c - c0;
   P.gsz = c1 - c0;
-  part((GQ + 2) * HDIM, P.gi, P.gsz, P.q0, P.q1);
-  part(D, P.gi, P.gsz, P.o0, P.o1);
-  part(m.FF / 4, c, N, P.u0, P.u1);
-  const int k0 = 4 * P.u0, k1 = 4 * P.u1;
-  P.ga = k0 / G;
-  P.nsg = k1 > k0 ? (k1 - 1) / G - P.ga + 1 : 0;
-  P.bytes[CK_QKV] = (uint32_t)(P.q1 - P.q0) * rowb(D, G);
-  P.bytes[CK_O] = (uint32_t)(P.o1 - P.o0) * rowb_heads(GQ, G);
-  P.bytes[CK_GU] = 2u * (uint32_t)(k1 - k0) * rowb(D, G);
-  P.bytes[CK_D] = (uint32_t)(P.u1 - P.u0) * D * 4 + (uint32_t)P.nsg * D * 2;
-  part(m.V, c, N, P.hlo, P.hhi);
-  P.hnch = (P.hhi - P.hlo + p.lm_rows - 1) / p.lm_rows;
-  P.total = 4 * m.n_layers + P.hnch;
-  return P;
+  int lo, hi;
+  part((GQ + 2) * HDIM / TR, P.gi, P.gsz, lo, hi);
+  P.qt0 = lo;
+  P.qnt = hi - lo;
+  part(m.D / TR, P.gi, P.gsz, lo, hi);
+  P.ot0 = lo;
+  P.ont = hi - lo;
+  const int TG = m.FF / TR, TD = m.D / TR;
+  part(TG, c, N, lo, hi);
+  P.gt0 = lo;
+  P.gnt = hi - lo;
+  const int q = TG / N, nlight = N - TG % N;
+  const int extras_below = (int)((long long)TG * c / N) - q * c;
+  if (P.gnt == q) {
+    part(TD, c - extras_below, nlight, lo, hi);
+    P.dt0 = lo;
+    P.dnt = hi - lo;
+  } else {
+    P.dt0 = 0;
+    P.dnt = 0;
+  }
 }
 
-// source row of group-local QKV row r of KV head h (q rows of heads h*GQ.., k, v)
-__device__ __forceinline__ int qkv_src_row(int r, int h, int GQ, int Hq, int Hkv) {
-  if (r < GQ * HDIM) return h * GQ * HDIM + r;
-  if (r < (GQ + 1) * HDIM) return Hq * HDIM + h * HDIM + (r - GQ * HDIM);
-  return (Hq + Hkv) * HDIM + h * HDIM + (r - (GQ + 1) * HDIM);
+__device__ Plan make_plan(const Kp& p, int pos) {
+  const iron_qwen3_model& m = p.m;
+  Plan P;
+  const int N = gridDim.x, c = blockIdx.x;
+  plan_tiles(m, c, N, P);
+  const int L = pos + 1, chunk = (L + P.gsz - 1) / P.gsz;
+  const int st = min(L, P.gi * chunk), en = min(L, st + chunk);
+  P.own = pos >= st && pos < en;
+  P.kst = st;
+  P.ken = max(st, min(en, pos));
+  P.nkv = (P.ken - P.kst + KVP - 1) / KVP;
+  P.cpl = 4 + P.nkv;
+  if (m.lm_w8) {
+    part((m.V + TR - 1) / TR, c, N, P.hlo, P.hhi);
+    P.hnch = (P.hhi - P.hlo + LMT - 1) / LMT;
+  } else {
+    part(m.V, c, N, P.hlo, P.hhi);
+    P.hnch = (P.hhi - P.hlo + p.lm_rows - 1) / p.lm_rows;
+  }
+  P.total = P.cpl * m.n_layers + P.hnch;
+  return P;
 }
 
 // ---------------------------------------------------------------------------
@@ -270,37 +336,36 @@ struct RingState {                // shared by the producer lane and compute thr
 
 struct Smem {
   uint8_t* ring;
-  uint16_t* xhi;   // [kst] bf16 bits, then int16 hi words
-  uint16_t* xlo;   // [kst] norm weights before the BFP pass, then lo words
-  float* xs;       // [kst / 16] block factors
+  uint8_t* xb;     // [kmax / 32][XBS] B fragments of the staged activation
+  double* xsd;     // [kmax / G] activation group scales (x 2^-15)
+  double* part;    // [2][NTMAX][TR] slice sums of a projection
   uint16_t* sx;    // [D] residual x (bf16 bits)
   uint16_t* sx1;   // [D] residual x1
-  float* xf;       // [D] final normed x (bf16 lm_head path)
-  float* ghv;      // [SLICE_MAX] this CTA's SwiGLU outputs
-  uint16_t* dh;    // [SLICE_MAX] their int16 hi words
-  uint16_t* dl;    // [SLICE_MAX] lo words
-  float* att;      // attention scratch
-  float* mst;      // [GMAX][GQ][HD + 2] the split partials of this CTA's KV head
+  uint16_t* nw;    // [D] weights of the next RMSNorm
+  uint16_t* hb;    // [hbn] polled bf16 vectors (q/k/v rows, merged heads, h)
+  uint16_t* outb;  // [NTMAX * TR] bf16 outputs of a projection before they are published
+  float* att;      // q [GQ][HD], k [HD], v [HD], warp partials [NWARP][GQ][HD + 2]
+  float* ml;       // [GMAX][GQ][2] the group's split (m, l)
+  float* xf;       // [D] final normed x (lm_head)
   iron_qwen3_layer* lay;  // [n_layers] copy of the layer pointer table
   double* red;     // [32]
-  uint64_t* mbar;  // [NMB + 1]
+  uint64_t* mbar;  // [NMB]
   RingState* rs;
-  int* flag;       // [8]; flag[4] holds the down slice's block factor (float bits)
+  int* flag;       // [8]
 };
 
 __host__ __device__ inline size_t att_floats(int GQ) {
   return (size_t)GQ * HDIM + 2 * HDIM + (size_t)NWARP * GQ * (HDIM + 2);
 }
 
-// bytes of everything but the ring (carve's layout: 17 arrays, each rounded up to 16 bytes)
-__host__ __device__ inline size_t fixed_smem(int kst, int D, int GQ, int n_layers) {
-  size_t o = 32 * 8 + (NMB + 1) * 8 + sizeof(RingState) + 8 * 4;
-  o += (size_t)kst * 4 + (size_t)(kst / 16) * 4;
-  o += (size_t)D * 2 * 2 + (size_t)D * 4;
-  o += SLICE_MAX * 4 + SLICE_MAX * 2 * 2;
-  o += att_floats(GQ) * 4 + (size_t)GMAX * GQ * (HDIM + 2) * 4;
+// bytes of everything but the ring (carve's layout: 16 arrays, each rounded up to 16 bytes)
+__host__ __device__ inline size_t fixed_smem(int kmax, int hbn, int D, int G, int GQ, int n_layers) {
+  size_t o = 32 * 8 + NMB * 8 + sizeof(RingState) + 8 * 4;
+  o += (size_t)(kmax / 32) * XBS + (size_t)(kmax / G) * 8 + 2 * NTMAX * TR * 8;
+  o += (size_t)D * 2 * 3 + (size_t)hbn * 2 + NTMAX * TR * 2;
+  o += att_floats(GQ) * 4 + (size_t)GMAX * GQ * 2 * 4 + (size_t)D * 4;
   o += (size_t)n_layers * sizeof(iron_qwen3_layer);
-  return o + 17 * 16 + 64;
+  return o + 16 * 16 + 64;
 }
 
 __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
@@ -312,27 +377,29 @@ __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
     o += (bytes + 15) & ~(size_t)15;
     return r;
   };
+  const iron_qwen3_model& m = p.m;
   s.red = (double*)take(32 * 8);
-  s.mbar = (uint64_t*)take((NMB + 1) * 8);  // ring slots, then the split-merge copy
+  s.mbar = (uint64_t*)take(NMB * 8);
   s.rs = (RingState*)take((sizeof(RingState) + 15) & ~(size_t)15);
   s.flag = (int*)take(8 * 4);
-  s.xhi = (uint16_t*)take((size_t)p.kst * 2);
-  s.xlo = (uint16_t*)take((size_t)p.kst * 2);
-  s.xs = (float*)take((size_t)(p.kst / 16) * 4);
-  s.sx = (uint16_t*)take((size_t)p.m.D * 2);
-  s.sx1 = (uint16_t*)take((size_t)p.m.D * 2);
-  s.xf = (float*)take((size_t)p.m.D * 4);
-  s.ghv = (float*)take(SLICE_MAX * 4);
-  s.dh = (uint16_t*)take(SLICE_MAX * 2);
-  s.dl = (uint16_t*)take(SLICE_MAX * 2);
+  s.xb = take((size_t)(p.kmax / 32) * XBS);
+  s.xsd = (double*)take((size_t)(p.kmax / m.group) * 8);
+  s.part = (double*)take(2 * NTMAX * TR * 8);
+  s.sx = (uint16_t*)take((size_t)m.D * 2);
+  s.sx1 = (uint16_t*)take((size_t)m.D * 2);
+  s.nw = (uint16_t*)take((size_t)m.D * 2);
+  s.hb = (uint16_t*)take((size_t)p.hbn * 2);
+  s.outb = (uint16_t*)take(NTMAX * TR * 2);
   s.att = (float*)take(att_floats(GQ) * 4);
-  s.mst = (float*)take((size_t)GMAX * GQ * (HDIM + 2) * 4);
-  s.lay = (iron_qwen3_layer*)take((size_t)p.m.n_layers * sizeof(iron_qwen3_layer));
+  s.ml = (float*)take((size_t)GMAX * GQ * 2 * 4);
+  s.xf = (float*)take((size_t)m.D * 4);
+  s.lay = (iron_qwen3_layer*)take((size_t)m.n_layers * sizeof(iron_qwen3_layer));
   return s;
 }
 
 // ---------------------------------------------------------------------------
-// the chunk stream: per layer QKV, O, gate/up, down; then the lm_head
+// the chunk stream: per layer QKV tiles, the split's K/V pieces, O tiles, gate/up
+// pair tiles, down tiles; then the lm_head
 // ---------------------------------------------------------------------------
 struct Seg {
   const uint8_t* src;
@@ -340,65 +407,49 @@ struct Seg {
 };
 
 // segments of chunk i, copied back to back into one ring slot; returns their count
-__device__ int chunk_segs(const Kp& p, const Plan& P, const Smem& S, int i, Seg (&sg)[3]) {
+__device__ int chunk_segs(const Kp& p, const Plan& P, const Smem& S, int i, Seg (&sg)[2]) {
   const iron_qwen3_model& m = p.m;
   const int G = m.group, D = m.D, GQ = m.Hq / m.Hkv;
-  const int lay = i >> 2;
+  const int lay = i / P.cpl;
   if (lay >= m.n_layers) {
-    const int j = i - 4 * m.n_layers;
-    const int r0 = P.hlo + j * p.lm_rows, r1 = min(P.hhi, r0 + p.lm_rows);
-    const uint32_t rb = m.lm_w8 ? rowb(D, G) : D * 2;
-    const uint8_t* base = m.lm_w8 ? (const uint8_t*)m.lm_w8 : (const uint8_t*)m.embed;
-    sg[0] = {base + (size_t)r0 * rb, (uint32_t)(r1 - r0) * rb};
+    const int j = i - P.cpl * m.n_layers;
+    if (m.lm_w8) {
+      const int t0 = P.hlo + j * LMT, t1 = min(P.hhi, t0 + LMT);
+      sg[0] = {(const uint8_t*)m.lm_w8 + (size_t)t0 * tileb(D, G), (uint32_t)((t1 - t0) * tileb(D, G))};
+    } else {
+      const int r0 = P.hlo + j * p.lm_rows, r1 = min(P.hhi, r0 + p.lm_rows);
+      sg[0] = {(const uint8_t*)m.embed + (size_t)r0 * D * 2, (uint32_t)(r1 - r0) * D * 2};
+    }
     return 1;
   }
   const iron_qwen3_layer& L = S.lay[lay];
-  switch (i & 3) {
-    case CK_QKV: {
-      const uint32_t rb = rowb(D, G);
-      int n = 0, r = P.q0;
-      while (r < P.q1) {  // split at the q / k / v boundaries of the group-local order
-        const int lim = r < GQ * HDIM ? GQ * HDIM : (r < (GQ + 1) * HDIM ? (GQ + 1) * HDIM : (GQ + 2) * HDIM);
-        const int e = min(P.q1, lim);
-        sg[n++] = {(const uint8_t*)L.wqkv + (size_t)qkv_src_row(r, P.h, GQ, m.Hq, m.Hkv) * rb,
-                   (uint32_t)(e - r) * rb};
-        r = e;
-      }
-      return n;
-    }
-    case CK_O: {
-      const uint32_t rb = rowb_heads(GQ, G);
-      sg[0] = {(const uint8_t*)L.wo_heads + ((size_t)P.h * D + P.o0) * rb, (uint32_t)(P.o1 - P.o0) * rb};
-      return 1;
-    }
-    case CK_GU: {
-      const uint32_t rb = rowb(D, G);
-      const size_t off = (size_t)(4 * P.u0) * rb;
-      const uint32_t bytes = (uint32_t)(4 * (P.u1 - P.u0)) * rb;
-      sg[0] = {(const uint8_t*)L.wg + off, bytes};
-      sg[1] = {(const uint8_t*)L.wu + off, bytes};
-      return 2;
-    }
-    default: {
-      sg[0] = {(const uint8_t*)L.wd_cols + (size_t)P.u0 * D * 4, (uint32_t)(P.u1 - P.u0) * D * 4};
-      sg[1] = {(const uint8_t*)L.wd_col_scales + (size_t)P.ga * D * 2, (uint32_t)P.nsg * D * 2};
-      return 2;
-    }
+  const int r = i - lay * P.cpl;
+  if (r == 0) {  // QKV: group h's tiles are contiguous (rows packed in head-group order)
+    const size_t tb = tileb(D, G);
+    sg[0] = {(const uint8_t*)L.wqkv_t + ((size_t)P.h * ((GQ + 2) * HDIM / TR) + P.qt0) * tb, (uint32_t)(P.qnt * tb)};
+    return 1;
   }
-}
-
-__device__ __forceinline__ uint32_t chunk_bytes(const Kp& p, const Plan& P, int i) {
-  if ((i >> 2) < p.m.n_layers) {  // a switch, not an indexed array: P stays in registers
-    switch (i & 3) {
-      case CK_QKV: return P.bytes[CK_QKV];
-      case CK_O: return P.bytes[CK_O];
-      case CK_GU: return P.bytes[CK_GU];
-      default: return P.bytes[CK_D];
-    }
+  if (r <= P.nkv) {  // cached K/V rows [K_t | V_t] of positions p0 .. p0 + n
+    const int p0 = P.kst + (r - 1) * KVP, n = min(KVP, P.ken - p0);
+    const uint16_t* head = m.kv + ((size_t)lay * m.Hkv + P.h) * 2 * (size_t)m.max_seq * HDIM;
+    sg[0] = {(const uint8_t*)(head + (size_t)p0 * 2 * HDIM), (uint32_t)n * 4 * HDIM};
+    return 1;
   }
-  const int j = i - 4 * p.m.n_layers;
-  const int r0 = P.hlo + j * p.lm_rows, r1 = min(P.hhi, r0 + p.lm_rows);
-  return (uint32_t)(r1 - r0) * (p.m.lm_w8 ? rowb(p.m.D, p.m.group) : p.m.D * 2);
+  const int k = r - P.nkv;
+  if (k == 1) {  // O: head h's column block, row tiles [ot0, ot0 + ont)
+    const size_t tb = tileb(GQ * HDIM, G);
+    sg[0] = {(const uint8_t*)L.wo_t + ((size_t)P.h * (D / TR) + P.ot0) * tb, (uint32_t)(P.ont * tb)};
+    return 1;
+  }
+  if (k == 2) {  // gate then up tiles [gt0, gt0 + gnt)
+    const size_t tb = tileb(D, G);
+    sg[0] = {(const uint8_t*)L.wg_t + (size_t)P.gt0 * tb, (uint32_t)(P.gnt * tb)};
+    sg[1] = {(const uint8_t*)L.wu_t + (size_t)P.gt0 * tb, (uint32_t)(P.gnt * tb)};
+    return 2;
+  }
+  const size_t tb = tileb(m.FF, G);  // down
+  sg[0] = {(const uint8_t*)L.wd_t + (size_t)P.dt0 * tb, (uint32_t)(P.dnt * tb)};
+  return 1;
 }
 
 // wait (bounded) until the copies of chunks [from, to) have landed
@@ -413,16 +464,16 @@ __device__ void drain(const Smem& S, int from, int to) {
 // The producer lane: issue every chunk of the token in stream order, each as soon
 // as its ring space and slot are released.  Every wait is bounded; it stops when
 // the compute threads leave early or the grid's error word is set, and then waits
-// for its copies in flight.
-// (inlined: a call that takes P or S by address would move the compute threads' copies
-// to local memory, which the small L1 left beside 227 KB of shared memory does not keep)
+// for its copies in flight.  A chunk of 0 bytes completes its slot's phase at once.
 __device__ __forceinline__ void producer(const Kp& p, const Plan& P, const Smem& S, int32_t* sync) {
   volatile RingState& rs = *S.rs;
   const uint32_t R = (uint32_t)p.ring;
   unsigned long long head = 0;
   bool stop = false;
   for (int i = 0; i < P.total && !stop; ++i) {
-    const uint32_t bytes = chunk_bytes(p, P, i);
+    Seg sg[2];
+    const int ns = chunk_segs(p, P, S, i, sg);
+    const uint32_t bytes = sg[0].bytes + (ns > 1 ? sg[1].bytes : 0u);
     unsigned long long start = head;
     const uint32_t off = (uint32_t)(start % R);
     if (off + bytes > R) start += R - off;  // does not fit before the end: wrap
@@ -451,14 +502,10 @@ __device__ __forceinline__ void producer(const Kp& p, const Plan& P, const Smem&
     rs.slot[sl] = (uint32_t)(start % R);
     rs.end[sl] = start + bytes;
     head = start + bytes;
-    Seg sg[3];
-    const int ns = chunk_segs(p, P, S, i, sg);
     uint8_t* dst = S.ring + (uint32_t)(start % R);
     fence_proxy_async();  // the compute threads' reads of this space happen before the async writes
     mbar_expect(&S.mbar[sl], bytes);
-#pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      if (s >= ns) break;
+    for (int s = 0; s < ns; ++s) {
       for (uint32_t o = 0; o < sg[s].bytes; o += PIECE)
         bulk_g2s(dst + o, sg[s].src + o, min((uint32_t)PIECE, sg[s].bytes - o), &S.mbar[sl]);
       dst += sg[s].bytes;
@@ -466,21 +513,6 @@ __device__ __forceinline__ void producer(const Kp& p, const Plan& P, const Smem&
     rs.issued = i + 1;
   }
   if (stop) drain(S, rs.consumed, rs.issued);
-}
-
-// ---------------------------------------------------------------------------
-// bounded waits (thread 0)
-// ---------------------------------------------------------------------------
-__device__ bool wait_count(int32_t* sync, int word, unsigned target) {
-  const unsigned long long t0 = gtimer();
-  for (unsigned it = 0;; ++it) {
-    if (ld_acquire(&sync[word]) >= target) return true;
-    if (ld_acquire(&sync[SYNC_ERR]) != 0) return false;
-    if ((it & 63) == 63 && gtimer() - t0 > TIMEOUT_NS) {
-      atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_BARRIER);
-      return false;
-    }
-  }
 }
 
 __device__ bool wait_slot(uint64_t* mb, int32_t* sync, uint32_t parity) {
@@ -498,164 +530,89 @@ __device__ bool wait_slot(uint64_t* mb, int32_t* sync, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------
-// activation staging (the arithmetic of gemv_w8_kernel's prologue)
+// activation staging: K values -> B fragments of exact 31-bit block floating point
+// (the arithmetic of gemv_mma_kernel's prologue, one batch row)
 // ---------------------------------------------------------------------------
-// In place: xhi holds the bf16 bits of K values -> int16 hi words; xlo lo words;
-// xs the group factors.  Eight lanes per quant group.
-__device__ __forceinline__ void bfp_stage_p(uint16_t* xhi, uint16_t* xlo, float* xs, int K, int G) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int sub = lane >> 3, sl = lane & 7, per = G / 8;
-  const int ng = K / G;
-  for (int g0 = wid * 4; g0 < ng; g0 += NWARP * 4) {
-    const int gi = g0 + sub;
-    const bool valid = gi < ng;
-    uint16_t* base = xhi + (size_t)(valid ? gi : 0) * G + sl * per;
-    float v[16];
+// src(k, v) fills v[0..7] with the values k..k+7 (bf16-representable floats).  Eight
+// consecutive values per thread, G / 8 lanes per quantisation group.
+template <int G, class Src>
+__device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src) {
+  constexpr int TEAM = G / 8;
+  const int nchunk = K >> 3;
+  for (int c0 = 0; c0 < nchunk; c0 += NT) {
+    const int c = c0 + threadIdx.x;
+    const bool ok = c < nchunk;  // a group's TEAM lanes are all in range or all out
+    float v[8];
+    if (ok) {
+      src(c * 8, v);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    }
     float mx = 0.f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e)
-      if (e < per) {
-        v[e] = valid ? bf2f(base[e]) : 0.f;
-        mx = fmaxf(mx, fabsf(v[e]));
-      }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
+#pragma unroll
+    for (int o = 1; o < TEAM; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(~0u, mx, o));
+    if (!ok) continue;
     float sc, inv;
     bfp_scale(mx, sc, inv);
-    if (valid) {
+    // X = rn(v * 2^(30-e)); Y = (X + 0x808080) ^ 0x808080 has the balanced base-256
+    // digits d0..d3 of X as its four bytes
+    uint32_t Y[8];
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (e < per) {
-          const float t = v[e] * sc;
-          const int hi = __float2int_rn(t);
-          base[e] = (uint16_t)(int16_t)hi;
-          xlo[(base - xhi) + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
-        }
-      if (sl == 0) xs[gi] = inv;
+    for (int e = 0; e < 8; ++e) Y[e] = (uint32_t)(__float2int_rn(v[e] * sc * 32768.0f) + 0x808080) ^ 0x808080u;
+    const int k = c * 8;
+    uint8_t* blk = S.xb + (size_t)(k >> 5) * XBS;
+#pragma unroll
+    for (int qd = 0; qd < 2; ++qd) {  // 4 values -> one word per digit (4x4 byte transpose)
+      const uint32_t t0 = __byte_perm(Y[4 * qd], Y[4 * qd + 1], 0x5140);
+      const uint32_t t1 = __byte_perm(Y[4 * qd], Y[4 * qd + 1], 0x7362);
+      const uint32_t t2 = __byte_perm(Y[4 * qd + 2], Y[4 * qd + 3], 0x5140);
+      const uint32_t t3 = __byte_perm(Y[4 * qd + 2], Y[4 * qd + 3], 0x7362);
+      const uint32_t wd[4] = {__byte_perm(t0, t2, 0x5410), __byte_perm(t0, t2, 0x7632),
+                              __byte_perm(t1, t3, 0x5410), __byte_perm(t1, t3, 0x7632)};
+      // B fragment: column n = digit, lane n * 4 + (kk & 15) / 4, register kk / 16
+      const int kk = (k & 31) + 4 * qd;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) *(uint32_t*)(blk + ((d * 4 + ((kk & 15) >> 2)) * 8 + (kk >> 4) * 4)) = wd[d];
     }
-  }
-}
-
-__device__ __forceinline__ void bfp_stage(const Smem& S, int K, int G) { bfp_stage_p(S.xhi, S.xlo, S.xs, K, G); }
-
-// RMSNorm of the bf16 bits in `src` (shared) with the weight bits already in xlo
-// -> bf16 bits in xhi (mode 0 kernel form, 1 golden form); `outf` (shared)
-// receives the values as floats when non-null.
-__device__ __forceinline__ void stage_norm_p(uint16_t* xhi, const uint16_t* xlo, double* red, const uint16_t* src, int K,
-                                         float eps, int mode, float* outf) {
-  double ss = 0.0;
-  for (int i = threadIdx.x; i < K; i += NT) ss += rms_sq(bf2f(src[i]), mode);
-  ss = csum_d(ss, red);
-  const RmsCoef rc = rms_coef(ss, K, eps, mode);
-  for (int i = threadIdx.x; i < K; i += NT) {
-    const uint16_t o = f2bf(rms_apply(bf2f(src[i]), bf2f(xlo[i]), rc));
-    xhi[i] = o;
-    if (outf) outf[i] = bf2f(o);
-  }
-}
-
-__device__ __forceinline__ void stage_norm(const Smem& S, const uint16_t* src, int K, float eps, int mode, float* outf) {
-  stage_norm_p(S.xhi, S.xlo, S.red, src, K, eps, mode, outf);
-}
-
-// dst[i] = bf16(src[i] + bf16(sum over the nrep replicas acc[r*D + i])) over the D
-// residual rows, replicas summed in a fixed order; every accumulator load of a thread
-// is issued before the first store (D <= 4 * NT)
-template <int NREP>
-__device__ __forceinline__ void resid_add(uint16_t* dst, const uint16_t* src, const double* acc, int D) {
-  constexpr int MAXV = 4;
-  double v[MAXV][NREP];
-#pragma unroll
-  for (int k = 0; k < MAXV; ++k) {
-    const int i = threadIdx.x + k * NT;
-#pragma unroll
-    for (int r = 0; r < NREP; ++r) v[k][r] = i < D ? __ldcg(acc + (size_t)r * D + i) : 0.0;
-  }
-#pragma unroll
-  for (int k = 0; k < MAXV; ++k) {
-    const int i = threadIdx.x + k * NT;
-    double a = v[k][0];
-#pragma unroll
-    for (int r = 1; r < NREP; ++r) a += v[k][r];
-    if (i < D) dst[i] = f2bf(bf2f(src[i]) + rbf_d(a));
-  }
-}
-
-// A layer-phase prologue in one pass.  With acc: x = bf16(src + bf16(sum of the NREP
-// accumulator replicas)) into dst (every load of a thread issued first); without: x is
-// dst as it stands.  Then RMSNorm(x) * w (w's bf16 bits already in xlo; mode 0 kernel
-// form, 1 golden form) goes straight into exact int16 block floating point (xhi, xlo,
-// xs), eight lanes per quant group: the arithmetic of stage_norm + bfp_stage with one
-// shared-memory pass.  outf (shared) gets the normalised values, trace (global) gets x.
-template <int G, int NREP>
-__device__ __forceinline__ void prologue(const Smem& S, uint16_t* dst, const uint16_t* src, const double* acc, int D,
-                                         float eps, int mode, float* outf, uint16_t* trace) {
-  constexpr int MAXV = 4;  // D <= 4 * NT
-  double ss = 0.0;
-  if (acc) {
-    double v[MAXV][NREP];
-#pragma unroll
-    for (int k = 0; k < MAXV; ++k) {
-      const int i = threadIdx.x + k * NT;
-#pragma unroll
-      for (int r = 0; r < NREP; ++r) v[k][r] = i < D ? __ldcg(acc + (size_t)r * D + i) : 0.0;
-    }
-#pragma unroll
-    for (int k = 0; k < MAXV; ++k) {
-      const int i = threadIdx.x + k * NT;
-      double a = v[k][0];
-#pragma unroll
-      for (int r = 1; r < NREP; ++r) a += v[k][r];
-      if (i < D) {
-        const uint16_t x = f2bf(bf2f(src[i]) + rbf_d(a));
-        dst[i] = x;
-        ss += rms_sq(bf2f(x), mode);
-        if (trace) trace[i] = x;
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < D; i += NT) {
-      ss += rms_sq(bf2f(dst[i]), mode);
-      if (trace) trace[i] = dst[i];
-    }
-  }
-  ss = csum_d(ss, S.red);  // its barriers also publish dst
-  const RmsCoef rc = rms_coef(ss, D, eps, mode);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int sub = lane >> 3, sl = lane & 7, per = G / 8;
-  const int ng = D / G;
-  for (int g0 = wid * 4; g0 < ng; g0 += NWARP * 4) {
-    const int gi = g0 + sub;
-    const bool valid = gi < ng;
-    const int base = (valid ? gi : 0) * G + sl * per;
-    float v[16];
-    float mx = 0.f;
-#pragma unroll
-    for (int e = 0; e < 16; ++e)
-      if (e < per) {
-        v[e] = valid ? bf2f(f2bf(rms_apply(bf2f(dst[base + e]), bf2f(S.xlo[base + e]), rc))) : 0.f;
-        mx = fmaxf(mx, fabsf(v[e]));
-      }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    float sc, inv;
-    bfp_scale(mx, sc, inv);
-    if (valid) {
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (e < per) {
-          if (outf) outf[base + e] = v[e];
-          const float t = v[e] * sc;
-          const int hi = __float2int_rn(t);
-          S.xhi[base + e] = (uint16_t)(int16_t)hi;
-          S.xlo[base + e] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
-        }
-      if (sl == 0) S.xs[gi] = inv;
-    }
+    if (k % G == 0) S.xsd[k / G] = (double)inv * (1.0 / 32768.0);
   }
   csync();
+}
+
+// RMSNorm (mode 0 kernel form, 1 golden form) of the D bf16 values x (shared) with
+// the weights nw (shared) -> bf16 -> staged digits; outf (shared) gets the values.
+template <int G>
+__device__ __forceinline__ void norm_stage(const Smem& S, const uint16_t* x, int D, float eps, int mode,
+                                           float* outf) {
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < D; i += NT) ss += rms_sq(bf2f(x[i]), mode);
+  ss = csum_d(ss, S.red);  // its barriers also publish x and nw
+  const RmsCoef rc = rms_coef(ss, D, eps, mode);
+  stage_digits<G>(S, D, [&](int k, float(&v)[8]) {
+    const uint4 xa = *(const uint4*)(x + k), wa = *(const uint4*)(S.nw + k);
+    const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w}, ww[4] = {wa.x, wa.y, wa.z, wa.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float xv = bf2f((uint16_t)(xw[e >> 1] >> (16 * (e & 1))));
+      const float wv = bf2f((uint16_t)(ww[e >> 1] >> (16 * (e & 1))));
+      v[e] = rbf(rms_apply(xv, wv, rc));
+      if (outf) outf[k + e] = v[e];
+    }
+  });
+}
+
+// stage K bf16 values from shared memory (no norm)
+template <int G>
+__device__ __forceinline__ void plain_stage(const Smem& S, const uint16_t* x, int K) {
+  stage_digits<G>(S, K, [&](int k, float(&v)[8]) {
+    const uint4 xa = *(const uint4*)(x + k);
+    const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = bf2f((uint16_t)(xw[e >> 1] >> (16 * (e & 1))));
+  });
 }
 
 // K bf16 values (K % 8 == 0, read-only data) into shared memory with 16-byte loads
@@ -664,118 +621,79 @@ __device__ __forceinline__ void load_ro(uint16_t* dst, const uint16_t* src, int 
 }
 
 // ---------------------------------------------------------------------------
-// int8 rows from shared memory: LPR lanes per row, 16 columns a lane per step, NR rows
-// (2NR for gate/up pairs) per lane group at once: sum_k q*s*x exactly as
-// gemv_w8_kernel with LO staging and float64 accumulation.  The 16-column dp2a sums
-// run as two chains of four so that their latencies overlap.
+// Projection of nt packed weight tiles (16 rows x K) in a ring slot against the
+// staged activation.  PAIR: the slot holds nt gate tiles then nt up tiles.  Tile
+// layout: K/32 blocks of 512 bytes (lane L's A fragment at L * 16), then K/G groups
+// of 8 x 2 bf16 scales (rows g and g + 8 in one word).  The warps split each tile's
+// blocks into SL slices; the slice sums meet in shared memory and are added in slice
+// order.  epi(t, r, a, b) runs once per row r of tile t (b: the up row's sum).
 // ---------------------------------------------------------------------------
-template <int G, int NR, int LPR>
-__device__ __forceinline__ void rows_dot(const uint8_t* const (&rp)[NR], int K, const Smem& S, double (&out)[NR]) {
-  const int sub = threadIdx.x & (LPR - 1);
-  double acc[NR];
+template <int G, bool PAIR, class Epi>
+__device__ __forceinline__ void gemv_tiles(const uint8_t* slot, int nt, int K, const Smem& S, Epi epi) {
+  constexpr int NW = PAIR ? 2 : 1;
+  if (nt <= 0) return;  // uniform across the CTA
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int KB = K >> 5;
+  const size_t TB = tileb(K, G);
+  const int SL = nt >= NWARP ? 1 : NWARP / nt;
+  const int items = nt * SL;
+  for (int it = wid; it < items; it += NWARP) {
+    const int t = it / SL, s = it - t * SL;
+    const int kb0 = s * KB / SL, kb1 = (s + 1) * KB / SL;
+    const uint8_t* tb[NW];
+    tb[0] = slot + (size_t)t * TB;
+    if (PAIR) tb[NW - 1] = slot + (size_t)(nt + t) * TB;
+    double acc[NW][2];
 #pragma unroll
-  for (int i = 0; i < NR; ++i) acc[i] = 0.0;
+    for (int w = 0; w < NW; ++w) acc[w][0] = acc[w][1] = 0.0;
 #pragma unroll 2
-  for (int c = sub; c < (K >> 4); c += LPR) {
-    const int g = (c * 16) / G;
-    const uint4 xa = *(const uint4*)(S.xhi + c * 16), xb = *(const uint4*)(S.xhi + c * 16 + 8);
-    const uint4 la = *(const uint4*)(S.xlo + c * 16), lb = *(const uint4*)(S.xlo + c * 16 + 8);
-    const float xsc = S.xs[g];
-    uint4 w[NR];
-    float sv[NR];
+    for (int kb = kb0; kb < kb1; ++kb) {
+      const uint2 bv = *(const uint2*)(S.xb + (size_t)kb * XBS + lane * 8);
+      const int gl = (kb * 32) / G;
+      const double xs = S.xsd[gl];
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      w[i] = *(const uint4*)(rp[i] + c * 16);
-      sv[i] = bf2f(((const uint16_t*)(rp[i] + K))[g]);
+      for (int w = 0; w < NW; ++w) {
+        const uint4 a = *(const uint4*)(tb[w] + (size_t)kb * 512 + lane * 16);
+        const uint32_t sw = *(const uint32_t*)(tb[w] + (size_t)KB * 512 + gl * 32 + (lane >> 2) * 4);
+        int cc[4];
+        mma_s8(cc, a, bv);
+        acc[w][0] = fma((double)(cc[0] + 256 * cc[1]), (double)bf_lo(sw) * xs, acc[w][0]);
+        acc[w][1] = fma((double)(cc[2] + 256 * cc[3]), (double)bf_hi(sw) * xs, acc[w][1]);
+      }
     }
+    // odd lanes hold the digit pieces weighted 2^16; after the pair sum lanes 4g hold
+    // rows g and g + 8 (lanes 4g + 2 hold the empty second batch row)
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      int a0 = __dp2a_lo((int)xa.x, (int)w[i].x, 0), a1 = __dp2a_hi((int)xa.y, (int)w[i].x, 0);
-      a0 = __dp2a_lo((int)xa.z, (int)w[i].y, a0);
-      a1 = __dp2a_hi((int)xa.w, (int)w[i].y, a1);
-      a0 = __dp2a_lo((int)xb.x, (int)w[i].z, a0);
-      a1 = __dp2a_hi((int)xb.y, (int)w[i].z, a1);
-      a0 = __dp2a_lo((int)xb.z, (int)w[i].w, a0);
-      a1 = __dp2a_hi((int)xb.w, (int)w[i].w, a1);
-      int l0 = __dp2a_lo((int)la.x, (int)w[i].x, 0), l1 = __dp2a_hi((int)la.y, (int)w[i].x, 0);
-      l0 = __dp2a_lo((int)la.z, (int)w[i].y, l0);
-      l1 = __dp2a_hi((int)la.w, (int)w[i].y, l1);
-      l0 = __dp2a_lo((int)lb.x, (int)w[i].z, l0);
-      l1 = __dp2a_hi((int)lb.y, (int)w[i].z, l1);
-      l0 = __dp2a_lo((int)lb.z, (int)w[i].w, l0);
-      l1 = __dp2a_hi((int)lb.w, (int)w[i].w, l1);
-      const long long t = (long long)(a0 + a1) * 32768 + (l0 + l1);
-      acc[i] = fma((double)t, (double)(sv[i] * xsc) * (1.0 / 32768.0), acc[i]);
+    for (int w = 0; w < NW; ++w)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        double v = acc[w][hh];
+        if (lane & 1) v *= 65536.0;
+        acc[w][hh] = v + __shfl_xor_sync(~0u, v, 1);
+      }
+    if ((lane & 3) == 0) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        double* pp = S.part + (size_t)w * NTMAX * TR + (size_t)it * TR;
+        pp[lane >> 2] = acc[w][0];
+        pp[(lane >> 2) + 8] = acc[w][1];
+      }
     }
   }
-#pragma unroll
-  for (int i = 0; i < NR; ++i) {
-    double v = acc[i];
-#pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    out[i] = v;
-  }
-}
-
-// The n rows of one chunk (rb bytes each; with PAIR the n gate rows, then the n up
-// rows).  The NG = NT/LPR lane groups take rows b + rg + i*NG of each block of
-// NG*R rows; every lane of a warp runs the same trip count (the shuffles need it).
-template <int G, int R, int LPR, bool PAIR, class Epi>
-__device__ void chunk_rows(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
-  constexpr int NR = PAIR ? 2 * R : R;
-  constexpr int NG = NT / LPR;
-  const int rg = threadIdx.x / LPR, sub = threadIdx.x & (LPR - 1);
-  for (int b = 0; b < n; b += NG * R) {
-    const uint8_t* rp[NR];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int r = min(b + rg + i * NG, n - 1);
-      rp[i] = wb + (size_t)r * rb;
-      if (PAIR) rp[R + i] = wb + (size_t)(n + r) * rb;
+  csync();
+  for (int e = threadIdx.x; e < nt * TR; e += NT) {
+    const int t = e / TR, r = e - t * TR;
+    double a = 0.0, b = 0.0;
+    for (int s = 0; s < SL; ++s) {
+      a += S.part[(size_t)(t * SL + s) * TR + r];
+      if (PAIR) b += S.part[(size_t)NTMAX * TR + (size_t)(t * SL + s) * TR + r];
     }
-    double out[NR];
-    rows_dot<G, NR, LPR>(rp, K, S, out);  // every lane of the group holds all the sums
-#pragma unroll
-    for (int i = 0; i < R; ++i)  // lane i of the group finishes row i, the epilogues side by side
-      if (sub == i && b + rg + i * NG < n) epi(b + rg + i * NG, out[i], PAIR ? out[R + i] : 0.0);
+    epi(t, r, a, b);
   }
 }
 
-// one row-block width R per call site keeps a single copy of the row loop in the kernel
-template <int G, int LPR, int R, bool PAIR, class Epi>
-__device__ __forceinline__ void chunk_gemv(const uint8_t* wb, int n, int rb, int K, const Smem& S, Epi epi) {
-  chunk_rows<G, R, LPR, PAIR>(wb, n, rb, K, S, epi);
-}
-
-// bf16 rows with float32 activations: the lm_head arithmetic of gemv_bf16_kernel
-template <int R>
-__device__ __forceinline__ void rows_dot_bf16(const uint8_t* const (&rp)[R], int K, const float* xf, float (&out)[R]) {
-  const int lane = threadIdx.x & 31;
-  float a[R];
-#pragma unroll
-  for (int i = 0; i < R; ++i) a[i] = 0.f;
-  for (int c = lane; c < (K >> 3); c += 32) {
-    const float4 x0 = *(const float4*)(xf + c * 8), x1 = *(const float4*)(xf + c * 8 + 4);
-    uint4 w[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) w[i] = *(const uint4*)(rp[i] + c * 16);
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      a[i] = fmaf(bf_lo(w[i].x), x0.x, a[i]);
-      a[i] = fmaf(bf_hi(w[i].x), x0.y, a[i]);
-      a[i] = fmaf(bf_lo(w[i].y), x0.z, a[i]);
-      a[i] = fmaf(bf_hi(w[i].y), x0.w, a[i]);
-      a[i] = fmaf(bf_lo(w[i].z), x1.x, a[i]);
-      a[i] = fmaf(bf_hi(w[i].z), x1.y, a[i]);
-      a[i] = fmaf(bf_lo(w[i].w), x1.z, a[i]);
-      a[i] = fmaf(bf_hi(w[i].w), x1.w, a[i]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
-}
-
-// the same with this lane's activations held in registers: xr[k] = xf[(lane + 32k)*8 ..]
+// bf16 rows with this lane's activations held in registers: xr[k] = xf[(lane + 32k)*8 ..]
+// (the lm_head arithmetic of gemv_bf16_kernel)
 template <int R, int KC>
 __device__ __forceinline__ void rows_dot_bf16_reg(const uint8_t* const (&rp)[R], const float (&xr)[KC][8],
                                                   float (&out)[R]) {
@@ -804,254 +722,74 @@ __device__ __forceinline__ void rows_dot_bf16_reg(const uint8_t* const (&rp)[R],
   for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
 }
 
+// the same for any D (a multiple of 256) with the activations in shared memory
+template <int R>
+__device__ __forceinline__ void rows_dot_bf16(const uint8_t* const (&rp)[R], int K, const float* xf, float (&out)[R]) {
+  const int lane = threadIdx.x & 31;
+  float a[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) a[i] = 0.f;
+  for (int c = lane; c < (K >> 3); c += 32) {
+    const float4 x0 = *(const float4*)(xf + c * 8), x1 = *(const float4*)(xf + c * 8 + 4);
+    uint4 w[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) w[i] = *(const uint4*)(rp[i] + c * 16);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      a[i] = fmaf(bf_lo(w[i].x), x0.x, a[i]);
+      a[i] = fmaf(bf_hi(w[i].x), x0.y, a[i]);
+      a[i] = fmaf(bf_lo(w[i].y), x0.z, a[i]);
+      a[i] = fmaf(bf_hi(w[i].y), x0.w, a[i]);
+      a[i] = fmaf(bf_lo(w[i].z), x1.x, a[i]);
+      a[i] = fmaf(bf_hi(w[i].z), x1.y, a[i]);
+      a[i] = fmaf(bf_lo(w[i].w), x1.z, a[i]);
+      a[i] = fmaf(bf_hi(w[i].w), x1.w, a[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) out[i] = warp_sum(a[i]);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
 // ---------------------------------------------------------------------------
-// attention: KV head h, split s of ns over the positions; writes the split's
-// partial (o, m, l) per query head to the workspace slot [h][s]
+// attention of one split: online softmax state of a warp over U positions at a time
+// (the arithmetic of attn_split_kernel)
 // ---------------------------------------------------------------------------
-// raw: the flagged q/k/v words of this layer (epoch `ep`); returns false when a wait
-// for them gave up
-template <int GQ>
-__device__ bool attention_split(const Kp& p, const Smem& S, int layer, int h, int s, int ns, int P,
-                                const unsigned long long* raw, uint32_t ep) {
-  const iron_qwen3_model& m = p.m;
-  constexpr int PER = HDIM / 32;
-  constexpr int U = 4;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int L = P + 1;
-  const int chunk = (L + ns - 1) / ns;
-  const int start = min(L, s * chunk), end = min(L, start + chunk);
-  float* qf = S.att;                   // [GQ][HD]
-  float* kt = qf + GQ * HDIM;          // [HD]
-  float* vt = kt + HDIM;               // [HD]
-  float* part = vt + HDIM;             // [NWARP][GQ][HD+2]
-  uint16_t* head = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
-  const uint16_t* ang = m.angles + (size_t)P * HDIM;
-  const bool owner = P >= start && P < end;
-  // the first K/V positions do not depend on q/k: their loads go out before the norms
-  auto load = [&](int j0, uint2 (&kk)[U], uint2 (&vv)[U]) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = min(j0 + u, end - 1);
-      if (j != P) {
-        const uint16_t* kr = head + (size_t)j * 2 * HDIM + lane * PER;
-        kk[u] = ldg_stream8(kr);
-        vv[u] = ldg_stream8(kr + HDIM);
-      }
-    }
-  };
-  uint2 kc[U], vc[U], kn[U], vn[U];
-  int j0 = start + wid * U;
-  if (j0 < end) load(j0, kc, vc);
-  // per-head q/k RMSNorm (golden form) + RoPE and the v copy: qk_norm_rope_kv_kernel's arithmetic
-  int bad = 0;
-  if (threadIdx.x == 0) S.flag[6] = 0;
-  csync();
-  for (int t = wid; t < GQ + 2; t += NWARP) {
-    if (t == GQ + 1) {
-      const unsigned long long* vs = raw + (size_t)(m.Hq + m.Hkv + h) * HDIM + lane * 4;
-      uint32_t b[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) b[e] = ll_get(vs + e, ep, m.sync, bad);
-      const uint2 v = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
-      vt[lane * 4 + 0] = bf_lo(v.x);
-      vt[lane * 4 + 1] = bf_hi(v.x);
-      vt[lane * 4 + 2] = bf_lo(v.y);
-      vt[lane * 4 + 3] = bf_hi(v.y);
-      if (owner) ((uint2*)(head + (size_t)P * 2 * HDIM + HDIM))[lane] = v;
-      continue;
-    }
-    const bool isq = t < GQ;
-    const int hh = isq ? h * GQ + t : m.Hq + h;
-    const unsigned long long* src = raw + (size_t)hh * HDIM;
-    const uint16_t* nw = isq ? S.lay[layer].qn : S.lay[layer].kn;
-    float v[PER], wv[PER], cs[PER], sn[PER];
-#pragma unroll
-    for (int j = 0; j < PER / 2; ++j) {
-      const int i = lane + 32 * j;
-      v[2 * j] = bf2f(ll_get(src + i, ep, m.sync, bad));
-      v[2 * j + 1] = bf2f(ll_get(src + i + HDIM / 2, ep, m.sync, bad));
-      wv[2 * j] = bf2f(__ldg(nw + i));
-      wv[2 * j + 1] = bf2f(__ldg(nw + i + HDIM / 2));
-      cs[j] = bf2f(__ldg(ang + 2 * i));
-      sn[j] = bf2f(__ldg(ang + 2 * i + 1));
-    }
-    double ss = 0.0;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) ss += rms_sq(v[e], 1);
-    ss = warp_sum_d(ss);
-    const RmsCoef rc = rms_coef(ss, HDIM, m.eps, 1);
-    float* dst = isq ? qf + t * HDIM : kt;
-#pragma unroll
-    for (int j = 0; j < PER / 2; ++j) {
-      const int i = lane + 32 * j;
-      const float x1 = rbf(rms_apply(v[2 * j], wv[2 * j], rc));
-      const float x2 = rbf(rms_apply(v[2 * j + 1], wv[2 * j + 1], rc));
-      const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, cs[j]), __fmul_rn(x2, sn[j])));
-      const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, cs[j]), __fmul_rn(x1, sn[j])));
-      dst[i] = bf2f(o1);
-      dst[i + HDIM / 2] = bf2f(o2);
-      if (!isq && owner) {
-        head[(size_t)P * 2 * HDIM + i] = o1;
-        head[(size_t)P * 2 * HDIM + i + HDIM / 2] = o2;
-      }
-    }
-  }
-  if (bad) S.flag[6] = 1;
-  csync();
-  if (S.flag[6]) return false;
-  STEP_MARK(layer, 14);
-  // flash decoding over [start, end): the online softmax of attn_split_kernel, with the
-  // next group of positions loaded while the current one is reduced
-  const float scale = 1.4426950408889634f / sqrtf((float)HDIM);
-  float q[GQ][PER];
-#pragma unroll
-  for (int g = 0; g < GQ; ++g)
-#pragma unroll
-    for (int e = 0; e < PER; ++e) q[g][e] = qf[g * HDIM + lane * PER + e];
-  float mm[GQ], ll[GQ], o[GQ][PER];
+template <int GQ, int U>
+__device__ __forceinline__ void attn_update(const float (&q)[GQ][4], const float (&kf)[U][4], const float (&vf)[U][4],
+                                            int nvalid, float scale, float (&mm)[GQ], float (&ll)[GQ],
+                                            float (&o)[GQ][4]) {
 #pragma unroll
   for (int g = 0; g < GQ; ++g) {
-    mm[g] = -INFINITY;
-    ll[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) o[g][e] = 0.f;
-  }
-  for (; j0 < end; j0 += NWARP * U) {
-    const int jn = j0 + NWARP * U;
-    if (jn < end) load(jn, kn, vn);
-    float kf[U][PER], vf[U][PER];
+    float sv[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = min(j0 + u, end - 1);
-      if (j == P) {
+      float d = 0.f;
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-          kf[u][e] = kt[lane * PER + e];
-          vf[u][e] = vt[lane * PER + e];
-        }
-      } else {
-        kf[u][0] = bf_lo(kc[u].x);
-        kf[u][1] = bf_hi(kc[u].x);
-        kf[u][2] = bf_lo(kc[u].y);
-        kf[u][3] = bf_hi(kc[u].y);
-        vf[u][0] = bf_lo(vc[u].x);
-        vf[u][1] = bf_hi(vc[u].x);
-        vf[u][2] = bf_lo(vc[u].y);
-        vf[u][3] = bf_hi(vc[u].y);
-      }
+      for (int e = 0; e < 4; ++e) d = fmaf(q[g][e], kf[u][e], d);
+      sv[u] = warp_sum(d) * scale;
+      if (u >= nvalid) sv[u] = -INFINITY;
     }
+    float mn = mm[g];
 #pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-      float sv[U];
+    for (int u = 0; u < U; ++u) mn = fmaxf(mn, sv[u]);
+    const float corr = exp2f(mm[g] - mn);
+    float ls = ll[g] * corr;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) d = fmaf(q[g][e], kf[u][e], d);
-        sv[u] = warp_sum(d) * scale;
-        if (j0 + u >= end) sv[u] = -INFINITY;
-      }
-      float mn = mm[g];
-#pragma unroll
-      for (int u = 0; u < U; ++u) mn = fmaxf(mn, sv[u]);
-      const float corr = exp2f(mm[g] - mn);
-      float ls = ll[g] * corr;
-#pragma unroll
-      for (int e = 0; e < PER; ++e) o[g][e] *= corr;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float pu = exp2f(sv[u] - mn);
-        ls += pu;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) o[g][e] = fmaf(pu, vf[u][e], o[g][e]);
-      }
-      ll[g] = ls;
-      mm[g] = mn;
-    }
+    for (int e = 0; e < 4; ++e) o[g][e] *= corr;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      kc[u] = kn[u];
-      vc[u] = vn[u];
-    }
-  }
-  // merge the warps; write this split's partial per head
+      const float pu = exp2f(sv[u] - mn);
+      ls += pu;
 #pragma unroll
-  for (int g = 0; g < GQ; ++g) {
-    float* pw = part + (wid * GQ + g) * (HDIM + 2);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) pw[lane * PER + e] = o[g][e];
-    if (lane == 0) {
-      pw[HDIM] = mm[g];
-      pw[HDIM + 1] = ll[g];
+      for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pu, vf[u][e], o[g][e]);
     }
+    ll[g] = ls;
+    mm[g] = mn;
   }
-  csync();
-  float* ws = m.attn_ws + ((size_t)(h * GMAX + s) * GQ) * (HDIM + 2);
-  for (int t = threadIdx.x; t < GQ * HDIM; t += NT) {
-    const int g = t / HDIM, d = t - g * HDIM;
-    float M = -INFINITY;
-    for (int w = 0; w < NWARP; ++w) M = fmaxf(M, part[(w * GQ + g) * (HDIM + 2) + HDIM]);
-    float oo = 0.f, lsum = 0.f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < NWARP; ++w) {
-        const float* pw = part + (w * GQ + g) * (HDIM + 2);
-        const float f = exp2f(pw[HDIM] - M);
-        oo = fmaf(pw[d], f, oo);
-        lsum = fmaf(pw[HDIM + 1], f, lsum);
-      }
-    }
-    ws[g * (HDIM + 2) + d] = oo;
-    if (d == 0) {
-      ws[g * (HDIM + 2) + HDIM] = M;
-      ws[g * (HDIM + 2) + HDIM + 1] = lsum;
-    }
-  }
-  return true;
-}
-
-// Merge the ns split partials of KV head h (attn_combine_kernel's arithmetic) into
-// bf16 bits in xhi[0, GQ*HD).  The partials are contiguous in the workspace and
-// come in with one bulk copy; `use` counts the calls (mbarrier phase).
-template <int GQ>
-__device__ bool merge_splits(const Kp& p, const Smem& S, int h, int ns, int use) {
-  const int tid = threadIdx.x;
-  if (tid == 0) {
-    const float* base = p.m.attn_ws + (size_t)h * GMAX * GQ * (HDIM + 2);
-    const uint32_t bytes = (uint32_t)ns * GQ * (HDIM + 2) * 4;
-    // the partials were written through the generic proxy by the group's CTAs
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    mbar_expect(&S.mbar[NMB], bytes);
-    bulk_g2s(S.mst, base, bytes, &S.mbar[NMB]);
-    S.flag[3] = wait_slot(&S.mbar[NMB], p.m.sync, (uint32_t)(use & 1)) ? 1 : 0;
-    if (!S.flag[3]) {  // leaving early: let the copy land first (bounded)
-      const unsigned long long t0 = gtimer();
-      while (!mbar_test(&S.mbar[NMB], (uint32_t)(use & 1)) && gtimer() - t0 < 20ull * 1000 * 1000) {
-      }
-    }
-  }
-  csync();
-  if (!S.flag[3]) return false;
-  for (int t = tid; t < GQ * HDIM; t += NT) {
-    const int g = t / HDIM, d = t - g * HDIM;
-    const float* ps = S.mst + g * (HDIM + 2);
-    float M = -INFINITY;
-    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, ps[sp * GQ * (HDIM + 2) + HDIM]);
-    float oo = 0.f, lsum = 0.f;
-    if (M != -INFINITY) {
-      for (int sp = 0; sp < ns; ++sp) {
-        const float* q = ps + sp * GQ * (HDIM + 2);
-        const float f = exp2f(q[HDIM] - M);
-        oo = fmaf(q[d], f, oo);
-        lsum = fmaf(q[HDIM + 1], f, lsum);
-      }
-    }
-    S.xhi[t] = f2bf(lsum > 0.f ? oo / lsum : 0.f);
-  }
-  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -1063,9 +801,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   const iron_qwen3_model& m = p.m;
   const Smem S = carve(smem_raw, p, GQ);
   int32_t* sync = m.sync;
-  const int tid = threadIdx.x;
-  const int N = gridDim.x, D = m.D, NL = m.n_layers;
-  const Plan P = make_plan(p);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int N = gridDim.x, D = m.D, NL = m.n_layers, FF = m.FF;
   const int pos = m.pos[0];
   // a position outside the cache or a token outside the vocabulary: record and leave
   // before touching memory (every CTA takes the same decision)
@@ -1073,24 +810,25 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     if (tid == 0) atomicCAS((int*)&sync[SYNC_ERR], 0, ERR_INPUT);
     return;
   }
-  // projection accumulators: two sets of [NL][O, down][D] float64 that alternate by
-  // token; this token zeroes the other set for the next one
-  const int parity = __ldcg((const int*)&sync[SYNC_PARITY]) & 1;
+  const Plan P = make_plan(p, pos);
   const uint32_t tok_epoch = (uint32_t)__ldcg((const int*)&sync[SYNC_EPOCH]);
-  double* acc_base = (double*)((uint8_t*)m.attn_ws + (size_t)m.Hkv * GMAX * GQ * (HDIM + 2) * 4);
-  const size_t lstride = (size_t)(1 + XREP) * D;  // accumulator doubles per layer
-  double* acc = acc_base + (size_t)parity * NL * lstride;
-  // flagged q/k/v words of the current layer, after the accumulators
-  unsigned long long* raw_ll = (unsigned long long*)(acc_base + (size_t)2 * NL * lstride);
+  // hand-off words (zeroed by iron_qwen3_sync_reset)
+  constexpr int RAWW = (GQ + 2) * HDIM / 2;  // q/k/v words of one KV-head group
+  constexpr int ATTW = GQ * (HDIM + 2);      // words of one attention split
+  unsigned long long* xw = (unsigned long long*)m.attn_ws;          // [D / 2] x between layers
+  unsigned long long* raww = xw + D / 2;                            // [Hkv][RAWW]
+  unsigned long long* attw = raww + (size_t)m.Hkv * RAWW;           // [Hkv][GMAX][ATTW]
+  unsigned long long* ow = attw + (size_t)m.Hkv * GMAX * ATTW;      // [Hkv][D] O partial sums
+  unsigned long long* hw = ow + (size_t)m.Hkv * D;                  // [FF / 2] SwiGLU outputs
   if (tid < NT) {
-    double* other = acc_base + (size_t)(parity ^ 1) * NL * lstride;
-    for (size_t i = (size_t)blockIdx.x * NT + tid; i < NL * lstride; i += (size_t)N * NT) other[i] = 0.0;
-    // the layer pointer table, read once
+    // the layer pointer table, read once; the unused second batch row of the B
+    // fragments stays zero
     const int nw = NL * (int)(sizeof(iron_qwen3_layer) / 8);
     for (int i = tid; i < nw; i += NT) ((unsigned long long*)S.lay)[i] = __ldg(((const unsigned long long*)m.layers) + i);
+    for (int i = tid; i < (p.kmax / 32) * XBS / 16; i += NT) ((uint4*)S.xb)[i] = make_uint4(0u, 0u, 0u, 0u);
   }
   if (tid == 0) {
-    for (int i = 0; i <= NMB; ++i) mbar_init(&S.mbar[i]);
+    for (int i = 0; i < NMB; ++i) mbar_init(&S.mbar[i]);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     S.rs->tail = 0;
     S.rs->issued = S.rs->consumed = S.rs->abort = 0;
@@ -1102,21 +840,22 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   }
   // layer-0 input: the token's embedding row, or the hidden state given in x
   load_ro(S.sx, p.embed_input ? m.embed + (size_t)m.tok[0] * D : m.x, D);
-  load_ro(S.xlo, S.lay[0].norm1, D);
-  csync();  // the prologue reads these rows across threads
 
   bool ok = true;
-  // consume chunk i: fn(buffer) once its copy landed, then release its space
   volatile RingState& vrs = *S.rs;
-  auto consume = [&](int i, auto&& fn) -> bool {
+  int ci = 0;  // next chunk
+  // consume the next chunk: fn(buffer) once its copy landed, then release its space
+  // (mark: the profiling stamp taken when the copy has landed, in row mrow)
+  auto consume = [&](int mrow, int mark, auto&& fn) -> bool {
+    const int i = ci++;
     const int sl = i % NMB;
     if (tid == 0) S.flag[2] = wait_slot(&S.mbar[sl], sync, (uint32_t)((i / NMB) & 1)) ? 1 : 0;
     csync();
     if (!S.flag[2]) return false;
-    if ((i >> 2) < NL) STEP_MARK(i >> 2, 16 + (i & 3));
+    if (mark >= 0) STEP_MARK(mrow, mark);
+    (void)mrow;
     fn(S.ring + vrs.slot[sl]);
     csync();
-    if ((i >> 2) < NL) STEP_MARK(i >> 2, 20 + (i & 3));
     if (tid == 0) {
       fence_proxy_async();
       vrs.tail = vrs.end[sl];
@@ -1124,180 +863,359 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     }
     return true;
   };
-  auto arrive = [&](int word) {
-    csync();
-    if (tid == 0) {
-      __threadfence();
-      atomicAdd((unsigned*)&sync[word], 1u);
-    }
-  };
-  auto wait = [&](int word, unsigned target) -> bool {
-    if (tid == 0) S.flag[0] = wait_count(sync, word, target) ? 1 : 0;
-    csync();
-    return S.flag[0] != 0;
-  };
+  // a bounded poll by every compute thread, then a CTA-wide verdict
+  auto all_ok = [&](bool mine) -> bool { return !cvote_any(!mine); };
 
-  const int h = P.h, gsz = P.gsz;
-  const int k0 = 4 * P.u0, w = 4 * (P.u1 - P.u0);
+  const int h = P.h;
+  const float scale = 1.4426950408889634f / sqrtf((float)HDIM);
   for (int layer = 0; layer < NL && ok; ++layer) {
     const iron_qwen3_layer& Lw = S.lay[layer];
-    double* oacc = acc + (size_t)layer * lstride;
-    double* xacc = oacc + (size_t)D * (1 + h % XREP);  // this KV-head group's replica
-    const int c0 = 4 * layer;
     const uint32_t ep = tok_epoch * (uint32_t)NL + (uint32_t)layer + 1u;  // this layer's flag value
+    const uint32_t tg = tag16_of(ep);
     STEP_MARK(layer, 0);
-    STEP_CLK(layer, 28);
-    // ---- QKV: x = bf16(x1 + bf16(down)), hn = RMSNorm_golden(x, norm1), raw = bf16(Wqkv @ hn) ----
-    if (layer > 0) {
-      if (!(ok = wait(SYNC_B1, (unsigned)layer * N))) break;
-      STEP_MARK(layer, 1);
+    // ---- x: the previous layer's output rows ----
+    load_ro(S.nw, Lw.norm1, D);
+    if (layer > 0) {  // written by the previous layer's down projection, with its epoch
+      ok = all_ok(poll<2>(xw, D / 2, ep - 1u, 32, sync, [&](int i, unsigned long long w) {
+        ((uint32_t*)S.sx)[i] = (uint32_t)w;
+      }));
+      if (!ok) break;
+    } else {
+      csync();  // the embedding row (or x) in sx, written across threads
     }
-    prologue<G, XREP>(S, S.sx, S.sx1, layer > 0 ? acc + (size_t)(layer - 1) * lstride + D : nullptr, D, m.eps, 1,
-                      nullptr, (m.trace && blockIdx.x == 0) ? m.trace + (size_t)layer * D : nullptr);
-    STEP_MARK(layer, 24);
-    STEP_MARK(layer, 25);
+    if (m.trace && blockIdx.x == 0)
+      for (int i = tid; i < D; i += NT) m.trace[(size_t)layer * D + i] = S.sx[i];
+    STEP_MARK(layer, 1);
+    // ---- QKV rows of group h: raw = bf16(Wqkv @ RMSNorm_golden(x, norm1)) ----
+    norm_stage<G>(S, S.sx, D, m.eps, 1, nullptr);
     STEP_MARK(layer, 2);
-    ok = consume(c0 + CK_QKV, [&](const uint8_t* wb) {
-      chunk_gemv<G, 32, 4, false>(wb, P.q1 - P.q0, rowb(D, G), D, S, [&](int r, double a, double) {
-        ll_put(raw_ll + qkv_src_row(P.q0 + r, h, GQ, m.Hq, m.Hkv), f2bf((float)a), ep);
+    ok = consume(layer, 3, [&](const uint8_t* wb) {
+      gemv_tiles<G, false>(wb, P.qnt, D, S, [&](int t, int r, double a, double) {
+        S.outb[t * TR + r] = f2bf((float)a);
       });
     });
     if (!ok) break;
-    STEP_MARK(layer, 3);
-    if (tid == 0) {  // this CTA's KV range of this layer, ahead of the attention
-      const int L = pos + 1, chunk = (L + gsz - 1) / gsz;
-      const int st = min(L, P.gi * chunk), en = min(min(L, st + chunk), pos);
-      if (en > st) {
-        const uint16_t* hb = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
-        prefetch_l2(hb + (size_t)st * 2 * HDIM, (uint32_t)(en - st) * 4 * HDIM);
-      }
-    }
+    for (int i = tid; i < P.qnt * TR / 2; i += NT)
+      ll_put(raww + (size_t)h * RAWW + P.qt0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
     STEP_MARK(layer, 4);
-    // ---- attention: KV head h, split gi of gsz (its q/k/v rows arrive as flagged words) ----
-    if (!(ok = attention_split<GQ>(p, S, layer, h, P.gi, gsz, pos, raw_ll, ep))) break;
+    // ---- attention: KV head h, one split of the positions ----
+    ok = all_ok(poll<2>(raww + (size_t)h * RAWW, RAWW, ep, 32, sync, [&](int i, unsigned long long w) {
+      ((uint32_t*)S.hb)[i] = (uint32_t)w;
+    }));
+    if (!ok) break;
     STEP_MARK(layer, 5);
-    arrive(SYNC_G1 + m.Hkv + h);
-    if (!(ok = wait(SYNC_G1 + m.Hkv + h, (unsigned)(layer + 1) * gsz))) break;
-    STEP_MARK(layer, 6);
-    // ---- O (head h's column block): oacc += Wo[:, head h] @ attn[head h] ----
-    if (!(ok = merge_splits<GQ>(p, S, h, gsz, layer))) break;
-    csync();
-    STEP_MARK(layer, 15);
-    bfp_stage(S, GQ * HDIM, G);
-    csync();
-    STEP_MARK(layer, 7);
-    ok = consume(c0 + CK_O, [&](const uint8_t* wb) {
-      chunk_gemv<G, GQ * HDIM / 16 < 32 ? GQ * HDIM / 16 : 32, 4, false>(wb, P.o1 - P.o0, rowb_heads(GQ, G), GQ * HDIM, S,
-                               [&](int r, double a, double) { red_add(oacc + P.o0 + r, a); });
-    });
-    if (!ok) break;
-    STEP_MARK(layer, 8);
-    load_ro(S.xlo, Lw.norm2, D);
-    arrive(SYNC_B2);
-    if (!(ok = wait(SYNC_B2, (unsigned)(layer + 1) * N))) break;
-    STEP_MARK(layer, 9);
-    // ---- gate/up: x1 = bf16(x + bf16(O)), hf = RMSNorm_kernel(x1, norm2),
-    //      gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for this CTA's slice ----
-    prologue<G, 1>(S, S.sx1, S.sx, oacc, D, m.eps, 0, nullptr, nullptr);
-    STEP_MARK(layer, 26);
-    STEP_MARK(layer, 10);
-    ok = consume(c0 + CK_GU, [&](const uint8_t* wb) {
-      chunk_gemv<G, 32, 3, true>(wb, w, rowb(D, G), D, S, [&](int r, double g, double u) {
-        S.ghv[r] = rbf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
-      });
-    });
-    if (!ok) break;
-    STEP_MARK(layer, 11);
-    // the slice as one exact int16 block (hi + lo words)
-    if (tid < 32) {
-      float mx = 0.f;
-      for (int j = tid; j < w; j += 32) mx = fmaxf(mx, fabsf(S.ghv[j]));
-      mx = warp_max(mx);
-      float sc, inv;
-      bfp_scale(mx, sc, inv);
-      for (int j = tid; j < w; j += 32) {
-        const float t = S.ghv[j] * sc;
-        const int hi = __float2int_rn(t);
-        S.dh[j] = (uint16_t)(int16_t)hi;
-        S.dl[j] = (uint16_t)(int16_t)__float2int_rn((t - (float)hi) * 32768.0f);
-      }
-      if (tid == 0) S.flag[4] = __float_as_int(inv);
-    }
-    csync();
-    STEP_MARK(layer, 12);
-    // ---- down (this CTA's K slice): xacc += Wd[:, k0:k0+w] @ gh[k0:k0+w] ----
-    ok = consume(c0 + CK_D, [&](const uint8_t* wb) {
-      const uint32_t* wq = (const uint32_t*)wb;
-      const uint16_t* wsc = (const uint16_t*)(wb + (size_t)w * D);
-      const uint32_t* xh = (const uint32_t*)S.dh;
-      const uint32_t* xl = (const uint32_t*)S.dl;
-      const float inv = __int_as_float(S.flag[4]);
-      // words j < jb1 belong to the slice's first scale group, j < jb2 to its second,
-      // the rest to its third (a 32-column slice touches at most two groups of 32)
-      const int nw4 = w >> 2;
-      const int jb1 = (min(w, (P.ga + 1) * G - k0)) >> 2, jb2 = (min(w, (P.ga + 2) * G - k0)) >> 2;
-      constexpr int RPT = 4;  // rows per thread and pass, their loads overlapped
-      for (int r0 = tid; r0 < D; r0 += NT * RPT) {
-        int ah[RPT][3], al[RPT][3];
+    float* qf = S.att;           // [GQ][HD]
+    float* kt = qf + GQ * HDIM;  // [HD]
+    float* vt = kt + HDIM;       // [HD]
+    float* wpart = vt + HDIM;    // [NWARP][GQ][HD + 2]
+    uint16_t* head = m.kv + ((size_t)layer * m.Hkv + h) * 2 * (size_t)m.max_seq * HDIM;
+    {
+      // per-head q/k RMSNorm (golden form) + RoPE and the v copy: the arithmetic of
+      // qk_norm_rope_kv_kernel; the split that holds pos writes K_t, V_t
+      const uint16_t* ang = m.angles + (size_t)pos * HDIM;
+      for (int t = wid; t < GQ + 2; t += NWARP) {
+        const uint16_t* src = S.hb + t * HDIM;
+        if (t == GQ + 1) {
+          for (int i = lane; i < HDIM; i += 32) {
+            vt[i] = bf2f(src[i]);
+            if (P.own) head[(size_t)pos * 2 * HDIM + HDIM + i] = src[i];
+          }
+          continue;
+        }
+        const bool isq = t < GQ;
+        const uint16_t* nwt = isq ? Lw.qn : Lw.kn;
+        constexpr int PER = HDIM / 32;
+        float v[PER], wv[PER], cs[PER / 2], sn[PER / 2];
 #pragma unroll
-        for (int q = 0; q < RPT; ++q)
+        for (int j = 0; j < PER / 2; ++j) {
+          const int i = lane + 32 * j;
+          v[2 * j] = bf2f(src[i]);
+          v[2 * j + 1] = bf2f(src[i + HDIM / 2]);
+          wv[2 * j] = bf2f(__ldg(nwt + i));
+          wv[2 * j + 1] = bf2f(__ldg(nwt + i + HDIM / 2));
+          cs[j] = bf2f(__ldg(ang + 2 * i));
+          sn[j] = bf2f(__ldg(ang + 2 * i + 1));
+        }
+        double ss = 0.0;
 #pragma unroll
-          for (int e = 0; e < 3; ++e) ah[q][e] = al[q][e] = 0;
+        for (int e = 0; e < PER; ++e) ss += rms_sq(v[e], 1);
+        ss = warp_sum_d(ss);
+        const RmsCoef rc = rms_coef(ss, HDIM, m.eps, 1);
+        float* dst = isq ? qf + t * HDIM : kt;
 #pragma unroll
-        for (int j = 0; j < SLICE_MAX / 4; ++j) {
-          if (j < nw4) {
-            const int h0 = (int)xh[2 * j], h1 = (int)xh[2 * j + 1], l0 = (int)xl[2 * j], l1 = (int)xl[2 * j + 1];
-            const int e = j < jb1 ? 0 : (j < jb2 ? 1 : 2);
-#pragma unroll
-            for (int q = 0; q < RPT; ++q) {
-              const int r = r0 + q * NT;
-              const int wv = r < D ? (int)wq[(size_t)j * D + r] : 0;
-              const int dh = __dp2a_hi(h1, wv, __dp2a_lo(h0, wv, 0));
-              const int dl = __dp2a_hi(l1, wv, __dp2a_lo(l0, wv, 0));
-              ah[q][0] += e == 0 ? dh : 0;
-              ah[q][1] += e == 1 ? dh : 0;
-              ah[q][2] += e == 2 ? dh : 0;
-              al[q][0] += e == 0 ? dl : 0;
-              al[q][1] += e == 1 ? dl : 0;
-              al[q][2] += e == 2 ? dl : 0;
-            }
+        for (int j = 0; j < PER / 2; ++j) {
+          const int i = lane + 32 * j;
+          const float x1 = rbf(rms_apply(v[2 * j], wv[2 * j], rc));
+          const float x2 = rbf(rms_apply(v[2 * j + 1], wv[2 * j + 1], rc));
+          const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, cs[j]), __fmul_rn(x2, sn[j])));
+          const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, cs[j]), __fmul_rn(x1, sn[j])));
+          dst[i] = bf2f(o1);
+          dst[i + HDIM / 2] = bf2f(o2);
+          if (!isq && P.own) {
+            head[(size_t)pos * 2 * HDIM + i] = o1;
+            head[(size_t)pos * 2 * HDIM + i + HDIM / 2] = o2;
           }
         }
+      }
+    }
+    csync();
+    STEP_MARK(layer, 6);
+    // flash decoding over the cached positions (K/V chunks in the ring) and, in the
+    // split that holds it, the current position (K/V from the registers above)
+    float q[GQ][4], mm[GQ], ll[GQ], o[GQ][4];
 #pragma unroll
-        for (int q = 0; q < RPT; ++q) {
-          const int r = r0 + q * NT;
-          if (r >= D) continue;
-          double a = 0.0;
+    for (int g = 0; g < GQ; ++g) {
+      mm[g] = -INFINITY;
+      ll[g] = 0.f;
 #pragma unroll
-          for (int e = 0; e < 3; ++e)
-            if (e < P.nsg) {
-              const long long t = (long long)ah[q][e] * 32768 + al[q][e];
-              a = fma((double)t, (double)(bf2f(wsc[(size_t)e * D + r]) * inv) * (1.0 / 32768.0), a);
-            }
-          red_add(xacc + r, a);
+      for (int e = 0; e < 4; ++e) {
+        q[g][e] = qf[g * HDIM + lane * 4 + e];
+        o[g][e] = 0.f;
+      }
+    }
+    constexpr int U = 4;
+    for (int j = 0; j < P.nkv && ok; ++j) {
+      const int n = min(KVP, P.ken - (P.kst + j * KVP));
+      ok = consume(layer, -1, [&](const uint8_t* kvb) {
+        for (int j0 = wid * U; j0 < n; j0 += NWARP * U) {
+          float kf[U][4], vf[U][4];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int jj = min(j0 + u, n - 1);
+            const uint2 kk = *(const uint2*)(kvb + (size_t)jj * 4 * HDIM + lane * 8);
+            const uint2 vv = *(const uint2*)(kvb + (size_t)jj * 4 * HDIM + 2 * HDIM + lane * 8);
+            kf[u][0] = bf_lo(kk.x);
+            kf[u][1] = bf_hi(kk.x);
+            kf[u][2] = bf_lo(kk.y);
+            kf[u][3] = bf_hi(kk.y);
+            vf[u][0] = bf_lo(vv.x);
+            vf[u][1] = bf_hi(vv.x);
+            vf[u][2] = bf_lo(vv.y);
+            vf[u][3] = bf_hi(vv.y);
+          }
+          attn_update<GQ, U>(q, kf, vf, n - j0, scale, mm, ll, o);
+        }
+      });
+    }
+    if (!ok) break;
+    if (P.own && wid == NWARP - 1) {
+      float kf[1][4], vf[1][4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        kf[0][e] = kt[lane * 4 + e];
+        vf[0][e] = vt[lane * 4 + e];
+      }
+      attn_update<GQ, 1>(q, kf, vf, 1, scale, mm, ll, o);
+    }
+    STEP_MARK(layer, 7);
+    // merge the warps; publish this split's partial (o, m, l) per head
+#pragma unroll
+    for (int g = 0; g < GQ; ++g) {
+      float* pw = wpart + (wid * GQ + g) * (HDIM + 2);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pw[lane * 4 + e] = o[g][e];
+      if (lane == 0) {
+        pw[HDIM] = mm[g];
+        pw[HDIM + 1] = ll[g];
+      }
+    }
+    csync();
+    {
+      unsigned long long* ws = attw + ((size_t)h * GMAX + P.gi) * ATTW;
+      for (int t = tid; t < GQ * HDIM; t += NT) {
+        const int g = t / HDIM, d = t - g * HDIM;
+        float M = -INFINITY;
+        for (int w = 0; w < NWARP; ++w) M = fmaxf(M, wpart[(w * GQ + g) * (HDIM + 2) + HDIM]);
+        float oo = 0.f, lsum = 0.f;
+        if (M != -INFINITY) {
+          for (int w = 0; w < NWARP; ++w) {
+            const float* pw = wpart + (w * GQ + g) * (HDIM + 2);
+            const float f = exp2f(pw[HDIM] - M);
+            oo = fmaf(pw[d], f, oo);
+            lsum = fmaf(pw[HDIM + 1], f, lsum);
+          }
+        }
+        ll_put(ws + g * (HDIM + 2) + d, __float_as_uint(oo), ep);
+        if (d == 0) {
+          ll_put(ws + g * (HDIM + 2) + HDIM, __float_as_uint(M), ep);
+          ll_put(ws + g * (HDIM + 2) + HDIM + 1, __float_as_uint(lsum), ep);
         }
       }
+    }
+    STEP_MARK(layer, 8);
+    // ---- merge the group's splits (attn_combine_kernel's arithmetic) -> bf16 heads ----
+    {
+      const unsigned long long* gws = attw + (size_t)h * GMAX * ATTW;
+      bool mine = true;
+      // (m, l) of every split and head into shared memory
+      {
+        const int nml = P.gsz * GQ * 2;
+        unsigned long long v[2];
+        uint32_t want = 0;
+        auto ml_addr = [&](int u) {
+          const int t = tid + u * NT, s = t / (2 * GQ), r = t - s * 2 * GQ;
+          return gws + (size_t)s * ATTW + (r >> 1) * (HDIM + 2) + HDIM + (r & 1);
+        };
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          v[u] = 0ull;
+          if (tid + u * NT < nml) {
+            v[u] = ll_ld(ml_addr(u));
+            want |= 1u << u;
+          }
+        }
+        mine = poll_rounds<2>(ml_addr, v, want, ep, 32, sync);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if ((want >> u) & 1u) S.ml[tid + u * NT] = __uint_as_float((uint32_t)v[u]);
+      }
+      for (int t0 = 0; t0 < GQ * HDIM; t0 += NT) {
+        const int t = t0 + tid;
+        const int g = t / HDIM, d = t - g * HDIM;
+        // the split outputs o[s][g][d]: loaded and reloaded together
+        float ov[GMAX];
+        unsigned long long v[GMAX];
+        uint32_t want = 0;
+        const unsigned long long* ob = gws + g * (HDIM + 2) + d;
+#pragma unroll
+        for (int s = 0; s < GMAX; ++s) {
+          v[s] = 0ull;
+          if (s < P.gsz && t < GQ * HDIM) {
+            v[s] = ll_ld(ob + (size_t)s * ATTW);
+            want |= 1u << s;
+          }
+        }
+        mine = mine && poll_rounds<GMAX>([&](int s) { return ob + (size_t)s * ATTW; }, v, want, ep, 32, sync);
+#pragma unroll
+        for (int s = 0; s < GMAX; ++s) ov[s] = __uint_as_float((uint32_t)v[s]);
+        if (!all_ok(mine)) {  // also publishes ml
+          ok = false;
+          break;
+        }
+        if (t < GQ * HDIM) {
+          const float* mlg = S.ml + g * 2;
+          float M = -INFINITY;
+          for (int s = 0; s < P.gsz; ++s) M = fmaxf(M, mlg[s * 2 * GQ]);
+          float oo = 0.f, lsum = 0.f;
+          if (M != -INFINITY) {
+#pragma unroll
+            for (int s = 0; s < GMAX; ++s) {
+              if (s >= P.gsz) continue;
+              const float f = exp2f(mlg[s * 2 * GQ] - M);
+              oo = fmaf(ov[s], f, oo);
+              lsum = fmaf(mlg[s * 2 * GQ + 1], f, lsum);
+            }
+          }
+          S.hb[t] = f2bf(lsum > 0.f ? oo / lsum : 0.f);
+        }
+      }
+      if (!ok) break;
+    }
+    csync();  // the merged heads in hb, one value per thread, are staged eight per thread
+    STEP_MARK(layer, 9);
+    plain_stage<G>(S, S.hb, GQ * HDIM);
+    STEP_MARK(layer, 10);
+    // ---- O (head h's column block): partial[h][row] = Wo[row, head h] @ attn[head h] ----
+    ok = consume(layer, 11, [&](const uint8_t* wb) {
+      gemv_tiles<G, false>(wb, P.ont, GQ * HDIM, S, [&](int t, int r, double a, double) {
+        ll_put_d(ow + (size_t)h * D + (P.ot0 + t) * TR + r, a, tg);
+      });
     });
     if (!ok) break;
+    STEP_MARK(layer, 12);
+    // ---- x1 = bf16(x + bf16(sum over the KV-head groups, in order)); MLP RMSNorm ----
+    load_ro(S.nw, Lw.norm2, D);
+    {
+      // thread tid sums rows tid + k * NT (k < 4: D <= 4 * NT) over the KV-head groups in
+      // order; all 4 * Hkv words are loaded and reloaded together
+      constexpr int RPT = 4, NU = RPT * HKVMAX;
+      unsigned long long v[NU];
+      uint32_t want = 0;
+      auto o_addr = [&](int u) { return ow + (size_t)(u % HKVMAX) * D + (u / HKVMAX) * NT + tid; };
+#pragma unroll
+      for (int u = 0; u < NU; ++u) {
+        v[u] = 0ull;
+        if ((u / HKVMAX) * NT + tid < D && (u % HKVMAX) < m.Hkv) {
+          v[u] = ll_ld(o_addr(u));
+          want |= 1u << u;
+        }
+      }
+      const bool mine = poll_rounds<NU>(o_addr, v, want, tg, 48, sync);
+      if (!(ok = all_ok(mine))) break;
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) {
+        const int r = k * NT + tid;
+        if (r >= D) continue;
+        double acc = 0.0;
+#pragma unroll
+        for (int hh = 0; hh < HKVMAX; ++hh)
+          if (hh < m.Hkv) acc += ll_val_d(v[k * HKVMAX + hh]);
+        S.sx1[r] = f2bf(bf2f(S.sx[r]) + rbf_d(acc));
+      }
+    }
     STEP_MARK(layer, 13);
-    load_ro(S.xlo, layer + 1 < NL ? S.lay[layer + 1].norm1 : m.final_norm, D);
-    arrive(SYNC_B1);
+    norm_stage<G>(S, S.sx1, D, m.eps, 0, nullptr);
+    STEP_MARK(layer, 14);
+    // ---- gate/up: gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for the CTA's tiles ----
+    ok = consume(layer, 15, [&](const uint8_t* wb) {
+      gemv_tiles<G, true>(wb, P.gnt, D, S, [&](int t, int r, double g, double u) {
+        S.outb[t * TR + r] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
+      });
+    });
+    if (!ok) break;
+    for (int i = tid; i < P.gnt * TR / 2; i += NT) ll_put(hw + P.gt0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
+    STEP_MARK(layer, 16);
+    // ---- down: x_next = bf16(x1 + bf16(Wd @ gh)) for the CTA's row tiles ----
+    if (P.dnt > 0) {
+      ok = all_ok(poll<6>(hw, FF / 2, ep, 32, sync, [&](int i, unsigned long long w) {
+        ((uint32_t*)S.hb)[i] = (uint32_t)w;
+      }));
+      if (!ok) break;
+      STEP_MARK(layer, 17);
+      plain_stage<G>(S, S.hb, FF);
+      STEP_MARK(layer, 18);
+    }
+    ok = consume(layer, 19, [&](const uint8_t* wb) {
+      gemv_tiles<G, false>(wb, P.dnt, FF, S, [&](int t, int r, double a, double) {
+        const int row = (P.dt0 + t) * TR + r;
+        S.outb[t * TR + r] = f2bf(bf2f(S.sx1[row]) + rbf_d(a));
+      });
+    });
+    if (!ok) break;
+    for (int i = tid; i < P.dnt * TR / 2; i += NT) ll_put(xw + P.dt0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
+    STEP_MARK(layer, 20);
   }
 
   STEP_MARK(NL, 0);
-  if (ok) ok = wait(SYNC_B1, (unsigned)NL * N);
-  STEP_MARK(NL, 1);
-  STEP_CLK(NL, 29);
   if (ok) {
-    // ---- final: x = bf16(x1 + bf16(down)), RMSNorm (golden) + lm_head + greedy argmax ----
-    prologue<G, XREP>(S, S.sx, S.sx1, acc + (size_t)(NL - 1) * lstride + D, D, m.eps, 1, S.xf,
-                      blockIdx.x == 0 ? m.x : nullptr);
-    if (m.trace && blockIdx.x == 0)
-      for (int i = tid; i < D; i += NT) m.trace[(size_t)NL * D + i] = S.sx[i];
-    const int lane = tid & 31, wid = tid >> 5;
+    // ---- final: x = the last layer's output, RMSNorm (golden) + lm_head + greedy argmax ----
+    const uint32_t ep = tok_epoch * (uint32_t)NL + (uint32_t)NL;
+    load_ro(S.nw, m.final_norm, D);
+    ok = all_ok(poll<2>(xw, D / 2, ep, 32, sync, [&](int i, unsigned long long w) {
+      ((uint32_t*)S.sx)[i] = (uint32_t)w;
+    }));
+  }
+  if (ok) {
+    if (blockIdx.x == 0) {
+      for (int i = tid; i < D; i += NT) {
+        m.x[i] = S.sx[i];
+        if (m.trace) m.trace[(size_t)NL * D + i] = S.sx[i];
+      }
+    }
+    if (m.lm_w8) {
+      norm_stage<G>(S, S.sx, D, m.eps, 1, S.xf);
+    } else {
+      // golden RMSNorm -> float activations (no staging)
+      double ss = 0.0;
+      for (int i = tid; i < D; i += NT) ss += rms_sq(bf2f(S.sx[i]), 1);
+      ss = csum_d(ss, S.red);
+      const RmsCoef rc = rms_coef(ss, D, m.eps, 1);
+      for (int i = tid; i < D; i += NT) S.xf[i] = rbf(rms_apply(bf2f(S.sx[i]), bf2f(S.nw[i]), rc));
+      csync();
+    }
+    STEP_MARK(NL, 1);
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    const int rbh = m.lm_w8 ? rowb(D, G) : D * 2;
     auto track = [&](int idx, uint16_t o) {
       if (m.logits) m.logits[idx] = o;
       if (better(bf2f(o), idx, bv, bi)) {
@@ -1306,23 +1224,29 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
       }
     };
     float xr[4][8];  // this lane's activations for the D == 1024 bf16 rows
-    if (D == 1024) {
+    if (D == 1024 && !m.lm_w8) {
 #pragma unroll
       for (int k = 0; k < 4; ++k)
 #pragma unroll
         for (int e = 0; e < 8; ++e) xr[k][e] = S.xf[(lane + 32 * k) * 8 + e];
     }
     for (int j = 0; j < P.hnch && ok; ++j) {
-      const int r0 = P.hlo + j * p.lm_rows, n = min(P.hhi, r0 + p.lm_rows) - r0;
-      ok = consume(4 * NL + j, [&](const uint8_t* wb) {
-        if (m.lm_w8) {
-          chunk_gemv<G, 32, 4, false>(wb, n, rbh, D, S, [&](int r, double a, double) { track(r0 + r, f2bf((float)a)); });
-        } else {
+      if (m.lm_w8) {
+        const int t0 = P.hlo + j * LMT, nt = min(P.hhi, t0 + LMT) - t0;
+        ok = consume(NL, -1, [&](const uint8_t* wb) {
+          gemv_tiles<G, false>(wb, nt, D, S, [&](int t, int r, double a, double) {
+            const int row = (t0 + t) * TR + r;
+            if (row < m.V) track(row, f2bf((float)a));
+          });
+        });
+      } else {
+        const int r0 = P.hlo + j * p.lm_rows, n = min(P.hhi, r0 + p.lm_rows) - r0;
+        ok = consume(NL, -1, [&](const uint8_t* wb) {
           constexpr int R = 4;
           for (int rr = wid * R; rr < n; rr += NWARP * R) {
             const uint8_t* rp[R];
 #pragma unroll
-            for (int i = 0; i < R; ++i) rp[i] = wb + (size_t)min(rr + i, n - 1) * rbh;
+            for (int i = 0; i < R; ++i) rp[i] = wb + (size_t)min(rr + i, n - 1) * D * 2;
             float out[R];
             if (D == 1024)
               rows_dot_bf16_reg<R, 4>(rp, xr, out);
@@ -1334,8 +1258,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
                 if (rr + i < n) track(r0 + rr + i, f2bf(out[i]));
             }
           }
-        }
-      });
+        });
+      }
     }
     STEP_MARK(NL, 2);
     if (ok) {
@@ -1378,13 +1302,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
             m.seq_len[0] = np + 1;
             m.kv_off[0] = np * 2 * HDIM;
           }
-          // every CTA has passed every wait of this token: reset the counters and
-          // hand the other accumulator set to the next token
-          sync[SYNC_B1] = 0;
-          sync[SYNC_B2] = 0;
-          for (int k = 0; k < 2 * m.Hkv; ++k) sync[SYNC_G1 + k] = 0;
+          // every CTA has read every word of this token: the next token's epoch
           sync[SYNC_ARGMAX] = 0;
-          sync[SYNC_PARITY] = parity ^ 1;
           sync[SYNC_EPOCH] = (int)(tok_epoch + 1u);
           __threadfence();
         }
@@ -1399,43 +1318,38 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------------------
-// weight packing for the step kernel
+// weight packing for the step kernel: 16-row tiles in mma.sync A-fragment order
 // ---------------------------------------------------------------------------
-// wo_heads[h][r] = [wo[r, h*GQ*HD : (h+1)*GQ*HD] int8 | its GQ*HD/G bf16 scales | 0 pad]
-__global__ void pack_wo_heads_kernel(const uint8_t* wire, int D, int QD, int Hkv, int G, uint8_t* out) {
-  const int GQH = QD / Hkv, rb_in = rowb(QD, G), rb_out = rowb_heads(GQH / HDIM, G);
-  const long long total = (long long)Hkv * D * rb_out;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+// Rows [0, M) of a plain wire (row stride `stride` bytes: K_full int8, then K_full/G
+// bf16 scales), columns [col0, col0 + K) -> tiles: per 32-column block kb, 32 lanes x
+// 16 bytes {row g, cols 4t..4t+3 | row g+8, same | row g, cols 16+4t.. | row g+8, same}
+// (g = lane / 4, t = lane % 4); then per group 8 x {scale row g, scale row g + 8}.
+// Rows past M are zero.
+__global__ void pack_tiles_kernel(const uint8_t* wire, long long stride, int M, int K_full, int col0, int K, int G,
+                                  uint8_t* out) {
+  const int KB = K / 32, KG = K / G;
+  const int ntile = (M + TR - 1) / TR;
+  const int tw = KB * 32 * 4 + KG * 8;  // 4-byte words per tile
+  const long long words = (long long)ntile * tw;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
        i += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(i % rb_out);
-    const long long hr = i / rb_out;
-    const int r = (int)(hr % D), h = (int)(hr / D);
-    const uint8_t* row = wire + (size_t)r * rb_in;
-    uint8_t v = 0;
-    if (b < GQH)
-      v = row[h * GQH + b];
-    else if (b < GQH + 2 * (GQH / G))
-      v = row[QD + 2 * (h * (GQH / G)) + (b - GQH)];
-    out[i] = v;
-  }
-}
-
-// wd_cols[k/4][r][k%4] = wd[r, k]; wd_col_scales[g][r] = the scale of wd row r, group g
-__global__ void pack_wd_cols_kernel(const uint8_t* wire, int D, int FF, int G, uint8_t* q, uint16_t* s) {
-  const int rb = rowb(FF, G);
-  const long long nq = (long long)FF * D, ns = (long long)(FF / G) * D;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nq + ns;
-       i += (long long)gridDim.x * blockDim.x) {
-    if (i < nq) {
-      const int e = (int)(i & 3);
-      const long long jr = i >> 2;
-      const int r = (int)(jr % D), j = (int)(jr / D);
-      q[i] = wire[(size_t)r * rb + 4 * j + e];
+    const int t = (int)(i / tw);
+    const int w = (int)(i - (long long)t * tw);
+    uint32_t v = 0;
+    if (w < KB * 128) {
+      const int kb = w / 128, r4 = w - kb * 128, lane = r4 >> 2, reg = r4 & 3;
+      const int row = t * TR + (lane >> 2) + ((reg & 1) ? 8 : 0);
+      const int col = col0 + kb * 32 + (lane & 3) * 4 + ((reg & 2) ? 16 : 0);
+      if (row < M) v = *(const uint32_t*)(wire + (size_t)row * stride + col);
     } else {
-      const long long k = i - nq;
-      const int r = (int)(k % D), g = (int)(k / D);
-      s[k] = ((const uint16_t*)(wire + (size_t)r * rb + FF))[g];
+      const int s = w - KB * 128, gl = s / 8, g = s - gl * 8;
+      const size_t soff = (size_t)K_full + 2 * (size_t)(col0 / G + gl);
+      const int r0 = t * TR + g, r1 = r0 + 8;
+      const uint32_t lo = r0 < M ? *(const uint16_t*)(wire + (size_t)r0 * stride + soff) : 0u;
+      const uint32_t hi = r1 < M ? *(const uint16_t*)(wire + (size_t)r1 * stride + soff) : 0u;
+      v = lo | (hi << 16);
     }
+    *(uint32_t*)(out + (long long)i * 4) = v;
   }
 }
 
@@ -1461,22 +1375,27 @@ static int grid_for(const iron_qwen3_model* m) {
   return iron_num_sms();
 }
 
-// host mirror of the per-CTA chunk sizes: the largest chunk of any CTA
+// host mirror of the per-CTA weight chunks: the largest of any CTA
 static size_t max_chunk(const iron_qwen3_model* m, int N, int lm_rows) {
   const int G = m->group, GQ = m->Hq / m->Hkv, D = m->D;
-  size_t mx = (size_t)lm_rows * (m->lm_w8 ? rowb(D, G) : D * 2);
+  size_t mx = std::max((size_t)KVP * 4 * HDIM, m->lm_w8 ? (size_t)LMT * tileb(D, G) : (size_t)lm_rows * D * 2);
   for (int c = 0; c < N; ++c) {
-    int h, c0, c1, lo, hi;
-    head_group(c, N, m->Hkv, h, c0, c1);
-    part((GQ + 2) * HDIM, c - c0, c1 - c0, lo, hi);
-    mx = std::max(mx, (size_t)(hi - lo) * rowb(D, G));
-    part(D, c - c0, c1 - c0, lo, hi);
-    mx = std::max(mx, (size_t)(hi - lo) * rowb_heads(GQ, G));
-    part(m->FF / 4, c, N, lo, hi);
-    const int k0 = 4 * lo, k1 = 4 * hi;
-    const int nsg = k1 > k0 ? (k1 - 1) / G - k0 / G + 1 : 0;
-    mx = std::max(mx, (size_t)2 * (k1 - k0) * rowb(D, G));
-    mx = std::max(mx, (size_t)(hi - lo) * D * 4 + (size_t)nsg * D * 2);
+    Plan P;
+    plan_tiles(*m, c, N, P);
+    mx = std::max(mx, (size_t)P.qnt * tileb(D, G));
+    mx = std::max(mx, (size_t)P.ont * tileb(GQ * HDIM, G));
+    mx = std::max(mx, (size_t)2 * P.gnt * tileb(D, G));
+    mx = std::max(mx, (size_t)P.dnt * tileb(m->FF, G));
+  }
+  return mx;
+}
+
+static int max_tiles(const iron_qwen3_model* m, int N) {
+  int mx = 0;
+  for (int c = 0; c < N; ++c) {
+    Plan P;
+    plan_tiles(*m, c, N, P);
+    mx = std::max(std::max(mx, P.qnt), std::max(P.ont, std::max(P.gnt, P.dnt)));
   }
   return mx;
 }
@@ -1485,21 +1404,23 @@ static int validate(const iron_qwen3_model* m, int grid) {
   IRON_REQUIRE(m != nullptr, IRON_ERR_ARG, "qwen3 step: null model");
   IRON_REQUIRE(m->HD == HDIM, IRON_ERR_UNSUPPORTED, "qwen3 step: head_dim %d (supported: 128)", m->HD);
   IRON_REQUIRE(m->Hkv >= 1 && m->Hq % m->Hkv == 0, IRON_ERR_ARG, "qwen3 step: Hq=%d, Hkv=%d", m->Hq, m->Hkv);
+  IRON_REQUIRE(m->Hkv <= HKVMAX, IRON_ERR_UNSUPPORTED, "qwen3 step: %d KV heads (at most %d)", m->Hkv, HKVMAX);
   const int GQ = m->Hq / m->Hkv;
-  IRON_REQUIRE(GQ == 1 || GQ == 2 || GQ == 4 || GQ == 8, IRON_ERR_UNSUPPORTED, "qwen3 step: GQA group %d", GQ);
+  IRON_REQUIRE(GQ == 1 || GQ == 2 || GQ == 4, IRON_ERR_UNSUPPORTED, "qwen3 step: GQA group %d", GQ);
   IRON_REQUIRE(m->group == 32 || m->group == 64 || m->group == 128, IRON_ERR_ARG, "qwen3 step: group %d",
                m->group);
-  IRON_REQUIRE(m->D % m->group == 0 && m->FF % m->group == 0 && m->D % 256 == 0 && m->D <= 4096 && m->FF % 4 == 0,
-               IRON_ERR_ARG, "qwen3 step: D=%d FF=%d must be multiples of the group and D a multiple of 256 (<= 4096)",
-               m->D, m->FF);
+  IRON_REQUIRE(m->D % m->group == 0 && m->FF % m->group == 0 && (GQ * HDIM) % m->group == 0 && m->D % 256 == 0 &&
+                   m->FF % 32 == 0 && m->D <= 4 * NT,
+               IRON_ERR_ARG, "qwen3 step: D=%d FF=%d must be multiples of the group, D a multiple of 256 (<= %d)",
+               m->D, m->FF, 4 * NT);
+  IRON_REQUIRE(m->FF <= 12288, IRON_ERR_UNSUPPORTED, "qwen3 step: intermediate size %d above 12288", m->FF);
   IRON_REQUIRE(grid >= m->Hkv && (grid + m->Hkv - 1) / m->Hkv <= GMAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: %d CTAs cannot form %d KV-head groups of at most %d", grid, m->Hkv, GMAX);
-  IRON_REQUIRE(4 * ((m->FF / 4 + grid - 1) / grid) <= SLICE_MAX, IRON_ERR_UNSUPPORTED,
-               "qwen3 step: down-projection slice wider than %d columns", SLICE_MAX);
-  IRON_REQUIRE(m->D <= 4 * NT, IRON_ERR_UNSUPPORTED, "qwen3 step: hidden size %d above %d", m->D, 4 * NT);
+  IRON_REQUIRE(max_tiles(m, grid) <= NTMAX, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: more than %d row tiles of one projection per CTA", NTMAX);
   IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
-  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->attn_ws &&
-                   m->cand && m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
+  IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->attn_ws && m->cand &&
+                   m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
                IRON_ERR_ARG, "qwen3 step: null buffer in the model descriptor");
   return IRON_OK;
 }
@@ -1515,58 +1436,49 @@ extern "C" int iron_qwen3_step_profile_buffer(void* buf) {
 }
 #endif
 
-extern "C" int iron_qwen3_sync_words(const iron_qwen3_model* m) { return SYNC_G1 + 2 * (m ? m->Hkv : 64); }
+extern "C" int iron_qwen3_sync_words(const iron_qwen3_model* m) {
+  (void)m;
+  return SYNC_WORDS;
+}
 extern "C" int64_t iron_qwen3_cand_bytes(void) { return 1024 * 8; }
 extern "C" int iron_qwen3_grid(const iron_qwen3_model* m) { return grid_for(m); }
 
-static int64_t partial_bytes(const iron_qwen3_model* m) {
-  return (int64_t)m->Hkv * GMAX * (m->Hq / m->Hkv) * (HDIM + 2) * 4;
-}
-static int64_t acc_bytes(const iron_qwen3_model* m) { return (int64_t)2 * m->n_layers * (1 + XREP) * m->D * 8; }
-static int64_t raw_ll_bytes(const iron_qwen3_model* m) { return (int64_t)(m->Hq + 2 * m->Hkv) * HDIM * 8; }
-
 extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
   if (!m || m->Hkv < 1 || m->Hq % m->Hkv != 0) return 0;
-  return partial_bytes(m) + acc_bytes(m) + raw_ll_bytes(m);
+  const int GQ = m->Hq / m->Hkv;
+  const int64_t words = (int64_t)m->D / 2 + (int64_t)m->Hkv * (GQ + 2) * HDIM / 2 +
+                        (int64_t)m->Hkv * GMAX * GQ * (HDIM + 2) + (int64_t)m->Hkv * m->D + m->FF / 2;
+  return words * 8;
 }
 
 extern "C" int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream) {
   IRON_REQUIRE(m && m->sync && m->attn_ws, IRON_ERR_ARG, "qwen3 sync reset: null");
-  cudaError_t e = cudaMemsetAsync(m->sync, 0, (size_t)iron_qwen3_sync_words(m) * 4, (cudaStream_t)stream);
+  cudaError_t e = cudaMemsetAsync(m->sync, 0, (size_t)SYNC_WORDS * 4, (cudaStream_t)stream);
   if (e == cudaSuccess)
-    e = cudaMemsetAsync((uint8_t*)m->attn_ws + partial_bytes(m), 0, (size_t)(acc_bytes(m) + raw_ll_bytes(m)),
-                        (cudaStream_t)stream);
+    e = cudaMemsetAsync(m->attn_ws, 0, (size_t)iron_qwen3_attn_ws_bytes(m), (cudaStream_t)stream);
   if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 sync reset: %s", cudaGetErrorString(e));
   return IRON_OK;
 }
 
-extern "C" int64_t iron_qwen3_pack_wo_heads_bytes(int D, int QD, int Hkv, int group) {
-  if (D < 1 || Hkv < 1 || group < 1 || QD % (Hkv * HDIM) != 0) return -1;
-  return (int64_t)Hkv * D * rowb_heads(QD / Hkv / HDIM, group);
+extern "C" int64_t iron_qwen3_tiles_bytes(int M, int K, int group) {
+  if (M < 1 || K < 32 || K % 32 || group < 32 || K % group) return -1;
+  return (int64_t)((M + TR - 1) / TR) * (int64_t)tileb(K, group);
 }
 
-extern "C" int iron_qwen3_pack_wo_heads(const void* wo_wire, int D, int QD, int Hkv, int group, void* out,
-                                        void* stream) {
-  IRON_REQUIRE(wo_wire && out, IRON_ERR_ARG, "pack_wo_heads: null pointer");
-  IRON_REQUIRE(D >= 1 && Hkv >= 1 && group >= 16 && QD % (Hkv * HDIM) == 0 && (QD / Hkv) % group == 0,
-               IRON_ERR_ARG, "pack_wo_heads: D=%d QD=%d Hkv=%d group=%d", D, QD, Hkv, group);
-  const long long total = iron_qwen3_pack_wo_heads_bytes(D, QD, Hkv, group);
-  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
-  pack_wo_heads_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)wo_wire, D, QD, Hkv, group,
-                                                                  (uint8_t*)out);
-  return iron_check_launch("pack_wo_heads_kernel");
-}
-
-extern "C" int iron_qwen3_pack_wd_cols(const void* wd_wire, int D, int FF, int group, void* out_q,
-                                       uint16_t* out_scales, void* stream) {
-  IRON_REQUIRE(wd_wire && out_q && out_scales, IRON_ERR_ARG, "pack_wd_cols: null pointer");
-  IRON_REQUIRE(D >= 1 && group >= 4 && FF % 4 == 0 && FF % group == 0, IRON_ERR_ARG,
-               "pack_wd_cols: D=%d FF=%d group=%d", D, FF, group);
-  const long long total = (long long)FF * D + (long long)(FF / group) * D;
-  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
-  pack_wd_cols_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)wd_wire, D, FF, group,
-                                                                 (uint8_t*)out_q, out_scales);
-  return iron_check_launch("pack_wd_cols_kernel");
+extern "C" int iron_qwen3_pack_tiles(const void* wire, int64_t row_stride, int M, int K_full, int col0, int K,
+                                     int group, void* out, void* stream) {
+  IRON_REQUIRE(wire && out, IRON_ERR_ARG, "pack_tiles: null pointer");
+  IRON_REQUIRE(M >= 1 && K >= 32 && K % 32 == 0 && (group == 32 || group == 64 || group == 128) && K % group == 0 &&
+                   col0 >= 0 && col0 % group == 0 && col0 + K <= K_full && K_full % group == 0 &&
+                   row_stride >= K_full + 2 * (K_full / group) && row_stride % 4 == 0,
+               IRON_ERR_ARG, "pack_tiles: M=%d K_full=%d col0=%d K=%d group=%d stride=%lld", M, K_full, col0, K, group,
+               (long long)row_stride);
+  IRON_REQUIRE(iron_aligned(wire, 4) && iron_aligned(out, 16), IRON_ERR_ALIGN, "pack_tiles: misaligned pointer");
+  const long long words = iron_qwen3_tiles_bytes(M, K, group) / 4;
+  const int blocks = (int)std::min<long long>((words + 255) / 256, 8192);
+  pack_tiles_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)wire, (long long)row_stride, M, K_full,
+                                                               col0, K, group, (uint8_t*)out);
+  return iron_check_launch("pack_tiles_kernel");
 }
 
 extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream) {
@@ -1578,8 +1490,9 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   p.m = *m;
   p.embed_input = embed_input;
   p.advance = advance;
-  p.kst = std::max(m->D, GQ * HDIM);
-  const size_t fixed = fixed_smem(p.kst, m->D, GQ, m->n_layers);
+  p.kmax = std::max(std::max(m->D, GQ * HDIM), m->FF);
+  p.hbn = std::max(m->FF, (GQ + 2) * HDIM);
+  const size_t fixed = fixed_smem(p.kmax, p.hbn, m->D, m->group, GQ, m->n_layers);
   IRON_REQUIRE(fixed + 64 * 1024 <= (size_t)SMEM_MAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: %zu bytes of fixed shared memory leave no room for the weight ring", fixed);
   p.ring = (int)(((size_t)SMEM_MAX - fixed) & ~(size_t)1023);
@@ -1592,8 +1505,8 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   cudaStream_t st = (cudaStream_t)stream;
 #define IRON_STEP_CASE(g, gq) \
   if (m->group == g && GQ == gq) return launch<g, gq>(p, grid, smem, st);
-  IRON_STEP_CASE(32, 2) IRON_STEP_CASE(32, 1) IRON_STEP_CASE(32, 4) IRON_STEP_CASE(32, 8)
-  IRON_STEP_CASE(64, 2) IRON_STEP_CASE(64, 4) IRON_STEP_CASE(128, 2) IRON_STEP_CASE(128, 4)
+  IRON_STEP_CASE(32, 2) IRON_STEP_CASE(32, 1) IRON_STEP_CASE(32, 4) IRON_STEP_CASE(64, 2) IRON_STEP_CASE(64, 4)
+  IRON_STEP_CASE(128, 2) IRON_STEP_CASE(128, 4)
 #undef IRON_STEP_CASE
   return iron_set_error(IRON_ERR_UNSUPPORTED, "qwen3 step: group %d with GQA group %d", m->group, GQ);
 }

@@ -155,7 +155,7 @@ class Qwen3Weights:
 class _StepLayer(C.Structure):
     """iron_qwen3_layer (include/iron_b200.h)."""
     _fields_ = [(n, C.c_void_p) for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd",
-                                          "wo_heads", "wd_cols", "wd_col_scales")]
+                                          "wqkv_t", "wo_t", "wg_t", "wu_t", "wd_t")]
 
 
 class _StepModel(C.Structure):
@@ -221,37 +221,71 @@ class Qwen3B200:
                 raise ValueError("the persistent step kernel decodes one stream (batch 1)")
             self._init_step(dev)
 
+    def _pack_tiles(self, wire, M, K_full, col0, K, dev, st, out=None):
+        """16-row tiles of rows [0, M), columns [col0, col0 + K) of a plain wire
+        (iron_qwen3_pack_tiles); into ``out`` when given."""
+        G = self.w.group
+        n = _lib.lib().iron_qwen3_tiles_bytes(M, K, G)
+        if out is None:
+            out = torch.empty(n, dtype=torch.uint8, device=dev)
+        abi("iron_qwen3_pack_tiles", ptr(wire), K_full + 2 * (K_full // G), M, K_full, col0, K, G, ptr(out), st)
+        return out
+
+    def _qkv_group_rows(self) -> torch.Tensor:
+        """Row order of the step kernel's QKV tiles: per KV head h the q rows of its
+        query heads, then its k rows, then its v rows."""
+        c = self.cfg
+        GQ, HD = c.Hq // c.Hkv, c.HD
+        rows = []
+        for h in range(c.Hkv):
+            rows.append(torch.arange(h * GQ * HD, (h + 1) * GQ * HD))
+            rows.append(torch.arange(c.QD + h * HD, c.QD + (h + 1) * HD))
+            rows.append(torch.arange(c.QD + c.Hkv * HD + h * HD, c.QD + c.Hkv * HD + (h + 1) * HD))
+        return torch.cat(rows)
+
     def _init_step(self, dev):
         c, w = self.cfg, self.w
         L = _lib.lib()
+        G = w.group
+        GQ = c.Hq // c.Hkv
         st = torch.cuda.current_stream(dev).cuda_stream
-        # the column-blocked O / down forms of the K-split projections (made once)
+        # the step kernel's weight tiles (made once; the plain wires stay for the other paths)
+        perm = self._qkv_group_rows().to(dev)
         self._step_packed = []
         layers = (_StepLayer * len(w.layers))()
         for i, Lw in enumerate(w.layers):
-            wo_h = torch.empty(L.iron_qwen3_pack_wo_heads_bytes(c.D, c.QD, c.Hkv, w.group), dtype=torch.uint8,
-                               device=dev)
-            abi("iron_qwen3_pack_wo_heads", ptr(Lw["wo"]), c.D, c.QD, c.Hkv, w.group, ptr(wo_h), st)
-            wd_q = torch.empty(c.FF * c.D, dtype=torch.uint8, device=dev)
-            wd_s = torch.empty((c.FF // w.group) * c.D, dtype=torch.int16, device=dev)
-            abi("iron_qwen3_pack_wd_cols", ptr(Lw["wd"]), c.D, c.FF, w.group, ptr(wd_q), ptr(wd_s), st)
-            self._step_packed.append((wo_h, wd_q, wd_s))
             for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd"):
-                if ptr(Lw[n]) % 16:  # the kernel bulk-copies weight rows: 16-byte aligned bases
+                if ptr(Lw[n]) % 16:  # the kernel bulk-copies weights: 16-byte aligned bases
                     raise ValueError(f"layer {i} {n}: device pointer not 16-byte aligned")
                 setattr(layers[i], n, ptr(Lw[n]))
-            layers[i].wo_heads, layers[i].wd_cols, layers[i].wd_col_scales = ptr(wo_h), ptr(wd_q), ptr(wd_s)
+            qkv_rows = Lw["wqkv"].view(c.QKV, -1).index_select(0, perm).contiguous()
+            wqkv_t = self._pack_tiles(qkv_rows, c.QKV, c.D, 0, c.D, dev, st)
+            per_head = L.iron_qwen3_tiles_bytes(c.D, GQ * c.HD, G)
+            wo_t = torch.empty(c.Hkv * per_head, dtype=torch.uint8, device=dev)
+            for h in range(c.Hkv):
+                self._pack_tiles(Lw["wo"], c.D, c.QD, h * GQ * c.HD, GQ * c.HD, dev, st,
+                                 out=wo_t[h * per_head:(h + 1) * per_head])
+            wg_t = self._pack_tiles(Lw["wg"], c.FF, c.D, 0, c.D, dev, st)
+            wu_t = self._pack_tiles(Lw["wu"], c.FF, c.D, 0, c.D, dev, st)
+            wd_t = self._pack_tiles(Lw["wd"], c.D, c.FF, 0, c.FF, dev, st)
+            torch.cuda.current_stream(dev).synchronize()  # qkv_rows is released below
+            del qkv_rows
+            self._step_packed.append((wqkv_t, wo_t, wg_t, wu_t, wd_t))
+            layers[i].wqkv_t, layers[i].wo_t = ptr(wqkv_t), ptr(wo_t)
+            layers[i].wg_t, layers[i].wu_t, layers[i].wd_t = ptr(wg_t), ptr(wu_t), ptr(wd_t)
+        self._lm_tiles = None
+        if self.lm_head == "int8":
+            self._lm_tiles = self._pack_tiles(w.lm_wire, c.V, c.D, 0, c.D, dev, st)
         torch.cuda.current_stream(dev).synchronize()
-        for n, t in (("embed", w.embed), ("lm_head wire", w.lm_wire)):
-            if t is not None and ptr(t) % 16:
-                raise ValueError(f"{n}: device pointer not 16-byte aligned")
+        if ptr(w.embed) % 16:
+            raise ValueError("embed: device pointer not 16-byte aligned")
         self._layer_table = torch.frombuffer(bytearray(bytes(layers)), dtype=torch.uint8).to(dev)
         m = _StepModel()
         m.D, m.FF, m.Hq, m.Hkv, m.HD, m.V = c.D, c.FF, c.Hq, c.Hkv, c.HD, c.V
         m.n_layers, m.group, m.max_seq, m.eps = len(w.layers), w.group, self.max_seq, c.eps
         m.layers = ptr(self._layer_table)
         m.final_norm, m.embed = ptr(w.final_norm), ptr(w.embed)
-        m.lm_w8 = ptr(w.lm_wire) if self.lm_head == "int8" else None
+        m.lm_w8 = ptr(self._lm_tiles) if self._lm_tiles is not None else None
         m.angles, m.kv = ptr(self.angles), ptr(self.kv)
         m.x, m.raw, m.attn, m.x1, m.gh = ptr(self.x), ptr(self.raw), ptr(self.attn), ptr(self.x1), ptr(self.gh)
         mp = C.byref(m)

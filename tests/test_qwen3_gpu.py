@@ -198,3 +198,87 @@ def test_batched_streams_match_single_stream(small):
         m = multi.step_tokens([toks[b][pos] for b in range(3)], pos)
         for b in range(3):
             assert int(single[b].step_tokens([toks[b][pos]], pos)[0]) == int(m[b])
+
+
+def test_step_kernel_is_bit_reproducible(full):
+    """The one-launch step forms every sum in a fixed order (no floating-point atomics,
+    no timing-dependent reduction): the same 28-layer step run three times from the same
+    KV cache and position gives bit-identical logits, K/V rows and final hidden state."""
+    cfg, w = full
+    S = 256
+    dec = Qwen3B200(w, max_seq=S, impl="step", keep_logits=True)
+    prompt = [int(t) for t in np.random.default_rng(21).integers(0, cfg.V, 150)]
+    for p, t in enumerate(prompt[:-1]):
+        dec.step_tokens([t], p)
+    kv0 = dec.kv.clone()
+    runs = []
+    for _ in range(3):
+        dec.kv.copy_(kv0)
+        tok = int(dec.step_tokens([prompt[-1]], len(prompt) - 1)[0])
+        runs.append((tok, dec.logits.clone(), dec.kv.clone(), dec.x.clone()))
+    for tok, lg, kv, x in runs[1:]:
+        assert tok == runs[0][0]
+        assert torch.equal(lg, runs[0][1]), "logits differ between identical steps"
+        assert torch.equal(kv, runs[0][2]), "K/V rows differ between identical steps"
+        assert torch.equal(x, runs[0][3]), "final hidden state differs between identical steps"
+
+
+def test_c1_single_layer_at_position_512():
+    """BASELINE configuration 1 as written: one Qwen3-0.6B-shaped decoder layer, one
+    decode step at position 512 over a KV cache of 512 positions filled with bf16 N(0,1),
+    input hidden state x ~ bf16 N(0,1), through the one-launch step kernel
+    (Qwen3NPU.__call__ form).  The layer output, the K/V row it writes and the logits
+    match the oracle run on the same cache."""
+    from oracle import ops
+    cfg = Qwen3Config.qwen3_0_6b()
+    w = Qwen3Weights.synthetic(cfg, seed=11, group=32, n_layers=1)
+    S = 640
+    dec = Qwen3B200(w, max_seq=S, impl="step", keep_logits=True)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    kv = dec.kv.view(1, 1, cfg.Hkv, S, 2, cfg.HD)
+    kv[:, :, :, :512] = torch.randn(1, 1, cfg.Hkv, 512, 2, cfg.HD, generator=g, device="cuda").to(torch.bfloat16)
+    x = torch.randn(cfg.D, generator=g, device="cuda").to(torch.bfloat16)
+    orc = OracleQwen3(Qwen3Shape(n_layers=1), w.to_numpy(), S, angles=host(dec.angles))
+    orc.kv[0] = host(dec.kv[0, 0]).reshape(cfg.Hkv, S, 2, cfg.HD)
+    got = dec(x, 512)
+    want_x = orc.layer(0, host(x), 512)
+    assert_close(host(dec.x[0]), want_x, what="C1 layer output")
+    kvg = host(dec.kv[0, 0]).reshape(cfg.Hkv, S, 2, cfg.HD)
+    assert_close(kvg[:, 512], orc.kv[0, :, 512], what="C1 K/V row written at 512")
+    wn = w.to_numpy()
+    xf = ops.rms_norm_ref(host(dec.x[0]).reshape(1, -1), wn["final_norm"], weighted=True, eps=cfg.eps).reshape(-1)
+    logits = ops.gemv_bf16(wn["embed"], xf)
+    assert_close(host(dec.logits[0]), logits, what="C1 logits")
+    assert got == int(np.argmax(logits))
+
+
+def test_greedy_top1_agreement_teacher_forced(full):
+    """Greedy top-1 agreement on the 28-layer model (the north-star gate): the GPU
+    prefills 48 random tokens and decodes 16 greedy steps; the oracle starts from the
+    GPU's KV cache after the prompt and is fed the GPU's input token at every step
+    (teacher forcing; its own K/V rows for the new positions).  Every step's token must
+    be the oracle's argmax, or a near-tie: a candidate whose oracle logit lies within
+    the bf16 gate of the oracle's maximum."""
+    cfg, w = full
+    S = 96
+    dec = Qwen3B200(w, max_seq=S, impl="step", keep_logits=True)
+    prompt = [int(t) for t in np.random.default_rng(31).integers(0, cfg.V, 48)]
+    for p, t in enumerate(prompt):
+        tok = int(dec.step_tokens([t], p)[0])
+    orc = OracleQwen3(Qwen3Shape(group=32), w.to_numpy(), S, angles=host(dec.angles))
+    orc.kv[...] = host(dec.kv).reshape(orc.kv.shape)
+    steps, agree, ties = 16, 0, 0
+    inp = tok
+    for i in range(steps):
+        p = len(prompt) + i
+        got = int(dec.step_tokens([inp], p)[0])
+        logits, want = orc.step(orc.embed(inp), p)
+        if got == want:
+            agree += 1
+        else:
+            gap = float(logits[want] - logits[got])
+            assert gap <= ATOL + RTOL * abs(float(logits[want])), f"step {i}: token {got} vs {want}, gap {gap:.4g}"
+            ties += 1
+        inp = got
+    print(f"top-1 agreement {agree}/{steps}, near-ties {ties}")
+    assert agree + ties == steps

@@ -18,7 +18,7 @@ from iron_b200.qwen3 import quantize_to_wire, wire_to_numpy
 from oracle import ops
 from oracle.bf16 import from_bits, rnd
 
-from helpers import host
+from helpers import assert_close, host
 
 pytestmark = pytest.mark.gpu
 
@@ -39,6 +39,8 @@ def _check(out, q, s_bits, x, G, what):
     lim2 = 2.0 ** -8 * np.abs(exact) + 2.0 ** -8 * mag + 1e-30
     err2 = np.abs(np.asarray(out, np.float64) - exact)
     assert np.all(err2 <= lim2), f"{what}: vs exact, worst {np.max(err2 / lim2):.3g}"
+    # the decode path's bf16 gate against the exact dequantised sum
+    assert_close(np.asarray(out, np.float64), exact, what=f"{what}: bf16 gate vs exact")
 
 
 def _gemv(wire, M, K, G, domain, x, residual=None):

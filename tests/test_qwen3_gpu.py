@@ -282,3 +282,31 @@ def test_greedy_top1_agreement_teacher_forced(full):
         inp = got
     print(f"top-1 agreement {agree}/{steps}, near-ties {ties}")
     assert agree + ties == steps
+
+
+def test_batch32_two_layer_decode_matches_oracle(small):
+    """Batch 32 (the north-star bs32 metric): the chained kernels with every projection
+    and the tied lm_head on the tcgen05 tensor cores, 2 layers of the Qwen3-0.6B shape and
+    the full vocabulary, 32 streams at two positions against the oracle per stream.
+    Logits within the bf16 gate; each token the oracle's argmax or a near-tie."""
+    cfg, w = small
+    B, S = 32, 16
+    dec = Qwen3B200(w, max_seq=S, batch=B, keep_logits=True)
+    assert dec.impl == "ops"
+    wn = w.to_numpy()
+    orcs = [OracleQwen3(Qwen3Shape(n_layers=2, group=32), wn, S, angles=host(dec.angles)) for _ in range(B)]
+    rng = np.random.default_rng(41)
+    toks = [int(t) for t in rng.integers(0, cfg.V, B)]
+    for pos in range(2):
+        got = dec.step_tokens(toks, pos)
+        lg = host(dec.logits)
+        nxt = []
+        for b in range(B):
+            logits, want = orcs[b].step(orcs[b].embed(toks[b]), pos)
+            assert_close(lg[b], logits, what=f"stream {b} pos {pos} logits")
+            g = int(got[b])
+            if g != want:
+                gap = float(logits[want] - logits[g])
+                assert gap <= ATOL + RTOL * abs(float(logits[want])), f"stream {b} pos {pos}: {g} vs {want}"
+            nxt.append(g)
+        toks = nxt

@@ -59,8 +59,8 @@ int64_t iron_launch_count(void);
  * biased: mv_int8.cc:60-114).  batch: activation rows sharing the weight.  Batch 1..8
  * (and 9..15) computes the exact dequantised sum (one bf16 rounding; launches of 8
  * rows); batch 16..256 on plain wires runs one tcgen05 tensor-core contraction with
- * the weight dequantised to bf16 (bf16(q*s), float32 accumulation), within the
- * bf16 tolerance of the exact sum (see iron_tc_status).  That contraction keeps its
+ * each weight q*s written as two bf16 planes (hi + lo, exact products) and float32
+ * accumulation: the exact sum up to float32 summation order (see iron_tc_status).  That contraction keeps its
  * split-K partial sums in one scratch array per GPU (and normalises RMS inputs into
  * another): such calls on different streams of one GPU must not overlap.
  * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.

@@ -8,23 +8,27 @@
 //     128-row tile (box 64 x 128, no swizzle) and the activations (box 64 x N bf16,
 //     128-byte swizzle, rows past the batch zero-filled), plus the tile's group
 //     scales for its whole K range once;
-//   - warps 1-8 dequantise the tile into bf16 w = bf16(q * s) straight into the
-//     128-byte-swizzled K-major layout the tensor core reads, and after the last
-//     k-block run the epilogue (warp w reads TMEM lane quarter w % 4, half of the
+//   - warps 1-8 dequantise the tile: w = q * s is exact in float32 (an 8-bit q times
+//     the 8-bit significand of s), and is written as two bf16 planes, hi = bf16(w) and
+//     lo = w - hi (exact in bf16: the low 8 of w's 16 significant bits), straight into
+//     the 128-byte-swizzled K-major layout the tensor core reads; after the last
+//     k-block they run the epilogue (warp w reads TMEM lane quarter w % 4, half of the
 //     columns each);
 //   - warp 9 allocates TMEM (N float32 columns per output tile, 2N for a gate/up
 //     pair), one lane issues tcgen05.mma (M = 128, N = batch padded to 16, K = 16 per
-//     instruction, bf16 x bf16 -> f32) and commits each k-block's MMAs to the stage's
-//     mbarrier, which frees the stage for the next copies.
+//     instruction, bf16 x bf16 -> f32) for the hi and the lo plane into the same
+//     accumulator and commits each k-block's MMAs to the stage's mbarrier, which frees
+//     the stage for the next copies.
 // K is split over CTAs so that the grid fills the GPU; each split writes its float32
 // partial tile to a fixed scratch array and the tile's last split (per-tile arrival
 // counter) adds the partials in split order and applies the epilogue, so results do
 // not depend on timing.
 //
-// Numerics: weights rounded to bf16 once (relative error <= 2^-9 per weight),
-// products and sums in float32 on the tensor core, the same bf16 epilogues as the
-// exact GEMV.  Within the bf16 gate (rtol 2e-2, atol 1e-2) of the exact sum; the
-// batch <= 8 kernels keep the exact form.
+// Numerics: every product q * s * x is exact (hi and lo planes times the bf16
+// activation, each product exact in float32), sums in float32 on the tensor core, the
+// same bf16 epilogues as the exact GEMV: the exact dequantised sum up to float32
+// summation order.  A single bf16 plane (bf16(q * s), 2^-9 relative per weight) flipped
+// enough bf16 roundings that a batch-32 Qwen3 step's logits left the bf16 gate.
 //
 // Every wait is bounded by %globaltimer; on a timeout the CTA records an error code
 // in a device word (iron_tc_status), lets its copies and MMAs finish (bounded), frees
@@ -181,7 +185,8 @@ __global__ void __launch_bounds__(NTH, 2)
   const int nkb = min(p.kbps, p.K / BK - kb0);
   const int k0 = kb0 * BK;
   const int N = p.N, S = p.stages;
-  uint8_t* atile = sm + p.off_a;      // [S][NW][128 rows][128 B] bf16, swizzled
+  constexpr int APL = W16 ? 1 : 2;     // bf16 planes of the weight tile (hi, lo)
+  uint8_t* atile = sm + p.off_a;      // [S][NW][APL][128 rows][128 B] bf16, swizzled
   uint8_t* xtile = sm + p.off_x;      // [S][N rows][128 B] bf16, swizzled
   uint8_t* raw = sm + p.off_raw;      // [S][NW][128 rows][64 B] int8
   uint8_t* scales = sm + p.off_scale; // [NW][128 rows][sbox B] bf16 group scales
@@ -269,13 +274,15 @@ __global__ void __launch_bounds__(NTH, 2)
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(sa(xtile + (size_t)s * N * 128));
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const uint64_t adesc = sw128_desc(sa(atile + (size_t)(s * NW + w) * BM * 128));
+        for (int w = 0; w < NW; ++w)
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes per 16 columns inside the swizzle atom
-            mma_bf16(tmem + (uint32_t)(w * N), adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
-                     (i > 0 || kk > 0) ? 1u : 0u);
-        }
+          for (int pl = 0; pl < APL; ++pl) {
+            const uint64_t adesc = sw128_desc(sa(atile + ((size_t)(s * NW + w) * APL + pl) * BM * 128));
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes per 16 columns inside the swizzle atom
+              mma_bf16(tmem + (uint32_t)(w * N), adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
+                       (i > 0 || kk > 0 || pl > 0) ? 1u : 0u);
+          }
         mma_commit(&freeb[s]);
       }
       mma_commit(acc_full);  // arrives once every MMA issued above has completed
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(NTH, 2)
 #pragma unroll
       for (int w = 0; w < NW; ++w) {
         const uint8_t* rt = raw + (size_t)(s * NW + w) * BM * BK;
-        uint8_t* at = atile + (size_t)(s * NW + w) * BM * 128;
+        uint8_t* at = atile + (size_t)(s * NW + w) * APL * BM * 128;  // hi plane, lo plane after it
         const uint16_t* sc = (const uint16_t*)(scales + (size_t)w * BM * p.sbox);
 #pragma unroll
         for (int it = 0; it < 4 * 4 / NDQ; ++it) {
@@ -314,22 +321,27 @@ __global__ void __launch_bounds__(NTH, 2)
           // -(2^23 + 2^7) * s is exact: the 8-bit significand of s shifted by 7 and by 23
           // spans 24 bits
           const float soff = -8388736.0f * sf;
-          uint32_t o[8];
+          uint32_t o[8], ol[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             // one byte permute gives the float 2^23 + (b + 128); one fma with s and soff
-            // gives b * s, exact in float32 (8-bit b times 8-bit s), rounded to bf16 once
-            // by the pack -- the same bits as bf16(float(b) * s)
+            // gives b * s, exact in float32 (8-bit b times 8-bit s); hi = bf16(b * s) and
+            // lo = b * s - hi, both exact in bf16
             float f[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               f[j] = fmaf(__uint_as_float(__byte_perm(qw[e], 0x4B000000u, 0x7440u | (uint32_t)j)), sf, soff);
             o[2 * e] = pack_bf16x2(f[0], f[1]);
             o[2 * e + 1] = pack_bf16x2(f[2], f[3]);
+            ol[2 * e] = pack_bf16x2(f[0] - bf_lo(o[2 * e]), f[1] - bf_hi(o[2 * e]));
+            ol[2 * e + 1] = pack_bf16x2(f[2] - bf_lo(o[2 * e + 1]), f[3] - bf_hi(o[2 * e + 1]));
           }
           // 16-byte chunk j of row r sits at chunk j ^ (r & 7) (128-byte swizzle)
-          *(uint4*)(at + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *(uint4*)(at + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          const int c0 = r * 128 + (((2 * c) ^ (r & 7)) << 4), c1 = r * 128 + (((2 * c + 1) ^ (r & 7)) << 4);
+          *(uint4*)(at + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+          *(uint4*)(at + c1) = make_uint4(o[4], o[5], o[6], o[7]);
+          *(uint4*)(at + BM * 128 + c0) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+          *(uint4*)(at + BM * 128 + c1) = make_uint4(ol[4], ol[5], ol[6], ol[7]);
         }
       }
       fence_proxy_async();  // the tensor core reads these stores through the async proxy
@@ -537,7 +549,7 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   tp.y = p.y;
   tp.ld_y = p.ld_y;
   tp.xor_mask = p.wa.xor_mask;
-  const int per_stage = NW * BM * 128 + N * 128 + NW * BM * BK;
+  const int per_stage = NW * 2 * BM * 128 + N * 128 + NW * BM * BK;  // hi + lo planes, activations, raw int8
   const int fixed = NW * BM * tp.sbox + 1024 /* alignment slack */ + 256 /* barriers, flags */;
   int S = (SMEM_CTA - fixed) / per_stage;
   if (S < 2) S = (SMEM_MAX - fixed) / per_stage;  // large batches: one CTA per SM
@@ -545,7 +557,7 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   if (S < 2) return 1;
   tp.stages = S;
   tp.off_a = 0;
-  tp.off_x = tp.off_a + S * NW * BM * 128;
+  tp.off_x = tp.off_a + S * NW * 2 * BM * 128;
   tp.off_raw = tp.off_x + S * N * 128;
   tp.off_scale = tp.off_raw + S * NW * BM * BK;
   tp.off_bar = (tp.off_scale + NW * BM * tp.sbox + 15) / 16 * 16;

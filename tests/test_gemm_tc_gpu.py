@@ -1,13 +1,13 @@
 """Batch >= 16 int8 projections on the tcgen05 tensor cores (csrc/gemm_tc.cu).
 
-The kernel dequantises each weight to bf16(q*s) and accumulates in float32 on the
-tensor core, so it is checked (a) tightly against the same bf16-dequantised weights
-in float64 (only the float32 summation order and the output rounding differ) and
-(b) against the exact dequantised sum (oracle.ops.gemv_int8_exact) within one bf16
-rounding of every weight -- the bf16 gate.  Shapes cover split K,
-ragged row tiles, groups 64/128 (a split may start inside a group), the biased
-payload domain, the residual / float32 / gate-up + RMSNorm epilogues, and batches
-16..256."""
+The kernel writes each dequantised weight q*s (exact in float32) as a bf16 hi plane
+and a bf16 lo plane and multiplies both, so every product is exact and only the
+float32 summation order differs from the exact dequantised sum
+(oracle.ops.gemv_int8_exact).  Checked (a) tightly against that sum: one bf16 output
+rounding plus float32 summation error, and (b) against the decode path's bf16 gate
+(rtol 2e-2, atol 1e-2).  Shapes cover split K, ragged row tiles, groups 64/128 (a
+split may start inside a group), the biased payload domain, the residual / float32 /
+gate-up + RMSNorm epilogues, and batches 16..256."""
 
 import numpy as np
 import pytest
@@ -23,22 +23,17 @@ from helpers import assert_close, host
 pytestmark = pytest.mark.gpu
 
 
-def _deq_bf16(q, s_bits, G):
-    return rnd(q.astype(np.float32) * np.repeat(from_bits(s_bits), G, axis=1)).astype(np.float64)
+def _deq(q, s_bits, G):
+    return (q.astype(np.float64) * np.repeat(from_bits(s_bits), G, axis=1).astype(np.float64))
 
 
 def _check(out, q, s_bits, x, G, what):
     x = np.asarray(x, np.float64)
-    w = _deq_bf16(q, s_bits, G)
-    want = x @ w.T
-    mag = np.abs(x) @ np.abs(w).T
-    lim = 2.0 ** -8 * np.abs(want) + 1e-5 * mag + 1e-30
-    err = np.abs(np.asarray(out, np.float64) - want)
-    assert np.all(err <= lim), f"{what}: vs bf16 weights, worst {np.max(err / lim):.3g}"
     exact = ops.gemv_int8_exact(q, s_bits, x)
-    lim2 = 2.0 ** -8 * np.abs(exact) + 2.0 ** -8 * mag + 1e-30
-    err2 = np.abs(np.asarray(out, np.float64) - exact)
-    assert np.all(err2 <= lim2), f"{what}: vs exact, worst {np.max(err2 / lim2):.3g}"
+    mag = np.abs(x) @ np.abs(_deq(q, s_bits, G)).T
+    lim = 2.0 ** -8 * np.abs(exact) + 1e-5 * mag + 1e-30
+    err = np.abs(np.asarray(out, np.float64) - exact)
+    assert np.all(err <= lim), f"{what}: vs the exact sum, worst {np.max(err / lim):.3g}"
     # the decode path's bf16 gate against the exact dequantised sum
     assert_close(np.asarray(out, np.float64), exact, what=f"{what}: bf16 gate vs exact")
 
@@ -101,8 +96,8 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     torch.cuda.synchronize()
     assert _lib.lib().iron_tc_status(0) == 0
     h = ops.rms_norm_f32(host(x), host(nw), 1e-6)
-    g = rnd(h.astype(np.float64) @ _deq_bf16(qg, sg, G).T)
-    u = rnd(h.astype(np.float64) @ _deq_bf16(qu, su, G).T)
+    g = rnd(h.astype(np.float64) @ _deq(qg, sg, G).T)
+    u = rnd(h.astype(np.float64) @ _deq(qu, su, G).T)
     want = rnd(ops.silu_tanh_bf16(g) * u)
     got = host(gh)
     # one bf16 step of g or u (float32 summation order) moves an output by ~2 ulps

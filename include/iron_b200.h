@@ -240,7 +240,9 @@ int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, con
  * the caller's other paths.  wqkv_t holds the QKV rows in KV-head-group order: for
  * each KV head h the q rows of query heads h*Hq/Hkv .. (h+1)*Hq/Hkv - 1, then the k
  * rows of head h, then its v rows.  wo_t holds, for each KV head h, the tiles of the
- * D rows of Wo restricted to h's (Hq/Hkv)*HD columns.  lm_w8, when set, is the int8
+ * D rows of Wo restricted to h's (Hq/Hkv)*HD columns.  wgu_t tile t holds gate rows
+ * 8t..8t+7 then up rows 8t..8t+7.  wd_t holds for every 16-row tile t of Wd its 4
+ * column slices of FF/4 (tiles of K = FF/4), at index 4t + j.  lm_w8, when set, is the int8
  * lm_head in tiles (iron_qwen3_pack_tiles of the V x D wire).
  * Every pointer in the descriptor is a device pointer, weight and table pointers
  * 16-byte aligned (they are bulk-copied); `layers` points to a DEVICE array of n_layers
@@ -265,9 +267,8 @@ typedef struct iron_qwen3_layer {
   const void* wd;         /* (D, FF) wire */
   const void* wqkv_t;     /* tiles of wqkv, rows in KV-head-group order */
   const void* wo_t;       /* tiles of wo, per KV head h its column block */
-  const void* wg_t;       /* tiles of wg */
-  const void* wu_t;       /* tiles of wu */
-  const void* wd_t;       /* tiles of wd */
+  const void* wgu_t;      /* tiles of 8 rows of wg over the same 8 rows of wu */
+  const void* wd_t;       /* tiles of wd cut into 4 slices along K, tile-major */
 } iron_qwen3_layer;
 
 typedef struct iron_qwen3_model {

@@ -21,8 +21,11 @@
 //                      heads by head h's column block of Wo for its O row tiles: a
 //                      K-split partial per (h, row) as words
 //   O partials   -->   every CTA: x1 = x + sum over h (fixed order), RMSNorm, its
-//                      gate/up row tiles, SiLU * up: h values as words
-//   h words      -->   the CTAs holding down row tiles: x_next = x1 + Wd h as words
+//                      gate/up tiles (8 gate rows over the matching 8 up rows), SiLU * up:
+//                      h values as words
+//   h words      -->   every CTA: its slices of the down projection (a 16-row tile cut
+//                      into DSL pieces along K) as partial-sum words
+//   down partials -->  every CTA: x_next = x1 + sum over the slices (fixed order)
 //
 // Projections.  Weight tiles of 16 rows are pre-packed in the A-fragment order of
 // mma.sync m16n8k32 (s8): a lane loads its fragment of a 32-column block with one
@@ -54,6 +57,7 @@ constexpr int KVP = 64;           // cached positions per K/V chunk (32 KB)
 constexpr int NTMAX = 16;         // most tiles of one projection in one CTA
 constexpr int HKVMAX = 8;         // most KV heads (O partial sums summed per row)
 constexpr int LMT = 4;            // int8 lm_head tiles per chunk
+constexpr int DSL = 4;            // K slices of a down-projection tile
 constexpr int XBS = 288;          // bytes of one 32-column block of B fragments (padded)
 constexpr int PIECE = 32768;      // bytes per cp.async.bulk instruction
 constexpr int SMEM_MAX = 227 * 1024;
@@ -262,16 +266,16 @@ struct Plan {
   int h, gi, gsz;       // KV-head group, index in the group, group size
   int qt0, qnt;         // QKV tiles of group h (q rows of its heads, then k, then v)
   int ot0, ont;         // O tiles of head h's column block (D / TR per head)
-  int gt0, gnt;         // gate/up pair tiles
-  int dt0, dnt;         // down tiles
+  int gt0, gnt;         // gate/up tiles (8 gate rows over the matching 8 up rows)
+  int ds0, dns;         // down slices (tile ds / DSL, K slice ds % DSL)
   int kst, ken, own;    // cached K/V positions [kst, ken) of this split; it holds pos
   int nkv, cpl;         // K/V chunks per layer; chunks per layer (4 + nkv)
   int hlo, hhi, hnch;   // lm_head rows (bf16) or tiles (int8), chunks
   int total;            // chunks of the token
 };
 
-// Tiles per CTA are balanced two ways: QKV and O within the KV-head group, gate/up
-// over all CTAs; the down tiles go to the CTAs holding the smaller gate/up share.
+// Tiles per CTA are balanced two ways: QKV and O within the KV-head group; gate/up
+// tiles and down slices (a 16-row tile cut into DSL pieces along K) over all CTAs.
 __host__ __device__ inline void plan_tiles(const iron_qwen3_model& m, int c, int N, Plan& P) {
   const int GQ = m.Hq / m.Hkv;
   int c0, c1;
@@ -285,20 +289,12 @@ __host__ __device__ inline void plan_tiles(const iron_qwen3_model& m, int c, int
   part(m.D / TR, P.gi, P.gsz, lo, hi);
   P.ot0 = lo;
   P.ont = hi - lo;
-  const int TG = m.FF / TR, TD = m.D / TR;
-  part(TG, c, N, lo, hi);
+  part(m.FF / 8, c, N, lo, hi);
   P.gt0 = lo;
   P.gnt = hi - lo;
-  const int q = TG / N, nlight = N - TG % N;
-  const int extras_below = (int)((long long)TG * c / N) - q * c;
-  if (P.gnt == q) {
-    part(TD, c - extras_below, nlight, lo, hi);
-    P.dt0 = lo;
-    P.dnt = hi - lo;
-  } else {
-    P.dt0 = 0;
-    P.dnt = 0;
-  }
+  part(m.D / TR * DSL, c, N, lo, hi);
+  P.ds0 = lo;
+  P.dns = hi - lo;
 }
 
 __device__ Plan make_plan(const Kp& p, int pos) {
@@ -337,8 +333,8 @@ struct RingState {                // shared by the producer lane and compute thr
 struct Smem {
   uint8_t* ring;
   uint8_t* xb;     // [kmax / 32][XBS] B fragments of the staged activation
-  double* xsd;     // [kmax / G] activation group scales (x 2^-15)
-  double* part;    // [2][NTMAX][TR] slice sums of a projection
+  int* xse;        // [kmax / G] activation group scale exponents: scale 2^xse (the 2^-15 included)
+  double* part;    // [NTMAX][TR] slice sums of a projection
   uint16_t* sx;    // [D] residual x (bf16 bits)
   uint16_t* sx1;   // [D] residual x1
   uint16_t* nw;    // [D] weights of the next RMSNorm
@@ -361,7 +357,7 @@ __host__ __device__ inline size_t att_floats(int GQ) {
 // bytes of everything but the ring (carve's layout: 16 arrays, each rounded up to 16 bytes)
 __host__ __device__ inline size_t fixed_smem(int kmax, int hbn, int D, int G, int GQ, int n_layers) {
   size_t o = 32 * 8 + NMB * 8 + sizeof(RingState) + 8 * 4;
-  o += (size_t)(kmax / 32) * XBS + (size_t)(kmax / G) * 8 + 2 * NTMAX * TR * 8;
+  o += (size_t)(kmax / 32) * XBS + (size_t)(kmax / G) * 4 + NTMAX * TR * 8;
   o += (size_t)D * 2 * 3 + (size_t)hbn * 2 + NTMAX * TR * 2;
   o += att_floats(GQ) * 4 + (size_t)GMAX * GQ * 2 * 4 + (size_t)D * 4;
   o += (size_t)n_layers * sizeof(iron_qwen3_layer);
@@ -383,8 +379,8 @@ __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
   s.rs = (RingState*)take((sizeof(RingState) + 15) & ~(size_t)15);
   s.flag = (int*)take(8 * 4);
   s.xb = take((size_t)(p.kmax / 32) * XBS);
-  s.xsd = (double*)take((size_t)(p.kmax / m.group) * 8);
-  s.part = (double*)take(2 * NTMAX * TR * 8);
+  s.xse = (int*)take((size_t)(p.kmax / m.group) * 4);
+  s.part = (double*)take(NTMAX * TR * 8);
   s.sx = (uint16_t*)take((size_t)m.D * 2);
   s.sx1 = (uint16_t*)take((size_t)m.D * 2);
   s.nw = (uint16_t*)take((size_t)m.D * 2);
@@ -441,14 +437,13 @@ __device__ int chunk_segs(const Kp& p, const Plan& P, const Smem& S, int i, Seg 
     sg[0] = {(const uint8_t*)L.wo_t + ((size_t)P.h * (D / TR) + P.ot0) * tb, (uint32_t)(P.ont * tb)};
     return 1;
   }
-  if (k == 2) {  // gate then up tiles [gt0, gt0 + gnt)
+  if (k == 2) {  // gate/up tiles [gt0, gt0 + gnt)
     const size_t tb = tileb(D, G);
-    sg[0] = {(const uint8_t*)L.wg_t + (size_t)P.gt0 * tb, (uint32_t)(P.gnt * tb)};
-    sg[1] = {(const uint8_t*)L.wu_t + (size_t)P.gt0 * tb, (uint32_t)(P.gnt * tb)};
-    return 2;
+    sg[0] = {(const uint8_t*)L.wgu_t + (size_t)P.gt0 * tb, (uint32_t)(P.gnt * tb)};
+    return 1;
   }
-  const size_t tb = tileb(m.FF, G);  // down
-  sg[0] = {(const uint8_t*)L.wd_t + (size_t)P.dt0 * tb, (uint32_t)(P.dnt * tb)};
+  const size_t tb = tileb(m.FF / DSL, G);  // down slices [ds0, ds0 + dns), tile-major
+  sg[0] = {(const uint8_t*)L.wd_t + (size_t)P.ds0 * tb, (uint32_t)(P.dns * tb)};
   return 1;
 }
 
@@ -536,7 +531,7 @@ __device__ bool wait_slot(uint64_t* mb, int32_t* sync, uint32_t parity) {
 // src(k, v) fills v[0..7] with the values k..k+7 (bf16-representable floats).  Eight
 // consecutive values per thread, G / 8 lanes per quantisation group.
 template <int G, class Src>
-__device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src) {
+__device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src, int k_ofs = 0) {
   constexpr int TEAM = G / 8;
   const int nchunk = K >> 3;
   for (int c0 = 0; c0 < nchunk; c0 += NT) {
@@ -544,7 +539,7 @@ __device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src) {
     const bool ok = c < nchunk;  // a group's TEAM lanes are all in range or all out
     float v[8];
     if (ok) {
-      src(c * 8, v);
+      src(c * 8, v);  // values k_ofs + c * 8 ..
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = 0.f;
@@ -562,7 +557,7 @@ __device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src) {
     uint32_t Y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) Y[e] = (uint32_t)(__float2int_rn(v[e] * sc * 32768.0f) + 0x808080) ^ 0x808080u;
-    const int k = c * 8;
+    const int k = k_ofs + c * 8;  // staged position (k_ofs: a multiple of the group)
     uint8_t* blk = S.xb + (size_t)(k >> 5) * XBS;
 #pragma unroll
     for (int qd = 0; qd < 2; ++qd) {  // 4 values -> one word per digit (4x4 byte transpose)
@@ -577,7 +572,9 @@ __device__ __forceinline__ void stage_digits(const Smem& S, int K, Src src) {
 #pragma unroll
       for (int d = 0; d < 4; ++d) *(uint32_t*)(blk + ((d * 4 + ((kk & 15) >> 2)) * 8 + (kk >> 4) * 4)) = wd[d];
     }
-    if (k % G == 0) S.xsd[k / G] = (double)inv * (1.0 / 32768.0);
+    // the group's scale inv * 2^-15 is a power of two: keep its exponent (inv == 0 only
+    // for an all-zero group, whose digits are all zero)
+    if (k % G == 0) S.xse[k / G] = inv == 0.f ? 0 : (int)((__float_as_uint(inv) >> 23) & 0xffu) - 127 - 15;
   }
   csync();
 }
@@ -606,13 +603,16 @@ __device__ __forceinline__ void norm_stage(const Smem& S, const uint16_t* x, int
 
 // stage K bf16 values from shared memory (no norm)
 template <int G>
-__device__ __forceinline__ void plain_stage(const Smem& S, const uint16_t* x, int K) {
-  stage_digits<G>(S, K, [&](int k, float(&v)[8]) {
-    const uint4 xa = *(const uint4*)(x + k);
-    const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
+__device__ __forceinline__ void plain_stage(const Smem& S, const uint16_t* x, int K, int k_ofs = 0) {
+  stage_digits<G>(
+      S, K,
+      [&](int k, float(&v)[8]) {
+        const uint4 xa = *(const uint4*)(x + k);
+        const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = bf2f((uint16_t)(xw[e >> 1] >> (16 * (e & 1))));
-  });
+        for (int e = 0; e < 8; ++e) v[e] = bf2f((uint16_t)(xw[e >> 1] >> (16 * (e & 1))));
+      },
+      k_ofs);
 }
 
 // K bf16 values (K % 8 == 0, read-only data) into shared memory with 16-byte loads
@@ -622,73 +622,95 @@ __device__ __forceinline__ void load_ro(uint16_t* dst, const uint16_t* src, int 
 
 // ---------------------------------------------------------------------------
 // Projection of nt packed weight tiles (16 rows x K) in a ring slot against the
-// staged activation.  PAIR: the slot holds nt gate tiles then nt up tiles.  Tile
-// layout: K/32 blocks of 512 bytes (lane L's A fragment at L * 16), then K/G groups
-// of 8 x 2 bf16 scales (rows g and g + 8 in one word).  The warps split each tile's
-// blocks into SL slices; the slice sums meet in shared memory and are added in slice
-// order.  epi(t, r, a, b) runs once per row r of tile t (b: the up row's sum).
+// staged activation.  Tile layout: K/32 blocks of 512 bytes (lane L's A fragment at
+// L * 16), then K/G groups of 8 x 2 bf16 scales (rows g and g + 8 in one word).  Tile
+// t reads the staged 32-column blocks from xkb0 + t * xkbs on (xkbs = 0: one shared
+// activation vector).  The warps split each tile's blocks into SL slices; the slice
+// sums meet in shared memory and are added in slice order.  PAIR: rows 8..15 of a
+// tile are the up rows of its gate rows 0..7, and epi(t, i, gate sum, up sum) runs
+// for i < 8; otherwise epi(t, r, sum, 0) for r < 16.
+//
+// Per 32-column block a lane turns its two exact integer sums c into c * 2^e (the
+// activation group's power-of-two scale) by building the double 2^52 + c + 2^31 at
+// exponent e and subtracting 2^52 + 2^31 at the same exponent (both exact), then
+// multiplies by the bf16 weight scale and accumulates in float64: the products are
+// exact, as before any rounding of the sum.
 // ---------------------------------------------------------------------------
 template <int G, bool PAIR, class Epi>
-__device__ __forceinline__ void gemv_tiles(const uint8_t* slot, int nt, int K, const Smem& S, Epi epi) {
-  constexpr int NW = PAIR ? 2 : 1;
+__device__ __forceinline__ void gemv_tiles(const uint8_t* slot, int nt, int K, int xkb0, int xkbs, const Smem& S,
+                                           Epi epi) {
   if (nt <= 0) return;  // uniform across the CTA
+  constexpr int UN = 4;  // blocks whose loads go out together
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int KB = K >> 5;
   const size_t TB = tileb(K, G);
-  const int SL = nt >= NWARP ? 1 : NWARP / nt;
-  const int items = nt * SL;
+  const int lsl = nt >= NWARP ? 0 : (nt >= 4 ? 1 : (nt >= 2 ? 2 : 3));  // log2 of the slices per tile
+  const int SL = 1 << lsl, items = nt << lsl;
   for (int it = wid; it < items; it += NWARP) {
-    const int t = it / SL, s = it - t * SL;
-    const int kb0 = s * KB / SL, kb1 = (s + 1) * KB / SL;
-    const uint8_t* tb[NW];
-    tb[0] = slot + (size_t)t * TB;
-    if (PAIR) tb[NW - 1] = slot + (size_t)(nt + t) * TB;
-    double acc[NW][2];
+    const int t = it >> lsl, s = it & (SL - 1);
+    const int kb0 = (s * KB) >> lsl, kb1 = ((s + 1) * KB) >> lsl;
+    const uint8_t* tb = slot + (size_t)t * TB;
+    const uint8_t* scb = tb + (size_t)KB * 512 + (lane >> 2) * 4;
+    const int xk = xkb0 + t * xkbs;  // this tile's first staged block
+    double a0 = 0.0, a1 = 0.0;
+    auto step = [&](uint4 a, uint2 bv, uint32_t sw, int ex) {
+      int cc[4];
+      mma_s8(cc, a, bv);
+      const uint32_t hi = (uint32_t)(0x433 + ex) << 20;
+      const double bias = __hiloint2double((int)hi, (int)0x80000000u);
+      const double d0 = __hiloint2double((int)hi, (int)((uint32_t)(cc[0] + 256 * cc[1]) ^ 0x80000000u)) - bias;
+      const double d1 = __hiloint2double((int)hi, (int)((uint32_t)(cc[2] + 256 * cc[3]) ^ 0x80000000u)) - bias;
+      a0 = fma(d0, (double)bf_lo(sw), a0);
+      a1 = fma(d1, (double)bf_hi(sw), a1);
+    };
+    int kb = kb0;
+    for (; kb + UN <= kb1; kb += UN) {
+      uint2 bv[UN];
+      uint4 a[UN];
+      uint32_t sw[UN];
+      int ex[UN];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) acc[w][0] = acc[w][1] = 0.0;
-#pragma unroll 2
-    for (int kb = kb0; kb < kb1; ++kb) {
-      const uint2 bv = *(const uint2*)(S.xb + (size_t)kb * XBS + lane * 8);
-      const int gl = (kb * 32) / G;
-      const double xs = S.xsd[gl];
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const uint4 a = *(const uint4*)(tb[w] + (size_t)kb * 512 + lane * 16);
-        const uint32_t sw = *(const uint32_t*)(tb[w] + (size_t)KB * 512 + gl * 32 + (lane >> 2) * 4);
-        int cc[4];
-        mma_s8(cc, a, bv);
-        acc[w][0] = fma((double)(cc[0] + 256 * cc[1]), (double)bf_lo(sw) * xs, acc[w][0]);
-        acc[w][1] = fma((double)(cc[2] + 256 * cc[3]), (double)bf_hi(sw) * xs, acc[w][1]);
+      for (int u = 0; u < UN; ++u) {
+        bv[u] = *(const uint2*)(S.xb + (size_t)(xk + kb + u) * XBS + lane * 8);
+        a[u] = *(const uint4*)(tb + (size_t)(kb + u) * 512 + lane * 16);
+        sw[u] = *(const uint32_t*)(scb + (((kb + u) * 32) / G) * 32);
+        ex[u] = S.xse[((xk + kb + u) * 32) / G];
       }
+#pragma unroll
+      for (int u = 0; u < UN; ++u) step(a[u], bv[u], sw[u], ex[u]);
     }
+    for (; kb < kb1; ++kb)
+      step(*(const uint4*)(tb + (size_t)kb * 512 + lane * 16), *(const uint2*)(S.xb + (size_t)(xk + kb) * XBS + lane * 8),
+           *(const uint32_t*)(scb + ((kb * 32) / G) * 32), S.xse[((xk + kb) * 32) / G]);
     // odd lanes hold the digit pieces weighted 2^16; after the pair sum lanes 4g hold
     // rows g and g + 8 (lanes 4g + 2 hold the empty second batch row)
-#pragma unroll
-    for (int w = 0; w < NW; ++w)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        double v = acc[w][hh];
-        if (lane & 1) v *= 65536.0;
-        acc[w][hh] = v + __shfl_xor_sync(~0u, v, 1);
-      }
+    a0 = (lane & 1) ? 65536.0 * a0 : a0;
+    a1 = (lane & 1) ? 65536.0 * a1 : a1;
+    a0 += __shfl_xor_sync(~0u, a0, 1);
+    a1 += __shfl_xor_sync(~0u, a1, 1);
     if ((lane & 3) == 0) {
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        double* pp = S.part + (size_t)w * NTMAX * TR + (size_t)it * TR;
-        pp[lane >> 2] = acc[w][0];
-        pp[(lane >> 2) + 8] = acc[w][1];
-      }
+      S.part[(size_t)it * TR + (lane >> 2)] = a0;
+      S.part[(size_t)it * TR + (lane >> 2) + 8] = a1;
     }
   }
   csync();
-  for (int e = threadIdx.x; e < nt * TR; e += NT) {
-    const int t = e / TR, r = e - t * TR;
-    double a = 0.0, b = 0.0;
-    for (int s = 0; s < SL; ++s) {
-      a += S.part[(size_t)(t * SL + s) * TR + r];
-      if (PAIR) b += S.part[(size_t)NTMAX * TR + (size_t)(t * SL + s) * TR + r];
+  if (PAIR) {
+    for (int e = threadIdx.x; e < nt * 8; e += NT) {
+      const int t = e >> 3, i = e & 7;
+      double g = 0.0, u = 0.0;
+      for (int s = 0; s < SL; ++s) {
+        g += S.part[(size_t)((t << lsl) + s) * TR + i];
+        u += S.part[(size_t)((t << lsl) + s) * TR + i + 8];
+      }
+      epi(t, i, g, u);
     }
-    epi(t, r, a, b);
+  } else {
+    for (int e = threadIdx.x; e < nt * TR; e += NT) {
+      const int t = e >> 4, r = e & 15;
+      double a = 0.0;
+      for (int s = 0; s < SL; ++s) a += S.part[(size_t)((t << lsl) + s) * TR + r];
+      epi(t, r, a, 0.0);
+    }
   }
 }
 
@@ -815,8 +837,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   // hand-off words (zeroed by iron_qwen3_sync_reset)
   constexpr int RAWW = (GQ + 2) * HDIM / 2;  // q/k/v words of one KV-head group
   constexpr int ATTW = GQ * (HDIM + 2);      // words of one attention split
-  unsigned long long* xw = (unsigned long long*)m.attn_ws;          // [D / 2] x between layers
-  unsigned long long* raww = xw + D / 2;                            // [Hkv][RAWW]
+  unsigned long long* dpw = (unsigned long long*)m.attn_ws;         // [D / TR][DSL][TR] down partial sums
+  unsigned long long* raww = dpw + (size_t)DSL * D;                 // [Hkv][RAWW]
   unsigned long long* attw = raww + (size_t)m.Hkv * RAWW;           // [Hkv][GMAX][ATTW]
   unsigned long long* ow = attw + (size_t)m.Hkv * GMAX * ATTW;      // [Hkv][D] O partial sums
   unsigned long long* hw = ow + (size_t)m.Hkv * D;                  // [FF / 2] SwiGLU outputs
@@ -866,6 +888,40 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   // a bounded poll by every compute thread, then a CTA-wide verdict
   auto all_ok = [&](bool mine) -> bool { return !cvote_any(!mine); };
 
+  // x = bf16(x1 + bf16(sum of the DSL down slices, in slice order)) for rows
+  // tid + k * NT (k < 4: D <= 4 * NT), from the words of the layer tagged tg; all 4 * DSL
+  // words of a thread are loaded and reloaded together
+  auto next_x = [&](uint32_t tg) -> bool {
+    constexpr int RPT = 4, NU = RPT * DSL;
+    unsigned long long v[NU];
+    uint32_t want = 0;
+    auto d_addr = [&](int u) {
+      const int r = (u / DSL) * NT + tid;
+      return dpw + ((size_t)(r >> 4) * DSL + (u % DSL)) * TR + (r & 15);
+    };
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      v[u] = 0ull;
+      if ((u / DSL) * NT + tid < D) {
+        v[u] = ll_ld(d_addr(u));
+        want |= 1u << u;
+      }
+    }
+    const bool mine = poll_rounds<NU>(d_addr, v, want, tg, 48, sync);
+    if (!all_ok(mine)) return false;
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = k * NT + tid;
+      if (r >= D) continue;
+      double acc = 0.0;
+#pragma unroll
+      for (int j = 0; j < DSL; ++j) acc += ll_val_d(v[k * DSL + j]);
+      S.sx[r] = f2bf(bf2f(S.sx1[r]) + rbf_d(acc));
+    }
+    csync();  // sx is read across threads
+    return true;
+  };
+
   const int h = P.h;
   const float scale = 1.4426950408889634f / sqrtf((float)HDIM);
   for (int layer = 0; layer < NL && ok; ++layer) {
@@ -875,11 +931,8 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 0);
     // ---- x: the previous layer's output rows ----
     load_ro(S.nw, Lw.norm1, D);
-    if (layer > 0) {  // written by the previous layer's down projection, with its epoch
-      ok = all_ok(poll<2>(xw, D / 2, ep - 1u, 32, sync, [&](int i, unsigned long long w) {
-        ((uint32_t*)S.sx)[i] = (uint32_t)w;
-      }));
-      if (!ok) break;
+    if (layer > 0) {  // the previous layer's down slices, with its epoch
+      if (!(ok = next_x(tag16_of(ep - 1u)))) break;
     } else {
       csync();  // the embedding row (or x) in sx, written across threads
     }
@@ -890,7 +943,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     norm_stage<G>(S, S.sx, D, m.eps, 1, nullptr);
     STEP_MARK(layer, 2);
     ok = consume(layer, 3, [&](const uint8_t* wb) {
-      gemv_tiles<G, false>(wb, P.qnt, D, S, [&](int t, int r, double a, double) {
+      gemv_tiles<G, false>(wb, P.qnt, D, 0, 0, S, [&](int t, int r, double a, double) {
         S.outb[t * TR + r] = f2bf((float)a);
       });
     });
@@ -1117,7 +1170,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 10);
     // ---- O (head h's column block): partial[h][row] = Wo[row, head h] @ attn[head h] ----
     ok = consume(layer, 11, [&](const uint8_t* wb) {
-      gemv_tiles<G, false>(wb, P.ont, GQ * HDIM, S, [&](int t, int r, double a, double) {
+      gemv_tiles<G, false>(wb, P.ont, GQ * HDIM, 0, 0, S, [&](int t, int r, double a, double) {
         ll_put_d(ow + (size_t)h * D + (P.ot0 + t) * TR + r, a, tg);
       });
     });
@@ -1158,31 +1211,34 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 14);
     // ---- gate/up: gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for the CTA's tiles ----
     ok = consume(layer, 15, [&](const uint8_t* wb) {
-      gemv_tiles<G, true>(wb, P.gnt, D, S, [&](int t, int r, double g, double u) {
-        S.outb[t * TR + r] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
+      gemv_tiles<G, true>(wb, P.gnt, D, 0, 0, S, [&](int t, int i, double g, double u) {
+        S.outb[t * 8 + i] = f2bf(silu_tanh_bf16(rbf_d(g)) * rbf_d(u));
       });
     });
     if (!ok) break;
-    for (int i = tid; i < P.gnt * TR / 2; i += NT) ll_put(hw + P.gt0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
+    for (int i = tid; i < P.gnt * 4; i += NT) ll_put(hw + P.gt0 * 4 + i, ((const uint32_t*)S.outb)[i], ep);
     STEP_MARK(layer, 16);
-    // ---- down: x_next = bf16(x1 + bf16(Wd @ gh)) for the CTA's row tiles ----
-    if (P.dnt > 0) {
-      ok = all_ok(poll<6>(hw, FF / 2, ep, 32, sync, [&](int i, unsigned long long w) {
-        ((uint32_t*)S.hb)[i] = (uint32_t)w;
-      }));
-      if (!ok) break;
+    // ---- down: this CTA's slices, partial[t][j][r] = Wd[tile t rows, K slice j] @ gh[slice j] ----
+    {
+      const int KS = FF / DSL;  // columns of a slice
+      bool mine = true;
+      for (int q = 0; q < P.dns; ++q) {  // the gh values of each slice, staged at blocks q * KS / 32 ..
+        const int j = (P.ds0 + q) % DSL;
+        mine = mine && poll<3>(hw + (size_t)j * KS / 2, KS / 2, ep, 32, sync, [&](int i, unsigned long long w) {
+                 ((uint32_t*)(S.hb + q * KS))[i] = (uint32_t)w;
+               });
+      }
+      if (!(ok = all_ok(mine))) break;
       STEP_MARK(layer, 17);
-      plain_stage<G>(S, S.hb, FF);
+      for (int q = 0; q < P.dns; ++q) plain_stage<G>(S, S.hb + q * KS, KS, q * KS);
       STEP_MARK(layer, 18);
-    }
-    ok = consume(layer, 19, [&](const uint8_t* wb) {
-      gemv_tiles<G, false>(wb, P.dnt, FF, S, [&](int t, int r, double a, double) {
-        const int row = (P.dt0 + t) * TR + r;
-        S.outb[t * TR + r] = f2bf(bf2f(S.sx1[row]) + rbf_d(a));
+      ok = consume(layer, 19, [&](const uint8_t* wb) {
+        gemv_tiles<G, false>(wb, P.dns, KS, 0, KS / 32, S, [&](int q, int r, double a, double) {
+          ll_put_d(dpw + (size_t)(P.ds0 + q) * TR + r, a, tg);
+        });
       });
-    });
-    if (!ok) break;
-    for (int i = tid; i < P.dnt * TR / 2; i += NT) ll_put(xw + P.dt0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
+      if (!ok) break;
+    }
     STEP_MARK(layer, 20);
   }
 
@@ -1191,9 +1247,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     // ---- final: x = the last layer's output, RMSNorm (golden) + lm_head + greedy argmax ----
     const uint32_t ep = tok_epoch * (uint32_t)NL + (uint32_t)NL;
     load_ro(S.nw, m.final_norm, D);
-    ok = all_ok(poll<2>(xw, D / 2, ep, 32, sync, [&](int i, unsigned long long w) {
-      ((uint32_t*)S.sx)[i] = (uint32_t)w;
-    }));
+    ok = next_x(tag16_of(ep));
   }
   if (ok) {
     if (blockIdx.x == 0) {
@@ -1234,7 +1288,7 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
       if (m.lm_w8) {
         const int t0 = P.hlo + j * LMT, nt = min(P.hhi, t0 + LMT) - t0;
         ok = consume(NL, -1, [&](const uint8_t* wb) {
-          gemv_tiles<G, false>(wb, nt, D, S, [&](int t, int r, double a, double) {
+          gemv_tiles<G, false>(wb, nt, D, 0, 0, S, [&](int t, int r, double a, double) {
             const int row = (t0 + t) * TR + r;
             if (row < m.V) track(row, f2bf((float)a));
           });
@@ -1384,8 +1438,8 @@ static size_t max_chunk(const iron_qwen3_model* m, int N, int lm_rows) {
     plan_tiles(*m, c, N, P);
     mx = std::max(mx, (size_t)P.qnt * tileb(D, G));
     mx = std::max(mx, (size_t)P.ont * tileb(GQ * HDIM, G));
-    mx = std::max(mx, (size_t)2 * P.gnt * tileb(D, G));
-    mx = std::max(mx, (size_t)P.dnt * tileb(m->FF, G));
+    mx = std::max(mx, (size_t)P.gnt * tileb(D, G));
+    mx = std::max(mx, (size_t)P.dns * tileb(m->FF / DSL, G));
   }
   return mx;
 }
@@ -1395,7 +1449,7 @@ static int max_tiles(const iron_qwen3_model* m, int N) {
   for (int c = 0; c < N; ++c) {
     Plan P;
     plan_tiles(*m, c, N, P);
-    mx = std::max(std::max(mx, P.qnt), std::max(P.ont, std::max(P.gnt, P.dnt)));
+    mx = std::max(std::max(mx, P.qnt), std::max(P.ont, std::max(P.gnt, P.dns)));
   }
   return mx;
 }
@@ -1413,11 +1467,17 @@ static int validate(const iron_qwen3_model* m, int grid) {
                    m->FF % 32 == 0 && m->D <= 4 * NT,
                IRON_ERR_ARG, "qwen3 step: D=%d FF=%d must be multiples of the group, D a multiple of 256 (<= %d)",
                m->D, m->FF, 4 * NT);
-  IRON_REQUIRE(m->FF <= 12288, IRON_ERR_UNSUPPORTED, "qwen3 step: intermediate size %d above 12288", m->FF);
+  IRON_REQUIRE(m->FF <= 12288 && m->FF % (DSL * 128) == 0, IRON_ERR_UNSUPPORTED,
+               "qwen3 step: intermediate size %d (a multiple of %d up to 12288)", m->FF, DSL * 128);
   IRON_REQUIRE(grid >= m->Hkv && (grid + m->Hkv - 1) / m->Hkv <= GMAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: %d CTAs cannot form %d KV-head groups of at most %d", grid, m->Hkv, GMAX);
   IRON_REQUIRE(max_tiles(m, grid) <= NTMAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: more than %d row tiles of one projection per CTA", NTMAX);
+  for (int c = 0; c < grid; ++c) {  // the down slices of a CTA are staged side by side
+    Plan P;
+    plan_tiles(*m, c, grid, P);
+    IRON_REQUIRE(P.dns <= DSL, IRON_ERR_UNSUPPORTED, "qwen3 step: %d down slices on one CTA", P.dns);
+  }
   IRON_REQUIRE(grid <= 1024, IRON_ERR_UNSUPPORTED, "qwen3 step: grid %d exceeds the candidate slots", grid);
   IRON_REQUIRE(m->layers && m->final_norm && m->embed && m->angles && m->kv && m->x && m->attn_ws && m->cand &&
                    m->tok && m->pos && m->seq_len && m->kv_off && m->sync,
@@ -1446,7 +1506,7 @@ extern "C" int iron_qwen3_grid(const iron_qwen3_model* m) { return grid_for(m); 
 extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
   if (!m || m->Hkv < 1 || m->Hq % m->Hkv != 0) return 0;
   const int GQ = m->Hq / m->Hkv;
-  const int64_t words = (int64_t)m->D / 2 + (int64_t)m->Hkv * (GQ + 2) * HDIM / 2 +
+  const int64_t words = (int64_t)DSL * m->D + (int64_t)m->Hkv * (GQ + 2) * HDIM / 2 +
                         (int64_t)m->Hkv * GMAX * GQ * (HDIM + 2) + (int64_t)m->Hkv * m->D + m->FF / 2;
   return words * 8;
 }

@@ -155,7 +155,7 @@ class Qwen3Weights:
 class _StepLayer(C.Structure):
     """iron_qwen3_layer (include/iron_b200.h)."""
     _fields_ = [(n, C.c_void_p) for n in ("norm1", "wqkv", "qn", "kn", "wo", "norm2", "wg", "wu", "wd",
-                                          "wqkv_t", "wo_t", "wg_t", "wu_t", "wd_t")]
+                                          "wqkv_t", "wo_t", "wgu_t", "wd_t")]
 
 
 class _StepModel(C.Structure):
@@ -265,14 +265,19 @@ class Qwen3B200:
             for h in range(c.Hkv):
                 self._pack_tiles(Lw["wo"], c.D, c.QD, h * GQ * c.HD, GQ * c.HD, dev, st,
                                  out=wo_t[h * per_head:(h + 1) * per_head])
-            wg_t = self._pack_tiles(Lw["wg"], c.FF, c.D, 0, c.D, dev, st)
-            wu_t = self._pack_tiles(Lw["wu"], c.FF, c.D, 0, c.D, dev, st)
-            wd_t = self._pack_tiles(Lw["wd"], c.D, c.FF, 0, c.FF, dev, st)
-            torch.cuda.current_stream(dev).synchronize()  # qkv_rows is released below
-            del qkv_rows
-            self._step_packed.append((wqkv_t, wo_t, wg_t, wu_t, wd_t))
+            # gate/up: tile t = gate rows 8t..8t+7 over up rows 8t..8t+7
+            gu_rows = torch.stack([Lw["wg"].view(c.FF // 8, 8, -1), Lw["wu"].view(c.FF // 8, 8, -1)], 1)
+            gu_rows = gu_rows.reshape(2 * c.FF, -1).contiguous()
+            wgu_t = self._pack_tiles(gu_rows, 2 * c.FF, c.D, 0, c.D, dev, st)
+            # down: the 4 column slices of every 16-row tile, tile-major
+            ks = c.FF // 4
+            sl = [self._pack_tiles(Lw["wd"], c.D, c.FF, j * ks, ks, dev, st).view(c.D // 16, -1) for j in range(4)]
+            wd_t = torch.stack(sl, 1).reshape(-1).contiguous()
+            torch.cuda.current_stream(dev).synchronize()  # the row copies are released below
+            del qkv_rows, gu_rows, sl
+            self._step_packed.append((wqkv_t, wo_t, wgu_t, wd_t))
             layers[i].wqkv_t, layers[i].wo_t = ptr(wqkv_t), ptr(wo_t)
-            layers[i].wg_t, layers[i].wu_t, layers[i].wd_t = ptr(wg_t), ptr(wu_t), ptr(wd_t)
+            layers[i].wgu_t, layers[i].wd_t = ptr(wgu_t), ptr(wd_t)
         self._lm_tiles = None
         if self.lm_head == "int8":
             self._lm_tiles = self._pack_tiles(w.lm_wire, c.V, c.D, 0, c.D, dev, st)

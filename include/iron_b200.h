@@ -232,15 +232,14 @@ int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, con
  * the one of the per-operator entry points above (iron_qkv_head with the golden
  * RMSNorm form, iron_decode_attn, iron_mlp_block, iron_rmsnorm mode 1,
  * iron_lm_head_*_argmax): exact int8 x block-floating-point dot products summed in
- * float64, one bf16 rounding per projection output; the O projection is summed over
- * the KV-head groups in group order.  Results do not depend on timing: two steps from
+ * float64, one bf16 rounding per projection output; the down projection is summed
+ * over its K slices in slice order.  Results do not depend on timing: two steps from
  * the same state give the same bits.
  * The projections read their weights in 16-row tiles made once by
  * iron_qwen3_pack_tiles (the *_t fields); the plain wires stay in the descriptor for
  * the caller's other paths.  wqkv_t holds the QKV rows in KV-head-group order: for
  * each KV head h the q rows of query heads h*Hq/Hkv .. (h+1)*Hq/Hkv - 1, then the k
- * rows of head h, then its v rows.  wo_t holds, for each KV head h, the tiles of the
- * D rows of Wo restricted to h's (Hq/Hkv)*HD columns.  wgu_t tile t holds gate rows
+ * rows of head h, then its v rows.  wo_t holds the row tiles of Wo.  wgu_t tile t holds gate rows
  * 8t..8t+7 then up rows 8t..8t+7.  wd_t holds for every 16-row tile t of Wd its 4
  * column slices of FF/4 (tiles of K = FF/4), at index 4t + j.  lm_w8, when set, is the int8
  * lm_head in tiles (iron_qwen3_pack_tiles of the V x D wire).
@@ -266,7 +265,7 @@ typedef struct iron_qwen3_layer {
   const void* wu;         /* (FF, D) wire */
   const void* wd;         /* (D, FF) wire */
   const void* wqkv_t;     /* tiles of wqkv, rows in KV-head-group order */
-  const void* wo_t;       /* tiles of wo, per KV head h its column block */
+  const void* wo_t;       /* tiles of wo (16 rows, all columns) */
   const void* wgu_t;      /* tiles of 8 rows of wg over the same 8 rows of wu */
   const void* wd_t;       /* tiles of wd cut into 4 slices along K, tile-major */
 } iron_qwen3_layer;

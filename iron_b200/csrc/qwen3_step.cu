@@ -17,10 +17,9 @@
 //   x  --(all CTAs)-->  RMSNorm + QKV rows of KV head h (group h's CTAs, 16-row tiles)
 //   q/k/v words  -->   every CTA of group h: q/k RMSNorm + RoPE, one split of head h's
 //                      positions (flash decoding); the split's (m, l, o) as words
-//   split words  -->   every CTA of group h merges the splits and multiplies the merged
-//                      heads by head h's column block of Wo for its O row tiles: a
-//                      K-split partial per (h, row) as words
-//   O partials   -->   every CTA: x1 = x + sum over h (fixed order), RMSNorm, its
+//   split words  -->   the group's first CTA merges the splits: the bf16 heads as words
+//   merged heads -->   the CTAs holding O row tiles: x1 = x + Wo attn, rows as words
+//   x1 words     -->   every CTA: RMSNorm, its
 //                      gate/up tiles (8 gate rows over the matching 8 up rows), SiLU * up:
 //                      h values as words
 //   h words      -->   every CTA: its slices of the down projection (a 16-row tile cut
@@ -55,7 +54,6 @@ constexpr int NMB = 16;           // ring slots (chunks in flight at most)
 constexpr int GMAX = 24;          // most CTAs in one KV-head group (attention splits)
 constexpr int KVP = 64;           // cached positions per K/V chunk (32 KB)
 constexpr int NTMAX = 16;         // most tiles of one projection in one CTA
-constexpr int HKVMAX = 8;         // most KV heads (O partial sums summed per row)
 constexpr int LMT = 4;            // int8 lm_head tiles per chunk
 constexpr int DSL = 4;            // K slices of a down-projection tile
 constexpr int XBS = 288;          // bytes of one 32-column block of B fragments (padded)
@@ -71,7 +69,7 @@ struct Kp {
   int embed_input, advance;
   int ring;     // ring bytes
   int lm_rows;  // bf16 lm_head rows per chunk
-  int kmax;     // longest staged activation (max of D, GQ*HD, FF)
+  int kmax;     // longest staged activation (max of D, Hq*HD, FF)
   int hbn;      // bf16 values of the polled-vector buffer
 };
 
@@ -265,7 +263,7 @@ __host__ __device__ inline void head_group(int c, int N, int Hkv, int& h, int& c
 struct Plan {
   int h, gi, gsz;       // KV-head group, index in the group, group size
   int qt0, qnt;         // QKV tiles of group h (q rows of its heads, then k, then v)
-  int ot0, ont;         // O tiles of head h's column block (D / TR per head)
+  int ot0, ont;         // O row tiles (all Hq * HD columns)
   int gt0, gnt;         // gate/up tiles (8 gate rows over the matching 8 up rows)
   int ds0, dns;         // down slices (tile ds / DSL, K slice ds % DSL)
   int kst, ken, own;    // cached K/V positions [kst, ken) of this split; it holds pos
@@ -274,8 +272,8 @@ struct Plan {
   int total;            // chunks of the token
 };
 
-// Tiles per CTA are balanced two ways: QKV and O within the KV-head group; gate/up
-// tiles and down slices (a 16-row tile cut into DSL pieces along K) over all CTAs.
+// Tiles per CTA: QKV within the KV-head group; O row tiles, gate/up tiles and down
+// slices (a 16-row tile cut into DSL pieces along K) over all CTAs.
 __host__ __device__ inline void plan_tiles(const iron_qwen3_model& m, int c, int N, Plan& P) {
   const int GQ = m.Hq / m.Hkv;
   int c0, c1;
@@ -286,7 +284,7 @@ __host__ __device__ inline void plan_tiles(const iron_qwen3_model& m, int c, int
   part((GQ + 2) * HDIM / TR, P.gi, P.gsz, lo, hi);
   P.qt0 = lo;
   P.qnt = hi - lo;
-  part(m.D / TR, P.gi, P.gsz, lo, hi);
+  part(m.D / TR, c, N, lo, hi);
   P.ot0 = lo;
   P.ont = hi - lo;
   part(m.FF / 8, c, N, lo, hi);
@@ -432,9 +430,9 @@ __device__ int chunk_segs(const Kp& p, const Plan& P, const Smem& S, int i, Seg 
     return 1;
   }
   const int k = r - P.nkv;
-  if (k == 1) {  // O: head h's column block, row tiles [ot0, ot0 + ont)
-    const size_t tb = tileb(GQ * HDIM, G);
-    sg[0] = {(const uint8_t*)L.wo_t + ((size_t)P.h * (D / TR) + P.ot0) * tb, (uint32_t)(P.ont * tb)};
+  if (k == 1) {  // O: row tiles [ot0, ot0 + ont)
+    const size_t tb = tileb(m.Hq * HDIM, G);
+    sg[0] = {(const uint8_t*)L.wo_t + (size_t)P.ot0 * tb, (uint32_t)(P.ont * tb)};
     return 1;
   }
   if (k == 2) {  // gate/up tiles [gt0, gt0 + gnt)
@@ -840,8 +838,9 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   unsigned long long* dpw = (unsigned long long*)m.attn_ws;         // [D / TR][DSL][TR] down partial sums
   unsigned long long* raww = dpw + (size_t)DSL * D;                 // [Hkv][RAWW]
   unsigned long long* attw = raww + (size_t)m.Hkv * RAWW;           // [Hkv][GMAX][ATTW]
-  unsigned long long* ow = attw + (size_t)m.Hkv * GMAX * ATTW;      // [Hkv][D] O partial sums
-  unsigned long long* hw = ow + (size_t)m.Hkv * D;                  // [FF / 2] SwiGLU outputs
+  unsigned long long* mw = attw + (size_t)m.Hkv * GMAX * ATTW;      // [Hkv][GQ * HD / 2] merged heads
+  unsigned long long* x1w = mw + (size_t)m.Hq * HDIM / 2;           // [D / 2] x1 rows
+  unsigned long long* hw = x1w + D / 2;                             // [FF / 2] SwiGLU outputs
   if (tid < NT) {
     // the layer pointer table, read once; the unused second batch row of the B
     // fragments stays zero
@@ -1096,8 +1095,9 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
       }
     }
     STEP_MARK(layer, 8);
-    // ---- merge the group's splits (attn_combine_kernel's arithmetic) -> bf16 heads ----
-    {
+    // ---- the group's first CTA merges its splits (attn_combine_kernel's arithmetic) and
+    //      publishes the merged heads as bf16 words ----
+    if (P.gi == 0) {
       const unsigned long long* gws = attw + (size_t)h * GMAX * ATTW;
       bool mine = true;
       // (m, l) of every split and head into shared memory
@@ -1163,49 +1163,34 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
         }
       }
       if (!ok) break;
+      csync();  // the merged heads, one value per thread, go out two per word
+      for (int i = tid; i < GQ * HDIM / 2; i += NT)
+        ll_put(mw + (size_t)h * (GQ * HDIM / 2) + i, ((const uint32_t*)S.hb)[i], ep);
     }
-    csync();  // the merged heads in hb, one value per thread, are staged eight per thread
     STEP_MARK(layer, 9);
-    plain_stage<G>(S, S.hb, GQ * HDIM);
+    // ---- O row tiles over all heads: x1 = bf16(x + bf16(Wo @ attn)) ----
+    if (P.ont > 0) {
+      ok = all_ok(poll<4>(mw, m.Hq * HDIM / 2, ep, 32, sync, [&](int i, unsigned long long w) {
+        ((uint32_t*)S.hb)[i] = (uint32_t)w;
+      }));
+      if (!ok) break;
+      plain_stage<G>(S, S.hb, m.Hq * HDIM);
+    }
     STEP_MARK(layer, 10);
-    // ---- O (head h's column block): partial[h][row] = Wo[row, head h] @ attn[head h] ----
     ok = consume(layer, 11, [&](const uint8_t* wb) {
-      gemv_tiles<G, false>(wb, P.ont, GQ * HDIM, 0, 0, S, [&](int t, int r, double a, double) {
-        ll_put_d(ow + (size_t)h * D + (P.ot0 + t) * TR + r, a, tg);
+      gemv_tiles<G, false>(wb, P.ont, m.Hq * HDIM, 0, 0, S, [&](int t, int r, double a, double) {
+        S.outb[t * TR + r] = f2bf(bf2f(S.sx[(P.ot0 + t) * TR + r]) + rbf_d(a));
       });
     });
     if (!ok) break;
+    for (int i = tid; i < P.ont * TR / 2; i += NT) ll_put(x1w + P.ot0 * TR / 2 + i, ((const uint32_t*)S.outb)[i], ep);
     STEP_MARK(layer, 12);
-    // ---- x1 = bf16(x + bf16(sum over the KV-head groups, in order)); MLP RMSNorm ----
+    // ---- x1 rows from the O tiles; MLP RMSNorm ----
     load_ro(S.nw, Lw.norm2, D);
-    {
-      // thread tid sums rows tid + k * NT (k < 4: D <= 4 * NT) over the KV-head groups in
-      // order; all 4 * Hkv words are loaded and reloaded together
-      constexpr int RPT = 4, NU = RPT * HKVMAX;
-      unsigned long long v[NU];
-      uint32_t want = 0;
-      auto o_addr = [&](int u) { return ow + (size_t)(u % HKVMAX) * D + (u / HKVMAX) * NT + tid; };
-#pragma unroll
-      for (int u = 0; u < NU; ++u) {
-        v[u] = 0ull;
-        if ((u / HKVMAX) * NT + tid < D && (u % HKVMAX) < m.Hkv) {
-          v[u] = ll_ld(o_addr(u));
-          want |= 1u << u;
-        }
-      }
-      const bool mine = poll_rounds<NU>(o_addr, v, want, tg, 48, sync);
-      if (!(ok = all_ok(mine))) break;
-#pragma unroll
-      for (int k = 0; k < RPT; ++k) {
-        const int r = k * NT + tid;
-        if (r >= D) continue;
-        double acc = 0.0;
-#pragma unroll
-        for (int hh = 0; hh < HKVMAX; ++hh)
-          if (hh < m.Hkv) acc += ll_val_d(v[k * HKVMAX + hh]);
-        S.sx1[r] = f2bf(bf2f(S.sx[r]) + rbf_d(acc));
-      }
-    }
+    ok = all_ok(poll<2>(x1w, D / 2, ep, 32, sync, [&](int i, unsigned long long w) {
+      ((uint32_t*)S.sx1)[i] = (uint32_t)w;
+    }));
+    if (!ok) break;
     STEP_MARK(layer, 13);
     norm_stage<G>(S, S.sx1, D, m.eps, 0, nullptr);
     STEP_MARK(layer, 14);
@@ -1437,7 +1422,7 @@ static size_t max_chunk(const iron_qwen3_model* m, int N, int lm_rows) {
     Plan P;
     plan_tiles(*m, c, N, P);
     mx = std::max(mx, (size_t)P.qnt * tileb(D, G));
-    mx = std::max(mx, (size_t)P.ont * tileb(GQ * HDIM, G));
+    mx = std::max(mx, (size_t)P.ont * tileb(m->Hq * HDIM, G));
     mx = std::max(mx, (size_t)P.gnt * tileb(D, G));
     mx = std::max(mx, (size_t)P.dns * tileb(m->FF / DSL, G));
   }
@@ -1458,7 +1443,6 @@ static int validate(const iron_qwen3_model* m, int grid) {
   IRON_REQUIRE(m != nullptr, IRON_ERR_ARG, "qwen3 step: null model");
   IRON_REQUIRE(m->HD == HDIM, IRON_ERR_UNSUPPORTED, "qwen3 step: head_dim %d (supported: 128)", m->HD);
   IRON_REQUIRE(m->Hkv >= 1 && m->Hq % m->Hkv == 0, IRON_ERR_ARG, "qwen3 step: Hq=%d, Hkv=%d", m->Hq, m->Hkv);
-  IRON_REQUIRE(m->Hkv <= HKVMAX, IRON_ERR_UNSUPPORTED, "qwen3 step: %d KV heads (at most %d)", m->Hkv, HKVMAX);
   const int GQ = m->Hq / m->Hkv;
   IRON_REQUIRE(GQ == 1 || GQ == 2 || GQ == 4, IRON_ERR_UNSUPPORTED, "qwen3 step: GQA group %d", GQ);
   IRON_REQUIRE(m->group == 32 || m->group == 64 || m->group == 128, IRON_ERR_ARG, "qwen3 step: group %d",
@@ -1507,7 +1491,8 @@ extern "C" int64_t iron_qwen3_attn_ws_bytes(const iron_qwen3_model* m) {
   if (!m || m->Hkv < 1 || m->Hq % m->Hkv != 0) return 0;
   const int GQ = m->Hq / m->Hkv;
   const int64_t words = (int64_t)DSL * m->D + (int64_t)m->Hkv * (GQ + 2) * HDIM / 2 +
-                        (int64_t)m->Hkv * GMAX * GQ * (HDIM + 2) + (int64_t)m->Hkv * m->D + m->FF / 2;
+                        (int64_t)m->Hkv * GMAX * GQ * (HDIM + 2) + (int64_t)m->Hq * HDIM / 2 + m->D / 2 +
+                        m->FF / 2;
   return words * 8;
 }
 
@@ -1550,8 +1535,8 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   p.m = *m;
   p.embed_input = embed_input;
   p.advance = advance;
-  p.kmax = std::max(std::max(m->D, GQ * HDIM), m->FF);
-  p.hbn = std::max(m->FF, (GQ + 2) * HDIM);
+  p.kmax = std::max(std::max(m->D, m->Hq * HDIM), m->FF);
+  p.hbn = std::max(std::max(m->FF, m->Hq * HDIM), (GQ + 2) * HDIM);
   const size_t fixed = fixed_smem(p.kmax, p.hbn, m->D, m->group, GQ, m->n_layers);
   IRON_REQUIRE(fixed + 64 * 1024 <= (size_t)SMEM_MAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: %zu bytes of fixed shared memory leave no room for the weight ring", fixed);

@@ -247,7 +247,6 @@ class Qwen3B200:
         c, w = self.cfg, self.w
         L = _lib.lib()
         G = w.group
-        GQ = c.Hq // c.Hkv
         st = torch.cuda.current_stream(dev).cuda_stream
         # the step kernel's weight tiles (made once; the plain wires stay for the other paths)
         perm = self._qkv_group_rows().to(dev)
@@ -260,11 +259,7 @@ class Qwen3B200:
                 setattr(layers[i], n, ptr(Lw[n]))
             qkv_rows = Lw["wqkv"].view(c.QKV, -1).index_select(0, perm).contiguous()
             wqkv_t = self._pack_tiles(qkv_rows, c.QKV, c.D, 0, c.D, dev, st)
-            per_head = L.iron_qwen3_tiles_bytes(c.D, GQ * c.HD, G)
-            wo_t = torch.empty(c.Hkv * per_head, dtype=torch.uint8, device=dev)
-            for h in range(c.Hkv):
-                self._pack_tiles(Lw["wo"], c.D, c.QD, h * GQ * c.HD, GQ * c.HD, dev, st,
-                                 out=wo_t[h * per_head:(h + 1) * per_head])
+            wo_t = self._pack_tiles(Lw["wo"], c.D, c.QD, 0, c.QD, dev, st)
             # gate/up: tile t = gate rows 8t..8t+7 over up rows 8t..8t+7
             gu_rows = torch.stack([Lw["wg"].view(c.FF // 8, 8, -1), Lw["wu"].view(c.FF // 8, 8, -1)], 1)
             gu_rows = gu_rows.reshape(2 * c.FF, -1).contiguous()

@@ -147,16 +147,18 @@ __device__ __forceinline__ double rms_sq(float v, int mode) {
 __device__ __forceinline__ RmsCoef rms_coef(double sum_sq, int n, float eps, int mode) {
   RmsCoef c;
   c.mode = mode;
+  // the mean: a multiply when n is a power of two (1/n exact, the same value as the divide)
+  const double mean_sq = (n & (n - 1)) == 0 ? sum_sq * (1.0 / (double)n) : sum_sq / (double)n;
   if (mode == 0) {
-    c.inv = 1.0 / sqrt(sum_sq / (double)n + (double)eps);
+    c.inv = 1.0 / sqrt(mean_sq + (double)eps);
     c.rms = 0.f;
   } else if (mode == 1) {
-    const float mean = rbf((float)(sum_sq / (double)n));
+    const float mean = rbf((float)mean_sq);
     const float ms = rbf(mean + eps);
     c.rms = rbf(sqrtf(ms));
     c.inv = 0.0;
   } else {  // mode 2: c.rms holds r = bf16(rsqrt(bf16(mean + eps)))
-    const float mean = rbf((float)(sum_sq / (double)n));
+    const float mean = rbf((float)mean_sq);
     const float ms = rbf(mean + eps);
     c.rms = rbf((float)(1.0 / sqrt((double)ms)));
     c.inv = 0.0;

@@ -613,6 +613,77 @@ __device__ __forceinline__ void plain_stage(const Smem& S, const uint16_t* x, in
       k_ofs);
 }
 
+// Digits of the four consecutive values v at position k (k % 4 == 0) into the B
+// fragments: G / 4 consecutive lanes hold a quantisation group and take its block
+// scale together.  Every lane of the warp calls (own = false: no values).
+template <int G>
+__device__ __forceinline__ void stage_quad(const Smem& S, int k, const float (&v)[4], bool own) {
+  constexpr int TEAM = G / 4;
+  float mx = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) mx = fmaxf(mx, own ? fabsf(v[e]) : 0.f);
+#pragma unroll
+  for (int o = 1; o < TEAM; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(~0u, mx, o));
+  if (!own) return;
+  float sc, inv;
+  bfp_scale(mx, sc, inv);
+  uint32_t Y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) Y[e] = (uint32_t)(__float2int_rn(v[e] * sc * 32768.0f) + 0x808080) ^ 0x808080u;
+  const uint32_t t0 = __byte_perm(Y[0], Y[1], 0x5140), t1 = __byte_perm(Y[0], Y[1], 0x7362);
+  const uint32_t t2 = __byte_perm(Y[2], Y[3], 0x5140), t3 = __byte_perm(Y[2], Y[3], 0x7362);
+  const uint32_t wd[4] = {__byte_perm(t0, t2, 0x5410), __byte_perm(t0, t2, 0x7632), __byte_perm(t1, t3, 0x5410),
+                          __byte_perm(t1, t3, 0x7632)};
+  uint8_t* blk = S.xb + (size_t)(k >> 5) * XBS;
+  const int kk = k & 31;
+#pragma unroll
+  for (int d = 0; d < 4; ++d) *(uint32_t*)(blk + ((d * 4 + ((kk & 15) >> 2)) * 8 + (kk >> 4) * 4)) = wd[d];
+  if (k % G == 0) S.xse[k / G] = inv == 0.f ? 0 : (int)((__float_as_uint(inv) >> 23) & 0xffu) - 127 - 15;
+}
+
+// RMSNorm (mode 0 kernel form, 1 golden form) of D values held four per thread (thread
+// t: values 4t..4t+3 in vx; threads with 4t >= D hold none) with the weights nw (shared)
+// -> bf16 -> staged digits; outf (shared) gets the normalised values.  One block
+// reduction: every thread adds the warps' partial sums in warp order.
+template <int G>
+__device__ __forceinline__ void norm_stage_q(const Smem& S, const float (&vx)[4], int D, float eps, int mode,
+                                             float* outf) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, k = 4 * threadIdx.x;
+  const bool own = k < D;
+  double ss = 0.0;
+  if (own) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += rms_sq(vx[e], mode);
+  }
+  ss = warp_sum_d(ss);
+  if (lane == 0) S.red[wid] = ss;
+  csync();
+  double tot = 0.0;
+#pragma unroll
+  for (int w = 0; w < NWARP; ++w) tot += S.red[w];
+  const RmsCoef rc = rms_coef(tot, D, eps, mode);
+  float v[4];
+  if (own) {
+    const uint2 wa = *(const uint2*)(S.nw + k);
+    const uint32_t ww[2] = {wa.x, wa.y};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[e] = rbf(rms_apply(vx[e], bf2f((uint16_t)(ww[e >> 1] >> (16 * (e & 1)))), rc));
+      if (outf) outf[k + e] = v[e];
+    }
+  }
+  stage_quad<G>(S, k, v, own);
+  csync();
+}
+
+// the four bf16 values of the two words w0 (values 0, 1) and w1 (2, 3)
+__device__ __forceinline__ void quad_of(uint32_t w0, uint32_t w1, float (&v)[4]) {
+  v[0] = bf_lo(w0);
+  v[1] = bf_hi(w0);
+  v[2] = bf_lo(w1);
+  v[3] = bf_hi(w1);
+}
+
 // K bf16 values (K % 8 == 0, read-only data) into shared memory with 16-byte loads
 __device__ __forceinline__ void load_ro(uint16_t* dst, const uint16_t* src, int K) {
   for (int i = threadIdx.x; i < (K >> 3); i += NT) ((uint4*)dst)[i] = __ldg(((const uint4*)src) + i);
@@ -859,8 +930,12 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     if (tid == NT) producer(p, P, S, sync);
     return;
   }
-  // layer-0 input: the token's embedding row, or the hidden state given in x
-  load_ro(S.sx, p.embed_input ? m.embed + (size_t)m.tok[0] * D : m.x, D);
+  // layer-0 input: the token's embedding row, or the hidden state given in x (thread t
+  // loads values 4t..4t+3, the ones it normalises)
+  {
+    const uint16_t* src = p.embed_input ? m.embed + (size_t)m.tok[0] * D : m.x;
+    if (4 * tid < D) *(uint2*)(S.sx + 4 * tid) = __ldg((const uint2*)(src + 4 * tid));
+  }
 
   bool ok = true;
   volatile RingState& vrs = *S.rs;
@@ -887,37 +962,33 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
   // a bounded poll by every compute thread, then a CTA-wide verdict
   auto all_ok = [&](bool mine) -> bool { return !cvote_any(!mine); };
 
-  // x = bf16(x1 + bf16(sum of the DSL down slices, in slice order)) for rows
-  // tid + k * NT (k < 4: D <= 4 * NT), from the words of the layer tagged tg; all 4 * DSL
-  // words of a thread are loaded and reloaded together
-  auto next_x = [&](uint32_t tg) -> bool {
-    constexpr int RPT = 4, NU = RPT * DSL;
+  // x = bf16(x1 + bf16(sum of the DSL down slices, in slice order)) for rows 4t..4t+3
+  // of thread t (D <= 4 * NT), from the words of the layer tagged tg; all 4 * DSL words
+  // of a thread are loaded and reloaded together.  The values go to xv and to sx.
+  auto next_x = [&](uint32_t tg, float (&xv)[4]) -> bool {
+    constexpr int NU = 4 * DSL;
     unsigned long long v[NU];
-    uint32_t want = 0;
+    const bool own = 4 * tid < D;
     auto d_addr = [&](int u) {
-      const int r = (u / DSL) * NT + tid;
+      const int r = 4 * tid + u / DSL;
       return dpw + ((size_t)(r >> 4) * DSL + (u % DSL)) * TR + (r & 15);
     };
 #pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      v[u] = 0ull;
-      if ((u / DSL) * NT + tid < D) {
-        v[u] = ll_ld(d_addr(u));
-        want |= 1u << u;
-      }
-    }
-    const bool mine = poll_rounds<NU>(d_addr, v, want, tg, 48, sync);
+    for (int u = 0; u < NU; ++u) v[u] = own ? ll_ld(d_addr(u)) : 0ull;
+    const bool mine = poll_rounds<NU>(d_addr, v, own ? 0xffffu : 0u, tg, 48, sync);
     if (!all_ok(mine)) return false;
+    if (own) {
+      uint16_t o[4];
 #pragma unroll
-    for (int k = 0; k < RPT; ++k) {
-      const int r = k * NT + tid;
-      if (r >= D) continue;
-      double acc = 0.0;
+      for (int e = 0; e < 4; ++e) {
+        double acc = 0.0;
 #pragma unroll
-      for (int j = 0; j < DSL; ++j) acc += ll_val_d(v[k * DSL + j]);
-      S.sx[r] = f2bf(bf2f(S.sx1[r]) + rbf_d(acc));
+        for (int j = 0; j < DSL; ++j) acc += ll_val_d(v[e * DSL + j]);
+        o[e] = f2bf(bf2f(S.sx1[4 * tid + e]) + rbf_d(acc));
+        xv[e] = bf2f(o[e]);
+      }
+      *(uint2*)(S.sx + 4 * tid) = make_uint2(o[0] | ((uint32_t)o[1] << 16), o[2] | ((uint32_t)o[3] << 16));
     }
-    csync();  // sx is read across threads
     return true;
   };
 
@@ -930,16 +1001,20 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 0);
     // ---- x: the previous layer's output rows ----
     load_ro(S.nw, Lw.norm1, D);
+    float xv[4];
     if (layer > 0) {  // the previous layer's down slices, with its epoch
-      if (!(ok = next_x(tag16_of(ep - 1u)))) break;
-    } else {
-      csync();  // the embedding row (or x) in sx, written across threads
+      if (!(ok = next_x(tag16_of(ep - 1u), xv))) break;
+    } else {  // the embedding row (or x) as this thread loaded it into sx
+      if (4 * tid < D) {
+        const uint2 w2 = *(const uint2*)(S.sx + 4 * tid);
+        quad_of(w2.x, w2.y, xv);
+      }
     }
-    if (m.trace && blockIdx.x == 0)
-      for (int i = tid; i < D; i += NT) m.trace[(size_t)layer * D + i] = S.sx[i];
     STEP_MARK(layer, 1);
     // ---- QKV rows of group h: raw = bf16(Wqkv @ RMSNorm_golden(x, norm1)) ----
-    norm_stage<G>(S, S.sx, D, m.eps, 1, nullptr);
+    norm_stage_q<G>(S, xv, D, m.eps, 1, nullptr);  // its barriers also publish sx and nw
+    if (m.trace && blockIdx.x == 0)
+      for (int i = tid; i < D; i += NT) m.trace[(size_t)layer * D + i] = S.sx[i];
     STEP_MARK(layer, 2);
     ok = consume(layer, 3, [&](const uint8_t* wb) {
       gemv_tiles<G, false>(wb, P.qnt, D, 0, 0, S, [&](int t, int r, double a, double) {
@@ -1169,12 +1244,19 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     }
     STEP_MARK(layer, 9);
     // ---- O row tiles over all heads: x1 = bf16(x + bf16(Wo @ attn)) ----
-    if (P.ont > 0) {
-      ok = all_ok(poll<4>(mw, m.Hq * HDIM / 2, ep, 32, sync, [&](int i, unsigned long long w) {
-        ((uint32_t*)S.hb)[i] = (uint32_t)w;
-      }));
-      if (!ok) break;
-      plain_stage<G>(S, S.hb, m.Hq * HDIM);
+    if (P.ont > 0) {  // quad q = tid + j * NT: words 2q, 2q + 1 -> staged values 4q..4q+3
+      const int nq = m.Hq * HDIM / 4;
+      bool mine = true;
+      for (int q0 = 0; q0 < nq; q0 += NT) {
+        const int q = q0 + tid;
+        const bool own = q < nq;
+        unsigned long long v[2] = {own ? ll_ld(mw + 2 * q) : 0ull, own ? ll_ld(mw + 2 * q + 1) : 0ull};
+        mine = mine && poll_rounds<2>([&](int u) { return mw + 2 * q + u; }, v, own ? 3u : 0u, ep, 32, sync);
+        float hv[4];
+        quad_of((uint32_t)v[0], (uint32_t)v[1], hv);
+        stage_quad<G>(S, 4 * q, hv, own);
+      }
+      if (!(ok = all_ok(mine))) break;  // also publishes the staged digits
     }
     STEP_MARK(layer, 10);
     ok = consume(layer, 11, [&](const uint8_t* wb) {
@@ -1187,12 +1269,16 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     STEP_MARK(layer, 12);
     // ---- x1 rows from the O tiles; MLP RMSNorm ----
     load_ro(S.nw, Lw.norm2, D);
-    ok = all_ok(poll<2>(x1w, D / 2, ep, 32, sync, [&](int i, unsigned long long w) {
-      ((uint32_t*)S.sx1)[i] = (uint32_t)w;
-    }));
-    if (!ok) break;
+    {  // thread t: x1 rows 4t..4t+3 (words 2t, 2t + 1)
+      const bool own = 4 * tid < D;
+      unsigned long long v[2] = {own ? ll_ld(x1w + 2 * tid) : 0ull, own ? ll_ld(x1w + 2 * tid + 1) : 0ull};
+      if (!(ok = all_ok(poll_rounds<2>([&](int u) { return x1w + 2 * tid + u; }, v, own ? 3u : 0u, ep, 32, sync))))
+        break;
+      quad_of((uint32_t)v[0], (uint32_t)v[1], xv);
+      if (own) *(uint2*)(S.sx1 + 4 * tid) = make_uint2((uint32_t)v[0], (uint32_t)v[1]);
+    }
     STEP_MARK(layer, 13);
-    norm_stage<G>(S, S.sx1, D, m.eps, 0, nullptr);
+    norm_stage_q<G>(S, xv, D, m.eps, 0, nullptr);
     STEP_MARK(layer, 14);
     // ---- gate/up: gh = bf16(silu_tanh(bf16(Wg@hf)) * bf16(Wu@hf)) for the CTA's tiles ----
     ok = consume(layer, 15, [&](const uint8_t* wb) {
@@ -1206,16 +1292,23 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     // ---- down: this CTA's slices, partial[t][j][r] = Wd[tile t rows, K slice j] @ gh[slice j] ----
     {
       const int KS = FF / DSL;  // columns of a slice
+      // the gh values of the CTA's slices, staged side by side: staged quad i (value 4i)
+      // is quad i % (KS / 4) of slice i / (KS / 4)
+      const int nq = P.dns * (KS / 4);
       bool mine = true;
-      for (int q = 0; q < P.dns; ++q) {  // the gh values of each slice, staged at blocks q * KS / 32 ..
-        const int j = (P.ds0 + q) % DSL;
-        mine = mine && poll<3>(hw + (size_t)j * KS / 2, KS / 2, ep, 32, sync, [&](int i, unsigned long long w) {
-                 ((uint32_t*)(S.hb + q * KS))[i] = (uint32_t)w;
-               });
+      for (int q0 = 0; q0 < nq; q0 += NT) {
+        const int q = q0 + tid;
+        const bool own = q < nq;
+        const int sl = own ? q / (KS / 4) : 0, qi = q - sl * (KS / 4);
+        const unsigned long long* wp = hw + (size_t)((P.ds0 + sl) % DSL) * (KS / 2) + 2 * qi;
+        unsigned long long v[2] = {own ? ll_ld(wp) : 0ull, own ? ll_ld(wp + 1) : 0ull};
+        mine = mine && poll_rounds<2>([&](int u) { return wp + u; }, v, own ? 3u : 0u, ep, 32, sync);
+        float hv[4];
+        quad_of((uint32_t)v[0], (uint32_t)v[1], hv);
+        stage_quad<G>(S, 4 * q, hv, own);
       }
-      if (!(ok = all_ok(mine))) break;
+      if (!(ok = all_ok(mine))) break;  // also publishes the staged digits
       STEP_MARK(layer, 17);
-      for (int q = 0; q < P.dns; ++q) plain_stage<G>(S, S.hb + q * KS, KS, q * KS);
       STEP_MARK(layer, 18);
       ok = consume(layer, 19, [&](const uint8_t* wb) {
         gemv_tiles<G, false>(wb, P.dns, KS, 0, KS / 32, S, [&](int q, int r, double a, double) {
@@ -1232,7 +1325,9 @@ __global__ void __launch_bounds__(NT + 32, 1) qwen3_step_kernel(const __grid_con
     // ---- final: x = the last layer's output, RMSNorm (golden) + lm_head + greedy argmax ----
     const uint32_t ep = tok_epoch * (uint32_t)NL + (uint32_t)NL;
     load_ro(S.nw, m.final_norm, D);
-    ok = next_x(tag16_of(ep));
+    float xv[4];
+    ok = next_x(tag16_of(ep), xv);
+    csync();  // sx, written four values per thread, is read across threads below
   }
   if (ok) {
     if (blockIdx.x == 0) {

@@ -54,7 +54,6 @@ constexpr int NMB = 16;           // ring slots (chunks in flight at most)
 constexpr int GMAX = 24;          // most CTAs in one KV-head group (attention splits)
 constexpr int KVP = 64;           // cached positions per K/V chunk (32 KB)
 constexpr int NTMAX = 16;         // most tiles of one projection in one CTA
-constexpr int PSEG = 3;           // most tiles a warp's share of a projection meets
 constexpr int LMT = 4;            // int8 lm_head tiles per chunk
 constexpr int DSL = 4;            // K slices of a down-projection tile
 constexpr int XBS = 288;          // bytes of one 32-column block of B fragments (padded)
@@ -333,7 +332,7 @@ struct Smem {
   uint8_t* ring;
   uint8_t* xb;     // [kmax / 32][XBS] B fragments of the staged activation
   int* xse;        // [kmax / G] activation group scale exponents: scale 2^xse (the 2^-15 included)
-  double* part;    // [NWARP][PSEG][TR] the warps' partial sums of a projection
+  double* part;    // [NTMAX][TR] slice sums of a projection
   uint16_t* sx;    // [D] residual x (bf16 bits)
   uint16_t* sx1;   // [D] residual x1
   uint16_t* nw;    // [D] weights of the next RMSNorm
@@ -356,7 +355,7 @@ __host__ __device__ inline size_t att_floats(int GQ) {
 // bytes of everything but the ring (carve's layout: 16 arrays, each rounded up to 16 bytes)
 __host__ __device__ inline size_t fixed_smem(int kmax, int hbn, int D, int G, int GQ, int n_layers) {
   size_t o = 32 * 8 + NMB * 8 + sizeof(RingState) + 8 * 4;
-  o += (size_t)(kmax / 32) * XBS + (size_t)(kmax / G) * 4 + NWARP * PSEG * TR * 8;
+  o += (size_t)(kmax / 32) * XBS + (size_t)(kmax / G) * 4 + NTMAX * TR * 8;
   o += (size_t)D * 2 * 3 + (size_t)hbn * 2 + NTMAX * TR * 2;
   o += att_floats(GQ) * 4 + (size_t)GMAX * GQ * 2 * 4 + (size_t)D * 4;
   o += (size_t)n_layers * sizeof(iron_qwen3_layer);
@@ -379,7 +378,7 @@ __device__ Smem carve(uint8_t* base, const Kp& p, int GQ) {
   s.flag = (int*)take(8 * 4);
   s.xb = take((size_t)(p.kmax / 32) * XBS);
   s.xse = (int*)take((size_t)(p.kmax / m.group) * 4);
-  s.part = (double*)take(NWARP * PSEG * TR * 8);
+  s.part = (double*)take(NTMAX * TR * 8);
   s.sx = (uint16_t*)take((size_t)m.D * 2);
   s.sx1 = (uint16_t*)take((size_t)m.D * 2);
   s.nw = (uint16_t*)take((size_t)m.D * 2);
@@ -714,12 +713,11 @@ __device__ __forceinline__ void gemv_tiles(const uint8_t* slot, int nt, int K, i
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int KB = K >> 5;
   const size_t TB = tileb(K, G);
-  // the nt * KB (tile, block) units in order, an even share per warp; a warp's share
-  // covers at most PSEG tiles, whose partial sums it keeps apart
-  const int units = nt * KB;
-  const int u0 = wid * units / NWARP, u1 = (wid + 1) * units / NWARP;
-  for (int t = u0 / KB; u1 > u0 && t <= (u1 - 1) / KB; ++t) {
-    const int kb0 = max(u0, t * KB) - t * KB, kb1 = min(u1, (t + 1) * KB) - t * KB;
+  const int lsl = nt >= NWARP ? 0 : (nt >= 4 ? 1 : (nt >= 2 ? 2 : 3));  // log2 of the slices per tile
+  const int SL = 1 << lsl, items = nt << lsl;
+  for (int it = wid; it < items; it += NWARP) {
+    const int t = it >> lsl, s = it & (SL - 1);
+    const int kb0 = (s * KB) >> lsl, kb1 = ((s + 1) * KB) >> lsl;
     const uint8_t* tb = slot + (size_t)t * TB;
     const uint8_t* scb = tb + (size_t)KB * 512 + (lane >> 2) * 4;
     const int xk = xkb0 + t * xkbs;  // this tile's first staged block
@@ -760,25 +758,28 @@ __device__ __forceinline__ void gemv_tiles(const uint8_t* slot, int nt, int K, i
     a0 += __shfl_xor_sync(~0u, a0, 1);
     a1 += __shfl_xor_sync(~0u, a1, 1);
     if ((lane & 3) == 0) {
-      double* pp = S.part + ((size_t)wid * PSEG + (t - u0 / KB)) * TR;
-      pp[lane >> 2] = a0;
-      pp[(lane >> 2) + 8] = a1;
+      S.part[(size_t)it * TR + (lane >> 2)] = a0;
+      S.part[(size_t)it * TR + (lane >> 2) + 8] = a1;
     }
   }
   csync();
-  // tile t's sum: the partials of the warps whose share meets it, in warp order
-  auto tile_sum = [&](int t, int r) {
-    double a = 0.0;
-    for (int w = 0; w < NWARP; ++w) {
-      const int v0 = w * units / NWARP, v1 = (w + 1) * units / NWARP;
-      if (v1 > v0 && v0 < (t + 1) * KB && v1 > t * KB) a += S.part[((size_t)w * PSEG + (t - v0 / KB)) * TR + r];
-    }
-    return a;
-  };
   if (PAIR) {
-    for (int e = threadIdx.x; e < nt * 8; e += NT) epi(e >> 3, e & 7, tile_sum(e >> 3, e & 7), tile_sum(e >> 3, (e & 7) + 8));
+    for (int e = threadIdx.x; e < nt * 8; e += NT) {
+      const int t = e >> 3, i = e & 7;
+      double g = 0.0, u = 0.0;
+      for (int s = 0; s < SL; ++s) {
+        g += S.part[(size_t)((t << lsl) + s) * TR + i];
+        u += S.part[(size_t)((t << lsl) + s) * TR + i + 8];
+      }
+      epi(t, i, g, u);
+    }
   } else {
-    for (int e = threadIdx.x; e < nt * TR; e += NT) epi(e >> 4, e & 15, tile_sum(e >> 4, e & 15), 0.0);
+    for (int e = threadIdx.x; e < nt * TR; e += NT) {
+      const int t = e >> 4, r = e & 15;
+      double a = 0.0;
+      for (int s = 0; s < SL; ++s) a += S.part[(size_t)((t << lsl) + s) * TR + r];
+      epi(t, r, a, 0.0);
+    }
   }
 }
 
@@ -1510,7 +1511,7 @@ static int grid_for(const iron_qwen3_model* m) {
 
 // host mirror of the per-CTA weight chunks: the largest of any CTA
 static size_t max_chunk(const iron_qwen3_model* m, int N, int lm_rows) {
-  const int G = m->group, D = m->D;
+  const int G = m->group, GQ = m->Hq / m->Hkv, D = m->D;
   size_t mx = std::max((size_t)KVP * 4 * HDIM, m->lm_w8 ? (size_t)LMT * tileb(D, G) : (size_t)lm_rows * D * 2);
   for (int c = 0; c < N; ++c) {
     Plan P;
@@ -1551,10 +1552,6 @@ static int validate(const iron_qwen3_model* m, int grid) {
                "qwen3 step: %d CTAs cannot form %d KV-head groups of at most %d", grid, m->Hkv, GMAX);
   IRON_REQUIRE(max_tiles(m, grid) <= NTMAX, IRON_ERR_UNSUPPORTED,
                "qwen3 step: more than %d row tiles of one projection per CTA", NTMAX);
-  // a warp's even share of one projection (nt tiles of KB blocks) meets at most PSEG tiles:
-  // it holds at most ceil(nt * KB / NWARP) blocks, so nt <= NWARP * (PSEG - 1) suffices
-  IRON_REQUIRE(max_tiles(m, grid) <= NWARP * (PSEG - 1), IRON_ERR_UNSUPPORTED,
-               "qwen3 step: more than %d row tiles of one projection per CTA", NWARP * (PSEG - 1));
   for (int c = 0; c < grid; ++c) {  // the down slices of a CTA are staged side by side
     Plan P;
     plan_tiles(*m, c, grid, P);

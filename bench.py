@@ -65,6 +65,15 @@ def parse():
                          "lengths U[256, 8192], replicas across GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
+    ap.add_argument("--phases", action="store_true",
+                    help="phase breakdown of the one-launch step (a profiling copy of the library), not a bench line")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="per-kernel device time of --steps decode steps at --batch (CUPTI), not a bench line")
+    ap.add_argument("--sweep", action="store_true", help="operator sweep of configuration 3, not a bench line")
+    ap.add_argument("--sweep-reps", type=int, default=50)
+    ap.add_argument("--sweep-json", type=str, default=None)
+    ap.add_argument("--sweep-capture", nargs="?", const="", default=None,
+                    help="with --sweep: only the small ncu capture case of the GEMV (optional NxKxB,... shapes)")
     args = ap.parse_args()
     if args.model == "qwen3-8b" and args.prompt == PROMPT:
         args.prompt = 4096
@@ -611,6 +620,282 @@ def run_llama(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+
+# ---------------------------------------------------------------------------
+# measurement modes behind the numbers in profiles/ (not the bench line)
+# ---------------------------------------------------------------------------
+SWEEP_GEMV_SHAPES = [(6144, 1024), (3072, 1024), (1024, 3072), (12288, 4096), (4096, 12288)]
+SWEEP_GEMV_BATCH = [1, 8, 32]
+SWEEP_ATTN_BATCH = [1, 8, 32, 64]
+SWEEP_ATTN_LEN = [512, 4096, 32768]
+L2_BYTES = 126 * 1024 * 1024
+SWEEP_CAPTURE_CASES = [(6144, 1024, 8), (1024, 3072, 8), (6144, 1024, 1)]
+
+
+def _sweep_copies(nbytes: int, cap: int) -> int:
+    """Operand copies whose total exceeds twice the L2."""
+    return max(2, min(cap, -(-2 * L2_BYTES // nbytes)))
+
+
+def _sweep_timed(fns, reps: int) -> float:
+    """Mean milliseconds per launch of ``fns`` (one per operand copy) run back to back."""
+    import torch
+    for f in fns:
+        f()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(reps, len(fns))
+    # hold the stream for ~10 ms so every launch below is queued before the first event
+    # fires: the host's per-launch cost stays outside the measured interval
+    torch.cuda._sleep(20_000_000)
+    e0.record(st)
+    for i in range(n):
+        fns[i % len(fns)]()
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def run_sweep(args):
+    """Operator sweep (configuration 3): achieved HBM bandwidth of the int8 group-32 GEMV
+    ``iron_gemv_w8a16`` at (N, K) x batch {1, 8, 32} and of decode attention
+    ``iron_decode_attn`` (32 query / 8 KV heads, head_dim 128) at batch {1, 8, 32, 64} x
+    KV length {512, 4096, 32768}, values N(0, 1).  Launches run back to back over enough
+    operand copies to exceed twice the L2 (each reads a copy the previous ones evicted);
+    a first row times an 8-element add the same way: the per-launch floor of the method.
+    GB/s = algorithmic bytes / time per launch (GEMV N*K + N*(K/G)*2 + B*K*2 + B*N*2,
+    attention B*2*Hkv*HD*L*2 + B*Hq*HD*4).  ``--sweep-capture [NxKxB,...]`` instead runs
+    the small case of an ncu capture of the GEMV: ~300 MB of weight copies each run once,
+    then one launch per case on a copy that has left the L2."""
+    import torch
+    from iron_b200 import _lib
+    from iron_b200.qwen3 import quantize_to_wire
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    G = GROUP
+    if args.sweep_capture is not None:
+        shapes = [tuple(int(v) for v in c.split("x")) for c in args.sweep_capture.split(",") if c] or SWEEP_CAPTURE_CASES
+        st = torch.cuda.current_stream().cuda_stream
+        cases, warm = [], 0
+        for N, K, B in shapes:
+            w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)
+            ws = [w0] + [w0.clone() for _ in range(max(1, 300 * 2**20 // (N * K)) - 1)]
+            x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty(B, N, dtype=torch.bfloat16, device=dev)
+            cases.append((N, K, B, ws, x, y))
+
+        def run(N, K, B, w, x, y):
+            _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B, None, y.data_ptr(), st)
+
+        for N, K, B, ws, x, y in cases:
+            for w in ws[1:]:
+                run(N, K, B, w, x, y)
+                warm += 1
+        torch.cuda.synchronize()
+        for N, K, B, ws, x, y in cases:
+            run(N, K, B, ws[0], x, y)
+        torch.cuda.synchronize()
+        print(f"warm-up launches: {warm}; then one launch each of {shapes}")
+        return
+    peaks = ROOT / "MEASURED_PEAKS.json"
+    peak = json.loads(peaks.read_text())["hbm_gbs"] if peaks.exists() else 6650.0
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    reps = args.sweep_reps
+    rows = []
+    a = torch.zeros(8, dtype=torch.bfloat16, device=dev)
+    s_ = st()
+    ms = _sweep_timed([lambda: _lib.call("iron_add", a.data_ptr(), a.data_ptr(), a.data_ptr(), 8, s_)], reps)
+    rows.append({"kernel": "launch_floor", "us": ms * 1e3})
+    print(json.dumps(rows[-1]), flush=True)
+    for N, K in SWEEP_GEMV_SHAPES:
+        wbytes = N * K + N * (K // G) * 2
+        w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)
+        ws = [w0] + [w0.clone() for _ in range(_sweep_copies(wbytes, 64) - 1)]
+        for B in SWEEP_GEMV_BATCH:
+            x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty(B, N, dtype=torch.bfloat16, device=dev)
+            s_ = st()
+            fns = [(lambda w=w: _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B,
+                                          None, y.data_ptr(), s_)) for w in ws]
+            ms = _sweep_timed(fns, reps)
+            nbytes = wbytes + B * K * 2 + B * N * 2
+            rows.append({"kernel": "gemv_w8a16", "N": N, "K": K, "batch": B, "us": ms * 1e3,
+                         "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / peak, "bytes": nbytes,
+                         "copies": len(ws)})
+            print(json.dumps(rows[-1]), flush=True)
+        del ws, w0
+    H, KV, HD = 32, 8, 128
+    for B in SWEEP_ATTN_BATCH:
+        for L in SWEEP_ATTN_LEN:
+            kvbytes = B * 2 * KV * HD * L * 2
+            q = torch.randn(B, H, HD, generator=g, device=dev).to(torch.bfloat16)
+            kvs = [torch.randn(B, KV, 2 * L * HD, generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(_sweep_copies(kvbytes, 16))]
+            out = torch.empty(B, H, HD, dtype=torch.bfloat16, device=dev)
+            nws = _lib.lib().iron_decode_attn_workspace_bytes(B, H, HD, L)
+            wsp = torch.empty(nws, dtype=torch.uint8, device=dev)
+            s_ = st()
+            fns = [(lambda kv=kv: _lib.call("iron_decode_attn", q.data_ptr(), kv.data_ptr(), out.data_ptr(), B, H, KV,
+                                            HD, L, 0, 0, L, None, wsp.data_ptr(), nws, s_)) for kv in kvs]
+            ms = _sweep_timed(fns, reps)
+            nbytes = kvbytes + B * H * HD * 4
+            rows.append({"kernel": "decode_attn", "batch": B, "kv_len": L, "us": ms * 1e3,
+                         "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / peak, "bytes": nbytes,
+                         "copies": len(kvs)})
+            print(json.dumps(rows[-1]), flush=True)
+            del kvs, wsp
+    if args.sweep_json:
+        Path(args.sweep_json).write_text("\n".join(json.dumps(r) for r in rows) + "\n")
+
+
+def run_breakdown(args):
+    """Per-kernel device time of decode steps from a CUPTI trace (torch.profiler):
+    ``--batch`` random prompts of ``--prompt`` tokens prefilled into a synthetic
+    Qwen3-0.6B (int8 g32), then ``--steps`` traced decode steps; per kernel name the
+    device time per step, its share and the launches per step."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from iron_b200.qwen3 import Qwen3B200, Qwen3Config, Qwen3Weights
+    B, P = args.batch, args.prompt
+    dev = torch.device("cuda")
+    cfg = Qwen3Config.qwen3_0_6b()
+    w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
+    dec = Qwen3B200(w, max_seq=P + args.steps + 16, batch=B, device=dev)
+    g = torch.Generator().manual_seed(args.seed + 1)
+    prompts = torch.randint(0, cfg.V, (B, P), generator=g).tolist()
+    for p in range(P):
+        nxt = dec.step_tokens([prompts[b][p] for b in range(B)], p)
+    dec.set_position(P)
+    with torch.cuda.stream(dec.stream):
+        dec.tok.copy_(nxt.to(dev))
+    for _ in range(3):
+        dec.run_step(from_tokens=True, advance=True)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.steps):
+            dec.run_step(from_tokens=True, advance=True)
+        torch.cuda.synchronize()
+    tot: dict[str, tuple[int, float]] = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            k = e.name.split("(")[0][:70]
+            c, t = tot.get(k, (0, 0.0))
+            tot[k] = (c + 1, t + e.device_time)
+    all_t = sum(t for _, t in tot.values())
+    n = args.steps
+    print(f"batch {B}, context ~{P}: {all_t / n:.1f} us of kernels per step")
+    for k, (c, t) in sorted(tot.items(), key=lambda x: -x[1][1]):
+        print(f"{t / n:9.1f} us/step {100 * t / all_t:5.1f} %  x{c / n:.0f}  {k}")
+
+
+PHASE_MARKS = 32   # stamps per layer row
+PHASE_ROWS = 64    # layer rows per CTA
+# (label, first mark, second mark, from layer): time between two stamps of qwen3_step.cu
+PHASE_SPANS = [("x poll (previous layer's down)", 0, 1, 1), ("QKV RMSNorm + staging", 1, 2, 0),
+               ("QKV weights wait", 2, 3, 0), ("QKV tiles + publish", 3, 4, 0), ("q/k/v poll", 4, 5, 0),
+               ("q/k RMSNorm + RoPE", 5, 6, 0), ("attention split", 6, 7, 0), ("split reduce + publish", 7, 8, 0),
+               ("merge (first CTA of a group)", 8, 9, 0), ("merged poll + staging (O CTAs)", 9, 10, 0),
+               ("O weights wait", 10, 11, 0), ("O tiles + publish", 11, 12, 0), ("x1 poll", 12, 13, 0),
+               ("MLP RMSNorm + staging", 13, 14, 0), ("gate/up weights wait", 14, 15, 0),
+               ("gate/up tiles + publish", 15, 16, 0), ("down inputs poll + staging", 16, 17, 0),
+               ("down weights wait", 18, 19, 0), ("down slices + publish", 19, 20, 0)]
+PHASE_EVENTS = [("QKV rows published", 4), ("q/k/v polled", 5), ("attention splits published", 8),
+                ("merged heads published", 9), ("merged heads polled + staged", 10), ("x1 rows published", 12),
+                ("x1 polled", 13), ("SwiGLU outputs published", 16), ("down inputs polled", 17),
+                ("down slices published", 20)]
+
+
+def build_profiling_library():
+    """A second copy of the library with the step kernel's phase stamps compiled in
+    (-DIRON_STEP_PROFILE: thread 0 of each CTA stores %globaltimer at fixed points of
+    each layer); the product library is untouched."""
+    from iron_b200 import build as b
+    lib = b.PKG / "libiron_b200_prof.so"
+    objd = b.PKG / "_build_prof"
+    objd.mkdir(exist_ok=True)
+    objs = []
+    for src in sorted(b.CSRC.glob("*.cu")):
+        obj = objd / (src.stem + ".o")
+        if not obj.exists() or any(d.stat().st_mtime > obj.stat().st_mtime for d in b._deps(src)):
+            subprocess.run([b.nvcc(), *b.ARCH, *b.FLAGS, "-DIRON_STEP_PROFILE", f"-I{b.INCLUDE}", "-c", str(src),
+                            "-o", str(obj)], check=True, capture_output=True, text=True)
+        objs.append(str(obj))
+    subprocess.run([b.nvcc(), *b.ARCH, "-shared", "-o", str(lib), *objs, "-lcudart"], check=True)
+    return lib
+
+
+def run_phases(args):
+    """Phase breakdown of the one-launch decode step at context ``--prompt``: per phase the
+    microseconds per token summed over the layers (mean over CTAs) and per layer the
+    slowest and the fastest CTA; then the global timeline of a layer: when the LAST CTA
+    reached each hand-off, relative to the moment the last CTA had the layer's input
+    (mean over the inner layers)."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from iron_b200.qwen3 import Qwen3B200, Qwen3Config, Qwen3Weights
+    lib = C.CDLL(str(build_profiling_library()))
+    lib.iron_qwen3_decode_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+    lib.iron_qwen3_step_profile_buffer.argtypes = [C.c_void_p]
+    lib.iron_qwen3_grid.argtypes = [C.c_void_p]
+    cfg = Qwen3Config.qwen3_0_6b()
+    P = args.prompt
+    dec = Qwen3B200(Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP), max_seq=P + 128, impl="step")
+    for p in range(P):
+        dec.step_tokens([p % 1000], p)
+    dec.set_position(P)
+    st, mp = dec.stream, C.addressof(dec._model)
+    n_cta = int(lib.iron_qwen3_grid(mp))
+
+    def run(n):
+        for _ in range(n):
+            if lib.iron_qwen3_decode_step(mp, 1, 1, st.cuda_stream) != 0:
+                raise RuntimeError("profiling step failed")
+
+    run(5)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(st)
+    run(20)
+    ev[1].record(st)
+    st.synchronize()
+    plain_us = ev[0].elapsed_time(ev[1]) / 20 * 1000
+    buf = torch.zeros(n_cta * PHASE_ROWS * PHASE_MARKS, dtype=torch.int64, device=dec.x.device)
+    lib.iron_qwen3_step_profile_buffer(C.c_void_p(buf.data_ptr()))
+    NL = cfg.n_layers
+    spans, events, lm, totals = {}, {}, [], []
+    for _ in range(10):
+        buf.zero_()
+        run(1)
+        st.synchronize()
+        t = buf.cpu().numpy().reshape(n_cta, PHASE_ROWS, PHASE_MARKS).astype(np.float64)
+        lay = t[:, :NL]
+        for name, a, b2, first in PHASE_SPANS:
+            A, B_ = lay[:, first:, a], lay[:, first:, b2]
+            v = np.where((A > 0) & (B_ > 0), (B_ - A) / 1000.0, np.nan)
+            spans.setdefault(name, []).append((np.nanmean(np.nansum(v, 1)), np.nanmean(np.nanmax(v, 0)),
+                                               np.nanmean(np.nanmin(v, 0))))
+        for name, mk in PHASE_EVENTS:
+            vals = []
+            for l in range(1, NL - 1):
+                col = lay[:, l, mk]
+                col = col[col > 0]
+                vals.append((col.max() - lay[:, l, 1].max()) / 1000.0)
+            events.setdefault(name, []).append(np.mean(vals))
+        fin = t[:, NL]
+        lm.append(((fin[:, 2] - fin[:, 1]) / 1000.0).mean())
+        totals.append((fin[:, 2].max() - t[:, 0, 0].min()) / 1000.0)
+    lib.iron_qwen3_step_profile_buffer(C.c_void_p(0))
+    print(f"step without stamps {plain_us:.1f} us; with stamps {np.mean(totals):.1f} us (first to last stamp); "
+          f"context {P}; {n_cta} CTAs; per layer {np.mean(totals) / NL:.2f} us incl. the lm_head share")
+    print(f"{'phase':34s} {'us/token':>9s} {'slowest/layer':>14s} {'fastest/layer':>14s}")
+    for name, vals in spans.items():
+        m = np.nanmean(np.array(vals, dtype=np.float64), axis=0)
+        print(f"{name:34s} {m[0]:9.1f} {m[1]:14.2f} {m[2]:14.2f}")
+    print(f"{'final RMSNorm + lm_head + argmax':34s} {np.mean(lm):9.1f}")
+    print("timeline of a layer (last CTA, us after the last CTA had x):")
+    for name, vals in events.items():
+        print(f"  {name:32s} {np.mean(vals):6.2f}")
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -618,6 +903,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.phases or args.breakdown or args.sweep:
+        (run_phases if args.phases else run_breakdown if args.breakdown else run_sweep)(args)
         return
     if world > 1:
         import datetime

@@ -682,18 +682,19 @@ def run_sweep(args):
             ws = [w0] + [w0.clone() for _ in range(max(1, 300 * 2**20 // (N * K)) - 1)]
             x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
             y = torch.empty(B, N, dtype=torch.bfloat16, device=dev)
-            cases.append((N, K, B, ws, x, y))
+            cases.append((N, K, B, ws, x, y, _lib.tc_workspace([(N, K)], B, dev)))
 
-        def run(N, K, B, w, x, y):
-            _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B, None, y.data_ptr(), st)
+        def run(N, K, B, w, x, y, tw):
+            _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B, None, y.data_ptr(),
+                      tw.data_ptr(), tw.numel(), st)
 
-        for N, K, B, ws, x, y in cases:
+        for N, K, B, ws, x, y, tw in cases:
             for w in ws[1:]:
-                run(N, K, B, w, x, y)
+                run(N, K, B, w, x, y, tw)
                 warm += 1
         torch.cuda.synchronize()
-        for N, K, B, ws, x, y in cases:
-            run(N, K, B, ws[0], x, y)
+        for N, K, B, ws, x, y, tw in cases:
+            run(N, K, B, ws[0], x, y, tw)
         torch.cuda.synchronize()
         print(f"warm-up launches: {warm}; then one launch each of {shapes}")
         return
@@ -715,8 +716,9 @@ def run_sweep(args):
             x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
             y = torch.empty(B, N, dtype=torch.bfloat16, device=dev)
             s_ = st()
+            tw = _lib.tc_workspace([(N, K)], B, dev)
             fns = [(lambda w=w: _lib.call("iron_gemv_w8a16", w.data_ptr(), N, K, G, 1, 0, 0, 0, x.data_ptr(), B,
-                                          None, y.data_ptr(), s_)) for w in ws]
+                                          None, y.data_ptr(), tw.data_ptr(), tw.numel(), s_)) for w in ws]
             ms = _sweep_timed(fns, reps)
             nbytes = wbytes + B * K * 2 + B * N * 2
             rows.append({"kernel": "gemv_w8a16", "N": N, "K": K, "batch": B, "us": ms * 1e3,

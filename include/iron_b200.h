@@ -9,7 +9,9 @@
  *   - Return 0 on success, a negative IRON_ERR_* code on failure; the message is
  *     available from iron_last_error() (thread-local).  No entry point
  *     allocates device memory; scratch space ("workspace") is caller-provided,
- *     sized by the matching *_workspace_bytes() query.
+ *     sized by the matching *_workspace_bytes() query, and zero-filled once before
+ *     its first use.  Calls with different workspaces may run on different streams
+ *     at the same time; calls sharing a workspace must not overlap.
  *   - Runtime parameters that change between CUDA-graph replays (positions,
  *     KV lengths) are read from device memory when the *_dev pointer is non-NULL.
  *
@@ -60,20 +62,26 @@ int64_t iron_launch_count(void);
  * (and 9..15) computes the exact dequantised sum (one bf16 rounding; launches of 8
  * rows); batch 16..256 on plain wires runs one tcgen05 tensor-core contraction with
  * each weight q*s written as two bf16 planes (hi + lo, exact products) and float32
- * accumulation: the exact sum up to float32 summation order (see iron_tc_status).  That contraction keeps its
- * split-K partial sums in one scratch array per GPU (and normalises RMS inputs into
- * another): such calls on different streams of one GPU must not overlap.
+ * accumulation: the exact sum up to float32 summation order.  That contraction keeps
+ * its scratch (status word, split-K arrival counters and partial tiles, RMS-normalised
+ * inputs) in `workspace` (iron_tc_workspace_bytes(M, K, batch) bytes, 256-byte
+ * aligned, zero-filled before first use); with no workspace, or a smaller one, batch
+ * 16+ runs the exact kernel in launches of 8 rows instead.
  * group in {32, 64, 128}; K a multiple of 16*... see iron_gemv_w8a16 checks.
  */
 int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
                     int rows_per_core, int tiles_per_core, int domain,
                     const uint16_t* x, int batch, const uint16_t* residual,
-                    uint16_t* y, void* stream);
+                    uint16_t* y, void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Error word of the tensor-core path (batch >= 16) on the current device: 0, or
- * the code of the first bounded device wait that timed out.  clear != 0 also resets
- * it (and the kernel's split-K counters).  No reference counterpart. */
-int iron_tc_status(int clear);
+/* Workspace bytes of a batch 16..256 tensor-core projection of M rows x K columns
+ * (any epilogue, a gate/up pair and an RMSNorm prologue included); 256 below batch 16.
+ * No reference counterpart. */
+int64_t iron_tc_workspace_bytes(int M, int K, int batch);
+/* Error word of the tensor-core projections that used `workspace` (its first int32):
+ * 0, or the code of the first bounded device wait that timed out.  clear != 0 also
+ * resets it.  Synchronous.  No reference counterpart. */
+int iron_tc_status(void* workspace, int clear);
 
 /* Dequantise a wire to float32 q*s (exact), row-major (M, K).  Test/inspection
  * entry point for the bit-exact dequant check (GEMVInt8.reference, op.py:173-178). */
@@ -93,23 +101,27 @@ int iron_quantize_rtn(const uint16_t* w, int M, int K, int group, int tile_m, in
  * independent != 0: `batch` independent GEMVs, A[b] (M, K) each (the num_batches
  * mode of iron/operators/gemv/op.py:151-157).  Replaces GEMV (gemv/op.py:20-163,
  * kernel aie_kernels/generic/mv.cc:47-90).  A shared weight with 16..256 rows runs
- * the tcgen05 contraction of iron_gemv_w8a16 (same per-GPU scratch: such calls on
- * different streams of one GPU must not overlap). */
+ * the tcgen05 contraction of iron_gemv_w8a16 with its scratch in `workspace`
+ * (iron_tc_workspace_bytes(M, K, batch); NULL: launches of 8 rows instead). */
 int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
-                   int independent, uint16_t* y, void* stream);
+                   int independent, uint16_t* y, void* workspace, int64_t workspace_bytes,
+                   void* stream);
 
 /* lm_head GEMV fused with a greedy argmax over the bf16-rounded logits (ties ->
  * lowest index, as numpy.argmax in qwen3_npu_int8.py:619-620).  logits may be
- * NULL (not stored).  token_out: int32[batch].  workspace: iron_argmax_workspace_bytes().
- * Batch 16..256: one tcgen05 contraction; with logits NULL the logits go to a per-GPU
- * scratch array (batch * M <= 8 Mi values), so such calls on different streams of one
- * GPU must not overlap. */
+ * NULL (not stored; the int8 form needs it).  token_out: int32[batch].  workspace:
+ * iron_lm_head_workspace_bytes(M, K, batch) bytes, 256-byte aligned, zero-filled
+ * before first use.  From batch 16 on it holds the tcgen05 contraction's scratch
+ * first (so iron_tc_status reads its status word), then the argmax candidates, then
+ * the logits when logits is NULL; iron_argmax_workspace_bytes(batch) bytes (the
+ * candidates only) run the launches of 8 rows instead. */
 int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
                              uint16_t* logits, int32_t* token_out, void* workspace,
-                             void* stream);
+                             int64_t workspace_bytes, void* stream);
 int iron_lm_head_w8_argmax(const void* wire, int M, int K, int group, const uint16_t* x,
                            int batch, uint16_t* logits, int32_t* token_out, void* workspace,
-                           void* stream);
+                           int64_t workspace_bytes, void* stream);
+int64_t iron_lm_head_workspace_bytes(int M, int K, int batch);
 int64_t iron_argmax_workspace_bytes(int batch);
 /* Greedy argmax over bf16 rows: token_out[b] = argmax_m logits[b, m]. */
 int iron_argmax_bf16(const uint16_t* logits, int M, int batch, int32_t* token_out,
@@ -166,13 +178,14 @@ int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int bat
  * 1: ang is a (max_seq, HD) table and the row kv_off/(2*HD) is used.
  * norm_mode selects the RMSNorm arithmetic of the input and q/k norms (see
  * iron_rmsnorm; the QKV golden uses mode 1).
- * raw_ws: bf16 workspace of batch*(Hq+2*Hkv)*HD elements. */
+ * raw_ws: bf16 workspace of batch*(Hq+2*Hkv)*HD elements.  workspace: the projection's
+ * tensor-core scratch from batch 16 on (iron_tc_workspace_bytes; may be NULL). */
 int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const void* wqkv_wire, int group,
                   int tile_m, int domain, const uint16_t* n_qn, const uint16_t* n_kn,
                   const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv_cache,
                   int D, int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
                   const int32_t* kv_off_dev, float eps, int norm_mode, uint16_t* raw_ws,
-                  void* stream);
+                  void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---- decode attention ---------------------------------------------------------
  * GQA single-query attention per stream over positions [0, seq_len), base-2
@@ -217,12 +230,15 @@ int iron_decode_attn_static(const uint16_t* q, const uint16_t* kv, uint16_t* out
  *   nxt = bf16(x1 + bf16(Wd@gh))
  * Wires are described like iron_gemv_w8a16 (tile_m, rows_per_core, tiles_per_core).
  * x1_ws (batch*D) and gh_ws (batch*FF) are bf16 workspaces (the reference's
- * a_scratch / gh_scratch round-trip buffers). */
+ * a_scratch / gh_scratch round-trip buffers); workspace: the projections' tensor-core
+ * scratch from batch 16 on (the largest iron_tc_workspace_bytes of the three; may be
+ * NULL), used by one projection at a time. */
 int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, const uint16_t* n_pf,
                    const void* wo, int wo_tile_m, int wo_rows_per_core, int wo_tiles_per_core,
                    const void* wg, const void* wu, int gu_tile_m, const void* wd, int d_tile_m,
                    int group, int domain, uint16_t* x1_ws, uint16_t* gh_ws, uint16_t* nxt,
-                   int D, int FF, int QD, int batch, float eps, void* stream);
+                   int D, int FF, int QD, int batch, float eps, void* workspace,
+                   int64_t workspace_bytes, void* stream);
 
 /* ---- whole decode step ----------------------------------------------------------
  * One greedy Qwen3 decode token (batch 1) in ONE persistent cooperative kernel:
@@ -326,10 +342,12 @@ int iron_qwen3_sync_reset(const iron_qwen3_model* m, void* stream);
  * epilogues exposed.  wire_b != NULL: gate/up pair, y = bf16(silu_tanh(bf16(Wa@h)) *
  * bf16(Wb@h)) (epi 0 only).  rms_w != NULL: h = bf16(RMSNorm_w(x)) first (rms_mode as
  * iron_rmsnorm).  epi 0: y bf16 = bf16(sum); 1: y bf16 = bf16(residual + bf16(sum));
- * 2: y float32 = float(sum) (a rank's partial sum).  x rows ld_x apart, y rows ld_y. */
+ * 2: y float32 = float(sum) (a rank's partial sum).  x rows ld_x apart, y rows ld_y.
+ * workspace: as iron_gemv_w8a16. */
 int iron_gemv_w8a16_ex(const void* wire_a, const void* wire_b, int M, int K, int group, int domain,
                        const uint16_t* x, int ld_x, int batch, const uint16_t* rms_w, float eps,
-                       int rms_mode, const uint16_t* residual, int epi, void* y, int ld_y, void* stream);
+                       int rms_mode, const uint16_t* residual, int epi, void* y, int ld_y,
+                       void* workspace, int64_t workspace_bytes, void* stream);
 /* y = bf16(res + bf16(sum)) elementwise (sum: float32, the all-reduced partials). */
 int iron_resid_add_f32(const uint16_t* res, const float* sum, uint16_t* y, int64_t n, void* stream);
 /* pairs[b] = (float bits of logits[b, tok[b]], tok[b] + offset): a rank's greedy

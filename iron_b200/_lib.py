@@ -20,20 +20,22 @@ F = C.c_float
 SIGNATURES: dict[str, tuple] = {
     "iron_version": (C.c_char_p, []),
     "iron_last_error": (I, [C.c_char_p, I]),
-    "iron_gemv_w8a16": (I, [P, I, I, I, I, I, I, I, P, I, P, P, P]),
+    "iron_gemv_w8a16": (I, [P, I, I, I, I, I, I, I, P, I, P, P, P, I64, P]),
     "iron_dequant_w8": (I, [P, I, I, I, I, I, I, I, P, P]),
     "iron_quantize_rtn": (I, [P, I, I, I, I, I, P, P]),
-    "iron_gemv_bf16": (I, [P, I, I, P, I, I, P, P]),
-    "iron_lm_head_bf16_argmax": (I, [P, I, I, P, I, P, P, P, P]),
-    "iron_lm_head_w8_argmax": (I, [P, I, I, I, P, I, P, P, P, P]),
+    "iron_gemv_bf16": (I, [P, I, I, P, I, I, P, P, I64, P]),
+    "iron_lm_head_bf16_argmax": (I, [P, I, I, P, I, P, P, P, I64, P]),
+    "iron_lm_head_w8_argmax": (I, [P, I, I, I, P, I, P, P, P, I64, P]),
+    "iron_lm_head_workspace_bytes": (I64, [I, I, I]),
     "iron_argmax_workspace_bytes": (I64, [I]),
     "iron_argmax_bf16": (I, [P, I, I, P, P, P]),
     "iron_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
     "iron_add": (I, [P, P, P, I64, P]),
-    "iron_tc_status": (I, [I]),
+    "iron_tc_status": (I, [P, I]),
+    "iron_tc_workspace_bytes": (I64, [I, I, I]),
     "iron_launch_count": (I64, []),
     "iron_rope_kv": (I, [P, P, P, P, I, I, I, I, I, P, P]),
-    "iron_gemv_w8a16_ex": (I, [P, P, I, I, I, I, P, I, I, P, C.c_float, I, P, I, P, I, P]),
+    "iron_gemv_w8a16_ex": (I, [P, P, I, I, I, I, P, I, I, P, C.c_float, I, P, I, P, I, P, I64, P]),
     "iron_resid_add_f32": (I, [P, P, P, I64, P]),
     "iron_argmax_pair": (I, [P, I, I, P, I, P, P]),
     "iron_argmax_merge": (I, [P, I, I, P, P]),
@@ -41,7 +43,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_silu": (I, [P, P, I64, I, P]),
     "iron_embedding": (I, [P, I, P, I, I, P, P]),
     "iron_decode_advance": (I, [P, P, P, I, I, P]),
-    "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, I, P, P]),
+    "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, I, P, P, I64, P]),
     "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
     "iron_decode_attn_static_capacity_bytes": (I64, []),
@@ -54,7 +56,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_qwen3_sync_reset": (I, [P, P]),
     "iron_qwen3_tiles_bytes": (I64, [I, I, I]),
     "iron_qwen3_pack_tiles": (I, [P, I64, I, I, I, I, I, P, P]),
-    "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P]),
+    "iron_mlp_block": (I, [P, P, I, P, P, I, I, I, P, P, I, P, I, I, I, P, P, P, I, I, I, I, F, P, I64, P]),
 }
 
 _LIB = None
@@ -111,3 +113,33 @@ def stream_ptr(stream=None) -> int:
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
     return s.cuda_stream
+
+
+def workspace(nbytes: int, device):
+    """Zero-filled device scratch of ``nbytes`` (at least 256) bytes.  torch's caching
+    allocator hands out 512-byte aligned blocks, above the 256 bytes the entry points
+    ask for."""
+    import torch
+    return torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def tc_workspace(shapes, batch: int, device, lm_head: bool = False):
+    """Scratch for the batch 16..256 tensor-core projections of ``shapes`` ((M, K) pairs)
+    that run one after another on one stream (``iron_tc_workspace_bytes``, the largest),
+    or of a batched lm_head + argmax (``iron_lm_head_workspace_bytes``)."""
+    L = lib()
+    fn = L.iron_lm_head_workspace_bytes if lm_head else L.iron_tc_workspace_bytes
+    return workspace(max(fn(M, K, batch) for M, K in shapes), device)
+
+
+def status_word(ws):
+    """The int32 status word at the head of a tensor-core workspace, as a device view
+    (read it with the step's results; ``iron_tc_status`` is the synchronous form)."""
+    import torch
+    return ws[:4].view(torch.int32)
+
+
+def raise_on_status(code: int, what: str):
+    if code:
+        raise IronError(f"{what}: a tensor-core projection stopped on a bounded device wait "
+                        f"(code {code}); its outputs are not valid")

@@ -16,7 +16,7 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
                              const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv_cache,
                              int D, int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
                              const int32_t* kv_off_dev, float eps, int norm_mode, uint16_t* raw_ws,
-                             void* stream) {
+                             void* workspace, int64_t workspace_bytes, void* stream) {
   IRON_REQUIRE(cur && n_in && n_qn && n_kn && ang && q_out && kv_cache && raw_ws, IRON_ERR_ARG,
                "qkv_head: null pointer");
   IRON_REQUIRE(kv_off_dev || (kv_off >= 0 && kv_off % (2 * HD) == 0 && kv_off / (2 * HD) < max_seq),
@@ -37,6 +37,8 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
   p.ld_y = M;
   p.nb = batch;
   p.epi = EPI_STORE;
+  p.tc_ws = workspace;
+  p.tc_ws_bytes = workspace_bytes;
   cudaStream_t st = (cudaStream_t)stream;
   rc = gemv_w8_launch(p, false, st);
   if (rc) return rc;
@@ -48,7 +50,8 @@ extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int 
                               const void* wo, int wo_tile_m, int wo_rows_per_core, int wo_tiles_per_core,
                               const void* wg, const void* wu, int gu_tile_m, const void* wd, int d_tile_m,
                               int group, int domain, uint16_t* x1_ws, uint16_t* gh_ws, uint16_t* nxt, int D,
-                              int FF, int QD, int batch, float eps, void* stream) {
+                              int FF, int QD, int batch, float eps, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
   IRON_REQUIRE(cur && a_or_cx && n_pf && wg && wu && wd && x1_ws && gh_ws && nxt, IRON_ERR_ARG,
                "mlp_block: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
@@ -69,6 +72,8 @@ extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int 
     p.ld_y = D;
     p.nb = batch;
     p.epi = EPI_RESID;
+    p.tc_ws = workspace;
+    p.tc_ws_bytes = workspace_bytes;
     rc = gemv_w8_launch(p, false, st);
   } else {
     rc = iron_add(cur, a_or_cx, x1_ws, (int64_t)batch * D, stream);
@@ -92,6 +97,8 @@ extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int 
     p.nb = batch;
     p.epi = EPI_STORE;
     p.xor_mask = p.wa.xor_mask;
+    p.tc_ws = workspace;
+    p.tc_ws_bytes = workspace_bytes;
     rc = gemv_w8_launch(p, true, st);
     if (rc) return rc;
   }
@@ -110,14 +117,24 @@ extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int 
     p.ld_y = D;
     p.nb = batch;
     p.epi = EPI_RESID;
+    p.tc_ws = workspace;
+    p.tc_ws_bytes = workspace_bytes;
     return gemv_w8_launch(p, false, st);
   }
 }
 
 extern "C" int iron_lm_head_w8_argmax(const void* wire, int M, int K, int group, const uint16_t* x, int batch,
-                                      uint16_t* logits, int32_t* token_out, void* workspace, void* stream) {
+                                      uint16_t* logits, int32_t* token_out, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
   IRON_REQUIRE(logits != nullptr, IRON_ERR_ARG, "lm_head_w8_argmax: logits buffer required");
-  int rc = iron_gemv_w8a16(wire, M, K, group, 1, 0, 0, 0, x, batch, nullptr, logits, stream);
+  IRON_REQUIRE(workspace && workspace_bytes >= iron_argmax_workspace_bytes(batch), IRON_ERR_ARG,
+               "lm_head_w8_argmax: workspace below iron_lm_head_workspace_bytes");
+  // batch 16+ with iron_lm_head_workspace_bytes: [tensor-core scratch | argmax
+  // candidates]; otherwise the candidates from offset 0 and launches of 8 rows
+  const bool tc = batch >= 16 && workspace_bytes >= iron_lm_head_workspace_bytes(M, K, batch);
+  const int64_t tcb = tc ? iron_tc_workspace_bytes(M, K, batch) : 0;
+  int rc = iron_gemv_w8a16(wire, M, K, group, 1, 0, 0, 0, x, batch, nullptr, logits, tc ? workspace : nullptr,
+                           tcb, stream);
   if (rc) return rc;
-  return iron_argmax_bf16(logits, M, batch, token_out, workspace, stream);
+  return iron_argmax_bf16(logits, M, batch, token_out, (uint8_t*)workspace + tcb, stream);
 }

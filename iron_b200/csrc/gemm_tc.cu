@@ -31,10 +31,15 @@
 // enough bf16 roundings that a batch-32 Qwen3 step's logits left the bf16 gate.
 //
 // Every wait is bounded by %globaltimer; on a timeout the CTA records an error code
-// in a device word (iron_tc_status), lets its copies and MMAs finish (bounded), frees
-// its TMEM and returns.  The split-K scratch is one array per GPU: launches on
-// different streams of one GPU must not overlap.
+// in the status word of its workspace (iron_tc_status), lets its copies and MMAs finish
+// (bounded), frees its TMEM and returns.  All scratch (status word, split-K arrival
+// counters, float32 partial tiles, RMS-normalised activations) lives in the caller's
+// workspace (iron_tc_workspace_bytes), so launches with their own workspaces may run on
+// different streams at once.  Every split arrives at its tile's counter, aborted ones
+// too, and the last one resets it: a timed-out launch leaves no counter mid-count.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "gemv_w8.cuh"
@@ -57,9 +62,6 @@ constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;
 // the last CTA; fewer leave the small-M projections with too few CTAs).
 constexpr int MIN_KB = 4;
 
-__device__ float g_ws[WS_FLOATS];
-__device__ int g_counters[MAX_TILES];
-__device__ int g_status;
 
 struct TcParams {
   int M, K, N, nb;              // N: MMA n (batch padded to 16); nb: batch rows
@@ -71,6 +73,9 @@ struct TcParams {
   void* y;
   int ld_y;
   uint32_t xor_mask;
+  int* status;    // the workspace's error word
+  int* counters;  // [tiles] split-K arrival counters (zero between launches)
+  float* part;    // [tiles][splits][NW * N][BM] float32 partial tiles
   int off_a, off_x, off_raw, off_scale, off_bar;
 };
 
@@ -100,7 +105,7 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 // Bounded wait for the phase of parity `par`; on a timeout (or another role's abort)
 // sets the abort flag and returns false.
-__device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t par, volatile int* abort_, int code) {
+__device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t par, volatile int* abort_, int code, int* status) {
   if (mbar_test(b, par)) return true;
   const unsigned long long t0 = gtimer();
   for (unsigned it = 1;; ++it) {
@@ -109,7 +114,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t par, volatile i
       if (*abort_) return false;
       if (gtimer() - t0 > TIMEOUT_NS) {
         *abort_ = 1;
-        atomicExch(&g_status, code);
+        atomicExch(status, code);
         return false;
       }
     }
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(NTH, 2)
       }
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
-        if (i >= S && !wait_phase(&freeb[s], (uint32_t)((i / S - 1) & 1), abort_, 1)) break;
+        if (i >= S && !wait_phase(&freeb[s], (uint32_t)((i / S - 1) & 1), abort_, 1, p.status)) break;
         const int kx = k0 + i * BK;
         if (W16) {
           mbar_expect(&raw_full[s], (uint32_t)(BM * 128 + N * 128));
@@ -270,7 +275,9 @@ __global__ void __launch_bounds__(NTH, 2)
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t par = (uint32_t)((i / S) & 1);
-        if (!wait_phase(&raw_full[s], par, abort_, 2) || (!W16 && !wait_phase(&a_full[s], par, abort_, 3))) break;
+        if (!wait_phase(&raw_full[s], par, abort_, 2, p.status) ||
+            (!W16 && !wait_phase(&a_full[s], par, abort_, 3, p.status)))
+          break;
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(sa(xtile + (size_t)s * N * 128));
 #pragma unroll
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(NTH, 2)
     // lane 0 waits and the warp follows its answer: warp-uniform control flow
     auto wait_warp = [&](uint64_t* b, uint32_t par, int code) -> bool {
       int r = 1;
-      if (lane == 0) r = wait_phase(b, par, abort_, code);
+      if (lane == 0) r = wait_phase(b, par, abort_, code, p.status);
       r = __shfl_sync(~0u, r, 0);
       if (r) mbar_test(b, par);  // every lane observes the completed phase
       return r != 0;
@@ -374,7 +381,7 @@ __global__ void __launch_bounds__(NTH, 2)
       }
     };
     if (ok) {
-      float* part = g_ws + ((size_t)(tile * p.splits + split) * NW * N) * BM;
+      float* part = p.part + ((size_t)(tile * p.splits + split) * NW * N) * BM;
       for (int c0 = 16 * half; c0 < N; c0 += 32) {
         float v[16], u[16];
         tmem_ld16(taddr + (uint32_t)c0, v);
@@ -389,17 +396,22 @@ __global__ void __launch_bounds__(NTH, 2)
           }
         }
       }
-      if (p.splits > 1) {
-        __threadfence();
-        bar_epi();
-        if (t == 0) *lastf = atomicAdd(&g_counters[tile], 1) == p.splits - 1;
-        bar_epi();
-        if (*lastf) {
+    }
+    if (p.splits > 1 && nkb > 0) {
+      // every split arrives, aborted ones too, and the last resets the counter
+      __threadfence();
+      bar_epi();
+      if (t == 0) {
+        *lastf = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+        if (*lastf) p.counters[tile] = 0;
+      }
+      bar_epi();
+      if (*lastf && ok) {
           __threadfence();
           // CB columns at a time, the partials of U splits loaded before any is added:
           // U * CB * NW loads in flight per thread; sums in split order as always
           constexpr int CB = 4, U = 4;
-          const float* base = g_ws + (size_t)tile * p.splits * NW * N * BM + row;
+          const float* base = p.part + (size_t)tile * p.splits * NW * N * BM + row;
           for (int b0 = half; b0 < N; b0 += 2 * CB) {
             float a0[CB], a1[CB];
 #pragma unroll
@@ -431,9 +443,7 @@ __global__ void __launch_bounds__(NTH, 2)
             for (int c = 0; c < CB; ++c)
               if (b0 + 2 * c < N) finish(b0 + 2 * c, a0[c], a1[c]);
           }
-          if (t == 0) g_counters[tile] = 0;
         }
-      }
     }
   }
   tc_fence_before();
@@ -472,7 +482,6 @@ __global__ void rms_rows_kernel(const uint16_t* x, int ld_x, const uint16_t* w, 
     y[(size_t)b * K + i] = f2bf(rms_apply(bf2f(xr[i]), bf2f(w[i]), rc));
 }
 
-__device__ uint16_t g_xnorm[256 * 16384];  // normalised activations of one launch
 
 }  // namespace tc
 
@@ -509,8 +518,62 @@ static bool map2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// K split over CTAs so that they make about one wave (two per SM), at least MIN_KB
+// k-blocks per split (a shorter split is mostly start-up, and every split adds a partial
+// tile to the last CTA's reduction), the partials within WS_FLOATS
+static void tc_split_plan(int M, int K, int N, int NW, int& splits, int& kbps) {
+  using namespace tc;
+  const int tiles = (M + BM - 1) / BM;
+  const int kblocks = K / BK;
+  splits = 2 * iron_num_sms() / tiles;
+  if (splits > kblocks / MIN_KB) splits = kblocks / MIN_KB;
+  if (splits < 1) splits = 1;
+  kbps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kbps - 1) / kbps;
+  while (splits > 1 && (size_t)tiles * splits * NW * N * BM > WS_FLOATS) {
+    kbps *= 2;
+    splits = (kblocks + kbps - 1) / kbps;
+  }
+}
+
+static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// Workspace layout: [status word | counters (tiles) | partials | normalised activations]
+struct TcWs {
+  int* status;
+  int* counters;
+  float* part;
+  uint16_t* xnorm;
+};
+static size_t tc_ws_need(int M, int K, int nb, int NW, bool rms) {
+  using namespace tc;
+  const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
+  int splits, kbps;
+  tc_split_plan(M, K, N, NW, splits, kbps);
+  size_t n = 256 + r256((size_t)tiles * 4);
+  if (splits > 1) n += r256((size_t)tiles * splits * NW * N * BM * 4);
+  if (rms) n += r256((size_t)nb * K * 2);
+  return n;
+}
+static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, bool rms, TcWs& o) {
+  using namespace tc;
+  if (!ws || !iron_aligned(ws, 256) || (size_t)bytes < tc_ws_need(M, K, nb, NW, rms)) return false;
+  const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
+  int splits, kbps;
+  tc_split_plan(M, K, N, NW, splits, kbps);
+  uint8_t* b = (uint8_t*)ws;
+  o.status = (int*)b;
+  size_t off = 256;
+  o.counters = (int*)(b + off);
+  off += r256((size_t)tiles * 4);
+  o.part = (float*)(b + off);
+  if (splits > 1) off += r256((size_t)tiles * splits * NW * N * BM * 4);
+  o.xnorm = (uint16_t*)(b + off);
+  return true;
+}
+
 template <int G, bool PAIR>
-static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStream_t st) {
+static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const TcWs& ws, cudaStream_t st) {
   using namespace tc;
   constexpr int NW = PAIR ? 2 : 1;
   const int M = p.M, K = p.K, nb = p.nb;
@@ -518,19 +581,13 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
   const int tiles = (M + BM - 1) / BM;
   const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
-  // split K so that the CTAs make about one wave (two per SM), at least 4 k-blocks per
-  // split (a shorter split is mostly start-up, and every split adds a partial tile to
-  // the last CTA's reduction)
-  int splits = 2 * iron_num_sms() / tiles;
-  if (splits > kblocks / MIN_KB) splits = kblocks / MIN_KB;
-  if (splits < 1) splits = 1;
-  int kbps = (kblocks + splits - 1) / splits;
-  splits = (kblocks + kbps - 1) / kbps;
-  while (splits > 1 && (size_t)tiles * splits * NW * N * BM > WS_FLOATS) {
-    kbps *= 2;
-    splits = (kblocks + kbps - 1) / kbps;
-  }
+  (void)kblocks;
+  int splits, kbps;
+  tc_split_plan(M, K, N, NW, splits, kbps);
   TcParams tp = {};
+  tp.status = ws.status;
+  tp.counters = ws.counters;
+  tp.part = ws.part;
   tp.M = M;
   tp.K = K;
   tp.N = N;
@@ -589,23 +646,20 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, cudaStr
 
 // bf16 weights: y[b, m] = bf16(sum_k A[m, k] x[b, k]), float32 accumulation.
 int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int ld_x, int nb, uint16_t* y,
-                        int ld_y, cudaStream_t st) {
+                        int ld_y, void* workspace, int64_t workspace_bytes, cudaStream_t st) {
   using namespace tc;
   if (nb < 16 || nb > 256 || K % 64 || !iron_aligned(A, 16) || !iron_aligned(x, 16) || ld_x % 8) return 1;
   const int N = (nb + 15) / 16 * 16;
   const int tiles = (M + BM - 1) / BM;
-  const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
-  int splits = 2 * iron_num_sms() / tiles;
-  if (splits > kblocks / MIN_KB) splits = kblocks / MIN_KB;
-  if (splits < 1) splits = 1;
-  int kbps = (kblocks + splits - 1) / splits;
-  splits = (kblocks + kbps - 1) / kbps;
-  while (splits > 1 && (size_t)tiles * splits * N * BM > WS_FLOATS) {
-    kbps *= 2;
-    splits = (kblocks + kbps - 1) / kbps;
-  }
+  TcWs ws;
+  if (!tc_ws_carve(workspace, workspace_bytes, M, K, nb, 1, false, ws)) return 1;
+  int splits, kbps;
+  tc_split_plan(M, K, N, 1, splits, kbps);
   TcParams tp = {};
+  tp.status = ws.status;
+  tp.counters = ws.counters;
+  tp.part = ws.part;
   tp.M = M;
   tp.K = K;
   tp.N = N;
@@ -655,11 +709,12 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
   if (p.nb < 16 || p.nb > 256 || !p.wa.plain1 || (pair && !p.wb.plain1)) return 1;
   if (p.K % 64 || p.K % (8 * p.wa.G) || p.K > 16384) return 1;
   if (!iron_aligned(p.wa.base, 16) || (pair && !iron_aligned(p.wb.base, 16))) return 1;
+  TcWs ws;  // without a workspace large enough the caller runs the exact kernel
+  if (!tc_ws_carve(p.tc_ws, p.tc_ws_bytes, p.M, p.K, p.nb, pair ? 2 : 1, p.rms_w != nullptr, ws)) return 1;
   const uint16_t* x = p.x;
   int ld_x = p.ld_x;
   if (p.rms_w) {  // normalise first: the tensor-core kernel reads x through TMA
-    uint16_t* xn = nullptr;
-    if (cudaGetSymbolAddress((void**)&xn, g_xnorm) != cudaSuccess) return 1;
+    uint16_t* xn = ws.xnorm;
     rms_rows_kernel<<<p.nb, 256, 0, st>>>(p.x, p.ld_x, p.rms_w, p.K, p.eps, p.rms_mode, xn);
     int rc = iron_check_launch("rms_rows_kernel");
     if (rc) return rc;
@@ -668,9 +723,9 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
   }
   if (!iron_aligned(x, 16) || ld_x % 8) return 1;
   switch (p.wa.G) {
-    case 32: return pair ? tc_launch<32, true>(p, x, ld_x, st) : tc_launch<32, false>(p, x, ld_x, st);
-    case 64: return pair ? tc_launch<64, true>(p, x, ld_x, st) : tc_launch<64, false>(p, x, ld_x, st);
-    case 128: return pair ? tc_launch<128, true>(p, x, ld_x, st) : tc_launch<128, false>(p, x, ld_x, st);
+    case 32: return pair ? tc_launch<32, true>(p, x, ld_x, ws, st) : tc_launch<32, false>(p, x, ld_x, ws, st);
+    case 64: return pair ? tc_launch<64, true>(p, x, ld_x, ws, st) : tc_launch<64, false>(p, x, ld_x, ws, st);
+    case 128: return pair ? tc_launch<128, true>(p, x, ld_x, ws, st) : tc_launch<128, false>(p, x, ld_x, ws, st);
   }
   return 1;
 }
@@ -679,18 +734,22 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
 
 using namespace iron;
 
-// Error word of the tensor-core projections on the current device: 0, or the code of
-// the first bounded wait that timed out.  clear != 0 resets it together with the
-// split-K arrival counters (an aborted launch can leave them mid-count).
-extern "C" int iron_tc_status(int clear) {
+// Bytes of workspace a batch >= 16 projection of M rows x K columns needs (a gate/up
+// pair with an RMSNorm prologue included; a bf16 weight needs no more).
+extern "C" int64_t iron_tc_workspace_bytes(int M, int K, int batch) {
+  if (M < 1 || K < 64 || batch < 16 || batch > 256) return 256;
+  return (int64_t)std::max(tc_ws_need(M, K, batch, 1, true), tc_ws_need(M, K, batch, 2, true));
+}
+
+// Error word of the tensor-core projections that used `workspace`: 0, or the code of
+// the first bounded wait that timed out.  clear != 0 also resets it.  Synchronous.
+extern "C" int iron_tc_status(void* workspace, int clear) {
+  if (!workspace) return IRON_ERR_ARG;
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)) != cudaSuccess) return -1;
+  if (cudaMemcpy(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return IRON_ERR_CUDA;
   if (clear && v) {
     const int z = 0;
-    cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int));
-    void* c = nullptr;
-    if (cudaGetSymbolAddress(&c, tc::g_counters) == cudaSuccess) cudaMemset(c, 0, sizeof(tc::g_counters));
-    cudaDeviceSynchronize();
+    if (cudaMemcpy(workspace, &z, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return IRON_ERR_CUDA;
   }
   return v;
 }

@@ -291,10 +291,7 @@ static int gemv_bf16_dispatch(GemvBf16Params p, cudaStream_t st) {
 }
 
 int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int ld_x, int nb, uint16_t* y,
-                        int ld_y, cudaStream_t st);
-
-// logits of a batched lm_head whose caller keeps none (batch x vocab <= 8 M values)
-__device__ uint16_t g_lm_logits[8u << 20];
+                        int ld_y, void* workspace, int64_t workspace_bytes, cudaStream_t st);
 
 }  // namespace iron
 
@@ -304,13 +301,25 @@ extern "C" int64_t iron_argmax_workspace_bytes(int batch) {
   return (int64_t)batch * kMaxCand * 8;
 }
 
+extern "C" int64_t iron_tc_workspace_bytes(int M, int K, int batch);
+
+// Batch 16+ with iron_lm_head_workspace_bytes: [tensor-core scratch (its status word
+// first) | argmax candidates | logits when the caller keeps none]; smaller workspaces
+// and batch 1..15: the argmax candidates from offset 0.
+extern "C" int64_t iron_lm_head_workspace_bytes(int M, int K, int batch) {
+  const int64_t am = (iron_argmax_workspace_bytes(batch) + 255) & ~(int64_t)255;
+  if (batch < 16) return am;
+  return iron_tc_workspace_bytes(M, K, batch) + am + (((int64_t)batch * M * 2 + 255) & ~(int64_t)255);
+}
+
 extern "C" int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,
-                              int independent, uint16_t* y, void* stream) {
+                              int independent, uint16_t* y, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
   IRON_REQUIRE(y != nullptr, IRON_ERR_ARG, "gemv_bf16: null output");
   IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "gemv_bf16: batch %d below 1", batch);
   // 16+ rows of a shared weight: one tensor-core contraction (gemm_tc.cu)
   if (!independent && batch >= 16) {
-    const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, y, M, (cudaStream_t)stream);
+    const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, y, M, workspace, workspace_bytes, (cudaStream_t)stream);
     if (rc <= 0) return rc;
   }
   // a shared weight with more than 8 activation rows: launches over 8 rows each
@@ -332,21 +341,21 @@ extern "C" int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x
 
 extern "C" int iron_lm_head_bf16_argmax(const uint16_t* A, int M, int K, const uint16_t* x,
                                         int batch, uint16_t* logits, int32_t* token_out,
-                                        void* workspace, void* stream) {
+                                        void* workspace, int64_t workspace_bytes, void* stream) {
   IRON_REQUIRE(workspace && token_out, IRON_ERR_ARG, "lm_head_argmax: null workspace/token_out");
+  IRON_REQUIRE(workspace_bytes >= iron_argmax_workspace_bytes(batch), IRON_ERR_ARG,
+               "lm_head_argmax: workspace below iron_lm_head_workspace_bytes");
   IRON_REQUIRE(batch >= 1, IRON_ERR_UNSUPPORTED, "lm_head_argmax: batch %d below 1", batch);
   cudaStream_t st = (cudaStream_t)stream;
   // 16+ rows: the logits from one tensor-core contraction, then the argmax passes
-  if (batch >= 16) {
-    uint16_t* L = logits;
-    if (!L && (size_t)batch * M <= (8u << 20) &&
-        cudaGetSymbolAddress((void**)&L, g_lm_logits) != cudaSuccess)
-      L = nullptr;
-    if (L) {
-      const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, L, M, st);
-      if (rc < 0) return rc;
-      if (rc == 0) return iron_argmax_bf16(L, M, batch, token_out, workspace, stream);
-    }
+  if (batch >= 16 && workspace_bytes >= iron_lm_head_workspace_bytes(M, K, batch)) {
+    const int64_t tcb = iron_tc_workspace_bytes(M, K, batch);
+    const int64_t am = (iron_argmax_workspace_bytes(batch) + 255) & ~(int64_t)255;
+    uint8_t* cand = (uint8_t*)workspace + tcb;
+    uint16_t* L = logits ? logits : (uint16_t*)(cand + am);
+    const int rc = gemm_tc_bf16_launch(A, M, K, x, K, batch, L, M, workspace, tcb, st);
+    if (rc < 0) return rc;
+    if (rc == 0) return iron_argmax_bf16(L, M, batch, token_out, cand, stream);
   }
   // up to 8 activation rows per launch; rows b0.. use the workspace's candidate slots
   // from b0 * kMaxCand on

@@ -361,8 +361,10 @@ using namespace iron;
 extern "C" int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
                                int rows_per_core, int tiles_per_core, int domain,
                                const uint16_t* x, int batch, const uint16_t* residual,
-                               uint16_t* y, void* stream) {
+                               uint16_t* y, void* workspace, int64_t workspace_bytes, void* stream) {
   GemvW8Params p = {};
+  p.tc_ws = workspace;
+  p.tc_ws_bytes = workspace_bytes;
   int rc = make_wire(p.wa, wire, M, K, group, tile_m, rows_per_core, tiles_per_core, domain);
   if (rc) return rc;
   p.wb = p.wa;

@@ -48,6 +48,8 @@ struct GemvW8Params {
   int epi;
   int ksplit;           // warps sharing one row group along K (set by the launcher)
   uint32_t xor_mask;
+  void* tc_ws;          // scratch of the tensor-core path (batch >= 16), or null
+  int64_t tc_ws_bytes;
 };
 
 // The same call restricted to batch rows [b0, b0 + n).

@@ -54,7 +54,7 @@ using namespace iron;
 extern "C" int iron_gemv_w8a16_ex(const void* wire_a, const void* wire_b, int M, int K, int group, int domain,
                                   const uint16_t* x, int ld_x, int batch, const uint16_t* rms_w, float eps,
                                   int rms_mode, const uint16_t* residual, int epi, void* y, int ld_y,
-                                  void* stream) {
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
   IRON_REQUIRE(wire_a && x && y, IRON_ERR_ARG, "gemv_ex: null pointer");
   IRON_REQUIRE(epi >= 0 && epi <= 2, IRON_ERR_ARG, "gemv_ex: epilogue %d not in 0..2", epi);
   IRON_REQUIRE(epi != 1 || residual, IRON_ERR_ARG, "gemv_ex: the residual epilogue needs a residual");
@@ -83,6 +83,8 @@ extern "C" int iron_gemv_w8a16_ex(const void* wire_a, const void* wire_b, int M,
   p.ld_y = ld_y;
   p.nb = batch;
   p.epi = epi;
+  p.tc_ws = workspace;
+  p.tc_ws_bytes = workspace_bytes;
   return gemv_w8_launch(p, wire_b != nullptr, (cudaStream_t)stream);
 }
 

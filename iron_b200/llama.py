@@ -116,7 +116,10 @@ class LlamaB200:
         self.host_params = torch.zeros(2, B, dtype=torch.int32, pin_memory=True)
         self.attn_ws = torch.empty(_lib.lib().iron_decode_attn_workspace_bytes(B, c.Hq, c.HD, max_seq),
                                    dtype=torch.uint8, device=dev)
-        self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
+        # scratch of the 16+ stream tensor-core projections (one at a time on the decoder
+        # stream: one shared workspace) and of the lm_head + argmax
+        self.tc_ws = _lib.tc_workspace([(c.QKV, c.D), (c.D, c.QD), (c.FF, c.D), (c.D, c.FF)], B, dev)
+        self.head_ws = _lib.tc_workspace([(c.V, c.D)], B, dev, lm_head=True)
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict = {}
         self._step_launches: dict = {}  # advance -> kernels one step launched
@@ -139,27 +142,29 @@ class LlamaB200:
 
     def _launch_step(self, advance: bool, st: int):
         c, w, B = self.cfg, self.w, self.B
+        tw = (ptr(self.tc_ws), self.tc_ws.numel())
         abi("iron_embedding", ptr(w.embed), c.V, ptr(self.tok), B, c.D, ptr(self.x), st)
         for i, Lw in enumerate(w.layers):
             kv = self.kv[i]
             abi("iron_rmsnorm", ptr(self.x), ptr(Lw["norm1"]), ptr(self.xn), B, c.D, c.eps, 2, st)
-            abi("iron_gemv_bf16", ptr(Lw["wqkv"]), c.QKV, c.D, ptr(self.xn), B, 0, ptr(self.raw), st)
+            abi("iron_gemv_bf16", ptr(Lw["wqkv"]), c.QKV, c.D, ptr(self.xn), B, 0, ptr(self.raw), *tw, st)
             abi("iron_rope_kv", ptr(self.raw), ptr(self.angles), ptr(self.q), ptr(kv), c.HD, c.Hq, c.Hkv,
                 self.max_seq, B, ptr(self.off), st)
             abi("iron_decode_attn", ptr(self.q), ptr(kv), ptr(self.attn), B, c.Hq, c.Hkv, c.HD, self.max_seq,
                 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
-            abi("iron_gemv_bf16", ptr(Lw["wo"]), c.D, c.QD, ptr(self.attn), B, 0, ptr(self.o), st)
+            abi("iron_gemv_bf16", ptr(Lw["wo"]), c.D, c.QD, ptr(self.attn), B, 0, ptr(self.o), *tw, st)
             abi("iron_add", ptr(self.x), ptr(self.o), ptr(self.x1), B * c.D, st)
             abi("iron_rmsnorm", ptr(self.x1), ptr(Lw["norm2"]), ptr(self.xn), B, c.D, c.eps, 2, st)
-            abi("iron_gemv_bf16", ptr(Lw["wg"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.g), st)
-            abi("iron_gemv_bf16", ptr(Lw["wu"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.u), st)
+            abi("iron_gemv_bf16", ptr(Lw["wg"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.g), *tw, st)
+            abi("iron_gemv_bf16", ptr(Lw["wu"]), c.FF, c.D, ptr(self.xn), B, 0, ptr(self.u), *tw, st)
             abi("iron_silu", ptr(self.g), ptr(self.g), B * c.FF, 0, st)
             abi("iron_mul", ptr(self.g), ptr(self.u), ptr(self.g), B * c.FF, st)
-            abi("iron_gemv_bf16", ptr(Lw["wd"]), c.D, c.FF, ptr(self.g), B, 0, ptr(self.o), st)
+            abi("iron_gemv_bf16", ptr(Lw["wd"]), c.D, c.FF, ptr(self.g), B, 0, ptr(self.o), *tw, st)
             abi("iron_add", ptr(self.x1), ptr(self.o), ptr(self.x), B * c.D, st)
         abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xn), B, c.D, c.eps, 2, st)
         abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xn), B,
-            None if self.logits is None else ptr(self.logits), ptr(self.tok), ptr(self.argmax_ws), st)
+            None if self.logits is None else ptr(self.logits), ptr(self.tok), ptr(self.head_ws),
+            self.head_ws.numel(), st)
         if advance:
             abi("iron_decode_advance", ptr(self.pos), ptr(self.len), ptr(self.off), B, c.HD, st)
 
@@ -195,5 +200,14 @@ class LlamaB200:
             self.len.copy_(self.pos + 1)
             self.off.copy_(self.pos * (2 * self.cfg.HD))
         self.run_step(advance=False)
+        if self.B < 16:  # no tensor-core projection ran; the head workspace holds candidates
+            with torch.cuda.stream(self.stream):
+                return self.tok.cpu()
         with torch.cuda.stream(self.stream):
-            return self.tok.cpu()
+            both = torch.cat([self.tok, _lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)]).cpu()
+        code = int(both[-2]) or int(both[-1])
+        if code:
+            self.tc_ws[:4].zero_()
+            self.head_ws[:4].zero_()
+            _lib.raise_on_status(code, "decode step")
+        return both[:-2]

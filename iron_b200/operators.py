@@ -78,6 +78,7 @@ class GEMVInt8(Operator):
             raise ValueError("M must be a multiple of tile_size_input")
         if self.batch_rows < 1:
             raise ValueError("batch_rows must be at least 1")
+        self._tc_ws = None  # tensor-core scratch, from 16 batch rows on
 
     @property
     def tile_bytes(self) -> int:
@@ -98,11 +99,29 @@ class GEMVInt8(Operator):
     def launch(self, bufs, params, stream):
         wire, x, y = bufs
         wb = self.wire_bytes()
+        ws = self._workspace(x.device)
         for i in range(self.num_batches):
             abi("iron_gemv_w8a16", wire.data_ptr() + i * wb, self.M, self.K, self.group_size,
                 self.tile_size_input, 0, 0, _domain(self.kernel_source),
                 x.data_ptr() + i * self.batch_rows * self.K * 2, self.batch_rows, None,
-                y.data_ptr() + i * self.batch_rows * self.M * 2, stream)
+                y.data_ptr() + i * self.batch_rows * self.M * 2, ptr(ws),
+                0 if ws is None else ws.numel(), stream)
+
+    def _workspace(self, device):
+        """The tensor-core contraction's scratch (16+ batch rows on plain wires); the
+        GEMVs of one call run in order on one stream and share it."""
+        if self.batch_rows < 16 or self.tile_size_input != 1:
+            return None
+        if self._tc_ws is None or self._tc_ws.device != device:
+            self._tc_ws = _lib.tc_workspace([(self.M, self.K)], self.batch_rows, device)
+        return self._tc_ws
+
+    def tc_status(self, clear: bool = True) -> int:
+        """Status word of the tensor-core contraction (0, or the code of a bounded device
+        wait that timed out); synchronous."""
+        if self._tc_ws is None:
+            return 0
+        return int(_lib.lib().iron_tc_status(ptr(self._tc_ws), int(clear)))
 
 
 @dataclass
@@ -150,7 +169,7 @@ class GEMV(Operator):
     def launch(self, bufs, params, stream):
         A, x, y = bufs
         abi("iron_gemv_bf16", ptr(A), self.M, self.K, ptr(x), self.num_batches,
-            1 if self.num_batches > 1 else 0, ptr(y), stream)
+            1 if self.num_batches > 1 else 0, ptr(y), None, 0, stream)
 
 
 # ---------------------------------------------------------------------------
@@ -423,7 +442,7 @@ class QKVHeadDataParallel(Operator):
         abi("iron_qkv_head", ptr(cur), ptr(n_in), ptr(wire), self.group_size, self.tile_size_input,
             _domain(self.kernel_source), ptr(n_qn), ptr(n_kn), ptr(ang), 0, ptr(q), ptr(kv),
             self.D, self.HD, self.Hq, self.Hkv, self.max_seq, 1, self.kv_offset, ptr(off_dev),
-            float(self.epsilon), 1, ptr(self._raw), stream)
+            float(self.epsilon), 1, ptr(self._raw), None, 0, stream)
 
 
 @dataclass
@@ -488,11 +507,11 @@ class SwiGLUMLPDataParallel(Operator):
         g, u = self._tmp[3 * D:3 * D + FF], self._tmp[3 * D + FF:]
         abi("iron_add", ptr(cur), ptr(a), ptr(x1), D, stream)
         abi("iron_rmsnorm", ptr(x1), ptr(n_pf), ptr(hf), 1, D, float(self.epsilon), 0, stream)
-        abi("iron_gemv_bf16", ptr(wg), FF, D, ptr(hf), 1, 0, ptr(g), stream)
-        abi("iron_gemv_bf16", ptr(wu), FF, D, ptr(hf), 1, 0, ptr(u), stream)
+        abi("iron_gemv_bf16", ptr(wg), FF, D, ptr(hf), 1, 0, ptr(g), None, 0, stream)
+        abi("iron_gemv_bf16", ptr(wu), FF, D, ptr(hf), 1, 0, ptr(u), None, 0, stream)
         abi("iron_silu", ptr(g), ptr(g), FF, 1, stream)
         abi("iron_mul", ptr(g), ptr(u), ptr(gh), FF, stream)
-        abi("iron_gemv_bf16", ptr(wd), D, FF, ptr(gh), 1, 0, ptr(d), stream)
+        abi("iron_gemv_bf16", ptr(wd), D, FF, ptr(gh), 1, 0, ptr(d), None, 0, stream)
         abi("iron_add", ptr(x1), ptr(d), ptr(nxt), D, stream)
 
 
@@ -570,14 +589,14 @@ class SwiGLUMLPDataParallelOurs(SwiGLUMLPDataParallel):
             n, n_o, tsi_o, _ = self._wo_tiling()
             abi("iron_mlp_block", ptr(cur), ptr(cx), 1, ptr(n_pf), ptr(wo), tsi_o, self.D // n, n_o,
                 ptr(wg), ptr(wu), tsi_gu, ptr(wd), tsi_d, self.group_size, dom, ptr(a_s), ptr(gh),
-                ptr(nxt), self.D, self.FF, self.QD, 1, float(self.epsilon), stream)
+                ptr(nxt), self.D, self.FF, self.QD, 1, float(self.epsilon), None, 0, stream)
         else:
             cur, a, n_pf, wg, wu, wd, gh, nxt = bufs
             if self._tmp is None or self._tmp.device != cur.device:
                 self._tmp = torch.empty(self.D, dtype=torch.bfloat16, device=cur.device)
             abi("iron_mlp_block", ptr(cur), ptr(a), 0, ptr(n_pf), None, 1, 0, 0,
                 ptr(wg), ptr(wu), tsi_gu, ptr(wd), tsi_d, self.group_size, dom, ptr(self._tmp), ptr(gh),
-                ptr(nxt), self.D, self.FF, 0, 1, float(self.epsilon), stream)
+                ptr(nxt), self.D, self.FF, 0, 1, float(self.epsilon), None, 0, stream)
 
 
 __all__ = [

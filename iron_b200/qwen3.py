@@ -207,7 +207,12 @@ class Qwen3B200:
         self.host_params = torch.zeros(2, B, dtype=torch.int32, pin_memory=True)
         self.attn_ws = torch.empty(_lib.lib().iron_decode_attn_workspace_bytes(B, cfg.Hq, cfg.HD, max_seq),
                                    dtype=torch.uint8, device=dev)
-        self.argmax_ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(B), dtype=torch.uint8, device=dev)
+        # scratch of the batch 16+ tensor-core projections (run one at a time on the
+        # decoder stream, so they share one) and of the lm_head + argmax; each starts
+        # with a status word that _read_tokens brings back with the tokens
+        self.tc_ws = _lib.tc_workspace([(cfg.QKV, cfg.D), (cfg.D, cfg.QD), (cfg.FF, cfg.D), (cfg.D, cfg.FF)],
+                                       B, dev)
+        self.head_ws = _lib.tc_workspace([(cfg.V, cfg.D)], B, dev, lm_head=True)
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
         self._step_launches: dict = {}  # (from_tokens, advance) -> kernels one step launched
@@ -326,19 +331,20 @@ class Qwen3B200:
             kv = self.kv[i]
             abi("iron_qkv_head", ptr(self.x), ptr(Lw["norm1"]), ptr(Lw["wqkv"]), G, 1, 0, ptr(Lw["qn"]),
                 ptr(Lw["kn"]), ptr(self.angles), 1, ptr(self.q), ptr(kv), c.D, c.HD, c.Hq, c.Hkv,
-                self.max_seq, B, 0, ptr(self.off), c.eps, 1, ptr(self.raw), st)
+                self.max_seq, B, 0, ptr(self.off), c.eps, 1, ptr(self.raw), ptr(self.tc_ws),
+                self.tc_ws.numel(), st)
             abi("iron_decode_attn", ptr(self.q), ptr(kv), ptr(self.attn), B, c.Hq, c.Hkv, c.HD,
                 self.max_seq, 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
             abi("iron_mlp_block", ptr(self.x), ptr(self.attn), 1, ptr(Lw["norm2"]), ptr(Lw["wo"]), 1, 0, 0,
                 ptr(Lw["wg"]), ptr(Lw["wu"]), 1, ptr(Lw["wd"]), 1, G, 0, ptr(self.x1), ptr(self.gh),
-                ptr(self.x), c.D, c.FF, c.QD, B, c.eps, st)
+                ptr(self.x), c.D, c.FF, c.QD, B, c.eps, ptr(self.tc_ws), self.tc_ws.numel(), st)
         abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xf), B, c.D, c.eps, 1, st)
         if self.lm_head == "bf16":
             abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xf), B, ptr(self.logits),
-                ptr(self.tok), ptr(self.argmax_ws), st)
+                ptr(self.tok), ptr(self.head_ws), self.head_ws.numel(), st)
         else:
             abi("iron_lm_head_w8_argmax", ptr(w.lm_wire), c.V, c.D, G, ptr(self.xf), B, ptr(self.logits),
-                ptr(self.tok), ptr(self.argmax_ws), st)
+                ptr(self.tok), ptr(self.head_ws), self.head_ws.numel(), st)
         if advance:
             abi("iron_decode_advance", ptr(self.pos), ptr(self.len), ptr(self.off), B, c.HD, st)
 
@@ -360,7 +366,7 @@ class Qwen3B200:
         c, st = self.cfg, self.stream
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         args = (ptr(self.w.embed), c.V, c.D, ptr(self.xf), self.B, ptr(self.logits), ptr(self.tok),
-                ptr(self.argmax_ws), st.cuda_stream)
+                ptr(self.head_ws), self.head_ws.numel(), st.cuda_stream)
         for _ in range(3):
             abi("iron_lm_head_bf16_argmax", *args)
         ev[0].record(st)
@@ -415,8 +421,17 @@ class Qwen3B200:
             if int(both[-1]):
                 self.check()
             return both[:-1]
+        if self.B < 16:  # no tensor-core projection ran; the head workspace holds candidates
+            with torch.cuda.stream(self.stream):
+                return self.tok.cpu()
         with torch.cuda.stream(self.stream):
-            return self.tok.cpu()
+            both = torch.cat([self.tok, _lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)]).cpu()
+        code = int(both[-2]) or int(both[-1])
+        if code:
+            self.tc_ws[:4].zero_()
+            self.head_ws[:4].zero_()
+            _lib.raise_on_status(code, "decode step")
+        return both[:-2]
 
     def _put_inputs(self, tokens, pos):
         """(token, position) per stream -> device in one copy from pinned memory."""

@@ -186,26 +186,28 @@ class Qwen3TP(Qwen3B200):
             kv = self.kv[i]
             abi("iron_qkv_head", ptr(self.x), ptr(Lw["norm1"]), ptr(Lw["wqkv"]), G, 1, 0, ptr(Lw["qn"]),
                 ptr(Lw["kn"]), ptr(self.angles), 1, ptr(self.q), ptr(kv), c.D, c.HD, c.Hq, c.Hkv,
-                self.max_seq, B, 0, ptr(self.off), c.eps, 1, ptr(self.raw), st)
+                self.max_seq, B, 0, ptr(self.off), c.eps, 1, ptr(self.raw), ptr(self.tc_ws),
+                self.tc_ws.numel(), st)
             abi("iron_decode_attn", ptr(self.q), ptr(kv), ptr(self.attn), B, c.Hq, c.Hkv, c.HD,
                 self.max_seq, 0, 0, 1, ptr(self.len), ptr(self.attn_ws), self.attn_ws.numel(), st)
             # O, row-parallel: float32 partials -> sum over ranks -> x1 = bf16(x + bf16(sum))
             abi("iron_gemv_w8a16_ex", ptr(Lw["wo"]), None, c.D, c.QD, G, 0, ptr(self.attn), c.QD, B, None,
-                0.0, 0, None, EPI_F32, ptr(self.part), c.D, st)
+                0.0, 0, None, EPI_F32, ptr(self.part), c.D, ptr(self.tc_ws), self.tc_ws.numel(), st)
             yield ("sum", self.part)
             abi("iron_resid_add_f32", ptr(self.x), ptr(self.part), ptr(self.x1), B * c.D, st)
             # gate/up, column-parallel, RMSNorm(x1) in the prologue
             abi("iron_gemv_w8a16_ex", ptr(Lw["wg"]), ptr(Lw["wu"]), c.FF, c.D, G, 0, ptr(self.x1), c.D, B,
-                ptr(Lw["norm2"]), c.eps, 0, None, EPI_STORE, ptr(self.gh), c.FF, st)
+                ptr(Lw["norm2"]), c.eps, 0, None, EPI_STORE, ptr(self.gh), c.FF, ptr(self.tc_ws),
+                self.tc_ws.numel(), st)
             # down, row-parallel: x = bf16(x1 + bf16(sum))
             abi("iron_gemv_w8a16_ex", ptr(Lw["wd"]), None, c.D, c.FF, G, 0, ptr(self.gh), c.FF, B, None,
-                0.0, 0, None, EPI_F32, ptr(self.part), c.D, st)
+                0.0, 0, None, EPI_F32, ptr(self.part), c.D, ptr(self.tc_ws), self.tc_ws.numel(), st)
             yield ("sum", self.part)
             abi("iron_resid_add_f32", ptr(self.x1), ptr(self.part), ptr(self.x), B * c.D, st)
         abi("iron_rmsnorm", ptr(self.x), ptr(w.final_norm), ptr(self.xf), B, c.D, c.eps, 1, st)
         # vocabulary-parallel greedy argmax
         abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(self.xf), B, ptr(self.logits),
-            ptr(self.tok), ptr(self.argmax_ws), st)
+            ptr(self.tok), ptr(self.head_ws), self.head_ws.numel(), st)
         abi("iron_argmax_pair", ptr(self.logits), c.V, B, ptr(self.tok), self.v0, ptr(self.pairs), st)
         yield ("gather", self.gathered, self.pairs)
         abi("iron_argmax_merge", ptr(self.gathered), self.world, B, ptr(self.tok), st)

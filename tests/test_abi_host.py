@@ -34,9 +34,9 @@ def test_error_reporting_without_gpu():
     rejected call launches nothing (iron_launch_count stays put)."""
     c0 = _lib.launch_count()
     with pytest.raises(_lib.IronError, match="group must be"):
-        _lib.call("iron_gemv_w8a16", 16, 64, 1024, 48, 1, 0, 0, 0, 16, 1, None, 16, None)
+        _lib.call("iron_gemv_w8a16", 16, 64, 1024, 48, 1, 0, 0, 0, 16, 1, None, 16, None, 0, None)
     with pytest.raises(_lib.IronError, match="batch 0 below 1"):
-        _lib.call("iron_lm_head_bf16_argmax", 16, 8, 8, 16, 0, None, 16, 16, None)
+        _lib.call("iron_lm_head_bf16_argmax", 16, 8, 8, 16, 0, None, 16, 16, 0, None)
     assert _lib.launch_count() == c0 >= 0
 
 
@@ -92,6 +92,6 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libiron_b200.so")
     monkeypatch.setattr(_lib, "_LIB", None)
     with pytest.raises(ImportError, match="not built"):
-        _lib.call("iron_gemv_w8a16", 16, 64, 1024, 32, 1, 0, 0, 0, 16, 1, None, 16, None)
+        _lib.call("iron_gemv_w8a16", 16, 64, 1024, 32, 1, 0, 0, 0, 16, 1, None, 16, None, 0, None)
     with pytest.raises(ImportError, match="not built"):
         _lib.launch_count()

@@ -38,12 +38,20 @@ def _check(out, q, s_bits, x, G, what):
     assert_close(np.asarray(out, np.float64), exact, what=f"{what}: bf16 gate vs exact")
 
 
-def _gemv(wire, M, K, G, domain, x, residual=None):
+def _gemv(wire, M, K, G, domain, x, residual=None, ws="new", stream=None, sync=True):
+    """One projection; ws: a workspace tensor, "new" (a fresh one) or None (no workspace:
+    the exact launches of 8 rows)."""
     B = x.shape[0]
+    if isinstance(ws, str):
+        ws = _lib.tc_workspace([(M, K)], B, "cuda")
     y = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
     _lib.call("iron_gemv_w8a16", wire.data_ptr(), M, K, G, 1, 0, 0, domain, x.data_ptr(), B,
-              None if residual is None else residual.data_ptr(), y.data_ptr(), _lib.stream_ptr())
-    torch.cuda.synchronize()
+              None if residual is None else residual.data_ptr(), y.data_ptr(),
+              None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _lib.stream_ptr(stream))
+    if sync:
+        torch.cuda.synchronize()
+        if ws is not None:
+            assert _lib.lib().iron_tc_status(ws.data_ptr(), 0) == 0
     return y
 
 
@@ -52,15 +60,17 @@ def _gemv(wire, M, K, G, domain, x, residual=None):
                                             (300, 2048, 128, 64, 0), (3072, 1024, 32, 256, 0),
                                             (1024, 3072, 32, 33, 0)])
 def test_tc_projection_matches_dequantised_reference(M, K, G, B, domain):
-    assert _lib.lib().iron_tc_status(1) == 0
     torch.manual_seed(M + K + B)
     w = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
     wire = quantize_to_wire(w, G, domain=domain)
     q, s = wire_to_numpy(quantize_to_wire(w, G, domain=0), M, K, G)
     x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
-    y1 = _gemv(wire, M, K, G, domain, x)
-    y2 = _gemv(wire, M, K, G, domain, x)
-    assert _lib.lib().iron_tc_status(0) == 0
+    ws = _lib.tc_workspace([(M, K)], B, "cuda")
+    y1 = _gemv(wire, M, K, G, domain, x, ws=ws)
+    # the last split of each 128-row tile puts its arrival counter back to zero, so the
+    # workspace is ready for the next launch with nothing to clear
+    assert int(ws[:256 + 4 * ((M + 127) // 128)].count_nonzero()) == 0
+    y2 = _gemv(wire, M, K, G, domain, x, ws=ws)
     assert torch.equal(y1, y2), "not deterministic"
     _check(host(y1), q, s, host(x), G, f"{M}x{K} g{G} b{B}")
 
@@ -83,8 +93,9 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     assert np.array_equal(host(y), want)
     # float32 partial sums (epilogue 2) round to the bf16 result
     y32 = torch.empty(B, M, dtype=torch.float32, device="cuda")
+    tw = _lib.tc_workspace([(M, K)], B, "cuda")
     _lib.call("iron_gemv_w8a16_ex", gw.data_ptr(), None, M, K, G, 0, x.data_ptr(), K, B, None, 0.0, 0, None, 2,
-              y32.data_ptr(), M, st)
+              y32.data_ptr(), M, tw.data_ptr(), tw.numel(), st)
     torch.cuda.synchronize()
     assert np.array_equal(rnd(host(y32)), base)
     _check(host(y32), qg, sg, host(x), G, "f32 epilogue")
@@ -92,9 +103,9 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     nw = (1 + 0.1 * torch.randn(K, device="cuda")).to(torch.bfloat16)
     gh = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
     _lib.call("iron_gemv_w8a16_ex", gw.data_ptr(), uw.data_ptr(), M, K, G, 0, x.data_ptr(), K, B, nw.data_ptr(),
-              1e-6, 0, None, 0, gh.data_ptr(), M, st)
+              1e-6, 0, None, 0, gh.data_ptr(), M, tw.data_ptr(), tw.numel(), st)
     torch.cuda.synchronize()
-    assert _lib.lib().iron_tc_status(0) == 0
+    assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
     h = ops.rms_norm_f32(host(x), host(nw), 1e-6)
     g = rnd(h.astype(np.float64) @ _deq(qg, sg, G).T)
     u = rnd(h.astype(np.float64) @ _deq(qu, su, G).T)
@@ -104,3 +115,45 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     err = np.abs(got - want)
     lim = 2.0 ** -6 * np.abs(want) + 1e-4
     assert np.mean(err <= lim) >= 0.999 and np.max(err) <= 0.05, f"pair: {np.mean(err <= lim):.4f}, max {err.max()}"
+
+
+def test_tc_without_workspace_runs_the_exact_launches():
+    """No workspace: batch 16+ runs the exact kernel in launches of 8 rows, whose every
+    output is the exact dequantised sum rounded once to bf16."""
+    torch.manual_seed(8)
+    M, K, G, B = 2048, 1024, 32, 24
+    w = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    wire = quantize_to_wire(w, G)
+    q, s = wire_to_numpy(wire, M, K, G)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    y = _gemv(wire, M, K, G, 0, x, ws=None)
+    assert np.array_equal(host(y), rnd(ops.gemv_int8_exact(q, s, host(x).astype(np.float64))))
+    # a workspace too small for the split-K counters takes the same exact path
+    assert torch.equal(_gemv(wire, M, K, G, 0, x, ws=_lib.workspace(256, "cuda")), y)
+
+
+def test_tc_concurrent_projections_on_two_streams():
+    """Two batch-32 projections in flight at once on two streams, each with its own
+    workspace, give the results each gives alone: the kernels share no global scratch."""
+    torch.manual_seed(9)
+    G, B = 32, 32
+    shapes = [(6144, 1024), (1024, 3072)]
+    cases = []
+    for M, K in shapes:
+        w = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+        x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+        wire = quantize_to_wire(w, G)
+        cases.append((M, K, wire, x, _gemv(wire, M, K, G, 0, x)))
+    streams = [torch.cuda.Stream() for _ in cases]
+    wss = [_lib.tc_workspace([(M, K)], B, "cuda") for M, K, *_ in cases]
+    torch.cuda.synchronize()
+    outs = [[] for _ in cases]
+    for _ in range(8):  # interleaved launches: the two kernels overlap on the GPU
+        for i, (M, K, wire, x, _) in enumerate(cases):
+            with torch.cuda.stream(streams[i]):
+                outs[i].append(_gemv(wire, M, K, G, 0, x, ws=wss[i], stream=streams[i], sync=False))
+    torch.cuda.synchronize()
+    for i, (M, K, wire, x, want) in enumerate(cases):
+        assert _lib.lib().iron_tc_status(wss[i].data_ptr(), 0) == 0
+        for y in outs[i]:
+            assert torch.equal(y, want), f"projection {M}x{K} changed under a concurrent one"

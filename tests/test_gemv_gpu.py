@@ -22,10 +22,12 @@ pytestmark = pytest.mark.gpu
 
 def _run_w8(wire_u8, M, K, group, tile_m, domain, x, batch=1, residual=None, rpc=0, tpc=0):
     y = torch.empty(batch, M, dtype=torch.bfloat16, device="cuda")
+    tw = _lib.tc_workspace([(M, K)], batch, "cuda")
     _lib.call("iron_gemv_w8a16", wire_u8.data_ptr(), M, K, group, tile_m, rpc, tpc, domain,
               x.data_ptr(), batch, None if residual is None else residual.data_ptr(), y.data_ptr(),
-              _lib.stream_ptr())
+              tw.data_ptr(), tw.numel(), _lib.stream_ptr())
     torch.cuda.synchronize()
+    assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
     return host(y)
 
 
@@ -198,9 +200,9 @@ def test_lm_head_bf16_argmax(batch):
     x[0] = E[777].float() * 40
     logits = torch.empty(batch, V, dtype=torch.bfloat16, device="cuda")
     tok = torch.empty(batch, dtype=torch.int32, device="cuda")
-    ws = torch.empty(_lib.lib().iron_argmax_workspace_bytes(batch), dtype=torch.uint8, device="cuda")
+    ws = _lib.tc_workspace([(V, D)], batch, "cuda", lm_head=True)
     _lib.call("iron_lm_head_bf16_argmax", E.data_ptr(), V, D, x.data_ptr(), batch, logits.data_ptr(),
-              tok.data_ptr(), ws.data_ptr(), _lib.stream_ptr())
+              tok.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
     torch.cuda.synchronize()
     lg = host(logits)
     for b in range(batch):
@@ -208,13 +210,22 @@ def test_lm_head_bf16_argmax(batch):
     assert int(tok[0]) == 777
     want = ops.gemv_bf16(host(E)[:4096], host(x)[0])
     assert_ulps(lg[0][:4096], want, max_ulp=1, frac_exact=0.95, what="logits")
-    if batch >= 16:  # the tensor-core path with no logits buffer gives the same tokens
+    if batch >= 16:
+        # the tensor-core path with no logits buffer (kept in the workspace) gives the same tokens
         tok2 = torch.empty(batch, dtype=torch.int32, device="cuda")
         _lib.call("iron_lm_head_bf16_argmax", E.data_ptr(), V, D, x.data_ptr(), batch, None, tok2.data_ptr(),
-                  ws.data_ptr(), _lib.stream_ptr())
+                  ws.data_ptr(), ws.numel(), _lib.stream_ptr())
         torch.cuda.synchronize()
         assert torch.equal(tok, tok2)
-        assert _lib.lib().iron_tc_status(0) == 0
+        assert _lib.lib().iron_tc_status(ws.data_ptr(), 0) == 0
+        # a workspace of the argmax candidates only: the launches of 8 rows, same tokens
+        small = _lib.workspace(_lib.lib().iron_argmax_workspace_bytes(batch), "cuda")
+        tok3 = torch.empty(batch, dtype=torch.int32, device="cuda")
+        _lib.call("iron_lm_head_bf16_argmax", E.data_ptr(), V, D, x.data_ptr(), batch, None, tok3.data_ptr(),
+                  small.data_ptr(), small.numel(), _lib.stream_ptr())
+        torch.cuda.synchronize()
+        near = sum(int(tok3[b]) != int(tok[b]) and lg[b][int(tok3[b])] == lg[b][int(tok[b])] for b in range(batch))
+        assert sum(int(tok3[b]) != int(tok[b]) for b in range(batch)) == near
 
 
 def test_bf16_gemv_shared_weight_batch32_tensor_cores():
@@ -223,7 +234,10 @@ def test_bf16_gemv_shared_weight_batch32_tensor_cores():
     A = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
     x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
     y = torch.empty(B, M, dtype=torch.bfloat16, device="cuda")
-    _lib.call("iron_gemv_bf16", A.data_ptr(), M, K, x.data_ptr(), B, 0, y.data_ptr(), _lib.stream_ptr())
+    tw = _lib.tc_workspace([(M, K)], B, "cuda")
+    _lib.call("iron_gemv_bf16", A.data_ptr(), M, K, x.data_ptr(), B, 0, y.data_ptr(), tw.data_ptr(), tw.numel(),
+              _lib.stream_ptr())
     torch.cuda.synchronize()
+    assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
     for b in (0, 13, 31):
         assert_ulps(host(y[b]), ops.gemv_bf16(host(A), host(x[b])), max_ulp=1, frac_exact=0.95, what=f"row {b}")

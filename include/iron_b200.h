@@ -220,6 +220,21 @@ int iron_decode_attn_static(const uint16_t* q, const uint16_t* kv, uint16_t* out
                             int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
                             const int32_t* seq_lens_dev, void* stream);
 
+/* ---- multi-query attention over one KV stream ------------------------------------
+ * The verify mode of DecodeAttention (batch_queries / num_new_tokens / causal,
+ * decode_attn/op.py:40-56; golden cpu_reference_batch, decode_attn/test_batch.py:31-46)
+ * and the causal attention of a prompt (MHA, mha/op.py:21-153; golden
+ * mha/reference.py:26-93).  q, out: (T, H, HD) token-major.  Token t sits at position
+ * base + t and attends the positions j < kv_len, and with causal != 0 only j <= base + t.
+ * base_dev (int32, may be NULL) overrides base: the S_kv_base runtime parameter.
+ * kv: ONE stream's cache (KV, 2*max_seq*HD) in kv_layout 0/1/2 as iron_decode_attn.
+ * HD 64 or 128; q and kv 16-byte aligned.  Split-KV partials in `workspace`
+ * (iron_attn_mq_workspace_bytes), merged by a second pass. */
+int64_t iron_attn_mq_workspace_bytes(int T, int H, int KV, int HD, int max_seq);
+int iron_attn_mq(const uint16_t* q, const uint16_t* kv, uint16_t* out, int T, int H, int KV, int HD,
+                 int max_seq, int kv_layout, int block_kv, int base, const int32_t* base_dev, int kv_len,
+                 int causal, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ---- fused SwiGLU MLP block ---------------------------------------------------
  * SwiGLUMLPDataParallelOurs (iron/operators/swiglu_mlp_dp/op_ours.py:47-582;
  * golden swiglu_mlp_dp/test.py:79-91, reference.py:8-67):

@@ -48,6 +48,8 @@ SIGNATURES: dict[str, tuple] = {
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),
     "iron_decode_attn_static_capacity_bytes": (I64, []),
     "iron_decode_attn_static": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P]),
+    "iron_attn_mq_workspace_bytes": (I64, [I, I, I, I, I]),
+    "iron_attn_mq": (I, [P, P, P, I, I, I, I, I, I, I, I, P, I, I, P, I64, P]),
     "iron_qwen3_sync_words": (I, [P]),
     "iron_qwen3_attn_ws_bytes": (I64, [P]),
     "iron_qwen3_cand_bytes": (I64, []),

@@ -285,7 +285,10 @@ class SiLU(Operator):
 class DecodeAttention(Operator):
     """Fused single-query GQA decode attention (iron/operators/decode_attn/op.py:20-181).
 
-    Split-KV flash decoding.  ``use_runtime_seq_len`` reads the valid length
+    Split-KV flash decoding.  ``batch_queries`` > 0 is the multi-query verify mode
+    (op.py:40-56): ``num_new_tokens`` queries at positions ``S_kv_base`` .. (runtime
+    parameter), causal or over the whole cache (``iron_attn_mq``).
+    ``use_runtime_seq_len`` reads the valid length
     from the ``S_kv_eff`` runtime parameter (qwen3_npu_int8.py:609); otherwise
     every cached position is valid.  KV layouts: per-token ``[K_t|V_t]``
     (``kv_token_interleaved``, the default), IRON's legacy ``[K_block|V_block]``
@@ -324,7 +327,6 @@ class DecodeAttention(Operator):
                                  f"of batch_queries ({self.batch_queries})")
             if not self.use_runtime_seq_len:
                 raise ValueError("batch mode requires use_runtime_seq_len")
-            raise NotImplementedError("multi-query (batch_queries) verify mode is not implemented on B200")
         if self.kv_layout != "combined":
             raise NotImplementedError("only the combined KV argument is implemented on B200")
         if self.num_heads % self.num_kv_heads:
@@ -335,6 +337,8 @@ class DecodeAttention(Operator):
 
     @property
     def runtime_params(self):
+        if self.batch_queries:  # verify mode: the cached-token count before the new block
+            return ("S_kv_base",)
         return ("S_kv_eff",) if self.use_runtime_seq_len else ()
 
     @property
@@ -344,13 +348,22 @@ class DecodeAttention(Operator):
         return 0 if self.kv_token_interleaved else 2
 
     def get_arg_spec(self):
+        """Verify mode (op.py:156-181): Q is (num_new_tokens*H, D) token-major and O has
+        max(out_buffer_tokens, num_new_tokens) tokens, of which num_new_tokens are written."""
         H, KV, D, S = self.num_heads, self.num_kv_heads, self.head_dim, self.seq_len_kv
-        return [AIERuntimeArgSpec("in", (H, D)),
+        q_rows = self.num_new_tokens * H if self.batch_queries else H
+        o_tokens = max(self.out_buffer_tokens, self.num_new_tokens) if self.batch_queries else 1
+        return [AIERuntimeArgSpec("in", (q_rows, D)),
                 AIERuntimeArgSpec("in", (KV, 2 * S * D)),
-                AIERuntimeArgSpec("out", (H, D))]
+                AIERuntimeArgSpec("out", (o_tokens * H, D))]
 
     def workspace(self, device) -> torch.Tensor:
-        n = _lib.lib().iron_decode_attn_workspace_bytes(1, self.num_heads, self.head_dim, self.seq_len_kv)
+        L = _lib.lib()
+        if self.batch_queries:
+            n = L.iron_attn_mq_workspace_bytes(self.num_new_tokens, self.num_heads, self.num_kv_heads,
+                                               self.head_dim, self.seq_len_kv)
+        else:
+            n = L.iron_decode_attn_workspace_bytes(1, self.num_heads, self.head_dim, self.seq_len_kv)
         if self._ws is None or self._ws.numel() < n or self._ws.device != device:
             self._ws = torch.empty(n, dtype=torch.uint8, device=device)
         return self._ws
@@ -358,6 +371,13 @@ class DecodeAttention(Operator):
     def launch(self, bufs, params, stream):
         q, kv, o = bufs
         ws = self.workspace(q.device)
+        if self.batch_queries:
+            # the query groups of the reference (batch_queries per KV pass) are one
+            # kernel here: every CTA streams its positions once for 64 (token, head) rows
+            abi("iron_attn_mq", ptr(q), ptr(kv), ptr(o), self.num_new_tokens, self.num_heads,
+                self.num_kv_heads, self.head_dim, self.seq_len_kv, self.layout_code, self.block_kv, 0,
+                ptr(params.slot("S_kv_base")), self.seq_len_kv, int(self.causal), ptr(ws), ws.numel(), stream)
+            return
         dev_len = params.slot("S_kv_eff") if self.use_runtime_seq_len else None
         abi("iron_decode_attn", ptr(q), ptr(kv), ptr(o), 1, self.num_heads, self.num_kv_heads,
             self.head_dim, self.seq_len_kv, self.layout_code, self.block_kv, self.seq_len_kv,

@@ -72,6 +72,19 @@ def test_qkv_and_attention_arg_specs():
     assert a.get_params_used() == ("S_kv_eff",)
     with pytest.raises(ValueError):
         DecodeAttention(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=500)
+    # verify mode (decode_attn/op.py:156-181): token-major Q of num_new_tokens*H rows, a
+    # taller O when out_buffer_tokens asks, and the S_kv_base runtime parameter
+    v = DecodeAttention(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=256, block_kv=32,
+                        use_runtime_seq_len=True, batch_queries=8, num_new_tokens=16, out_buffer_tokens=32)
+    assert [s.shape for s in v.get_arg_spec()] == [(16 * 16, 128), (8, 2 * 256 * 128), (32 * 16, 128)]
+    assert v.get_params_used() == ("S_kv_base",)
+    assert "m8" in v.name and "new16" in v.name
+    with pytest.raises(ValueError, match="multiple"):
+        DecodeAttention(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=256, use_runtime_seq_len=True,
+                        batch_queries=8, num_new_tokens=12)
+    with pytest.raises(ValueError, match="use_runtime_seq_len"):
+        DecodeAttention(num_heads=16, num_kv_heads=8, head_dim=128, seq_len_kv=256, batch_queries=8,
+                        num_new_tokens=16)
 
 
 def test_sequence_layout_slices_and_conflicts():

@@ -9,7 +9,7 @@ from iron_b200.operators import (DecodeAttention, ElementwiseAdd, ElementwiseMul
                                  RMSNorm, SiLU, SwiGLUMLPDataParallel, SwiGLUMLPDataParallelOurs)
 from iron_b200.test_utils import verify_buffer
 from oracle import ops
-from oracle.bf16 import from_bits, rnd
+from oracle.bf16 import from_bits, rnd, round_bits
 
 from helpers import assert_close, assert_ulps, dev_bf16, dev_u8, host
 
@@ -165,6 +165,115 @@ def test_decode_attention_layouts_and_unaligned_lengths(layout, L):
     want = ops.decode_attention(Q, K, V, L - 1, D, H, KV)
     assert_close(host(o).reshape(H, D), want, what=f"L={L}")
     assert not np.isnan(host(o)).any()
+
+
+def _pack_kv(K, V, layout, block=32):
+    """One stream's cache (KV, 2*S*D) from K, V (KV, S, D) in the three layouts."""
+    KV, S, D = K.shape
+    if layout == "token":
+        return np.stack([K, V], axis=2).reshape(KV, 2 * S * D)
+    if layout == "block":
+        return np.concatenate([K.reshape(KV, S // block, block, D), V.reshape(KV, S // block, block, D)],
+                              axis=2).reshape(KV, -1)
+    return np.concatenate([K, V], axis=1).reshape(KV, -1)
+
+
+def _near_rounding(got, want, what):
+    """bf16 outputs against a float reference: the float32 sums of the kernel differ
+    from the reference's only in order, so almost every output is the reference's
+    rounding and the rest one ulp off -- except values so near zero that the absolute
+    summation error spans several of their ulps, held to 1e-4 absolute instead."""
+    got = np.asarray(got, np.float32).reshape(-1)
+    want = np.asarray(want, np.float64).reshape(-1)
+    g = round_bits(got).astype(np.int32)
+    w = round_bits(rnd(want.astype(np.float32))).astype(np.int32)
+    d = np.abs(np.where(g >= 0x8000, 0x8000 - g, g) - np.where(w >= 0x8000, 0x8000 - w, w))
+    assert np.mean(d == 0) >= 0.9, f"{what}: only {np.mean(d == 0):.4f} bit-exact"
+    assert np.mean(d <= 1) >= 0.995, f"{what}: {np.mean(d <= 1):.4f} within one ulp"
+    far = d > 2
+    assert np.all(np.abs(got[far] - want[far]) <= 1e-4), f"{what}: {np.abs(got[far] - want[far]).max()}"
+
+
+def _verify_op(H, KV, D, S, T, causal, layout, block=32, **kw):
+    return DecodeAttention(num_heads=H, num_kv_heads=KV, head_dim=D, seq_len_kv=S, block_kv=block,
+                           use_runtime_seq_len=True, batch_queries=T if T % 8 else 8, num_new_tokens=T,
+                           causal=causal, kv_token_interleaved=layout != "block", kv_halves=layout == "halves",
+                           **kw)
+
+
+@pytest.mark.parametrize("layout", ["token", "block", "halves"])
+@pytest.mark.parametrize("tag", ["causal", "noncausal"])
+def test_decode_attention_verify_mode_against_reference_golden(golden, tag, layout):
+    """The multi-query verify mode (decode_attn/op.py:40-56) on the batch test's golden
+    (decode_attn/test_batch.py:31-46): 16 new tokens at positions 192..207 of a 256-position
+    cache; causal (query m sees [0, 192 + m]) and over the whole cache.  The golden is
+    float32; the bf16 output is held to the decode gate and to its rounding."""
+    g = golden("decode_attn_batch")
+    N, H, KV, D, S, base = (int(v) for v in g["dims"])
+    Q, K, V = (from_bits(g[k]) for k in ("Q", "K", "V"))
+    op = _verify_op(H, KV, D, S, N, tag == "causal", layout)
+    call = op.get_callable()
+    call.params.write("S_kv_base", base)
+    call.params.sync()
+    o = _out(N * H * D)
+    call(dev_bf16(Q).reshape(N * H, D), dev_bf16(_pack_kv(K, V, layout)), o.reshape(N * H, D))
+    torch.cuda.synchronize()
+    want = g[f"O_{tag}"]
+    got = host(o).reshape(N, H, D)
+    assert_close(got, want, what=f"verify {tag} {layout}")
+    _near_rounding(got, want, f"verify {tag} {layout}")
+    _near_rounding(got, ops.decode_attention_batch(Q, K, V, base, tag == "causal", D, H, KV), "vs oracle")
+
+
+def test_decode_attention_verify_mask_matters():
+    """Causal and whole-cache outputs differ (decode_attn/test_batch.py main: the mask
+    must do something), and a runtime base written later takes effect without a rebuild."""
+    rng = np.random.default_rng(3)
+    H, KV, D, S, T = 16, 8, 128, 256, 16
+    Q = rnd(rng.standard_normal((T, H, D)).astype(np.float32))
+    K = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    V = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    kv = dev_bf16(_pack_kv(K, V, "token"))
+    outs = {}
+    for causal in (True, False):
+        call = _verify_op(H, KV, D, S, T, causal, "token").get_callable()
+        for base in (192, 40):
+            call.params.write("S_kv_base", base)
+            call.params.sync()
+            o = _out(T * H * D)
+            call(dev_bf16(Q).reshape(T * H, D), kv, o.reshape(T * H, D))
+            torch.cuda.synchronize()
+            outs[causal, base] = host(o).reshape(T, H, D)
+            want = ops.decode_attention_batch(Q, K, V, base, causal, D, H, KV)
+            assert_close(outs[causal, base], want, what=f"causal={causal} base={base}")
+    assert not np.array_equal(outs[True, 192], outs[False, 192])
+    assert not np.array_equal(outs[True, 192], outs[True, 40])
+    assert np.array_equal(outs[False, 192], outs[False, 40])
+
+
+@pytest.mark.parametrize("T,H,KV,D,S,base,causal", [
+    (1, 16, 8, 128, 512, 300, True), (5, 16, 8, 128, 512, 507, True), (37, 32, 8, 128, 640, 100, True),
+    (100, 16, 8, 64, 256, 0, True), (33, 8, 8, 128, 320, 77, False), (64, 16, 4, 128, 1024, 960, True)])
+def test_attn_mq_shapes_against_oracle(T, H, KV, D, S, base, causal):
+    """iron_attn_mq over ragged token counts (row blocks past the last row), GQA 1..8,
+    head_dim 64, prompts from position 0 and blocks ending at the cache's end, against
+    the oracle's per-query decode attention."""
+    from iron_b200 import _lib
+    rng = np.random.default_rng(T * 1000 + S)
+    Q = rnd(rng.standard_normal((T, H, D)).astype(np.float32))
+    K = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    V = rnd(rng.standard_normal((KV, S, D)).astype(np.float32))
+    kv = dev_bf16(_pack_kv(K, V, "token"))
+    o = torch.full((T, H, D), float("nan"), dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(_lib.lib().iron_attn_mq_workspace_bytes(T, H, KV, D, S), dtype=torch.uint8, device="cuda")
+    _lib.call("iron_attn_mq", dev_bf16(Q).data_ptr(), kv.data_ptr(), o.data_ptr(), T, H, KV, D, S, 0, 0, base,
+              None, S, int(causal), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    want = ops.decode_attention_batch(Q, K, V, base, causal, D, H, KV)
+    got = host(o)
+    assert not np.isnan(got).any()
+    assert_close(got, want, what=f"T{T} H{H} KV{KV} D{D}")
+    _near_rounding(got, want, f"T{T} H{H} KV{KV} D{D}")
 
 
 def test_mlp_kernel_golden_biased_wire(golden):

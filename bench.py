@@ -4,8 +4,8 @@
 Workload (Qwen3-0.6B, the headline configuration): 28 layers, hidden 1024, 16/8 heads, head_dim 128,
 SwiGLU 3072, vocab 151936 with a tied bf16 embedding/lm_head, projection
 weights int8 RTN in groups of 32 (synthetic, seeded), batch 1.  A 1024-token
-random prompt is prefilled token by token (as the reference does), then greedy
-decode steps are timed.  One step = one decoded token.  Every step streams
+random prompt is prefilled (all prompt rows of a layer at once, Qwen3B200.prefill;
+reported as prefill_s), then greedy decode steps are timed.  One step = one decoded token.  Every step streams
 ~0.78 GB of weights + the KV cache from HBM, far more than the 126 MB L2, so no
 L2 flush is needed between steps.
 
@@ -64,7 +64,9 @@ def parse():
                          "config 5, --batch streams per GPU (default 64) with ragged synthetic KV "
                          "lengths U[256, 8192], replicas across GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-tokens", type=int, default=2, help="oracle tokens in the CPU baseline sample")
+    ap.add_argument("--oracle-steps", type=int, default=32,
+                    help="teacher-forced oracle steps (greedy top-1 agreement; also the CPU baseline sample)")
+    ap.add_argument("--no-extra", action="store_true", help="no bs32 / tp sub-records")
     ap.add_argument("--phases", action="store_true",
                     help="phase breakdown of the one-launch step (a profiling copy of the library), not a bench line")
     ap.add_argument("--breakdown", action="store_true",
@@ -174,28 +176,44 @@ def token_bytes(cfg, group, ctx, batch=1):
 # ---------------------------------------------------------------------------
 # CPU oracle sample (test infrastructure: the checker and the CPU baseline only)
 # ---------------------------------------------------------------------------
-def cpu_sample(weights_np, kv_np, shape, pos, token, n_tokens, threads, angles=None):
-    """Time the composed CPU oracle (oracle/qwen3.py) for ``n_tokens`` decode steps at
-    ``pos`` on the GPU run's own weights and KV cache.  Returns (tokens/s, info, logits)."""
+def oracle_replay(weights_np, kv_np, shape, pos, inputs, gpu_next, threads, angles=None):
+    """Teacher-forced replay of ``len(inputs)`` GPU decode steps on the composed CPU oracle
+    (oracle/qwen3.py), from the GPU's own weights and K/V cache at ``pos``: step i feeds
+    the GPU's input token ``inputs[i]`` at ``pos + i`` (the oracle keeps its own K/V from
+    there on) and compares the oracle's greedy token with the GPU's ``gpu_next[i]``.  A
+    disagreement counts as a near-tie when the two tokens' oracle logits differ by no
+    more than the bf16 gate (atol 1e-2 + rtol 2e-2 of the larger).  Returns (tokens/s of
+    the oracle, threads used, agreement record)."""
+    import numpy as np
     from oracle import ops
     from oracle.qwen3 import OracleQwen3
     used = ops.set_threads(threads)
     orc = OracleQwen3(shape, weights_np, kv_np.shape[2], angles=angles)
     orc.kv[...] = kv_np
-    t_layer, t_head = [], []
-    logits = None
-    for _ in range(n_tokens):
-        x = orc.embed(token)
-        for i in range(shape.n_layers):
-            t0 = time.perf_counter()
-            x = orc.layer(i, x, pos)
-            t_layer.append(time.perf_counter() - t0)
+    t_tok, agree, near = [], 0, 0
+    for i, (tin, tgpu) in enumerate(zip(inputs, gpu_next)):
         t0 = time.perf_counter()
-        xf = ops.rms_norm_ref(x.reshape(1, -1), weights_np["final_norm"], weighted=True, eps=shape.eps).reshape(-1)
-        logits = ops.gemv_bf16(weights_np["embed"], xf)
-        t_head.append(time.perf_counter() - t0)
-    per_token = statistics.mean(t_layer) * shape.n_layers + statistics.mean(t_head)
-    return 1.0 / per_token, used, logits
+        logits, want = orc.step(orc.embed(tin), pos + i)
+        t_tok.append(time.perf_counter() - t0)
+        if want == tgpu:
+            agree += 1
+        elif abs(float(logits[want]) - float(logits[tgpu])) <= 1e-2 + 2e-2 * float(np.abs(logits[want])):
+            near += 1
+    n = len(inputs)
+    rec = {"steps": n, "from_position": pos, "top1_agree": agree / n, "near_ties": near,
+           "top1_agree_or_near_tie": (agree + near) / n,
+           "method": "teacher-forced: the oracle steps on the GPU's input tokens from the GPU's K/V cache"}
+    return 1.0 / statistics.mean(t_tok), used, rec
+
+
+def oracle_spot(weights_np, kv_np, shape, pos, token, threads, angles=None):
+    """One oracle decode token at ``pos`` from a GPU K/V cache: its greedy token."""
+    from oracle import ops
+    from oracle.qwen3 import OracleQwen3
+    ops.set_threads(threads)
+    orc = OracleQwen3(shape, weights_np, kv_np.shape[2], angles=angles)
+    orc.kv[...] = kv_np
+    return orc.step(orc.embed(token), pos)[1]
 
 
 # ---------------------------------------------------------------------------
@@ -272,6 +290,43 @@ def run_reference(args, rank):
 
 # ---------------------------------------------------------------------------
 def run_ours(args, rank, world, local_rank):
+    """The headline line (Qwen3-0.6B, ``--batch`` streams per GPU, replicas across the
+    world), with sub-records under ``extra``: ``bs32`` (the same workload at 32 streams
+    per GPU) and, under ``--gpus N``, ``tp`` (Qwen3-8B tensor parallel over the N ranks,
+    batch 1, context 4096, 16 steps)."""
+    import torch
+    oracle = world == 1 and not args.no_cpu_baseline
+    line = qwen3_line(args, rank, world, local_rank, oracle=oracle)
+    torch.cuda.empty_cache()
+    extra = {}
+    if args.batch == 1 and not args.no_extra:
+        sub = qwen3_line(argparse.Namespace(**{**vars(args), "batch": 32}), rank, world, local_rank,
+                         oracle=False, spot=oracle)
+        torch.cuda.empty_cache()
+        if rank == 0:
+            extra["bs32"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline", "gpu_launches",
+                                                 "oracle_spot_check", "prefill_s") if k in sub}
+            extra["bs32"]["config"] = sub["config"]["workload"]
+        if world > 1:
+            tp_args = argparse.Namespace(**{**vars(args), "model": "qwen3-8b", "batch": 1, "prompt": 4096,
+                                            "steps": 16, "warmup": 4, "no_cpu_baseline": True})
+            sub = run_tp(tp_args, rank, world, local_rank, emit=False)
+            if rank == 0:
+                extra["tp"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline", "gpu_launches",
+                                                   "n_gpus", "steps", "warmup", "limiter") if k in sub}
+                extra["tp"]["config"] = sub["config"]["workload"] + f", tp{world}"
+    if rank == 0:
+        if extra:
+            line["extra"] = extra
+        print(json.dumps(line), flush=True)
+
+
+def qwen3_line(args, rank, world, local_rank, oracle=False, spot=False):
+    """Qwen3-0.6B greedy decode at ``args.batch`` streams per GPU: batched prefill, W
+    warm-up and K timed device-fed steps, K end-to-end steps through the public API.
+    ``oracle``: the CPU baseline and the teacher-forced oracle agreement on stream 0
+    (rank 0, one GPU); ``spot``: one oracle token of stream 0.  Returns the bench line
+    (rank 0; None elsewhere)."""
     import torch
     import torch.distributed as dist
     from iron_b200.qwen3 import Qwen3B200, Qwen3Config, Qwen3Weights
@@ -279,8 +334,8 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = Qwen3Config.qwen3_0_6b()
-    K, W = args.steps, args.warmup
-    max_seq = (args.prompt + W + 2 * K + 8 + 63) // 64 * 64
+    K, W, NA = args.steps, args.warmup, args.oracle_steps if oracle else 0
+    max_seq = (args.prompt + W + 2 * K + NA + 8 + 63) // 64 * 64
     w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
     B = args.batch
     dec = Qwen3B200(w, max_seq=max_seq, batch=B, device=dev)
@@ -294,15 +349,20 @@ def run_ours(args, rank, world, local_rank):
     clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
                           if "CUDA_VISIBLE_DEVICES" in os.environ and world == 1 else local_rank)
     clocks.start()
-    # prefill, token by token through the decode step (qwen3_0.6b/check_cosine_int8.py:51-52)
+    # prefill: each stream's prompt through every layer at once (Qwen3B200.prefill; the
+    # reference runs its prompt loop token by token, check_cosine_int8.py:49-54).  The
+    # first pass loads the kernels; the second, over the same positions (it rewrites
+    # the same K/V), is the one timed.
+    for b in range(B):
+        dec.prefill(prompts[b], stream=b)
+    torch.cuda.synchronize()
     t_pre = time.perf_counter()
-    for p in range(args.prompt):
-        nxt = dec.step_tokens([prompts[b][p] for b in range(B)], p)
+    for b in range(B):
+        dec.prefill(prompts[b], stream=b)
+    torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pre
     pos = args.prompt
     dec.set_position(pos)
-    with torch.cuda.stream(dec.stream):
-        dec.tok.copy_(nxt.to(dev))
     for _ in range(W):
         dec.run_step(from_tokens=True, advance=True)
     pos += W
@@ -324,18 +384,24 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     e2.record(dec.stream)
-    last_in, last_pos = toks[0], pos
     for _ in range(K):
-        last_in, last_pos = toks[0], pos
         toks = [int(t) for t in dec.step_tokens(toks, pos)]
         pos += 1
-    tok = toks[0]
     e3.record(dec.stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e2.elapsed_time(e3)
     clocks.stop()
     clk = clocks.summary()
+    # ---- oracle material (stream 0): the K/V cache at pos, then NA teacher-forced steps ----
+    if (oracle or spot) and rank == 0:
+        kvnp = dec.kv[:, 0].float().cpu().numpy().reshape(cfg.n_layers, cfg.Hkv, max_seq, 2, cfg.HD)
+        ins, outs, p0 = [], [], pos
+        for _ in range(max(NA, 1)):
+            ins.append(toks[0])
+            toks = [int(t) for t in dec.step_tokens(toks, pos)]
+            outs.append(toks[0])
+            pos += 1
     # ---- dominant kernel: the persistent step kernel (the only launch of a step) ----
     # algorithmic bytes of the timed steps, averaged over their attention lengths
     ctx0 = args.prompt + W + 1
@@ -343,8 +409,7 @@ def run_ours(args, rank, world, local_rank):
     # ---- aggregate over ranks ----
     t_ms, e2e_ms, value, e2e = aggregate_replicas(t_ms, e2e_ms, K * B, world, dev)
     if rank != 0:
-        return
-    from iron_b200 import _lib  # noqa: F401
+        return None
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = step_bytes / (t_ms / K / 1000.0) / 1e9
@@ -352,7 +417,8 @@ def run_ours(args, rank, world, local_rank):
             "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xbf16", "data": "synthetic", "config": workload(args),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B,
-                    "d2h_bytes_per_step": (8 if dec.impl == "step" else 4) * B},
+                    # the tokens, and the step kernel's error word / the two tensor-core status words
+                    "d2h_bytes_per_step": 8 * B if dec.impl == "step" else 4 * B + (8 if B >= 16 else 0)},
             "gpu_launches": K * dec.launches_per_step(),
             "roofline": {"bound": "hbm",
                          "kernel": ("qwen3_step_kernel (one persistent launch per token)" if dec.impl == "step"
@@ -364,26 +430,25 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_source": "ncu dram bytes of one launch at context 71, scaled by the K/V bytes"},
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "prefill_s": prefill_s}
-    if world == 1 and not args.no_cpu_baseline:
+    if oracle or spot:
         from oracle.qwen3 import Qwen3Shape
         wnp = w.to_numpy()
-        kvnp = dec.kv[:, 0].float().cpu().numpy().reshape(cfg.n_layers, cfg.Hkv, max_seq, 2, cfg.HD)
         threads = len(os.sched_getaffinity(0))
-        # the oracle reproduces the GPU's last token from the same state (parity spot check)
-        ptok = last_pos
-        tps, used, logits = cpu_sample(wnp, kvnp, Qwen3Shape(group=GROUP), ptok, last_in,
-                                       args.cpu_tokens, threads, angles=dec.angles.float().cpu().numpy())
-        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": used, "kind": "port",
-                                "sample": f"{args.cpu_tokens} full decode tokens (28 layers + bf16 lm_head) of "
-                                          f"the numpy oracle at position {ptok} on this run's weights and KV cache"
-                                          + (" (stream 0 of the batch)" if B > 1 else "")}
-        import numpy as np
-        line["oracle_spot_check"] = {"position": ptok, "input_token": last_in,
-                                     "gpu_token": tok, "oracle_token": int(np.argmax(logits))}
-    print(json.dumps(line), flush=True)
+        angles = dec.angles.float().cpu().numpy()
+        if oracle:
+            tps, used, rec = oracle_replay(wnp, kvnp, Qwen3Shape(group=GROUP), p0, ins, outs, threads, angles)
+            line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": used, "kind": "port",
+                                    "sample": f"{len(ins)} full decode tokens (28 layers + bf16 lm_head) of the "
+                                              f"numpy oracle from position {p0}, teacher-forced on this run's "
+                                              f"weights, K/V cache and tokens" + (" (stream 0)" if B > 1 else "")}
+            line["oracle_agreement"] = rec
+        line["oracle_spot_check"] = {"position": p0, "input_token": ins[0], "gpu_token": outs[0],
+                                     "oracle_token": oracle_spot(wnp, kvnp, Qwen3Shape(group=GROUP), p0, ins[0],
+                                                                 threads, angles)}
+    return line
 
 
-def run_tp(args, rank, world, local_rank):
+def run_tp(args, rank, world, local_rank, emit=True):
     """Qwen3-8B int8-g32 greedy decode, tensor parallel over the
     torchrun world (iron_b200/tp.py; NCCL all-reduce of the O / down partials, all-gather
     of the vocabulary-parallel argmax).  The context is ``--prompt`` positions of N(0, 1)
@@ -444,16 +509,36 @@ def run_tp(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e2.elapsed_time(e3)
+    # the collectives alone: a step's 2 x n_layers all-reduces of its float32 partials
+    # (and one all-gather of the argmax pairs), timed back to back on the same stream
+    coll_ms = 0.0
+    if world > 1:
+        import torch.distributed as dist
+        n_ar = 2 * cfg.n_layers
+        with torch.cuda.stream(dec.stream):
+            for _ in range(2 * n_ar):
+                dist.all_reduce(dec.part)
+            barrier()
+            torch.cuda.synchronize()
+            e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e4.record(dec.stream)
+            for _ in range(4 * n_ar):
+                dist.all_reduce(dec.part)
+            for _ in range(4):
+                dist.all_gather_into_tensor(dec.gathered, dec.pairs)
+            e5.record(dec.stream)
+        torch.cuda.synchronize()
+        coll_ms = e4.elapsed_time(e5) / 4
     clocks.stop()
     clk = clocks.summary()
-    tt = torch.tensor([t_ms, e2e_ms], dtype=torch.float64, device=dev)
+    tt = torch.tensor([t_ms, e2e_ms, coll_ms], dtype=torch.float64, device=dev)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms = float(tt[0]), float(tt[1])
+    t_ms, e2e_ms, coll_ms = float(tt[0]), float(tt[1]), float(tt[2])
     dec.close()
     if rank != 0:
-        return
+        return None
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("hbm_gbs", 6650.0)
     # every weight, the lm_head and the K/V heads are split over the ranks: bytes per GPU
@@ -478,6 +563,11 @@ def run_tp(args, rank, world, local_rank):
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
                          "unit": "GB/s", "frac": achieved / peak, "traffic": None},
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    if world > 1:
+        line["limiter"] = {"collectives_ms_per_step": coll_ms, "step_ms": t_ms / K,
+                           "share": coll_ms / (t_ms / K),
+                           "what": f"{2 * cfg.n_layers} NCCL all-reduces of {B} x {cfg.D} float32 + one "
+                                   f"all-gather per step, timed alone back to back"}
     if cpu_layer is not None:
         from oracle import ops
         from oracle.bf16 import rnd
@@ -500,7 +590,9 @@ def run_tp(args, rank, world, local_rank):
                                 "sample": f"one Qwen3-8B decoder layer of the numpy oracle at position {P} "
                                           f"(x 36) + the bf16 lm_head on 1/16 of its rows (x 16), this run's "
                                           f"weights"}
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
 def llama_step_bytes(cfg, lens):
@@ -765,11 +857,9 @@ def run_breakdown(args):
     dec = Qwen3B200(w, max_seq=P + args.steps + 16, batch=B, device=dev)
     g = torch.Generator().manual_seed(args.seed + 1)
     prompts = torch.randint(0, cfg.V, (B, P), generator=g).tolist()
-    for p in range(P):
-        nxt = dec.step_tokens([prompts[b][p] for b in range(B)], p)
+    for b in range(B):
+        dec.prefill(prompts[b], stream=b)
     dec.set_position(P)
-    with torch.cuda.stream(dec.stream):
-        dec.tok.copy_(nxt.to(dev))
     for _ in range(3):
         dec.run_step(from_tokens=True, advance=True)
     torch.cuda.synchronize()

@@ -147,6 +147,16 @@ int iron_mul(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n, void*
  * per-head norms of iron_qkv_head: the Llama path (llama_cpu.py:14-38, 94-115). */
 int iron_rope_kv(const uint16_t* raw, const uint16_t* ang_table, uint16_t* q_out, uint16_t* kv_cache, int HD,
                  int Hq, int Hkv, int max_seq, int batch, const int32_t* kv_off_dev, void* stream);
+/* The per-head epilogue of iron_qkv_head (q/k RMSNorm with n_qn / n_kn in norm_mode,
+ * RoPE from the (max_seq, HD) angle table, q to q_out (rows, Hq*HD), K_t / V_t into the
+ * cache) over the consecutive tokens of ONE prompt: raw row r is the token at position
+ * pos0 + r, written to that position of the single stream cache kv_cache (Hkv,
+ * 2*max_seq*HD).  The prompt-rows form of the decode head (qkv_head_dp/reference.py
+ * :29-33), for a prefill that does at once what the reference's token-by-token prompt
+ * loop does (check_cosine_int8.py:49-54, one Qwen3NPU.__call__ per token). */
+int iron_qkv_rows(const uint16_t* raw, int rows, const uint16_t* n_qn, const uint16_t* n_kn,
+                  const uint16_t* ang_table, uint16_t* q_out, uint16_t* kv_cache, int HD, int Hq, int Hkv,
+                  int max_seq, int pos0, float eps, int norm_mode, void* stream);
 /* y = bf16(silu(x)); mode 0: x*sigmoid(x) in f32 (silu/reference.py:8-10),
  * mode 1: the tanh form with bf16 roundings (aie_kernels/aie2p/silu.cc). */
 int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream);

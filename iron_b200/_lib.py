@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_tc_workspace_bytes": (I64, [I, I, I]),
     "iron_launch_count": (I64, []),
     "iron_rope_kv": (I, [P, P, P, P, I, I, I, I, I, P, P]),
+    "iron_qkv_rows": (I, [P, I, P, P, P, P, P, I, I, I, I, I, F, I, P]),
     "iron_gemv_w8a16_ex": (I, [P, P, I, I, I, I, P, I, I, P, C.c_float, I, P, I, P, I, P, I64, P]),
     "iron_resid_add_f32": (I, [P, P, P, I64, P]),
     "iron_argmax_pair": (I, [P, I, I, P, I, P, P]),

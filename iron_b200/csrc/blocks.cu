@@ -7,7 +7,7 @@ namespace iron {
 int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                            const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
                            int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st);
+                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st, int pos0);
 }
 using namespace iron;
 
@@ -43,7 +43,7 @@ extern "C" int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const vo
   rc = gemv_w8_launch(p, false, st);
   if (rc) return rc;
   return qk_norm_rope_kv_launch(raw_ws, n_qn, n_kn, ang, ang_is_table, q_out, kv_cache, HD, Hq, Hkv,
-                                max_seq, batch, kv_off, kv_off_dev, eps, norm_mode, st);
+                                max_seq, batch, kv_off, kv_off_dev, eps, norm_mode, st, -1);
 }
 
 extern "C" int iron_mlp_block(const uint16_t* cur, const uint16_t* a_or_cx, int fuse_o, const uint16_t* n_pf,

@@ -572,18 +572,19 @@ static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, b
   return true;
 }
 
+// plan_nb: the batch the workspace was carved for (>= p.nb); the split plan is the one
+// of that batch, so this launch's partial tiles fit the carved region
 template <int G, bool PAIR>
-static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const TcWs& ws, cudaStream_t st) {
+static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const TcWs& ws, int plan_nb,
+                     cudaStream_t st) {
   using namespace tc;
   constexpr int NW = PAIR ? 2 : 1;
   const int M = p.M, K = p.K, nb = p.nb;
   const int N = (nb + 15) / 16 * 16;
   const int tiles = (M + BM - 1) / BM;
-  const int kblocks = K / BK;
   if (tiles > MAX_TILES) return 1;
-  (void)kblocks;
   int splits, kbps;
-  tc_split_plan(M, K, N, NW, splits, kbps);
+  tc_split_plan(M, K, (plan_nb + 15) / 16 * 16, NW, splits, kbps);
   TcParams tp = {};
   tp.status = ws.status;
   tp.counters = ws.counters;
@@ -722,12 +723,29 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
     ld_x = p.K;
   }
   if (!iron_aligned(x, 16) || ld_x % 8) return 1;
-  switch (p.wa.G) {
-    case 32: return pair ? tc_launch<32, true>(p, x, ld_x, ws, st) : tc_launch<32, false>(p, x, ld_x, ws, st);
-    case 64: return pair ? tc_launch<64, true>(p, x, ld_x, ws, st) : tc_launch<64, false>(p, x, ld_x, ws, st);
-    case 128: return pair ? tc_launch<128, true>(p, x, ld_x, ws, st) : tc_launch<128, false>(p, x, ld_x, ws, st);
+  if (p.wa.G != 32 && p.wa.G != 64 && p.wa.G != 128) return 1;
+  // a gate/up pair keeps two weight tiles per stage: its stages fit shared memory for
+  // up to 128 activation rows, so larger batches run as launches of equal row blocks
+  const int nchunk = pair ? (p.nb + 127) / 128 : 1;
+  const int rows = (p.nb + nchunk - 1) / nchunk;
+  const size_t ysz = p.epi == EPI_F32 ? 4 : 2;
+  for (int b0 = 0; b0 < p.nb; b0 += rows) {
+    GemvW8Params q = p;
+    q.nb = std::min(rows, p.nb - b0);
+    q.y = (uint16_t*)((uint8_t*)p.y + (size_t)b0 * p.ld_y * ysz);
+    if (p.res) q.res = p.res + (size_t)b0 * p.ld_y;
+    const uint16_t* xb = x + (size_t)b0 * ld_x;
+    int rc = 1;
+    switch (p.wa.G) {
+      case 32: rc = pair ? tc_launch<32, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<32, false>(q, xb, ld_x, ws, p.nb, st); break;
+      case 64: rc = pair ? tc_launch<64, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<64, false>(q, xb, ld_x, ws, p.nb, st); break;
+      case 128: rc = pair ? tc_launch<128, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<128, false>(q, xb, ld_x, ws, p.nb, st); break;
+    }
+    // 1 (not handled) can only come from the first block: the later ones have the same
+    // shape but fewer rows; the caller then runs every row on the exact kernel
+    if (rc) return rc;
   }
-  return 1;
+  return 0;
 }
 
 }  // namespace iron

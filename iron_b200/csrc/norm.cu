@@ -48,16 +48,19 @@ __global__ void embedding_kernel(const uint16_t* table, const int32_t* ids, int 
 // Per-head epilogue of the fused QKV head (qkv_head_dp/reference.py:29-33).
 // grid (Hq + Hkv, batch), one warp per head.  q heads: RMSNorm_w(n_qn) -> RoPE ->
 // q_out.  kv heads: RMSNorm_w(n_kn) -> RoPE -> K_t, and V_t = raw v, both written
-// to the cache at the stream's position.
+// to the cache at the stream's position.  pos0 >= 0: the rows are consecutive tokens
+// of ONE stream (a prompt), row b at position pos0 + b of that stream's cache.
 template <int HD>
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                                        const uint16_t* ang, int ang_is_table, uint16_t* q_out,
                                        uint16_t* kv, int Hq, int Hkv, int max_seq, int kv_off,
-                                       const int32_t* kv_off_dev, float eps, int norm_mode) {
+                                       const int32_t* kv_off_dev, float eps, int norm_mode, int pos0) {
   constexpr int PER = HD / 32;
   const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
   const int QKV = (Hq + 2 * Hkv) * HD;
-  const int off = kv_off_dev ? kv_off_dev[b] : kv_off;  // element offset of K_t in a head region
+  // element offset of K_t in a head region
+  const int off = pos0 >= 0 ? (pos0 + b) * 2 * HD : (kv_off_dev ? kv_off_dev[b] : kv_off);
+  const int stream = pos0 >= 0 ? 0 : b;
   // an offset outside the cache (e.g. a stale runtime parameter) writes nothing
   if (off < 0 || off % (2 * HD) != 0 || off / (2 * HD) >= max_seq) return;
   const bool isq = head < Hq;
@@ -98,7 +101,7 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
     }
   } else {
     const int kh = head - Hq;
-    uint16_t* dst = kv + ((size_t)b * Hkv + kh) * max_seq * 2 * HD + off;
+    uint16_t* dst = kv + ((size_t)stream * Hkv + kh) * max_seq * 2 * HD + off;
     const uint16_t* vsrc = raw + (size_t)b * QKV + (size_t)(Hq + Hkv + kh) * HD;
 #pragma unroll
     for (int j = 0; j < PER / 2; ++j) {
@@ -112,14 +115,14 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn
 int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                            const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
                            int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
-                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st) {
+                           const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st, int pos0) {
   dim3 g(Hq + Hkv, batch);
   if (HD == 128) {
     qk_norm_rope_kv_kernel<128><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                   max_seq, kv_off, kv_off_dev, eps, norm_mode);
+                                                   max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0);
   } else if (HD == 64) {
     qk_norm_rope_kv_kernel<64><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                  max_seq, kv_off, kv_off_dev, eps, norm_mode);
+                                                  max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0);
   } else {
     return iron_set_error(IRON_ERR_UNSUPPORTED, "qkv head: head_dim %d (supported: 64, 128)", HD);
   }
@@ -175,7 +178,21 @@ extern "C" int iron_rope_kv(const uint16_t* raw, const uint16_t* ang_table, uint
   IRON_REQUIRE(raw && ang_table && q_out && kv_cache && kv_off_dev && batch >= 1 && Hq >= 1 && Hkv >= 1,
                IRON_ERR_ARG, "rope_kv: bad arguments");
   return qk_norm_rope_kv_launch(raw, nullptr, nullptr, ang_table, 1, q_out, kv_cache, HD, Hq, Hkv, max_seq, batch,
-                                0, kv_off_dev, 0.f, 0, (cudaStream_t)stream);
+                                0, kv_off_dev, 0.f, 0, (cudaStream_t)stream, -1);
+}
+
+// The QKV head epilogue over the consecutive tokens of one prompt: row r of raw is the
+// token at position pos0 + r of the single stream whose cache is kv_cache.
+extern "C" int iron_qkv_rows(const uint16_t* raw, int rows, const uint16_t* n_qn, const uint16_t* n_kn,
+                             const uint16_t* ang_table, uint16_t* q_out, uint16_t* kv_cache, int HD, int Hq,
+                             int Hkv, int max_seq, int pos0, float eps, int norm_mode, void* stream) {
+  IRON_REQUIRE(raw && ang_table && q_out && kv_cache && rows >= 1 && Hq >= 1 && Hkv >= 1, IRON_ERR_ARG,
+               "qkv_rows: bad arguments");
+  IRON_REQUIRE(pos0 >= 0 && pos0 + rows <= max_seq, IRON_ERR_ARG,
+               "qkv_rows: positions %d..%d outside a %d-token cache", pos0, pos0 + rows - 1, max_seq);
+  IRON_REQUIRE(norm_mode >= 0 && norm_mode <= 2, IRON_ERR_ARG, "qkv_rows: norm_mode must be 0, 1 or 2");
+  return qk_norm_rope_kv_launch(raw, n_qn, n_kn, ang_table, 1, q_out, kv_cache, HD, Hq, Hkv, max_seq, rows, 0,
+                                nullptr, eps, norm_mode, (cudaStream_t)stream, pos0);
 }
 
 extern "C" int iron_silu(const uint16_t* x, uint16_t* y, int64_t n, int mode, void* stream) {

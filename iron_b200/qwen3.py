@@ -459,18 +459,98 @@ class Qwen3B200:
         self.run_step(from_tokens=True, advance=False)
         return self._read_tokens()
 
-    def generate(self, prompt, n_new: int) -> list:
-        """Prefill ``prompt`` (ids, batch 1) token by token, then greedy-decode ``n_new`` tokens.
+    #: prompt rows per tensor-core launch of the prefill (the contraction's batch limit)
+    PREFILL_ROWS = 256
 
-        The decode steps replay the captured step back to back: the device advances
-        the position and feeds each argmax token to the next step's embedding; the
-        tokens are gathered on the device and read back once."""
+    def prefill(self, prompt, stream: int = 0, start: int = 0, exact: bool = False) -> int:
+        """Run the prompt ``prompt`` (token ids) of stream ``stream`` through every layer
+        at once, its tokens at positions ``start`` .. ``start + len(prompt) - 1``.
+
+        Does what the reference's prompt loop does one token at a time
+        (check_cosine_int8.py:49-54: one ``Qwen3NPU.__call__`` per token): fills the K/V
+        cache of those positions and returns the greedy token after the last one,
+        which the stream's next step reads (its position is set to the one after the
+        prompt).  Per layer, blocks of up to ``PREFILL_ROWS`` prompt rows run the
+        decode step's operators as batched launches: the QKV projection with its
+        RMSNorm (tcgen05 contraction from 16 rows on), the per-head q/k norms, RoPE and
+        K/V writes at the rows' positions (``iron_qkv_rows``), causal attention over
+        the cache (``iron_attn_mq``), and the O / gate-up / down block
+        (``iron_mlp_block``).  The last row's final RMSNorm, lm_head and argmax
+        follow; the logits are kept in ``self.prefill_logits``.  ``exact`` runs the
+        projections with the decode step's exact kernel in launches of 8 rows instead of
+        the tensor-core contraction (slower; no float32 summation in the projections)."""
+        c, w, G = self.cfg, self.w, self.w.group
+        ids = [int(t) for t in prompt]
+        P = len(ids)
+        if P < 1 or start < 0 or start + P > self.max_seq:
+            raise ValueError(f"prompt of {P} tokens at {start} does not fit a {self.max_seq}-token cache")
+        if not 0 <= stream < self.B:
+            raise ValueError(f"stream {stream} outside the batch of {self.B}")
+        dev, st = self.x.device, self.stream
+        R = min(P, self.PREFILL_ROWS)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        x = torch.empty(P, c.D, **bf)
+        raw, q, attn = torch.empty(R, c.QKV, **bf), torch.empty(R, c.QD, **bf), torch.empty(R, c.QD, **bf)
+        x1, gh = torch.empty(R, c.D, **bf), torch.empty(R, c.FF, **bf)
+        xf = torch.empty(1, c.D, **bf)
+        L = _lib.lib()
+        tw = _lib.tc_workspace([(c.QKV, c.D), (c.D, c.QD), (c.FF, c.D), (c.D, c.FF)], 1 if exact else R, dev)
+        aw = _lib.workspace(L.iron_attn_mq_workspace_bytes(R, c.Hq, c.Hkv, c.HD, self.max_seq), dev)
+        hw = _lib.workspace(L.iron_argmax_workspace_bytes(1), dev)
+        self.prefill_logits = torch.empty(1, c.V, **bf)
+        ids_dev = torch.tensor(ids, dtype=torch.int32).pin_memory()
+        with torch.cuda.stream(st):
+            ids_d = ids_dev.to(dev, non_blocking=True)
+            s_ = st.cuda_stream
+            abi("iron_embedding", ptr(w.embed), c.V, ptr(ids_d), P, c.D, ptr(x), s_)
+            for li, Lw in enumerate(w.layers):
+                kv = self.kv[li, stream]
+                for r0 in range(0, P, R):
+                    n = min(R, P - r0)
+                    xr = x[r0:r0 + n]
+                    abi("iron_gemv_w8a16_ex", ptr(Lw["wqkv"]), None, c.QKV, c.D, G, 0, ptr(xr), c.D, n,
+                        ptr(Lw["norm1"]), c.eps, 1, None, 0, ptr(raw), c.QKV, ptr(tw), tw.numel(), s_)
+                    abi("iron_qkv_rows", ptr(raw), n, ptr(Lw["qn"]), ptr(Lw["kn"]), ptr(self.angles), ptr(q),
+                        ptr(kv), c.HD, c.Hq, c.Hkv, self.max_seq, start + r0, c.eps, 1, s_)
+                    abi("iron_attn_mq", ptr(q), ptr(kv), ptr(attn), n, c.Hq, c.Hkv, c.HD, self.max_seq, 0, 0,
+                        start + r0, None, self.max_seq, 1, ptr(aw), aw.numel(), s_)
+                    abi("iron_mlp_block", ptr(xr), ptr(attn), 1, ptr(Lw["norm2"]), ptr(Lw["wo"]), 1, 0, 0,
+                        ptr(Lw["wg"]), ptr(Lw["wu"]), 1, ptr(Lw["wd"]), 1, G, 0, ptr(x1), ptr(gh), ptr(xr),
+                        c.D, c.FF, c.QD, n, c.eps, ptr(tw), tw.numel(), s_)
+            abi("iron_rmsnorm", ptr(x[P - 1:]), ptr(w.final_norm), ptr(xf), 1, c.D, c.eps, 1, s_)
+            tok = self.tok[stream:stream + 1]
+            if self.lm_head == "bf16":
+                abi("iron_lm_head_bf16_argmax", ptr(w.embed), c.V, c.D, ptr(xf), 1, ptr(self.prefill_logits),
+                    ptr(tok), ptr(hw), hw.numel(), s_)
+            else:
+                abi("iron_lm_head_w8_argmax", ptr(w.lm_wire), c.V, c.D, G, ptr(xf), 1, ptr(self.prefill_logits),
+                    ptr(tok), ptr(hw), hw.numel(), s_)
+            status = torch.stack([_lib.status_word(tw)[0], tok[0]]).cpu()
+            # the stream continues after the prompt
+            nxt = start + P
+            self.pos[stream].fill_(nxt)
+            self.len[stream].fill_(nxt + 1)
+            self.off[stream].fill_(nxt * 2 * c.HD)
+        _lib.raise_on_status(int(status[0]), "prefill")
+        return int(status[1])
+
+    def generate(self, prompt, n_new: int, batched_prefill: bool = True) -> list:
+        """Prefill ``prompt`` (ids, batch 1), then greedy-decode ``n_new`` tokens.
+
+        ``batched_prefill`` runs the prompt through ``prefill`` (all rows of a layer at
+        once); otherwise token by token through the decode step, as the reference's
+        prompt loop.  The decode steps replay the captured step back to back: the device
+        advances the position and feeds each argmax token to the next step's
+        embedding; the tokens are gathered on the device and read back once."""
         if self.B != 1:
             raise ValueError("generate() is batch 1")
         if len(prompt) + n_new > self.max_seq:
             raise ValueError("prompt + new tokens exceed max_seq")
-        for p, t in enumerate(prompt):
-            self.step_tokens([t], p)
+        if batched_prefill:
+            self.prefill(prompt)
+        else:
+            for p, t in enumerate(prompt):
+                self.step_tokens([t], p)
         hist = torch.empty(n_new, dtype=torch.int32, device=self.tok.device)
         self.set_position(len(prompt))
         with torch.cuda.stream(self.stream):

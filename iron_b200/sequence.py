@@ -38,6 +38,15 @@ class DeviceBuffer:
         """Host copy of the buffer contents."""
         return self.torch_view(dtype).cpu()
 
+    def to(self, device) -> "DeviceBuffer":
+        """IRON's host/device sync of a buffer (``to("npu")`` / ``to("cpu")``,
+        iron/common/sequence.py XRT buffers).  The buffer is device memory and
+        ``torch_view`` reads and writes it directly, so there is nothing to move; device
+        work of earlier calls has finished when a call returns."""
+        if device not in ("npu", "cpu", "cuda"):
+            raise ValueError(f"unknown device {device!r}")
+        return self
+
     @property
     def nbytes(self) -> int:
         return self.raw.numel()

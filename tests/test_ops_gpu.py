@@ -370,3 +370,27 @@ def test_mlp_bf16_arm():
                                       lambda v: Wu.astype(np.float64) @ v, lambda v: Wd.astype(np.float64) @ v,
                                       1e-6)
     assert_close(host(nxt), want, what="bf16 arm")
+
+
+@pytest.mark.parametrize("S", [128, 96])
+def test_attn_mq_prefill_against_mha_golden(golden, S):
+    """Prompt attention (iron_attn_mq from position 0, causal) on the prefill MHA golden
+    (mha/reference.py:26-93: torch's causal SDPA in bf16, GQA 4/2, head_dim 64), a 128-
+    and a 96-token prompt; torch rounds intermediates to bf16, so a few percent of the
+    golden's outputs sit one ulp from the float32 result."""
+    from iron_b200 import _lib
+    g = golden("mha_prefill")
+    Q, K, V = (from_bits(g[f"{k}_{S}"])[:, :S] for k in "QKV")
+    H, KV, D = 4, 2, 64
+    kv = dev_bf16(_pack_kv(np.ascontiguousarray(K), np.ascontiguousarray(V), "token"))
+    q = dev_bf16(np.ascontiguousarray(Q.transpose(1, 0, 2)))
+    o = torch.empty(S, H, D, dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(_lib.lib().iron_attn_mq_workspace_bytes(S, H, KV, D, S), dtype=torch.uint8, device="cuda")
+    _lib.call("iron_attn_mq", q.data_ptr(), kv.data_ptr(), o.data_ptr(), S, H, KV, D, S, 0, 0, 0, None, S, 1,
+              ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    got = host(o).transpose(1, 0, 2)
+    want = from_bits(g[f"O_{S}"])[:, :S]
+    assert_close(got, want, what=f"prefill S={S}")
+    assert_ulps(got, want, max_ulp=2, frac_exact=0.85, what=f"prefill S={S}")
+    _near_rounding(got, ops.mha_prefill(Q, K, V, D, H, KV), f"prefill S={S} vs oracle")

@@ -327,3 +327,64 @@ def test_batch32_decode_matches_oracle(n_layers):
                 assert gap <= ATOL + RTOL * abs(float(logits[want])), f"stream {b} pos {pos}: {g} vs {want}"
             nxt.append(g)
         toks = nxt
+
+
+@pytest.mark.parametrize("impl", ["step", "ops"])
+def test_prefill_matches_token_by_token(small, impl):
+    """Qwen3B200.prefill (a layer's prompt rows at once: tcgen05 projections from 16 rows
+    on, causal multi-query attention) against the reference's prompt loop, one decode
+    step per token (check_cosine_int8.py:49-54): a 300-token prompt (a block of 256 rows
+    and one of 44) from position 20 of a cache whose first 20 positions were filled by
+    decode steps.
+
+    The two differ only in float32 summation order (batched contraction vs the
+    one-token kernels, flash attention vs split decoding), which flips a few bf16
+    roundings per layer; every flip moves the next RMSNorm's scale and so every later
+    value by about an ulp (with the projections on the exact kernel too the second
+    layer agrees no better: the attention's flips alone spread as far).  So: the first
+    layer's K/V agree bit for bit almost everywhere and within the bf16 gate
+    everywhere; the second layer's agree within the gate almost everywhere, a few ulps
+    at most, with the token loop and with the oracle (teacher-forced from position 0)
+    alike; the logits agree within the whole-model gate, the next token is the same or
+    a near-tie, and decoding continues from both alike."""
+    cfg, w = small
+    S, P0, P = 384, 20, 300
+    rng = np.random.default_rng(21)
+    head = [int(t) for t in rng.integers(0, cfg.V, P0)]
+    prompt = [int(t) for t in rng.integers(0, cfg.V, P)]
+    a = Qwen3B200(w, max_seq=S, impl=impl, keep_logits=True)
+    b = Qwen3B200(w, max_seq=S, impl=impl, keep_logits=True)
+    for d in (a, b):
+        for p, t in enumerate(head):
+            d.step_tokens([t], p)
+    ta = a.prefill(prompt, start=P0)
+    for p, t in enumerate(prompt):
+        tb = int(b.step_tokens([t], P0 + p)[0])
+    L = len(w.layers)
+    kva = host(a.kv).reshape(L, cfg.Hkv, S, 2, cfg.HD)[:, :, :P0 + P]
+    kvb = host(b.kv).reshape(L, cfg.Hkv, S, 2, cfg.HD)[:, :, :P0 + P]
+    assert np.array_equal(kva[:, :, :P0], kvb[:, :, :P0])
+    assert_close(kva[0], kvb[0], what="first layer K/V")
+    assert np.mean(kva[0] == kvb[0]) >= 0.999, f"{np.mean(kva[0] == kvb[0]):.5f} of layer-0 K/V bit-identical"
+    err = np.abs(kva[1] - kvb[1])
+    assert np.mean(err <= ATOL + RTOL * np.abs(kvb[1])) >= 0.995 and err.max() <= 0.1, \
+        f"second layer K/V: {np.mean(err <= ATOL + RTOL * np.abs(kvb[1])):.4f} within the gate, max {err.max()}"
+    # both against the oracle, teacher-forced on the same tokens from position 0
+    shape = Qwen3Shape(n_layers=L, group=32)
+    orc = OracleQwen3(shape, w.to_numpy(), S, angles=host(a.angles))
+    n_chk = 4
+    for p, t in enumerate(head + prompt[:n_chk]):
+        orc.step(orc.embed(t), p)
+    ko = orc.kv[1, :, P0:P0 + n_chk]                       # (Hkv, n, 2, HD)
+    e = np.abs(kva[1, :, P0:P0 + n_chk] - ko)
+    assert np.mean(e <= ATOL + RTOL * np.abs(ko)) >= 0.995 and e.max() <= 0.1, "second layer K/V vs the oracle"
+    assert_close(kva[0, :, P0:P0 + n_chk], orc.kv[0, :, P0:P0 + n_chk], what="first layer K/V vs the oracle")
+    la, lb = host(a.prefill_logits[0]), host(b.logits[0])
+    logit_gate(la, lb, "prefill logits", max_outside=0.02)
+    assert ta == tb or abs(lb[ta] - lb[tb]) <= float(np.abs(la - lb).max()), "next token: not a near-tie"
+    # both continue from position P0 + P with the same token
+    for k in range(3):
+        a.step_tokens([tb], P0 + P + k)
+        nb = int(b.step_tokens([tb], P0 + P + k)[0])
+        logit_gate(host(a.logits[0]), host(b.logits[0]), f"decode {k} after prefill", max_outside=0.02)
+        tb = nb

@@ -367,19 +367,20 @@ __global__ void __launch_bounds__(NTH, 2)
     const int q = warp & 3, row = 32 * q + lane, m = row0 + row;
     const int half = (warp - 1) / 4;  // columns [half * N/2, (half + 1) * N/2) in 16-column steps
     const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
-    auto finish = [&](int b, float a0, float a1) {
-      if (b >= p.nb || m >= p.M) return;
-      uint16_t* yo = (uint16_t*)p.y + (size_t)b * p.ld_y + m;
+    auto finish_at = [&](int mr, int b, float a0, float a1) {
+      if (b >= p.nb || mr >= p.M) return;
+      uint16_t* yo = (uint16_t*)p.y + (size_t)b * p.ld_y + mr;
       if (PAIR) {
         *yo = f2bf(silu_tanh_bf16(rbf(a0)) * rbf(a1));
       } else if (p.epi == EPI_RESID) {
-        *yo = f2bf(bf2f(p.res[(size_t)b * p.ld_y + m]) + rbf(a0));
+        *yo = f2bf(bf2f(p.res[(size_t)b * p.ld_y + mr]) + rbf(a0));
       } else if (p.epi == EPI_F32) {
-        ((float*)p.y)[(size_t)b * p.ld_y + m] = a0;
+        ((float*)p.y)[(size_t)b * p.ld_y + mr] = a0;
       } else {
         *yo = f2bf(a0);
       }
     };
+    auto finish = [&](int b, float a0, float a1) { finish_at(m, b, a0, a1); };
     if (ok) {
       float* part = p.part + ((size_t)(tile * p.splits + split) * NW * N) * BM;
       for (int c0 = 16 * half; c0 < N; c0 += 32) {
@@ -408,25 +409,29 @@ __global__ void __launch_bounds__(NTH, 2)
       bar_epi();
       if (*lastf && ok) {
           __threadfence();
-          // CB columns at a time, the partials of U splits loaded before any is added:
-          // U * CB * NW loads in flight per thread; sums in split order as always
-          constexpr int CB = 4, U = 4;
-          const float* base = p.part + (size_t)tile * p.splits * NW * N * BM + row;
-          for (int b0 = half; b0 < N; b0 += 2 * CB) {
-            float a0[CB], a1[CB];
+          // Thread t sums rows 4(t % 32) .. +3 (float4 loads) of the columns c = t / 32
+          // (mod 8): CB columns x U splits x NW float4 loads in flight (fewer for a pair,
+          // whose registers are shared with the second accumulator), added in split order
+          // as always.  The partial tiles are [split][NW][column][row].
+          constexpr int CB = PAIR ? 2 : 4, U = PAIR ? 2 : 4, CS = 32 * NDQ / (BM / 4);  // column stride: 8
+          const int r4 = 4 * (t % (BM / 4)), cofs = t / (BM / 4);
+          const float* base = p.part + (size_t)tile * p.splits * NW * N * BM + r4;
+          for (int b0 = cofs; b0 < N; b0 += CS * CB) {
+            float4 a0[CB], a1[CB];
 #pragma unroll
-            for (int c = 0; c < CB; ++c) a0[c] = a1[c] = 0.f;
+            for (int c = 0; c < CB; ++c) a0[c] = a1[c] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int s0 = 0; s0 < p.splits; s0 += U) {
-              float v0[U][CB], v1[U][CB];
+              float4 v0[U][CB], v1[U][CB];
 #pragma unroll
               for (int u = 0; u < U; ++u) {
                 const float* pp = base + (size_t)(s0 + u) * NW * N * BM;
 #pragma unroll
                 for (int c = 0; c < CB; ++c) {
-                  const int b = b0 + 2 * c;
+                  const int b = b0 + CS * c;
                   const bool in = s0 + u < p.splits && b < N;
-                  v0[u][c] = in ? __ldcg(pp + (size_t)b * BM) : 0.f;
-                  v1[u][c] = (PAIR && in) ? __ldcg(pp + (size_t)(N + b) * BM) : 0.f;
+                  v0[u][c] = in ? __ldcg((const float4*)(pp + (size_t)b * BM)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  v1[u][c] = (PAIR && in) ? __ldcg((const float4*)(pp + (size_t)(N + b) * BM))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
               }
 #pragma unroll
@@ -434,14 +439,28 @@ __global__ void __launch_bounds__(NTH, 2)
                 if (s0 + u < p.splits) {
 #pragma unroll
                   for (int c = 0; c < CB; ++c) {
-                    a0[c] += v0[u][c];
-                    if (PAIR) a1[c] += v1[u][c];
+                    a0[c].x += v0[u][c].x;
+                    a0[c].y += v0[u][c].y;
+                    a0[c].z += v0[u][c].z;
+                    a0[c].w += v0[u][c].w;
+                    if (PAIR) {
+                      a1[c].x += v1[u][c].x;
+                      a1[c].y += v1[u][c].y;
+                      a1[c].z += v1[u][c].z;
+                      a1[c].w += v1[u][c].w;
+                    }
                   }
                 }
             }
 #pragma unroll
-            for (int c = 0; c < CB; ++c)
-              if (b0 + 2 * c < N) finish(b0 + 2 * c, a0[c], a1[c]);
+            for (int c = 0; c < CB; ++c) {
+              const int b = b0 + CS * c;
+              if (b >= N) continue;
+              finish_at(row0 + r4, b, a0[c].x, a1[c].x);
+              finish_at(row0 + r4 + 1, b, a0[c].y, a1[c].y);
+              finish_at(row0 + r4 + 2, b, a0[c].z, a1[c].z);
+              finish_at(row0 + r4 + 3, b, a0[c].w, a1[c].w);
+            }
           }
         }
     }

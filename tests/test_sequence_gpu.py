@@ -49,8 +49,11 @@ def test_swiglu_decode_sequence(embedding_dim, hidden_dim):
     xn, wgn, wun, wdn = (host(t) for t in (x, wg, wu, wd))
     assert_ulps(buf["left"], ops.gemv_bf16(wgn, xn), max_ulp=1, frac_exact=0.95, what="left")
     assert_ulps(buf["right"], ops.gemv_bf16(wun, xn), max_ulp=1, frac_exact=0.95, what="right")
-    # float32 x * sigmoid(x): CUDA's and numpy's exp differ in the last float32 bits
-    assert_ulps(buf["left_swished"], ops.silu_ref(buf["left"]), max_ulp=1, frac_exact=0.99, what="left_swished")
+    # float32 x * sigmoid(x): CUDA's and numpy's exp differ in the last float32 bits, and
+    # for large negative inputs both are tiny values (or zero) many ulps apart
+    ls_want = ops.silu_ref(buf["left"])
+    assert_close(buf["left_swished"], ls_want, what="left_swished")
+    assert np.mean(buf["left_swished"] == ls_want) >= 0.99
     assert np.array_equal(buf["intermediate"], ops.mul_ref(buf["left_swished"], buf["right"]))
     assert_ulps(buf["out"], ops.gemv_bf16(wdn, buf["intermediate"]), max_ulp=1, frac_exact=0.9, what="out")
     # end to end, the reference test's tolerances on the float32 chain

@@ -14,8 +14,10 @@ import pytest
 import torch
 
 from iron_b200 import _lib
+from oracle import ops
+from oracle.bf16 import rnd
 
-from helpers import assert_close, host
+from helpers import assert_close, dev_bf16, host
 
 pytestmark = pytest.mark.gpu
 
@@ -72,3 +74,30 @@ def test_static_scratch_rejects_oversized_shapes():
     with pytest.raises(_lib.IronError, match="needs .* bytes of scratch"):
         _lib.call("iron_decode_attn_static", q.data_ptr(), q.data_ptr(), q.data_ptr(), batch, H, 8, HD, S,
                   0, 0, 1, None, _lib.stream_ptr())
+
+
+def test_static_scratch_block_layout_against_oracle():
+    """IRON's block layout ([K_block | V_block] per block_kv positions, kv_layout 2,
+    decode_attn.cc:95-97) with block_kv 64 at a length that ends inside a block, twice:
+    against the oracle's decode attention (decode_attn/reference.py:26-38) and
+    bit-for-bit against the workspace entry point."""
+    rng = np.random.default_rng(5)
+    H, KV, HD, S, B = 16, 8, 128, 512, 64
+    Q = rnd(rng.standard_normal((H, HD)).astype(np.float32))
+    K = rnd(rng.standard_normal((KV, S, HD)).astype(np.float32))
+    V = rnd(rng.standard_normal((KV, S, HD)).astype(np.float32))
+    kv = dev_bf16(np.concatenate([K.reshape(KV, S // B, B, HD), V.reshape(KV, S // B, B, HD)],
+                                 axis=2).reshape(KV, -1))
+    q = dev_bf16(Q)
+    n = _lib.lib().iron_decode_attn_workspace_bytes(1, H, HD, S)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    for L in (300, 449):
+        got = torch.empty(H, HD, dtype=torch.bfloat16, device="cuda")
+        want_ws = torch.empty(H, HD, dtype=torch.bfloat16, device="cuda")
+        _lib.call("iron_decode_attn_static", q.data_ptr(), kv.data_ptr(), got.data_ptr(), 1, H, KV, HD, S, 2, B,
+                  L, None, _lib.stream_ptr())
+        _lib.call("iron_decode_attn", q.data_ptr(), kv.data_ptr(), want_ws.data_ptr(), 1, H, KV, HD, S, 2, B, L,
+                  None, ws.data_ptr(), n, _lib.stream_ptr())
+        torch.cuda.synchronize()
+        assert_close(host(got), ops.decode_attention(Q, K, V, L - 1, HD, H, KV), what=f"static, block layout, L={L}")
+        assert torch.equal(got, want_ws)

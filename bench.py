@@ -67,6 +67,9 @@ def parse():
     ap.add_argument("--oracle-steps", type=int, default=32,
                     help="teacher-forced oracle steps (greedy top-1 agreement; also the CPU baseline sample)")
     ap.add_argument("--no-extra", action="store_true", help="no bs32 / tp sub-records")
+    ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="peer",
+                    help="cross-rank steps of the tensor-parallel decoder: the library's peer-memory exchange "
+                         "(one GPU per rank) or NCCL")
     ap.add_argument("--phases", action="store_true",
                     help="phase breakdown of the one-launch step (a profiling copy of the library), not a bench line")
     ap.add_argument("--breakdown", action="store_true",
@@ -453,8 +456,9 @@ def qwen3_line(args, rank, world, local_rank, oracle=False, spot=False):
 
 def run_tp(args, rank, world, local_rank, emit=True):
     """Qwen3-8B int8-g32 greedy decode, tensor parallel over the
-    torchrun world (iron_b200/tp.py; NCCL all-reduce of the O / down partials, all-gather
-    of the vocabulary-parallel argmax).  The context is ``--prompt`` positions of N(0, 1)
+    torchrun world (iron_b200/tp.py): the O / down partials summed and the
+    vocabulary-parallel argmax pairs gathered over peer memory (``--tp-collective peer``,
+    the library's exchange) or NCCL.  The context is ``--prompt`` positions of N(0, 1)
     K/V per stream (synthetic: prefilling 4096 tokens through 36 layers would only
     repeat the decode step); then W warm-up and K timed greedy steps."""
     import numpy as np
@@ -469,7 +473,8 @@ def run_tp(args, rank, world, local_rank, emit=True):
     max_seq = (P + W + 2 * K + 8 + 63) // 64 * 64
     w = Qwen3Weights.synthetic(cfg, seed=args.seed, group=GROUP, device=dev)
     cpu_layer = w.to_numpy(n_layers=1) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
-    dec = Qwen3TP(w, rank, world, max_seq=max_seq, batch=B, device=dev)
+    coll = args.tp_collective if world > 1 else None
+    dec = Qwen3TP(w, rank, world, max_seq=max_seq, batch=B, device=dev, collective=coll)
     del w
     torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(args.seed + 17 + rank)
@@ -517,23 +522,22 @@ def run_tp(args, rank, world, local_rank, emit=True):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e2.elapsed_time(e3)
-    # the collectives alone: a step's 2 x n_layers all-reduces of its float32 partials
-    # (and one all-gather of the argmax pairs), timed back to back on the same stream
+    # the cross-rank steps alone: a step's 2 x n_layers sums of its float32 partials and
+    # one gather of the argmax pairs, through the step's own collective, back to back
     coll_ms = 0.0
     if world > 1:
-        import torch.distributed as dist
         n_ar = 2 * cfg.n_layers
         with torch.cuda.stream(dec.stream):
             for _ in range(2 * n_ar):
-                dist.all_reduce(dec.part)
+                dec.collective(("sum", dec.part))
             barrier()
             torch.cuda.synchronize()
             e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e4.record(dec.stream)
             for _ in range(4 * n_ar):
-                dist.all_reduce(dec.part)
+                dec.collective(("sum", dec.part))
             for _ in range(4):
-                dist.all_gather_into_tensor(dec.gathered, dec.pairs)
+                dec.collective(("gather", dec.gathered, dec.pairs))
             e5.record(dec.stream)
         torch.cuda.synchronize()
         coll_ms = e4.elapsed_time(e5) / 4
@@ -559,8 +563,8 @@ def run_tp(args, rank, world, local_rank, emit=True):
                                    f"{P}-position synthetic N(0,1) KV context",
                        "batch": B, "layers": 36, "hidden": 4096, "vocab": 151936, "group": GROUP,
                        "context": P, "parallelism": f"tp{world}",
-                       "collectives": "NCCL all_reduce of batch x 4096 float32 twice per layer, "
-                                      "all_gather of 8 bytes per stream per step",
+                       "collectives": (f"{args.tp_collective if world > 1 else 'none'}: all-reduce of batch x "
+                                       f"4096 float32 twice per layer, all-gather of 8 bytes per stream per step"),
                        "l2": "no flush: ~9 GB / world of weights streamed per step, larger than the L2"},
             "e2e": {"value": K * B / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": 8 * B,
                     "d2h_bytes_per_step": 4 * B},
@@ -574,8 +578,8 @@ def run_tp(args, rank, world, local_rank, emit=True):
     if world > 1:
         line["limiter"] = {"collectives_ms_per_step": coll_ms, "step_ms": t_ms / K,
                            "share": coll_ms / (t_ms / K),
-                           "what": f"{2 * cfg.n_layers} NCCL all-reduces of {B} x {cfg.D} float32 + one "
-                                   f"all-gather per step, timed alone back to back"}
+                           "what": f"{2 * cfg.n_layers} all-reduces of {B} x {cfg.D} float32 + one all-gather "
+                                   f"per step over {args.tp_collective}, timed alone back to back"}
     if cpu_layer is not None:
         from oracle import ops
         from oracle.bf16 import rnd

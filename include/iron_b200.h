@@ -382,6 +382,26 @@ int iron_argmax_pair(const uint16_t* logits, int M, int batch, const int32_t* to
 /* tok_out[b] = index of the largest value over pairs[r][b], r < n (ties -> lowest index). */
 int iron_argmax_merge(const int32_t* pairs, int n, int batch, int32_t* tok_out, void* stream);
 
+/* ---- cross-rank steps over peer memory (NVLink) ------------------------------
+ * The all-reduce of the row-parallel partial sums and the all-gather of the argmax
+ * pairs without NCCL.  Every rank allocates one symmetric buffer of
+ * iron_peer_buffer_bytes(world, cap_words) bytes, zero-filled, whose base addresses
+ * (as this rank sees them) are in peers_dev[world]; epochs_dev is a zero-filled
+ * uint32[iron_peer_epoch_words(cap_words)] of this rank, err_dev an int32.  A call
+ * pushes this rank's n_words 32-bit words of `in` into every rank's buffer with plain
+ * stores, publishes them with a system-scope release flag, waits (bounded, 200 ms)
+ * for every rank's flags in its own buffer and writes `out`: mode 0 the float32 sum
+ * over ranks in rank order (n_words floats, in place allowed), mode 1 the rows of all
+ * ranks (world * n_words words).  Every rank makes the same calls in the same order,
+ * each on its own GPU: the call waits for the other ranks' calls.  A timed-out wait
+ * stores 1 in *err_dev and leaves `out` unwritten.  Replaces NCCL's all_reduce /
+ * all_gather in the tensor-parallel split (no reference counterpart: IRON decodes on
+ * one NPU). */
+int64_t iron_peer_buffer_bytes(int world, int cap_words);
+int iron_peer_epoch_words(int cap_words);
+int iron_peer_exchange(const unsigned long long* peers_dev, int world, int rank, int cap_words, const void* in,
+                       void* out, int n_words, int mode, uint32_t* epochs_dev, int* err_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

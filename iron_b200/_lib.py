@@ -40,6 +40,9 @@ SIGNATURES: dict[str, tuple] = {
     "iron_resid_add_f32": (I, [P, P, P, I64, P]),
     "iron_argmax_pair": (I, [P, I, I, P, I, P, P]),
     "iron_argmax_merge": (I, [P, I, I, P, P]),
+    "iron_peer_buffer_bytes": (I64, [I, I]),
+    "iron_peer_epoch_words": (I, [I]),
+    "iron_peer_exchange": (I, [P, I, I, I, P, P, I, I, P, P, P]),
     "iron_mul": (I, [P, P, P, I64, P]),
     "iron_silu": (I, [P, P, I64, I, P]),
     "iron_embedding": (I, [P, I, P, I, I, P, P]),

@@ -1,4 +1,4 @@
-"""Tensor-parallel Qwen3 decode: one process per GPU, NCCL between them.
+"""Tensor-parallel Qwen3 decode: one process per GPU, NCCL or peer memory between them.
 
 IRON decodes on one NPU; its operators have no tensor parallelism.  Here a
 Qwen3 model (Qwen3-8B: 32 query / 8 KV heads, FF 12288) is split over ``world``
@@ -23,9 +23,11 @@ rounding that the fused residual epilogue applies.
 
 ``Qwen3TP._stages`` is a generator of launches that yields at every cross-rank
 step; ``NcclCollective`` performs them with ``torch.distributed`` on the decode
-stream (captured, with the kernels, in the step's CUDA graph after one eager
-step), and tests drive several ranks on one GPU in lock step (``step_lockstep``)
-to check the split arithmetic with the real kernels.
+stream, ``PeerCollective`` with the library's peer-memory exchange (plain stores
+over NVLink into symmetric buffers, bounded flag waits); both are captured, with the
+kernels, in the step's CUDA graph after one eager step.  Tests drive several ranks
+on one GPU in lock step (``step_lockstep``) to check the split arithmetic with the
+real kernels.
 """
 
 from __future__ import annotations
@@ -112,6 +114,9 @@ class LocalCollective:
         if op[0] == "gather":
             op[1][0].copy_(op[2])
 
+    def error(self):
+        return None
+
 
 class NcclCollective:
     """The cross-rank steps over ``torch.distributed`` (NCCL), on the current stream."""
@@ -125,6 +130,54 @@ class NcclCollective:
             self.dist.all_reduce(op[1], group=self.group)
         else:
             self.dist.all_gather_into_tensor(op[1], op[2], group=self.group)
+
+    def error(self):
+        return None
+
+
+class PeerCollective:
+    """The cross-rank steps over peer memory (``iron_peer_exchange``): each rank pushes
+    its float32 partials (or argmax pairs) into every rank's symmetric buffer with plain
+    stores over NVLink and a release flag, waits (bounded) for the others' flags in its
+    own buffer and sums the rows in rank order -- deterministic, no NCCL on the data
+    path.  The symmetric buffer comes from ``torch.distributed._symmetric_memory``
+    (peer-mapped device memory, no multicast).  Every rank must own its GPU: the
+    kernel of one rank waits for the kernels of the others."""
+
+    def __init__(self, world: int, rank: int, cap_words: int, device, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        group = group or dist.group.WORLD
+        where = [None] * world
+        dist.all_gather_object(where, (__import__("socket").gethostname(), torch.cuda.current_device()), group=group)
+        if len(set(where)) != world:
+            raise RuntimeError(f"peer exchange needs one GPU per rank, got {where}")
+        L = _lib.lib()
+        self.world, self.rank, self.cap = world, rank, cap_words
+        self.buf = symm.empty(int(L.iron_peer_buffer_bytes(world, cap_words)), dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.hdl = symm.rendezvous(self.buf, group)
+        self.peers = torch.tensor(list(self.hdl.buffer_ptrs), dtype=torch.int64, device=device)
+        self.epochs = torch.zeros(int(L.iron_peer_epoch_words(cap_words)), dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every buffer is zero before any rank pushes
+
+    def __call__(self, op):
+        st = torch.cuda.current_stream().cuda_stream
+        if op[0] == "sum":
+            t = op[1]
+            abi("iron_peer_exchange", ptr(self.peers), self.world, self.rank, self.cap, ptr(t), ptr(t), t.numel(), 0,
+                ptr(self.epochs), ptr(self.err), st)
+        else:
+            out, src = op[1], op[2]
+            abi("iron_peer_exchange", ptr(self.peers), self.world, self.rank, self.cap, ptr(src), ptr(out),
+                src.numel(), 1, ptr(self.epochs), ptr(self.err), st)
+
+    def error(self):
+        """The device error word (a timed-out wait), read with the step's tokens."""
+        return self.err
 
 
 class Qwen3TP(Qwen3B200):
@@ -150,8 +203,10 @@ class Qwen3TP(Qwen3B200):
         self.part = torch.zeros(batch, local.cfg.D, dtype=torch.float32, device=dev)
         self.pairs = torch.zeros(batch, 2, dtype=torch.int32, device=dev)
         self.gathered = torch.zeros(world, batch, 2, dtype=torch.int32, device=dev)
-        if collective is None:
+        if collective is None or collective == "nccl":
             collective = LocalCollective() if world == 1 else NcclCollective()
+        elif collective == "peer":
+            collective = LocalCollective() if world == 1 else PeerCollective(world, rank, batch * local.cfg.D, dev)
         self.collective = collective
         self._eager_done: set = set()
 
@@ -217,6 +272,28 @@ class Qwen3TP(Qwen3B200):
     def _launch_step(self, from_tokens: bool, advance: bool, st: int):
         for op in self._stages(from_tokens, advance, st):
             self.collective(op)
+
+    def _read_tokens(self) -> torch.Tensor:
+        """Next tokens to the host, with the tensor-core status words (16+ streams) and the
+        peer exchange's error word riding along; raises on a nonzero one."""
+        from . import _lib
+        err = self.collective.error() if hasattr(self.collective, "error") else None
+        words = [self.tok]
+        if self.B >= 16:
+            words += [_lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)]
+        if err is not None:
+            words.append(err)
+        with torch.cuda.stream(self.stream):
+            got = torch.cat(words).cpu()
+        if err is not None and int(got[-1]):
+            raise RuntimeError("tensor-parallel step: a peer exchange gave up on a bounded wait")
+        if self.B >= 16:
+            code = int(got[self.B]) or int(got[self.B + 1])
+            if code:
+                self.tc_ws[:4].zero_()
+                self.head_ws[:4].zero_()
+                _lib.raise_on_status(code, "decode step")
+        return got[:self.B]
 
     def close(self):
         """Release the captured step graphs (before the process group is destroyed)."""

@@ -67,7 +67,7 @@ def parse():
     ap.add_argument("--oracle-steps", type=int, default=32,
                     help="teacher-forced oracle steps (greedy top-1 agreement; also the CPU baseline sample)")
     ap.add_argument("--no-extra", action="store_true", help="no bs32 / tp sub-records")
-    ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="nccl",
                     help="cross-rank steps of the tensor-parallel decoder: the library's peer-memory exchange "
                          "(one GPU per rank) or NCCL")
     ap.add_argument("--phases", action="store_true",

@@ -303,21 +303,30 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.empty_cache()
     extra = {}
     if args.batch == 1 and not args.no_extra:
-        sub = qwen3_line(argparse.Namespace(**{**vars(args), "batch": 32}), rank, world, local_rank,
-                         oracle=False, spot=oracle)
+        # a sub-record that fails (the same way on every rank) is reported, not fatal
+        try:
+            sub = qwen3_line(argparse.Namespace(**{**vars(args), "batch": 32}), rank, world, local_rank,
+                             oracle=False, spot=oracle)
+            if rank == 0:
+                extra["bs32"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline",
+                                                     "gpu_launches", "oracle_spot_check", "prefill_s") if k in sub}
+                extra["bs32"]["config"] = sub["config"]["workload"]
+        except Exception as e:  # noqa: BLE001
+            extra["bs32"] = {"error": f"{type(e).__name__}: {e}"[:300]}
         torch.cuda.empty_cache()
-        if rank == 0:
-            extra["bs32"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline", "gpu_launches",
-                                                 "oracle_spot_check", "prefill_s") if k in sub}
-            extra["bs32"]["config"] = sub["config"]["workload"]
         if world > 1:
             tp_args = argparse.Namespace(**{**vars(args), "model": "qwen3-8b", "batch": 1, "prompt": 4096,
                                             "steps": 16, "warmup": 4, "no_cpu_baseline": True})
-            sub = run_tp(tp_args, rank, world, local_rank, emit=False)
-            if rank == 0:
-                extra["tp"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline", "gpu_launches",
-                                                   "n_gpus", "steps", "warmup", "limiter") if k in sub}
-                extra["tp"]["config"] = sub["config"]["workload"] + f", tp{world}"
+            try:
+                sub = run_tp(tp_args, rank, world, local_rank, emit=False)
+                if rank == 0:
+                    extra["tp"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline",
+                                                       "gpu_launches", "n_gpus", "steps", "warmup", "limiter")
+                                   if k in sub}
+                    extra["tp"]["config"] = sub["config"]["workload"] + f", tp{world}"
+            except Exception as e:  # noqa: BLE001
+                extra["tp"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.empty_cache()
     if rank == 0:
         if extra:
             line["extra"] = extra

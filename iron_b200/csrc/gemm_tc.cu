@@ -566,20 +566,32 @@ struct TcWs {
   int* counters;
   float* part;
   uint16_t* xnorm;
+  uint16_t* gs;  // a gate/up pair above 128 rows: the gate and up outputs (nb x M bf16 each)
+  uint16_t* us;
 };
+
+// A gate/up pair of more than 128 activation rows runs as two single contractions
+// (gate, then up) and a SiLU * up pass: the pair's two weight tiles per stage leave
+// room for only two pipeline stages at that width.
+static bool tc_split_pair(int NW, int nb) { return NW == 2 && nb > 128; }
 static size_t tc_ws_need(int M, int K, int nb, int NW, bool rms) {
   using namespace tc;
+  const bool sp = tc_split_pair(NW, nb);
+  if (sp) NW = 1;
   const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
   int splits, kbps;
   tc_split_plan(M, K, N, NW, splits, kbps);
   size_t n = 256 + r256((size_t)tiles * 4);
   if (splits > 1) n += r256((size_t)tiles * splits * NW * N * BM * 4);
   if (rms) n += r256((size_t)nb * K * 2);
+  if (sp) n += 2 * r256((size_t)nb * M * 2);
   return n;
 }
 static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, bool rms, TcWs& o) {
   using namespace tc;
   if (!ws || !iron_aligned(ws, 256) || (size_t)bytes < tc_ws_need(M, K, nb, NW, rms)) return false;
+  const bool sp = tc_split_pair(NW, nb);
+  if (sp) NW = 1;
   const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
   int splits, kbps;
   tc_split_plan(M, K, N, NW, splits, kbps);
@@ -591,7 +603,20 @@ static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, b
   o.part = (float*)(b + off);
   if (splits > 1) off += r256((size_t)tiles * splits * NW * N * BM * 4);
   o.xnorm = (uint16_t*)(b + off);
+  if (rms) off += r256((size_t)nb * K * 2);
+  o.gs = sp ? (uint16_t*)(b + off) : nullptr;
+  if (sp) off += r256((size_t)nb * M * 2);
+  o.us = sp ? (uint16_t*)(b + off) : nullptr;
   return true;
+}
+
+// y[b, m] = bf16(silu_tanh(g) * u) of the split pair's two outputs (the pair epilogue)
+__global__ void silu_mul_rows_kernel(const uint16_t* g, const uint16_t* u, int M, int nb, uint16_t* y, int ld_y) {
+  const size_t n = (size_t)nb * M;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / M), m = (int)(i - (size_t)b * M);
+    y[(size_t)b * ld_y + m] = f2bf(silu_tanh_bf16(bf2f(g[i])) * bf2f(u[i]));
+  }
 }
 
 // plan_nb: the batch the workspace was carved for (>= p.nb); the split plan is the one
@@ -746,28 +771,39 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
   }
   if (!iron_aligned(x, 16) || ld_x % 8) return 1;
   if (p.wa.G != 32 && p.wa.G != 64 && p.wa.G != 128) return 1;
-  // a gate/up pair keeps two weight tiles per stage: its stages fit shared memory for
-  // up to 128 activation rows, so larger batches run as launches of equal row blocks
-  const int nchunk = pair ? (p.nb + 127) / 128 : 1;
-  const int rows = (p.nb + nchunk - 1) / nchunk;
-  const size_t ysz = p.epi == EPI_F32 ? 4 : 2;
-  for (int b0 = 0; b0 < p.nb; b0 += rows) {
-    GemvW8Params q = p;
-    q.nb = std::min(rows, p.nb - b0);
-    q.y = (uint16_t*)((uint8_t*)p.y + (size_t)b0 * p.ld_y * ysz);
-    if (p.res) q.res = p.res + (size_t)b0 * p.ld_y;
-    const uint16_t* xb = x + (size_t)b0 * ld_x;
-    int rc = 1;
-    switch (p.wa.G) {
-      case 32: rc = pair ? tc_launch<32, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<32, false>(q, xb, ld_x, ws, p.nb, st); break;
-      case 64: rc = pair ? tc_launch<64, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<64, false>(q, xb, ld_x, ws, p.nb, st); break;
-      case 128: rc = pair ? tc_launch<128, true>(q, xb, ld_x, ws, p.nb, st) : tc_launch<128, false>(q, xb, ld_x, ws, p.nb, st); break;
+  auto single = [&](const GemvW8Params& q) -> int {
+    switch (q.wa.G) {
+      case 32: return tc_launch<32, false>(q, x, ld_x, ws, p.nb, st);
+      case 64: return tc_launch<64, false>(q, x, ld_x, ws, p.nb, st);
+      default: return tc_launch<128, false>(q, x, ld_x, ws, p.nb, st);
     }
-    // 1 (not handled) can only come from the first block: the later ones have the same
-    // shape but fewer rows; the caller then runs every row on the exact kernel
-    if (rc) return rc;
+  };
+  if (pair && tc_split_pair(2, p.nb)) {
+    // gate and up as single contractions into the workspace, then SiLU * up
+    GemvW8Params q = p;
+    q.epi = EPI_STORE;
+    q.res = nullptr;
+    q.ld_y = p.M;
+    q.y = ws.gs;
+    int rc = single(q);
+    if (rc) return rc;  // 1 before any launch: the caller runs the exact kernel
+    q.wa = p.wb;
+    q.y = ws.us;
+    rc = single(q);
+    if (rc) return rc < 0 ? rc : iron_set_error(IRON_ERR_UNSUPPORTED, "gemm_tc: up half not launched");
+    const int64_t n = (int64_t)p.nb * p.M;
+    int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)iron_num_sms() * 8);
+    silu_mul_rows_kernel<<<grid, 256, 0, st>>>(ws.gs, ws.us, p.M, p.nb, p.y, p.ld_y);
+    return iron_check_launch("silu_mul_rows_kernel");
   }
-  return 0;
+  if (pair) {
+    switch (p.wa.G) {
+      case 32: return tc_launch<32, true>(p, x, ld_x, ws, p.nb, st);
+      case 64: return tc_launch<64, true>(p, x, ld_x, ws, p.nb, st);
+      default: return tc_launch<128, true>(p, x, ld_x, ws, p.nb, st);
+    }
+  }
+  return single(p);
 }
 
 }  // namespace iron

@@ -117,6 +117,39 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     assert np.mean(err <= lim) >= 0.999 and np.max(err) <= 0.05, f"pair: {np.mean(err <= lim):.4f}, max {err.max()}"
 
 
+@pytest.mark.parametrize("B", [128, 200, 256])
+def test_tc_gate_up_pair_wide_batches(B):
+    """A gate/up pair with the RMSNorm prologue at 128 rows (one pair launch) and above
+    (gate and up as single contractions, then SiLU * up: the prefill's 256-row blocks):
+    the pair epilogue's arithmetic, bf16(silu_tanh(bf16(Wg h)) * bf16(Wu h)), against the
+    exact sums."""
+    torch.manual_seed(40 + B)
+    M, K, G = 3072, 1024, 32
+    wg = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    wu = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    gw, uw = quantize_to_wire(wg, G), quantize_to_wire(wu, G)
+    qg, sg = wire_to_numpy(gw, M, K, G)
+    qu, su = wire_to_numpy(uw, M, K, G)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, device="cuda")).to(torch.bfloat16)
+    gh = torch.full((B, M), float("nan"), dtype=torch.bfloat16, device="cuda")
+    tw = _lib.tc_workspace([(M, K)], B, "cuda")
+    _lib.call("iron_gemv_w8a16_ex", gw.data_ptr(), uw.data_ptr(), M, K, G, 0, x.data_ptr(), K, B, nw.data_ptr(),
+              1e-6, 0, None, 0, gh.data_ptr(), M, tw.data_ptr(), tw.numel(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
+    rows = [0, B // 2, B - 1]
+    h = ops.rms_norm_f32(host(x)[rows], host(nw), 1e-6)
+    g = rnd(h.astype(np.float64) @ _deq(qg, sg, G).T)
+    u = rnd(h.astype(np.float64) @ _deq(qu, su, G).T)
+    want = rnd(ops.silu_tanh_bf16(g) * u)
+    got = host(gh)[rows]
+    err = np.abs(got - want)
+    lim = 2.0 ** -6 * np.abs(want) + 1e-4
+    assert not np.isnan(host(gh)).any()
+    assert np.mean(err <= lim) >= 0.999 and np.max(err) <= 0.05, f"pair: {np.mean(err <= lim):.4f}, max {err.max()}"
+
+
 def test_tc_without_workspace_runs_the_exact_launches():
     """No workspace: batch 16+ runs the exact kernel in launches of 8 rows, whose every
     output is the exact dequantised sum rounded once to bf16."""

@@ -172,6 +172,39 @@ int iron_embedding(const uint16_t* table, int vocab, const int32_t* ids, int n, 
 int iron_decode_advance(int32_t* pos, int32_t* seq_len, int32_t* kv_off, int batch, int HD,
                         void* stream);
 
+/* ---- data-movement operators of the Llama decode runlist (llama_npu.py:279-557) ---- */
+/* RoPE over (rows, cols) bf16 (RoPE, iron/operators/rope/op.py; golden
+ * rope/reference.py:88-154): y1 = x1*c - x2*s, y2 = x2*c + x1*s in float32, one bf16
+ * rounding, with (x1, x2) columns (j, j + cols/2) for method 0 (two halves) or
+ * (2j, 2j + 1) for method 1 (interleaved); angles (angle_rows, cols) interleaved
+ * [cos, sin] pairs, angle row r / (rows / angle_rows) for row r.  y may alias x. */
+int iron_rope_rows(const uint16_t* x, const uint16_t* angles, uint16_t* y, int rows, int cols,
+                   int angle_rows, int method, void* stream);
+/* StridedCopy (iron/operators/strided_copy/op.py; golden strided_copy/reference.py):
+ * gather by the input access pattern, scatter by the output one.  A pattern is up to 4
+ * (size, stride) pairs (host arrays, outermost first, read at call time) and an element
+ * offset; the innermost non-empty dimension is cut into `channels` parts paired one to
+ * one.  *in_addend_dev / *out_addend_dev (nullable device int32, elements) are the
+ * runtime offset parameters.  Out-of-range elements are skipped and set *err_dev = 1
+ * (nullable).  Elements of the output the pattern does not visit keep their values. */
+int iron_strided_copy(const void* in, int64_t in_elems, void* out, int64_t out_elems, int elem_bytes,
+                      int in_ndim, const int64_t* in_sizes, const int64_t* in_strides, int64_t in_offset,
+                      int out_ndim, const int64_t* out_sizes, const int64_t* out_strides,
+                      int64_t out_offset, int channels, const int32_t* in_addend_dev,
+                      const int32_t* out_addend_dev, int32_t* err_dev, void* stream);
+/* Repeat (iron/operators/repeat/op.py; golden repeat/reference.py): row r of `in`
+ * (row_bytes bytes) becomes rows r*repeat .. r*repeat + repeat - 1 of `out`. */
+int iron_repeat_rows(const void* in, void* out, int64_t rows, int64_t row_bytes, int repeat, void* stream);
+/* Softmax (iron/operators/softmax/op.py; golden softmax/reference.py) over each of
+ * `rows` bf16 rows of `cols`: the first n = clamp(vector_size, 0, cols) entries get
+ * float32 exp(x - max) * (1 / sum), the rest are masked to zero; vector_size is read
+ * from *vector_size_dev when it is not NULL (the runtime vector-size parameter). */
+int iron_softmax_rows(const uint16_t* x, uint16_t* y, int rows, int cols, int vector_size,
+                      const int32_t* vector_size_dev, void* stream);
+/* Transpose (iron/operators/transpose/op.py; golden transpose/reference.py): `batches`
+ * bf16 (M, N) matrices laid back to back -> (N, M) each; not in place. */
+int iron_transpose(const uint16_t* in, uint16_t* out, int M, int N, int batches, void* stream);
+
 /* ---- fused QKV head ------------------------------------------------------------
  * QKVHeadDataParallelOurs (iron/operators/qkv_head_dp/op_ours.py:31-262; golden
  * qkv_head_dp/reference.py:13-33): hn = RMSNorm_w(cur, n_in); raw = bf16(Wqkv@hn);

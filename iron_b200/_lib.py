@@ -47,6 +47,11 @@ SIGNATURES: dict[str, tuple] = {
     "iron_silu": (I, [P, P, I64, I, P]),
     "iron_embedding": (I, [P, I, P, I, I, P, P]),
     "iron_decode_advance": (I, [P, P, P, I, I, P]),
+    "iron_rope_rows": (I, [P, P, P, I, I, I, I, P]),
+    "iron_strided_copy": (I, [P, I64, P, I64, I, I, P, P, I64, I, P, P, I64, I, P, P, P, P]),
+    "iron_repeat_rows": (I, [P, P, I64, I64, I, P]),
+    "iron_softmax_rows": (I, [P, P, I, I, I, P, P]),
+    "iron_transpose": (I, [P, P, I, I, I, P]),
     "iron_qkv_head": (I, [P, P, P, I, I, I, P, P, P, I, P, P, I, I, I, I, I, I, I, P, F, I, P, P, I64, P]),
     "iron_decode_attn_workspace_bytes": (I64, [I, I, I, I]),
     "iron_decode_attn": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P, I64, P]),

@@ -278,6 +278,243 @@ class SiLU(Operator):
 
 
 # ---------------------------------------------------------------------------
+# data movement and softmax of the Llama decode runlist (llama_npu.py:279-557)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class RoPE(Operator):
+    """Rotary position embedding over (rows, cols) (iron/operators/rope/op.py:18-102;
+    golden rope/reference.py:88-154): method 0 two halves, 1 interleaved; ``angles``
+    holds interleaved [cos, sin] pairs, and each of its ``angle_rows`` rows serves
+    ``rows / angle_rows`` consecutive rows of x.  The output may be the input buffer."""
+
+    rows: int
+    cols: int
+    angle_rows: int | None = None
+    num_aie_columns: int = 1
+    method_type: int = 0
+    context: object = field(default=None, repr=False)
+
+    _name_aliases: ClassVar[dict[str, str]] = {
+        **Operator._name_aliases, "num_aie_columns": "col", "angle_rows": "arows", "method_type": "m"}
+
+    def __post_init__(self):
+        if self.angle_rows is None:
+            self.angle_rows = self.rows
+        if not (self.cols % 32 == 0 and self.cols >= 32):
+            raise ValueError("cols must be multiple of 32 and >= 32")
+        if self.rows % self.num_aie_columns != 0:
+            raise ValueError("rows must be divisible by num_aie_columns")
+        if not (self.angle_rows <= self.rows and self.rows % self.angle_rows == 0):
+            raise ValueError("angle_rows must divide rows")
+        if not (self.angle_rows >= self.num_aie_columns and self.angle_rows % self.num_aie_columns == 0):
+            raise ValueError("angle_rows must be divisible by num_aie_columns")
+        if self.method_type not in {0, 1}:
+            raise ValueError(f"method_type must be 0 or 1, got {self.method_type}")
+
+    def get_arg_spec(self):
+        return [AIERuntimeArgSpec("in", (self.rows, self.cols)),
+                AIERuntimeArgSpec("in", (self.angle_rows, self.cols)),
+                AIERuntimeArgSpec("out", (self.rows, self.cols))]
+
+    def launch(self, bufs, params, stream):
+        x, ang, y = bufs
+        abi("iron_rope_rows", ptr(x), ptr(ang), ptr(y), self.rows, self.cols, self.angle_rows,
+            self.method_type, stream)
+
+
+def _i64_array(vals):
+    import ctypes
+    vals = [int(v) for v in vals]
+    return (ctypes.c_int64 * max(1, len(vals)))(*vals)
+
+
+@dataclass
+class StridedCopy(Operator):
+    """Strided copy between two flat buffers (iron/operators/strided_copy/op.py:18-100;
+    golden strided_copy/reference.py): elements gathered by the input access pattern
+    (sizes, strides, offset; up to 4 dimensions) are scattered by the output one.
+    ``input_offset_parameter`` / ``output_offset_parameter`` name runtime parameters
+    (element counts) added to the offsets on every call, as the reference's DMA reads
+    them from the scratchpad.  Output elements the pattern does not visit keep their
+    values (the KV cache of the Llama runlist).  An element that would land outside
+    its buffer is skipped and sets the device word ``err`` (``status()``)."""
+
+    input_sizes: list
+    input_strides: list
+    input_offset: int
+    output_sizes: list
+    output_strides: list
+    output_offset: int
+    input_buffer_size: int = field(repr=False)
+    output_buffer_size: int = field(repr=False)
+    dtype: object = field(default=torch.bfloat16, repr=False)
+    transfer_size: int | None = None
+    num_aie_channels: int = 1
+    input_offset_parameter: str | None = None
+    output_offset_parameter: str | None = None
+    kwargs: dict = field(default_factory=dict, repr=False)
+    context: object = field(default=None, repr=False)
+
+    _name_aliases: ClassVar[dict[str, str]] = {
+        **Operator._name_aliases, "input_sizes": "isz", "input_strides": "ist", "input_offset": "ioff",
+        "output_sizes": "osz", "output_strides": "ost", "output_offset": "ooff", "transfer_size": "tr",
+        "num_aie_channels": "ch", "input_offset_parameter": "ipar", "output_offset_parameter": "opar"}
+
+    def __post_init__(self):
+        if len(self.input_sizes) != len(self.input_strides):
+            raise ValueError(f"input_sizes and input_strides must have the same length "
+                             f"({len(self.input_sizes)} vs {len(self.input_strides)})")
+        if len(self.output_sizes) != len(self.output_strides):
+            raise ValueError(f"output_sizes and output_strides must have the same length "
+                             f"({len(self.output_sizes)} vs {len(self.output_strides)})")
+        if not (1 <= len(self.input_sizes) <= 4 and 1 <= len(self.output_sizes) <= 4):
+            raise ValueError("access patterns have 1 to 4 dimensions")
+        self._err = None
+
+    @property
+    def runtime_params(self):
+        return tuple(p for p in (self.input_offset_parameter, self.output_offset_parameter) if p)
+
+    def get_arg_spec(self):
+        return [AIERuntimeArgSpec("in", (int(self.input_buffer_size),), dtype=self.dtype),
+                AIERuntimeArgSpec("out", (int(self.output_buffer_size),), dtype=self.dtype)]
+
+    def status(self) -> int:
+        """1 if a call skipped an element outside its buffer (then cleared), else 0."""
+        if self._err is None:
+            return 0
+        v = int(self._err.item())
+        self._err.zero_()
+        return v
+
+    def launch(self, bufs, params, stream):
+        src, dst = bufs
+        if self._err is None or self._err.device != src.device:
+            self._err = torch.zeros(1, dtype=torch.int32, device=src.device)
+        ia = params.slot(self.input_offset_parameter) if self.input_offset_parameter else None
+        oa = params.slot(self.output_offset_parameter) if self.output_offset_parameter else None
+        abi("iron_strided_copy", ptr(src), int(self.input_buffer_size), ptr(dst), int(self.output_buffer_size),
+            src.element_size(), len(self.input_sizes), _i64_array(self.input_sizes),
+            _i64_array(self.input_strides), int(self.input_offset), len(self.output_sizes),
+            _i64_array(self.output_sizes), _i64_array(self.output_strides), int(self.output_offset),
+            int(self.num_aie_channels), ptr(ia), ptr(oa), ptr(self._err), stream)
+
+
+@dataclass
+class Repeat(Operator):
+    """Repeat-interleave along the leading dimension (iron/operators/repeat/op.py:18-69;
+    golden repeat/reference.py): (rows, cols) -> (rows * repeat, cols)."""
+
+    rows: int
+    cols: int
+    repeat: int
+    transfer_size: int | None = None
+    dtype: object = field(default=torch.bfloat16, repr=False)
+    context: object = field(default=None, repr=False)
+
+    _name_aliases: ClassVar[dict[str, str]] = {**Operator._name_aliases, "repeat": "by", "transfer_size": "ts"}
+
+    def __post_init__(self):
+        if self.rows < 1 or self.cols < 1 or self.repeat < 1:
+            raise ValueError("rows, cols and repeat must be positive")
+
+    def get_arg_spec(self):
+        return [AIERuntimeArgSpec("in", (self.rows, self.cols), dtype=self.dtype),
+                AIERuntimeArgSpec("out", (self.rows * self.repeat, self.cols), dtype=self.dtype)]
+
+    def launch(self, bufs, params, stream):
+        x, y = bufs
+        abi("iron_repeat_rows", ptr(x), ptr(y), self.rows, self.cols * x.element_size(), self.repeat, stream)
+
+
+@dataclass
+class Softmax(Operator):
+    """Row softmax over ``cols`` (iron/operators/softmax/op.py:18-109; golden
+    softmax/reference.py), float32 inside, bf16 out.  With ``vector_size_parameter`` the
+    runtime parameter of that name gives the row length that counts (the mask kernel of
+    softmax/design.py:86-103): entries past it are masked and come out zero.  Without
+    it, ``rtp_vector_size`` (default ``cols``) does."""
+
+    rows: int
+    cols: int
+    num_aie_columns: int = 1
+    num_channels: int = 1
+    rtp_vector_size: int | None = None
+    vector_size_parameter: str | None = None
+    context: object = field(default=None, repr=False)
+
+    @property
+    def size(self):
+        return self.rows * self.cols
+
+    def __post_init__(self):
+        if self.rows % 16 != 0:
+            raise ValueError(f"rows ({self.rows}) must be a multiple of 16")
+        if self.cols % 16 != 0:
+            raise ValueError(f"cols ({self.cols}) must be a multiple of 16")
+        if self.rows % self.num_aie_columns != 0:
+            raise ValueError(f"rows ({self.rows}) must be a multiple of num_aie_columns ({self.num_aie_columns})")
+
+    @property
+    def runtime_params(self):
+        return (self.vector_size_parameter,) if self.vector_size_parameter else ()
+
+    def get_arg_spec(self):
+        return [AIERuntimeArgSpec("in", (self.size,)), AIERuntimeArgSpec("out", (self.size,))]
+
+    def launch(self, bufs, params, stream):
+        x, y = bufs
+        n = self.cols if self.rtp_vector_size is None else int(self.rtp_vector_size)
+        dev = params.slot(self.vector_size_parameter) if self.vector_size_parameter else None
+        abi("iron_softmax_rows", ptr(x), ptr(y), self.rows, self.cols, n, ptr(dev), stream)
+
+
+@dataclass
+class Transpose(Operator):
+    """Transpose of (M, N) bf16 matrices (iron/operators/transpose/op.py:18-129; golden
+    transpose/reference.py); ``num_batches`` > 1 transposes that many matrices laid
+    back to back."""
+
+    M: int
+    N: int
+    num_aie_columns: int
+    num_channels: int
+    m: int
+    n: int
+    s: int
+    num_batches: int = 1
+    context: object = field(default=None, repr=False)
+
+    _name_aliases: ClassVar[dict[str, str]] = {**Operator._name_aliases, "num_batches": "batch"}
+
+    def __post_init__(self):
+        if self.M % self.m != 0:
+            raise ValueError(f"Matrix rows ({self.M}) must be a multiple of {self.m}")
+        if self.N % self.n != 0:
+            raise ValueError(f"Matrix columns ({self.N}) must be a multiple of {self.n}")
+        if self.m % self.s != 0:
+            raise ValueError(f"AIE tile rows ({self.m}) must be a multiple of {self.s}")
+        if self.n % self.s != 0:
+            raise ValueError(f"AIE tile columns ({self.n}) must be a multiple of {self.s}")
+        if self.M * self.N % (self.m * self.n * self.num_aie_columns * self.num_channels) != 0:
+            raise ValueError("Transfer size must be divisible by m*n*num_columns*num_channels")
+        if self.N // self.num_aie_columns // self.n < 1:
+            raise ValueError(f"num_aie_columns ({self.num_aie_columns}) exceeds N/n ({self.N // self.n})")
+        if self.M // self.num_channels // self.m < 1:
+            raise ValueError(f"num_channels ({self.num_channels}) exceeds M/m ({self.M // self.m})")
+
+    def get_arg_spec(self):
+        bd = (self.num_batches,) if self.num_batches > 1 else ()
+        return [AIERuntimeArgSpec("in", bd + (self.M * self.N,)),
+                AIERuntimeArgSpec("out", bd + (self.N * self.M,))]
+
+    def launch(self, bufs, params, stream):
+        x, y = bufs
+        abi("iron_transpose", ptr(x), ptr(y), self.M, self.N, self.num_batches, stream)
+
+
+# ---------------------------------------------------------------------------
 # decode attention
 # ---------------------------------------------------------------------------
 

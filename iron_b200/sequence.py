@@ -47,6 +47,12 @@ class DeviceBuffer:
             raise ValueError(f"unknown device {device!r}")
         return self
 
+    def fill_(self, value, dtype=torch.bfloat16) -> "DeviceBuffer":
+        """Fill every element (read as ``dtype``) with ``value`` (the XRT tensor's
+        ``fill_``, which also syncs it to the device)."""
+        self.torch_view(dtype).fill_(value)
+        return self
+
     @property
     def nbytes(self) -> int:
         return self.raw.numel()
@@ -167,6 +173,15 @@ class SequenceCallable:
 
     def sync_independent_buffers(self):
         """Buffers are device-resident; nothing to push."""
+
+    @property
+    def input_buffer(self) -> DeviceBuffer:
+        """IRON's input / scratch / output XRT buffers are one device arena here: each
+        name is the whole arena, whose ``to()`` has nothing to move."""
+        return DeviceBuffer(self.arena, "arena")
+
+    scratch_buffer = input_buffer
+    output_buffer = input_buffer
 
     def _run_eager(self):
         for op, bufs in self._plan:

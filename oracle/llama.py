@@ -77,12 +77,19 @@ class OracleLlama:
     All bf16 values as float32."""
 
     def __init__(self, shape: LlamaShape, weights: dict, max_seq: int, angles=None,
-                 exact_attention: bool = False):
+                 exact_attention: bool = False, norm_form: str = "llama"):
         """``exact_attention``: softmax and context in float64, rounded once -- the
         quantity the reference's bf16 op chain approximates (its scores and
         probabilities are rounded to bf16); the float32 flash attention of the GPU
-        path is checked against this form."""
+        path is checked against this form.  ``norm_form``: "llama" is
+        ``rms_norm_forward`` of llama_cpu.py:41-46; "golden" is the RMSNorm operator's
+        golden (rms_norm/reference.py:8-17, ``ops.rms_norm_ref``), the form of the
+        ``RMSNorm`` operators in the NPU decode runlist (llama_npu.py:385-392)."""
+        if norm_form not in ("llama", "golden"):
+            raise ValueError(f"norm_form {norm_form!r}")
         self.s, self.w, self.exact_attention = shape, weights, exact_attention
+        self.norm = rms_norm if norm_form == "llama" else (
+            lambda x, w, eps: ops.rms_norm_ref(x, w, weighted=True, eps=eps))
         self.kv = np.zeros((shape.n_layers, shape.Hkv, max_seq, 2, shape.HD), F32)
         self.angles = (ops.rope_angle_table(max_seq, shape.HD, shape.theta) if angles is None
                        else np.asarray(angles, F32))
@@ -90,7 +97,7 @@ class OracleLlama:
     def layer(self, i: int, x, pos: int):
         s, L = self.s, self.w["layers"][i]
         QD, KVD = s.Hq * s.HD, s.Hkv * s.HD
-        h = rms_norm(x, L["norm1"], s.eps)
+        h = self.norm(x, L["norm1"], s.eps)
         qkv = linear(L["wqkv"], h)
         q = rope(qkv[:QD].reshape(s.Hq, s.HD), self.angles[pos])
         k = rope(qkv[QD:QD + KVD].reshape(s.Hkv, s.HD), self.angles[pos])
@@ -115,7 +122,7 @@ class OracleLlama:
             ctx[hh] = rnd((p.astype(np.float64) @ V).astype(F32))
         a = linear(L["wo"], ctx.reshape(-1))
         x1 = ops.add_ref(x, a)
-        h2 = rms_norm(x1, L["norm2"], s.eps)
+        h2 = self.norm(x1, L["norm2"], s.eps)
         g = linear(L["wg"], h2)
         u = linear(L["wu"], h2)
         gh = ops.mul_ref(ops.silu_ref(g), u)
@@ -126,6 +133,6 @@ class OracleLlama:
         x = np.asarray(self.w["embed"][token], F32)
         for i in range(self.s.n_layers):
             x = self.layer(i, x, pos)
-        xf = rms_norm(x, self.w["final_norm"], self.s.eps)
+        xf = self.norm(x, self.w["final_norm"], self.s.eps)
         logits = linear(self.w["embed"], xf)
         return logits, int(np.argmax(logits))

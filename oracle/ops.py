@@ -422,3 +422,72 @@ def pack_wo_tiled(q, scale_bits, cols: int, tsi_o: int, n_o_tiles: int, domain: 
             chunks.append(W[r0:r0 + tsi_o].reshape(-1))
             chunks.append(S[r0:r0 + tsi_o].reshape(-1))
     return np.concatenate(chunks)
+
+
+# ---------------------------------------------------------------------------
+# data movement and softmax of the Llama decode runlist
+# ---------------------------------------------------------------------------
+
+def rope_interleaved(x, ang):
+    """RoPE, interleaved method: columns (2j, 2j + 1) rotate by pair j of the angle row.
+
+    Restates ``rope/reference.py:94-113`` (``x_even*cos - x_odd*sin``,
+    ``x_even*sin + x_odd*cos``) in float32 with one bf16 rounding."""
+    x = np.asarray(x, dtype=F32)
+    ang = np.asarray(ang, dtype=F32)
+    c, s = ang[..., 0::2], ang[..., 1::2]
+    xe, xo = x[..., 0::2], x[..., 1::2]
+    y = np.empty_like(x)
+    y[..., 0::2] = (xe * c).astype(F32) - (xo * s).astype(F32)
+    y[..., 1::2] = (xo * c).astype(F32) + (xe * s).astype(F32)
+    return rnd(y)
+
+
+def _tap_offsets(sizes, strides, offset):
+    grids = np.meshgrid(*[np.arange(s) for s in sizes], indexing="ij")
+    flat = np.full(grids[0].shape, offset, dtype=np.int64)
+    for g, st in zip(grids, strides):
+        flat = flat + g * st
+    return flat.reshape(-1)
+
+
+def _channel_offsets(sizes, strides, offset, channels):
+    sizes = [1] * (4 - len(sizes)) + list(sizes)
+    strides = [0] * (4 - len(strides)) + list(strides)
+    hi = max(i for i, s in enumerate(sizes) if s >= 1)
+    per = sizes[hi] // channels
+    split = sizes[:hi] + [per] + sizes[hi + 1:]
+    return [_tap_offsets(split, strides, offset + c * per * strides[hi]) for c in range(channels)]
+
+
+def strided_copy(inp, out, in_sizes, in_strides, in_offset, out_sizes, out_strides, out_offset,
+                 channels=1, in_addend=0, out_addend=0):
+    """Gather by the input access pattern, scatter by the output one, channel by channel,
+    into a copy of ``out`` (elements the pattern does not visit keep their values).
+
+    Restates ``strided_copy/reference.py`` (``_pad_to_4d``, ``_tap_offsets``,
+    ``_channel_offsets``, ``reference``); the addends are the runtime offset
+    parameters, in elements."""
+    out = np.array(out, copy=True)
+    src = _channel_offsets(in_sizes, in_strides, in_offset + in_addend, channels)
+    dst = _channel_offsets(out_sizes, out_strides, out_offset + out_addend, channels)
+    for s, d in zip(src, dst):
+        if len(s) != len(d):
+            raise ValueError("tap element counts differ")
+        out[d] = np.asarray(inp)[s]
+    return out
+
+
+def softmax_rows(x, n=None):
+    """Row softmax over the first ``n`` entries (all when None), the rest zero, in float64
+    and rounded once to bf16.  Restates ``softmax/reference.py`` (``torch.softmax`` over
+    the last dim) with the runtime vector-size mask of ``softmax/design.py:86-103``."""
+    x = np.asarray(x, dtype=np.float64)
+    cols = x.shape[-1]
+    n = cols if n is None else max(0, min(int(n), cols))
+    out = np.zeros_like(x)
+    if n:
+        v = x[..., :n]
+        e = np.exp(v - v.max(axis=-1, keepdims=True))
+        out[..., :n] = e / e.sum(axis=-1, keepdims=True)
+    return rnd(out.astype(F32))

@@ -16,7 +16,7 @@ extracted with ``ast`` and executed unchanged in a small namespace.
 Outputs (numpy ``.npz``; bf16 stored as uint16 bit patterns):
   gemv_int8.npz, rtn_pack.npz, rms_norm.npz, rope.npz, qkv_head.npz,
   decode_attn.npz, swiglu.npz, elementwise.npz, gemv_bf16.npz, llama_block.npz,
-  gptq_pack.npz, decode_attn_batch.npz, mha_prefill.npz
+  gptq_pack.npz, decode_attn_batch.npz, mha_prefill.npz, seqops.npz
 """
 
 from __future__ import annotations
@@ -158,11 +158,72 @@ def mha_prefill(ref: Path):
     np.savez_compressed(OUT / "mha_prefill.npz", **out)
 
 
+def seqops(ref: Path):
+    """The data-movement and softmax operators of the Llama decode runlist, from their
+    own golden generators: RoPE (``rope/reference.py``; the exact target from the bf16
+    angle buffer: ``reference`` for the two halves, ``apply_rope`` with the buffer's
+    cos/sin for the interleaved method; rows laid out as the rope test lays them,
+    ``(seq_len, n_heads, cols)``), StridedCopy (the cases of ``strided_copy/test.py``
+    plus runtime offset addends), Repeat, Softmax and Transpose."""
+    import json
+    rope = load(ref, "iron/operators/rope/reference.py", "ref_rope_seq")
+    sc = load(ref, "iron/operators/strided_copy/reference.py", "ref_strided_copy")
+    rep = load(ref, "iron/operators/repeat/reference.py", "ref_repeat")
+    smx = load(ref, "iron/operators/softmax/reference.py", "ref_softmax")
+    tr = load(ref, "iron/operators/transpose/reference.py", "ref_transpose")
+    out = {}
+    for i, (rows, cols, arows, method) in enumerate(((32, 512, 8, 0), (32, 128, 16, 1), (64, 128, 32, 1),
+                                                     (64, 128, 8, 0))):
+        g = rope.generate_golden_reference(rows=rows, cols=cols, context_len=arows, method_type=method)
+        x = g["A"].transpose(0, 1).contiguous().reshape(rows, cols)
+        ang = g["B"]
+        if method == 0:
+            y = rope.reference(x, ang, 0, rows, cols)
+        else:
+            cos, sin = ang[:, 0::2].float(), ang[:, 1::2].float()
+            y = rope.apply_rope(g["A"], cos, sin, 1).transpose(0, 1).contiguous().reshape(rows, cols)
+        out.update({f"rope{i}_x": bits(x), f"rope{i}_ang": bits(ang), f"rope{i}_y": bits(y),
+                    f"rope{i}_dims": np.array([rows, cols, arows, method])})
+
+    def kv_slot(seq, slot, ch=1):
+        return dict(input_sizes=[8, 64], input_strides=[64, 1], input_offset=0, input_buffer_size=8 * 64,
+                    output_sizes=[1, 8, 64], output_strides=[0, seq * 64, 1], output_offset=slot * 64,
+                    output_buffer_size=8 * seq * 64, num_aie_channels=ch)
+
+    def flat(n, ch=1):
+        return dict(input_sizes=[n], input_strides=[1], input_offset=0, input_buffer_size=n,
+                    output_sizes=[n], output_strides=[1], output_offset=0, output_buffer_size=n,
+                    num_aie_channels=ch)
+
+    cases = [flat(1024), flat(1024, 2), flat(1024, 4), kv_slot(128, 5), kv_slot(128, 5, 2), kv_slot(128, 5, 4),
+             dict(kv_slot(128, 0), output_offset_addend=37 * 64),
+             dict(input_sizes=[4, 16, 8], input_strides=[8, 32, 1], input_offset=3, input_buffer_size=600,
+                  output_sizes=[16, 32], output_strides=[40, 1], output_offset=0, output_buffer_size=700,
+                  num_aie_channels=2, input_offset_addend=5, output_offset_addend=11)]
+    for i, kw in enumerate(cases):
+        g = sc.generate_golden_reference(**kw)
+        out.update({f"sc{i}_in": bits(g["input"]), f"sc{i}_out": bits(g["output"]),
+                    f"sc{i}_kw": np.array(json.dumps(kw))})
+    for i, (rows, cols, r) in enumerate(((8, 64, 4), (8, 512, 4), (4, 1024, 2))):
+        g = rep.generate_golden_reference(rows=rows, cols=cols, repeat=r)
+        out.update({f"rep{i}_in": bits(g["input"]), f"rep{i}_out": bits(g["output"]),
+                    f"rep{i}_dims": np.array([rows, cols, r])})
+    for i, (rows, cols) in enumerate(((32, 256), (16, 1024))):
+        g = smx.generate_golden_reference(rows=rows, cols=cols)
+        out.update({f"smx{i}_in": bits(g["input"]), f"smx{i}_out": bits(g["output"])})
+    for i, (M, N, b) in enumerate(((256, 64, 1), (64, 128, 4))):
+        g = tr.generate_golden_reference(rows=M, cols=N, num_batches=b)
+        out.update({f"tr{i}_in": bits(g["input"]), f"tr{i}_out": bits(g["output"]),
+                    f"tr{i}_dims": np.array([M, N, b])})
+    np.savez_compressed(OUT / "seqops.npz", **out)
+
+
 def main(ref: Path, only: list[str] | None = None):
     setup_shim(ref)
     if only:
         for name in only:
-            {"gptq_pack": gptq_pack, "decode_attn_batch": decode_attn_batch, "mha_prefill": mha_prefill}[name](ref)
+            {"gptq_pack": gptq_pack, "decode_attn_batch": decode_attn_batch, "mha_prefill": mha_prefill,
+             "seqops": seqops}[name](ref)
         print("wrote", ", ".join(only), "to", OUT)
         return
     rms = load(ref, "iron/operators/rms_norm/reference.py", "iron.operators.rms_norm.reference")
@@ -322,6 +383,7 @@ def main(ref: Path, only: list[str] | None = None):
     gptq_pack(ref)
     decode_attn_batch(ref)
     mha_prefill(ref)
+    seqops(ref)
     print("wrote fixtures to", OUT)
 
 

@@ -220,3 +220,38 @@ def test_llama_block_matches_reference_cpu_path(golden):
     assert_bf16_pinned(orc.kv[0, :, T, 1], g["v_new"])
     want = from_bits(g["out"])
     assert np.all(np.abs(out - want) <= 1e-2 + 2e-2 * np.abs(want))
+
+
+def test_llama_runlist_data_movement(golden):
+    """The oracle's RoPE (both methods, angle rows serving consecutive rows), strided copy
+    (channel splits, runtime addends), repeat-interleave, softmax and transpose against
+    the reference's own golden generators (tests/golden/make_golden.py ``seqops``)."""
+    import json
+    g = golden("seqops")
+    for i in range(4):
+        rows, cols, arows, method = (int(v) for v in g[f"rope{i}_dims"])
+        x = from_bits(g[f"rope{i}_x"]).reshape(rows, cols)
+        ang = np.repeat(from_bits(g[f"rope{i}_ang"]).reshape(arows, cols), rows // arows, axis=0)
+        y = ops.rope_two_halves(x, ang) if method == 0 else ops.rope_interleaved(x, ang)
+        assert_bf16_pinned(y, g[f"rope{i}_y"], min_exact=1.0)
+    i = 0
+    while f"sc{i}_in" in g:
+        kw = json.loads(str(g[f"sc{i}_kw"]))
+        src = g[f"sc{i}_in"]
+        out = ops.strided_copy(src, np.zeros(kw["output_buffer_size"], np.uint16), kw["input_sizes"],
+                               kw["input_strides"], kw["input_offset"], kw["output_sizes"], kw["output_strides"],
+                               kw["output_offset"], kw.get("num_aie_channels", 1),
+                               kw.get("input_offset_addend", 0), kw.get("output_offset_addend", 0))
+        assert np.array_equal(out, g[f"sc{i}_out"]), f"strided copy case {i}"
+        i += 1
+    assert i == 8
+    for i in range(3):
+        rows, cols, r = (int(v) for v in g[f"rep{i}_dims"])
+        assert np.array_equal(np.repeat(g[f"rep{i}_in"].reshape(rows, cols), r, axis=0),
+                              g[f"rep{i}_out"].reshape(rows * r, cols))
+    for i in range(2):
+        x = from_bits(g[f"smx{i}_in"])
+        assert_bf16_pinned(ops.softmax_rows(x), g[f"smx{i}_out"])
+    for i in range(2):
+        M, N, b = (int(v) for v in g[f"tr{i}_dims"])
+        assert np.array_equal(g[f"tr{i}_in"].reshape(b, M, N).transpose(0, 2, 1), g[f"tr{i}_out"].reshape(b, N, M))

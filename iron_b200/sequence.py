@@ -6,8 +6,8 @@ specs (with ``name[start:end]`` byte slices and explicit ``buffer_sizes``),
 ``get_buffer(name).torch_view()``, a ``params`` scratchpad written by name and
 ``sync()``-ed before a call, and ``__call__()`` that runs the whole runlist and
 waits for it.  On the first call the runlist is run once eagerly (workspaces
-are allocated then) and captured into a CUDA graph; later calls replay the
-graph, reading runtime parameters from device memory.  All buffers live in
+are allocated then) and captured into a CUDA graph (recorded, not run again); later
+calls replay the graph, reading runtime parameters from device memory.  All buffers live in
 one device arena with 256-byte aligned members.
 """
 
@@ -202,13 +202,16 @@ class SequenceCallable:
             if not self.op.use_cuda_graph:
                 self._run_eager()
             elif self._graph is None:
-                self._run_eager()  # allocates operator workspaces outside the capture
+                # this call's work, run eagerly (operator workspaces are allocated here,
+                # outside the capture); the capture then records the same launches without
+                # running them, so a runlist that updates buffers in place (the residual
+                # adds of a decoder) runs exactly once per call
+                self._run_eager()
                 self.stream.synchronize()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=self.stream):
                     self._run_eager()
                 self._graph = g
-                self._graph.replay()
             else:
                 self._graph.replay()
         self.stream.synchronize()

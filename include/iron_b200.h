@@ -60,7 +60,8 @@ int64_t iron_launch_count(void);
  * matvec_vectorized_int8_bf16 (aie_kernels/aie2p/mv_int8_signed.cc:103-115,
  * biased: mv_int8.cc:60-114).  batch: activation rows sharing the weight.  Batch 1..8
  * (and 9..15) computes the exact dequantised sum (one bf16 rounding; launches of 8
- * rows); batch 16..256 on plain wires runs one tcgen05 tensor-core contraction with
+ * rows); batch 16..4096 on plain wires runs one tcgen05 tensor-core contraction (in row
+ * blocks of up to 128 activation rows, a second grid dimension) with
  * each weight q*s written as two bf16 planes (hi + lo, exact products) and float32
  * accumulation: the exact sum up to float32 summation order.  That contraction keeps
  * its scratch (status word, split-K arrival counters and partial tiles, RMS-normalised
@@ -74,8 +75,8 @@ int iron_gemv_w8a16(const void* wire, int M, int K, int group, int tile_m,
                     const uint16_t* x, int batch, const uint16_t* residual,
                     uint16_t* y, void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Workspace bytes of a batch 16..256 tensor-core projection of M rows x K columns
- * (any epilogue, a gate/up pair and an RMSNorm prologue included); 256 below batch 16.
+/* Workspace bytes of a batch 16..4096 tensor-core projection of M rows x K columns
+ * (any epilogue, a gate/up pair and an RMSNorm prologue included); 256 outside that range.
  * No reference counterpart. */
 int64_t iron_tc_workspace_bytes(int M, int K, int batch);
 /* Error word of the tensor-core projections that used `workspace` (its first int32):
@@ -100,7 +101,7 @@ int iron_quantize_rtn(const uint16_t* w, int M, int K, int group, int tile_m, in
  * y[b, m] = bf16( sum_k A[m, k] * x[b, k] )  (f32 accumulation).
  * independent != 0: `batch` independent GEMVs, A[b] (M, K) each (the num_batches
  * mode of iron/operators/gemv/op.py:151-157).  Replaces GEMV (gemv/op.py:20-163,
- * kernel aie_kernels/generic/mv.cc:47-90).  A shared weight with 16..256 rows runs
+ * kernel aie_kernels/generic/mv.cc:47-90).  A shared weight with 16..4096 rows runs
  * the tcgen05 contraction of iron_gemv_w8a16 with its scratch in `workspace`
  * (iron_tc_workspace_bytes(M, K, batch); NULL: launches of 8 rows instead). */
 int iron_gemv_bf16(const uint16_t* A, int M, int K, const uint16_t* x, int batch,

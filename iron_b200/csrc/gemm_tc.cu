@@ -54,8 +54,13 @@ constexpr int NTH = 32 * (NDQ + 2);  // warp 0 TMA, warps 1..NDQ dequant + epilo
 constexpr int MMA_WARP = NDQ + 1;
 constexpr int SMEM_MAX = 227 * 1024;
 constexpr int SMEM_CTA = 113 * 1024;  // two CTAs per SM
-constexpr size_t WS_FLOATS = 4u << 20;  // 16 MB of split-K partials
-constexpr int MAX_TILES = 4096;
+constexpr size_t WS_FLOATS = 4u << 20;  // 16 MB of split-K partials per row block
+constexpr int MAX_TILES = 4096;         // weight tiles of one launch
+// activation rows of a row block: 128 leaves room for 3 pipeline stages (a 256-row block
+// for 2; the prefill's contractions: 5.20 ms with 256, 5.01 ms with 128 per 1024-token
+// prompt)
+constexpr int BLOCK_ROWS = 128;
+constexpr int MAX_ROWS = 4096;          // activation rows of one launch
 constexpr unsigned long long TIMEOUT_NS = 200ull * 1000 * 1000;
 // Fewest k-blocks per split.  Measured on the batch-32 Qwen3-0.6B step: 2 -> 8,460
 // tok/s, 4 -> 9,826, 6 -> 9,354, 8 -> 9,331 (more splits add reduction work to
@@ -64,7 +69,7 @@ constexpr int MIN_KB = 4;
 
 
 struct TcParams {
-  int M, K, N, nb;              // N: MMA n (batch padded to 16); nb: batch rows
+  int M, K, N, nb;              // N: MMA n (activation rows of a row block, padded to 16); nb: rows
   int splits, kbps;             // k-block splits and k-blocks per split
   int sbox;                     // bytes of scales loaded per row and split
   int stages, ncols;            // pipeline stages, TMEM columns
@@ -74,8 +79,8 @@ struct TcParams {
   int ld_y;
   uint32_t xor_mask;
   int* status;    // the workspace's error word
-  int* counters;  // [tiles] split-K arrival counters (zero between launches)
-  float* part;    // [tiles][splits][NW * N][BM] float32 partial tiles
+  int* counters;  // [row blocks][tiles] split-K arrival counters (zero between launches)
+  float* part;    // [row blocks][tiles][splits][NW * N][BM] float32 partial tiles
   int off_a, off_x, off_raw, off_scale, off_bar;
 };
 
@@ -185,6 +190,9 @@ __global__ void __launch_bounds__(NTH, 2)
   uint8_t* sm = sm_dyn + ((1024 - (sa(sm_dyn) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x / p.splits, split = blockIdx.x - tile * p.splits;
+  // blockIdx.y: the row block of N activation rows starting at row bofs; tix numbers the
+  // (row block, weight tile) pairs for the split-K partials and counters
+  const int tix = blockIdx.y * (gridDim.x / p.splits) + tile, bofs = blockIdx.y * p.N;
   const int row0 = tile * BM;
   const int kb0 = split * p.kbps;
   const int nkb = min(p.kbps, p.K / BK - kb0);
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(NTH, 2)
           tma_2d(raw + (size_t)(s * NW) * BM * BK, &tm_raw0, kx, row0, &raw_full[s]);
           if (PAIR) tma_2d(raw + (size_t)(s * NW + 1) * BM * BK, &tm_raw1, kx, row0, &raw_full[s]);
         }
-        tma_2d(xtile + (size_t)s * N * 128, &tm_x, kx, 0, &raw_full[s]);
+        tma_2d(xtile + (size_t)s * N * 128, &tm_x, kx, bofs, &raw_full[s]);
         issued = i + 1;
       }
       // no copy may still be in flight when the CTA exits
@@ -380,9 +388,9 @@ __global__ void __launch_bounds__(NTH, 2)
         *yo = f2bf(a0);
       }
     };
-    auto finish = [&](int b, float a0, float a1) { finish_at(m, b, a0, a1); };
+    auto finish = [&](int b, float a0, float a1) { finish_at(m, bofs + b, a0, a1); };
     if (ok) {
-      float* part = p.part + ((size_t)(tile * p.splits + split) * NW * N) * BM;
+      float* part = p.part + ((size_t)(tix * p.splits + split) * NW * N) * BM;
       for (int c0 = 16 * half; c0 < N; c0 += 32) {
         float v[16], u[16];
         tmem_ld16(taddr + (uint32_t)c0, v);
@@ -403,8 +411,8 @@ __global__ void __launch_bounds__(NTH, 2)
       __threadfence();
       bar_epi();
       if (t == 0) {
-        *lastf = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
-        if (*lastf) p.counters[tile] = 0;
+        *lastf = atomicAdd(&p.counters[tix], 1) == p.splits - 1;
+        if (*lastf) p.counters[tix] = 0;
       }
       bar_epi();
       if (*lastf && ok) {
@@ -415,7 +423,7 @@ __global__ void __launch_bounds__(NTH, 2)
           // as always.  The partial tiles are [split][NW][column][row].
           constexpr int CB = PAIR ? 2 : 4, U = PAIR ? 2 : 4, CS = 32 * NDQ / (BM / 4);  // column stride: 8
           const int r4 = 4 * (t % (BM / 4)), cofs = t / (BM / 4);
-          const float* base = p.part + (size_t)tile * p.splits * NW * N * BM + r4;
+          const float* base = p.part + (size_t)tix * p.splits * NW * N * BM + r4;
           for (int b0 = cofs; b0 < N; b0 += CS * CB) {
             float4 a0[CB], a1[CB];
 #pragma unroll
@@ -456,10 +464,10 @@ __global__ void __launch_bounds__(NTH, 2)
             for (int c = 0; c < CB; ++c) {
               const int b = b0 + CS * c;
               if (b >= N) continue;
-              finish_at(row0 + r4, b, a0[c].x, a1[c].x);
-              finish_at(row0 + r4 + 1, b, a0[c].y, a1[c].y);
-              finish_at(row0 + r4 + 2, b, a0[c].z, a1[c].z);
-              finish_at(row0 + r4 + 3, b, a0[c].w, a1[c].w);
+              finish_at(row0 + r4, bofs + b, a0[c].x, a1[c].x);
+              finish_at(row0 + r4 + 1, bofs + b, a0[c].y, a1[c].y);
+              finish_at(row0 + r4 + 2, bofs + b, a0[c].z, a1[c].z);
+              finish_at(row0 + r4 + 3, bofs + b, a0[c].w, a1[c].w);
             }
           }
         }
@@ -537,14 +545,24 @@ static bool map2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// K split over CTAs so that they make about one wave (two per SM), at least MIN_KB
-// k-blocks per split (a shorter split is mostly start-up, and every split adds a partial
-// tile to the last CTA's reduction), the partials within WS_FLOATS
-static void tc_split_plan(int M, int K, int N, int NW, int& splits, int& kbps) {
+// The activation rows of a launch in nt row blocks of N rows each (N a multiple of 16,
+// at most BLOCK_ROWS; the blocks are one grid row each and share the weight tiles, which
+// they read from L2 after the first)
+static void tc_rows(int nb, int& N, int& nt) {
   using namespace tc;
-  const int tiles = (M + BM - 1) / BM;
+  nt = nb > BLOCK_ROWS ? (nb + BLOCK_ROWS - 1) / BLOCK_ROWS : 1;
+  N = ((nb + nt - 1) / nt + 15) / 16 * 16;
+}
+
+// K split over CTAs so that they make about one wave (two per SM for one row block, one
+// per SM for several: their stages fill an SM), at least MIN_KB k-blocks per split (a
+// shorter split is mostly start-up, and every split adds a partial tile to the last
+// CTA's reduction), the partials within WS_FLOATS per row block
+static void tc_split_plan(int M, int K, int N, int NW, int nt, int& splits, int& kbps) {
+  using namespace tc;
+  const int tiles = (M + BM - 1) / BM * nt;  // (row block, weight tile) pairs
   const int kblocks = K / BK;
-  splits = 2 * iron_num_sms() / tiles;
+  splits = (nt > 1 ? 1 : 2) * iron_num_sms() / tiles;
   // from 128 rows on, each k-block is a large MMA and every split adds a large partial
   // tile to the reduction: twice the floor (1024x3072 at 256 rows: 40.0 -> 33.2 us)
   const int min_kb = N >= 128 ? 2 * MIN_KB : MIN_KB;
@@ -552,7 +570,7 @@ static void tc_split_plan(int M, int K, int N, int NW, int& splits, int& kbps) {
   if (splits < 1) splits = 1;
   kbps = (kblocks + splits - 1) / splits;
   splits = (kblocks + kbps - 1) / kbps;
-  while (splits > 1 && (size_t)tiles * splits * NW * N * BM > WS_FLOATS) {
+  while (splits > 1 && (size_t)tiles * splits * NW * N * BM > WS_FLOATS * nt) {
     kbps *= 2;
     splits = (kblocks + kbps - 1) / kbps;
   }
@@ -578,9 +596,11 @@ static size_t tc_ws_need(int M, int K, int nb, int NW, bool rms) {
   using namespace tc;
   const bool sp = tc_split_pair(NW, nb);
   if (sp) NW = 1;
-  const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
+  int N, nt;
+  tc_rows(nb, N, nt);
+  const int tiles = (M + BM - 1) / BM * nt;
   int splits, kbps;
-  tc_split_plan(M, K, N, NW, splits, kbps);
+  tc_split_plan(M, K, N, NW, nt, splits, kbps);
   size_t n = 256 + r256((size_t)tiles * 4);
   if (splits > 1) n += r256((size_t)tiles * splits * NW * N * BM * 4);
   if (rms) n += r256((size_t)nb * K * 2);
@@ -592,9 +612,11 @@ static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, b
   if (!ws || !iron_aligned(ws, 256) || (size_t)bytes < tc_ws_need(M, K, nb, NW, rms)) return false;
   const bool sp = tc_split_pair(NW, nb);
   if (sp) NW = 1;
-  const int N = (nb + 15) / 16 * 16, tiles = (M + BM - 1) / BM;
+  int N, nt;
+  tc_rows(nb, N, nt);
+  const int tiles = (M + BM - 1) / BM * nt;
   int splits, kbps;
-  tc_split_plan(M, K, N, NW, splits, kbps);
+  tc_split_plan(M, K, N, NW, nt, splits, kbps);
   uint8_t* b = (uint8_t*)ws;
   o.status = (int*)b;
   size_t off = 256;
@@ -610,28 +632,40 @@ static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, b
   return true;
 }
 
-// y[b, m] = bf16(silu_tanh(g) * u) of the split pair's two outputs (the pair epilogue)
+// y[b, m] = bf16(silu_tanh(g) * u) of the split pair's two outputs (the pair epilogue),
+// eight values per thread with 16-byte accesses (M and ld_y multiples of 8, y 16-byte
+// aligned; the caller checks)
 __global__ void silu_mul_rows_kernel(const uint16_t* g, const uint16_t* u, int M, int nb, uint16_t* y, int ld_y) {
-  const size_t n = (size_t)nb * M;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const int b = (int)(i / M), m = (int)(i - (size_t)b * M);
-    y[(size_t)b * ld_y + m] = f2bf(silu_tanh_bf16(bf2f(g[i])) * bf2f(u[i]));
+  const unsigned m8 = (unsigned)M / 8, n = (unsigned)nb * m8;  // nb * M / 8 < 2^31 (the caller's rows)
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned b = i / m8, m = (i - b * m8) * 8;
+    const uint4 gv = __ldcg((const uint4*)(g + (size_t)b * M + m));
+    const uint4 uv = __ldcg((const uint4*)(u + (size_t)b * M + m));
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint16_t lo = f2bf(silu_tanh_bf16(bf_lo(gw[e])) * bf_lo(uw[e]));
+      const uint16_t hi = f2bf(silu_tanh_bf16(bf_hi(gw[e])) * bf_hi(uw[e]));
+      o[e] = lo | ((uint32_t)hi << 16);
+    }
+    *(uint4*)(y + (size_t)b * ld_y + m) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-// plan_nb: the batch the workspace was carved for (>= p.nb); the split plan is the one
-// of that batch, so this launch's partial tiles fit the carved region
+// The split plan is the one the workspace was carved with (the same rows and weights),
+// so this launch's partial tiles fit the carved region
 template <int G, bool PAIR>
-static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const TcWs& ws, int plan_nb,
-                     cudaStream_t st) {
+static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const TcWs& ws, cudaStream_t st) {
   using namespace tc;
   constexpr int NW = PAIR ? 2 : 1;
   const int M = p.M, K = p.K, nb = p.nb;
-  const int N = (nb + 15) / 16 * 16;
+  int N, nt;
+  tc_rows(nb, N, nt);
   const int tiles = (M + BM - 1) / BM;
   if (tiles > MAX_TILES) return 1;
   int splits, kbps;
-  tc_split_plan(M, K, (plan_nb + 15) / 16 * 16, NW, splits, kbps);
+  tc_split_plan(M, K, N, NW, nt, splits, kbps);
   TcParams tp = {};
   tp.status = ws.status;
   tp.counters = ws.counters;
@@ -688,7 +722,7 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const T
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
     attr[dev] = true;
   }
-  fn<<<tiles * splits, NTH, smem, st>>>(tp, mr0, ms0, mr1, ms1, mx);
+  fn<<<dim3(tiles * splits, nt), NTH, smem, st>>>(tp, mr0, ms0, mr1, ms1, mx);
   return iron_check_launch("gemm_tc_kernel");
 }
 
@@ -696,14 +730,15 @@ static int tc_launch(const GemvW8Params& p, const uint16_t* x, int ld_x, const T
 int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int ld_x, int nb, uint16_t* y,
                         int ld_y, void* workspace, int64_t workspace_bytes, cudaStream_t st) {
   using namespace tc;
-  if (nb < 16 || nb > 256 || K % 64 || !iron_aligned(A, 16) || !iron_aligned(x, 16) || ld_x % 8) return 1;
-  const int N = (nb + 15) / 16 * 16;
+  if (nb < 16 || nb > MAX_ROWS || K % 64 || !iron_aligned(A, 16) || !iron_aligned(x, 16) || ld_x % 8) return 1;
+  int N, nt;
+  tc_rows(nb, N, nt);
   const int tiles = (M + BM - 1) / BM;
   if (tiles > MAX_TILES) return 1;
   TcWs ws;
   if (!tc_ws_carve(workspace, workspace_bytes, M, K, nb, 1, false, ws)) return 1;
   int splits, kbps;
-  tc_split_plan(M, K, N, 1, splits, kbps);
+  tc_split_plan(M, K, N, 1, nt, splits, kbps);
   TcParams tp = {};
   tp.status = ws.status;
   tp.counters = ws.counters;
@@ -745,16 +780,16 @@ int gemm_tc_bf16_launch(const uint16_t* A, int M, int K, const uint16_t* x, int 
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
     attr[dev] = true;
   }
-  fn<<<tiles * splits, NTH, smem, st>>>(tp, ma, ma, ma, ma, mx);
+  fn<<<dim3(tiles * splits, nt), NTH, smem, st>>>(tp, ma, ma, ma, ma, mx);
   return iron_check_launch("gemm_tc_kernel");
 }
 
 // 0: launched (or a launch error < 0); 1: not handled (the caller runs the exact GEMV
-// in 8-row launches).  Plain wires, 16 <= batch <= 256, K a multiple of 64 and of
+// in 8-row launches).  Plain wires, 16 <= batch <= MAX_ROWS, K a multiple of 64 and of
 // 8 * group, 16-byte aligned activations with rows a multiple of 8 elements apart.
 int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
   using namespace tc;
-  if (p.nb < 16 || p.nb > 256 || !p.wa.plain1 || (pair && !p.wb.plain1)) return 1;
+  if (p.nb < 16 || p.nb > MAX_ROWS || !p.wa.plain1 || (pair && !p.wb.plain1)) return 1;
   if (p.K % 64 || p.K % (8 * p.wa.G) || p.K > 16384) return 1;
   if (!iron_aligned(p.wa.base, 16) || (pair && !iron_aligned(p.wb.base, 16))) return 1;
   TcWs ws;  // without a workspace large enough the caller runs the exact kernel
@@ -773,12 +808,14 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
   if (p.wa.G != 32 && p.wa.G != 64 && p.wa.G != 128) return 1;
   auto single = [&](const GemvW8Params& q) -> int {
     switch (q.wa.G) {
-      case 32: return tc_launch<32, false>(q, x, ld_x, ws, p.nb, st);
-      case 64: return tc_launch<64, false>(q, x, ld_x, ws, p.nb, st);
-      default: return tc_launch<128, false>(q, x, ld_x, ws, p.nb, st);
+      case 32: return tc_launch<32, false>(q, x, ld_x, ws, st);
+      case 64: return tc_launch<64, false>(q, x, ld_x, ws, st);
+      default: return tc_launch<128, false>(q, x, ld_x, ws, st);
     }
   };
   if (pair && tc_split_pair(2, p.nb)) {
+    // the SiLU * up pass moves 8 values per access: otherwise the exact kernel runs
+    if (p.M % 8 || p.ld_y % 8 || !iron_aligned(p.y, 16)) return 1;
     // gate and up as single contractions into the workspace, then SiLU * up
     GemvW8Params q = p;
     q.epi = EPI_STORE;
@@ -791,16 +828,16 @@ int gemm_tc_launch(const GemvW8Params& p, bool pair, cudaStream_t st) {
     q.y = ws.us;
     rc = single(q);
     if (rc) return rc < 0 ? rc : iron_set_error(IRON_ERR_UNSUPPORTED, "gemm_tc: up half not launched");
-    const int64_t n = (int64_t)p.nb * p.M;
+    const int64_t n = (int64_t)p.nb * (p.M / 8);
     int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)iron_num_sms() * 8);
     silu_mul_rows_kernel<<<grid, 256, 0, st>>>(ws.gs, ws.us, p.M, p.nb, p.y, p.ld_y);
     return iron_check_launch("silu_mul_rows_kernel");
   }
   if (pair) {
     switch (p.wa.G) {
-      case 32: return tc_launch<32, true>(p, x, ld_x, ws, p.nb, st);
-      case 64: return tc_launch<64, true>(p, x, ld_x, ws, p.nb, st);
-      default: return tc_launch<128, true>(p, x, ld_x, ws, p.nb, st);
+      case 32: return tc_launch<32, true>(p, x, ld_x, ws, st);
+      case 64: return tc_launch<64, true>(p, x, ld_x, ws, st);
+      default: return tc_launch<128, true>(p, x, ld_x, ws, st);
     }
   }
   return single(p);
@@ -813,7 +850,7 @@ using namespace iron;
 // Bytes of workspace a batch >= 16 projection of M rows x K columns needs (a gate/up
 // pair with an RMSNorm prologue included; a bf16 weight needs no more).
 extern "C" int64_t iron_tc_workspace_bytes(int M, int K, int batch) {
-  if (M < 1 || K < 64 || batch < 16 || batch > 256) return 256;
+  if (M < 1 || K < 64 || batch < 16 || batch > tc::MAX_ROWS) return 256;
   return (int64_t)std::max(tc_ws_need(M, K, batch, 1, true), tc_ws_need(M, K, batch, 2, true));
 }
 

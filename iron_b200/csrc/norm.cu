@@ -54,9 +54,11 @@ template <int HD>
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* raw, const uint16_t* n_qn, const uint16_t* n_kn,
                                        const uint16_t* ang, int ang_is_table, uint16_t* q_out,
                                        uint16_t* kv, int Hq, int Hkv, int max_seq, int kv_off,
-                                       const int32_t* kv_off_dev, float eps, int norm_mode, int pos0) {
+                                       const int32_t* kv_off_dev, float eps, int norm_mode, int pos0, int batch) {
   constexpr int PER = HD / 32;
-  const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+  // one warp per (head, row): warp threadIdx.y of the block takes row blockIdx.y * blockDim.y + threadIdx.y
+  const int head = blockIdx.x, b = blockIdx.y * blockDim.y + threadIdx.y, lane = threadIdx.x;
+  if (b >= batch) return;
   const int QKV = (Hq + 2 * Hkv) * HD;
   // element offset of K_t in a head region
   const int off = pos0 >= 0 ? (pos0 + b) * 2 * HD : (kv_off_dev ? kv_off_dev[b] : kv_off);
@@ -116,13 +118,15 @@ int qk_norm_rope_kv_launch(const uint16_t* raw, const uint16_t* n_qn, const uint
                            const uint16_t* ang, int ang_is_table, uint16_t* q_out, uint16_t* kv,
                            int HD, int Hq, int Hkv, int max_seq, int batch, int kv_off,
                            const int32_t* kv_off_dev, float eps, int norm_mode, cudaStream_t st, int pos0) {
-  dim3 g(Hq + Hkv, batch);
+  // a warp per (head, row), up to 8 rows per block
+  const int rpb = batch >= 64 ? 8 : 1;
+  const dim3 g(Hq + Hkv, (batch + rpb - 1) / rpb), blk(32, rpb);
   if (HD == 128) {
-    qk_norm_rope_kv_kernel<128><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                   max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0);
+    qk_norm_rope_kv_kernel<128><<<g, blk, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
+                                                    max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0, batch);
   } else if (HD == 64) {
-    qk_norm_rope_kv_kernel<64><<<g, 32, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
-                                                  max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0);
+    qk_norm_rope_kv_kernel<64><<<g, blk, 0, st>>>(raw, n_qn, n_kn, ang, ang_is_table, q_out, kv, Hq, Hkv,
+                                                   max_seq, kv_off, kv_off_dev, eps, norm_mode, pos0, batch);
   } else {
     return iron_set_error(IRON_ERR_UNSUPPORTED, "qkv head: head_dim %d (supported: 64, 128)", HD);
   }

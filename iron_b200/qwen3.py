@@ -459,8 +459,9 @@ class Qwen3B200:
         self.run_step(from_tokens=True, advance=False)
         return self._read_tokens()
 
-    #: prompt rows per tensor-core launch of the prefill (the contraction's batch limit)
-    PREFILL_ROWS = 256
+    #: prompt rows per prefill block: each projection of a block is one tensor-core
+    #: contraction launch (its rows in row blocks of up to 128, a second grid dimension)
+    PREFILL_ROWS = 1024
 
     def prefill(self, prompt, stream: int = 0, start: int = 0, exact: bool = False) -> int:
         """Run the prompt ``prompt`` (token ids) of stream ``stream`` through every layer

@@ -7,7 +7,8 @@ float32 summation order differs from the exact dequantised sum
 rounding plus float32 summation error, and (b) against the decode path's bf16 gate
 (rtol 2e-2, atol 1e-2).  Shapes cover split K, ragged row tiles, groups 64/128 (a
 split may start inside a group), the biased payload domain, the residual / float32 /
-gate-up + RMSNorm epilogues, and batches 16..256."""
+gate-up + RMSNorm epilogues, and batches 16..1024 (above 128 rows a launch runs row
+blocks of equal size, up to 128 rows each, as a second grid dimension)."""
 
 import numpy as np
 import pytest
@@ -58,7 +59,8 @@ def _gemv(wire, M, K, G, domain, x, residual=None, ws="new", stream=None, sync=T
 @pytest.mark.parametrize("M,K,G,B,domain", [(6144, 1024, 32, 32, 0), (12288, 4096, 32, 32, 0),
                                             (4096, 12288, 32, 16, 0), (1000, 3072, 64, 20, 1),
                                             (300, 2048, 128, 64, 0), (3072, 1024, 32, 256, 0),
-                                            (1024, 3072, 32, 33, 0)])
+                                            (1024, 3072, 32, 33, 0), (4096, 1024, 32, 1024, 0),
+                                            (1024, 3072, 32, 300, 0), (1000, 2048, 64, 600, 1)])
 def test_tc_projection_matches_dequantised_reference(M, K, G, B, domain):
     torch.manual_seed(M + K + B)
     w = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
@@ -67,9 +69,10 @@ def test_tc_projection_matches_dequantised_reference(M, K, G, B, domain):
     x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
     ws = _lib.tc_workspace([(M, K)], B, "cuda")
     y1 = _gemv(wire, M, K, G, domain, x, ws=ws)
-    # the last split of each 128-row tile puts its arrival counter back to zero, so the
-    # workspace is ready for the next launch with nothing to clear
-    assert int(ws[:256 + 4 * ((M + 127) // 128)].count_nonzero()) == 0
+    # the last split of each (row block, 128-row tile) puts its arrival counter back to
+    # zero, so the workspace is ready for the next launch with nothing to clear
+    blocks = max(1, -(-B // 128))
+    assert int(ws[:256 + 4 * ((M + 127) // 128) * blocks].count_nonzero()) == 0
     y2 = _gemv(wire, M, K, G, domain, x, ws=ws)
     assert torch.equal(y1, y2), "not deterministic"
     _check(host(y1), q, s, host(x), G, f"{M}x{K} g{G} b{B}")
@@ -117,7 +120,7 @@ def test_tc_residual_f32_and_gate_up_rms_epilogues():
     assert np.mean(err <= lim) >= 0.999 and np.max(err) <= 0.05, f"pair: {np.mean(err <= lim):.4f}, max {err.max()}"
 
 
-@pytest.mark.parametrize("B", [128, 200, 256])
+@pytest.mark.parametrize("B", [128, 200, 256, 520, 1024])
 def test_tc_gate_up_pair_wide_batches(B):
     """A gate/up pair with the RMSNorm prologue at 128 rows (one pair launch) and above
     (gate and up as single contractions, then SiLU * up: the prefill's 256-row blocks):
@@ -138,7 +141,7 @@ def test_tc_gate_up_pair_wide_batches(B):
               1e-6, 0, None, 0, gh.data_ptr(), M, tw.data_ptr(), tw.numel(), _lib.stream_ptr())
     torch.cuda.synchronize()
     assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
-    rows = [0, B // 2, B - 1]
+    rows = sorted({0, B // 2, 255 % B, 256 % B, B - 1})
     h = ops.rms_norm_f32(host(x)[rows], host(nw), 1e-6)
     g = rnd(h.astype(np.float64) @ _deq(qg, sg, G).T)
     u = rnd(h.astype(np.float64) @ _deq(qu, su, G).T)
@@ -190,3 +193,27 @@ def test_tc_concurrent_projections_on_two_streams():
         assert _lib.lib().iron_tc_status(wss[i].data_ptr(), 0) == 0
         for y in outs[i]:
             assert torch.equal(y, want), f"projection {M}x{K} changed under a concurrent one"
+
+
+@pytest.mark.parametrize("B", [32, 520])
+def test_tc_bf16_weight_row_blocks(B):
+    """bf16 weights (the lm_head and shared-weight bf16 GEMV path) at 32 rows and in row
+    blocks (520 rows: five blocks of 112) against the float64 sum: one bf16 output
+    rounding plus float32 summation error (which is relative to the terms' magnitudes,
+    so an output near zero may sit a few ulps away), 95 % bit-exact."""
+    torch.manual_seed(70 + B)
+    M, K = 2048, 1024
+    A = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+    y = torch.full((B, M), float("nan"), dtype=torch.bfloat16, device="cuda")
+    tw = _lib.tc_workspace([(M, K)], B, "cuda")
+    _lib.call("iron_gemv_bf16", A.data_ptr(), M, K, x.data_ptr(), B, 0, y.data_ptr(), tw.data_ptr(), tw.numel(),
+              _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert _lib.lib().iron_tc_status(tw.data_ptr(), 0) == 0
+    a64, x64 = host(A).astype(np.float64), host(x).astype(np.float64)
+    exact = x64 @ a64.T
+    lim = 2.0 ** -8 * np.abs(exact) + 1e-5 * (np.abs(x64) @ np.abs(a64).T) + 1e-30
+    err = np.abs(host(y).astype(np.float64) - exact)
+    assert np.all(err <= lim), f"{B} rows: worst {np.max(err / lim):.3g} of the bound"
+    assert np.mean(host(y) == rnd(exact.astype(np.float32))) >= 0.95

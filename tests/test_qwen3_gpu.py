@@ -329,20 +329,21 @@ def test_batch32_decode_matches_oracle(n_layers):
         toks = nxt
 
 
-@pytest.mark.parametrize("impl", ["step", "ops"])
-def test_prefill_matches_token_by_token(small, impl):
+@pytest.mark.parametrize("impl,rows", [("step", 1024), ("ops", 1024), ("step", 256)])
+def test_prefill_matches_token_by_token(small, impl, rows):
     """Qwen3B200.prefill (a layer's prompt rows at once: tcgen05 projections from 16 rows
     on, causal multi-query attention) against the reference's prompt loop, one decode
-    step per token (check_cosine_int8.py:49-54): a 300-token prompt (a block of 256 rows
-    and one of 44) from position 20 of a cache whose first 20 positions were filled by
-    decode steps.
+    step per token (check_cosine_int8.py:49-54): a 300-token prompt from position 20 of
+    a cache whose first 20 positions were filled by decode steps, as one block of 300
+    rows (each contraction in three row blocks of 112) or, with 256-row prefill blocks,
+    a block of 256 rows and one of 44.
 
     The two differ only in float32 summation order (batched contraction vs the
     one-token kernels, flash attention vs split decoding), which flips a few bf16
     roundings per layer; every flip moves the next RMSNorm's scale and so every later
     value by about an ulp (with the projections on the exact kernel too the second
     layer agrees no better: the attention's flips alone spread as far).  So: the first
-    layer's K/V agree bit for bit almost everywhere and within the bf16 gate
+    layer's K/V agree bit for bit almost everywhere (>= 99.8 %) and within the bf16 gate
     everywhere; the second layer's agree within the gate almost everywhere, a few ulps
     at most, with the token loop and with the oracle (teacher-forced from position 0)
     alike; the logits agree within the whole-model gate, the next token is the same or
@@ -354,6 +355,7 @@ def test_prefill_matches_token_by_token(small, impl):
     prompt = [int(t) for t in rng.integers(0, cfg.V, P)]
     a = Qwen3B200(w, max_seq=S, impl=impl, keep_logits=True)
     b = Qwen3B200(w, max_seq=S, impl=impl, keep_logits=True)
+    a.PREFILL_ROWS = rows
     for d in (a, b):
         for p, t in enumerate(head):
             d.step_tokens([t], p)
@@ -365,7 +367,9 @@ def test_prefill_matches_token_by_token(small, impl):
     kvb = host(b.kv).reshape(L, cfg.Hkv, S, 2, cfg.HD)[:, :, :P0 + P]
     assert np.array_equal(kva[:, :, :P0], kvb[:, :, :P0])
     assert_close(kva[0], kvb[0], what="first layer K/V")
-    assert np.mean(kva[0] == kvb[0]) >= 0.999, f"{np.mean(kva[0] == kvb[0]):.5f} of layer-0 K/V bit-identical"
+    # float32 summation flips a few bf16 roundings of the QKV projection (0.1-0.2 % of
+    # values, more when a row block's whole K runs in one sum than when it is split)
+    assert np.mean(kva[0] == kvb[0]) >= 0.998, f"{np.mean(kva[0] == kvb[0]):.5f} of layer-0 K/V bit-identical"
     err = np.abs(kva[1] - kvb[1])
     assert np.mean(err <= ATOL + RTOL * np.abs(kvb[1])) >= 0.995 and err.max() <= 0.1, \
         f"second layer K/V: {np.mean(err <= ATOL + RTOL * np.abs(kvb[1])):.4f} within the gate, max {err.max()}"

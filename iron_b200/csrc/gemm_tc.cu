@@ -56,6 +56,10 @@ constexpr int SMEM_MAX = 227 * 1024;
 constexpr int SMEM_CTA = 113 * 1024;  // two CTAs per SM
 constexpr size_t WS_FLOATS = 4u << 20;  // 16 MB of split-K partials per row block
 constexpr int MAX_TILES = 4096;         // weight tiles of one launch
+// split-K arrival counters: a fixed region at the head of every workspace, so that
+// projections of different shapes sharing one workspace (one after another) never
+// find their counters where another left its partial tiles
+constexpr int COUNTERS = 16384;
 // activation rows of a row block: 128 leaves room for 3 pipeline stages (a 256-row block
 // for 2; the prefill's contractions: 5.20 ms with 256, 5.01 ms with 128 per 1024-token
 // prompt)
@@ -578,7 +582,8 @@ static void tc_split_plan(int M, int K, int N, int NW, int nt, int& splits, int&
 
 static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
 
-// Workspace layout: [status word | counters (tiles) | partials | normalised activations]
+// Workspace layout: [status word | COUNTERS counters | partials | normalised activations |
+// gate outputs of a split pair | up outputs]
 struct TcWs {
   int* status;
   int* counters;
@@ -601,7 +606,7 @@ static size_t tc_ws_need(int M, int K, int nb, int NW, bool rms) {
   const int tiles = (M + BM - 1) / BM * nt;
   int splits, kbps;
   tc_split_plan(M, K, N, NW, nt, splits, kbps);
-  size_t n = 256 + r256((size_t)tiles * 4);
+  size_t n = 256 + (size_t)COUNTERS * 4;
   if (splits > 1) n += r256((size_t)tiles * splits * NW * N * BM * 4);
   if (rms) n += r256((size_t)nb * K * 2);
   if (sp) n += 2 * r256((size_t)nb * M * 2);
@@ -615,13 +620,14 @@ static bool tc_ws_carve(void* ws, int64_t bytes, int M, int K, int nb, int NW, b
   int N, nt;
   tc_rows(nb, N, nt);
   const int tiles = (M + BM - 1) / BM * nt;
+  if (tiles > COUNTERS) return false;
   int splits, kbps;
   tc_split_plan(M, K, N, NW, nt, splits, kbps);
   uint8_t* b = (uint8_t*)ws;
   o.status = (int*)b;
   size_t off = 256;
   o.counters = (int*)(b + off);
-  off += r256((size_t)tiles * 4);
+  off += (size_t)COUNTERS * 4;
   o.part = (float*)(b + off);
   if (splits > 1) off += r256((size_t)tiles * splits * NW * N * BM * 4);
   o.xnorm = (uint16_t*)(b + off);

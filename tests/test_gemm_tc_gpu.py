@@ -217,3 +217,21 @@ def test_tc_bf16_weight_row_blocks(B):
     err = np.abs(host(y).astype(np.float64) - exact)
     assert np.all(err <= lim), f"{B} rows: worst {np.max(err / lim):.3g} of the bound"
     assert np.mean(host(y) == rnd(exact.astype(np.float32))) >= 0.95
+
+
+def test_tc_shared_workspace_across_shapes():
+    """Projections of different shapes one after another on ONE workspace at 300 rows
+    (the prefill's pattern: down, then the next layer's QKV): the split-K arrival
+    counters sit in a fixed region, so a projection with many (row block, tile) pairs
+    never reads another's partial tiles as counters.  Every row against the exact
+    kernel."""
+    torch.manual_seed(90)
+    G, B = 32, 300
+    shapes = [(1024, 3072), (4096, 1024), (1024, 2048), (3072, 1024), (4096, 1024)]
+    ws = _lib.tc_workspace(shapes, B, "cuda")
+    for M, K in shapes:
+        w = quantize_to_wire((torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16), G)
+        x = torch.randn(B, K, device="cuda").to(torch.bfloat16)
+        got = host(_gemv(w, M, K, G, 0, x, ws=ws))
+        q, s = wire_to_numpy(w, M, K, G)
+        _check(got, q, s, host(x), G, f"{M}x{K} after other shapes")

@@ -377,6 +377,16 @@ int64_t iron_qwen3_cand_bytes(void);
 /* Grid size the step kernel will use on the current device (one CTA per SM). */
 int iron_qwen3_grid(const iron_qwen3_model* m);
 int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream);
+/* One greedy token with HOST buffers, the form of Qwen3NPU.__call__
+ * (qwen3_npu_int8.py:594-621: host writes the step's inputs and params, one dispatch,
+ * wait, the result read back on the host).  Copies host_in = {token id, position}
+ * (int32; pinned memory keeps the copy asynchronous) to m->tok / m->pos, runs
+ * iron_qwen3_decode_step(m, embed_input, advance = 0), copies the next token and the
+ * step's error word back into host_out = {next token, error word} and waits for the
+ * stream.  Returns IRON_ERR_TIMEOUT (host_out[1] = the device code) when the step
+ * stopped on a bounded wait; iron_qwen3_sync_reset clears that state. */
+int iron_qwen3_step_host(const iron_qwen3_model* m, const int32_t* host_in, int32_t* host_out, int embed_input,
+                         void* stream);
 /* Weight tiles for the step kernel, made once at load time from plain wires (no
  * reference counterpart: they re-order the wires that qwen3_npu_int8.py:381-436 packs
  * for the NPU).  Rows [0, M) of a wire whose rows are `row_stride` bytes apart

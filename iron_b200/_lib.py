@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
     "iron_qwen3_cand_bytes": (I64, []),
     "iron_qwen3_grid": (I, [P]),
     "iron_qwen3_decode_step": (I, [P, I, I, P]),
+    "iron_qwen3_step_host": (I, [P, P, P, I, P]),
     "iron_qwen3_sync_reset": (I, [P, P]),
     "iron_qwen3_tiles_bytes": (I64, [I, I, I]),
     "iron_qwen3_pack_tiles": (I, [P, I64, I, I, I, I, I, P, P]),

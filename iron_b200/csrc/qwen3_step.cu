@@ -40,6 +40,7 @@
 // the sync words and leaves; the other CTAs see it in their own waits and leave too.
 // In-flight bulk copies are drained (bounded) before a CTA exits.
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -1621,15 +1622,26 @@ extern "C" int iron_qwen3_pack_tiles(const void* wire, int64_t row_stride, int M
   return iron_check_launch("pack_tiles_kernel");
 }
 
-extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream) {
+// Launch parameters of one model descriptor on one device.  A decode loop passes the
+// same descriptor every token and the checks walk every CTA's plan (~15 us of host
+// time), so the last checked descriptor is kept per host thread and compared bytewise.
+struct Prepared {
+  bool valid = false;
+  int dev = -1, grid = 0;
+  size_t smem = 0;
+  iron_qwen3_model m;
+  Kp p;
+};
+
+static int prepare(const iron_qwen3_model* m, Prepared& out) {
   const int grid = grid_for(m);
   int rc = validate(m, grid);
   if (rc) return rc;
   const int GQ = m->Hq / m->Hkv;
-  Kp p;
+  Kp& p = out.p;
   p.m = *m;
-  p.embed_input = embed_input;
-  p.advance = advance;
+  p.embed_input = 0;
+  p.advance = 0;
   p.kmax = std::max(std::max(m->D, m->Hq * HDIM), m->FF);
   p.hbn = std::max(std::max(m->FF, m->Hq * HDIM), (GQ + 2) * HDIM);
   const size_t fixed = fixed_smem(p.kmax, p.hbn, m->D, m->group, GQ, m->n_layers);
@@ -1641,12 +1653,72 @@ extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input
   IRON_REQUIRE(mc <= (size_t)p.ring, IRON_ERR_UNSUPPORTED,
                "qwen3 step: a %zu-byte weight share exceeds the %d-byte ring (model too large for one launch)", mc,
                p.ring);
-  const size_t smem = (size_t)p.ring + fixed;
+  IRON_REQUIRE((m->group == 32 && (GQ == 1 || GQ == 2 || GQ == 4)) || (m->group == 64 && (GQ == 2 || GQ == 4)) ||
+                   (m->group == 128 && (GQ == 2 || GQ == 4)),
+               IRON_ERR_UNSUPPORTED, "qwen3 step: group %d with GQA group %d", m->group, GQ);
+  out.grid = grid;
+  out.smem = (size_t)p.ring + fixed;
+  out.m = *m;
+  return IRON_OK;
+}
+
+static int prepared_for(const iron_qwen3_model* m, const Prepared*& P) {
+  static thread_local Prepared cache;
+  IRON_REQUIRE(m != nullptr, IRON_ERR_ARG, "qwen3 step: null model");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  if (!(cache.valid && cache.dev == dev && std::memcmp(&cache.m, m, sizeof(*m)) == 0)) {
+    cache.valid = false;
+    Prepared fresh;
+    const int rc = prepare(m, fresh);
+    if (rc) return rc;
+    fresh.dev = dev;
+    fresh.valid = true;
+    cache = fresh;
+  }
+  P = &cache;
+  return IRON_OK;
+}
+
+extern "C" int iron_qwen3_decode_step(const iron_qwen3_model* m, int embed_input, int advance, void* stream) {
+  const Prepared* P = nullptr;
+  const int rc = prepared_for(m, P);
+  if (rc) return rc;
+  Kp p = P->p;
+  p.embed_input = embed_input;
+  p.advance = advance;
+  const int GQ = m->Hq / m->Hkv;
   cudaStream_t st = (cudaStream_t)stream;
 #define IRON_STEP_CASE(g, gq) \
-  if (m->group == g && GQ == gq) return launch<g, gq>(p, grid, smem, st);
+  if (m->group == g && GQ == gq) return launch<g, gq>(p, P->grid, P->smem, st);
   IRON_STEP_CASE(32, 2) IRON_STEP_CASE(32, 1) IRON_STEP_CASE(32, 4) IRON_STEP_CASE(64, 2) IRON_STEP_CASE(64, 4)
   IRON_STEP_CASE(128, 2) IRON_STEP_CASE(128, 4)
 #undef IRON_STEP_CASE
   return iron_set_error(IRON_ERR_UNSUPPORTED, "qwen3 step: group %d with GQA group %d", m->group, GQ);
+}
+
+extern "C" int iron_qwen3_step_host(const iron_qwen3_model* m, const int32_t* host_in, int32_t* host_out,
+                                    int embed_input, void* stream) {
+  IRON_REQUIRE(m && host_in && host_out && m->tok && m->pos && m->sync, IRON_ERR_ARG,
+               "qwen3 host step: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  if (m->pos == m->tok + 1) {  // token and position side by side: one 8-byte copy
+    e = cudaMemcpyAsync(m->tok, host_in, 8, cudaMemcpyHostToDevice, st);
+  } else {
+    e = cudaMemcpyAsync(m->tok, host_in, 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, host_in + 1, 4, cudaMemcpyHostToDevice, st);
+  }
+  if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 host step: input copy: %s", cudaGetErrorString(e));
+  const int rc = iron_qwen3_decode_step(m, embed_input, 0, stream);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(host_out, m->tok, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(host_out + 1, m->sync + SYNC_ERR, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return iron_set_error(IRON_ERR_CUDA, "qwen3 host step: %s", cudaGetErrorString(e));
+  if (host_out[1] != 0)
+    return iron_set_error(IRON_ERR_TIMEOUT,
+                          "qwen3 step aborted on a bounded device wait (code %d); iron_qwen3_sync_reset clears it",
+                          host_out[1]);
+  return IRON_OK;
 }

@@ -167,6 +167,16 @@ class _StepModel(C.Structure):
                                              "kv_off", "logits", "sync", "trace")])
 
 
+def _one(v) -> int:
+    """The single value of an int or a one-element sequence / array."""
+    if isinstance(v, int):
+        return v
+    a = np.asarray(v).reshape(-1)
+    if a.size != 1:
+        raise ValueError(f"the batch-1 step takes one value (got {a.size})")
+    return int(a[0])
+
+
 class Qwen3B200:
     """Greedy Qwen3 decoder over ``batch`` independent streams on one GPU.
 
@@ -303,6 +313,13 @@ class Qwen3B200:
         m.sync = ptr(self.sync)
         m.trace = None
         self._model = m
+        self._mref = C.byref(m)
+        # host side of step_tokens: {token, position | next token, error word}, pinned
+        self._host_io = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        self._host_np = self._host_io.numpy()
+        self._host_in = self._host_io.data_ptr()
+        self._host_out = self._host_in + 8
+        self._step_host = L.iron_qwen3_step_host
 
     def enable_trace(self) -> torch.Tensor:
         """Step kernel only: record the hidden state entering every layer and the final
@@ -455,6 +472,15 @@ class Qwen3B200:
 
     def step_tokens(self, tokens, pos) -> torch.Tensor:
         """One step for B streams from token ids at positions ``pos`` -> next tokens (host)."""
+        if self.impl == "step":  # one library call: copy in, the step, copy out, wait
+            hn = self._host_np
+            hn[0], hn[1] = _one(tokens), _one(pos)
+            rc = self._step_host(self._mref, self._host_in, self._host_out, 1, self.stream.cuda_stream)
+            if rc < 0:
+                if int(hn[3]):
+                    self.check()  # resets the hand-off words and raises
+                raise _lib.IronError(f"iron_qwen3_step_host failed ({rc}): {_lib.last_error()}")
+            return torch.from_numpy(hn[2:3].copy())
         self._put_inputs(tokens, pos)
         self.run_step(from_tokens=True, advance=False)
         return self._read_tokens()

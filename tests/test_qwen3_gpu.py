@@ -174,6 +174,34 @@ def test_step_error_word_aborts_and_resets(small):
     assert int(dec.step_tokens([5], 0)[0]) == want
 
 
+def test_host_buffer_step_equals_device_fed_step(small):
+    """iron_qwen3_step_host (token and position read from host memory, next token and
+    error word written back, one call) decodes what the device-fed launch decodes, with
+    pinned buffers (step_tokens) and with plain pageable host arrays through the C ABI."""
+    import ctypes as C
+
+    from iron_b200 import _lib
+
+    cfg, w = small
+    a, b, c = (Qwen3B200(w, max_seq=32, impl="step", keep_logits=True) for _ in range(3))
+    hin, hout = np.zeros(2, np.int32), np.full(2, -1, np.int32)
+    t = 17
+    for pos in range(6):
+        ta = int(a.step_tokens([t], pos)[0])
+        with torch.cuda.stream(b.stream):
+            b.tok.fill_(t)
+            b.pos.fill_(pos)
+        b.run_step(from_tokens=True, advance=False)
+        b.stream.synchronize()
+        hin[:] = (t, pos)
+        _lib.call("iron_qwen3_step_host", C.byref(c._model), hin.ctypes.data, hout.ctypes.data, 1,
+                  c.stream.cuda_stream)
+        assert ta == int(b.tok[0]) == int(hout[0]), f"pos {pos}"
+        assert int(hout[1]) == 0
+        assert torch.equal(a.logits, b.logits) and torch.equal(a.logits, c.logits), f"pos {pos}"
+        t = ta
+
+
 def test_batch_above_eight_matches_single_streams(small):
     """Ten streams (the projections run in launches of 8 activation rows) against ten
     single-stream decoders."""

@@ -391,16 +391,16 @@ def qwen3_line(args, rank, world, local_rank, oracle=False, spot=False):
     pos += K
     t_ms = e0.elapsed_time(e1)
     # ---- e2e: public API per step (H2D token+position, D2H token) ----
-    toks = [int(t) for t in dec.tok.cpu()]
+    toks = dec.tok.cpu().tolist()
     # one untimed call first: it captures the host-fed step's graph
-    toks = [int(t) for t in dec.step_tokens(toks, pos)]
+    toks = dec.step_tokens(toks, pos).tolist()
     pos += 1
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e2.record(dec.stream)
     for _ in range(K):
-        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        toks = dec.step_tokens(toks, pos).tolist()
         pos += 1
     e3.record(dec.stream)
     torch.cuda.synchronize()
@@ -414,7 +414,7 @@ def qwen3_line(args, rank, world, local_rank, oracle=False, spot=False):
         ins, outs, p0 = [], [], pos
         for _ in range(max(NA, 1)):
             ins.append(toks[0])
-            toks = [int(t) for t in dec.step_tokens(toks, pos)]
+            toks = dec.step_tokens(toks, pos).tolist()
             outs.append(toks[0])
             pos += 1
     # ---- dominant kernel: the persistent step kernel (the only launch of a step) ----
@@ -431,7 +431,9 @@ def qwen3_line(args, rank, world, local_rank, oracle=False, spot=False):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": t_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xbf16", "data": "synthetic", "config": workload(args),
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B,
+            # the step kernel reads (token, position); the chained kernels also the valid
+            # lengths and K/V offsets, written on the host and copied with them
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B if dec.impl == "step" else 16 * B,
                     # the tokens, and the step kernel's error word / the two tensor-core status words
                     "d2h_bytes_per_step": 8 * B if dec.impl == "step" else 4 * B + (8 if B >= 16 else 0)},
             "gpu_launches": K * dec.launches_per_step(),
@@ -514,18 +516,18 @@ def run_tp(args, rank, world, local_rank, emit=True):
     barrier()
     t_ms = e0.elapsed_time(e1)
     pos = P + W + K
-    toks = [int(t) for t in dec.tok.cpu()]
+    toks = dec.tok.cpu().tolist()
     # one untimed call first: it runs the host-fed step's first (eager) pass, which also
     # sets up the collectives, and captures its graph on the next
     for _ in range(2):
-        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        toks = dec.step_tokens(toks, pos).tolist()
         pos += 1
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e2.record(dec.stream)
     for _ in range(K):
-        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        toks = dec.step_tokens(toks, pos).tolist()
         pos += 1
     e3.record(dec.stream)
     torch.cuda.synchronize()
@@ -575,7 +577,7 @@ def run_tp(args, rank, world, local_rank, emit=True):
                        "collectives": (f"{args.tp_collective if world > 1 else 'none'}: all-reduce of batch x "
                                        f"4096 float32 twice per layer, all-gather of 8 bytes per stream per step"),
                        "l2": "no flush: ~9 GB / world of weights streamed per step, larger than the L2"},
-            "e2e": {"value": K * B / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": 8 * B,
+            "e2e": {"value": K * B / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": 16 * B,
                     "d2h_bytes_per_step": 4 * B},
             "gpu_launches": K * dec.launches_per_step(),
             "roofline": {"bound": "hbm", "kernel": f"the chained kernels of one step ({dec.launches_per_step()} "
@@ -672,13 +674,13 @@ def run_llama(args, rank, world, local_rank):
     barrier()
     t_ms = e0.elapsed_time(e1)
     pos = [n + W + K for n in lens]
-    toks = [int(t) for t in dec.tok.cpu()]
+    toks = dec.tok.cpu().tolist()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e2.record(dec.stream)
     for _ in range(K):
-        toks = [int(t) for t in dec.step_tokens(toks, pos)]
+        toks = dec.step_tokens(toks, pos).tolist()
         pos = [p + 1 for p in pos]
     e3.record(dec.stream)
     torch.cuda.synchronize()
@@ -701,7 +703,9 @@ def run_llama(args, rank, world, local_rank):
                        "batch_per_gpu": B, "layers": 16, "hidden": 2048, "vocab": 128256,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "no flush: ~11 GB streamed per step per GPU, larger than the L2"},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
+            # tokens, positions, lengths and K/V offsets in; tokens and the two status words out
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 16 * B,
+                    "d2h_bytes_per_step": 4 * B + (8 if B >= 16 else 0)},
             "gpu_launches": K * dec.launches_per_step(),
             "roofline": {"bound": "hbm", "kernel": f"the chained kernels of one step ({dec.launches_per_step()} "
                                                    f"launches)",

@@ -155,3 +155,47 @@ def raise_on_status(code: int, what: str):
     if code:
         raise IronError(f"{what}: a tensor-core projection stopped on a bounded device wait "
                         f"(code {code}); its outputs are not valid")
+
+
+class StepIO:
+    """Host side of one decode step of B streams on ``stream``.
+
+    ``put`` writes the step's token ids, positions, valid lengths (position + 1) and
+    K/V element offsets (position * 2 * HD) into a pinned (4, B) int32 buffer and copies
+    it to the device params in one copy; ``get`` copies the B next tokens and the given
+    status words into a pinned buffer, waits for the stream and returns that buffer as
+    a numpy array (tokens, then the status words)."""
+
+    def __init__(self, params, tok, status_words, HD: int, stream):
+        import torch
+        self.B, self.HD, self.stream = int(params.shape[1]), int(HD), stream
+        self.params, self.tok, self.status = params, tok, list(status_words)
+        self.hin = torch.zeros(4, self.B, dtype=torch.int32, pin_memory=True)
+        self.hout = torch.zeros(self.B + len(self.status), dtype=torch.int32, pin_memory=True)
+        self.nin, self.nout = self.hin.numpy(), self.hout.numpy()
+
+    @staticmethod
+    def _host(v):
+        import torch
+        return v.detach().cpu().numpy() if torch.is_tensor(v) else v
+
+    def put(self, tokens, pos):
+        import numpy as np
+        import torch
+        n = self.nin
+        n[0] = self._host(tokens)
+        n[1] = self._host(pos)
+        np.add(n[1], 1, out=n[2])
+        np.multiply(n[1], 2 * self.HD, out=n[3])
+        with torch.cuda.stream(self.stream):
+            self.params.copy_(self.hin, non_blocking=True)
+
+    def get(self):
+        import torch
+        B = self.B
+        with torch.cuda.stream(self.stream):
+            self.hout[:B].copy_(self.tok, non_blocking=True)
+            for i, s in enumerate(self.status):
+                self.hout[B + i:B + i + 1].copy_(s, non_blocking=True)
+        self.stream.synchronize()
+        return self.nout

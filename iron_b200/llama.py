@@ -113,7 +113,6 @@ class LlamaB200:
         self.params = torch.zeros(4, B, dtype=torch.int32, device=dev)
         self.params[2] = 1
         self.tok, self.pos, self.len, self.off = self.params[0], self.params[1], self.params[2], self.params[3]
-        self.host_params = torch.zeros(2, B, dtype=torch.int32, pin_memory=True)
         self.attn_ws = torch.empty(_lib.lib().iron_decode_attn_workspace_bytes(B, c.Hq, c.HD, max_seq),
                                    dtype=torch.uint8, device=dev)
         # scratch of the 16+ stream tensor-core projections (one at a time on the decoder
@@ -123,6 +122,9 @@ class LlamaB200:
         self.stream = torch.cuda.Stream(device=dev)
         self._graphs: dict = {}
         self._step_launches: dict = {}  # advance -> kernels one step launched
+        # below 16 streams no tensor-core projection runs: no status words to read
+        status = [_lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)] if B >= 16 else []
+        self.io = _lib.StepIO(self.params, self.tok, status, c.HD, self.stream)
 
     def launches_per_step(self, advance: bool = True) -> int:
         """Our kernels per step, as the library counted them over the last eager or captured
@@ -193,21 +195,13 @@ class LlamaB200:
 
     def step_tokens(self, tokens, pos) -> torch.Tensor:
         """One step for the B streams from token ids at positions ``pos`` -> next tokens (host)."""
-        self.host_params[0] = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).expand(self.B)
-        self.host_params[1] = torch.as_tensor(pos, dtype=torch.int32).reshape(-1).expand(self.B)
-        with torch.cuda.stream(self.stream):
-            self.params[0:2].copy_(self.host_params, non_blocking=True)
-            self.len.copy_(self.pos + 1)
-            self.off.copy_(self.pos * (2 * self.cfg.HD))
+        self.io.put(tokens, pos)  # tokens, positions, lengths, K/V offsets: one copy
         self.run_step(advance=False)
-        if self.B < 16:  # no tensor-core projection ran; the head workspace holds candidates
-            with torch.cuda.stream(self.stream):
-                return self.tok.cpu()
-        with torch.cuda.stream(self.stream):
-            both = torch.cat([self.tok, _lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)]).cpu()
-        code = int(both[-2]) or int(both[-1])
+        out = self.io.get()
+        B = self.B
+        code = int(out[B]) or int(out[B + 1]) if B >= 16 else 0
         if code:
             self.tc_ws[:4].zero_()
             self.head_ws[:4].zero_()
             _lib.raise_on_status(code, "decode step")
-        return both[:-2]
+        return torch.from_numpy(out[:B].copy())

@@ -235,6 +235,9 @@ class Qwen3B200:
             if batch != 1:
                 raise ValueError("the persistent step kernel decodes one stream (batch 1)")
             self._init_step(dev)
+        else:  # below 16 streams no tensor-core projection runs: no status words to read
+            status = [_lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)] if B >= 16 else []
+            self.io = _lib.StepIO(self.params, self.tok, status, cfg.HD, self.stream)
 
     def _pack_tiles(self, wire, M, K_full, col0, K, dev, st, out=None):
         """16-row tiles of rows [0, M), columns [col0, col0 + K) of a plain wire
@@ -438,27 +441,25 @@ class Qwen3B200:
             if int(both[-1]):
                 self.check()
             return both[:-1]
-        if self.B < 16:  # no tensor-core projection ran; the head workspace holds candidates
-            with torch.cuda.stream(self.stream):
-                return self.tok.cpu()
-        with torch.cuda.stream(self.stream):
-            both = torch.cat([self.tok, _lib.status_word(self.tc_ws), _lib.status_word(self.head_ws)]).cpu()
-        code = int(both[-2]) or int(both[-1])
+        out = self.io.get()
+        B = self.B
+        code = int(out[B]) or int(out[B + 1]) if B >= 16 else 0
         if code:
             self.tc_ws[:4].zero_()
             self.head_ws[:4].zero_()
             _lib.raise_on_status(code, "decode step")
-        return both[:-2]
+        return torch.from_numpy(out[:B].copy())
 
     def _put_inputs(self, tokens, pos):
-        """(token, position) per stream -> device in one copy from pinned memory."""
+        """(token, position) per stream -> device in one copy from pinned memory (the
+        chained kernels' valid lengths and K/V offsets ride along)."""
+        if self.impl == "ops":
+            self.io.put(tokens, pos)
+            return
         self.host_params[0] = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).expand(self.B)
         self.host_params[1] = torch.as_tensor(pos, dtype=torch.int32).reshape(-1).expand(self.B)
         with torch.cuda.stream(self.stream):
             self.params[0:2].copy_(self.host_params, non_blocking=True)
-            if self.impl == "ops":  # the chained kernels read the derived length / offset too
-                self.len.copy_(self.pos + 1)
-                self.off.copy_(self.pos * (2 * self.cfg.HD))
 
     def __call__(self, x, seq_pos: int) -> int:
         """Qwen3NPU.__call__: hidden state (D,) bf16 of the new token -> argmax token."""

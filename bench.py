@@ -76,6 +76,8 @@ def parse():
                     help="per-kernel device time of --steps decode steps at --batch (CUPTI), not a bench line")
     ap.add_argument("--sweep", action="store_true", help="operator sweep of configuration 3, not a bench line")
     ap.add_argument("--sweep-reps", type=int, default=50)
+    ap.add_argument("--sweep-only", choices=["gemv", "attn"], default=None,
+                    help="run only the GEMV or only the decode-attention rows of the sweep")
     ap.add_argument("--sweep-json", type=str, default=None)
     ap.add_argument("--sweep-capture", nargs="?", const="", default=None,
                     help="with --sweep: only the small ncu capture case of the GEMV (optional NxKxB,... shapes)")
@@ -825,7 +827,7 @@ def run_sweep(args):
     ms = _sweep_timed([lambda: _lib.call("iron_add", a.data_ptr(), a.data_ptr(), a.data_ptr(), 8, s_)], reps)
     rows.append({"kernel": "launch_floor", "us": ms * 1e3})
     print(json.dumps(rows[-1]), flush=True)
-    for N, K in SWEEP_GEMV_SHAPES:
+    for N, K in (SWEEP_GEMV_SHAPES if args.sweep_only != "attn" else []):
         wbytes = N * K + N * (K // G) * 2
         w0 = quantize_to_wire((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), G)
         ws = [w0] + [w0.clone() for _ in range(_sweep_copies(wbytes, 64) - 1)]
@@ -844,7 +846,7 @@ def run_sweep(args):
             print(json.dumps(rows[-1]), flush=True)
         del ws, w0
     H, KV, HD = 32, 8, 128
-    for B in SWEEP_ATTN_BATCH:
+    for B in (SWEEP_ATTN_BATCH if args.sweep_only != "gemv" else []):
         for L in SWEEP_ATTN_LEN:
             kvbytes = B * 2 * KV * HD * L * 2
             q = torch.randn(B, H, HD, generator=g, device=dev).to(torch.bfloat16)

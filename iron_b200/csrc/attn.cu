@@ -11,6 +11,10 @@
 // and the CTA writes one partial per head.
 // Pass 2: grid (head, stream) merges the splits: M = max m_s,
 // o = sum o_s 2^(m_s-M) / sum l_s 2^(m_s-M)  (decode_attn/reference.py:26-38).
+#include <cstdlib>
+#include <cstring>
+
+#include "attn_tc.cuh"
 #include "common.cuh"
 
 namespace iron {
@@ -165,6 +169,218 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// The same pass 1 on the tensor pipe.  Grid, work split and partials are those of
+// attn_split_kernel (one (o, m, l) per query head and split, merged by
+// attn_combine_kernel).  The GQ query heads of the KV head are rows 0..GQ-1 of one
+// 16-row MMA tile (the other rows are zero).  K/V tiles of 64 positions stream
+// through a two-stage cp.async ring (16-byte chunks XOR-swizzled by row, so ldmatrix
+// reads are conflict-free); warp w takes positions 16w..16w+15 of every tile:
+// S = Q K^T on bf16 mma.sync m16n8k16 with float32 accumulation (products of bf16
+// values are exact in float32), a base-2 online softmax per row, and O += P V with P
+// as a bf16 high part plus a bf16 remainder (two MMAs: the probabilities enter at
+// about float32 precision).  The four warps' states merge in shared memory.  About
+// 12 warp instructions per cached position (against ~64 for the lane-load form at
+// GQA group 4) leave the kernel bound by the bytes in flight.
+// ---------------------------------------------------------------------------
+constexpr int TC_KEYS = 64;  // positions per K/V tile
+constexpr int TC_THREADS = 128;
+
+template <int HD>
+constexpr int tc_smem_bytes() {
+  return 16 * HD * 2 + 4 * TC_KEYS * HD * 2;  // Q tile, two stages of K and of V
+}
+
+template <int HD>
+__global__ void __launch_bounds__(TC_THREADS, 3) attn_split_tc_kernel(AttnParams p) {
+  constexpr int CH = HD / 8;   // 16-byte chunks per row
+  constexpr int KS = HD / 16;  // k-steps of Q K^T
+  constexpr int ND = HD / 8;   // n-tiles of the output
+  constexpr int TILE = TC_KEYS * HD * 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;                // [16][HD]
+  uint8_t* sK = smem + 16 * HD * 2;  // [2][64][HD]
+  uint8_t* sV = sK + 2 * TILE;       // [2][64][HD]
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int GQ = p.H / p.KV;
+  int L = p.seq_lens ? p.seq_lens[b] : p.seq_len;
+  L = L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
+  const int nblk = (L + TC_KEYS - 1) / TC_KEYS;
+  const int bps = (nblk + p.nsplit - 1) / p.nsplit;
+  const int b_begin = split * bps;
+  const int b_end = min(nblk, b_begin + bps);
+
+  // the GQ query rows of this KV head (zeros below them)
+  for (int i = tid; i < 16 * CH; i += TC_THREADS) {
+    const int r = i / CH, c = i - r * CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < GQ) v = *(const uint4*)(p.q + ((size_t)b * p.H + kvh * GQ + r) * HD + c * 8);
+    *(uint4*)(sQ + swz<HD>(r, c)) = v;
+  }
+  const uint16_t* head = p.kv + ((size_t)b * p.KV + kvh) * 2 * (size_t)p.max_seq * HD;
+  const size_t voff = p.layout == 0 ? HD : (p.layout == 1 ? (size_t)p.max_seq * HD : (size_t)p.block_kv * HD);
+  auto koff = [&](int j) -> size_t {
+    if (p.layout == 0) return (size_t)j * 2 * HD;
+    if (p.layout == 1) return (size_t)j * HD;
+    const int bk = j / p.block_kv, jj = j - bk * p.block_kv;
+    return ((size_t)bk * 2 * p.block_kv + jj) * HD;
+  };
+  // K/V tile of block blk into stage s; rows past the last position repeat it (masked
+  // below), so every copy reads inside the stream's cache
+  auto load_tile = [&](int blk, int s) {
+    const int jmax = L - 1;
+    for (int i = tid; i < TC_KEYS * CH; i += TC_THREADS) {
+      const int r = i / CH, c = i - r * CH;
+      const int j = min(blk * TC_KEYS + r, jmax);
+      const uint16_t* src = head + koff(j) + c * 8;
+      cp_async16(smem_u32(sK + s * TILE + swz<HD>(r, c)), src);
+      cp_async16(smem_u32(sV + s * TILE + swz<HD>(r, c)), src + voff);
+    }
+  };
+  if (b_begin < b_end) load_tile(b_begin, 0);
+  cp_async_commit();
+  __syncthreads();
+
+  uint32_t qf[KS][4];
+  {
+    const int mi = lane >> 3, rr = (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk)
+      ldsm_x4(smem_u32(sQ) + swz<HD>(rr, 2 * kk + (mi >> 1)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+  // the thread's rows: lane/4 (a) and lane/4 + 8 (b, always a zero row: GQ <= 8)
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float o[ND][4];
+#pragma unroll
+  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  for (int blk = b_begin; blk < b_end; ++blk) {
+    const int s = (blk - b_begin) & 1;
+    if (blk + 1 < b_end) load_tile(blk + 1, s ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t kbase = smem_u32(sK + s * TILE), vbase = smem_u32(sV + s * TILE);
+    // S = Q K^T for this warp's 16 positions (two n-tiles of 8)
+    float sc[2][4];
+    sc[0][0] = sc[0][1] = sc[0][2] = sc[0][3] = 0.f;
+    sc[1][0] = sc[1][1] = sc[1][2] = sc[1][3] = 0.f;
+    {
+      const int mi = lane >> 3, kr = (lane & 7) + 8 * (mi >> 1), kc = mi & 1;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + swz<HD>(16 * warp + kr, 2 * kk + kc), b0, b1, b2, b3);
+        mma_bf16(sc[0], qf[kk], b0, b1);
+        mma_bf16(sc[1], qf[kk], b2, b3);
+      }
+    }
+    const int j0 = blk * TC_KEYS + 16 * warp + 2 * (lane & 3);
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const int j = j0 + 8 * n;
+      sc[n][0] = j < L ? sc[n][0] * p.scale : -INFINITY;
+      sc[n][1] = j + 1 < L ? sc[n][1] * p.scale : -INFINITY;
+      sc[n][2] = j < L ? sc[n][2] * p.scale : -INFINITY;
+      sc[n][3] = j + 1 < L ? sc[n][3] * p.scale : -INFINITY;
+      mx_a = fmaxf(mx_a, fmaxf(sc[n][0], sc[n][1]));
+      mx_b = fmaxf(mx_b, fmaxf(sc[n][2], sc[n][3]));
+    }
+#pragma unroll
+    for (int x = 1; x < 4; x <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(~0u, mx_a, x));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(~0u, mx_b, x));
+    }
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    // a row that has seen only masked positions keeps everything at zero
+    const float u_a = mn_a == -INFINITY ? 0.f : mn_a, u_b = mn_b == -INFINITY ? 0.f : mn_b;
+    const float c_a = exp2f(m_a - u_a), c_b = exp2f(m_b - u_b);
+    m_a = mn_a;
+    m_b = mn_b;
+    l_a *= c_a;
+    l_b *= c_b;
+#pragma unroll
+    for (int n = 0; n < ND; ++n) {
+      o[n][0] *= c_a;
+      o[n][1] *= c_a;
+      o[n][2] *= c_b;
+      o[n][3] *= c_b;
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      sc[n][0] = exp2f(sc[n][0] - u_a);
+      sc[n][1] = exp2f(sc[n][1] - u_a);
+      sc[n][2] = exp2f(sc[n][2] - u_b);
+      sc[n][3] = exp2f(sc[n][3] - u_b);
+      l_a += sc[n][0] + sc[n][1];
+      l_b += sc[n][2] + sc[n][3];
+    }
+    // O += P V over the warp's 16 positions (one k-step)
+    {
+      uint32_t ph[4], pl[4];
+      split_pair(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split_pair(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split_pair(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split_pair(sc[1][2], sc[1][3], ph[3], pl[3]);
+      const int mi = lane >> 3, vr = (lane & 7) + 8 * (mi & 1), vc = mi >> 1;
+#pragma unroll
+      for (int n = 0; n < ND; n += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + swz<HD>(16 * warp + vr, n + vc), b0, b1, b2, b3);
+        mma_bf16(o[n], ph, b0, b1);
+        mma_bf16(o[n], pl, b0, b1);
+        mma_bf16(o[n + 1], ph, b2, b3);
+        mma_bf16(o[n + 1], pl, b2, b3);
+      }
+    }
+    __syncthreads();  // stage s is refilled two blocks on
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring is reused below
+
+  // row sums over the quad; the warps' states of the real rows into shared memory
+#pragma unroll
+  for (int x = 1; x < 4; x <<= 1) l_a += __shfl_xor_sync(~0u, l_a, x);
+  float* red_o = (float*)sK;   // [4][GQ][HD]
+  float* red_ml = (float*)sV;  // [4][GQ][2]
+  const int ra = lane >> 2, cb = 2 * (lane & 3);
+  if (ra < GQ) {
+    float* ro = red_o + ((size_t)warp * GQ + ra) * HD;
+#pragma unroll
+    for (int n = 0; n < ND; ++n) {
+      ro[8 * n + cb] = o[n][0];
+      ro[8 * n + cb + 1] = o[n][1];
+    }
+    if ((lane & 3) == 0) {
+      red_ml[(warp * GQ + ra) * 2] = m_a;
+      red_ml[(warp * GQ + ra) * 2 + 1] = l_a;
+    }
+  }
+  __syncthreads();
+  for (int t = tid; t < GQ * HD; t += TC_THREADS) {
+    const int r = t / HD, d = t - r * HD;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_ml[(w * GQ + r) * 2]);
+    float oo = 0.f, ll = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(red_ml[(w * GQ + r) * 2] - M);
+        oo = fmaf(red_o[((size_t)w * GQ + r) * HD + d], f, oo);
+        ll = fmaf(red_ml[(w * GQ + r) * 2 + 1], f, ll);
+      }
+    }
+    float* dst = p.ws + (((size_t)b * p.H + kvh * GQ + r) * p.nsplit + split) * (HD + 2);
+    dst[d] = oo;
+    if (d == 0) {
+      dst[HD] = M;
+      dst[HD + 1] = ll;
+    }
+  }
+}
+
 template <int HD>
 __global__ void attn_combine_kernel(const float* ws, int H, int nsplit, uint16_t* out) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -218,6 +434,42 @@ static int launch_split(AttnParams p, int batch, int cap, cudaStream_t st) {
   return ns;
 }
 
+// The tensor-pipe pass 1 is the default; IRON_DECODE_ATTN=lanes selects the
+// lane-load kernel (for comparisons).  Read once per process.
+static bool attn_tc_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("IRON_DECODE_ATTN");
+    return !(e && std::strcmp(e, "lanes") == 0);
+  }();
+  return on;
+}
+
+// Split count as launch_split, for the resident CTAs of the tensor-pipe kernel.
+template <int HD>
+static int launch_split_tc(AttnParams p, int batch, int cap, cudaStream_t st) {
+  static bool attr[64] = {false};
+  static int occ[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = dev >= 0 && dev < 64 ? occ[dev] : 0;
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(attn_split_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes<HD>());
+    attr[dev] = true;
+  }
+  if (per_sm < 1) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_split_tc_kernel<HD>, TC_THREADS, tc_smem_bytes<HD>());
+    if (per_sm < 1) per_sm = 1;
+    if (dev >= 0 && dev < 64) occ[dev] = per_sm;
+  }
+  const int wave = per_sm * iron_num_sms(), pairs = batch * p.KV;
+  const int target = 4 * pairs >= wave ? 3 * wave : wave;
+  int ns = target / pairs;
+  ns = ns < 1 ? 1 : (ns > cap ? cap : ns);
+  p.nsplit = ns;
+  attn_split_tc_kernel<HD><<<dim3(ns, p.KV, batch), TC_THREADS, tc_smem_bytes<HD>(), st>>>(p);
+  return ns;
+}
+
 }  // namespace iron
 
 using namespace iron;
@@ -257,6 +509,12 @@ extern "C" int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t*
   int ns = 0;
   const int GQ = H / KV;
   cudaStream_t st = (cudaStream_t)stream;
+  // the tensor-pipe kernel stages the query rows with 16-byte loads
+  if (attn_tc_enabled() && (HD == 128 || HD == 64) && (GQ == 1 || GQ == 2 || GQ == 4 || GQ == 8) &&
+      iron_aligned(q, 16)) {
+    ns = HD == 128 ? launch_split_tc<128>(p, batch, cap, st) : launch_split_tc<64>(p, batch, cap, st);
+    goto combine;
+  }
 #define IRON_ATTN_CASE(hd, gq) \
   if (HD == hd && GQ == gq) { ns = launch_split<hd, gq>(p, batch, cap, st); goto combine; }
   IRON_ATTN_CASE(128, 1) IRON_ATTN_CASE(128, 2) IRON_ATTN_CASE(128, 4) IRON_ATTN_CASE(128, 8)

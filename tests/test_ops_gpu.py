@@ -135,9 +135,11 @@ def test_decode_attention_against_reference_golden(golden, sp):
     o = _out(16 * 128)
     call(dev_bf16(g["Q"]), dev_bf16(kv).reshape(8, 2 * S * 128), o.reshape(16, 128))
     torch.cuda.synchronize()
-    want = from_bits(g[f"O_{sp}"])
+    want = from_bits(g[f"O_{sp}"])  # the float64 result rounded to bf16, to within one ulp
     assert_close(host(o), want, what=f"seq_pos {sp}")
-    assert_ulps(host(o), want, max_ulp=2, frac_exact=0.9, what=f"seq_pos {sp}")
+    # float32 sums in another order: the golden's rounding almost everywhere; outputs
+    # that nearly cancel (down to ~1e-6 here) may sit several of their ulps away
+    _near_rounding(host(o), want, f"seq_pos {sp}")
 
 
 @pytest.mark.parametrize("layout", ["token", "block"])
@@ -192,6 +194,43 @@ def _near_rounding(got, want, what):
     assert np.mean(d <= 1) >= 0.995, f"{what}: {np.mean(d <= 1):.4f} within one ulp"
     far = d > 2
     assert np.all(np.abs(got[far] - want[far]) <= 1e-4), f"{what}: {np.abs(got[far] - want[far]).max()}"
+
+
+@pytest.mark.parametrize("HD,GQ", [(128, 4), (128, 2), (128, 8), (64, 4)])
+def test_decode_attention_tensor_pipe_matches_lane_kernel(HD, GQ):
+    """Both pass-1 kernels of iron_decode_attn on the same ragged streams: the tensor-pipe
+    one (16-byte aligned queries) and the lane-load one (the same queries 4 bytes off a
+    16-byte boundary, which the tensor-pipe kernel does not take).  Both are float32
+    flash decoding over the same positions and differ only in summation order."""
+    from iron_b200 import _lib
+
+    B, KV, S = 5, 8, 700
+    H = KV * GQ
+    g = torch.Generator(device="cuda").manual_seed(HD * 10 + GQ)
+    qa = torch.randn(B * H * HD, generator=g, device="cuda").to(torch.bfloat16)
+    qbuf = torch.zeros(B * H * HD + 2, dtype=torch.bfloat16, device="cuda")
+    qb = qbuf[2:]  # 4 bytes past the allocation's aligned start
+    qb.copy_(qa)
+    assert qa.data_ptr() % 16 == 0 and qb.data_ptr() % 16 == 4
+    kv = torch.randn(B, KV, 2 * S * HD, generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.tensor([S, S // 2 + 3, 1, 65, 64], dtype=torch.int32, device="cuda")
+    nws = _lib.lib().iron_decode_attn_workspace_bytes(B, H, HD, S)
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    outs = []
+    for q in (qa, qb):
+        out = torch.zeros(B, H, HD, dtype=torch.bfloat16, device="cuda")
+        _lib.call("iron_decode_attn", q.data_ptr(), kv.data_ptr(), out.data_ptr(), B, H, KV, HD, S, 0, 0, 0,
+                  lens.data_ptr(), ws.data_ptr(), nws, _lib.stream_ptr())
+        torch.cuda.synchronize()
+        outs.append(host(out))
+    _near_rounding(outs[0], outs[1], f"HD {HD} GQ {GQ}")
+    kvr = kv.float().view(B, KV, S, 2, HD)
+    for b in range(B):
+        Lb = int(lens[b])
+        K = kvr[b, :, :Lb, 0].repeat_interleave(GQ, 0)
+        V = kvr[b, :, :Lb, 1].repeat_interleave(GQ, 0)
+        p = torch.softmax(torch.einsum("hd,hjd->hj", qa.view(B, H, HD)[b].float(), K) / HD ** 0.5, -1)
+        assert_close(outs[0][b], host(torch.einsum("hj,hjd->hd", p, V)), what=f"stream {b}")
 
 
 def _verify_op(H, KV, D, S, T, causal, layout, block=32, **kw):

@@ -241,7 +241,10 @@ int iron_qkv_head(const uint16_t* cur, const uint16_t* n_in, const void* wqkv_wi
  * 2 = [K_block | V_block] per block_kv tokens (decode_attn.cc:95-97).  seq_lens_dev (int32[batch]) overrides
  * seq_len when non-NULL (ragged streams).  kv must be 16-byte aligned (rows are
  * read as 16-byte vectors).  Split-KV flash decoding: partial (m, l, o) per split
- * in `workspace`, merged by a second pass. */
+ * in `workspace`, merged by a second pass.  With q 16-byte aligned and HD 64 or 128,
+ * the first pass runs on the tensor pipe (bf16 mma.sync, float32 accumulation);
+ * otherwise on 16-byte lane loads.  Both compute in float32 and differ only in
+ * summation order. */
 int64_t iron_decode_attn_workspace_bytes(int batch, int H, int HD, int max_seq);
 int iron_decode_attn(const uint16_t* q, const uint16_t* kv, uint16_t* out, int batch, int H,
                      int KV, int HD, int max_seq, int kv_layout, int block_kv, int seq_len,
